@@ -1,0 +1,304 @@
+#!/usr/bin/env python
+"""Benchmark of the Ivonar token loop on B200 (one JSON line on stdout from rank 0).
+
+Workload: Nano-shaped ternary hybrid (vocab 32768, d 1024, 24 blocks), batch 1,
+a 36-token random prompt, then 256 sampled decode tokens (T 0.5, top-k 40, repetition penalty 1.15).
+A step is one such generation. `value` is decode tokens/s of the persistent decode kernel with the
+prompt already prefilled in HBM (CUDA events around the one launch that decodes 256 tokens; L2 is
+flushed by a 256 MB write before every step, outside the timed region). `e2e` is the same metric
+through the public decoder API with the prompt in pinned host memory: prefill + sample + 16 bursts of
+advance_many(16), host copies included. With --gpus N (torchrun) every rank decodes its own
+independent sequences on its own GPU (data parallel, no collective on the data path); value is the
+total over ranks divided by the slowest rank's time.
+
+--impl reference times the reference algorithm's CPU implementation (the C port in oracle/, all host
+threads) on a bounded sample of the same workload, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+PROMPT = 36
+TOKENS = 256
+TEMPERATURE, TOP_K, PENALTY = 0.5, 40, 1.15
+WORKLOAD = "config1 nano b=1: 36-token random prompt + 256 sampled decode tokens (T 0.5, top-k 40, rp 1.15)"
+
+
+def log(*args) -> None:
+    print(*args, file=sys.stderr, flush=True)
+
+
+def parse() -> argparse.Namespace:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("b200", "reference"), default="b200")
+    ap.add_argument("--tokens", type=int, default=TOKENS)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks() -> tuple[float, str]:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
+    """Algorithmic HBM bytes of `tokens` decode steps starting at `first_position`.
+
+    Per token: every packed ternary byte + fp16 scale + fp32 bias once, the recurrent state read and
+    written, and the compressed latent cache read up to the current position (latent codes + scale +
+    fp16 k_rope per position per attention layer) plus its append.
+    """
+    cfg = model.config
+    weights = 0
+    for proj in model.projections():
+        weights += proj.packed_weight.numel() + proj.weight_scales.numel() * 2
+        if proj.bias is not None:
+            weights += proj.bias.numel() * 4
+    state = 0
+    per_pos = 0
+    for block in model.blocks:
+        m = block.mixer
+        if block.mixer_type == "mamba":
+            hsd = m.num_heads * m.state_dim * m.head_dim
+            state += 2 * 4 * (2 * hsd + hsd + cfg.hidden_dim * (m.conv_kernel_size - 1))
+        else:
+            per_pos += m.latent_dim + 4 + m.num_heads * m.rope_dim * 2
+    kv = sum(per_pos * (p + 1) for p in range(first_position, first_position + tokens)) + per_pos * tokens
+    total = tokens * (weights + state) + kv
+    return float(total), {"weights_per_token": weights, "state_per_token": state, "kv_bytes_per_position": per_pos}
+
+
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,utilization.gpu,power.draw,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int, enabled: bool = True) -> None:
+        self.index, self.proc, self.path = index, None, None
+        if not enabled:
+            return
+        out = ROOT / "gpurun_out"
+        out.mkdir(exist_ok=True)
+        self.path = out / f"clocks_rank{index}.csv"
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in self.path.read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        if not rows:
+            return None
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        loaded = [r for r in rows if r[3].isdigit() and int(r[3]) > 0] or rows
+        mhz = [float(r[1]) for r in loaded if r[1].replace(".", "").isdigit()]
+        reasons = sorted({names[i] for r in loaded for i in range(4) if r[5 + i].lower() == "active"})
+        return {
+            "sm_mhz": statistics.median(mhz) if mhz else None,
+            "sm_max_mhz": float(rows[0][2]) if rows[0][2].replace(".", "").isdigit() else None,
+            "reasons": reasons,
+            "samples": len(rows),
+            "samples_under_load": len(loaded),
+        }
+
+
+def cpu_baseline(model, prompt, tokens: int, threads: int = 0) -> dict:
+    """The C port of the reference token loop on this host's cores (bounded sample)."""
+    from oracle import oracle
+
+    dec = oracle.OracleDecoder(model, max_len=PROMPT + tokens + 1, threads=threads, seed=7)
+    dec.prefill(prompt)
+    dec.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
+    first = dec.sample()
+    start = time.perf_counter()
+    dec.generate(first, tokens)
+    seconds = time.perf_counter() - start
+    return {"value": tokens / seconds, "unit": "tok/s", "cores": dec.threads, "kind": "port",
+            "sample": f"config1 model, {PROMPT}-token prompt prefilled, {tokens} sampled decode tokens timed "
+                      f"(C port of the reference numba/GPU decode step, OpenMP, {dec.threads} threads)",
+            "seconds": seconds}
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import torch
+
+    from ivonar_inference_b200 import synthetic
+
+    model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
+    sample_tokens = 16
+    times = []
+    threads = 0
+    for step in range(args.warmup + args.steps):
+        prompt = synthetic.random_prompt(32768, PROMPT, seed=100 + step)[0].numpy()
+        result = cpu_baseline(model, prompt, sample_tokens)
+        threads = result["cores"]
+        if step >= args.warmup:
+            times.append(result["seconds"])
+    value = args.steps * sample_tokens / sum(times)
+    sample = (f"each step: config1 model, {PROMPT}-token prompt prefilled (untimed), {sample_tokens} sampled decode "
+              f"tokens timed; C port of the reference decode step, OpenMP {threads} threads")
+    line = {
+        "impl": "reference", "metric": "decode tok/s (b=1)", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+        "data": "synthetic", "config": {"workload": WORKLOAD, "runs_on": "host CPU"},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    del torch
+
+
+def run_b200(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from ivonar_inference_b200 import B200Decoder, synthetic
+    from ivonar_inference_b200 import _native as native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+    tokens = int(args.tokens)
+    model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
+    dec = B200Decoder(model, max_len=512, device=device, sampling=True, seed=1000 + rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+    stream = torch.cuda.current_stream(device)
+
+    def barrier() -> None:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(device)
+
+    # ---- device-timed decode (prompt already prefilled in HBM) --------------------------------
+    step_ms = []
+    clocks = None
+    for step in range(args.warmup + args.steps):
+        prompt = synthetic.random_prompt(32768, PROMPT, seed=10_000 * rank + step)
+        dec.prefill(prompt)
+        dec.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
+        dec.sample()
+        flush.zero_()
+        if step == args.warmup:
+            barrier()
+            clocks = ClockSampler(local, enabled=not args.no_clocks and rank == 0)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        dec._launch(tokens, None, native.IVB_RUN_SAMPLE)
+        end.record(stream)
+        dec._check()
+        if step >= args.warmup:
+            step_ms.append(start.elapsed_time(end))
+    barrier()
+    clock_info = clocks.stop() if clocks is not None else None
+    total_ms = torch.tensor([sum(step_ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(total_ms, op=dist.ReduceOp.MAX)
+    max_ms = float(total_ms.item())
+    value = world * args.steps * tokens / (max_ms / 1000.0)
+
+    # ---- end to end through the public API with host buffers ----------------------------------
+    dec.capture()
+    e2e_ms = []
+    h2d = d2h = 0
+    for step in range(args.warmup + args.steps):
+        prompt = synthetic.random_prompt(32768, PROMPT, seed=20_000 * rank + step).pin_memory()
+        flush.zero_()
+        barrier()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        dec.prefill(prompt)
+        dec.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
+        produced = [dec.sample()]
+        while len(produced) < tokens + 1:
+            produced += dec.advance_many(min(dec.burst_size, tokens + 1 - len(produced)))
+        end.record(stream)
+        torch.cuda.synchronize(device)
+        if step >= args.warmup:
+            e2e_ms.append(start.elapsed_time(end))
+        bursts = -(-tokens // max(dec.burst_size, 1))
+        h2d = prompt.numel() * prompt.element_size()
+        d2h = 8 * (tokens + 1) + 4 * (bursts + 2)
+    e2e_total = torch.tensor([sum(e2e_ms)], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
+    e2e_value = world * args.steps * tokens / (float(e2e_total.item()) / 1000.0)
+
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        nbytes, parts = decode_bytes(model, PROMPT + 1, tokens)
+        launch_s = (sum(step_ms) / len(step_ms)) / 1000.0
+        achieved = nbytes / launch_s / 1e9
+        roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                    "traffic": None, "peak_source": peak_kind, "kernel": "ivb::decode_kernel",
+                    "algorithmic_bytes_per_launch": nbytes, **parts}
+        line = {
+            "metric": "decode tok/s (b=1)", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "l2": "flushed (256 MB write) before every step", "parallelism": f"dp{world}",
+                       "ctas": dec.ctas, "phases_per_token": dec.num_phases},
+            "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": args.steps,
+            "roofline": roofline,
+            "clocks": clock_info,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            prompt = synthetic.random_prompt(32768, PROMPT, seed=99)[0].numpy()
+            line["cpu_baseline"] = cpu_baseline(model, prompt, 32)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_b200(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,180 @@
+/*
+ * ivonar_b200.h — C ABI of libivonar_b200.so, the sm_100a implementation of the
+ * Ivonar ternary token loop (decode step, prompt prefill, sampler).
+ *
+ * Every pointer named "device" is CUDA device memory owned by the caller (the
+ * Python host allocates it with torch). Streams are passed as `void*` holding a
+ * cudaStream_t. Every entry point returns 0 on success or an IVB_E* code; the
+ * message of the last failure on the calling thread is ivb_last_error().
+ * Nothing here allocates device memory: the decoder asks for a workspace size
+ * and the caller hands in the buffer.
+ *
+ * Weight format (unchanged from the reference checkpoint, q2_g128):
+ *   packed [rows][row_bytes] uint8: input 4j+f sits in bits 2f..2f+1 of byte j,
+ *          code = ternary value + 1 in {0,1,2}; row_bytes = ceil(in/4) padded to 16.
+ *   scales [rows][scale_stride] fp16: one positive scale per 128 inputs.
+ *   bias   [rows] fp32 or NULL.
+ * Reference: src/ivonar_inference/quantization.py:13-32 (unpack/dequantize),
+ * kernel_decoder.py:84-142 (Matrix: row concatenation/interleave, 16-byte rows).
+ */
+#ifndef IVONAR_B200_H
+#define IVONAR_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define IVB_ABI_VERSION 1
+
+enum {
+  IVB_OK = 0,
+  IVB_EINVAL = 1,       /* bad argument or unsupported shape */
+  IVB_ECUDA = 2,        /* a CUDA runtime call failed */
+  IVB_ETIMEOUT = 3,     /* a bounded inter-CTA wait ran out (device error word) */
+  IVB_ECAPACITY = 4,    /* the decoder has no free position left */
+  IVB_EUNSUPPORTED = 5  /* the device cannot run this build (not sm_100) */
+};
+
+/* GEMV epilogues (reference ternary.cu:53 EPI_STORE / EPI_RESIDUAL / EPI_SILU_PAIR). */
+enum { IVB_EPI_STORE = 0, IVB_EPI_RESIDUAL = 1, IVB_EPI_SILU_PAIR = 2 };
+
+/* Mixer kinds (reference config.py layer_types "mamba" / "mla"). */
+enum { IVB_MAMBA = 0, IVB_MLA = 1 };
+
+/* decode run flags */
+enum {
+  IVB_RUN_SAMPLE = 1,       /* sample a token after every step (reference StaticDecoder._step + _sample) */
+  IVB_RUN_SAMPLE_ONLY = 2,  /* sample from the current logits without a step (reference StaticDecoder.sample) */
+  IVB_RUN_HEAD_ALL = 4      /* compute logits on every fed step, not only the last one */
+};
+
+/* One ternary projection (or a row-stack of several) in device memory. */
+typedef struct IvbTernary {
+  const uint8_t* packed;
+  const uint16_t* scales;
+  const float* bias;
+  int32_t rows;
+  int32_t in_features;
+  int32_t row_bytes;
+  int32_t scale_stride;
+} IvbTernary;
+
+/* One residual block. Reference: model.py:32-35 (IvonarBlock.forward),
+ * recurrent.py:41-139 (RecurrentMixer), attention.py:75-151 (LatentAttention). */
+typedef struct IvbLayerDesc {
+  int32_t kind;               /* IVB_MAMBA or IVB_MLA */
+  const float* mixer_norm;    /* [hidden] RMSNorm weight */
+  float mixer_norm_eps;
+  const float* ffn_norm;      /* [hidden] */
+  float ffn_norm_eps;
+  IvbTernary entry;           /* mamba: [in_proj ; bc_dt_proj]   mla: [q_proj ; kv_down_proj ; k_rope_proj] */
+  IvbTernary out;             /* out_proj */
+  IvbTernary gate_up;         /* gate_proj and up_proj rows interleaved (2r = gate r, 2r+1 = up r) */
+  IvbTernary down;            /* down_proj */
+  /* mamba (RecurrentMixer) */
+  const float* decay;         /* [heads, state] = -softplus(log_decay) */
+  const float* theta;         /* [heads, state] */
+  const float* skip;          /* [heads * head_dim] */
+  const float* conv_weight;   /* [hidden, conv_taps] */
+  const float* conv_bias;     /* [hidden] */
+  float* ssm_state;           /* [heads, state, head_dim, 2] fp32 (complex) */
+  float* prev_force;          /* [heads, state, head_dim] */
+  float* conv_state;          /* [hidden, conv_taps - 1] */
+  int32_t conv_taps;
+  float half_dt_min;          /* 0.5 * dt_min */
+  float half_dt_range;        /* 0.5 * (dt_max - dt_min) */
+  /* mla (LatentAttention) over the compressed latent cache */
+  IvbTernary k_nope_up;       /* [heads * nope, latent] (absorbed into the query) */
+  IvbTernary v_up;            /* [hidden, latent]       (applied after the softmax) */
+  const float* rope;          /* [max_len, rope_dim / 2, 2] (cos, sin) */
+  int8_t* latent_q;           /* cache [max_len, latent] int8 codes of the quantised latent */
+  float* latent_scale;        /* cache [max_len] per-position activation scale */
+  uint16_t* k_rope_cache;     /* cache [max_len, heads, rope_dim] fp16 rotated k_rope */
+  float attn_scale;           /* 1 / sqrt(head_dim) */
+} IvbLayerDesc;
+
+/* The whole model plus the decoder state buffers. Reference: kernel_decoder.py:179-283. */
+typedef struct IvbModelDesc {
+  int32_t abi_version;        /* IVB_ABI_VERSION */
+  int32_t vocab, hidden, heads, head_dim, state_dim, latent_dim, rope_dim, nope_dim, dense;
+  int32_t num_layers, max_len, max_top_k;
+  float act_eps;              /* activation quantiser floor (TernaryLinear eps, 1e-5) */
+  float norm_clip;            /* RMSNorm clip (8.0) */
+  IvbTernary head;            /* tied token embedding / LM head [vocab, hidden] */
+  const float* final_norm;
+  float final_norm_eps;
+  const IvbLayerDesc* layers; /* host array [num_layers] */
+  /* state (device) */
+  float* logits;              /* [vocab] */
+  int64_t* token;             /* [1] last fed or sampled token */
+  int64_t* position;          /* [1] next cache slot */
+  uint8_t* seen;              /* [vocab] repetition-penalty flags (torch.bool) */
+  int64_t* history;           /* [history_len] tokens sampled by the last run */
+  int32_t history_len;
+  const float* sampling;      /* [3] temperature, penalty, inverse_penalty */
+  const int64_t* top_k;       /* [1] */
+  uint64_t* rng;              /* [2] philox key (seed), draw counter */
+} IvbModelDesc;
+
+typedef struct IvbDecoder IvbDecoder; /* host-side plan; opaque */
+
+/* ---- library ---------------------------------------------------------------------------------- */
+int32_t ivb_abi_version(void);
+const char* ivb_last_error(void);
+/* 1 when the current CUDA device is an sm_100 part this build runs on. */
+int32_t ivb_device_supported(void);
+
+/* ---- unit entry points (each one a single kernel launch) ------------------------------------- */
+
+/* Per-token int8 activation quantiser with optional fused RMSNorm (clip, then weight).
+ * Replaces ternary.cu:148-197 quantize_source and quantization.py:35-38 quantize_activations.
+ * q8 [n] natural order, *scale = max(amax/127, act_eps), xsum [ceil(n/64)] chunk sums (may be NULL). */
+int32_t ivb_quantize(const float* x, const float* norm_weight, int32_t n, float norm_eps, float norm_clip,
+                     float act_eps, int8_t* q8, float* scale, int32_t* xsum, void* stream);
+
+/* Exact integer core of the ternary GEMV: dots[r][g] = sum over the 128 inputs of group g of
+ * (code-1) * q8. Replaces the integer part of ternary.cu:241-258 chunk_dot (dot - xsum). */
+int32_t ivb_ternary_group_dots(const IvbTernary* m, const int8_t* q8, int32_t* dots, void* stream);
+
+/* Fused (RMSNorm +) quantise + ternary GEMV + epilogue, one launch over all rows.
+ * norm_weight == NULL: plain quantisation. Replaces ternary.cu:356-388 gemv_* entry points. */
+int32_t ivb_ternary_gemv(const IvbTernary* m, const float* x, const float* norm_weight, float norm_eps,
+                         float norm_clip, float act_eps, int32_t epilogue, float* out, void* stream);
+
+/* Sampler over one logits row: temperature, repetition penalty, exact top-k, softmax and an
+ * inverse-CDF draw with a Philox4x32-10 uniform (key rng[0], counter rng[1]++).
+ * Replaces ternary.cu:1064-1337 logit_bounds + sample_token. token/history: int64 [1] each. */
+int32_t ivb_sample(const float* logits, uint8_t* seen, int32_t vocab, const float* sampling,
+                   const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* token, int64_t* history,
+                   void* stream);
+
+/* Debug/failure-detection probe: one CTA waits for a barrier count that never arrives, with a
+ * bounded spin of timeout_ns; returns IVB_ETIMEOUT and leaves the context usable. */
+int32_t ivb_probe_wait_timeout(uint32_t* counter, uint32_t* error_word, uint64_t timeout_ns, void* stream);
+
+/* ---- persistent decoder ----------------------------------------------------------------------- */
+/* Replaces kernel_decoder.py KernelDecoder._build/_step/_capture_burst/advance_many: one persistent
+ * cooperative kernel runs every layer, the head and the sampler for `steps` tokens per launch. */
+int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** out);
+void ivb_decoder_destroy(IvbDecoder* dec);
+uint64_t ivb_decoder_workspace_bytes(const IvbDecoder* dec);
+int32_t ivb_decoder_num_phases(const IvbDecoder* dec);
+int32_t ivb_decoder_ctas(const IvbDecoder* dec);
+/* Uploads the phase program into the caller's workspace (device, >= workspace_bytes, 256-aligned). */
+int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream);
+/* Run `steps` tokens. feed == NULL: each step consumes the token sampled by the previous one
+ * (requires IVB_RUN_SAMPLE). feed != NULL: device int64 [steps] teacher-forced tokens.
+ * timeout_ns bounds every inter-CTA wait (0 = 1 s). Asynchronous; errors surface through
+ * ivb_decoder_check. */
+int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int32_t flags, uint64_t timeout_ns,
+                        void* stream);
+/* Synchronises the stream and returns IVB_ETIMEOUT/IVB_ECAPACITY if the device error word is set. */
+int32_t ivb_decoder_check(IvbDecoder* dec, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* IVONAR_B200_H */

@@ -1,0 +1,37 @@
+// Host-side helpers shared by the translation units of libivonar_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdint>
+#include <cstdio>
+
+#include "ivonar_b200.h"
+
+namespace ivb {
+
+// Records the message returned by ivb_last_error() on this thread; returns `code`.
+int32_t fail(int32_t code, const char* fmt, ...);
+
+// Maps a CUDA error to IVB_ECUDA with the call site in the message.
+inline int32_t cuda_fail(cudaError_t err, const char* what) {
+  return fail(IVB_ECUDA, "%s: %s (%s)", what, cudaGetErrorString(err), cudaGetErrorName(err));
+}
+
+#define IVB_CUDA(call)                                     \
+  do {                                                     \
+    cudaError_t ivb_err_ = (call);                         \
+    if (ivb_err_ != cudaSuccess) return ivb::cuda_fail(ivb_err_, #call); \
+  } while (0)
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Checks the layout contract of one ternary matrix (row_bytes 16-aligned and wide enough,
+// scale_stride covers ceil(in/128) groups, 16-byte aligned base pointer).
+int32_t check_ternary(const IvbTernary& m, const char* name);
+
+// True when the current device is compute capability 10.0 (B200 / sm_100a).
+bool device_is_sm100();
+
+}  // namespace ivb

@@ -1,0 +1,539 @@
+"""B200Decoder: the reference decoder interface over the sm_100a persistent decode kernel.
+
+Drop-in for ``ivonar_inference.kernel_decoder.KernelDecoder`` behind ``build_decoder``
+(reference src/ivonar_inference/decoder.py:61-466 for the interface, 479-529 for the dispatch):
+same constructor arguments, attributes (device, max_len, batch_size, burst_size, position,
+host_position, logits, token, seen, graph, graphs, attention_lengths) and methods (prefill, step,
+configure_sampling, sample, advance, advance_many, capture, reset, self_check, attention_length),
+same errors (ValueError "capacity" / "no free position left", RuntimeError without sampling).
+
+The model can be the reference ``IvonarModel`` or this package's ``PackedModel``; only their
+packed tensors are read. Weights stay in the q2_g128 format; rows are stacked per fused projection
+(entry, gate/up interleaved) and padded to 16-byte rows, as the reference Matrix does
+(kernel_decoder.py:84-142). The attention cache is the compressed latent (int8 codes + scale per
+position, fp16 rotated k_rope) instead of the reference's decompressed fp16 K/V.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from collections.abc import Iterable
+
+import torch
+import torch.nn.functional as F
+from torch import Tensor
+
+from . import _native as native
+from ._native import KernelError
+from .model import rope_table
+
+BURST = 16
+SELF_CHECK_TOLERANCE = 0.25
+DEFAULT_TIMEOUT_NS = 2_000_000_000
+
+
+def _pad_rows(packed: Tensor) -> Tensor:
+    row_bytes = int(packed.shape[1])
+    padded = (row_bytes + 15) // 16 * 16
+    return F.pad(packed, (0, padded - row_bytes)) if padded != row_bytes else packed
+
+
+def _stack(tensors: list[Tensor], interleave: bool) -> Tensor:
+    if len(tensors) == 1:
+        return tensors[0]
+    if interleave:
+        return torch.stack(tensors, dim=1).reshape(-1, *tensors[0].shape[1:])
+    return torch.cat(tensors, dim=0)
+
+
+class DeviceMatrix:
+    """A row-stack of packed projections on the device, in the layout the kernels read."""
+
+    def __init__(self, projections: list, device: torch.device, interleave: bool = False) -> None:
+        first = projections[0]
+        self.in_features = int(first.in_features)
+        for proj in projections:
+            if int(proj.in_features) != self.in_features:
+                raise KernelError("fused projections must share their input width")
+            if int(getattr(proj, "group_size", 128)) != 128:
+                raise KernelError("ternary kernels need group size 128")
+            if proj.weight_scales.dtype != torch.float16:
+                raise KernelError("ternary kernels need float16 group scales")
+            if interleave and int(proj.out_features) != int(first.out_features):
+                raise KernelError("interleaved projections must share their output width")
+        packed = _stack([p.packed_weight.to(device) for p in projections], interleave)
+        self.packed = _pad_rows(packed).contiguous()
+        self.scales = _stack([p.weight_scales.to(device) for p in projections], interleave).contiguous()
+        biases = [p.bias for p in projections]
+        if all(b is None for b in biases):
+            self.bias = None
+        else:
+            filled = [torch.zeros(int(p.out_features)) if b is None else b.float() for p, b in zip(projections, biases)]
+            self.bias = _stack([b.to(device) for b in filled], interleave).contiguous()
+        self.rows = int(self.packed.shape[0])
+
+    def desc(self) -> native.IvbTernary:
+        return native.ternary(self.packed, self.scales, self.bias, self.rows, self.in_features)
+
+    @property
+    def nbytes(self) -> int:
+        return self.packed.numel() + self.scales.numel() * 2 + (0 if self.bias is None else self.bias.numel() * 4)
+
+
+class B200Decoder:
+    """Batch-1 decoder whose whole token step is one persistent sm_100a kernel launch."""
+
+    backend_name = "ternary-b200"
+
+    def __init__(
+        self,
+        model,
+        max_len: int | None = None,
+        device: str | torch.device | None = None,
+        sampling: bool = False,
+        max_top_k: int = 256,
+        ctas: int = 0,
+        seed: int | None = None,
+        timeout_ns: int = DEFAULT_TIMEOUT_NS,
+    ) -> None:
+        target = model.device if device is None else torch.device(device)
+        if target.type != "cuda":
+            raise KernelError("ternary kernels need a CUDA device")
+        if target.index is None:
+            target = torch.device("cuda", torch.cuda.current_device())
+        if max_top_k <= 0:
+            raise ValueError("max_top_k must be positive")
+        self.lib = native.library()
+        self.model = model
+        self.device = target
+        config = model.config
+        self.max_len = int(config.seq_len if max_len is None else max_len)
+        if self.max_len <= 0 or self.max_len > int(config.seq_len):
+            raise ValueError("max_len must lie within the model context")
+        with torch.cuda.device(target):
+            if not self.lib.ivb_device_supported():
+                raise KernelError(f"{torch.cuda.get_device_name(target)} is not an sm_100 GPU this build runs on")
+        self.batch_size = 1
+        self.sampling = bool(sampling)
+        vocab = int(config.vocab_size)
+        self.vocab = vocab
+        self.max_top_k = min(int(max_top_k), vocab)
+        self.attention_lengths = (self.max_len,)
+        self.host_position = 0
+        self.burst_size = 1
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self._burst_graph: torch.cuda.CUDAGraph | None = None
+        self.timeout_ns = int(timeout_ns)
+        dev = target
+        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.position = torch.zeros(1, dtype=torch.int64, device=dev)
+        self.logits = torch.zeros(1, vocab, dtype=torch.float32, device=dev)
+        self.seen = torch.zeros(1, vocab, dtype=torch.bool, device=dev)
+        self._sampling = torch.ones(3, dtype=torch.float32, device=dev)
+        self.temperature = self._sampling[0:1]
+        self.penalty = self._sampling[1:2]
+        self.inverse_penalty = self._sampling[2:3]
+        self.top_k = torch.full((1,), self.max_top_k, dtype=torch.int64, device=dev)
+        self.history = torch.zeros(max(self.max_len, BURST), dtype=torch.int64, device=dev)
+        if seed is None:
+            seed = int(torch.randint(0, 2**62, (1,)).item())
+        self.rng = torch.tensor([int(seed), 0], dtype=torch.int64, device=dev)
+        self._build(model, dev)
+
+    # ------------------------------------------------------------------------------------------
+    def _build(self, model, dev: torch.device) -> None:
+        config = model.config
+        hidden, heads = int(config.hidden_dim), int(config.num_heads)
+        head_dim = hidden // heads
+        self.head = DeviceMatrix([model.token_io.projection], dev)
+        self.final_norm = model.final_norm.weight.float().to(dev).contiguous()
+        self.layer_matrices: list[dict[str, DeviceMatrix]] = []
+        self.recurrent_states: dict[int, dict[str, Tensor]] = {}
+        self.latent_caches: dict[int, tuple[Tensor, Tensor, Tensor]] = {}
+        self._keep: list[Tensor] = []
+        layers = (native.IvbLayerDesc * len(model.blocks))()
+        dims = {"state": int(config.state_dim), "latent": int(config.latent_dim), "rope": 2, "nope": head_dim - 2}
+        clip = 8.0
+        for index, block in enumerate(model.blocks):
+            mixer = block.mixer
+            kind = getattr(block, "mixer_type", None)
+            desc = layers[index]
+            mats: dict[str, DeviceMatrix] = {}
+            norm_m = block.mixer_norm.weight.float().to(dev).contiguous()
+            norm_f = block.ffn_norm.weight.float().to(dev).contiguous()
+            self._keep += [norm_m, norm_f]
+            clip = float(getattr(block.mixer_norm, "clip", 8.0))
+            desc.mixer_norm = norm_m.data_ptr()
+            desc.mixer_norm_eps = float(block.mixer_norm.eps)
+            desc.ffn_norm = norm_f.data_ptr()
+            desc.ffn_norm_eps = float(block.ffn_norm.eps)
+            if kind == "mamba":
+                desc.kind = native.IVB_MAMBA
+                mats["entry"] = DeviceMatrix([mixer.in_proj, mixer.bc_dt_proj], dev)
+                mats["out"] = DeviceMatrix([mixer.out_proj], dev)
+                taps = int(mixer.conv_kernel_size)
+                consts = {
+                    "decay": (-F.softplus(mixer.log_decay.float())).contiguous(),
+                    "theta": mixer.theta.float().contiguous(),
+                    "skip": mixer.skip.float().reshape(-1).contiguous(),
+                    "conv_weight": mixer.conv_weight.float().reshape(hidden, taps).contiguous(),
+                    "conv_bias": mixer.conv_bias.float().contiguous(),
+                }
+                consts = {k: v.to(dev) for k, v in consts.items()}
+                self._keep += list(consts.values())
+                state = {
+                    "ssm_state": torch.zeros(1, mixer.num_heads, mixer.state_dim, mixer.head_dim, 2, device=dev),
+                    "prev_force": torch.zeros(1, mixer.num_heads, mixer.state_dim, mixer.head_dim, device=dev),
+                    "conv_state": torch.zeros(1, hidden, max(taps - 1, 1), device=dev),
+                }
+                self.recurrent_states[index] = state
+                for key in ("decay", "theta", "skip", "conv_weight", "conv_bias"):
+                    setattr(desc, key, consts[key].data_ptr())
+                desc.ssm_state = state["ssm_state"].data_ptr()
+                desc.prev_force = state["prev_force"].data_ptr()
+                desc.conv_state = state["conv_state"].data_ptr()
+                desc.conv_taps = taps
+                desc.half_dt_min = 0.5 * float(mixer.dt_min)
+                desc.half_dt_range = 0.5 * (float(mixer.dt_max) - float(mixer.dt_min))
+                dims["state"] = int(mixer.state_dim)
+            elif kind == "mla":
+                desc.kind = native.IVB_MLA
+                mats["entry"] = DeviceMatrix([mixer.q_proj, mixer.kv_down_proj, mixer.k_rope_proj], dev)
+                mats["out"] = DeviceMatrix([mixer.out_proj], dev)
+                mats["k_nope_up"] = DeviceMatrix([mixer.k_nope_up_proj], dev)
+                mats["v_up"] = DeviceMatrix([mixer.v_up_proj], dev)
+                rope = rope_table(mixer.rope, self.max_len).to(dev)
+                latent_q = torch.zeros(self.max_len, mixer.latent_dim, dtype=torch.int8, device=dev)
+                latent_scale = torch.zeros(self.max_len, dtype=torch.float32, device=dev)
+                k_rope = torch.zeros(self.max_len, mixer.num_heads, mixer.rope_dim, dtype=torch.float16, device=dev)
+                self._keep.append(rope)
+                self.latent_caches[index] = (latent_q, latent_scale, k_rope)
+                desc.k_nope_up = mats["k_nope_up"].desc()
+                desc.v_up = mats["v_up"].desc()
+                desc.rope = rope.data_ptr()
+                desc.latent_q = latent_q.data_ptr()
+                desc.latent_scale = latent_scale.data_ptr()
+                desc.k_rope_cache = k_rope.data_ptr()
+                desc.attn_scale = 1.0 / math.sqrt(mixer.head_dim)
+                dims.update(latent=int(mixer.latent_dim), rope=int(mixer.rope_dim), nope=int(mixer.nope_dim))
+            else:
+                raise KernelError(f"unsupported mixer for the B200 kernels: {type(mixer).__name__}")
+            mats["gate_up"] = DeviceMatrix([block.ffn.gate_proj, block.ffn.up_proj], dev, interleave=True)
+            mats["down"] = DeviceMatrix([block.ffn.down_proj], dev)
+            desc.entry = mats["entry"].desc()
+            desc.out = mats["out"].desc()
+            desc.gate_up = mats["gate_up"].desc()
+            desc.down = mats["down"].desc()
+            self.layer_matrices.append(mats)
+        self._layers = layers
+        md = native.IvbModelDesc()
+        md.abi_version = native.IVB_ABI_VERSION
+        md.vocab = self.vocab
+        md.hidden = hidden
+        md.heads = heads
+        md.head_dim = head_dim
+        md.state_dim = dims["state"]
+        md.latent_dim = dims["latent"]
+        md.rope_dim = dims["rope"]
+        md.nope_dim = dims["nope"]
+        md.dense = int(config.dense_dim)
+        md.num_layers = len(model.blocks)
+        md.max_len = self.max_len
+        md.max_top_k = self.max_top_k
+        md.act_eps = float(getattr(model.token_io.projection, "eps", 1e-5))
+        md.norm_clip = clip
+        md.head = self.head.desc()
+        md.final_norm = self.final_norm.data_ptr()
+        md.final_norm_eps = float(model.final_norm.eps)
+        md.layers = ctypes.cast(layers, ctypes.POINTER(native.IvbLayerDesc))
+        md.logits = self.logits.data_ptr()
+        md.token = self.token.data_ptr()
+        md.position = self.position.data_ptr()
+        md.seen = self.seen.data_ptr()
+        md.history = self.history.data_ptr()
+        md.history_len = int(self.history.numel())
+        md.sampling = self._sampling.data_ptr()
+        md.top_k = self.top_k.data_ptr()
+        md.rng = self.rng.data_ptr()
+        self._desc = md
+        handle = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            native.check(self.lib.ivb_decoder_create(ctypes.byref(md), 0, ctypes.byref(handle)), "ivb_decoder_create")
+            self._plan = handle
+            self.workspace = torch.zeros(int(self.lib.ivb_decoder_workspace_bytes(handle)), dtype=torch.uint8, device=dev)
+            native.check(self.lib.ivb_decoder_bind(handle, self.workspace.data_ptr(), self._stream()), "ivb_decoder_bind")
+        self.ctas = int(self.lib.ivb_decoder_ctas(handle))
+        self.num_phases = int(self.lib.ivb_decoder_num_phases(handle))
+
+    def __del__(self) -> None:
+        plan = getattr(self, "_plan", None)
+        lib = getattr(self, "lib", None)
+        if plan is not None and lib is not None:
+            try:
+                lib.ivb_decoder_destroy(plan)
+            except Exception:
+                pass
+            self._plan = None
+
+    # ------------------------------------------------------------------------------------------
+    def _stream(self) -> int:
+        return torch.cuda.current_stream(self.device).cuda_stream
+
+    def _launch(self, steps: int, feed: Tensor | None, flags: int) -> None:
+        with torch.cuda.device(self.device):
+            rc = self.lib.ivb_decoder_run(
+                self._plan, int(steps), 0 if feed is None else feed.data_ptr(), int(flags), self.timeout_ns, self._stream()
+            )
+            native.check(rc, "ivb_decoder_run")
+
+    def _check(self) -> None:
+        with torch.cuda.device(self.device):
+            native.check(self.lib.ivb_decoder_check(self._plan, self._stream()), "decode kernel")
+
+    @property
+    def weight_bytes(self) -> int:
+        total = self.head.nbytes
+        for mats in self.layer_matrices:
+            total += sum(m.nbytes for m in mats.values())
+        return total
+
+    @property
+    def tile_prefill(self) -> bool:
+        return True
+
+    @property
+    def persisted_bytes(self) -> int:
+        return 0
+
+    @property
+    def graph(self) -> torch.cuda.CUDAGraph | None:
+        return self.graphs.get(self.max_len)
+
+    def attention_length(self, position: int) -> int:
+        if position < self.max_len:
+            return self.max_len
+        raise ValueError("the decoder has no free position left")
+
+    # ------------------------------------------------------------------------------------------
+    @torch.no_grad()
+    def prefill(self, input_ids: Tensor) -> Tensor:
+        """Run the prompt (teacher-forced through the persistent kernel) and return its last logits."""
+
+        if input_ids.ndim != 2 or input_ids.shape[0] != self.batch_size:
+            raise ValueError(f"input_ids must have shape [{self.batch_size}, seq_len]")
+        length = int(input_ids.shape[1])
+        if length == 0 or length > self.max_len:
+            raise ValueError("prompt length must lie within the decoder capacity")
+        if input_ids.device.type == "cpu" and input_ids.numel():
+            low, high = int(input_ids.min()), int(input_ids.max())
+            if low < 0 or high >= self.vocab:
+                raise IndexError(f"token id is out of range for vocab_size={self.vocab}")
+        ids = input_ids[0].to(device=self.device, dtype=torch.int64).contiguous()
+        for state in self.recurrent_states.values():
+            for buffer in state.values():
+                buffer.zero_()
+        self.position.zero_()
+        self.host_position = 0
+        self._feed = ids
+        self._launch(length, ids, 0)
+        self._check()
+        self.host_position = length
+        return self.logits
+
+    @torch.no_grad()
+    def step(self, token: Tensor) -> Tensor:
+        """Feed one token and return the next logits (samples too when the decoder samples)."""
+
+        if token.ndim == 2:
+            token = token[:, 0]
+        if token.shape != (self.batch_size,):
+            raise ValueError(f"token must have shape [{self.batch_size}]")
+        self.attention_length(self.host_position)
+        self.token.copy_(token.to(device=self.device, dtype=torch.int64))
+        graph = self.graphs.get(self.max_len)
+        if graph is not None:
+            graph.replay()
+        else:
+            self._launch(1, self.token, native.IVB_RUN_SAMPLE if self.sampling else 0)
+        self._check()
+        self.host_position += 1
+        return self.logits
+
+    def configure_sampling(self, temperature: float, top_k: int, repetition_penalty: float = 1.0,
+                           penalized_ids: Iterable[int] = ()) -> None:
+        """Set the sampling rule for the answer that starts now (reference decoder.py:335-361)."""
+
+        if not self.sampling:
+            raise RuntimeError("this decoder was created without sampling")
+        if temperature <= 0 or repetition_penalty <= 0:
+            raise ValueError("temperature and repetition_penalty must be positive")
+        effective = int(top_k) if 0 < int(top_k) <= self.max_top_k else self.max_top_k
+        self.temperature.fill_(float(temperature))
+        self.penalty.fill_(float(repetition_penalty))
+        self.inverse_penalty.fill_(1.0 / float(repetition_penalty))
+        self.top_k.fill_(effective)
+        self.seen.zero_()
+        seeds = [int(t) for t in penalized_ids if 0 <= int(t) < self.seen.shape[1]]
+        if seeds:
+            index = torch.tensor(sorted(set(seeds)), dtype=torch.int64, device=self.device)
+            self.seen.index_fill_(1, index, True)
+
+    @torch.no_grad()
+    def sample(self) -> int:
+        """Sample from the logits the last prefill or step produced."""
+
+        if not self.sampling:
+            raise RuntimeError("this decoder was created without sampling")
+        self._launch(0, None, native.IVB_RUN_SAMPLE_ONLY)
+        self._check()
+        return int(self.token[0])
+
+    @torch.no_grad()
+    def advance(self) -> int:
+        """Feed the sampled token, run one step and return the token sampled from it."""
+
+        if not self.sampling:
+            raise RuntimeError("this decoder was created without sampling")
+        return self.advance_many(1)[0]
+
+    @torch.no_grad()
+    def advance_many(self, count: int) -> list[int]:
+        """Produce ``count`` tokens, each fed back into the next step, in one kernel launch."""
+
+        if not self.sampling:
+            raise RuntimeError("this decoder was created without sampling")
+        count = int(count)
+        if count <= 0:
+            return []
+        room = self.max_len - self.host_position
+        run = min(count, room)
+        tokens: list[int] = []
+        if run > 0:
+            if run == BURST and self._burst_graph is not None:
+                self._burst_graph.replay()
+            else:
+                self._launch(run, None, native.IVB_RUN_SAMPLE)
+            self._check()
+            tokens = self.history[:run].tolist()
+            self.host_position += run
+        if run < count:
+            self.attention_length(self.host_position)
+        return tokens
+
+    @torch.no_grad()
+    def capture(self, warmup_steps: int = 2) -> bool:
+        """Record the one-step launch (and the 16-token burst when sampling) as CUDA graphs."""
+
+        if self.device.type != "cuda" or not torch.cuda.is_available():
+            return False
+        saved_position = int(self.position)
+        saved_token = self.token.clone()
+        saved_rng = self.rng.clone()
+        saved_seen = self.seen.clone()
+        saved_states = {i: {k: v.clone() for k, v in s.items()} for i, s in self.recurrent_states.items()}
+        graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        burst = None
+        flags = native.IVB_RUN_SAMPLE if self.sampling else 0
+        try:
+            stream = torch.cuda.Stream(device=self.device)
+            stream.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(stream):
+                for _ in range(max(1, warmup_steps)):
+                    self.position.zero_()
+                    self._launch(1, self.token, flags)
+                torch.cuda.synchronize(self.device)
+                graph = torch.cuda.CUDAGraph()
+                self.position.zero_()
+                with torch.cuda.graph(graph, stream=stream):
+                    self._launch(1, self.token, flags)
+                graphs[self.max_len] = graph
+                if self.sampling and self.max_len >= BURST:
+                    self.position.zero_()
+                    self._launch(BURST, None, flags)
+                    torch.cuda.synchronize(self.device)
+                    burst = torch.cuda.CUDAGraph()
+                    self.position.zero_()
+                    with torch.cuda.graph(burst, stream=stream):
+                        self._launch(BURST, None, flags)
+            torch.cuda.synchronize(self.device)
+            self._check()
+        except Exception:
+            graphs = {}
+            burst = None
+        self.graphs = graphs
+        self._burst_graph = burst
+        self.burst_size = BURST if burst is not None else 1
+        self.position.fill_(saved_position)
+        self.token.copy_(saved_token)
+        self.rng.copy_(saved_rng)
+        self.seen.copy_(saved_seen)
+        for i, state in saved_states.items():
+            for key, value in state.items():
+                self.recurrent_states[i][key].copy_(value)
+        return bool(graphs)
+
+    @torch.no_grad()
+    def self_check(self) -> None:
+        """Prefill a prompt whole and token by token; both must agree (reference kernel_decoder.py:525-549)."""
+
+        vocab = self.vocab
+        length = min(32 + 16 + 1, self.max_len)
+        ids = torch.randint(2, vocab, (1, length), generator=torch.Generator().manual_seed(0))
+        whole = self.prefill(ids).clone()
+        self.prefill(ids[:, :1])
+        for index in range(1, length):
+            self.step(ids[:, index])
+        stepped = self.logits.clone()
+        sampled = int(self.token[0])
+        self.reset()
+        scale = float(whole.norm())
+        if not (bool(torch.isfinite(whole).all()) and bool(torch.isfinite(stepped).all())) or scale == 0.0:
+            raise KernelError("the B200 kernels produced invalid numbers on this GPU")
+        difference = float((whole - stepped).norm()) / scale
+        if difference > SELF_CHECK_TOLERANCE:
+            raise KernelError(f"the B200 kernels disagree with themselves on this GPU ({difference:.1e})")
+        if not 0 <= sampled < vocab:
+            raise KernelError("the B200 sampler returned an invalid token on this GPU")
+
+    def reset(self) -> None:
+        self.position.zero_()
+        self.host_position = 0
+        self.seen.zero_()
+
+
+def _reference_static_decoder():
+    try:
+        from ivonar_inference.decoder import StaticDecoder  # type: ignore
+
+        return StaticDecoder
+    except Exception:
+        return None
+
+
+def build_decoder(model, device: str | torch.device, sampling: bool = False, max_top_k: int = 256,
+                  kernels: bool = True) -> tuple[object, str, str | None]:
+    """The decoder the engine serves: the B200 kernels where they run (reference decoder.py:479-507).
+
+    Returns ``(decoder, backend, note)`` with backend "ternary" for the kernel path, as the
+    reference does. When the kernels cannot run, the reference torch decoder is used if the
+    reference package is importable; otherwise the error is raised.
+    """
+
+    target = torch.device(device)
+    note = None
+    if kernels and target.type == "cuda":
+        try:
+            decoder = B200Decoder(model, device=target, sampling=sampling, max_top_k=max_top_k)
+            decoder.self_check()
+            return decoder, "ternary", None
+        except Exception as exc:
+            note = f"B200 ternary kernels unavailable, using the torch decoder: {exc}"
+            fallback = _reference_static_decoder()
+            if fallback is None:
+                raise
+    fallback = _reference_static_decoder()
+    if fallback is None:
+        raise KernelError("no decoder for this device: the B200 kernels need an sm_100 GPU")
+    decoder = fallback(model, device=target, sampling=sampling, max_top_k=max_top_k)
+    return decoder, "torch", note

@@ -1,0 +1,196 @@
+"""The CPU oracle against golden vectors recorded from the reference implementation.
+
+Fixtures come from tests/golden/make_golden.py (reference numba CpuDecoder kernels and the torch
+StaticDecoder, imported unmodified). These tests pin the oracle before it is used to judge the GPU.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+
+
+def test_plain_quantizer_is_bit_exact_with_the_reference(oracle_lib) -> None:
+    g = golden("quantizer")
+    for k in range(int(g["count"])):
+        q, scale, _ = oracle_lib.quantize(g[f"x{k}"])
+        assert np.float32(scale) == g[f"plain_scale{k}"]
+        np.testing.assert_array_equal(q, g[f"plain_q{k}"])
+
+
+def test_norm_quantizer_matches_the_reference_to_one_code(oracle_lib) -> None:
+    # The sum of squares is reduced in a different order than numba's sequential loop, so a code
+    # may move by one step when v / scale sits on a rounding boundary; nothing else may differ.
+    g = golden("quantizer")
+    mismatched = total = 0
+    for k in range(int(g["count"])):
+        q, scale, _ = oracle_lib.quantize(g[f"x{k}"], g[f"w{k}"], 1e-6, 8.0, 1e-5)
+        ref_q, ref_scale = g[f"norm_q{k}"], float(g[f"norm_scale{k}"])
+        assert abs(scale - ref_scale) <= 2e-6 * max(ref_scale, 1e-5)
+        diff = np.abs(q.astype(np.int32) - ref_q.astype(np.int32))
+        assert diff.max() <= 1
+        mismatched += int((diff > 0).sum())
+        total += q.size
+    assert mismatched <= max(2, total // 1000)
+
+
+def test_integer_group_dots_are_bit_exact(oracle_lib) -> None:
+    g = golden("ternary")
+    for k in range(int(g["count"])):
+        m = oracle_lib.Matrix.raw(g[f"packed{k}"], g[f"scales{k}"], int(g[f"in{k}"]), g[f"bias{k}"])
+        dots = m.group_dots(g[f"q8_{k}"])
+        np.testing.assert_array_equal(dots, g[f"dots{k}"])
+
+
+def test_gemv_matches_the_reference_fp32(oracle_lib) -> None:
+    g = golden("ternary")
+    for k in range(int(g["count"])):
+        n = int(g[f"in{k}"])
+        m = oracle_lib.Matrix.raw(g[f"packed{k}"], g[f"scales{k}"], n, g[f"bias{k}"])
+        out = np.zeros(m.rows, np.float32)
+        m.gemv(g[f"q8_{k}"], float(g[f"act_scale{k}"]), out, 0)
+        np.testing.assert_allclose(out, g[f"gemv{k}"], rtol=1e-5, atol=1e-6)
+        q, s, _ = oracle_lib.quantize(g[f"x{k}"], g[f"w{k}"], 1e-6, 8.0, 1e-5)
+        m.gemv(q, s, out, 0)
+        ref = g[f"normed_gemv{k}"]
+        np.testing.assert_allclose(out, ref, rtol=0, atol=2e-2 * float(np.abs(ref).max()) + 1e-6)
+        if f"silu{k}" in g:
+            half = m.rows // 2
+            inter_p = np.stack([g[f"packed{k}"][:half], g[f"packed{k}"][half:]], 1).reshape(m.rows, -1)
+            inter_s = np.stack([g[f"scales{k}"][:half], g[f"scales{k}"][half:]], 1).reshape(m.rows, -1)
+            inter_b = np.stack([g[f"bias{k}"][:half], g[f"bias{k}"][half:]], 1).reshape(-1)
+            pair = oracle_lib.Matrix.raw(inter_p, inter_s, n, inter_b)
+            mid = np.zeros(half, np.float32)
+            pair.gemv(q, s, mid, 2)
+            ref = g[f"silu{k}"]
+            np.testing.assert_allclose(mid, ref, rtol=0, atol=2e-2 * float(np.abs(ref).max()) + 1e-6)
+
+
+def test_recurrent_step_matches_the_reference(oracle_lib) -> None:
+    g = golden("ssm")
+    hidden, heads, state, hd, taps = 128, 4, 16, 32, 4
+    conv_state = np.zeros((hidden, taps - 1), np.float32)
+    ssm = np.zeros((heads, state, hd, 2), np.float32)
+    prev = np.zeros((heads, state, hd), np.float32)
+    L = oracle_lib.lib()
+    p = oracle_lib._p
+    for step in range(4):
+        mix = np.ascontiguousarray(g[f"in{step}"])
+        y = np.zeros(hidden, np.float32)
+        L.orc_ssm_step(p(mix), hidden, heads, state, hd, taps, p(g["conv_taps"]), p(g["conv_bias"]), p(conv_state),
+                       p(g["decay"]), p(g["theta"]), p(np.ascontiguousarray(g["skip"].reshape(-1))), p(ssm), p(prev),
+                       0.5e-3, 0.5 * (0.1 - 1e-3), p(y))
+        np.testing.assert_allclose(y, g[f"y{step}"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(ssm, g["ssm_state"], rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(prev, g["prev_force"], rtol=1e-6, atol=1e-7)
+    np.testing.assert_array_equal(conv_state, g["conv_state"])
+
+
+def test_attention_step_matches_the_reference(oracle_lib) -> None:
+    g = golden("attention")
+    heads, hd, nope, rope, latent, max_len = 4, 32, 16, 16, 64, 8
+    k_cache = np.zeros((heads, max_len, hd), np.float32)
+    v_cache = np.zeros((heads, max_len, hd), np.float32)
+    L = oracle_lib.lib()
+    p = oracle_lib._p
+    table = np.ascontiguousarray(g["rope"])
+    for pos in range(6):
+        y = np.zeros(heads * hd, np.float32)
+        L.orc_attention_step(p(np.ascontiguousarray(g[f"in{pos}"])), p(np.ascontiguousarray(g[f"kv{pos}"])), p(table),
+                             pos, p(k_cache), p(v_cache), max_len, heads, hd, nope, rope, latent,
+                             float(np.float32(1.0 / np.sqrt(hd))), p(y))
+        np.testing.assert_allclose(y, g[f"y{pos}"], rtol=1e-5, atol=1e-6)
+
+
+def test_greedy_sampler_with_penalty_matches_the_reference(oracle_lib) -> None:
+    g = golden("sampler")
+    L = oracle_lib.lib()
+    for k in range(6):
+        logits = np.ascontiguousarray(g[f"logits{k}"])
+        seen = np.zeros(logits.size, np.uint8)
+        seen[g[f"penalized{k}"]] = 1
+        rng = (oracle_lib.c_uint64 * 2)(7, 0)
+        token = L.orc_sample(oracle_lib._p(logits), oracle_lib._p(seen), logits.size, 0.7, 3.0,
+                             float(np.float32(1.0 / 3.0)), 1, 256, rng)
+        assert token == int(g[f"token{k}"])
+        assert seen[token] == 1
+
+
+def test_philox_matches_the_published_known_answers(oracle_lib) -> None:
+    # Random123 kat_vectors for philox4x32-10 (Salmon et al., SC'11).
+    L = oracle_lib.lib()
+    kats = [
+        ([0, 0, 0, 0], [0, 0], [0x6627E8D5, 0xE169C58D, 0xBC57AC4C, 0x9B00DBD8]),
+        ([0xFFFFFFFF] * 4, [0xFFFFFFFF] * 2, [0x408F276D, 0x41C83B0E, 0xA20BC7C6, 0x6D5451FD]),
+        ([0x243F6A88, 0x85A308D3, 0x13198A2E, 0x03707344], [0xA4093822, 0x299F31D0],
+         [0xD16CFE09, 0x94FDCCEB, 0x5001E420, 0x24126EA1]),
+    ]
+    for ctr, key, expected in kats:
+        c, k, o = np.array(ctr, np.uint32), np.array(key, np.uint32), np.zeros(4, np.uint32)
+        L.orc_philox4x32_10(c.ctypes.data, k.ctypes.data, o.ctypes.data)
+        assert o.tolist() == expected
+    values = [L.orc_philox_uniform(123, c) for c in range(2000)]
+    assert all(0.0 <= v < 1.0 for v in values)
+    assert abs(float(np.mean(values)) - 0.5) < 0.02
+
+
+def _model(payload, seed, style):
+    from ivonar_inference_b200 import synthetic
+
+    return synthetic.synthetic_model(payload, seed, style)
+
+
+@pytest.mark.parametrize("name,style", [("model_config0", "baseline"), ("model_tiny", "reference_tests")])
+def test_oracle_decoder_matches_the_reference_model(oracle_lib, name: str, style: str) -> None:
+    from ivonar_inference_b200 import synthetic
+
+    g = golden(name)
+    payload = synthetic.config0() if name == "model_config0" else synthetic.tiny(seq_len=64)
+    model = _model(payload, int(g["seed"]), style)
+    dec = oracle_lib.OracleDecoder(model)
+    logits = dec.prefill(g["prompt"]).copy()
+    ref = g["prefill_logits"]
+    assert float(np.abs(logits - ref).max()) < 0.05
+    assert int(logits.argmax()) == int(ref.argmax())
+    # teacher-forced along the reference's penalized greedy stream
+    stream = g["torch_greedy_rp"]
+    steps = g["torch_greedy_rp_step_logits"]
+    worst = 0.0
+    for i, tok in enumerate(stream[:-1]):
+        out = dec.step(int(tok))
+        worst = max(worst, float(np.abs(out - steps[i]).max()))
+    assert worst < 0.05
+    # free-running penalized greedy stream: same tokens as the reference
+    dec.prefill(g["prompt"])
+    dec.configure_sampling(1.0, 1, 4.0)
+    tokens = [dec.sample()]
+    tokens += dec.generate(tokens[0], len(stream) - 1)
+    assert tokens == stream.tolist()
+
+
+def test_oracle_decoder_on_the_nano_shape(oracle_lib) -> None:
+    from ivonar_inference_b200 import synthetic
+
+    g = golden("model_config1")
+    model = _model(synthetic.config1(seq_len=2048), 0, "baseline")
+    dec = oracle_lib.OracleDecoder(model, max_len=128)
+    logits = dec.prefill(g["prompt"]).copy()
+    ref = g["prefill_logits"]
+    # 24 quantised blocks amplify rounding-order differences: on this model the reference's own
+    # torch one-pass forward and its numba stepped decoder differ by 0.21 max / 0.033 mean |dlogit|
+    # (logit std 0.54), so that self-consistency is the bar here.
+    diff = np.abs(logits - ref)
+    assert float(diff.max()) < 0.25 and float(diff.mean()) < 0.04
+    assert int(logits.argmax()) == int(ref.argmax())
+    # like for like: the reference numba decoder stepping through the prompt as the oracle does
+    stepped = g["numba_stepped_logits"]
+    assert float(np.abs(logits - stepped).max()) < 0.15
+    assert float(np.abs(logits - stepped).mean()) < 0.03
+    dec.configure_sampling(1.0, 1, 1.0)
+    tokens = [dec.sample()]
+    tokens += dec.generate(tokens[0], len(g["numba_stepped_greedy"]) - 1)
+    agree = next((i for i, (a, b) in enumerate(zip(tokens, g["numba_stepped_greedy"])) if a != b), len(tokens))
+    assert agree >= 16, (agree, tokens[:24], g["numba_stepped_greedy"][:24].tolist())
