@@ -228,6 +228,40 @@ void orc_ssm_step(const float* mixer_in, int hidden, int heads, int state_dim, i
  * mixer_in = [q (hidden) | latent | k_rope (heads*rope)], kv = [k_nope (heads*nope) | v (hidden)] (the
  * up-projection of the quantised latent), rope = [max_len][rope/2][2]. Appends k, v at `position`
  * and writes the attention output y [hidden]. */
+static inline float round_half(float f) {
+  /* fp32 -> fp16 (round to nearest even) -> fp32, for the reference GPU's fp16 K/V cache */
+  uint32_t b;
+  memcpy(&b, &f, 4);
+  const uint32_t sign = b & 0x80000000u;
+  const float a = fabsf(f);
+  if (!(a < 65520.0f)) {
+    float r = a != a ? a : INFINITY;
+    uint32_t rb;
+    memcpy(&rb, &r, 4);
+    rb |= sign;
+    memcpy(&r, &rb, 4);
+    return r;
+  }
+  float r;
+  if (a < 6.103515625e-05f) { /* subnormal half: quantum 2^-24 */
+    r = rintf(a * 16777216.0f) / 16777216.0f;
+  } else {
+    int e;
+    frexpf(a, &e);                     /* a in [2^(e-1), 2^e) */
+    const float q = ldexpf(1.0f, e - 11); /* 10 fraction bits */
+    r = rintf(a / q) * q;
+  }
+  uint32_t rb;
+  memcpy(&rb, &r, 4);
+  rb |= sign;
+  memcpy(&r, &rb, 4);
+  return r;
+}
+
+int orc_kv_half = 0; /* 1: store K and V rounded to fp16 as the reference GPU kernel does */
+
+void orc_set_kv_half(int on) { orc_kv_half = on; }
+
 void orc_attention_step(const float* mixer_in, const float* kv, const float* rope, int position, float* k_cache,
                         float* v_cache, int max_len, int heads, int head_dim, int nope, int rope_dim, int latent,
                         float scale, float* y) {
@@ -256,6 +290,12 @@ void orc_attention_step(const float* mixer_in, const float* kv, const float* rop
       kc[(size_t)position * head_dim + 2 * pair + 1] = k0 * sn + k1 * cs;
     }
     for (int d = 0; d < head_dim; ++d) vc[(size_t)position * head_dim + d] = kv[heads * nope + h * head_dim + d];
+    if (orc_kv_half) {
+      for (int d = 0; d < head_dim; ++d) {
+        kc[(size_t)position * head_dim + d] = round_half(kc[(size_t)position * head_dim + d]);
+        vc[(size_t)position * head_dim + d] = round_half(vc[(size_t)position * head_dim + d]);
+      }
+    }
     float peak = -INFINITY;
     for (int t = 0; t <= position; ++t) {
       float s = 0.0f;

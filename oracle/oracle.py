@@ -57,6 +57,8 @@ def lib() -> ctypes.CDLL:
         L.orc_philox_uniform.argtypes = [c_uint64, c_uint64]
         L.orc_philox4x32_10.restype = None
         L.orc_philox4x32_10.argtypes = [c_void_p, c_void_p, c_void_p]
+        L.orc_set_kv_half.restype = None
+        L.orc_set_kv_half.argtypes = [c_int]
         L.orc_max_threads.restype = c_int
         _lib = L
     return _lib
