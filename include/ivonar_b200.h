@@ -170,6 +170,10 @@ int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream);
  * ivb_decoder_check. */
 int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int32_t flags, uint64_t timeout_ns,
                         void* stream);
+/* Device timeline for tuning: while `buffer` (device uint64 [num_phases][ctas][8]) is set, each run
+ * records the globaltimer (ns) of step `step`, per phase and CTA: [0] work start, [1..6] marks inside
+ * the phase (0 where a phase has fewer), [7] work end before the phase's barrier. NULL turns it off. */
+int32_t ivb_decoder_trace(IvbDecoder* dec, uint64_t* buffer, int32_t step);
 /* Synchronises the stream and returns IVB_ETIMEOUT/IVB_ECAPACITY if the device error word is set. */
 int32_t ivb_decoder_check(IvbDecoder* dec, void* stream);
 

@@ -12,10 +12,11 @@
 #include <algorithm>
 #include <cstring>
 #include <new>
+#include <string>
 #include <vector>
 
 #include "ivb_common.h"
-#include "ivb_device.cuh"
+#include "ivb_cluster.cuh"
 
 size_t ivb_sample_smem_bytes(int vocab);
 size_t ivb_gemv_smem_bytes(int n);
@@ -23,208 +24,564 @@ int ivb_lpr_log(int in_features);
 
 namespace ivb {
 
-enum PhaseKind : int32_t { PH_GEMV = 0, PH_SSM = 1, PH_ATTN = 2, PH_HEAD = 3, PH_SAMPLE = 4 };
-
-struct Phase {
-  int32_t kind;
-  int32_t epilogue;
-  int32_t layer;
-  int32_t embed_input;  // input vector = embedding row of the current token
-  IvbTernary mat;
-  const float* in_vec;
-  const float* norm_w;
-  float norm_eps;
-  int32_t rows_per_cta;
-  float* out_vec;
-  int32_t lpr_log;
-  int32_t pad_;
-};
-
-struct Dims {
-  int32_t vocab, hidden, heads, head_dim, state_dim, latent, rope, nope, dense, max_len, max_top_k, mixer_width;
-  float act_eps, clip;
-};
-
-struct RunParams {
-  const Phase* prog;
-  int32_t n_phases;
-  int32_t steps;
-  const IvbLayerDesc* layers;
-  Dims dims;
-  IvbTernary head;
-  float* residual;
-  float* mixer_in;
-  float* ybuf;
-  float* ffn_mid;
-  float* logits;
-  int64_t* token;
-  int64_t* position;
-  uint8_t* seen;
-  int64_t* history;
-  const float* sampling;
-  const int64_t* top_k;
-  uint64_t* rng;
-  unsigned* counter;
-  unsigned* error;
-  const int64_t* feed;
-  unsigned long long timeout_ns;
-  int32_t history_len;
-  int32_t flags;
-};
-
-struct SmemPlan {
-  size_t gemv, attn, sample, total;
-};
-
-__device__ __forceinline__ void carve_sample(unsigned char* smem, int vocab, SampleSmem& sm) {
-  sm.keys = reinterpret_cast<unsigned*>(smem);
-  sm.hist = sm.keys + vocab;
-  sm.ckey = sm.hist + kWarps * 256;
-  sm.cidx = reinterpret_cast<int*>(sm.ckey + kMaxTopK);
-  sm.cprob = reinterpret_cast<float*>(sm.cidx + kMaxTopK);
-  sm.misc = reinterpret_cast<int*>(sm.cprob + kMaxTopK);
-  sm.red = reinterpret_cast<float*>(sm.misc + 16);
+// Thread 0 of a failing CTA: record the code and tell every CTA of the cluster to stop after cluster
+// barrier number `stop_at` (the next one). The flag keeps the minimum, so every CTA stops at the same
+// barrier even when several fail at different times; no CTA is left waiting on a barrier alone.
+__device__ __forceinline__ void raise_error(const ClusterParams& p, unsigned* err_flag, unsigned code, unsigned stop_at) {
+  atomicCAS(p.error, 0u, code);
+  for (int r = 0; r < p.d.R; ++r) atom_min_cluster_u32(map_rank(err_flag, r), stop_at);
 }
 
-__device__ __forceinline__ void carve_attn(unsigned char* smem, const Dims& D, AttnSmem& sm) {
-  const int lpad = ((D.latent + 63) >> 6) << 6;
-  float* f = reinterpret_cast<float*>(smem);
-  sm.xv = f;
-  f += lpad;
-  sm.qa = f;
-  f += lpad;
-  sm.qr = f;
-  f += D.rope;
-  sm.kr = f;
-  f += D.rope;
-  sm.qn = f;
-  f += D.nope;
-  sm.red = f;
-  f += 64;
-  sm.part = f;
-  f += kWarps * (D.latent + 2);
-  sm.ql = reinterpret_cast<int8_t*>(f);
-}
-
-__host__ __device__ inline size_t attn_smem_bytes(int latent, int rope, int nope) {
-  const size_t lpad = static_cast<size_t>((latent + 63) / 64) * 64;
-  return (lpad * 2 + rope * 2 + nope + 64 + kWarps * (latent + 2)) * 4 + lpad + 16;
-}
-
-__global__ void __launch_bounds__(kThreads, 1) decode_kernel(const __grid_constant__ RunParams p) {
-  extern __shared__ __align__(16) unsigned char smem[];
-  __shared__ int bflag;
-  const int cta = blockIdx.x, G = gridDim.x, tid = threadIdx.x;
-  const Dims& D = p.dims;
-  if (p.flags & IVB_RUN_SAMPLE_ONLY) {
-    if (cta == 0) {
-      SampleSmem sm;
-      carve_sample(smem, D.vocab, sm);
-      sample_block(p.logits, p.seen, D.vocab, p.sampling, p.top_k, D.max_top_k, p.rng, p.token, nullptr, sm);
-    }
-    return;
+__device__ __forceinline__ void gather_vec(const float* pub_rd, int n, int per, float* dst) {
+  for (int i = threadIdx.x; i < n; i += kThreads) {
+    const int c = i / per;
+    dst[i] = ld_cluster_f32(map_rank(pub_rd + (i - c * per), c));
   }
-  const Sync sync{p.counter, p.error, p.timeout_ns};
-  const bool sample = (p.flags & IVB_RUN_SAMPLE) != 0;
-  unsigned bars = 0;
-  uint4 pf[kPrefetch];
-  float pfs[kPrefetch];
-  int pf_for = -1;
-  const int n = p.n_phases;  // [5 per layer] + HEAD + SAMPLE
-  for (int step = 0; step < p.steps; ++step) {
-    const long long tok = p.feed != nullptr ? ldcg_i64(p.feed + step) : ldcg_i64(p.token);
-    const long long pos = ldcg_i64(p.position);
-    if (pos < 0 || pos >= D.max_len) {
-      if (cta == 0 && tid == 0) atomicCAS(p.error, 0u, static_cast<unsigned>(IVB_ECAPACITY));
-      return;
+}
+
+// Bounded wait on an attention tile mbarrier; the verdict is uniform across the CTA.
+__device__ __forceinline__ bool tile_wait(unsigned long long* bar, unsigned parity, unsigned long long timeout_ns) {
+  const bool late = !mbar_wait_bounded(bar, parity, timeout_ns);
+  return !__syncthreads_or(late);
+}
+
+struct TileBuf {
+  int8_t* lat;      // [tile][lpad]
+  float* lsc;       // [tile]
+  uint16_t* kr;     // [tile][rpad]
+};
+
+__device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const ClusterDims& D, int b) {
+  const size_t one = round16(D.tile * D.lpad) + round16(D.tile * 4) + round16(D.tile * D.rpad * 2);
+  unsigned char* t = base + b * one;
+  TileBuf tb;
+  tb.lat = reinterpret_cast<int8_t*>(t);
+  tb.lsc = reinterpret_cast<float*>(t + round16(D.tile * D.lpad));
+  tb.kr = reinterpret_cast<uint16_t*>(t + round16(D.tile * D.lpad) + round16(D.tile * 4));
+  return tb;
+}
+
+// thread 0: bulk-copy cached positions [start, start + count) of head h into tile buffer b
+__device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const ClusterDims& D, const TileBuf& tb, int h,
+                                           int start, int count, unsigned long long* bar) {
+  const unsigned lat = count * D.lpad, lsc = round16(count * 4), kr = count * D.rpad * 2;
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  fence_proxy_async();
+  mbar_expect_tx(bar, lat + lsc + kr);
+  bulk_copy(tb.lat, L.latent_q + static_cast<size_t>(start) * D.lpad, lat, bar);
+  bulk_copy(tb.lsc, L.latent_scale + start, lsc, bar);
+  bulk_copy(tb.kr, L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + start) * D.rpad, kr, bar);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __grid_constant__ ClusterParams p) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  __shared__ __align__(8) unsigned long long full[kStages];
+  __shared__ __align__(8) unsigned long long abar[2];
+  __shared__ unsigned err_flag;  // cluster barrier number after which every CTA stops (~0u: none)
+  const unsigned rank = cluster_rank();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const ClusterDims& D = p.d;
+  const ClusterSmem& M = p.sm;
+  const int R = D.R;
+  float* xv = reinterpret_cast<float*>(smem + M.xv);
+  int8_t* act = reinterpret_cast<int8_t*>(smem + M.act);
+  int* xsum = reinterpret_cast<int*>(smem + M.xsum);
+  float* resid = reinterpret_cast<float*>(smem + M.resid);
+  float* pub = reinterpret_cast<float*>(smem + M.pub);
+  float* loc = reinterpret_cast<float*>(smem + M.loc);
+  float* red = reinterpret_cast<float*>(smem + M.red);
+  float* xl = reinterpret_cast<float*>(smem + M.xl);
+  unsigned char* U = smem + M.u;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
+    mbar_init(&abar[0], 1);
+    mbar_init(&abar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    err_flag = 0xffffffffu;
+  }
+  __syncthreads();
+  cluster_sync();
+  Stream st{full, smem + M.ring, M.stage_bytes, 0u, 0u, 0, 0};
+  if (tid == 0)
+    for (int k = 0; k < kStages; ++k) stream_issue(p, st, rank);
+  unsigned apar[2] = {0u, 0u};
+  int rd = 0, wr = 1;  // publish buffers: read (previous op) / write (this op)
+  const int first_head = static_cast<int>(rank) * D.hpc;
+  const int nh = max(0, min(D.heads - first_head, D.hpc));
+  long long pos = ldcg_i64(p.position);
+  long long tok = p.feed != nullptr ? ldcg_i64(p.feed) : ldcg_i64(p.token);
+  uint64_t rkey = p.rng[0], rctr = p.rng[1];
+  const float inv_t = 1.0f / __ldcg(p.sampling);
+  const float pen = __ldcg(p.sampling + 1), ipen = __ldcg(p.sampling + 2);
+  const bool sampling = (p.flags & IVB_RUN_SAMPLE) != 0;
+  int K = 1;
+  {
+    const long long kreq = ldcg_i64(p.top_k);
+    const int cap = min(min(D.max_top_k, D.vocab), kMaxTopK);
+    K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
+  }
+  bool alive = true;
+  unsigned nbar = 0;  // cluster barriers passed in this run
+  auto sync_ok = [&]() -> bool {
+    cluster_sync();
+    ++nbar;
+    return *reinterpret_cast<volatile unsigned*>(&err_flag) > nbar;
+  };
+  auto fail_here = [&](unsigned code) {
+    if (tid == 0) raise_error(p, &err_flag, code, nbar + 1);
+  };
+  for (int step = 0; step < p.steps && alive; ++step) {
+    if (step > 0 && p.feed != nullptr) tok = ldcg_i64(p.feed + step);
+    if (pos < 0 || pos >= D.max_len || tok < 0 || tok >= D.vocab) {
+      // every CTA sees the same values: stop together
+      if (rank == 0 && tid == 0) atomicCAS(p.error, 0u, static_cast<unsigned>(pos >= D.max_len ? IVB_ECAPACITY : IVB_EINVAL));
+      break;
     }
-    if (tok < 0 || tok >= D.vocab) {
-      if (cta == 0 && tid == 0) atomicCAS(p.error, 0u, static_cast<unsigned>(IVB_EINVAL));
-      return;
+    const bool head = head_needed(p, step);
+    const bool tracing = p.trace != nullptr && step == p.trace_step;
+    // embedding of the token -> residual replica (every CTA computes the whole row)
+    {
+      const uint8_t* erow = p.head.packed + static_cast<size_t>(tok) * p.head.row_bytes;
+      const uint16_t* srow = p.head.scales + static_cast<size_t>(tok) * p.head.scale_stride;
+      for (int i = tid; i < D.hidden; i += kThreads)
+        resid[i] = static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
     }
-    const bool head = sample || (p.flags & IVB_RUN_HEAD_ALL) != 0 || step == p.steps - 1;
-    const int last = sample ? n - 1 : (head ? n - 2 : n - 3);
-    for (int pi = 0; pi <= last; ++pi) {
-      const Phase ph = p.prog[pi];
-      if (ph.kind == PH_GEMV || ph.kind == PH_HEAD) {
-        const GemvGeom g = gemv_geom(ph.mat, ph.rows_per_cta, ph.lpr_log, cta);
-        if (pf_for != pi) gemv_prefetch(ph.mat, g, pf, pfs);
-        const int nin = ph.mat.in_features;
-        const int pad = ((nin + 63) >> 6) << 6;
-        float* xv = reinterpret_cast<float*>(smem);
-        int8_t* act = reinterpret_cast<int8_t*>(xv + pad);
-        int* xs = reinterpret_cast<int*>(act + pad);
-        float* red = reinterpret_cast<float*>(xs + (pad >> 6));
-        float* res = red + 64;
-        if (ph.embed_input) {
-          const uint8_t* erow = p.head.packed + static_cast<size_t>(tok) * p.head.row_bytes;
-          const uint16_t* srow = p.head.scales + static_cast<size_t>(tok) * p.head.scale_stride;
-          const int per = (nin + G - 1) / G;
-          for (int i = tid; i < nin; i += kThreads) {
-            const int code = (__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3;
-            const float v = static_cast<float>(code - 1) * h2f(__ldg(srow + (i >> 7)));
-            xv[i] = v;
-            if (i >= cta * per && i < (cta + 1) * per) p.residual[i] = v;
-          }
-        } else {
-          for (int i = tid; i < nin; i += kThreads) xv[i] = ldcg_f(ph.in_vec + i);
-        }
+    __syncthreads();
+    for (int oi = 0; oi < p.n_ops && alive; ++oi) {
+      const Op op = p.ops[oi];
+      if (op.kind == OP_HEAD && !head) break;
+      unsigned long long* marks = tracing ? p.trace + (static_cast<size_t>(oi) * R + rank) * 8 : nullptr;
+      mark(marks, 0);
+      float* pub_rd = pub + rd * M.pub_n;
+      float* pub_wr = pub + wr * M.pub_n;
+      // 1. input of this op from the cluster
+      if (op.gather == G_RESID) gather_vec(pub_rd, op.gather_n, op.gather_per, resid);
+      else if (op.gather == G_VEC) gather_vec(pub_rd, op.gather_n, op.gather_per, xv);
+      else if (op.gather == G_LATENT) gather_vec(pub_rd, op.gather_n, op.gather_per, xl);
+      __syncthreads();
+      mark(marks, 1);
+      const int lo = min(op.rows_total, static_cast<int>(rank) * op.rows_per);
+      const int rows_c = p.op_rows[oi * R + rank];
+      bool ok = true;
+      if (op.kind == OP_ATTN) {
+        // ---------------- latent attention over the compressed cache ----------------
+        const IvbLayerDesc& L = p.layers[op.layer];
+        const unsigned char* cst = stream_acquire(p, st);
+        if (cst == nullptr) ok = false;
+        float* qlat_f = reinterpret_cast<float*>(U);  // [latent] quantiser scratch
+        int8_t* qlc = reinterpret_cast<int8_t*>(U + round16(((D.latent + 63) / 64 * 64) * 4));
+        float* qa = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(qlc) + round16((D.latent + 63) / 64 * 64));
+        float* qr = qa + D.latent;
+        float* krc = qr + D.rope;
+        float* qn = krc + D.rope;
+        float* sc = qn + D.nope;
+        float* part = sc + D.tile + 4;
+        unsigned char* tiles = reinterpret_cast<unsigned char*>(part + kWarps * D.latent);
+        tiles += (16 - (reinterpret_cast<uintptr_t>(tiles) & 15)) & 15;
+        for (int j = tid; j < D.latent; j += kThreads) qlat_f[j] = xl[j];
         __syncthreads();
-        if (g.r0 < g.r1) {
-          const float s = quantize_block(xv, nin, ph.norm_w, ph.norm_eps, D.clip, D.act_eps, act, true, xs, red);
-          gemv_rows(ph.mat, g, act, xs, s, ph.epilogue, ph.out_vec, pf, pfs, res);
+        const float a_cur = quantize_block(qlat_f, D.latent, nullptr, 0.0f, 0.0f, D.act_eps, qlc, false, nullptr, red);
+        if (rank == 0) {
+          for (int j = tid; j < D.latent; j += kThreads) L.latent_q[static_cast<size_t>(pos) * D.lpad + j] = qlc[j];
+          if (tid == 0) L.latent_scale[pos] = a_cur;
         }
-      } else if (ph.kind == PH_SSM) {
-        const IvbLayerDesc L = p.layers[ph.layer];
-        const int per = (D.hidden + G - 1) / G;
-        const int c0 = min(D.hidden, cta * per), c1 = min(D.hidden, c0 + per);
-        ssm_channels(L, D.hidden, D.heads, D.head_dim, D.state_dim, p.mixer_in, p.ybuf, c0, c1);
-      } else if (ph.kind == PH_ATTN) {
-        const IvbLayerDesc L = p.layers[ph.layer];
-        AttnSmem sm;
-        carve_attn(smem, D, sm);
-        for (int h = cta; h < D.heads; h += G)
-          attention_head(L, D.hidden, D.heads, D.head_dim, D.nope, D.rope, D.latent, D.act_eps, p.mixer_in, p.ybuf, h,
-                         static_cast<int>(pos), sm);
-      } else if (ph.kind == PH_SAMPLE) {
-        if (cta == 0) {
-          SampleSmem sm;
-          carve_sample(smem, D.vocab, sm);
-          int64_t* hist = (p.history != nullptr && step < p.history_len) ? p.history + step : nullptr;
-          sample_block(p.logits, p.seen, D.vocab, p.sampling, p.top_k, D.max_top_k, p.rng, p.token, hist, sm);
+        const int P = static_cast<int>(pos);
+        const int n_tiles = P == 0 ? 1 : (P + D.tile - 1) / D.tile;
+        for (int hl = 0; hl < nh && ok; ++hl) {
+          const int h = first_head + hl;
+          const float* qh = loc + hl * D.head_dim;
+          const float* kh = loc + nh * D.head_dim + hl * D.rope;
+          const float scl = L.attn_scale;
+          const float* rtab = L.rope + static_cast<size_t>(P) * D.rope;
+          for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
+            const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+            const float q0 = qh[D.nope + 2 * jr], q1 = qh[D.nope + 2 * jr + 1];
+            const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
+            qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
+            qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+            const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
+            krc[2 * jr] = kr0;
+            krc[2 * jr + 1] = kr1;
+            uint16_t* kc = L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + P) * D.rpad;
+            kc[2 * jr] = f2h(kr0);
+            kc[2 * jr + 1] = f2h(kr1);
+          }
+          for (int e = tid; e < D.nope; e += kThreads) qn[e] = qh[e] * scl;
+          // first tile of this head
+          if (tid == 0 && P > 0) tile_issue(L, D, tile_buf(tiles, D, 0), h, 0, min(P, D.tile), &abar[0]);
+          __syncthreads();
+          // absorbed query qa[j] = sum_e qn[e] * W_knope[h][e][j] (weights in the constants chunk)
+          const unsigned char* wkn = cst + op.c_wkn + static_cast<size_t>(hl) * D.nope * D.rb_lat;
+          const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + op.c_skn) + hl * D.nope * D.ss_lat;
+          for (int j = tid; j < D.latent; j += kThreads) {
+            float acc = 0.0f;
+            for (int e = 0; e < D.nope; ++e)
+              acc = fmaf(qn[e], code_value(wkn + e * D.rb_lat, j) * h2f(skn[e * D.ss_lat + (j >> 7)]), acc);
+            qa[j] = acc;
+          }
+          float qb = 0.0f;
+          if (L.k_nope_up.bias != nullptr) {
+            const float* bkn = reinterpret_cast<const float*>(cst + op.c_bkn) + hl * D.nope;
+            float pp = 0.0f;
+            for (int e = tid; e < D.nope; e += kThreads) pp = fmaf(qn[e], bkn[e], pp);
+            qb = block_sum(pp, red);
+          } else {
+            __syncthreads();
+          }
+          const int per_lane = (D.latent + 31) >> 5;
+          float qa_r[kMaxLatentPerLane], u[kMaxLatentPerLane];
+#pragma unroll
+          for (int i = 0; i < kMaxLatentPerLane; ++i) {
+            const int j = lane + (i << 5);
+            qa_r[i] = (i < per_lane && j < D.latent) ? qa[j] : 0.0f;
+            u[i] = 0.0f;
+          }
+          float m_run = -INFINITY, l_run = 0.0f;
+          for (int ti = 0; ti < n_tiles; ++ti) {
+            const int start = ti * D.tile;
+            const int count = max(0, min(D.tile, P - start));
+            const bool last = ti == n_tiles - 1;
+            const TileBuf tb = tile_buf(tiles, D, ti & 1);
+            if (tid == 0 && ti + 1 < n_tiles)
+              tile_issue(L, D, tile_buf(tiles, D, (ti + 1) & 1), h, start + D.tile, min(D.tile, P - start - D.tile),
+                         &abar[(ti + 1) & 1]);
+            if (count > 0) {
+              if (!tile_wait(&abar[ti & 1], apar[ti & 1], p.timeout_ns)) {
+                ok = false;
+                break;
+              }
+              apar[ti & 1] ^= 1u;
+            }
+            const int npos = count + (last ? 1 : 0);
+            for (int k = warp; k < npos; k += kWarps) {
+              const bool cur = k == count;
+              const int8_t* ql = cur ? qlc : tb.lat + k * D.lpad;
+              const float at = cur ? a_cur : tb.lsc[k];
+              float dot = 0.0f;
+#pragma unroll
+              for (int i = 0; i < kMaxLatentPerLane; ++i) {
+                const int j = lane + (i << 5);
+                if (i < per_lane && j < D.latent) dot = fmaf(qa_r[i], static_cast<float>(ql[j]), dot);
+              }
+              float rp = 0.0f;
+              for (int r = lane; r < D.rope; r += 32) rp = fmaf(qr[r], cur ? krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
+              const float total = warp_sum(at * dot + rp);
+              if (lane == 0) sc[k] = total + qb;
+            }
+            __syncthreads();
+            float mx = -INFINITY;
+            for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, sc[k]);
+            mx = block_max(mx, red);
+            const float m_new = fmaxf(m_run, mx);
+            const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+            float ls = 0.0f;
+            for (int k = tid; k < npos; k += kThreads) {
+              const float e = expf(sc[k] - m_new);
+              sc[k] = e;
+              ls += e;
+            }
+            ls = block_sum(ls, red);
+            l_run = l_run * corr + ls;
+#pragma unroll
+            for (int i = 0; i < kMaxLatentPerLane; ++i) u[i] *= corr;
+            for (int k = warp; k < npos; k += kWarps) {
+              const bool cur = k == count;
+              const int8_t* ql = cur ? qlc : tb.lat + k * D.lpad;
+              const float ea = sc[k] * (cur ? a_cur : tb.lsc[k]);
+#pragma unroll
+              for (int i = 0; i < kMaxLatentPerLane; ++i) {
+                const int j = lane + (i << 5);
+                if (i < per_lane && j < D.latent) u[i] = fmaf(ea, static_cast<float>(ql[j]), u[i]);
+              }
+            }
+            m_run = m_new;
+            __syncthreads();
+          }
+          if (!ok) break;
+#pragma unroll
+          for (int i = 0; i < kMaxLatentPerLane; ++i) {
+            const int j = lane + (i << 5);
+            if (i < per_lane && j < D.latent) part[warp * D.latent + j] = u[i];
+          }
+          __syncthreads();
+          for (int j = tid; j < D.latent; j += kThreads) {
+            float v = part[j];
+#pragma unroll
+            for (int w = 1; w < kWarps; ++w) v += part[w * D.latent + j];
+            qlat_f[j] = v;
+          }
+          __syncthreads();
+          // out_h[e] = W_v[h][e] . u / l + b_v
+          const unsigned char* wv = cst + op.c_wv + static_cast<size_t>(hl) * D.head_dim * D.rb_lat;
+          const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + op.c_sv) + hl * D.head_dim * D.ss_lat;
+          const float* bv = reinterpret_cast<const float*>(cst + op.c_bv) + hl * D.head_dim;
+          int tpr = kThreads / D.head_dim;
+          if (tpr > 32) tpr = 32;
+          int tpr_log = 0;
+          while ((2 << tpr_log) <= tpr) ++tpr_log;
+          tpr = 1 << tpr_log;
+          const float inv_l = 1.0f / l_run;
+          for (int base = 0; base < D.head_dim; base += kThreads >> tpr_log) {
+            const int e = base + (tid >> tpr_log);
+            const int pid = tid & (tpr - 1);
+            float acc = 0.0f;
+            if (e < D.head_dim) {
+              const unsigned char* row = wv + e * D.rb_lat;
+              const int span = (D.latent + tpr - 1) / tpr;
+              const int j0 = pid * span, j1 = min(D.latent, j0 + span);
+              for (int j = j0; j < j1; ++j) acc = fmaf(code_value(row, j) * h2f(sv[e * D.ss_lat + (j >> 7)]), qlat_f[j], acc);
+            }
+            for (int off = 1; off < tpr; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
+            if (e < D.head_dim && pid == 0) {
+              float o = acc * inv_l;
+              if (L.v_up.bias != nullptr) o += bv[e];
+              pub_wr[hl * D.head_dim + e] = o;
+            }
+          }
+          __syncthreads();
+        }
+        asm volatile("fence.proxy.async.global;" ::: "memory");
+        if (!ok) fail_here(IVB_ETIMEOUT);
+        stream_release(p, st, rank);
+      } else {
+        // ---------------- GEMV ops ----------------
+        const unsigned char* cst = nullptr;
+        float act_scale = 0.0f;
+        if (op.has_const) {
+          cst = stream_acquire(p, st);
+          if (cst == nullptr) ok = false;
+        }
+        mark(marks, 2);
+        // quantiser input
+        if (op.kind == OP_ENTRY_MAMBA || op.kind == OP_ENTRY_MLA || op.kind == OP_GATE_UP || op.kind == OP_HEAD) {
+          for (int i = tid; i < D.hidden; i += kThreads) xv[i] = resid[i];
+          __syncthreads();
+        }
+        const float* norm_w = (op.has_norm && cst != nullptr) ? reinterpret_cast<const float*>(cst + op.c_norm) : nullptr;
+        act_scale = quantize_block(xv, op.in_n, norm_w, op.norm_eps, D.clip, D.act_eps, act, true, xsum, red);
+        mark(marks, 3);
+        // SSM constants leave the stage before it is recycled
+        float* ssmc = reinterpret_cast<float*>(U);
+        const int S = D.state_dim, hd = D.head_dim, taps = D.taps;
+        if (op.kind == OP_ENTRY_MAMBA && cst != nullptr) {
+          const float* src[5] = {reinterpret_cast<const float*>(cst + op.c_decay), reinterpret_cast<const float*>(cst + op.c_theta),
+                                 reinterpret_cast<const float*>(cst + op.c_skip), reinterpret_cast<const float*>(cst + op.c_convw),
+                                 reinterpret_cast<const float*>(cst + op.c_convb)};
+          const int len[5] = {nh * S, nh * S, nh * hd, nh * hd * taps, nh * hd};
+          int off = 0;
+          for (int a = 0; a < 5; ++a) {
+            for (int i = tid; i < len[a]; i += kThreads) ssmc[off + i] = src[a][i];
+            off += len[a];
+          }
+        }
+        if (op.has_const) stream_release(p, st, rank);
+        // rows of this CTA, chunk by chunk
+        float* rows_out = loc;
+        const int n_row_chunks = op.n_chunks - op.has_const;
+        for (int c = 0; c < n_row_chunks; ++c) {
+          const unsigned char* stage = stream_acquire(p, st);
+          if (c == 0) mark(marks, 4);
+          if (stage == nullptr) {
+            ok = false;
+          } else {
+            const int r0 = c * op.chunk_rows;
+            const int k = max(0, min(op.chunk_rows, rows_c - r0));
+            chunk_rows(op, stage, k, act, xsum, act_scale, rows_out + r0);
+          }
+          if (c == 0) mark(marks, 5);
+          stream_release(p, st, rank);
+        }
+        mark(marks, 6);
+        // epilogues
+        if (op.kind == OP_OUT || op.kind == OP_DOWN) {
+          for (int r = tid; r < rows_c; r += kThreads) pub_wr[r] = resid[lo + r] + rows_out[r];
+        } else if (op.kind == OP_GATE_UP) {
+          for (int m = tid; m < rows_c / 2; m += kThreads) pub_wr[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
+        } else if (op.kind == OP_ENTRY_MLA) {
+          const int lat0 = nh * (D.head_dim + D.rope);
+          for (int r = tid; r < rows_c - lat0; r += kThreads) pub_wr[r] = rows_out[lat0 + r];
+        } else if (op.kind == OP_HEAD) {
+          for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
+        } else if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
+          // recurrent step for the channels of my heads; rows_out = per head [value hd | gate hd | bc_dt 3S]
+          const IvbLayerDesc& L = p.layers[op.layer];
+          const float* decay = ssmc;
+          const float* theta = decay + nh * S;
+          const float* skip = theta + nh * S;
+          const float* convw = skip + nh * hd;
+          const float* convb = convw + nh * hd * taps;
+          const int channels = nh * hd;
+          int tpc = 1;
+          while (tpc * 2 * channels <= kThreads && tpc * 2 <= 32) tpc *= 2;
+          const int spt = (S + tpc - 1) / tpc;
+          for (int cb = 0; cb < channels; cb += kThreads / tpc) {
+            const int cl = cb + tid / tpc, sg = tid % tpc;
+            const bool live = cl < channels;
+            const int hl = live ? cl / hd : 0, dd = live ? cl - hl * hd : 0;
+            const int hg = first_head + hl;
+            const float* rowh = rows_out + hl * (2 * hd + 3 * S);
+            float value = 0.0f;
+            if (live && sg == 0) {
+              const int cg = hg * hd + dd;
+              float* win = L.conv_state + static_cast<size_t>(cg) * (taps - 1);
+              const float incoming = rowh[dd];
+              float conv = convb[cl];
+              for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
+              conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
+              for (int k2 = 0; k2 + 1 < taps - 1; ++k2) win[k2] = win[k2 + 1];
+              if (taps > 1) win[taps - 2] = incoming;
+              value = silu_f(conv);
+            }
+            value = __shfl_sync(kFull, value, lane & ~(tpc - 1));
+            float contrib = 0.0f;
+            if (live) {
+              const float* bcdt = rowh + 2 * hd;
+              for (int i = 0; i < spt; ++i) {
+                const int s2 = sg * spt + i;
+                if (s2 >= S) break;
+                const float b = tanhf(bcdt[s2]);
+                const float cc = tanhf(bcdt[S + s2]);
+                const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
+                const float mag = expf(2.0f * half_dt * decay[hl * S + s2]);
+                float sn, cs;
+                sincosf(2.0f * half_dt * theta[hl * S + s2], &sn, &cs);
+                const float ar = mag * cs, ai = mag * sn;
+                const size_t idx = (static_cast<size_t>(hg) * S + s2) * hd + dd;
+                const float prev = L.prev_force[idx];
+                float* stt = L.ssm_state + 2 * idx;
+                const float sr = stt[0], si = stt[1];
+                const float force = b * value;
+                const float dr = (force + ar * prev) * half_dt;
+                const float di = (ai * prev) * half_dt;
+                const float nr = sr * ar - si * ai + dr;
+                const float ni = sr * ai + si * ar + di;
+                stt[0] = nr;
+                stt[1] = ni;
+                L.prev_force[idx] = force;
+                contrib = fmaf(cc, nr, contrib);
+              }
+            }
+            for (int off = tpc >> 1; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
+            if (live && sg == 0)
+              pub_wr[cl] = (contrib + skip[cl] * value) * sigmoid_f(rowh[hd + dd]);
+          }
+        }
+        if (!ok) fail_here(IVB_ETIMEOUT);
+        // the head ends the token: local top-k of my vocabulary slice for the sampler
+        if (op.kind == OP_HEAD && sampling) {
+          unsigned* keys = reinterpret_cast<unsigned*>(U);
+          unsigned* ck = keys + op.rows_per;
+          int* ci = reinterpret_cast<int*>(ck + p.kc);
+          TopkScratch ts{reinterpret_cast<unsigned*>(ci + p.kc), reinterpret_cast<int*>(ci + p.kc) + kWarps * 256};
+          for (int r = tid; r < rows_c; r += kThreads) keys[r] = score_key(rows_out[r], __ldcg(p.seen + lo + r), inv_t, pen, ipen);
+          __syncthreads();
+          const int kl = min(K, rows_c);
+          if (kl > 0)
+            topk_sorted(keys, nullptr, lo, rows_c, kl, ts, ck, ci, p.cand_key + static_cast<size_t>(rank) * p.kc,
+                        p.cand_id + static_cast<size_t>(rank) * p.kc);
+          if (tid == 0) p.cand_n[rank] = kl;
         }
       }
-      if (pi == last && cta == 0 && tid == 0) p.position[0] = pos + 1;
-      // load the first weight chunks of the next GEMV slice before waiting
-      int nxt = pi < last ? pi + 1 : (step + 1 < p.steps ? 0 : -1);
-      pf_for = -1;
-      if (nxt >= 0) {
-        const Phase& q = p.prog[nxt];
-        if (q.kind == PH_GEMV || q.kind == PH_HEAD) {
-          const GemvGeom g = gemv_geom(q.mat, q.rows_per_cta, q.lpr_log, cta);
-          gemv_prefetch(q.mat, g, pf, pfs);
-          pf_for = nxt;
+      mark(marks, 7);
+      if (!sync_ok()) {
+        alive = false;
+        break;
+      }
+      rd = wr;
+      wr ^= 1;
+    }
+    if (!alive) break;
+    if (sampling) {
+      // every CTA merges the cluster's candidates and draws the same token
+      const int kc = p.kc;
+      unsigned* mk = reinterpret_cast<unsigned*>(U);
+      int* mi = reinterpret_cast<int*>(mk + R * kc);
+      unsigned* ck = reinterpret_cast<unsigned*>(mi + R * kc);
+      int* ci = reinterpret_cast<int*>(ck + kc);
+      unsigned* sk = reinterpret_cast<unsigned*>(ci + kc);
+      int* si = reinterpret_cast<int*>(sk + kc);
+      float* cdf = reinterpret_cast<float*>(si + kc);
+      TopkScratch ts{reinterpret_cast<unsigned*>(cdf + kc), reinterpret_cast<int*>(cdf + kc) + kWarps * 256};
+      int n = 0;
+      for (int r = 0; r < R; ++r) {
+        const int cn = __ldcg(p.cand_n + r);
+        for (int c = tid; c < cn; c += kThreads) {
+          mk[n + c] = __ldcg(p.cand_key + static_cast<size_t>(r) * kc + c);
+          mi[n + c] = __ldcg(p.cand_id + static_cast<size_t>(r) * kc + c);
+        }
+        n += cn;
+      }
+      __syncthreads();
+      const int kk = min(K, n);
+      topk_sorted(mk, mi, 0, n, kk, ts, ck, ci, sk, si);
+      const int chosen = draw_token(sk, si, kk, cdf, red, rkey, rctr);
+      ++rctr;
+      tok = chosen;
+      if (tid == 0) {
+        const int per = (D.vocab + R - 1) / R;
+        if (chosen / per == static_cast<int>(rank)) p.seen[chosen] = 1;
+        if (rank == 0) {
+          p.token[0] = chosen;
+          p.rng[1] = rctr;
+          if (p.history != nullptr && step < p.history_len) p.history[step] = chosen;
         }
       }
-      if (!grid_barrier(sync, (++bars) * static_cast<unsigned>(G), &bflag)) return;
+    }
+    ++pos;
+    if (rank == 0 && tid == 0) p.position[0] = pos;
+  }
+  // let every in-flight bulk copy land before the CTA's shared memory goes away
+  if (tid == 0) {
+    while (st.consumed < st.issued) {
+      if (!mbar_wait_bounded(st.full + st.consumed % kStages, (st.consumed / kStages) & 1u, p.timeout_ns)) break;
+      ++st.consumed;
     }
   }
+  __syncthreads();
+  cluster_sync();
 }
 
 }  // namespace ivb
 
 // ------------------------------------------------------------------------------------------------
-// host plan
+// host plan: per-CTA weight streams, op program, shared-memory map
 // ------------------------------------------------------------------------------------------------
+namespace {
+
+struct CopyOp {       // one device-to-device copy into the stream, executed at bind
+  size_t dst;         // byte offset in the stream
+  const void* src;    // nullptr: zero fill
+  size_t width;       // bytes per row
+  size_t rows;
+  size_t spitch, dpitch;
+};
+
+struct Segment {      // rows [row0, row0 + count) of one matrix
+  const IvbTernary* m;
+  int row0, count;
+};
+
+size_t r16(size_t v) { return (v + 15) / 16 * 16; }
+
+}  // namespace
+
 struct IvbDecoder {
   IvbModelDesc desc;
   std::vector<IvbLayerDesc> layers;
-  std::vector<ivb::Phase> prog;
-  ivb::Dims dims;
-  int32_t ctas;
-  size_t smem;
-  size_t off_prog, off_layers, off_sync, off_residual, off_mixer, off_y, off_ffn, total;
+  ivb::ClusterDims d;
+  ivb::ClusterSmem sm;
+  std::vector<ivb::Op> ops;
+  std::vector<int32_t> op_rows;
+  std::vector<unsigned long long> chunk_off;
+  std::vector<unsigned> chunk_bytes;
+  std::vector<CopyOp> copies;
+  int32_t R, cpt, head_first, kc;
+  size_t stream_bytes, smem;
+  size_t off_stream, off_ops, off_op_rows, off_chunk_off, off_chunk_bytes, off_layers, off_cand_key, off_cand_id,
+      off_cand_n, off_sync, total;
   unsigned char* ws;
+  unsigned long long* trace;
+  int32_t trace_step;
 };
 
 namespace ivb {
@@ -242,6 +599,7 @@ static int32_t validate(const IvbModelDesc& d) {
     return fail(IVB_EINVAL, "null state pointer in the model description");
   if (int32_t rc = check_ternary(d.head, "head")) return rc;
   if (d.head.rows != d.vocab || d.head.in_features != d.hidden) return fail(IVB_EINVAL, "head must be [vocab, hidden]");
+  int taps = -1;
   for (int i = 0; i < d.num_layers; ++i) {
     const IvbLayerDesc& L = d.layers[i];
     char name[64];
@@ -254,15 +612,18 @@ static int32_t validate(const IvbModelDesc& d) {
     snprintf(name, sizeof(name), "layer %d down", i);
     if (int32_t rc = check_ternary(L.down, name)) return rc;
     if (L.entry.in_features != d.hidden || L.out.rows != d.hidden || L.gate_up.rows != 2 * d.dense ||
-        L.down.rows != d.hidden || L.down.in_features != d.dense || L.gate_up.in_features != d.hidden)
+        L.down.rows != d.hidden || L.down.in_features != d.dense || L.gate_up.in_features != d.hidden ||
+        L.out.in_features != d.hidden)
       return fail(IVB_EINVAL, "layer %d: projection shapes do not match the model dimensions", i);
     if (!L.mixer_norm || !L.ffn_norm) return fail(IVB_EINVAL, "layer %d: null norm weight", i);
     if (L.kind == IVB_MAMBA) {
-      if (L.entry.rows != 2 * d.hidden + 3 * d.heads * d.state_dim || L.out.in_features != d.hidden)
+      if (L.entry.rows != 2 * d.hidden + 3 * d.heads * d.state_dim)
         return fail(IVB_EINVAL, "layer %d: mamba entry must be [2*hidden + 3*heads*state, hidden]", i);
       if (!L.decay || !L.theta || !L.skip || !L.conv_weight || !L.conv_bias || !L.ssm_state || !L.prev_force ||
           !L.conv_state || L.conv_taps < 1)
         return fail(IVB_EINVAL, "layer %d: missing recurrent constants or state", i);
+      if (taps >= 0 && taps != L.conv_taps) return fail(IVB_EINVAL, "all recurrent layers must share the conv width");
+      taps = L.conv_taps;
     } else if (L.kind == IVB_MLA) {
       if (L.entry.rows != d.hidden + d.latent_dim + d.heads * d.rope_dim)
         return fail(IVB_EINVAL, "layer %d: mla entry must be [hidden + latent + heads*rope, hidden]", i);
@@ -275,11 +636,374 @@ static int32_t validate(const IvbModelDesc& d) {
         return fail(IVB_EINVAL, "layer %d: latent up-projections have the wrong shape", i);
       if (!L.rope || !L.latent_q || !L.latent_scale || !L.k_rope_cache)
         return fail(IVB_EINVAL, "layer %d: missing rope table or latent cache", i);
+      if ((reinterpret_cast<uintptr_t>(L.latent_q) & 15) || (reinterpret_cast<uintptr_t>(L.latent_scale) & 15) ||
+          (reinterpret_cast<uintptr_t>(L.k_rope_cache) & 15))
+        return fail(IVB_EINVAL, "layer %d: the latent cache must be 16-byte aligned", i);
     } else {
       return fail(IVB_EINVAL, "layer %d: unknown kind %d", i, L.kind);
     }
   }
   return IVB_OK;
+}
+
+// Builds the stream, op program and shared-memory map for a cluster of R CTAs; false if it does not fit.
+static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
+  const IvbModelDesc& md = dec->desc;
+  ClusterDims& D = dec->d;
+  D = ClusterDims{};
+  D.vocab = md.vocab;
+  D.hidden = md.hidden;
+  D.heads = md.heads;
+  D.head_dim = md.head_dim;
+  D.state_dim = md.state_dim;
+  D.latent = md.latent_dim;
+  D.rope = md.rope_dim;
+  D.nope = md.nope_dim;
+  D.dense = md.dense;
+  D.max_len = md.max_len;
+  D.max_top_k = md.max_top_k;
+  D.R = R;
+  D.hpc = (md.heads + R - 1) / R;
+  D.taps = 1;
+  D.act_eps = md.act_eps;
+  D.clip = md.norm_clip;
+  D.lpad = static_cast<int>(r16(md.latent_dim));
+  D.rpad = (md.rope_dim + 7) / 8 * 8;
+  D.rb_lat = static_cast<int>(r16((md.latent_dim + 3) / 4));
+  D.ss_lat = ((md.latent_dim + 127) / 128 + 7) / 8 * 8;
+  for (const IvbLayerDesc& L : dec->layers) {
+    if (L.kind == IVB_MAMBA) {
+      D.taps = L.conv_taps;
+      D.half_dt_min = L.half_dt_min;
+      D.half_dt_range = L.half_dt_range;
+    }
+  }
+  const int d = md.hidden, F = md.dense, Lt = md.latent_dim, hd = md.head_dim, S = md.state_dim, H = md.heads;
+  const int hpc = D.hpc;
+  const int dper = (d + R - 1) / R, Fper = (F + R - 1) / R, Lper = (Lt + R - 1) / R, Vper = (md.vocab + R - 1) / R;
+  auto heads_of = [&](int c) { return std::max(0, std::min(H - c * hpc, hpc)); };
+  auto part = [&](int n, int per, int c) { return std::max(0, std::min(n, (c + 1) * per) - std::min(n, c * per)); };
+  const size_t stage = 28 * 1024;
+  dec->kc = std::min(std::min(md.max_top_k, md.vocab), kMaxTopK);
+  // ---- op program and per-CTA segments ------------------------------------------------------------
+  struct OpPlan {
+    Op op;
+    std::vector<std::vector<Segment>> segs;  // [R] row segments of each CTA
+    int const_kind;                           // 0 none, 1 norm, 2 mamba (norm + ssm), 3 attention
+    const float* norm;
+    const IvbLayerDesc* layer;
+  };
+  std::vector<OpPlan> plans;
+  auto gemv_op = [&](int kind, int layer, const IvbTernary& m, int in_n, int rows_per, int rows_total, int gather,
+                     int gather_n, int gather_per, const float* norm, float eps) {
+    OpPlan pl{};
+    pl.op.kind = kind;
+    pl.op.layer = layer;
+    pl.op.gather = gather;
+    pl.op.gather_n = gather_n;
+    pl.op.gather_per = gather_per;
+    pl.op.in_n = in_n;
+    pl.op.rows_per = rows_per;
+    pl.op.rows_total = rows_total;
+    pl.op.row_bytes = m.row_bytes;
+    pl.op.scale_stride = ((m.in_features + 127) / 128 + 7) / 8 * 8;
+    pl.op.has_bias = m.bias != nullptr;
+    const int chunks = (in_n + 63) / 64;
+    int lg = 0;
+    while ((1 << lg) < (chunks + 3) / 4 && lg < 5) ++lg;
+    pl.op.lpr_log = lg;
+    pl.op.has_norm = norm != nullptr;
+    pl.op.norm_eps = eps;
+    pl.norm = norm;
+    pl.const_kind = norm != nullptr ? 1 : 0;
+    pl.segs.assign(R, {});
+    return pl;
+  };
+  for (int li = 0; li < static_cast<int>(dec->layers.size()); ++li) {
+    const IvbLayerDesc& L = dec->layers[li];
+    const int gather0 = li == 0 ? G_NONE : G_RESID;
+    if (L.kind == IVB_MAMBA) {
+      OpPlan e = gemv_op(OP_ENTRY_MAMBA, li, L.entry, d, hpc * (2 * hd + 3 * S), H * (2 * hd + 3 * S), gather0, d, dper,
+                         L.mixer_norm, L.mixer_norm_eps);
+      e.const_kind = 2;
+      e.layer = &L;
+      for (int c = 0; c < R; ++c)
+        for (int hl = 0; hl < heads_of(c); ++hl) {
+          const int h = c * hpc + hl;
+          e.segs[c].push_back({&L.entry, h * hd, hd});
+          e.segs[c].push_back({&L.entry, d + h * hd, hd});
+          e.segs[c].push_back({&L.entry, 2 * d + h * 3 * S, 3 * S});
+        }
+      plans.push_back(e);
+    } else {
+      OpPlan e = gemv_op(OP_ENTRY_MLA, li, L.entry, d, hpc * (hd + D.rope) + Lper, H * (hd + D.rope) + Lt, gather0, d,
+                         dper, L.mixer_norm, L.mixer_norm_eps);
+      e.layer = &L;
+      for (int c = 0; c < R; ++c) {
+        for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, (c * hpc + hl) * hd, hd});
+        for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, d + Lt + (c * hpc + hl) * D.rope, D.rope});
+        const int l0 = std::min(Lt, c * Lper), ln = part(Lt, Lper, c);
+        if (ln > 0) e.segs[c].push_back({&L.entry, d + l0, ln});
+      }
+      plans.push_back(e);
+      OpPlan a{};
+      a.op.kind = OP_ATTN;
+      a.op.layer = li;
+      a.op.gather = G_LATENT;
+      a.op.gather_n = Lt;
+      a.op.gather_per = Lper;
+      a.op.in_n = Lt;
+      a.op.rows_per = hpc * hd;
+      a.op.rows_total = d;
+      a.op.lpr_log = 0;
+      a.const_kind = 3;
+      a.layer = &L;
+      a.segs.assign(R, {});
+      plans.push_back(a);
+    }
+    const int ygather_per = hpc * hd;
+    OpPlan o = gemv_op(OP_OUT, li, L.out, d, dper, d, G_VEC, d, ygather_per, nullptr, 0.0f);
+    for (int c = 0; c < R; ++c)
+      if (part(d, dper, c) > 0) o.segs[c].push_back({&L.out, c * dper, part(d, dper, c)});
+    plans.push_back(o);
+    OpPlan g = gemv_op(OP_GATE_UP, li, L.gate_up, d, 2 * Fper, 2 * F, G_RESID, d, dper, L.ffn_norm, L.ffn_norm_eps);
+    for (int c = 0; c < R; ++c)
+      if (part(F, Fper, c) > 0) g.segs[c].push_back({&L.gate_up, 2 * c * Fper, 2 * part(F, Fper, c)});
+    plans.push_back(g);
+    OpPlan dn = gemv_op(OP_DOWN, li, L.down, F, dper, d, G_VEC, F, Fper, nullptr, 0.0f);
+    for (int c = 0; c < R; ++c)
+      if (part(d, dper, c) > 0) dn.segs[c].push_back({&L.down, c * dper, part(d, dper, c)});
+    plans.push_back(dn);
+  }
+  {
+    OpPlan hp = gemv_op(OP_HEAD, -1, md.head, d, Vper, md.vocab, G_RESID, d, dper, md.final_norm, md.final_norm_eps);
+    for (int c = 0; c < R; ++c)
+      if (part(md.vocab, Vper, c) > 0) hp.segs[c].push_back({&md.head, c * Vper, part(md.vocab, Vper, c)});
+    plans.push_back(hp);
+  }
+  // ---- constants-chunk layouts (identical offsets for every CTA) ----------------------------------
+  size_t max_const = 16;
+  for (OpPlan& pl : plans) {
+    Op& op = pl.op;
+    size_t off = 0;
+    if (pl.const_kind == 1 || pl.const_kind == 2) {
+      op.c_norm = static_cast<int>(off);
+      off += r16(static_cast<size_t>(d) * 4);
+    }
+    if (pl.const_kind == 2) {
+      op.c_decay = static_cast<int>(off);
+      off += r16(hpc * S * 4);
+      op.c_theta = static_cast<int>(off);
+      off += r16(hpc * S * 4);
+      op.c_skip = static_cast<int>(off);
+      off += r16(hpc * hd * 4);
+      op.c_convw = static_cast<int>(off);
+      off += r16(static_cast<size_t>(hpc) * hd * D.taps * 4);
+      op.c_convb = static_cast<int>(off);
+      off += r16(hpc * hd * 4);
+    }
+    if (pl.const_kind == 3) {
+      op.c_wkn = static_cast<int>(off);
+      off += r16(static_cast<size_t>(hpc) * D.nope * D.rb_lat);
+      op.c_skn = static_cast<int>(off);
+      off += r16(static_cast<size_t>(hpc) * D.nope * D.ss_lat * 2);
+      op.c_bkn = static_cast<int>(off);
+      off += r16(hpc * D.nope * 4);
+      op.c_wv = static_cast<int>(off);
+      off += r16(static_cast<size_t>(hpc) * hd * D.rb_lat);
+      op.c_sv = static_cast<int>(off);
+      off += r16(static_cast<size_t>(hpc) * hd * D.ss_lat * 2);
+      op.c_bv = static_cast<int>(off);
+      off += r16(hpc * hd * 4);
+    }
+    op.has_const = pl.const_kind != 0;
+    max_const = std::max(max_const, off);
+    pl.op.n_chunks = 0;
+  }
+  if (max_const > stage) {
+    why = "a constants chunk does not fit a stream stage";
+    return false;
+  }
+  // ---- chunk the rows, lay out every CTA's stream ---------------------------------------------------
+  for (OpPlan& pl : plans) {
+    Op& op = pl.op;
+    if (op.kind == OP_ATTN) {
+      op.chunk_rows = 0;
+      op.n_chunks = 1;
+      continue;
+    }
+    const size_t per_row = op.row_bytes + op.scale_stride * 2 + 4;
+    int cr = static_cast<int>((stage - 64) / per_row);
+    if (op.kind == OP_GATE_UP) cr &= ~1;
+    cr = std::max(2, std::min(cr, std::max(2, op.rows_per)));
+    op.chunk_rows = cr;
+    op.n_chunks = op.has_const + (op.rows_per + cr - 1) / cr;
+  }
+  dec->ops.clear();
+  dec->op_rows.assign(plans.size() * R, 0);
+  int cpt = 0;
+  for (size_t i = 0; i < plans.size(); ++i) {
+    plans[i].op.first_chunk = cpt;
+    cpt += plans[i].op.n_chunks;
+    dec->ops.push_back(plans[i].op);
+  }
+  dec->cpt = cpt;
+  dec->head_first = plans.back().op.first_chunk;
+  dec->chunk_off.assign(static_cast<size_t>(R) * cpt, 0);
+  dec->chunk_bytes.assign(static_cast<size_t>(R) * cpt, 0);
+  dec->copies.clear();
+  size_t cursor = 0;
+  auto add = [&](size_t dst, const void* src, size_t width, size_t rows, size_t spitch, size_t dpitch) {
+    if (width == 0 || rows == 0) return;
+    dec->copies.push_back(CopyOp{dst, src, width, rows, spitch, dpitch});
+  };
+  for (int c = 0; c < R; ++c) {
+    int ci = 0;
+    for (size_t i = 0; i < plans.size(); ++i) {
+      const OpPlan& pl = plans[i];
+      const Op& op = pl.op;
+      int rows_c = 0;
+      for (const Segment& sg : pl.segs[c]) rows_c += sg.count;
+      if (op.kind == OP_ATTN) rows_c = heads_of(c) * hd;
+      dec->op_rows[i * R + c] = rows_c;
+      if (op.has_const) {
+        const size_t base = cursor;
+        size_t bytes = 16;
+        if (pl.const_kind == 1 || pl.const_kind == 2) {
+          add(base + op.c_norm, pl.norm, static_cast<size_t>(d) * 4, 1, 0, 0);
+          bytes = std::max(bytes, static_cast<size_t>(op.c_norm) + r16(static_cast<size_t>(d) * 4));
+        }
+        if (pl.const_kind == 2) {
+          const IvbLayerDesc& L = *pl.layer;
+          const int nh = heads_of(c), h0 = c * hpc;
+          if (nh > 0) {
+            add(base + op.c_decay, L.decay + h0 * S, nh * S * 4, 1, 0, 0);
+            add(base + op.c_theta, L.theta + h0 * S, nh * S * 4, 1, 0, 0);
+            add(base + op.c_skip, L.skip + h0 * hd, nh * hd * 4, 1, 0, 0);
+            add(base + op.c_convw, L.conv_weight + static_cast<size_t>(h0) * hd * D.taps, static_cast<size_t>(nh) * hd * D.taps * 4, 1, 0, 0);
+            add(base + op.c_convb, L.conv_bias + h0 * hd, nh * hd * 4, 1, 0, 0);
+          }
+          bytes = std::max(bytes, static_cast<size_t>(op.c_convb) + r16(hpc * hd * 4));
+        }
+        if (pl.const_kind == 3) {
+          const IvbLayerDesc& L = *pl.layer;
+          const int nh = heads_of(c), h0 = c * hpc;
+          const IvbTernary& kn = L.k_nope_up;
+          const IvbTernary& vu = L.v_up;
+          const size_t sgroups = static_cast<size_t>((Lt + 127) / 128) * 2;
+          if (nh > 0) {
+            add(base + op.c_wkn, kn.packed + static_cast<size_t>(h0) * D.nope * kn.row_bytes, D.rb_lat, nh * D.nope, kn.row_bytes, D.rb_lat);
+            add(base + op.c_skn, kn.scales + static_cast<size_t>(h0) * D.nope * kn.scale_stride, sgroups, nh * D.nope,
+                static_cast<size_t>(kn.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
+            add(base + op.c_bkn, kn.bias ? static_cast<const void*>(kn.bias + h0 * D.nope) : nullptr, nh * D.nope * 4, 1, 0, 0);
+            add(base + op.c_wv, vu.packed + static_cast<size_t>(h0) * hd * vu.row_bytes, D.rb_lat, nh * hd, vu.row_bytes, D.rb_lat);
+            add(base + op.c_sv, vu.scales + static_cast<size_t>(h0) * hd * vu.scale_stride, sgroups, nh * hd,
+                static_cast<size_t>(vu.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
+            add(base + op.c_bv, vu.bias ? static_cast<const void*>(vu.bias + h0 * hd) : nullptr, nh * hd * 4, 1, 0, 0);
+          }
+          bytes = std::max(bytes, static_cast<size_t>(op.c_bv) + r16(hpc * hd * 4));
+        }
+        dec->chunk_off[static_cast<size_t>(c) * cpt + ci] = base;
+        dec->chunk_bytes[static_cast<size_t>(c) * cpt + ci] = static_cast<unsigned>(r16(bytes));
+        cursor = r16(base + bytes);
+        ++ci;
+      }
+      if (op.kind == OP_ATTN) continue;
+      // row chunks: [k x row_bytes][k x scale_stride fp16, 16B pad][k x fp32 bias, 16B pad]
+      const int n_row_chunks = op.n_chunks - op.has_const;
+      for (int rc = 0; rc < n_row_chunks; ++rc) {
+        const int r0 = rc * op.chunk_rows;
+        const int k = std::max(0, std::min(op.chunk_rows, rows_c - r0));
+        const size_t base = cursor;
+        const size_t sc_off = static_cast<size_t>(k) * op.row_bytes;
+        const size_t b_off = sc_off + r16(static_cast<size_t>(k) * op.scale_stride * 2);
+        const size_t bytes = std::max<size_t>(16, b_off + r16(static_cast<size_t>(k) * 4));
+        // walk the segments covering virtual rows [r0, r0 + k)
+        int v = 0;
+        for (const Segment& sg : pl.segs[c]) {
+          const int a = std::max(r0, v), b = std::min(r0 + k, v + sg.count);
+          if (a < b) {
+            const int src_row = sg.row0 + (a - v);
+            const int n = b - a;
+            const IvbTernary& m = *sg.m;
+            const size_t dr = static_cast<size_t>(a - r0);
+            add(base + dr * op.row_bytes, m.packed + static_cast<size_t>(src_row) * m.row_bytes, op.row_bytes, n, m.row_bytes,
+                op.row_bytes);
+            add(base + sc_off + dr * op.scale_stride * 2, m.scales + static_cast<size_t>(src_row) * m.scale_stride,
+                static_cast<size_t>((m.in_features + 127) / 128) * 2, n, static_cast<size_t>(m.scale_stride) * 2,
+                static_cast<size_t>(op.scale_stride) * 2);
+            if (op.has_bias) add(base + b_off + dr * 4, m.bias + src_row, static_cast<size_t>(n) * 4, 1, 0, 0);
+          }
+          v += sg.count;
+        }
+        dec->chunk_off[static_cast<size_t>(c) * cpt + ci] = base;
+        dec->chunk_bytes[static_cast<size_t>(c) * cpt + ci] = static_cast<unsigned>(r16(bytes));
+        cursor = r16(base + bytes);
+        ++ci;
+      }
+    }
+  }
+  dec->stream_bytes = r16(cursor) + 256;
+  // ---- shared memory map ----------------------------------------------------------------------------
+  ClusterSmem& M = dec->sm;
+  size_t o = 0;
+  M.ring = 0;
+  M.stage_bytes = static_cast<int>(stage);
+  o += kStages * stage;
+  const int max_in = std::max(d, F);
+  const int pad_in = (max_in + 63) / 64 * 64;
+  M.xv = static_cast<int>(o);
+  o += r16(static_cast<size_t>(pad_in) * 4);
+  M.act = static_cast<int>(o);
+  o += r16(pad_in);
+  M.xsum = static_cast<int>(o);
+  o += r16(pad_in / 64 * 4);
+  M.resid = static_cast<int>(o);
+  o += r16(static_cast<size_t>(d) * 4);
+  int pub_n = std::max(std::max(hpc * hd, Lper), std::max(dper, Fper));
+  M.pub_n = pub_n;
+  M.pub = static_cast<int>(o);
+  o += r16(static_cast<size_t>(2) * pub_n * 4);
+  int loc_n = 0;
+  for (const Op& op : dec->ops) loc_n = std::max(loc_n, op.kind == OP_ATTN ? 0 : op.rows_per);
+  M.loc = static_cast<int>(o);
+  o += r16(static_cast<size_t>(loc_n) * 4);
+  M.red = static_cast<int>(o);
+  o += r16(64 * 4);
+  M.xl = static_cast<int>(o);
+  o += r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4);
+  M.u = static_cast<int>(o);
+  const int kc = dec->kc;
+  size_t u_need = r16(static_cast<size_t>(hpc) * (2 * S + hd * (2 + D.taps)) * 4);
+  u_need = std::max(u_need, r16(static_cast<size_t>(Vper) * 4) + 2 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
+  u_need = std::max(u_need, 2 * r16(static_cast<size_t>(R) * kc * 4) + 5 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
+  const size_t attn_fixed = r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4) + r16((Lt + 63) / 64 * 64) +
+                            static_cast<size_t>(Lt + 2 * D.rope + D.nope) * 4 + kWarps * Lt * 4 + 64;
+  const size_t per_pos = static_cast<size_t>(D.lpad) + 4 + static_cast<size_t>(D.rpad) * 2;
+  bool any_mla = false;
+  for (const IvbLayerDesc& L : dec->layers) any_mla |= L.kind == IVB_MLA;
+  int tile = 0;
+  if (any_mla) {
+    const size_t room = smem_cap > o + attn_fixed ? smem_cap - o - attn_fixed : 0;
+    tile = static_cast<int>(room / (2 * per_pos + 8)) / 16 * 16;
+    tile = std::min(tile, (md.max_len + 15) / 16 * 16);
+    if (tile < 16) {
+      why = "no room for an attention tile in shared memory";
+      return false;
+    }
+    tile = std::min(tile, 512);
+    u_need = std::max(u_need, attn_fixed + static_cast<size_t>(tile) * 4 + 64 + 2 * (r16(static_cast<size_t>(tile) * D.lpad) +
+                                                                                  r16(tile * 4) + r16(static_cast<size_t>(tile) * D.rpad * 2)));
+  }
+  D.tile = std::max(tile, 16);
+  o += r16(u_need);
+  M.total = static_cast<int>(o);
+  if (o > smem_cap) {
+    why = "the cluster decoder needs more shared memory than a CTA has";
+    return false;
+  }
+  dec->smem = o;
+  return true;
 }
 
 }  // namespace ivb
@@ -296,66 +1020,69 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
   dec->desc = *desc;
   dec->layers.assign(desc->layers, desc->layers + desc->num_layers);
   dec->desc.layers = nullptr;
-  Dims& D = dec->dims;
-  D.vocab = desc->vocab;
-  D.hidden = desc->hidden;
-  D.heads = desc->heads;
-  D.head_dim = desc->head_dim;
-  D.state_dim = desc->state_dim;
-  D.latent = desc->latent_dim;
-  D.rope = desc->rope_dim;
-  D.nope = desc->nope_dim;
-  D.dense = desc->dense;
-  D.max_len = desc->max_len;
-  D.max_top_k = desc->max_top_k;
-  D.act_eps = desc->act_eps;
-  D.clip = desc->norm_clip;
-  int mixer_width = D.hidden;
-  int widest = std::max(D.hidden, D.dense);
-  bool any_mla = false;
-  for (const IvbLayerDesc& L : dec->layers) {
-    mixer_width = std::max(mixer_width, L.entry.rows);
-    if (L.kind == IVB_MLA) any_mla = true;
-  }
-  D.mixer_width = mixer_width;
-  int dev = 0, sms = 0;
+  dec->ws = nullptr;
+  dec->trace = nullptr;
+  dec->trace_step = 0;
+  int dev = 0, optin = 0;
   IVB_CUDA(cudaGetDevice(&dev));
-  IVB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-  if (ctas <= 0) ctas = sms;
-  size_t smem = ivb_gemv_smem_bytes(widest);
-  if (any_mla) smem = std::max(smem, attn_smem_bytes(D.latent, D.rope, D.nope));
-  smem = std::max(smem, ivb_sample_smem_bytes(D.vocab));
-  if (smem > 227 * 1024) {
-    delete dec;
-    return fail(IVB_EINVAL, "the decoder needs %zu bytes of shared memory per CTA (vocab too large?)", smem);
+  IVB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  const size_t cap = static_cast<size_t>(optin) - 1024;  // static shared memory of the kernel
+  IVB_CUDA(cudaFuncSetAttribute(cluster_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
+  std::string why = "no cluster size fits";
+  bool planned = false;
+  for (int R : {16, 8, 4, 2, 1}) {
+    if (ctas > 0 && R > ctas) continue;
+    if (!plan(dec, R, cap, why)) continue;
+    IVB_CUDA(cudaFuncSetAttribute(cluster_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(R);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = dec->smem;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = R;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(cluster_decode_kernel), &cfg) != cudaSuccess ||
+        clusters < 1) {
+      cudaGetLastError();
+      why = "the device cannot schedule the cluster";
+      continue;
+    }
+    dec->R = R;
+    planned = true;
+    break;
   }
-  IVB_CUDA(cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  int per_sm = 0;
-  IVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_kernel, kThreads, smem));
-  if (per_sm < 1 || ctas > per_sm * sms) {
+  if (!planned) {
     delete dec;
-    return fail(IVB_EINVAL, "%d CTAs cannot be co-resident (%d per SM x %d SMs)", ctas, per_sm, sms);
+    return fail(IVB_EINVAL, "ivb_decoder_create: %s", why.c_str());
   }
-  dec->ctas = ctas;
-  dec->smem = smem;
+  const int R = dec->R;
   size_t off = 0;
-  const size_t n_phases = static_cast<size_t>(desc->num_layers) * 5 + 2;
-  dec->off_prog = off;
-  off = align_up(off + n_phases * sizeof(Phase), 256);
+  dec->off_stream = off;
+  off = align_up(off + dec->stream_bytes, 256);
+  dec->off_ops = off;
+  off = align_up(off + dec->ops.size() * sizeof(Op), 256);
+  dec->off_op_rows = off;
+  off = align_up(off + dec->op_rows.size() * 4, 256);
+  dec->off_chunk_off = off;
+  off = align_up(off + dec->chunk_off.size() * 8, 256);
+  dec->off_chunk_bytes = off;
+  off = align_up(off + dec->chunk_bytes.size() * 4, 256);
   dec->off_layers = off;
   off = align_up(off + dec->layers.size() * sizeof(IvbLayerDesc), 256);
+  dec->off_cand_key = off;
+  off = align_up(off + static_cast<size_t>(R) * dec->kc * 4, 256);
+  dec->off_cand_id = off;
+  off = align_up(off + static_cast<size_t>(R) * dec->kc * 4, 256);
+  dec->off_cand_n = off;
+  off = align_up(off + R * 4, 256);
   dec->off_sync = off;
   off = align_up(off + 256, 256);
-  dec->off_residual = off;
-  off = align_up(off + static_cast<size_t>(D.hidden) * 4, 256);
-  dec->off_mixer = off;
-  off = align_up(off + static_cast<size_t>(mixer_width) * 4, 256);
-  dec->off_y = off;
-  off = align_up(off + static_cast<size_t>(D.hidden) * 4, 256);
-  dec->off_ffn = off;
-  off = align_up(off + static_cast<size_t>(D.dense) * 4, 256);
   dec->total = off;
-  dec->ws = nullptr;
   *out = dec;
   return IVB_OK;
 }
@@ -364,11 +1091,9 @@ void ivb_decoder_destroy(IvbDecoder* dec) { delete dec; }
 
 uint64_t ivb_decoder_workspace_bytes(const IvbDecoder* dec) { return dec ? dec->total : 0; }
 
-int32_t ivb_decoder_num_phases(const IvbDecoder* dec) {
-  return dec ? static_cast<int32_t>(dec->layers.size() * 5 + 2) : 0;
-}
+int32_t ivb_decoder_num_phases(const IvbDecoder* dec) { return dec ? static_cast<int32_t>(dec->ops.size()) : 0; }
 
-int32_t ivb_decoder_ctas(const IvbDecoder* dec) { return dec ? dec->ctas : 0; }
+int32_t ivb_decoder_ctas(const IvbDecoder* dec) { return dec ? dec->R : 0; }
 
 int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream) {
   using namespace ivb;
@@ -376,55 +1101,26 @@ int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream) {
   if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(IVB_EINVAL, "workspace must be 256-byte aligned");
   unsigned char* ws = static_cast<unsigned char*>(workspace);
   dec->ws = ws;
-  float* residual = reinterpret_cast<float*>(ws + dec->off_residual);
-  float* mixer = reinterpret_cast<float*>(ws + dec->off_mixer);
-  float* y = reinterpret_cast<float*>(ws + dec->off_y);
-  float* ffn = reinterpret_cast<float*>(ws + dec->off_ffn);
-  const int G = dec->ctas;
-  auto gemv = [&](const IvbTernary& m, int epi, int layer, const float* in, const float* norm, float eps, float* out,
-                  int kind) {
-    Phase ph{};
-    ph.kind = kind;
-    ph.epilogue = epi;
-    ph.layer = layer;
-    ph.embed_input = 0;
-    ph.mat = m;
-    ph.in_vec = in;
-    ph.norm_w = norm;
-    ph.norm_eps = eps;
-    int per = (m.rows + G - 1) / G;
-    if (per & 1) ++per;
-    ph.rows_per_cta = per;
-    ph.out_vec = out;
-    ph.lpr_log = ivb_lpr_log(m.in_features);
-    return ph;
-  };
-  dec->prog.clear();
-  for (int i = 0; i < static_cast<int>(dec->layers.size()); ++i) {
-    const IvbLayerDesc& L = dec->layers[i];
-    Phase entry = gemv(L.entry, IVB_EPI_STORE, i, residual, L.mixer_norm, L.mixer_norm_eps, mixer, PH_GEMV);
-    entry.embed_input = i == 0 ? 1 : 0;
-    dec->prog.push_back(entry);
-    Phase mix{};
-    mix.kind = L.kind == IVB_MAMBA ? PH_SSM : PH_ATTN;
-    mix.layer = i;
-    dec->prog.push_back(mix);
-    dec->prog.push_back(gemv(L.out, IVB_EPI_RESIDUAL, i, y, nullptr, 0.0f, residual, PH_GEMV));
-    dec->prog.push_back(gemv(L.gate_up, IVB_EPI_SILU_PAIR, i, residual, L.ffn_norm, L.ffn_norm_eps, ffn, PH_GEMV));
-    dec->prog.push_back(gemv(L.down, IVB_EPI_RESIDUAL, i, ffn, nullptr, 0.0f, residual, PH_GEMV));
-  }
-  dec->prog.push_back(gemv(dec->desc.head, IVB_EPI_STORE, -1, residual, dec->desc.final_norm, dec->desc.final_norm_eps,
-                           dec->desc.logits, PH_HEAD));
-  Phase smp{};
-  smp.kind = PH_SAMPLE;
-  smp.layer = -1;
-  dec->prog.push_back(smp);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_prog, dec->prog.data(), dec->prog.size() * sizeof(Phase), cudaMemcpyHostToDevice, s));
+  unsigned char* blob = ws + dec->off_stream;
+  IVB_CUDA(cudaMemsetAsync(blob, 0, dec->stream_bytes, s));
+  for (const CopyOp& c : dec->copies) {
+    if (c.src == nullptr) {
+      IVB_CUDA(cudaMemsetAsync(blob + c.dst, 0, c.width * c.rows, s));
+    } else if (c.rows == 1) {
+      IVB_CUDA(cudaMemcpyAsync(blob + c.dst, c.src, c.width, cudaMemcpyDeviceToDevice, s));
+    } else {
+      IVB_CUDA(cudaMemcpy2DAsync(blob + c.dst, c.dpitch, c.src, c.spitch, c.width, c.rows, cudaMemcpyDeviceToDevice, s));
+    }
+  }
+  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_ops, dec->ops.data(), dec->ops.size() * sizeof(Op), cudaMemcpyHostToDevice, s));
+  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_op_rows, dec->op_rows.data(), dec->op_rows.size() * 4, cudaMemcpyHostToDevice, s));
+  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_off, dec->chunk_off.data(), dec->chunk_off.size() * 8, cudaMemcpyHostToDevice, s));
+  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_bytes, dec->chunk_bytes.data(), dec->chunk_bytes.size() * 4, cudaMemcpyHostToDevice, s));
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_layers, dec->layers.data(), dec->layers.size() * sizeof(IvbLayerDesc),
                            cudaMemcpyHostToDevice, s));
+  IVB_CUDA(cudaMemsetAsync(ws + dec->off_cand_n, 0, dec->R * 4, s));
   IVB_CUDA(cudaMemsetAsync(ws + dec->off_sync, 0, 256, s));
-  IVB_CUDA(cudaMemsetAsync(residual, 0, static_cast<size_t>(dec->dims.hidden) * 4, s));
   IVB_CUDA(cudaStreamSynchronize(s));
   return IVB_OK;
 }
@@ -434,48 +1130,72 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   using namespace ivb;
   if (dec == nullptr || dec->ws == nullptr) return fail(IVB_EINVAL, "ivb_decoder_run: decoder not bound");
   if (steps < 0) return fail(IVB_EINVAL, "ivb_decoder_run: negative step count");
-  const bool sample_only = (flags & IVB_RUN_SAMPLE_ONLY) != 0;
-  if (!sample_only && steps == 0) return IVB_OK;
-  if (!sample_only && feed == nullptr && !(flags & IVB_RUN_SAMPLE))
-    return fail(IVB_EINVAL, "ivb_decoder_run: without fed tokens every step must sample");
-  const long long barriers = static_cast<long long>(steps) * static_cast<long long>(dec->prog.size()) * dec->ctas;
-  if (barriers >= (1ll << 31)) return fail(IVB_EINVAL, "ivb_decoder_run: too many steps for one launch");
-  RunParams p{};
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   unsigned char* ws = dec->ws;
-  p.prog = reinterpret_cast<const Phase*>(ws + dec->off_prog);
-  p.n_phases = static_cast<int32_t>(dec->prog.size());
+  unsigned* error = reinterpret_cast<unsigned*>(ws + dec->off_sync);
+  const IvbModelDesc& md = dec->desc;
+  if (flags & IVB_RUN_SAMPLE_ONLY) {
+    IVB_CUDA(cudaMemsetAsync(error, 0, 4, s));
+    return ivb_sample(md.logits, md.seen, md.vocab, md.sampling, md.top_k, md.max_top_k, md.rng, md.token, nullptr, stream);
+  }
+  if (steps == 0) return IVB_OK;
+  if (feed == nullptr && !(flags & IVB_RUN_SAMPLE))
+    return fail(IVB_EINVAL, "ivb_decoder_run: without fed tokens every step must sample");
+  ClusterParams p{};
+  p.ops = reinterpret_cast<const Op*>(ws + dec->off_ops);
+  p.op_rows = reinterpret_cast<const int32_t*>(ws + dec->off_op_rows);
+  p.n_ops = static_cast<int32_t>(dec->ops.size());
+  p.kc = dec->kc;
+  p.head_first = dec->head_first;
+  p.chunks_per_token = dec->cpt;
   p.steps = steps;
+  p.chunk_off = reinterpret_cast<const unsigned long long*>(ws + dec->off_chunk_off);
+  p.chunk_bytes = reinterpret_cast<const unsigned*>(ws + dec->off_chunk_bytes);
+  p.stream = ws + dec->off_stream;
+  p.d = dec->d;
+  p.sm = dec->sm;
   p.layers = reinterpret_cast<const IvbLayerDesc*>(ws + dec->off_layers);
-  p.dims = dec->dims;
-  p.head = dec->desc.head;
-  p.residual = reinterpret_cast<float*>(ws + dec->off_residual);
-  p.mixer_in = reinterpret_cast<float*>(ws + dec->off_mixer);
-  p.ybuf = reinterpret_cast<float*>(ws + dec->off_y);
-  p.ffn_mid = reinterpret_cast<float*>(ws + dec->off_ffn);
-  p.logits = dec->desc.logits;
-  p.token = dec->desc.token;
-  p.position = dec->desc.position;
-  p.seen = dec->desc.seen;
-  p.history = dec->desc.history;
-  p.history_len = dec->desc.history_len;
-  p.sampling = dec->desc.sampling;
-  p.top_k = dec->desc.top_k;
-  p.rng = dec->desc.rng;
-  p.counter = reinterpret_cast<unsigned*>(ws + dec->off_sync);
-  p.error = p.counter + 1;
+  p.head = md.head;
+  p.logits = md.logits;
+  p.token = md.token;
+  p.position = md.position;
+  p.seen = md.seen;
+  p.history = md.history;
+  p.history_len = md.history_len;
+  p.sampling = md.sampling;
+  p.top_k = md.top_k;
+  p.rng = md.rng;
+  p.cand_key = reinterpret_cast<unsigned*>(ws + dec->off_cand_key);
+  p.cand_id = reinterpret_cast<int*>(ws + dec->off_cand_id);
+  p.cand_n = reinterpret_cast<int*>(ws + dec->off_cand_n);
+  p.error = error;
   p.feed = feed;
   p.timeout_ns = timeout_ns == 0 ? 1000000000ull : timeout_ns;
+  p.trace = dec->trace;
+  p.trace_step = dec->trace_step;
   p.flags = flags;
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
-  IVB_CUDA(cudaMemsetAsync(p.counter, 0, 2 * sizeof(unsigned), s));
-  if (sample_only) {
-    decode_kernel<<<1, kThreads, dec->smem, s>>>(p);
-    IVB_CUDA(cudaGetLastError());
-    return IVB_OK;
-  }
-  void* args[] = {&p};
-  IVB_CUDA(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(decode_kernel), dim3(dec->ctas), dim3(kThreads),
-                                       args, dec->smem, s));
+  IVB_CUDA(cudaMemsetAsync(error, 0, 4, s));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(dec->R);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = dec->smem;
+  cfg.stream = s;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeClusterDimension;
+  at[0].val.clusterDim.x = dec->R;
+  at[0].val.clusterDim.y = 1;
+  at[0].val.clusterDim.z = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  IVB_CUDA(cudaLaunchKernelEx(&cfg, cluster_decode_kernel, p));
+  return IVB_OK;
+}
+
+int32_t ivb_decoder_trace(IvbDecoder* dec, uint64_t* buffer, int32_t step) {
+  using namespace ivb;
+  if (dec == nullptr || step < 0) return fail(IVB_EINVAL, "ivb_decoder_trace: bad argument");
+  dec->trace = reinterpret_cast<unsigned long long*>(buffer);
+  dec->trace_step = step;
   return IVB_OK;
 }
 
@@ -485,10 +1205,10 @@ int32_t ivb_decoder_check(IvbDecoder* dec, void* stream) {
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   IVB_CUDA(cudaStreamSynchronize(s));
   unsigned word = 0;
-  IVB_CUDA(cudaMemcpy(&word, dec->ws + dec->off_sync + sizeof(unsigned), sizeof(word), cudaMemcpyDeviceToHost));
+  IVB_CUDA(cudaMemcpy(&word, dec->ws + dec->off_sync, sizeof(word), cudaMemcpyDeviceToHost));
   if (word == IVB_ECAPACITY) return fail(IVB_ECAPACITY, "the decoder has no free position left");
   if (word == IVB_EINVAL) return fail(IVB_EINVAL, "a token id is out of range for the vocabulary");
-  if (word != 0) return fail(static_cast<int32_t>(word), "a bounded inter-CTA wait gave up (device error word %u)", word);
+  if (word != 0) return fail(static_cast<int32_t>(word), "a bounded wait in the decode kernel gave up (device error word %u)", word);
   return IVB_OK;
 }
 

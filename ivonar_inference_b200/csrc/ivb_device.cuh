@@ -45,6 +45,57 @@ __device__ __forceinline__ unsigned long long global_ns() {
   return t;
 }
 
+// n floats from global (L2) into shared memory, eight independent loads in flight per thread.
+__device__ __forceinline__ void load_vector(const float* __restrict__ src, int n, float* dst) {
+  const int tid = threadIdx.x;
+  for (int base = 0; base < n; base += 8 * 256) {
+    float r[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + tid + k * 256;
+      r[k] = i < n ? __ldcg(src + i) : 0.0f;
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int i = base + tid + k * 256;
+      if (i < n) dst[i] = r[k];
+    }
+  }
+}
+
+// ---- bulk async copies (cp.async.bulk, TMA engine) into shared memory, completed on an mbarrier ----
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// dst, src 16-byte aligned; bytes a multiple of 16
+__device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
+  unsigned ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Timeline mark for tuning: thread 0 stores the globaltimer into marks[slot] when tracing.
+__device__ __forceinline__ void mark(unsigned long long* marks, int slot) {
+  if (marks != nullptr && threadIdx.x == 0) marks[slot] = global_ns();
+}
+
 __device__ __forceinline__ float sigmoid_f(float x) { return 1.0f / (1.0f + expf(-x)); }
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + expf(-x)); }
 __device__ __forceinline__ float h2f(uint16_t h) { return __half2float(__ushort_as_half(h)); }
@@ -149,7 +200,7 @@ static __device__ float quantize_block(float* xv, int n, const float* norm_w, fl
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
     for (int i = tid; i < n; i += kThreads) {
       const float a = __fmul_rn(xv[i], inv);
-      xv[i] = __fmul_rn(fminf(fmaxf(a, -clip), clip), __ldg(norm_w + i));
+      xv[i] = __fmul_rn(fminf(fmaxf(a, -clip), clip), norm_w[i]);  // norm_w may be shared or global
     }
   }
   float am = 0.0f;
@@ -234,8 +285,10 @@ __device__ __forceinline__ void gemv_prefetch(const IvbTernary& m, const GemvGeo
 
 // Dot products, reduction across lanes and epilogue. act/xsum/scale come from quantize_block.
 // res: shared scratch of kThreads floats (silu pairing).
+// pre: residual values of rows [r0, r1) loaded ahead (shared memory) or nullptr.
 static __device__ void gemv_rows(const IvbTernary& m, const GemvGeom& g, const int8_t* act, const int* xsum, float act_scale,
-                          int epilogue, float* out, uint4 (&pf)[kPrefetch], float (&pfs)[kPrefetch], float* res) {
+                          int epilogue, float* out, uint4 (&pf)[kPrefetch], float (&pfs)[kPrefetch], float* res,
+                          const float* pre) {
   const int tid = threadIdx.x;
   const int lpr = 1 << g.lpr_log;
   const int rpi = kThreads >> g.lpr_log;
@@ -279,7 +332,7 @@ static __device__ void gemv_rows(const IvbTernary& m, const GemvGeom& g, const i
             }
             __syncthreads();
           } else if (lead) {
-            if (epilogue == IVB_EPI_RESIDUAL) out[r] = ldcg_f(out + r) + result;
+            if (epilogue == IVB_EPI_RESIDUAL) out[r] = (pre != nullptr ? pre[r - g.r0] : ldcg_f(out + r)) + result;
             else out[r] = result;
           }
           acc = 0.0f;
@@ -354,176 +407,287 @@ static __device__ void ssm_channels(const IvbLayerDesc& L, int hidden, int heads
 // Latent attention for one head over the compressed cache (absorbed up-projections).
 //   score_t = a_t * <qa, ql_t> + qb + <q_rope_rot, k_rope_rot_t>     (qa = s * q_nope^T W_knope_h)
 //   out_h   = W_v_h (sum_t p_t a_t ql_t) + b_v_h
-// Exactly the reference's softmax(q.k) v with k_nope = up(latent), v = up(latent) (linear in the
+// Exactly the reference's softmax(q.k) v with k_nope = up(latent), v = up(latent) (both linear in the
 // int8 latent codes); reference ternary.cu:509-611, decoder.py:271-297, attention.py:136-151.
 // mixer_in = [q (hidden) | latent (L) | k_rope (heads * rope)].
+// Cache layout (device): latent codes [max_len][lpad] int8 (lpad = L rounded up to 16), scales
+// [max_len rounded up to 4] fp32, k_rope [heads][max_len][rpad] fp16 (rpad = rope rounded up to 8).
+// The head's weight rows and a tile of cached positions are bulk-copied (TMA engine) into shared
+// memory; the copies of the first tile are issued before the CTA waits for the entry projection.
 // ------------------------------------------------------------------------------------------------
-struct AttnSmem {
-  float* xv;      // [L]   latent fp32 (quantiser input)
-  int8_t* ql;     // [L]   codes of the current latent
-  float* qa;      // [L]
-  float* qr;      // [rope]  rotated, scaled query rope part
-  float* kr;      // [rope]  rotated k_rope of the current position
-  float* qn;      // [nope]  scaled query nope part
-  float* part;    // [kWarps][L + 2]
-  float* red;     // [64]
+struct AttnGeom {
+  int latent, lpad, rope, rpad, nope, head_dim, heads, max_len, tile;
+  int kn_rb, kn_ss, v_rb, v_ss;  // row bytes and scale strides of W_knope and W_v
+  // byte offsets into the attention shared-memory region
+  int o_wkn, o_skn, o_wv, o_sv, o_lat, o_lsc, o_kr, o_qa, o_qr, o_krc, o_qn, o_xv, o_ql, o_sc, o_part, o_red, total;
 };
 
-__device__ __forceinline__ float ternary_code_value(const uint8_t* row, int j) {
-  return static_cast<float>(static_cast<int>((__ldg(row + (j >> 2)) >> ((j & 3) << 1)) & 3) - 1);
+__host__ __device__ inline int round16(int v) { return (v + 15) / 16 * 16; }
+
+__host__ __device__ inline AttnGeom attn_geom(int latent, int rope, int nope, int head_dim, int heads, int max_len,
+                                              int kn_rb, int kn_ss, int v_rb, int v_ss, int tile) {
+  AttnGeom g;
+  g.latent = latent;
+  g.lpad = round16(latent);
+  g.rope = rope;
+  g.rpad = (rope + 7) / 8 * 8;
+  g.nope = nope;
+  g.head_dim = head_dim;
+  g.heads = heads;
+  g.max_len = max_len;
+  g.tile = tile;
+  g.kn_rb = kn_rb;
+  g.kn_ss = kn_ss;
+  g.v_rb = v_rb;
+  g.v_ss = v_ss;
+  int o = 0;
+  g.o_wkn = o;  o += round16(nope * kn_rb);
+  g.o_skn = o;  o += round16(nope * kn_ss * 2);
+  g.o_wv = o;   o += round16(head_dim * v_rb);
+  g.o_sv = o;   o += round16(head_dim * v_ss * 2);
+  g.o_lat = o;  o += round16(tile * g.lpad);
+  g.o_lsc = o;  o += round16(((tile + 3) / 4 * 4) * 4);
+  g.o_kr = o;   o += round16(tile * g.rpad * 2);
+  g.o_qa = o;   o += round16(latent * 4);
+  g.o_qr = o;   o += round16(rope * 4);
+  g.o_krc = o;  o += round16(rope * 4);
+  g.o_qn = o;   o += round16(nope * 4);
+  g.o_xv = o;   o += round16(((latent + 63) / 64 * 64) * 4);
+  g.o_ql = o;   o += round16((latent + 63) / 64 * 64);
+  g.o_sc = o;   o += round16((tile + 1) * 4);
+  g.o_part = o; o += round16(kWarps * latent * 4);
+  g.o_red = o;  o += round16(64 * 4);
+  g.total = o;
+  return g;
 }
 
-static __device__ void attention_head(const IvbLayerDesc& L, int hidden, int heads, int head_dim, int nope, int rope,
-                               int latent, float act_eps, const float* mixer_in, float* y, int h, int pos,
-                               const AttnSmem& sm) {
+// Thread 0 only: queue the bulk copies of the head's weights (if `weights`) and of cached positions
+// [start, start + count) on `bar`.
+__device__ __forceinline__ void attn_issue(const IvbLayerDesc& L, const AttnGeom& g, unsigned char* sm, int h, int start,
+                                           int count, bool weights, unsigned long long* bar) {
+  const unsigned wkn = g.nope * g.kn_rb, skn = g.nope * g.kn_ss * 2, wv = g.head_dim * g.v_rb, sv = g.head_dim * g.v_ss * 2;
+  const unsigned lat = count * g.lpad, lsc = ((count + 3) / 4 * 4) * 4, kr = count * g.rpad * 2;
+  unsigned bytes = (weights ? wkn + skn + wv + sv : 0u) + (count > 0 ? lat + lsc + kr : 0u);
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  fence_proxy_async();
+  mbar_expect_tx(bar, bytes);
+  if (weights) {
+    bulk_copy(sm + g.o_wkn, L.k_nope_up.packed + static_cast<size_t>(h) * g.nope * g.kn_rb, wkn, bar);
+    bulk_copy(sm + g.o_skn, L.k_nope_up.scales + static_cast<size_t>(h) * g.nope * g.kn_ss, skn, bar);
+    bulk_copy(sm + g.o_wv, L.v_up.packed + static_cast<size_t>(h) * g.head_dim * g.v_rb, wv, bar);
+    bulk_copy(sm + g.o_sv, L.v_up.scales + static_cast<size_t>(h) * g.head_dim * g.v_ss, sv, bar);
+  }
+  if (count > 0) {
+    bulk_copy(sm + g.o_lat, L.latent_q + static_cast<size_t>(start) * g.lpad, lat, bar);
+    bulk_copy(sm + g.o_lsc, L.latent_scale + start, lsc, bar);
+    bulk_copy(sm + g.o_kr, L.k_rope_cache + (static_cast<size_t>(h) * g.max_len + start) * g.rpad, kr, bar);
+  }
+}
+
+// Bounded wait for the bulk copies on `bar` (phase parity `parity`); false after timeout_ns.
+__device__ __forceinline__ bool attn_wait(unsigned long long* bar, unsigned parity, unsigned long long timeout_ns,
+                                          unsigned* error) {
+  unsigned long long t0 = 0ull;
+  unsigned spins = 0u;
+  while (!mbar_try_wait(bar, parity)) {
+    if ((++spins & 255u) == 0u) {
+      const unsigned long long t = global_ns();
+      if (t0 == 0ull) {
+        t0 = t;
+      } else if (t - t0 > timeout_ns) {
+        atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ float code_value(const unsigned char* row, int j) {
+  return static_cast<float>(static_cast<int>((row[j >> 2] >> ((j & 3) << 1)) & 3) - 1);
+}
+
+// Returns false if a bulk copy did not complete in time. `parity` is the CTA's mbarrier phase bit.
+// The caller issued attn_issue(weights = true, tile 0) for this head before the phase started.
+static __device__ bool attention_head(const IvbLayerDesc& L, const AttnGeom& g, int hidden, float act_eps,
+                                      const float* mixer_in, float* y, int h, int pos, unsigned char* sm,
+                                      unsigned long long* bar, unsigned& parity, unsigned long long timeout_ns,
+                                      unsigned* error, unsigned long long* marks = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  // 1. current latent -> int8 codes (natural order) and scale, exactly as the up-projection input
-  for (int j = tid; j < latent; j += kThreads) sm.xv[j] = ldcg_f(mixer_in + hidden + j);
+  const int latent = g.latent, rope = g.rope, nope = g.nope, hd = g.head_dim;
+  float* qa = reinterpret_cast<float*>(sm + g.o_qa);
+  float* qr = reinterpret_cast<float*>(sm + g.o_qr);
+  float* krc = reinterpret_cast<float*>(sm + g.o_krc);
+  float* qn = reinterpret_cast<float*>(sm + g.o_qn);
+  float* xv = reinterpret_cast<float*>(sm + g.o_xv);
+  int8_t* qlc = reinterpret_cast<int8_t*>(sm + g.o_ql);
+  float* sc = reinterpret_cast<float*>(sm + g.o_sc);
+  float* part = reinterpret_cast<float*>(sm + g.o_part);
+  float* red = reinterpret_cast<float*>(sm + g.o_red);
+  const int8_t* tlat = reinterpret_cast<const int8_t*>(sm + g.o_lat);
+  const float* tlsc = reinterpret_cast<const float*>(sm + g.o_lsc);
+  const uint16_t* tkr = reinterpret_cast<const uint16_t*>(sm + g.o_kr);
+  // 1. current latent -> int8 codes and scale (the up-projection's input quantisation)
+  load_vector(mixer_in + hidden, latent, xv);
   __syncthreads();
-  const float a_cur = quantize_block(sm.xv, latent, nullptr, 0.0f, 0.0f, act_eps, sm.ql, false, nullptr, sm.red);
+  const float a_cur = quantize_block(xv, latent, nullptr, 0.0f, 0.0f, act_eps, qlc, false, nullptr, red);
+  mark(marks, 1);
   if (h == 0) {
-    for (int j = tid; j < latent; j += kThreads) L.latent_q[static_cast<size_t>(pos) * latent + j] = sm.ql[j];
+    for (int j = tid; j < latent; j += kThreads) L.latent_q[static_cast<size_t>(pos) * g.lpad + j] = qlc[j];
     if (tid == 0) L.latent_scale[pos] = a_cur;
   }
-  // 2. RoPE on the query rope part and on k_rope; write k_rope to the cache
-  const float sc = L.attn_scale;
-  const float* rtab = L.rope + static_cast<size_t>(pos) * rope;  // [rope/2][2]
+  // 2. RoPE on the query rope part and on k_rope; append k_rope; scaled query nope part
+  const float scl = L.attn_scale;
+  const float* rtab = L.rope + static_cast<size_t>(pos) * rope;
   for (int jr = tid; jr < rope / 2; jr += kThreads) {
     const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
-    const float q0 = ldcg_f(mixer_in + h * head_dim + nope + 2 * jr);
-    const float q1 = ldcg_f(mixer_in + h * head_dim + nope + 2 * jr + 1);
-    const float k0 = ldcg_f(mixer_in + hidden + latent + h * rope + 2 * jr);
-    const float k1 = ldcg_f(mixer_in + hidden + latent + h * rope + 2 * jr + 1);
-    sm.qr[2 * jr] = (q0 * cs - q1 * sn) * sc;
-    sm.qr[2 * jr + 1] = (q0 * sn + q1 * cs) * sc;
+    const float q0 = __ldcg(mixer_in + h * hd + nope + 2 * jr), q1 = __ldcg(mixer_in + h * hd + nope + 2 * jr + 1);
+    const float k0 = __ldcg(mixer_in + hidden + latent + h * rope + 2 * jr);
+    const float k1 = __ldcg(mixer_in + hidden + latent + h * rope + 2 * jr + 1);
+    qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
+    qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
     const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
-    sm.kr[2 * jr] = kr0;
-    sm.kr[2 * jr + 1] = kr1;
-    uint16_t* kc = L.k_rope_cache + (static_cast<size_t>(pos) * heads + h) * rope;
+    krc[2 * jr] = kr0;
+    krc[2 * jr + 1] = kr1;
+    uint16_t* kc = L.k_rope_cache + (static_cast<size_t>(h) * g.max_len + pos) * g.rpad;
     kc[2 * jr] = f2h(kr0);
     kc[2 * jr + 1] = f2h(kr1);
   }
-  // 3. absorbed query qa[j] = sum_e s*q_nope[e] * W_knope[h*nope+e][j]
-  for (int e = tid; e < nope; e += kThreads) sm.qn[e] = ldcg_f(mixer_in + h * head_dim + e) * sc;
+  for (int e = tid; e < nope; e += kThreads) qn[e] = __ldcg(mixer_in + h * hd + e) * scl;
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  // 3. weights and the first cache tile
+  if (!attn_wait(bar, parity, timeout_ns, error)) return false;
+  parity ^= 1u;
   __syncthreads();
-  const IvbTernary& kn = L.k_nope_up;
+  mark(marks, 2);
+  // 4. absorbed query qa[j] = sum_e qn[e] * W_knope[e][j]
+  const unsigned char* wkn = sm + g.o_wkn;
+  const uint16_t* skn = reinterpret_cast<const uint16_t*>(sm + g.o_skn);
   for (int j = tid; j < latent; j += kThreads) {
     float acc = 0.0f;
-    for (int e = 0; e < nope; ++e) {
-      const int r = h * nope + e;
-      const uint8_t* row = kn.packed + static_cast<size_t>(r) * kn.row_bytes;
-      const float w = ternary_code_value(row, j) * h2f(__ldg(kn.scales + static_cast<size_t>(r) * kn.scale_stride + (j >> 7)));
-      acc = fmaf(sm.qn[e], w, acc);
-    }
-    sm.qa[j] = acc;
+    for (int e = 0; e < nope; ++e) acc = fmaf(qn[e], code_value(wkn + e * g.kn_rb, j) * h2f(skn[e * g.kn_ss + (j >> 7)]), acc);
+    qa[j] = acc;
   }
   float qb = 0.0f;
-  if (kn.bias != nullptr) {
+  if (L.k_nope_up.bias != nullptr) {
     float p = 0.0f;
-    for (int e = tid; e < nope; e += kThreads) p = fmaf(sm.qn[e], __ldg(kn.bias + h * nope + e), p);
-    qb = block_sum(p, sm.red);
+    for (int e = tid; e < nope; e += kThreads) p = fmaf(qn[e], __ldg(L.k_nope_up.bias + h * nope + e), p);
+    qb = block_sum(p, red);
   } else {
     __syncthreads();
   }
-  // 4. online softmax over t = warp, warp + 8, ...; lane owns latent j = lane + 32 i
+  mark(marks, 3);
+  // 5. scores / softmax / weighted latent sum over cache tiles (the current position ends the last one)
   const int per_lane = (latent + 31) >> 5;
+  float qa_r[kMaxLatentPerLane];
   float u[kMaxLatentPerLane];
-#pragma unroll
-  for (int i = 0; i < kMaxLatentPerLane; ++i) u[i] = 0.0f;
-  float m = -INFINITY, l = 0.0f;
-  for (int t = warp; t <= pos; t += kWarps) {
-    const bool cur = t == pos;
-    const int8_t* qlt = cur ? sm.ql : L.latent_q + static_cast<size_t>(t) * latent;
-    const float at = cur ? a_cur : ldcg_f(L.latent_scale + t);
-    float codes[kMaxLatentPerLane];
-    float part = 0.0f;
-#pragma unroll
-    for (int i = 0; i < kMaxLatentPerLane; ++i) {
-      const int j = lane + (i << 5);
-      float cval = 0.0f;
-      if (i < per_lane && j < latent) cval = static_cast<float>(cur ? qlt[j] : __ldcg(qlt + j));
-      codes[i] = cval;
-      if (i < per_lane && j < latent) part = fmaf(sm.qa[j], cval, part);
-    }
-    float rp = 0.0f;
-    const uint16_t* krt = L.k_rope_cache + (static_cast<size_t>(t) * heads + h) * rope;
-    for (int r = lane; r < rope; r += 32) {
-      const float kv = cur ? sm.kr[r] : h2f(__ldcg(krt + r));
-      rp = fmaf(sm.qr[r], kv, rp);
-    }
-    part = warp_sum(part);
-    rp = warp_sum(rp);
-    const float s = at * part + qb + rp;
-    const float mn = fmaxf(m, s);
-    const float corr = expf(m - mn);
-    const float wgt = expf(s - mn);
-    l = l * corr + wgt;
-    const float wa = wgt * at;
-#pragma unroll
-    for (int i = 0; i < kMaxLatentPerLane; ++i) u[i] = u[i] * corr + wa * codes[i];
-    m = mn;
-  }
-  // 5. merge the warps
-  float* mine = sm.part + warp * (latent + 2);
 #pragma unroll
   for (int i = 0; i < kMaxLatentPerLane; ++i) {
     const int j = lane + (i << 5);
-    if (i < per_lane && j < latent) mine[j] = u[i];
+    qa_r[i] = (i < per_lane && j < latent) ? qa[j] : 0.0f;
+    u[i] = 0.0f;
   }
-  if (lane == 0) {
-    mine[latent] = m;
-    mine[latent + 1] = l;
-  }
-  __syncthreads();
-  float mm = -INFINITY;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) mm = fmaxf(mm, sm.part[w * (latent + 2) + latent]);
-  float ltot = 0.0f;
-#pragma unroll
-  for (int w = 0; w < kWarps; ++w) {
-    const float mw = sm.part[w * (latent + 2) + latent];
-    const float f = mw == -INFINITY ? 0.0f : expf(mw - mm);
-    ltot += f * sm.part[w * (latent + 2) + latent + 1];
-  }
-  for (int j = tid; j < latent; j += kThreads) {
-    float v = 0.0f;
-#pragma unroll
-    for (int w = 0; w < kWarps; ++w) {
-      const float mw = sm.part[w * (latent + 2) + latent];
-      const float f = mw == -INFINITY ? 0.0f : expf(mw - mm);
-      v = fmaf(f, sm.part[w * (latent + 2) + j], v);
+  float m_run = -INFINITY, l_run = 0.0f;
+  const int n_tiles = pos == 0 ? 1 : (pos + g.tile - 1) / g.tile;
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    const int start = ti * g.tile;
+    const int count = min(g.tile, pos - start);
+    const bool last = ti == n_tiles - 1;
+    if (ti > 0) {
+      if (tid == 0) attn_issue(L, g, sm, h, start, count, false, bar);
+      if (!attn_wait(bar, parity, timeout_ns, error)) return false;
+      parity ^= 1u;
     }
-    sm.xv[j] = v;  // reuse as the weighted latent sum
+    const int npos = count + (last ? 1 : 0);
+    for (int k = warp; k < npos; k += kWarps) {
+      const bool cur = k == count;
+      const int8_t* ql = cur ? qlc : tlat + k * g.lpad;
+      const float at = cur ? a_cur : tlsc[k];
+      float dot = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kMaxLatentPerLane; ++i) {
+        const int j = lane + (i << 5);
+        if (i < per_lane && j < latent) dot = fmaf(qa_r[i], static_cast<float>(ql[j]), dot);
+      }
+      float rp = 0.0f;
+      for (int r = lane; r < rope; r += 32) rp = fmaf(qr[r], cur ? krc[r] : h2f(tkr[k * g.rpad + r]), rp);
+      dot = warp_sum(dot);
+      rp = warp_sum(rp);
+      if (lane == 0) sc[k] = at * dot + qb + rp;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, sc[k]);
+    mx = block_max(mx, red);
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+    float ls = 0.0f;
+    for (int k = tid; k < npos; k += kThreads) {
+      const float e = expf(sc[k] - m_new);
+      sc[k] = e;
+      ls += e;
+    }
+    ls = block_sum(ls, red);
+    l_run = l_run * corr + ls;
+#pragma unroll
+    for (int i = 0; i < kMaxLatentPerLane; ++i) u[i] *= corr;
+    for (int k = warp; k < npos; k += kWarps) {
+      const bool cur = k == count;
+      const int8_t* ql = cur ? qlc : tlat + k * g.lpad;
+      const float ea = sc[k] * (cur ? a_cur : tlsc[k]);
+#pragma unroll
+      for (int i = 0; i < kMaxLatentPerLane; ++i) {
+        const int j = lane + (i << 5);
+        if (i < per_lane && j < latent) u[i] = fmaf(ea, static_cast<float>(ql[j]), u[i]);
+      }
+    }
+    m_run = m_new;
+    __syncthreads();
+  }
+  mark(marks, 4);
+  // 6. merge the warps' partial sums (warps in order)
+#pragma unroll
+  for (int i = 0; i < kMaxLatentPerLane; ++i) {
+    const int j = lane + (i << 5);
+    if (i < per_lane && j < latent) part[warp * latent + j] = u[i];
   }
   __syncthreads();
-  // 6. out_h[e] = W_v[h*hd+e] . u / l + b_v
-  const IvbTernary& vu = L.v_up;
-  int tpr = kThreads / head_dim;
+  for (int j = tid; j < latent; j += kThreads) {
+    float v = part[j];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) v += part[w * latent + j];
+    xv[j] = v;
+  }
+  __syncthreads();
+  mark(marks, 5);
+  // 7. out_h[e] = W_v[h*hd+e] . u / l + b_v
+  const unsigned char* wv = sm + g.o_wv;
+  const uint16_t* sv = reinterpret_cast<const uint16_t*>(sm + g.o_sv);
+  int tpr = kThreads / hd;
   if (tpr > 32) tpr = 32;
   int tpr_log = 0;
   while ((2 << tpr_log) <= tpr) ++tpr_log;
   tpr = 1 << tpr_log;
-  const float inv_l = 1.0f / ltot;
-  for (int base = 0; base < head_dim; base += kThreads >> tpr_log) {
+  const float inv_l = 1.0f / l_run;
+  for (int base = 0; base < hd; base += kThreads >> tpr_log) {
     const int e = base + (tid >> tpr_log);
-    const int part_id = tid & (tpr - 1);
+    const int pid = tid & (tpr - 1);
     float acc = 0.0f;
-    if (e < head_dim) {
-      const int r = h * head_dim + e;
-      const uint8_t* row = vu.packed + static_cast<size_t>(r) * vu.row_bytes;
-      const uint16_t* srow = vu.scales + static_cast<size_t>(r) * vu.scale_stride;
+    if (e < hd) {
+      const unsigned char* row = wv + e * g.v_rb;
       const int span = (latent + tpr - 1) / tpr;
-      const int j0 = part_id * span, j1 = min(latent, j0 + span);
-      for (int j = j0; j < j1; ++j) acc = fmaf(ternary_code_value(row, j) * h2f(__ldg(srow + (j >> 7))), sm.xv[j], acc);
+      const int j0 = pid * span, j1 = min(latent, j0 + span);
+      for (int j = j0; j < j1; ++j) acc = fmaf(code_value(row, j) * h2f(sv[e * g.v_ss + (j >> 7)]), xv[j], acc);
     }
     for (int off = 1; off < tpr; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
-    if (e < head_dim && part_id == 0) {
+    if (e < hd && pid == 0) {
       float o = acc * inv_l;
-      if (vu.bias != nullptr) o += __ldg(vu.bias + h * head_dim + e);
-      y[h * head_dim + e] = o;
+      if (L.v_up.bias != nullptr) o += __ldg(L.v_up.bias + h * hd + e);
+      y[h * hd + e] = o;
     }
   }
   __syncthreads();
+  return true;
 }
 
 // ------------------------------------------------------------------------------------------------
@@ -565,82 +729,158 @@ __device__ __forceinline__ float key_value(unsigned k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
+constexpr int kCompact = 4096;  // candidates kept after the first radix pass when they fit
+
 struct SampleSmem {
   unsigned* keys;    // [vocab]
   unsigned* hist;    // [kWarps][256]
   unsigned* ckey;    // [kMaxTopK]
   int* cidx;         // [kMaxTopK]
   float* cprob;      // [kMaxTopK]
+  unsigned* pkey;    // [kCompact] keys sharing the selected prefix
+  int* pidx;         // [kCompact]
   int* misc;         // [16]
   float* red;        // [64]
 };
 
+__host__ __device__ inline size_t sample_smem_bytes(int vocab) {
+  return static_cast<size_t>(vocab) * 4 + kWarps * 256 * 4 + kMaxTopK * 12 + kCompact * 8 + 16 * 4 + 64 * 4 + 16;
+}
+
+__device__ __forceinline__ void carve_sample(unsigned char* smem, int vocab, SampleSmem& sm) {
+  sm.keys = reinterpret_cast<unsigned*>(smem);
+  sm.hist = sm.keys + vocab;
+  sm.ckey = sm.hist + kWarps * 256;
+  sm.cidx = reinterpret_cast<int*>(sm.ckey + kMaxTopK);
+  sm.cprob = reinterpret_cast<float*>(sm.cidx + kMaxTopK);
+  sm.pkey = reinterpret_cast<unsigned*>(sm.cprob + kMaxTopK);
+  sm.pidx = reinterpret_cast<int*>(sm.pkey + kCompact);
+  sm.misc = sm.pidx + kCompact;
+  sm.red = reinterpret_cast<float*>(sm.misc + 16);
+}
+
+__device__ __forceinline__ unsigned score_key(float logit, unsigned char flag, float inv_t, float pen, float ipen) {
+  float s = logit * inv_t;
+  if (flag) s *= s > 0.0f ? ipen : pen;
+  return order_key(s);
+}
+
+// One 8-bit radix digit over `n` keys (from `keys`, or from the compact list when compact): histogram
+// of the digit at `shift` among keys matching prefix/mask, then the digit holding the remaining-th
+// largest key. Updates prefix, mask, remaining; returns the count of keys in the selected bin.
+static __device__ int radix_digit(const SampleSmem& sm, const unsigned* keys, int n, int shift, unsigned& prefix, unsigned& mask,
+                           int& remaining) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  for (int b = tid; b < kWarps * 256; b += kThreads) sm.hist[b] = 0u;
+  __syncthreads();
+  unsigned* wh = sm.hist + warp * 256;
+  for (int base = 0; base < n; base += kThreads) {
+    const int i = base + tid;
+    const unsigned key = i < n ? keys[i] : 0u;
+    const bool in = i < n && (key & mask) == prefix;
+    const unsigned digit = in ? (key >> shift) & 255u : 256u;
+    const unsigned active = __ballot_sync(kFull, in);
+    if (in) {
+      const unsigned peers = __match_any_sync(active, digit);
+      if (lane == __ffs(peers) - 1) atomicAdd(wh + digit, static_cast<unsigned>(__popc(peers)));
+    }
+  }
+  __syncthreads();
+  // thread t owns digit d = 255 - t (descending) so an inclusive scan counts keys with digit >= d
+  const int d = 255 - tid;
+  unsigned cnt = 0;
+#pragma unroll
+  for (int w = 0; w < kWarps; ++w) cnt += sm.hist[w * 256 + d];
+  unsigned incl = cnt;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const unsigned o = __shfl_up_sync(kFull, incl, off);
+    if (lane >= off) incl += o;
+  }
+  if (lane == 31) sm.misc[warp] = static_cast<int>(incl);
+  __syncthreads();
+  unsigned carry = 0;
+  for (int w = 0; w < warp; ++w) carry += static_cast<unsigned>(sm.misc[w]);
+  incl += carry;
+  const unsigned above = incl - cnt;
+  if (cnt > 0 && static_cast<int>(above) < remaining && remaining <= static_cast<int>(above + cnt)) {
+    sm.misc[8] = d;
+    sm.misc[9] = remaining - static_cast<int>(above);
+    sm.misc[12] = static_cast<int>(cnt);
+  }
+  __syncthreads();
+  prefix |= static_cast<unsigned>(sm.misc[8]) << shift;
+  mask |= 255u << shift;
+  remaining = sm.misc[9];
+  const int bin = sm.misc[12];
+  __syncthreads();
+  return bin;
+}
+
 static __device__ void sample_block(const float* logits, uint8_t* seen, int vocab, const float* sampling, const int64_t* top_k_ptr,
-                             int max_top_k, uint64_t* rng, int64_t* token, int64_t* history, const SampleSmem& sm) {
+                                    int max_top_k, uint64_t* rng, int64_t* token, int64_t* history, const SampleSmem& sm,
+                                    unsigned long long* marks = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float inv_t = 1.0f / __ldcg(sampling);
   const float pen = __ldcg(sampling + 1), ipen = __ldcg(sampling + 2);
-  long long kreq = ldcg_i64(top_k_ptr);
-  int cap = min(min(max_top_k, vocab), kMaxTopK);
+  const long long kreq = ldcg_i64(top_k_ptr);
+  const int cap = min(min(max_top_k, vocab), kMaxTopK);
   const int K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
-  for (int i = tid; i < vocab; i += kThreads) {
-    float s = ldcg_f(logits + i) * inv_t;
-    if (__ldcg(seen + i)) s *= s > 0.0f ? ipen : pen;
-    sm.keys[i] = order_key(s);
+  // scores -> order-preserving keys, four logits and flags per load, four loads in flight
+  const int n4 = vocab >> 2;
+  const float4* l4 = reinterpret_cast<const float4*>(logits);
+  const uchar4* f4 = reinterpret_cast<const uchar4*>(seen);
+  for (int base = 0; base < n4; base += 4 * kThreads) {
+    float4 lv[4];
+    uchar4 fv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = base + tid + u * kThreads;
+      if (q < n4) {
+        lv[u] = __ldcg(l4 + q);
+        fv[u] = __ldcg(f4 + q);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = base + tid + u * kThreads;
+      if (q < n4) {
+        sm.keys[4 * q] = score_key(lv[u].x, fv[u].x, inv_t, pen, ipen);
+        sm.keys[4 * q + 1] = score_key(lv[u].y, fv[u].y, inv_t, pen, ipen);
+        sm.keys[4 * q + 2] = score_key(lv[u].z, fv[u].z, inv_t, pen, ipen);
+        sm.keys[4 * q + 3] = score_key(lv[u].w, fv[u].w, inv_t, pen, ipen);
+      }
+    }
   }
+  for (int i = 4 * n4 + tid; i < vocab; i += kThreads) sm.keys[i] = score_key(__ldcg(logits + i), __ldcg(seen + i), inv_t, pen, ipen);
   __syncthreads();
-  // radix select of the K-th largest key
+  mark(marks, 1);
+  // radix select of the K-th largest key: first digit over all keys, the rest over a compact list
   unsigned prefix = 0u, mask = 0u;
   int remaining = K;
-  for (int shift = 24; shift >= 0; shift -= 8) {
-    for (int b = tid; b < kWarps * 256; b += kThreads) sm.hist[b] = 0u;
+  const int bin = radix_digit(sm, sm.keys, vocab, 24, prefix, mask, remaining);
+  mark(marks, 2);
+  if (bin <= kCompact) {
+    if (tid == 0) sm.misc[13] = 0;
     __syncthreads();
-    unsigned* wh = sm.hist + warp * 256;
-    for (int base = 0; base < vocab; base += kThreads) {
-      const int i = base + tid;
-      const bool in = i < vocab && (sm.keys[i] & mask) == prefix;
-      const unsigned digit = in ? (sm.keys[i] >> shift) & 255u : 256u;
-      const unsigned active = __ballot_sync(kFull, in);
-      if (in) {
-        const unsigned peers = __match_any_sync(active, digit);
-        if (lane == __ffs(peers) - 1) atomicAdd(wh + digit, static_cast<unsigned>(__popc(peers)));
+    for (int i = tid; i < vocab; i += kThreads) {
+      const unsigned k = sm.keys[i];
+      if ((k & mask) == prefix) {
+        const int slot = atomicAdd(&sm.misc[13], 1);
+        sm.pkey[slot] = k;
+        sm.pidx[slot] = i;
       }
     }
     __syncthreads();
-    // thread t owns digit d = 255 - t (descending order) so an inclusive scan counts digits >= d
-    const int d = 255 - tid;
-    unsigned cnt = 0;
-    if (tid < 256) {
-#pragma unroll
-      for (int w = 0; w < kWarps; ++w) cnt += sm.hist[w * 256 + d];
-    }
-    unsigned incl = cnt;
-#pragma unroll
-    for (int off = 1; off < 32; off <<= 1) {
-      const unsigned o = __shfl_up_sync(kFull, incl, off);
-      if (lane >= off) incl += o;
-    }
-    if (lane == 31) sm.misc[warp] = static_cast<int>(incl);
-    __syncthreads();
-    unsigned carry = 0;
-    for (int w = 0; w < warp; ++w) carry += static_cast<unsigned>(sm.misc[w]);
-    incl += carry;
-    const unsigned above = incl - cnt;  // keys with a larger digit
-    __syncthreads();
-    if (tid < 256 && cnt > 0 && static_cast<int>(above) < remaining && remaining <= static_cast<int>(above + cnt)) {
-      sm.misc[8] = d;
-      sm.misc[9] = remaining - static_cast<int>(above);
-    }
-    __syncthreads();
-    prefix |= static_cast<unsigned>(sm.misc[8]) << shift;
-    mask |= 255u << shift;
-    remaining = sm.misc[9];
-    __syncthreads();
+    for (int shift = 16; shift >= 0; shift -= 8) radix_digit(sm, sm.pkey, bin, shift, prefix, mask, remaining);
+  } else {
+    for (int shift = 16; shift >= 0; shift -= 8) radix_digit(sm, sm.keys, vocab, shift, prefix, mask, remaining);
   }
-  const unsigned thr = prefix;  // K-th largest key; `remaining` copies of it are taken, lowest index first
+  mark(marks, 3);
+  const unsigned thr = prefix;  // the K-th largest key; `remaining` copies of it are taken
   if (tid == 0) {
-    sm.misc[10] = 0;  // count of keys > thr
-    sm.misc[11] = 0;  // count of keys == thr gathered
+    sm.misc[10] = 0;  // keys > thr gathered
+    sm.misc[11] = 0;  // keys == thr counted
   }
   __syncthreads();
   for (int i = tid; i < vocab; i += kThreads) {
@@ -649,12 +889,26 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
       const int slot = atomicAdd(&sm.misc[10], 1);
       sm.ckey[slot] = k;
       sm.cidx[slot] = i;
+    } else if (k == thr) {
+      atomicAdd(&sm.misc[11], 1);
     }
   }
   __syncthreads();
   const int greater = sm.misc[10];
-  if (warp == 0) {
-    // ties at the threshold: take the `remaining` lowest indices, scanning in index order
+  const int ties = sm.misc[11];
+  if (ties == remaining) {
+    // every key equal to the threshold is taken
+    if (tid == 0) sm.misc[14] = 0;
+    __syncthreads();
+    for (int i = tid; i < vocab; i += kThreads) {
+      if (sm.keys[i] == thr) {
+        const int slot = greater + atomicAdd(&sm.misc[14], 1);
+        sm.ckey[slot] = thr;
+        sm.cidx[slot] = i;
+      }
+    }
+  } else if (warp == 0) {
+    // more ties than places: the lowest indices win, scanned in index order
     int taken = 0;
     for (int base = 0; base < vocab && taken < remaining; base += 32) {
       const int i = base + lane;
@@ -669,6 +923,7 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
     }
   }
   __syncthreads();
+  mark(marks, 4);
   // order candidates by (key desc, index asc): rank by counting
   for (int c = tid; c < K; c += kThreads) {
     const unsigned kc = sm.ckey[c];
@@ -678,10 +933,11 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
       const unsigned ko = sm.ckey[o];
       rank += (ko > kc || (ko == kc && sm.cidx[o] < ic)) ? 1 : 0;
     }
-    sm.hist[rank] = kc;                        // sorted keys (hist reused, K <= 1024 < 2048)
+    sm.hist[rank] = kc;
     sm.hist[kMaxTopK + rank] = static_cast<unsigned>(ic);
   }
   __syncthreads();
+  mark(marks, 5);
   const float top = key_value(sm.hist[0]);
   for (int c = tid; c < K; c += kThreads) sm.cprob[c] = expf(key_value(sm.hist[c]) - top);
   __syncthreads();
@@ -701,6 +957,7 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
     }
   }
   __syncthreads();
+  mark(marks, 6);
   const uint64_t key = rng[0], ctr = rng[1];
   const float uval = fminf(philox_uniform(key, ctr), 0.99999994f);
   const float target = uval * sm.cprob[K - 1];
@@ -732,7 +989,7 @@ __device__ __forceinline__ bool wait_counter(const Sync& s, unsigned target) {
   unsigned long long t0 = 0ull;
   unsigned spins = 0u;
   while (true) {
-    const unsigned v = ld_acquire_u32(s.counter);
+    const unsigned v = ld_relaxed_u32(s.counter);
     if (static_cast<int>(v - target) >= 0) return true;
     ++spins;
     if ((spins & 63u) == 0u && ld_relaxed_u32(s.error) != 0u) return false;

@@ -100,7 +100,7 @@ __global__ void __launch_bounds__(kThreads) group_dots_kernel(const IvbTernary m
 struct GemvSmem {
   static size_t bytes(int n) {
     const size_t pad = static_cast<size_t>((n + 63) / 64) * 64;
-    return pad * 4 + pad + (pad / 64) * 4 + 64 * 4 + kThreads * 4 + 16;
+    return pad * 4 + pad + (pad / 64) * 4 + 64 * 4 + 2 * kThreads * 4 + 16;
   }
 };
 
@@ -120,10 +120,10 @@ __global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const IvbTernary m, c
   uint4 pf[kPrefetch];
   float pfs[kPrefetch];
   gemv_prefetch(m, g, pf, pfs);
-  for (int i = threadIdx.x; i < n; i += kThreads) xv[i] = __ldcg(x + i);
+  load_vector(x, n, xv);
   __syncthreads();
   const float s = quantize_block(xv, n, norm_w, norm_eps, clip, act_eps, act, true, xs, red);
-  gemv_rows(m, g, act, xs, s, epilogue, out, pf, pfs, res);
+  gemv_rows(m, g, act, xs, s, epilogue, out, pf, pfs, res, nullptr);
 }
 
 __global__ void __launch_bounds__(kThreads, 1) sample_kernel(const float* logits, uint8_t* seen, int vocab,
@@ -131,13 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1) sample_kernel(const float* logits
                                                              uint64_t* rng, int64_t* token, int64_t* history) {
   extern __shared__ __align__(16) unsigned char smem[];
   SampleSmem sm;
-  sm.keys = reinterpret_cast<unsigned*>(smem);
-  sm.hist = sm.keys + vocab;
-  sm.ckey = sm.hist + kWarps * 256;
-  sm.cidx = reinterpret_cast<int*>(sm.ckey + kMaxTopK);
-  sm.cprob = reinterpret_cast<float*>(sm.cidx + kMaxTopK);
-  sm.misc = reinterpret_cast<int*>(sm.cprob + kMaxTopK);
-  sm.red = reinterpret_cast<float*>(sm.misc + 16);
+  carve_sample(smem, vocab, sm);
   sample_block(logits, seen, vocab, sampling, top_k, max_top_k, rng, token, history, sm);
 }
 
@@ -150,10 +144,7 @@ __global__ void probe_wait_kernel(unsigned* counter, unsigned* error_word, unsig
 
 }  // namespace ivb
 
-size_t ivb_sample_smem_bytes(int vocab) {
-  using namespace ivb;
-  return static_cast<size_t>(vocab) * 4 + kWarps * 256 * 4 + kMaxTopK * 12 + 16 * 4 + 64 * 4 + 16;
-}
+size_t ivb_sample_smem_bytes(int vocab) { return ivb::sample_smem_bytes(vocab); }
 
 size_t ivb_gemv_smem_bytes(int n) { return ivb::GemvSmem::bytes(n); }
 

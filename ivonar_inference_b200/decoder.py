@@ -50,7 +50,7 @@ def _stack(tensors: list[Tensor], interleave: bool) -> Tensor:
 class DeviceMatrix:
     """A row-stack of packed projections on the device, in the layout the kernels read."""
 
-    def __init__(self, projections: list, device: torch.device, interleave: bool = False) -> None:
+    def __init__(self, projections: list, device: torch.device, interleave: bool = False, scale_align: int = 1) -> None:
         first = projections[0]
         self.in_features = int(first.in_features)
         for proj in projections:
@@ -64,7 +64,11 @@ class DeviceMatrix:
                 raise KernelError("interleaved projections must share their output width")
         packed = _stack([p.packed_weight.to(device) for p in projections], interleave)
         self.packed = _pad_rows(packed).contiguous()
-        self.scales = _stack([p.weight_scales.to(device) for p in projections], interleave).contiguous()
+        scales = _stack([p.weight_scales.to(device) for p in projections], interleave)
+        stride = (int(scales.shape[1]) + scale_align - 1) // scale_align * scale_align
+        if stride != int(scales.shape[1]):
+            scales = F.pad(scales, (0, stride - int(scales.shape[1])))
+        self.scales = scales.contiguous()
         biases = [p.bias for p in projections]
         if all(b is None for b in biases):
             self.bias = None
@@ -201,12 +205,18 @@ class B200Decoder:
                 desc.kind = native.IVB_MLA
                 mats["entry"] = DeviceMatrix([mixer.q_proj, mixer.kv_down_proj, mixer.k_rope_proj], dev)
                 mats["out"] = DeviceMatrix([mixer.out_proj], dev)
-                mats["k_nope_up"] = DeviceMatrix([mixer.k_nope_up_proj], dev)
-                mats["v_up"] = DeviceMatrix([mixer.v_up_proj], dev)
+                # up-projections are read by bulk copies: 16-byte scale rows
+                mats["k_nope_up"] = DeviceMatrix([mixer.k_nope_up_proj], dev, scale_align=8)
+                mats["v_up"] = DeviceMatrix([mixer.v_up_proj], dev, scale_align=8)
                 rope = rope_table(mixer.rope, self.max_len).to(dev)
-                latent_q = torch.zeros(self.max_len, mixer.latent_dim, dtype=torch.int8, device=dev)
-                latent_scale = torch.zeros(self.max_len, dtype=torch.float32, device=dev)
-                k_rope = torch.zeros(self.max_len, mixer.num_heads, mixer.rope_dim, dtype=torch.float16, device=dev)
+                # compressed cache: int8 latent codes (rows padded to 16 bytes), one scale per
+                # position (padded to a multiple of 4), head-major fp16 k_rope (rows padded to 8)
+                lpad = (int(mixer.latent_dim) + 15) // 16 * 16
+                rpad = (int(mixer.rope_dim) + 7) // 8 * 8
+                latent_q = torch.zeros(self.max_len, lpad, dtype=torch.int8, device=dev)
+                # bulk copies read scales in 16-byte units: pad so a tile ending at max_len stays inside
+                latent_scale = torch.zeros((self.max_len + 7) // 4 * 4, dtype=torch.float32, device=dev)
+                k_rope = torch.zeros(mixer.num_heads, self.max_len, rpad, dtype=torch.float16, device=dev)
                 self._keep.append(rope)
                 self.latent_caches[index] = (latent_q, latent_scale, k_rope)
                 desc.k_nope_up = mats["k_nope_up"].desc()
@@ -290,6 +300,28 @@ class B200Decoder:
     def _check(self) -> None:
         with torch.cuda.device(self.device):
             native.check(self.lib.ivb_decoder_check(self._plan, self._stream()), "decode kernel")
+
+    def trace(self, step: int | None) -> Tensor | None:
+        """Record a per-phase, per-CTA device timeline of step `step` of each following run
+        (None stops). Returns the int64 [num_phases, ctas, 8] globaltimer buffer (ns): work start,
+        marks inside the phase, work end."""
+        if step is None:
+            native.check(self.lib.ivb_decoder_trace(self._plan, None, 0), "ivb_decoder_trace")
+            self._trace = None
+            return None
+        self._trace = torch.zeros(self.num_phases, self.ctas, 8, dtype=torch.int64, device=self.device)
+        native.check(self.lib.ivb_decoder_trace(self._plan, self._trace.data_ptr(), int(step)), "ivb_decoder_trace")
+        return self._trace
+
+    def phase_kinds(self) -> list[str]:
+        """Names of the ops of one token, in the order of the trace buffer's first axis."""
+        kinds = []
+        for index in range(len(self.layer_matrices)):
+            if index in self.recurrent_states:
+                kinds += [f"L{index}.entry_ssm", f"L{index}.out", f"L{index}.gate_up", f"L{index}.down"]
+            else:
+                kinds += [f"L{index}.entry", f"L{index}.attention", f"L{index}.out", f"L{index}.gate_up", f"L{index}.down"]
+        return kinds + ["head"]
 
     @property
     def weight_bytes(self) -> int:
