@@ -29,7 +29,8 @@ struct Op {
   int32_t first_chunk, n_chunks;  // chunks of the weight stream this op consumes (constants chunk first)
   int32_t has_const;
   int32_t gather;                  // what is gathered from the cluster before the op runs
-  int32_t gather_n, gather_per;    // gathered vector length and per-CTA slice length
+  int32_t gather_n, gather_per;    // input vector length and per-CTA slice length of its producer
+  int32_t push_per;                // entry of an mla block: latent rows per CTA (output slice stride)
   int32_t in_n;                    // GEMV input length
   int32_t rows_per, rows_total;    // uniform row partition across the cluster
   int32_t chunk_rows;              // rows per stream chunk
@@ -115,6 +116,13 @@ __device__ __forceinline__ float ld_cluster_f32(unsigned addr) {
   asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
+__device__ __forceinline__ void st_cluster_f32(unsigned addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
+}
+__device__ __forceinline__ void st_cluster_v4(unsigned addr, float4 v) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
 __device__ __forceinline__ void atom_min_cluster_u32(unsigned addr, unsigned v) {
   asm volatile("red.shared::cluster.min.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
 }
@@ -188,39 +196,158 @@ __device__ __forceinline__ void stream_release(const ClusterParams& p, Stream& s
 }
 
 // ---- GEMV rows from a ring stage ----------------------------------------------------------------
+// dp4a with unsigned weight bytes and signed activation bytes.
+__device__ __forceinline__ int dp4a_us(unsigned a, int b, int c) {
+  int d;
+  asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+// Activations of one 64-input chunk in registers: q[k] are the four act words of weight word k.
+struct ActChunk {
+  int4 q[4];
+  int xsum;
+};
+
+// xsum == nullptr: the chunk sum of the codes is computed here (sixteen dp4a with ones).
+__device__ __forceinline__ ActChunk load_act_chunk(const int8_t* act, const int* xsum, int u) {
+  ActChunk c;
+  const int rot = (u >> 1) & 3;
+  const char* base = reinterpret_cast<const char*>(act) + (u << 6);
+#pragma unroll
+  for (int k = 0; k < 4; ++k) c.q[k] = *reinterpret_cast<const int4*>(base + (((k + rot) & 3) << 4));
+  if (xsum != nullptr) {
+    c.xsum = xsum[u];
+  } else {
+    int t = 0;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      t = __dp4a(c.q[k].x, 0x01010101, t);
+      t = __dp4a(c.q[k].y, 0x01010101, t);
+      t = __dp4a(c.q[k].z, 0x01010101, t);
+      t = __dp4a(c.q[k].w, 0x01010101, t);
+    }
+    c.xsum = t;
+  }
+  return c;
+}
+
+// Exact integer sum over the chunk of (code - 1) * q8. The two-bit field f of every weight byte is
+// masked in place (value code << 2f) and dotted with the activations of field f; the four partial
+// sums are exact multiples of 1, 4, 16 and 64, so the shifts below are exact.
+__device__ __forceinline__ int chunk_dot_regs(const uint4 w, const ActChunk& a) {
+  const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+  int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    s0 = dp4a_us(ws[k] & 0x03030303u, a.q[k].x, s0);
+    s1 = dp4a_us(ws[k] & 0x0C0C0C0Cu, a.q[k].y, s1);
+    s2 = dp4a_us(ws[k] & 0x30303030u, a.q[k].z, s2);
+    s3 = dp4a_us(ws[k] & 0xC0C0C0C0u, a.q[k].w, s3);
+  }
+  return (s0 + (s1 >> 2)) + ((s2 >> 4) + (s3 >> 6)) - a.xsum;
+}
+
 // rows [0, k) of a chunk laid out [k x row_bytes packed][k x scale_stride fp16 (16B pad)][k x fp32 bias]
-// Results of row r go to out[r] (after the lane reduction); act/xsum: transposed int8 input.
-__device__ void chunk_rows(const Op& op, const unsigned char* stage, int k, const int8_t* act, const int* xsum,
-                           float act_scale, float* out) {
+// Lane group of 2^lpr_log lanes per row; lane `sub` owns chunks sub + j * 2^lpr_log (j < KPL), whose
+// activations stay in registers for all rows. Every thread runs RPT rows per pass. Results of row r
+// go to out[r] (after the lane reduction).
+template <int KPL, int RPT>
+__device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char* stage, int k, const int8_t* act,
+                                               const int* xsum, float act_scale, float* out) {
   const int tid = threadIdx.x;
-  const int lpr = 1 << op.lpr_log;
-  const int rpi = kThreads >> op.lpr_log;
+  const int lg = op.lpr_log;
+  const int lpr = 1 << lg;
+  const int rpi = kThreads >> lg;
   const int chunks = (op.in_n + 63) >> 6;
-  const int kpl = (chunks + lpr - 1) >> op.lpr_log;
+  const int sub = tid & (lpr - 1);
+  ActChunk a[KPL];
+  bool have[KPL];
+#pragma unroll
+  for (int j = 0; j < KPL; ++j) {
+    const int u = sub + (j << lg);
+    have[j] = u < chunks;
+    if (have[j]) a[j] = load_act_chunk(act, nullptr, u);
+  }
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * op.row_bytes);
+  const float* bias =
+      reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * op.row_bytes + round16(k * op.scale_stride * 2));
+  for (int base = 0; base < k; base += RPT * rpi) {
+    int r[RPT];
+    bool v[RPT];
+    uint4 w[RPT][KPL];
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      r[t] = base + t * rpi + (tid >> lg);
+      v[t] = r[t] < k;
+      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r[t]) * op.row_bytes);
+#pragma unroll
+      for (int j = 0; j < KPL; ++j) {
+        const int u = sub + (j << lg);
+        w[t][j] = (have[j] && v[t]) ? wr[u] : make_uint4(0u, 0u, 0u, 0u);
+      }
+    }
+    float acc[RPT];
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      acc[t] = 0.0f;
+#pragma unroll
+      for (int j = 0; j < KPL; ++j) {
+        const int u = sub + (j << lg);
+        if (have[j] && v[t])
+          acc[t] = fmaf(static_cast<float>(chunk_dot_regs(w[t][j], a[j])), h2f(scales[r[t] * op.scale_stride + (u >> 1)]),
+                        acc[t]);
+      }
+    }
+    for (int off = 1; off < lpr; off <<= 1) {
+#pragma unroll
+      for (int t = 0; t < RPT; ++t) acc[t] += __shfl_xor_sync(kFull, acc[t], off);
+    }
+    if (sub == 0) {
+#pragma unroll
+      for (int t = 0; t < RPT; ++t)
+        if (v[t]) out[r[t]] = op.has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
+    }
+  }
+}
+
+// Fallback for inputs with more than three chunks per lane: activations re-read from shared memory,
+// chunk sums from xsum (the quantiser fills it for these ops).
+__device__ __forceinline__ void chunk_rows_wide(const Op& op, const unsigned char* stage, int k, const int8_t* act,
+                                                const int* xsum, float act_scale, float* out) {
+  const int tid = threadIdx.x;
+  const int lg = op.lpr_log;
+  const int lpr = 1 << lg;
+  const int rpi = kThreads >> lg;
+  const int chunks = (op.in_n + 63) >> 6;
   const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * op.row_bytes);
   const float* bias =
       reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * op.row_bytes + round16(k * op.scale_stride * 2));
   const int sub = tid & (lpr - 1);
   for (int base = 0; base < k; base += rpi) {
-    const int r = base + (tid >> op.lpr_log);
+    const int r = base + (tid >> lg);
     float acc = 0.0f;
     if (r < k) {
       const uint4* wrow = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * op.row_bytes);
       const uint16_t* srow = scales + r * op.scale_stride;
-      for (int j = 0; j < kpl; ++j) {
-        const int u = sub + (j << op.lpr_log);
-        if (u < chunks) {
-          const int dd = chunk_dot(wrow[u], act, u) - xsum[u];
-          acc = fmaf(static_cast<float>(dd), h2f(srow[u >> 1]), acc);
-        }
-      }
+#pragma unroll 2
+      for (int u = sub; u < chunks; u += lpr)
+        acc = fmaf(static_cast<float>(chunk_dot_regs(wrow[u], load_act_chunk(act, xsum, u))), h2f(srow[u >> 1]), acc);
     }
     for (int off = 1; off < lpr; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
-    if (r < k && sub == 0) {
-      float v = acc * act_scale;
-      if (op.has_bias) v += bias[r];
-      out[r] = v;
-    }
+    if (r < k && sub == 0) out[r] = op.has_bias ? acc * act_scale + bias[r] : acc * act_scale;
+  }
+}
+
+__device__ __forceinline__ void chunk_rows(const Op& op, const unsigned char* stage, int k, const int8_t* act, const int* xsum,
+                           float act_scale, float* out) {
+  const int chunks = (op.in_n + 63) >> 6;
+  const int kpl = (chunks + (1 << op.lpr_log) - 1) >> op.lpr_log;
+  switch (kpl) {
+    case 1: chunk_rows_kpl<1, 2>(op, stage, k, act, xsum, act_scale, out); break;
+    case 2: chunk_rows_kpl<2, 2>(op, stage, k, act, xsum, act_scale, out); break;
+    case 3: chunk_rows_kpl<3, 2>(op, stage, k, act, xsum, act_scale, out); break;
+    default: chunk_rows_wide(op, stage, k, act, xsum, act_scale, out); break;
   }
 }
 
@@ -372,4 +499,12 @@ static __device__ int draw_token(const unsigned* sorted_key, const int* sorted_i
   return sorted_id[chosen];
 }
 
+}  // namespace ivb
+
+namespace ivb {
+// true when chunk_rows reads the quantiser's chunk sums (more than three chunks per lane)
+__host__ __device__ __forceinline__ bool op_needs_xsum(const Op& op) {
+  const int chunks = (op.in_n + 63) >> 6;
+  return ((chunks + (1 << op.lpr_log) - 1) >> op.lpr_log) > 3;
+}
 }  // namespace ivb

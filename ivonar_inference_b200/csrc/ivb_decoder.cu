@@ -32,10 +32,58 @@ __device__ __forceinline__ void raise_error(const ClusterParams& p, unsigned* er
   for (int r = 0; r < p.d.R; ++r) atom_min_cluster_u32(map_rank(err_flag, r), stop_at);
 }
 
-__device__ __forceinline__ void gather_vec(const float* pub_rd, int n, int per, float* dst) {
-  for (int i = threadIdx.x; i < n; i += kThreads) {
-    const int c = i / per;
-    dst[i] = ld_cluster_f32(map_rank(pub_rd + (i - c * per), c));
+// floats of the recurrent constants copied out of the constants chunk: decay, theta, skip, conv w/b
+__host__ __device__ __forceinline__ int ssm_const_floats(int nh, int S, int hd, int taps) {
+  return 2 * nh * S + nh * hd * (2 + taps);
+}
+__device__ __forceinline__ void cp_async_f32(float* dst, const float* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+constexpr int kAttnPieces = 4;
+
+// The 16 two-bit codes of a packed word (input 4b + f in bits 8b + 2f) as exact floats code - 1.
+__device__ __forceinline__ void word_codes_m1(unsigned w, float* cm1) {
+#pragma unroll
+  for (int f = 0; f < 4; ++f) {
+    const unsigned m = (w >> (2 * f)) & 0x03030303u;
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      cm1[4 * b + f] = __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7440 | b)) - 8388609.0f;
+  }
+}  // 128-wide latent pieces per attention lane (latent <= 512)
+
+// Four signed bytes to exact floats without the conversion unit: biased byte b + 128 placed in the
+// low mantissa bits of 2^23, then 2^23 + 128 subtracted (exact for every byte value).
+__device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
+  const unsigned b = w ^ 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7441)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7442)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7443)) - 8388736.0f;
+}
+
+// Store v at dst[i] in the shared memory of every CTA of the cluster (the next op's input vector is
+// replicated; the cluster barrier after the op makes the stores visible).
+// All threads: copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n)
+// in every CTA of the cluster; one (slice, rank) pair per thread, 16-byte stores when aligned.
+__device__ __forceinline__ void push_vec(float* dst, int base, const float* src, int n, int R) {
+  if (((base | n) & 3) == 0) {
+    const int n4 = n >> 2;
+    for (int idx = threadIdx.x; idx < n4 * R; idx += kThreads) {
+      const int r = idx / n4, i = idx - r * n4;
+      st_cluster_v4(map_rank(dst + base + 4 * i, r), reinterpret_cast<const float4*>(src)[i]);
+    }
+  } else {
+    for (int idx = threadIdx.x; idx < n * R; idx += kThreads) {
+      const int r = idx / n, i = idx - r * n;
+      st_cluster_f32(map_rank(dst + base + i, r), src[i]);
+    }
   }
 }
 
@@ -78,6 +126,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
   __shared__ __align__(8) unsigned long long full[kStages];
   __shared__ __align__(8) unsigned long long abar[2];
   __shared__ unsigned err_flag;  // cluster barrier number after which every CTA stops (~0u: none)
+  __shared__ __align__(16) Op opbuf[2];  // descriptor of the running op and the next one
+  __shared__ __align__(16) int rowsbuf[2][4];
   const unsigned rank = cluster_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const ClusterDims& D = p.d;
@@ -87,10 +137,10 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
   int8_t* act = reinterpret_cast<int8_t*>(smem + M.act);
   int* xsum = reinterpret_cast<int*>(smem + M.xsum);
   float* resid = reinterpret_cast<float*>(smem + M.resid);
-  float* pub = reinterpret_cast<float*>(smem + M.pub);
   float* loc = reinterpret_cast<float*>(smem + M.loc);
   float* red = reinterpret_cast<float*>(smem + M.red);
   float* xl = reinterpret_cast<float*>(smem + M.xl);
+  float* stg = reinterpret_cast<float*>(smem + M.pub);  // this op's output slice before it is pushed
   unsigned char* U = smem + M.u;
   if (tid == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
@@ -102,10 +152,22 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
   __syncthreads();
   cluster_sync();
   Stream st{full, smem + M.ring, M.stage_bytes, 0u, 0u, 0, 0};
+  // op descriptors travel through a two-slot shared buffer: op k+1 is fetched while op k runs
+  auto fetch_op = [&](int oi, int slot) {
+    if (tid < static_cast<int>(sizeof(Op) / 16))
+      cp_async_16(reinterpret_cast<unsigned char*>(&opbuf[slot]) + 16 * tid,
+                  reinterpret_cast<const unsigned char*>(p.ops + oi) + 16 * tid);
+    else if (tid == 32)
+      cp_async_f32(reinterpret_cast<float*>(&rowsbuf[slot][0]), reinterpret_cast<const float*>(p.op_rows + oi * R + rank));
+    cp_async_commit();
+  };
+  fetch_op(0, 0);
+  cp_async_wait_all();
+  __syncthreads();
+  unsigned opk = 0;  // ops run so far (selects the descriptor slot)
   if (tid == 0)
     for (int k = 0; k < kStages; ++k) stream_issue(p, st, rank);
   unsigned apar[2] = {0u, 0u};
-  int rd = 0, wr = 1;  // publish buffers: read (previous op) / write (this op)
   const int first_head = static_cast<int>(rank) * D.hpc;
   const int nh = max(0, min(D.heads - first_head, D.hpc));
   long long pos = ldcg_i64(p.position);
@@ -147,21 +209,26 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         resid[i] = static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
     }
     __syncthreads();
-    for (int oi = 0; oi < p.n_ops && alive; ++oi) {
-      const Op op = p.ops[oi];
-      if (op.kind == OP_HEAD && !head) break;
+    const int n_run = head ? p.n_ops : p.n_ops - 1;  // the head is the last op of the program
+    for (int oi = 0; oi < n_run && alive; ++oi) {
+      const Op& op = opbuf[opk & 1];  // fields are read from shared memory where used
+      const int rows_c = rowsbuf[opk & 1][0];
+      fetch_op(oi + 1 < n_run ? oi + 1 : 0, (opk + 1) & 1);  // the op after this one (op 0 of the next token)
       unsigned long long* marks = tracing ? p.trace + (static_cast<size_t>(oi) * R + rank) * 8 : nullptr;
       mark(marks, 0);
-      float* pub_rd = pub + rd * M.pub_n;
-      float* pub_wr = pub + wr * M.pub_n;
-      // 1. input of this op from the cluster
-      if (op.gather == G_RESID) gather_vec(pub_rd, op.gather_n, op.gather_per, resid);
-      else if (op.gather == G_VEC) gather_vec(pub_rd, op.gather_n, op.gather_per, xv);
-      else if (op.gather == G_LATENT) gather_vec(pub_rd, op.gather_n, op.gather_per, xl);
-      __syncthreads();
-      mark(marks, 1);
+      // the input of this op (resid, xv or xl) was pushed into this CTA by every producer of the
+      // previous op before the cluster barrier
+      // tracing: slots 1..6 sum the SM cycles spent in six parts of the op (thread 0's view)
+      long long prof[6] = {0, 0, 0, 0, 0, 0};
+      long long prof_t = marks != nullptr ? clock64() : 0;
+      auto tick = [&](int part) {
+        if (marks != nullptr) {
+          const long long now = clock64();
+          prof[part] += now - prof_t;
+          prof_t = now;
+        }
+      };
       const int lo = min(op.rows_total, static_cast<int>(rank) * op.rows_per);
-      const int rows_c = p.op_rows[oi * R + rank];
       bool ok = true;
       if (op.kind == OP_ATTN) {
         // ---------------- latent attention over the compressed cache ----------------
@@ -178,15 +245,14 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         float* part = sc + D.tile + 4;
         unsigned char* tiles = reinterpret_cast<unsigned char*>(part + kWarps * D.latent);
         tiles += (16 - (reinterpret_cast<uintptr_t>(tiles) & 15)) & 15;
-        for (int j = tid; j < D.latent; j += kThreads) qlat_f[j] = xl[j];
-        __syncthreads();
-        const float a_cur = quantize_block(qlat_f, D.latent, nullptr, 0.0f, 0.0f, D.act_eps, qlc, false, nullptr, red);
+        const float a_cur = quantize_block(xl, D.latent, nullptr, 0.0f, 0.0f, D.act_eps, qlc, false, nullptr, red);
         if (rank == 0) {
           for (int j = tid; j < D.latent; j += kThreads) L.latent_q[static_cast<size_t>(pos) * D.lpad + j] = qlc[j];
           if (tid == 0) L.latent_scale[pos] = a_cur;
         }
         const int P = static_cast<int>(pos);
         const int n_tiles = P == 0 ? 1 : (P + D.tile - 1) / D.tile;
+        tick(0);
         for (int hl = 0; hl < nh && ok; ++hl) {
           const int h = first_head + hl;
           const float* qh = loc + hl * D.head_dim;
@@ -213,11 +279,42 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           // absorbed query qa[j] = sum_e qn[e] * W_knope[h][e][j] (weights in the constants chunk)
           const unsigned char* wkn = cst + op.c_wkn + static_cast<size_t>(hl) * D.nope * D.rb_lat;
           const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + op.c_skn) + hl * D.nope * D.ss_lat;
-          for (int j = tid; j < D.latent; j += kThreads) {
-            float acc = 0.0f;
-            for (int e = 0; e < D.nope; ++e)
-              acc = fmaf(qn[e], code_value(wkn + e * D.rb_lat, j) * h2f(skn[e * D.ss_lat + (j >> 7)]), acc);
-            qa[j] = acc;
+          const int words = (D.latent + 15) >> 4;  // 16-input words of a latent row
+          if ((words & (words - 1)) == 0) {
+            // thread: word wd of e-group eg; the e-groups of a warp meet by shuffles, the warps in `part`
+            const int wd = tid & (words - 1), eg = tid / words, n_eg = kThreads / words;
+            float acc[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+            for (int e = eg; e < D.nope; e += n_eg) {
+              const unsigned w = *reinterpret_cast<const unsigned*>(wkn + e * D.rb_lat + wd * 4);
+              const float sc_e = h2f(skn[e * D.ss_lat + (wd >> 3)]), q_e = qn[e];
+              float cm1[16];
+              word_codes_m1(w, cm1);
+#pragma unroll
+              for (int i = 0; i < 16; ++i) acc[i] = fmaf(q_e, cm1[i] * sc_e, acc[i]);
+            }
+            for (int off = words; off < 32; off <<= 1)
+#pragma unroll
+              for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], off);
+            if (lane < words)
+#pragma unroll
+              for (int i = 0; i < 16; ++i)
+                if (wd * 16 + i < D.latent) part[warp * D.latent + wd * 16 + i] = acc[i];
+            __syncthreads();
+            for (int j = tid; j < D.latent; j += kThreads) {
+              float v = part[j];
+#pragma unroll
+              for (int w2 = 1; w2 < kWarps; ++w2) v += part[w2 * D.latent + j];
+              qa[j] = v;
+            }
+          } else {
+            for (int j = tid; j < D.latent; j += kThreads) {
+              float acc = 0.0f;
+              for (int e = 0; e < D.nope; ++e)
+                acc = fmaf(qn[e], code_value(wkn + e * D.rb_lat, j) * h2f(skn[e * D.ss_lat + (j >> 7)]), acc);
+              qa[j] = acc;
+            }
           }
           float qb = 0.0f;
           if (L.k_nope_up.bias != nullptr) {
@@ -228,14 +325,25 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           } else {
             __syncthreads();
           }
-          const int per_lane = (D.latent + 31) >> 5;
-          float qa_r[kMaxLatentPerLane], u[kMaxLatentPerLane];
+          // Tiles of cached positions (plus the current one, last): scores with 8 lanes per position
+          // (lane `sub` owns latent pieces p * 128 + sub * 16 .. + 16, the absorbed query slice kept in
+          // registers), an online softmax, and the weighted latent sum u with one warp per position
+          // group (lane owns latent lane * 8 + 256 * p2 .. + 8).
+          tick(1);
+          const int sub = tid & 7, grp = tid >> 3;
+          float qa_r[kAttnPieces][16];
 #pragma unroll
-          for (int i = 0; i < kMaxLatentPerLane; ++i) {
-            const int j = lane + (i << 5);
-            qa_r[i] = (i < per_lane && j < D.latent) ? qa[j] : 0.0f;
-            u[i] = 0.0f;
-          }
+          for (int pc = 0; pc < kAttnPieces; ++pc)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              const int j = pc * 128 + sub * 16 + i;
+              qa_r[pc][i] = j < D.latent ? qa[j] : 0.0f;
+            }
+          float u[kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1][8];
+#pragma unroll
+          for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc)
+#pragma unroll
+            for (int i = 0; i < 8; ++i) u[pc][i] = 0.0f;
           float m_run = -INFINITY, l_run = 0.0f;
           for (int ti = 0; ti < n_tiles; ++ti) {
             const int start = ti * D.tile;
@@ -253,20 +361,37 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
               apar[ti & 1] ^= 1u;
             }
             const int npos = count + (last ? 1 : 0);
-            for (int k = warp; k < npos; k += kWarps) {
+            for (int k = grp; k - grp < npos; k += kThreads / 8) {
+              const bool valid = k < npos;
               const bool cur = k == count;
-              const int8_t* ql = cur ? qlc : tb.lat + k * D.lpad;
-              const float at = cur ? a_cur : tb.lsc[k];
-              float dot = 0.0f;
+              const int8_t* ql = cur ? qlc : tb.lat + (valid ? k : 0) * D.lpad;
+              float dot0 = 0.0f, dot1 = 0.0f;
 #pragma unroll
-              for (int i = 0; i < kMaxLatentPerLane; ++i) {
-                const int j = lane + (i << 5);
-                if (i < per_lane && j < D.latent) dot = fmaf(qa_r[i], static_cast<float>(ql[j]), dot);
+              for (int pc = 0; pc < kAttnPieces; ++pc) {
+                const int j0 = pc * 128 + sub * 16;
+                if (valid && j0 < D.latent) {
+                  const uint4 w = *reinterpret_cast<const uint4*>(ql + j0);
+                  float f[16];
+                  bytes_to_f32(w.x, f);
+                  bytes_to_f32(w.y, f + 4);
+                  bytes_to_f32(w.z, f + 8);
+                  bytes_to_f32(w.w, f + 12);
+#pragma unroll
+                  for (int i = 0; i < 16; i += 2) {
+                    dot0 = fmaf(qa_r[pc][i], f[i], dot0);
+                    dot1 = fmaf(qa_r[pc][i + 1], f[i + 1], dot1);
+                  }
+                }
               }
               float rp = 0.0f;
-              for (int r = lane; r < D.rope; r += 32) rp = fmaf(qr[r], cur ? krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
-              const float total = warp_sum(at * dot + rp);
-              if (lane == 0) sc[k] = total + qb;
+              if (valid)
+                for (int r = sub; r < D.rope; r += 8) rp = fmaf(qr[r], cur ? krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
+              const float at = valid ? (cur ? a_cur : tb.lsc[k]) : 0.0f;
+              float total = fmaf(at, dot0 + dot1, rp);
+              total += __shfl_xor_sync(kFull, total, 4);
+              total += __shfl_xor_sync(kFull, total, 2);
+              total += __shfl_xor_sync(kFull, total, 1);
+              if (valid && sub == 0) sc[k] = total + qb;
             }
             __syncthreads();
             float mx = -INFINITY;
@@ -277,31 +402,42 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             float ls = 0.0f;
             for (int k = tid; k < npos; k += kThreads) {
               const float e = expf(sc[k] - m_new);
-              sc[k] = e;
+              sc[k] = e * (k == count ? a_cur : tb.lsc[k]);  // softmax weight times the latent scale
               ls += e;
             }
             ls = block_sum(ls, red);
             l_run = l_run * corr + ls;
 #pragma unroll
-            for (int i = 0; i < kMaxLatentPerLane; ++i) u[i] *= corr;
-            for (int k = warp; k < npos; k += kWarps) {
-              const bool cur = k == count;
-              const int8_t* ql = cur ? qlc : tb.lat + k * D.lpad;
-              const float ea = sc[k] * (cur ? a_cur : tb.lsc[k]);
+            for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc)
 #pragma unroll
-              for (int i = 0; i < kMaxLatentPerLane; ++i) {
-                const int j = lane + (i << 5);
-                if (i < per_lane && j < D.latent) u[i] = fmaf(ea, static_cast<float>(ql[j]), u[i]);
+              for (int i = 0; i < 8; ++i) u[pc][i] *= corr;
+            for (int k = warp; k < npos; k += kWarps) {
+              const int8_t* ql = k == count ? qlc : tb.lat + k * D.lpad;
+              const float ea = sc[k];
+#pragma unroll
+              for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc) {
+                const int j0 = pc * 256 + lane * 8;
+                if (j0 < D.latent) {
+                  const uint2 w = *reinterpret_cast<const uint2*>(ql + j0);
+                  float f[8];
+                  bytes_to_f32(w.x, f);
+                  bytes_to_f32(w.y, f + 4);
+#pragma unroll
+                  for (int i = 0; i < 8; ++i) u[pc][i] = fmaf(ea, f[i], u[pc][i]);
+                }
               }
             }
             m_run = m_new;
             __syncthreads();
           }
           if (!ok) break;
+          tick(2);
 #pragma unroll
-          for (int i = 0; i < kMaxLatentPerLane; ++i) {
-            const int j = lane + (i << 5);
-            if (i < per_lane && j < D.latent) part[warp * D.latent + j] = u[i];
+          for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc) {
+            const int j0 = pc * 256 + lane * 8;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+              if (j0 + i < D.latent) part[warp * D.latent + j0 + i] = u[pc][i];
           }
           __syncthreads();
           for (int j = tid; j < D.latent; j += kThreads) {
@@ -315,12 +451,36 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           const unsigned char* wv = cst + op.c_wv + static_cast<size_t>(hl) * D.head_dim * D.rb_lat;
           const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + op.c_sv) + hl * D.head_dim * D.ss_lat;
           const float* bv = reinterpret_cast<const float*>(cst + op.c_bv) + hl * D.head_dim;
+          const float inv_l = 1.0f / l_run;
+          if ((words & (words - 1)) == 0) {
+            // lanes of a row own its 16-input words (the u slice in registers); rows step by kThreads/words
+            const int wd = tid & (words - 1);
+            float uj[16], cm1[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) uj[i] = wd * 16 + i < D.latent ? qlat_f[wd * 16 + i] : 0.0f;
+            for (int e0 = 0; e0 < D.head_dim; e0 += kThreads / words) {
+              const int e = e0 + tid / words;
+              float acc = 0.0f;
+              if (e < D.head_dim) {
+                const unsigned w = *reinterpret_cast<const unsigned*>(wv + e * D.rb_lat + wd * 4);
+                const float sc_e = h2f(sv[e * D.ss_lat + (wd >> 3)]);
+                word_codes_m1(w, cm1);
+#pragma unroll
+                for (int i = 0; i < 16; ++i) acc = fmaf(cm1[i] * sc_e, uj[i], acc);
+              }
+              for (int off = 1; off < words; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
+              if (e < D.head_dim && wd == 0) {
+                float o = acc * inv_l;
+                if (L.v_up.bias != nullptr) o += bv[e];
+                stg[hl * D.head_dim + e] = o;
+              }
+            }
+          } else {
           int tpr = kThreads / D.head_dim;
           if (tpr > 32) tpr = 32;
           int tpr_log = 0;
           while ((2 << tpr_log) <= tpr) ++tpr_log;
           tpr = 1 << tpr_log;
-          const float inv_l = 1.0f / l_run;
           for (int base = 0; base < D.head_dim; base += kThreads >> tpr_log) {
             const int e = base + (tid >> tpr_log);
             const int pid = tid & (tpr - 1);
@@ -335,11 +495,14 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             if (e < D.head_dim && pid == 0) {
               float o = acc * inv_l;
               if (L.v_up.bias != nullptr) o += bv[e];
-              pub_wr[hl * D.head_dim + e] = o;
+              stg[hl * D.head_dim + e] = o;
             }
           }
+          }
           __syncthreads();
+          tick(3);
         }
+        if (ok) push_vec(xv, first_head * D.head_dim, stg, nh * D.head_dim, R);  // stg written before the head loop's last sync
         asm volatile("fence.proxy.async.global;" ::: "memory");
         if (!ok) fail_here(IVB_ETIMEOUT);
         stream_release(p, st, rank);
@@ -347,22 +510,36 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         // ---------------- GEMV ops ----------------
         const unsigned char* cst = nullptr;
         float act_scale = 0.0f;
+        float* ssmc = reinterpret_cast<float*>(U);
+        const int S = D.state_dim, hd = D.head_dim, taps = D.taps;
+        if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
+          // the recurrent state of my heads streams into shared memory while the rows are computed
+          const IvbLayerDesc& L = p.layers[op.layer];
+          const int nhs = nh * S, channels = nh * hd;
+          float* dst = ssmc + ssm_const_floats(nh, S, hd, taps) + 5 * nhs + channels + max(kThreads, channels);
+          const float* src[3] = {L.ssm_state + static_cast<size_t>(first_head) * S * hd * 2,
+                                 L.prev_force + static_cast<size_t>(first_head) * S * hd,
+                                 L.conv_state + static_cast<size_t>(first_head) * hd * (taps - 1)};
+          const int len[3] = {2 * nhs * hd, nhs * hd, channels * (taps - 1)};
+          for (int a2 = 0; a2 < 3; ++a2) {
+            for (int i = tid; i < len[a2]; i += kThreads) cp_async_f32(dst + i, src[a2] + i);
+            dst += len[a2];
+          }
+          cp_async_commit();
+        }
         if (op.has_const) {
           cst = stream_acquire(p, st);
           if (cst == nullptr) ok = false;
         }
-        mark(marks, 2);
-        // quantiser input
-        if (op.kind == OP_ENTRY_MAMBA || op.kind == OP_ENTRY_MLA || op.kind == OP_GATE_UP || op.kind == OP_HEAD) {
-          for (int i = tid; i < D.hidden; i += kThreads) xv[i] = resid[i];
-          __syncthreads();
-        }
+        tick(0);
+        // quantiser input: the residual replica (entry, gate/up, head) or the pushed vector (out, down)
+        const bool from_resid =
+            op.kind == OP_ENTRY_MAMBA || op.kind == OP_ENTRY_MLA || op.kind == OP_GATE_UP || op.kind == OP_HEAD;
         const float* norm_w = (op.has_norm && cst != nullptr) ? reinterpret_cast<const float*>(cst + op.c_norm) : nullptr;
-        act_scale = quantize_block(xv, op.in_n, norm_w, op.norm_eps, D.clip, D.act_eps, act, true, xsum, red);
-        mark(marks, 3);
+        act_scale = quantize_block(from_resid ? resid : xv, op.in_n, norm_w, op.norm_eps, D.clip, D.act_eps, act, true,
+                                   op_needs_xsum(op) ? xsum : nullptr, red);
+        tick(1);
         // SSM constants leave the stage before it is recycled
-        float* ssmc = reinterpret_cast<float*>(U);
-        const int S = D.state_dim, hd = D.head_dim, taps = D.taps;
         if (op.kind == OP_ENTRY_MAMBA && cst != nullptr) {
           const float* src[5] = {reinterpret_cast<const float*>(cst + op.c_decay), reinterpret_cast<const float*>(cst + op.c_theta),
                                  reinterpret_cast<const float*>(cst + op.c_skip), reinterpret_cast<const float*>(cst + op.c_convw),
@@ -380,7 +557,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         const int n_row_chunks = op.n_chunks - op.has_const;
         for (int c = 0; c < n_row_chunks; ++c) {
           const unsigned char* stage = stream_acquire(p, st);
-          if (c == 0) mark(marks, 4);
+          tick(2);
           if (stage == nullptr) {
             ok = false;
           } else {
@@ -388,18 +565,25 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             const int k = max(0, min(op.chunk_rows, rows_c - r0));
             chunk_rows(op, stage, k, act, xsum, act_scale, rows_out + r0);
           }
-          if (c == 0) mark(marks, 5);
+          tick(3);
           stream_release(p, st, rank);
+          tick(4);
         }
-        mark(marks, 6);
         // epilogues
         if (op.kind == OP_OUT || op.kind == OP_DOWN) {
-          for (int r = tid; r < rows_c; r += kThreads) pub_wr[r] = resid[lo + r] + rows_out[r];
+          for (int r = tid; r < rows_c; r += kThreads) stg[r] = resid[lo + r] + rows_out[r];
+          __syncthreads();
+          push_vec(resid, lo, stg, rows_c, R);
         } else if (op.kind == OP_GATE_UP) {
-          for (int m = tid; m < rows_c / 2; m += kThreads) pub_wr[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
+          for (int m = tid; m < rows_c / 2; m += kThreads) stg[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
+          __syncthreads();
+          push_vec(xv, lo / 2, stg, rows_c / 2, R);
         } else if (op.kind == OP_ENTRY_MLA) {
           const int lat0 = nh * (D.head_dim + D.rope);
-          for (int r = tid; r < rows_c - lat0; r += kThreads) pub_wr[r] = rows_out[lat0 + r];
+          const int l0 = static_cast<int>(rank) * op.push_per;  // first latent row of this CTA
+          for (int r = tid; r < rows_c - lat0; r += kThreads) stg[r] = rows_out[lat0 + r];
+          __syncthreads();
+          push_vec(xl, l0, stg, rows_c - lat0, R);
         } else if (op.kind == OP_HEAD) {
           for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
         } else if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
@@ -410,61 +594,79 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           const float* skip = theta + nh * S;
           const float* convw = skip + nh * hd;
           const float* convb = convw + nh * hd * taps;
-          const int channels = nh * hd;
-          int tpc = 1;
-          while (tpc * 2 * channels <= kThreads && tpc * 2 <= 32) tpc *= 2;
-          const int spt = (S + tpc - 1) / tpc;
-          for (int cb = 0; cb < channels; cb += kThreads / tpc) {
-            const int cl = cb + tid / tpc, sg = tid % tpc;
-            const bool live = cl < channels;
-            const int hl = live ? cl / hd : 0, dd = live ? cl - hl * hd : 0;
-            const int hg = first_head + hl;
-            const float* rowh = rows_out + hl * (2 * hd + 3 * S);
-            float value = 0.0f;
-            if (live && sg == 0) {
-              const int cg = hg * hd + dd;
-              float* win = L.conv_state + static_cast<size_t>(cg) * (taps - 1);
-              const float incoming = rowh[dd];
-              float conv = convb[cl];
-              for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
-              conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
-              for (int k2 = 0; k2 + 1 < taps - 1; ++k2) win[k2] = win[k2 + 1];
-              if (taps > 1) win[taps - 2] = incoming;
-              value = silu_f(conv);
-            }
-            value = __shfl_sync(kFull, value, lane & ~(tpc - 1));
-            float contrib = 0.0f;
-            if (live) {
-              const float* bcdt = rowh + 2 * hd;
-              for (int i = 0; i < spt; ++i) {
-                const int s2 = sg * spt + i;
-                if (s2 >= S) break;
-                const float b = tanhf(bcdt[s2]);
-                const float cc = tanhf(bcdt[S + s2]);
-                const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
-                const float mag = expf(2.0f * half_dt * decay[hl * S + s2]);
-                float sn, cs;
-                sincosf(2.0f * half_dt * theta[hl * S + s2], &sn, &cs);
-                const float ar = mag * cs, ai = mag * sn;
-                const size_t idx = (static_cast<size_t>(hg) * S + s2) * hd + dd;
-                const float prev = L.prev_force[idx];
-                float* stt = L.ssm_state + 2 * idx;
-                const float sr = stt[0], si = stt[1];
-                const float force = b * value;
-                const float dr = (force + ar * prev) * half_dt;
-                const float di = (ai * prev) * half_dt;
-                const float nr = sr * ar - si * ai + dr;
-                const float ni = sr * ai + si * ar + di;
-                stt[0] = nr;
-                stt[1] = ni;
-                L.prev_force[idx] = force;
-                contrib = fmaf(cc, nr, contrib);
-              }
-            }
-            for (int off = tpc >> 1; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
-            if (live && sg == 0)
-              pub_wr[cl] = (contrib + skip[cl] * value) * sigmoid_f(rowh[hd + dd]);
+          const int channels = nh * hd, nhs = nh * S;
+          float* coef = ssmc + ssm_const_floats(nh, S, hd, taps);  // [5][nh*S]: b, c, half_dt, a_re, a_im
+          float* vals = coef + 5 * nhs;                            // [channels] conv + SiLU values
+          float* cpart = vals + channels;                          // [max(kThreads, channels)] partial readouts
+          const float* s_state = cpart + max(kThreads, channels);  // prefetched [nh][S][hd][2]
+          const float* s_prev = s_state + 2 * nhs * hd;             // [nh][S][hd]
+          const float* s_conv = s_prev + nhs * hd;                  // [channels][taps - 1]
+          cp_async_wait_all();
+          __syncthreads();
+          for (int t = tid; t < nhs; t += kThreads) {
+            const int hl = t / S, s2 = t - hl * S;
+            const float* bcdt = rows_out + hl * (2 * hd + 3 * S) + 2 * hd;
+            const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
+            const float mag = expf(2.0f * half_dt * decay[t]);
+            float sn, cs;
+            sincosf(2.0f * half_dt * theta[t], &sn, &cs);
+            coef[t] = tanhf(bcdt[s2]);
+            coef[nhs + t] = tanhf(bcdt[S + s2]);
+            coef[2 * nhs + t] = half_dt;
+            coef[3 * nhs + t] = mag * cs;
+            coef[4 * nhs + t] = mag * sn;
           }
+          for (int cl = tid; cl < channels; cl += kThreads) {
+            const int hl = cl / hd, dd = cl - hl * hd;
+            const float* win = s_conv + cl * (taps - 1);
+            float* gwin = L.conv_state + static_cast<size_t>(first_head * hd + cl) * (taps - 1);
+            const float incoming = rows_out[hl * (2 * hd + 3 * S) + dd];
+            float conv = convb[cl];
+            for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
+            conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
+            for (int k2 = 0; k2 + 1 < taps - 1; ++k2) gwin[k2] = win[k2 + 1];
+            if (taps > 1) gwin[taps - 2] = incoming;
+            vals[cl] = silu_f(conv);
+          }
+          __syncthreads();
+          // thread (group g, channel cl) advances states g*spt .. of channel cl; lanes run along the
+          // channels so the state loads and stores are contiguous
+          const int groups = max(1, min(S, kThreads / channels));
+          const int spt = (S + groups - 1) / groups;
+          for (int it = tid; it < groups * channels; it += kThreads) {
+            const int g = it / channels, cl = it - g * channels;
+            const int hl = cl / hd, dd = cl - hl * hd;
+            const float value = vals[cl];
+            float contrib = 0.0f;
+            for (int s2 = g * spt; s2 < min(S, (g + 1) * spt); ++s2) {
+              const int t = hl * S + s2;
+              const int li = t * hd + dd;  // local state index
+              const size_t gi = static_cast<size_t>(first_head * S + t) * hd + dd;
+              const float b = coef[t], cc = coef[nhs + t], half_dt = coef[2 * nhs + t];
+              const float ar = coef[3 * nhs + t], ai = coef[4 * nhs + t];
+              const float prev = s_prev[li];
+              const float sr = s_state[2 * li], si = s_state[2 * li + 1];
+              const float force = b * value;
+              const float dr = (force + ar * prev) * half_dt;
+              const float di = (ai * prev) * half_dt;
+              const float nr = sr * ar - si * ai + dr;
+              const float ni = sr * ai + si * ar + di;
+              reinterpret_cast<float2*>(L.ssm_state)[gi] = make_float2(nr, ni);
+              L.prev_force[gi] = force;
+              contrib = fmaf(cc, nr, contrib);
+            }
+            cpart[it] = contrib;
+          }
+          __syncthreads();
+          for (int cl = tid; cl < channels; cl += kThreads) {
+            const int hl = cl / hd, dd = cl - hl * hd;
+            float contrib = 0.0f;
+            for (int g = 0; g < groups; ++g) contrib += cpart[g * channels + cl];
+            const float y = (contrib + skip[cl] * vals[cl]) * sigmoid_f(rows_out[hl * (2 * hd + 3 * S) + hd + dd]);
+            stg[cl] = y;
+          }
+          __syncthreads();
+          push_vec(xv, first_head * hd, stg, channels, R);
         }
         if (!ok) fail_here(IVB_ETIMEOUT);
         // the head ends the token: local top-k of my vocabulary slice for the sampler
@@ -482,13 +684,16 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           if (tid == 0) p.cand_n[rank] = kl;
         }
       }
+      tick(5);
+      if (marks != nullptr && tid == 0)
+        for (int k = 0; k < 6; ++k) marks[1 + k] = static_cast<unsigned long long>(prof[k]);
       mark(marks, 7);
+      cp_async_wait_all();  // the next descriptor has landed
+      ++opk;
       if (!sync_ok()) {
         alive = false;
         break;
       }
-      rd = wr;
-      wr ^= 1;
     }
     if (!alive) break;
     if (sampling) {
@@ -530,7 +735,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     ++pos;
     if (rank == 0 && tid == 0) p.position[0] = pos;
   }
-  // let every in-flight bulk copy land before the CTA's shared memory goes away
+  // let every in-flight copy land before the CTA's shared memory goes away
+  cp_async_wait_all();
   if (tid == 0) {
     while (st.consumed < st.issued) {
       if (!mbar_wait_bounded(st.full + st.consumed % kStages, (st.consumed / kStages) & 1u, p.timeout_ns)) break;
@@ -683,7 +889,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   const int dper = (d + R - 1) / R, Fper = (F + R - 1) / R, Lper = (Lt + R - 1) / R, Vper = (md.vocab + R - 1) / R;
   auto heads_of = [&](int c) { return std::max(0, std::min(H - c * hpc, hpc)); };
   auto part = [&](int n, int per, int c) { return std::max(0, std::min(n, (c + 1) * per) - std::min(n, c * per)); };
-  const size_t stage = 28 * 1024;
+  const size_t stage = 36 * 1024;
   dec->kc = std::min(std::min(md.max_top_k, md.vocab), kMaxTopK);
   // ---- op program and per-CTA segments ------------------------------------------------------------
   struct OpPlan {
@@ -710,7 +916,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     pl.op.has_bias = m.bias != nullptr;
     const int chunks = (in_n + 63) / 64;
     int lg = 0;
-    while ((1 << lg) < (chunks + 3) / 4 && lg < 5) ++lg;
+    while ((1 << lg) < (chunks + 2) / 3 && lg < 5) ++lg;  // at most three chunks per lane when possible
     pl.op.lpr_log = lg;
     pl.op.has_norm = norm != nullptr;
     pl.op.norm_eps = eps;
@@ -739,6 +945,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
       OpPlan e = gemv_op(OP_ENTRY_MLA, li, L.entry, d, hpc * (hd + D.rope) + Lper, H * (hd + D.rope) + Lt, gather0, d,
                          dper, L.mixer_norm, L.mixer_norm_eps);
       e.layer = &L;
+      e.op.push_per = Lper;
       for (int c = 0; c < R; ++c) {
         for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, (c * hpc + hl) * hd, hd});
         for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, d + Lt + (c * hpc + hl) * D.rope, D.rope});
@@ -834,6 +1041,8 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     }
     const size_t per_row = op.row_bytes + op.scale_stride * 2 + 4;
     int cr = static_cast<int>((stage - 64) / per_row);
+    const int rpi = kThreads >> op.lpr_log;  // rows one pass of chunk_rows covers
+    if (cr >= rpi) cr = cr / rpi * rpi;
     if (op.kind == OP_GATE_UP) cr &= ~1;
     cr = std::max(2, std::min(cr, std::max(2, op.rows_per)));
     op.chunk_rows = cr;
@@ -963,7 +1172,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   int pub_n = std::max(std::max(hpc * hd, Lper), std::max(dper, Fper));
   M.pub_n = pub_n;
   M.pub = static_cast<int>(o);
-  o += r16(static_cast<size_t>(2) * pub_n * 4);
+  o += r16(static_cast<size_t>(pub_n) * 4);  // staging of the op's output slice
   int loc_n = 0;
   for (const Op& op : dec->ops) loc_n = std::max(loc_n, op.kind == OP_ATTN ? 0 : op.rows_per);
   M.loc = static_cast<int>(o);
@@ -974,7 +1183,9 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   o += r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4);
   M.u = static_cast<int>(o);
   const int kc = dec->kc;
-  size_t u_need = r16(static_cast<size_t>(hpc) * (2 * S + hd * (2 + D.taps)) * 4);
+  // recurrent op: constants, coefficients, values, partial readouts, prefetched state
+  size_t u_need = r16((static_cast<size_t>(ssm_const_floats(hpc, S, hd, D.taps)) + 5 * hpc * S + hpc * hd + std::max(kThreads, hpc * hd) +
+                       3 * static_cast<size_t>(hpc) * S * hd + static_cast<size_t>(hpc) * hd * (D.taps - 1)) * 4);
   u_need = std::max(u_need, r16(static_cast<size_t>(Vper) * 4) + 2 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
   u_need = std::max(u_need, 2 * r16(static_cast<size_t>(R) * kc * 4) + 5 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
   const size_t attn_fixed = r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4) + r16((Lt + 63) / 64 * 64) +

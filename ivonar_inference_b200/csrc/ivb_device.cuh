@@ -15,6 +15,9 @@ namespace ivb {
 
 constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
+// The quantiser's sum of squares keeps a fixed 256-lane order (lane t sums inputs t, t+256, ... with
+// fmaf, then a warp butterfly and the warps in order), independent of the CTA size.
+constexpr int kCanonLanes = 256;
 constexpr int kPrefetch = 8;          // weight chunks (16 B) per thread held in registers across a barrier
 constexpr int kMaxLatentPerLane = 16;  // latent_dim <= 512
 constexpr int kMaxStateDim = 16;
@@ -48,16 +51,16 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // n floats from global (L2) into shared memory, eight independent loads in flight per thread.
 __device__ __forceinline__ void load_vector(const float* __restrict__ src, int n, float* dst) {
   const int tid = threadIdx.x;
-  for (int base = 0; base < n; base += 8 * 256) {
+  for (int base = 0; base < n; base += 8 * kThreads) {
     float r[8];
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int i = base + tid + k * 256;
+      const int i = base + tid + k * kThreads;
       r[k] = i < n ? __ldcg(src + i) : 0.0f;
     }
 #pragma unroll
     for (int k = 0; k < 8; ++k) {
-      const int i = base + tid + k * 256;
+      const int i = base + tid + k * kThreads;
       if (i < n) dst[i] = r[k];
     }
   }
@@ -150,7 +153,14 @@ __device__ __forceinline__ int act_slot(int i) {
   return (u << 6) + (slot << 4) + ((i & 3) << 2) + ((i >> 2) & 3);
 }
 
-// int32 sum over 64 inputs of code * q8 (codes 0..2 = ternary value + 1).
+// int32 sum over 64 inputs of code * q8 (codes 0..2 = ternary value + 1). Four independent dp4a
+// chains (one per weight word) keep the dependency depth at four.
+__device__ __forceinline__ int word_dot(unsigned w, const int4 a) {
+  int d = __dp4a(static_cast<int>(w & 0x03030303u), a.x, 0);
+  d = __dp4a(static_cast<int>((w >> 2) & 0x03030303u), a.y, d);
+  d = __dp4a(static_cast<int>((w >> 4) & 0x03030303u), a.z, d);
+  return __dp4a(static_cast<int>((w >> 6) & 0x03030303u), a.w, d);
+}
 __device__ __forceinline__ int chunk_dot(const uint4 w, const int8_t* act, int u) {
   const int rot = (u >> 1) & 3;
   const char* base = reinterpret_cast<const char*>(act) + (u << 6);
@@ -158,71 +168,115 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const int8_t* act, int u
   const int4 a1 = *reinterpret_cast<const int4*>(base + (((1 + rot) & 3) << 4));
   const int4 a2 = *reinterpret_cast<const int4*>(base + (((2 + rot) & 3) << 4));
   const int4 a3 = *reinterpret_cast<const int4*>(base + (((3 + rot) & 3) << 4));
-  int d = 0;
-  d = __dp4a(static_cast<int>(w.x & 0x03030303u), a0.x, d);
-  d = __dp4a(static_cast<int>((w.x >> 2) & 0x03030303u), a0.y, d);
-  d = __dp4a(static_cast<int>((w.x >> 4) & 0x03030303u), a0.z, d);
-  d = __dp4a(static_cast<int>((w.x >> 6) & 0x03030303u), a0.w, d);
-  d = __dp4a(static_cast<int>(w.y & 0x03030303u), a1.x, d);
-  d = __dp4a(static_cast<int>((w.y >> 2) & 0x03030303u), a1.y, d);
-  d = __dp4a(static_cast<int>((w.y >> 4) & 0x03030303u), a1.z, d);
-  d = __dp4a(static_cast<int>((w.y >> 6) & 0x03030303u), a1.w, d);
-  d = __dp4a(static_cast<int>(w.z & 0x03030303u), a2.x, d);
-  d = __dp4a(static_cast<int>((w.z >> 2) & 0x03030303u), a2.y, d);
-  d = __dp4a(static_cast<int>((w.z >> 4) & 0x03030303u), a2.z, d);
-  d = __dp4a(static_cast<int>((w.z >> 6) & 0x03030303u), a2.w, d);
-  d = __dp4a(static_cast<int>(w.w & 0x03030303u), a3.x, d);
-  d = __dp4a(static_cast<int>((w.w >> 2) & 0x03030303u), a3.y, d);
-  d = __dp4a(static_cast<int>((w.w >> 4) & 0x03030303u), a3.z, d);
-  d = __dp4a(static_cast<int>((w.w >> 6) & 0x03030303u), a3.w, d);
-  return d;
+  return (word_dot(w.x, a0) + word_dot(w.y, a1)) + (word_dot(w.z, a2) + word_dot(w.w, a3));
 }
 
 // ------------------------------------------------------------------------------------------------
 // Canonical per-token int8 quantiser (optionally with RMSNorm: clamp(x * inv_rms, +-clip) * w).
-// xv holds the fp32 input (n values, shared). Thread t owns inputs t, t+256, ...; the sum of squares
-// uses fmaf in that order, then block_sum. inv_rms = 1 / sqrtf(ss / n + eps) (IEEE sqrt and divide),
+// src holds the fp32 input (n values, shared). For the sum of squares lane t < 256 owns inputs
+// t, t+256, ... and accumulates them with fmaf in that order, then block_sum. inv_rms = 1 / sqrtf(ss / n + eps) (IEEE sqrt and divide),
 // scale = max(amax / 127, act_eps), code = rintf(v / scale). Writes codes either in the transposed
 // GEMV layout (transposed = true) or in natural order, and 64-input chunk sums to xsum (if given).
 // Returns the activation scale. Reference: ternary.cu:148-197, cpu_decoder.py:30-70.
 // ------------------------------------------------------------------------------------------------
-static __device__ float quantize_block(float* xv, int n, const float* norm_w, float norm_eps, float clip, float act_eps,
-                                int8_t* codes, bool transposed, int* xsum, float* red) {
+// Register-resident form for n <= kThreads * M: every thread keeps its M inputs in registers from the
+// first read to the codes (same arithmetic and order as the generic form below; src is not written).
+template <int M>
+__device__ __forceinline__ float quantize_regs(const float* src, int n, const float* norm_w, float norm_eps, float clip,
+                                               float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
   const int tid = threadIdx.x;
   const int chunks = (n + 63) >> 6;
+  float v[M];
+#pragma unroll
+  for (int m = 0; m < M; ++m) {
+    const int i = tid + m * kThreads;
+    v[m] = i < n ? src[i] : 0.0f;
+  }
   if (norm_w != nullptr) {
     float p = 0.0f;
-    for (int i = tid; i < n; i += kThreads) {
-      const float x = xv[i];
-      p = fmaf(x, x, p);
-    }
-    const float ss = block_sum(p, red);
+    if (tid < kCanonLanes)
+      for (int i = tid; i < n; i += kCanonLanes) {
+        const float x = src[i];
+        p = fmaf(x, x, p);
+      }
+    const float ss = block_sum(p, red);  // warps beyond the canonical lanes add exact zeros
     const float inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
-    for (int i = tid; i < n; i += kThreads) {
-      const float a = __fmul_rn(xv[i], inv);
-      xv[i] = __fmul_rn(fminf(fmaxf(a, -clip), clip), norm_w[i]);  // norm_w may be shared or global
+#pragma unroll
+    for (int m = 0; m < M; ++m) {
+      const int i = tid + m * kThreads;
+      if (i < n) v[m] = __fmul_rn(fminf(fmaxf(__fmul_rn(v[m], inv), -clip), clip), norm_w[i]);
     }
   }
   float am = 0.0f;
-  for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(xv[i]));
+#pragma unroll
+  for (int m = 0; m < M; ++m) am = fmaxf(am, fabsf(v[m]));
+  if (xsum != nullptr)
+    for (int u = tid; u < chunks; u += kThreads) xsum[u] = 0;
   const float amax = block_max(am, red);
   const float scale = fmaxf(amax / 127.0f, act_eps);
-  for (int i = tid; i < n; i += kThreads) {
-    const int q = static_cast<int>(rintf(xv[i] / scale));
-    codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
-  }
-  for (int i = n + tid; i < (chunks << 6); i += kThreads) codes[transposed ? act_slot(i) : i] = 0;
-  __syncthreads();
-  if (xsum != nullptr) {
-    for (int u = tid; u < chunks; u += kThreads) {
-      const int* words = reinterpret_cast<const int*>(codes + (u << 6));
-      int total = 0;
+  const int lane = tid & 31;
 #pragma unroll
-      for (int w = 0; w < 16; ++w) total = __dp4a(words[w], 0x01010101, total);
-      xsum[u] = total;
+  for (int m = 0; m < M; ++m) {
+    const int i = tid + m * kThreads;
+    if (m * kThreads >= (chunks << 6)) break;  // uniform
+    const int q = i < n ? static_cast<int>(rintf(v[m] / scale)) : 0;
+    if (i < (chunks << 6)) codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
+    if (xsum != nullptr) {
+      int t = q;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(kFull, t, off);
+      if (lane == 0 && i < (chunks << 6)) atomicAdd(xsum + (i >> 6), t);
     }
-    __syncthreads();
   }
+  __syncthreads();
+  return scale;
+}
+
+// src is only read (it may be another CTA's push target of a later op, or a shared replica).
+static __device__ float quantize_block(const float* src, int n, const float* norm_w, float norm_eps, float clip,
+                                       float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
+  if (n <= 4 * kThreads) return quantize_regs<4>(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
+  if (n <= 12 * kThreads) return quantize_regs<12>(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
+  // generic form: the normalised value is recomputed (bit-identically) wherever it is needed
+  const int tid = threadIdx.x;
+  const int chunks = (n + 63) >> 6;
+  float inv = 0.0f;
+  if (norm_w != nullptr) {
+    float p = 0.0f;
+    if (tid < kCanonLanes)
+      for (int i = tid; i < n; i += kCanonLanes) {
+        const float x = src[i];
+        p = fmaf(x, x, p);
+      }
+    const float ss = block_sum(p, red);
+    inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
+  }
+  auto value = [&](int i) -> float {
+    const float x = src[i];
+    return norm_w != nullptr ? __fmul_rn(fminf(fmaxf(__fmul_rn(x, inv), -clip), clip), norm_w[i]) : x;
+  };
+  float am = 0.0f;
+  for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(value(i)));
+  if (xsum != nullptr)
+    for (int u = tid; u < chunks; u += kThreads) xsum[u] = 0;
+  const float amax = block_max(am, red);
+  const float scale = fmaxf(amax / 127.0f, act_eps);
+  // codes; each warp's 32 consecutive inputs of one pass share a 64-input chunk, so the chunk sums
+  // are warp reductions added with shared atomics (integer, so the order does not matter)
+  const int lane = tid & 31;
+  for (int base = 0; base < (chunks << 6); base += kThreads) {
+    const int i = base + tid;
+    int q = 0;
+    if (i < n) q = static_cast<int>(rintf(value(i) / scale));
+    if (i < (chunks << 6)) codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
+    if (xsum != nullptr) {
+      int t = q;
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(kFull, t, off);
+      if (lane == 0 && i < (chunks << 6)) atomicAdd(xsum + (i >> 6), t);
+    }
+  }
+  __syncthreads();
   return scale;
 }
 
