@@ -248,6 +248,21 @@ __device__ __forceinline__ int chunk_dot_regs(const uint4 w, const ActChunk& a) 
   return (s0 + (s1 >> 2)) + ((s2 >> 4) + (s3 >> 6)) - a.xsum;
 }
 
+// The same sum times 64, combined with shift-adds (64 s0 + 16 s1 + 4 s2 + s3 - 64 xsum); exact, and
+// the factor 64 is folded into the group scale by the caller (|result| < 2^23, so its float is exact).
+__device__ __forceinline__ int chunk_dot64(const uint4 w, const ActChunk& a) {
+  const unsigned ws[4] = {w.x, w.y, w.z, w.w};
+  int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
+#pragma unroll
+  for (int k = 0; k < 4; ++k) {
+    s0 = dp4a_us(ws[k] & 0x03030303u, a.q[k].x, s0);
+    s1 = dp4a_us(ws[k] & 0x0C0C0C0Cu, a.q[k].y, s1);
+    s2 = dp4a_us(ws[k] & 0x30303030u, a.q[k].z, s2);
+    s3 = dp4a_us(ws[k] & 0xC0C0C0C0u, a.q[k].w, s3);
+  }
+  return ((((s0 << 2) + s1) << 2) + s2) * 4 + s3 - (a.xsum << 6);
+}
+
 // rows [0, k) of a chunk laid out [k x row_bytes packed][k x scale_stride fp16 (16B pad)][k x fp32 bias]
 // Lane group of 2^lpr_log lanes per row; lane `sub` owns chunks sub + j * 2^lpr_log (j < KPL), whose
 // activations stay in registers for all rows. Every thread runs RPT rows per pass. Results of row r
@@ -260,6 +275,8 @@ __device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char
   const int lpr = 1 << lg;
   const int rpi = kThreads >> lg;
   const int chunks = (op.in_n + 63) >> 6;
+  const int row_bytes = op.row_bytes, sstride = op.scale_stride;  // op lives in shared memory
+  const bool has_bias = op.has_bias != 0;
   const int sub = tid & (lpr - 1);
   ActChunk a[KPL];
   bool have[KPL];
@@ -269,9 +286,8 @@ __device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char
     have[j] = u < chunks;
     if (have[j]) a[j] = load_act_chunk(act, nullptr, u);
   }
-  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * op.row_bytes);
-  const float* bias =
-      reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * op.row_bytes + round16(k * op.scale_stride * 2));
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
+  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
   for (int base = 0; base < k; base += RPT * rpi) {
     int r[RPT];
     bool v[RPT];
@@ -280,7 +296,7 @@ __device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char
     for (int t = 0; t < RPT; ++t) {
       r[t] = base + t * rpi + (tid >> lg);
       v[t] = r[t] < k;
-      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r[t]) * op.row_bytes);
+      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r[t]) * row_bytes);
 #pragma unroll
       for (int j = 0; j < KPL; ++j) {
         const int u = sub + (j << lg);
@@ -295,7 +311,7 @@ __device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char
       for (int j = 0; j < KPL; ++j) {
         const int u = sub + (j << lg);
         if (have[j] && v[t])
-          acc[t] = fmaf(static_cast<float>(chunk_dot_regs(w[t][j], a[j])), h2f(scales[r[t] * op.scale_stride + (u >> 1)]),
+          acc[t] = fmaf(static_cast<float>(chunk_dot_regs(w[t][j], a[j])), h2f(scales[r[t] * sstride + (u >> 1)]),
                         acc[t]);
       }
     }
@@ -306,8 +322,67 @@ __device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char
     if (sub == 0) {
 #pragma unroll
       for (int t = 0; t < RPT; ++t)
-        if (v[t]) out[r[t]] = op.has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
+        if (v[t]) out[r[t]] = has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
     }
+  }
+}
+
+// Compile-time lane geometry for the common shapes: LG = log2 lanes per row, KPL chunks per lane,
+// RPT rows per thread per pass. The lane's activation chunks (a, have) are loaded once per op by
+// load_act_ct and stay in registers for every stage of the op.
+template <int LG, int KPL>
+__device__ __forceinline__ void load_act_ct(const int8_t* act, int chunks, ActChunk (&a)[KPL], bool (&have)[KPL]) {
+  const int sub = threadIdx.x & ((1 << LG) - 1);
+#pragma unroll
+  for (int j = 0; j < KPL; ++j) {
+    const int u = sub + (j << LG);
+    have[j] = u < chunks;
+    if (have[j]) {
+      a[j] = load_act_chunk(act, nullptr, u);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a[j].q[q] = make_int4(0, 0, 0, 0);
+      a[j].xsum = 0;
+    }
+  }
+}
+
+template <int LG, int KPL, int RPT>
+__device__ __forceinline__ void rows_stage_ct(const ActChunk (&a)[KPL], const bool (&have)[KPL], const unsigned char* stage,
+                                              int k, int row_bytes, int sstride, bool has_bias, float act_scale, float* out) {
+  constexpr int LPR = 1 << LG, RPI = kThreads >> LG;
+  const int tid = threadIdx.x, sub = tid & (LPR - 1);
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
+  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
+  for (int base = 0; base < k; base += RPT * RPI) {
+    int r[RPT];
+    uint4 w[RPT][KPL];
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      r[t] = base + t * RPI + (tid >> LG);
+      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(min(r[t], k - 1)) * row_bytes);
+#pragma unroll
+      for (int j = 0; j < KPL; ++j) w[t][j] = have[j] ? wr[sub + (j << LG)] : make_uint4(0u, 0u, 0u, 0u);
+    }
+    float acc[RPT];
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      acc[t] = 0.0f;
+      const uint16_t* srow = scales + min(r[t], k - 1) * sstride;
+#pragma unroll
+      for (int j = 0; j < KPL; ++j) {
+        const float sc = have[j] ? h2f(srow[(sub + (j << LG)) >> 1]) * (1.0f / 64.0f) : 0.0f;
+        acc[t] = fmaf(static_cast<float>(chunk_dot64(w[t][j], a[j])), sc, acc[t]);
+      }
+    }
+#pragma unroll
+    for (int off = 1; off < LPR; off <<= 1)
+#pragma unroll
+      for (int t = 0; t < RPT; ++t) acc[t] += __shfl_xor_sync(kFull, acc[t], off);
+    if (sub == 0)
+#pragma unroll
+      for (int t = 0; t < RPT; ++t)
+        if (r[t] < k) out[r[t]] = has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
   }
 }
 
@@ -344,8 +419,8 @@ __device__ __forceinline__ void chunk_rows(const Op& op, const unsigned char* st
   const int chunks = (op.in_n + 63) >> 6;
   const int kpl = (chunks + (1 << op.lpr_log) - 1) >> op.lpr_log;
   switch (kpl) {
-    case 1: chunk_rows_kpl<1, 2>(op, stage, k, act, xsum, act_scale, out); break;
-    case 2: chunk_rows_kpl<2, 2>(op, stage, k, act, xsum, act_scale, out); break;
+    case 1: chunk_rows_kpl<1, 4>(op, stage, k, act, xsum, act_scale, out); break;
+    case 2: chunk_rows_kpl<2, 4>(op, stage, k, act, xsum, act_scale, out); break;
     case 3: chunk_rows_kpl<3, 2>(op, stage, k, act, xsum, act_scale, out); break;
     default: chunk_rows_wide(op, stage, k, act, xsum, act_scale, out); break;
   }

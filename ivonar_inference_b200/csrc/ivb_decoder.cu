@@ -121,6 +121,36 @@ __device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const ClusterD
   bulk_copy(tb.kr, L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + start) * D.rpad, kr, bar);
 }
 
+// Rows of all stages of a GEMV op with compile-time lane geometry; the lane's activation chunks are
+// loaded once and stay in registers across the stages. Returns false when a stage wait ran out.
+template <int LG, int KPL, int RPT, typename Tick>
+__device__ __forceinline__ bool rows_ct(const ClusterParams& p, Stream& st, unsigned rank, const Op& op, int rows_c,
+                                        const int8_t* act, float act_scale, float* rows_out, Tick& tick) {
+  const int chunks = (op.in_n + 63) >> 6;
+  const int row_bytes = op.row_bytes, sstride = op.scale_stride;
+  const bool has_bias = op.has_bias != 0;
+  const int n_row_chunks = op.n_chunks - op.has_const, crows = op.chunk_rows;
+  ActChunk a[KPL];
+  bool have[KPL];
+  load_act_ct<LG, KPL>(act, chunks, a, have);
+  bool ok = true;
+  for (int c = 0; c < n_row_chunks; ++c) {
+    const unsigned char* stage = stream_acquire(p, st);
+    tick(2);
+    if (stage == nullptr) {
+      ok = false;
+    } else {
+      const int r0 = c * crows;
+      rows_stage_ct<LG, KPL, RPT>(a, have, stage, max(0, min(crows, rows_c - r0)), row_bytes, sstride, has_bias, act_scale,
+                                  rows_out + r0);
+    }
+    tick(3);
+    stream_release(p, st, rank);
+    tick(4);
+  }
+  return ok;
+}
+
 __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __grid_constant__ ClusterParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long full[kStages];
@@ -555,7 +585,15 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         // rows of this CTA, chunk by chunk
         float* rows_out = loc;
         const int n_row_chunks = op.n_chunks - op.has_const;
-        for (int c = 0; c < n_row_chunks; ++c) {
+        const int kpl = (((op.in_n + 63) >> 6) + (1 << op.lpr_log) - 1) >> op.lpr_log;
+        const int geo = op.lpr_log * 8 + kpl;
+        bool done_ct = true;
+        if (geo == 3 * 8 + 2) ok &= rows_ct<3, 2, 4>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
+        else if (geo == 4 * 8 + 3) ok &= rows_ct<4, 3, 3>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
+        else if (geo == 5 * 8 + 2) ok &= rows_ct<5, 2, 4>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
+        else if (geo == 5 * 8 + 3) ok &= rows_ct<5, 3, 2>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
+        else done_ct = false;
+        for (int c = 0; c < (done_ct ? 0 : n_row_chunks); ++c) {
           const unsigned char* stage = stream_acquire(p, st);
           tick(2);
           if (stage == nullptr) {
@@ -1041,7 +1079,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     }
     const size_t per_row = op.row_bytes + op.scale_stride * 2 + 4;
     int cr = static_cast<int>((stage - 64) / per_row);
-    const int rpi = kThreads >> op.lpr_log;  // rows one pass of chunk_rows covers
+    const int rpi = kThreads >> op.lpr_log;  // rows one thread-row of chunk_rows covers
     if (cr >= rpi) cr = cr / rpi * rpi;
     if (op.kind == OP_GATE_UP) cr &= ~1;
     cr = std::max(2, std::min(cr, std::max(2, op.rows_per)));

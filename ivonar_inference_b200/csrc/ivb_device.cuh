@@ -127,6 +127,18 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
   __syncthreads();
   return t;
 }
+// Block maximum of non-negative floats: their bit patterns order like the values, so each warp
+// reduces with one redux instruction and the warps meet in a shared word (exact; order-free).
+__device__ __forceinline__ float block_max_nonneg(float v, float* red) {
+  const unsigned m = __reduce_max_sync(kFull, __float_as_uint(v));
+  unsigned* slot = reinterpret_cast<unsigned*>(red) + 32;
+  if (threadIdx.x == 0) *slot = 0u;
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) atomicMax(slot, m);
+  __syncthreads();
+  const float t = __uint_as_float(*slot);
+  return t;
+}
 __device__ __forceinline__ float block_max(float v, float* red) {
   v = warp_max(v);
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -171,6 +183,24 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const int8_t* act, int u
   return (word_dot(w.x, a0) + word_dot(w.y, a1)) + (word_dot(w.z, a2) + word_dot(w.w, a3));
 }
 
+// rintf(v / scale) without a division per element: y = v * (1 / scale) differs from the true quotient
+// v / scale by at most |v / scale| * 2^-23 (two roundings), and the correctly rounded quotient by at
+// most half an ulp more. When y is farther than that from every half-integer, both round to the same
+// integer; the rare values closer to a half-integer take the IEEE division. |v / scale| <= 128 here.
+// quant_code_fast returns the code and sets `near` instead of branching, so a caller can keep its
+// loop free of control flow and redo the flagged values afterwards.
+__device__ __forceinline__ int quant_code_fast(float v, float rscale, bool& near) {
+  const float y = v * rscale;
+  const float r = rintf(y);
+  near = !(fabsf(fabsf(y - r) - 0.5f) > 4.0e-5f);
+  return static_cast<int>(r);
+}
+__device__ __forceinline__ int quant_code(float v, float scale, float rscale) {
+  bool near;
+  const int q = quant_code_fast(v, rscale, near);
+  return near ? static_cast<int>(rintf(v / scale)) : q;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Canonical per-token int8 quantiser (optionally with RMSNorm: clamp(x * inv_rms, +-clip) * w).
 // src holds the fp32 input (n values, shared). For the sum of squares lane t < 256 owns inputs
@@ -179,76 +209,24 @@ __device__ __forceinline__ int chunk_dot(const uint4 w, const int8_t* act, int u
 // GEMV layout (transposed = true) or in natural order, and 64-input chunk sums to xsum (if given).
 // Returns the activation scale. Reference: ternary.cu:148-197, cpu_decoder.py:30-70.
 // ------------------------------------------------------------------------------------------------
-// Register-resident form for n <= kThreads * M: every thread keeps its M inputs in registers from the
-// first read to the codes (same arithmetic and order as the generic form below; src is not written).
-template <int M>
-__device__ __forceinline__ float quantize_regs(const float* src, int n, const float* norm_w, float norm_eps, float clip,
-                                               float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
-  const int tid = threadIdx.x;
-  const int chunks = (n + 63) >> 6;
-  float v[M];
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
-    const int i = tid + m * kThreads;
-    v[m] = i < n ? src[i] : 0.0f;
-  }
-  if (norm_w != nullptr) {
-    float p = 0.0f;
-    if (tid < kCanonLanes)
-      for (int i = tid; i < n; i += kCanonLanes) {
-        const float x = src[i];
-        p = fmaf(x, x, p);
-      }
-    const float ss = block_sum(p, red);  // warps beyond the canonical lanes add exact zeros
-    const float inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
-#pragma unroll
-    for (int m = 0; m < M; ++m) {
-      const int i = tid + m * kThreads;
-      if (i < n) v[m] = __fmul_rn(fminf(fmaxf(__fmul_rn(v[m], inv), -clip), clip), norm_w[i]);
-    }
-  }
-  float am = 0.0f;
-#pragma unroll
-  for (int m = 0; m < M; ++m) am = fmaxf(am, fabsf(v[m]));
-  if (xsum != nullptr)
-    for (int u = tid; u < chunks; u += kThreads) xsum[u] = 0;
-  const float amax = block_max(am, red);
-  const float scale = fmaxf(amax / 127.0f, act_eps);
-  const int lane = tid & 31;
-#pragma unroll
-  for (int m = 0; m < M; ++m) {
-    const int i = tid + m * kThreads;
-    if (m * kThreads >= (chunks << 6)) break;  // uniform
-    const int q = i < n ? static_cast<int>(rintf(v[m] / scale)) : 0;
-    if (i < (chunks << 6)) codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
-    if (xsum != nullptr) {
-      int t = q;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(kFull, t, off);
-      if (lane == 0 && i < (chunks << 6)) atomicAdd(xsum + (i >> 6), t);
-    }
-  }
-  __syncthreads();
-  return scale;
-}
-
-// src is only read (it may be another CTA's push target of a later op, or a shared replica).
+// One compact code path for every n (the decode kernel runs it between many other ops, so its
+// instruction footprint matters more than re-reading src): the normalised value is recomputed
+// bit-identically in each pass. src is only read (it may be a push target of a later op).
 static __device__ float quantize_block(const float* src, int n, const float* norm_w, float norm_eps, float clip,
                                        float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
-  if (n <= 4 * kThreads) return quantize_regs<4>(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
-  if (n <= 12 * kThreads) return quantize_regs<12>(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
-  // generic form: the normalised value is recomputed (bit-identically) wherever it is needed
-  const int tid = threadIdx.x;
-  const int chunks = (n + 63) >> 6;
+  const int tid = threadIdx.x, lane = tid & 31;
+  const int chunks = (n + 63) >> 6, padded = chunks << 6;
   float inv = 0.0f;
   if (norm_w != nullptr) {
     float p = 0.0f;
-    if (tid < kCanonLanes)
+    if (tid < kCanonLanes) {
+#pragma unroll 4
       for (int i = tid; i < n; i += kCanonLanes) {
         const float x = src[i];
         p = fmaf(x, x, p);
       }
-    const float ss = block_sum(p, red);
+    }
+    const float ss = block_sum(p, red);  // warps beyond the canonical lanes add exact zeros
     inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
   }
   auto value = [&](int i) -> float {
@@ -256,27 +234,44 @@ static __device__ float quantize_block(const float* src, int n, const float* nor
     return norm_w != nullptr ? __fmul_rn(fminf(fmaxf(__fmul_rn(x, inv), -clip), clip), norm_w[i]) : x;
   };
   float am = 0.0f;
+#pragma unroll 4
   for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(value(i)));
   if (xsum != nullptr)
     for (int u = tid; u < chunks; u += kThreads) xsum[u] = 0;
-  const float amax = block_max(am, red);
+  const float amax = block_max_nonneg(am, red);
   const float scale = fmaxf(amax / 127.0f, act_eps);
-  // codes; each warp's 32 consecutive inputs of one pass share a 64-input chunk, so the chunk sums
-  // are warp reductions added with shared atomics (integer, so the order does not matter)
-  const int lane = tid & 31;
-  for (int base = 0; base < (chunks << 6); base += kThreads) {
+  const float rscale = 1.0f / scale;
+  // codes; each warp's 32 consecutive inputs of one pass share a 64-input chunk, so the chunk sums are
+  // warp reductions added with shared atomics (integers: the order does not matter)
+  bool near = false;
+#pragma unroll 4
+  for (int base = 0; base < padded; base += kThreads) {
     const int i = base + tid;
-    int q = 0;
-    if (i < n) q = static_cast<int>(rintf(value(i) / scale));
-    if (i < (chunks << 6)) codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
+    bool nr = false;
+    const int q = i < n ? quant_code_fast(value(i), rscale, nr) : 0;
+    near |= nr;
+    if (i < padded) codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(q);
     if (xsum != nullptr) {
-      int t = q;
-#pragma unroll
-      for (int off = 16; off > 0; off >>= 1) t += __shfl_xor_sync(kFull, t, off);
-      if (lane == 0 && i < (chunks << 6)) atomicAdd(xsum + (i >> 6), t);
+      const int t = __reduce_add_sync(kFull, q);
+      if (lane == 0 && i < padded) atomicAdd(xsum + (i >> 6), t);
     }
   }
-  __syncthreads();
+  if (__syncthreads_or(near)) {
+    // rare: values within rounding distance of a half-integer take the IEEE division
+    for (int i = tid; i < n; i += kThreads) {
+      const float v = value(i);
+      bool nr = false;
+      const int q = quant_code_fast(v, rscale, nr);
+      if (nr) {
+        const int qe = static_cast<int>(rintf(v / scale));
+        if (qe != q) {
+          codes[transposed ? act_slot(i) : i] = static_cast<int8_t>(qe);
+          if (xsum != nullptr) atomicAdd(xsum + (i >> 6), qe - q);
+        }
+      }
+    }
+    __syncthreads();
+  }
   return scale;
 }
 
