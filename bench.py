@@ -59,6 +59,12 @@ def measured_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture (--set full) of a 16-token decode launch
+# of this workload (795,531,264 + 22,050,048 bytes), per token; scaled to a launch by the tokens it runs.
+NCU_DRAM_BYTES_PER_TOKEN = (795_531_264 + 22_050_048) / 16
+TRAFFIC_SOURCE = "ncu capture of a 16-token decode launch at positions 37-52, scaled by tokens per launch"
+
+
 def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
     """Algorithmic HBM bytes of `tokens` decode steps starting at `first_position`.
 
@@ -270,7 +276,8 @@ def run_b200(args) -> None:
         launch_s = (sum(step_ms) / len(step_ms)) / 1000.0
         achieved = nbytes / launch_s / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                    "traffic": None, "peak_source": peak_kind, "kernel": "ivb::decode_kernel",
+                    "traffic": NCU_DRAM_BYTES_PER_TOKEN * tokens, "traffic_source": TRAFFIC_SOURCE,
+                    "peak_source": peak_kind, "kernel": "ivb::cluster_decode_kernel",
                     "algorithmic_bytes_per_launch": nbytes, **parts}
         line = {
             "metric": "decode tok/s (b=1)", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,

@@ -43,6 +43,13 @@ struct Op {
   int32_t c_wkn, c_skn, c_bkn, c_wv, c_sv, c_bv;
 };
 
+// Device record of one op: its descriptor and a copy of its block's layer description, so one
+// prefetch brings every per-op parameter into shared memory.
+struct __align__(16) OpRec {
+  Op op;
+  IvbLayerDesc layer;  // zero for the head
+};
+
 struct ClusterDims {
   int32_t vocab, hidden, heads, head_dim, state_dim, latent, rope, nope, dense, max_len, max_top_k;
   int32_t R, hpc;                  // cluster size, heads per CTA
@@ -58,12 +65,15 @@ struct ClusterDims {
 struct ClusterSmem {
   int32_t ring, stage_bytes;
   int32_t xv, act, xsum, resid, pub, pub_n, loc, red, xl;
+  int32_t ctab;                    // chunk table of the CTA: [cpt] u64 offsets, then [cpt] u32 sizes
+  int32_t rope_row;                // rope (cos, sin) row of the current position, prefetched by the mla entry op
+  int32_t seen;                    // the CTA's slice of the repetition flags, prefetched by the head op
   int32_t u;                       // union region (attention / sampler)
   int32_t total;
 };
 
 struct ClusterParams {
-  const Op* ops;
+  const OpRec* ops;
   const int32_t* op_rows;          // [n_ops][R] output rows of each CTA
   int32_t n_ops;
   int32_t kc;                      // candidate slots per CTA (>= top-k)
@@ -135,6 +145,8 @@ struct Stream {
   unsigned long long* full;  // [kStages] mbarriers
   unsigned char* ring;
   int stage_bytes;
+  const unsigned long long* coff;  // this CTA's chunk table (shared copy): byte offsets into the stream
+  const unsigned* cbytes;          // chunk sizes
   unsigned consumed, issued;
   int p_step, p_chunk;       // producer cursor
 };
@@ -150,13 +162,12 @@ __device__ __forceinline__ void stream_issue(const ClusterParams& p, Stream& s, 
     s.p_chunk = 0;
     if (++s.p_step >= p.steps) return;
   }
-  const size_t idx = static_cast<size_t>(rank) * p.chunks_per_token + s.p_chunk;
-  const unsigned bytes = p.chunk_bytes[idx];
+  const unsigned bytes = s.cbytes[s.p_chunk];
   const int stage = s.issued % kStages;
   unsigned long long* bar = s.full + stage;
   fence_proxy_async();
   mbar_expect_tx(bar, bytes);
-  bulk_copy(s.ring + static_cast<size_t>(stage) * s.stage_bytes, p.stream + p.chunk_off[idx], bytes, bar);
+  bulk_copy(s.ring + static_cast<size_t>(stage) * s.stage_bytes, p.stream + s.coff[s.p_chunk], bytes, bar);
   ++s.issued;
   if (++s.p_chunk == p.chunks_per_token) {
     s.p_chunk = 0;

@@ -151,12 +151,15 @@ __device__ __forceinline__ bool rows_ct(const ClusterParams& p, Stream& st, unsi
   return ok;
 }
 
+// rope table of an mla block (the entry op's layer description)
+__device__ __forceinline__ const float* L_entry_rope(const IvbLayerDesc& L) { return L.rope; }
+
 __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __grid_constant__ ClusterParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long full[kStages];
   __shared__ __align__(8) unsigned long long abar[2];
   __shared__ unsigned err_flag;  // cluster barrier number after which every CTA stops (~0u: none)
-  __shared__ __align__(16) Op opbuf[2];  // descriptor of the running op and the next one
+  __shared__ __align__(16) OpRec opbuf[2];  // the running op and the next one (descriptor + layer)
   __shared__ __align__(16) int rowsbuf[2][4];
   const unsigned rank = cluster_rank();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -179,15 +182,23 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     err_flag = 0xffffffffu;
   }
+  unsigned long long* coff = reinterpret_cast<unsigned long long*>(smem + M.ctab);
+  unsigned* cbytes = reinterpret_cast<unsigned*>(coff + p.chunks_per_token);
+  for (int c = tid; c < p.chunks_per_token; c += kThreads) {
+    coff[c] = p.chunk_off[static_cast<size_t>(rank) * p.chunks_per_token + c];
+    cbytes[c] = p.chunk_bytes[static_cast<size_t>(rank) * p.chunks_per_token + c];
+  }
+  float* rope_s = reinterpret_cast<float*>(smem + M.rope_row);
+  float* seen_s = reinterpret_cast<float*>(smem + M.seen);  // bytes; float* for the 4-byte copies
   __syncthreads();
   cluster_sync();
-  Stream st{full, smem + M.ring, M.stage_bytes, 0u, 0u, 0, 0};
+  Stream st{full, smem + M.ring, M.stage_bytes, coff, cbytes, 0u, 0u, 0, 0};
   // op descriptors travel through a two-slot shared buffer: op k+1 is fetched while op k runs
   auto fetch_op = [&](int oi, int slot) {
-    if (tid < static_cast<int>(sizeof(Op) / 16))
+    if (tid < static_cast<int>(sizeof(OpRec) / 16))
       cp_async_16(reinterpret_cast<unsigned char*>(&opbuf[slot]) + 16 * tid,
                   reinterpret_cast<const unsigned char*>(p.ops + oi) + 16 * tid);
-    else if (tid == 32)
+    else if (tid == kThreads - 1)
       cp_async_f32(reinterpret_cast<float*>(&rowsbuf[slot][0]), reinterpret_cast<const float*>(p.op_rows + oi * R + rank));
     cp_async_commit();
   };
@@ -241,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     __syncthreads();
     const int n_run = head ? p.n_ops : p.n_ops - 1;  // the head is the last op of the program
     for (int oi = 0; oi < n_run && alive; ++oi) {
-      const Op& op = opbuf[opk & 1];  // fields are read from shared memory where used
+      const Op& op = opbuf[opk & 1].op;  // fields are read from shared memory where used
+      const IvbLayerDesc& lay = opbuf[opk & 1].layer;
       const int rows_c = rowsbuf[opk & 1][0];
       fetch_op(oi + 1 < n_run ? oi + 1 : 0, (opk + 1) & 1);  // the op after this one (op 0 of the next token)
       unsigned long long* marks = tracing ? p.trace + (static_cast<size_t>(oi) * R + rank) * 8 : nullptr;
@@ -262,7 +274,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
       bool ok = true;
       if (op.kind == OP_ATTN) {
         // ---------------- latent attention over the compressed cache ----------------
-        const IvbLayerDesc& L = p.layers[op.layer];
+        const IvbLayerDesc& L = lay;
         const unsigned char* cst = stream_acquire(p, st);
         if (cst == nullptr) ok = false;
         float* qlat_f = reinterpret_cast<float*>(U);  // [latent] quantiser scratch
@@ -288,9 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           const float* qh = loc + hl * D.head_dim;
           const float* kh = loc + nh * D.head_dim + hl * D.rope;
           const float scl = L.attn_scale;
-          const float* rtab = L.rope + static_cast<size_t>(P) * D.rope;
           for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
-            const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+            const float cs = rope_s[2 * jr], sn = rope_s[2 * jr + 1];  // prefetched by the entry op
             const float q0 = qh[D.nope + 2 * jr], q1 = qh[D.nope + 2 * jr + 1];
             const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
             qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
@@ -376,6 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             for (int i = 0; i < 8; ++i) u[pc][i] = 0.0f;
           float m_run = -INFINITY, l_run = 0.0f;
           for (int ti = 0; ti < n_tiles; ++ti) {
+            tick(5);
             const int start = ti * D.tile;
             const int count = max(0, min(D.tile, P - start));
             const bool last = ti == n_tiles - 1;
@@ -390,6 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
               }
               apar[ti & 1] ^= 1u;
             }
+            tick(4);
             const int npos = count + (last ? 1 : 0);
             for (int k = grp; k - grp < npos; k += kThreads / 8) {
               const bool valid = k < npos;
@@ -424,6 +437,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
               if (valid && sub == 0) sc[k] = total + qb;
             }
             __syncthreads();
+            tick(2);
             float mx = -INFINITY;
             for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, sc[k]);
             mx = block_max(mx, red);
@@ -461,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             __syncthreads();
           }
           if (!ok) break;
-          tick(2);
+          tick(5);
 #pragma unroll
           for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc) {
             const int j0 = pc * 256 + lane * 8;
@@ -542,9 +556,20 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         float act_scale = 0.0f;
         float* ssmc = reinterpret_cast<float*>(U);
         const int S = D.state_dim, hd = D.head_dim, taps = D.taps;
+        if (op.kind == OP_ENTRY_MLA) {
+          // the rope row of this position, for the attention op that follows
+          const float* rrow = L_entry_rope(lay) + static_cast<size_t>(pos) * D.rope;
+          for (int i = tid; i < D.rope; i += kThreads) cp_async_f32(rope_s + i, rrow + i);
+          cp_async_commit();
+        } else if (op.kind == OP_HEAD && sampling && ((lo | rows_c) & 3) == 0) {
+          // the repetition flags of my vocabulary slice, for the local top-k
+          const float* src = reinterpret_cast<const float*>(p.seen + lo);
+          for (int i = tid; i < rows_c / 4; i += kThreads) cp_async_f32(seen_s + i, src + i);
+          cp_async_commit();
+        }
         if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
           // the recurrent state of my heads streams into shared memory while the rows are computed
-          const IvbLayerDesc& L = p.layers[op.layer];
+          const IvbLayerDesc& L = lay;
           const int nhs = nh * S, channels = nh * hd;
           float* dst = ssmc + ssm_const_floats(nh, S, hd, taps) + 5 * nhs + channels + max(kThreads, channels);
           const float* src[3] = {L.ssm_state + static_cast<size_t>(first_head) * S * hd * 2,
@@ -626,7 +651,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
         } else if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
           // recurrent step for the channels of my heads; rows_out = per head [value hd | gate hd | bc_dt 3S]
-          const IvbLayerDesc& L = p.layers[op.layer];
+          const IvbLayerDesc& L = lay;
           const float* decay = ssmc;
           const float* theta = decay + nh * S;
           const float* skip = theta + nh * S;
@@ -713,7 +738,12 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           unsigned* ck = keys + op.rows_per;
           int* ci = reinterpret_cast<int*>(ck + p.kc);
           TopkScratch ts{reinterpret_cast<unsigned*>(ci + p.kc), reinterpret_cast<int*>(ci + p.kc) + kWarps * 256};
-          for (int r = tid; r < rows_c; r += kThreads) keys[r] = score_key(rows_out[r], __ldcg(p.seen + lo + r), inv_t, pen, ipen);
+          cp_async_wait_all();
+          __syncthreads();
+          const uint8_t* seen_b = reinterpret_cast<const uint8_t*>(seen_s);
+          const bool pref = ((lo | rows_c) & 3) == 0;
+          for (int r = tid; r < rows_c; r += kThreads)
+            keys[r] = score_key(rows_out[r], pref ? seen_b[r] : __ldcg(p.seen + lo + r), inv_t, pen, ipen);
           __syncthreads();
           const int kl = min(K, rows_c);
           if (kl > 0)
@@ -815,6 +845,7 @@ struct IvbDecoder {
   ivb::ClusterDims d;
   ivb::ClusterSmem sm;
   std::vector<ivb::Op> ops;
+  std::vector<ivb::OpRec> recs;  // device op records, kept alive until the upload completes
   std::vector<int32_t> op_rows;
   std::vector<unsigned long long> chunk_off;
   std::vector<unsigned> chunk_bytes;
@@ -1219,6 +1250,12 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   o += r16(64 * 4);
   M.xl = static_cast<int>(o);
   o += r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4);
+  M.ctab = static_cast<int>(o);
+  o += r16(static_cast<size_t>(dec->cpt) * 8) + r16(static_cast<size_t>(dec->cpt) * 4);
+  M.rope_row = static_cast<int>(o);
+  o += r16(static_cast<size_t>(std::max(md.rope_dim, 1)) * 4);
+  M.seen = static_cast<int>(o);
+  o += r16(static_cast<size_t>(Vper));
   M.u = static_cast<int>(o);
   const int kc = dec->kc;
   // recurrent op: constants, coefficients, values, partial readouts, prefetched state
@@ -1275,7 +1312,7 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
   int dev = 0, optin = 0;
   IVB_CUDA(cudaGetDevice(&dev));
   IVB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-  const size_t cap = static_cast<size_t>(optin) - 1024;  // static shared memory of the kernel
+  const size_t cap = static_cast<size_t>(optin) - 4096;  // static shared memory of the kernel
   IVB_CUDA(cudaFuncSetAttribute(cluster_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
   std::string why = "no cluster size fits";
   bool planned = false;
@@ -1314,7 +1351,7 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
   dec->off_stream = off;
   off = align_up(off + dec->stream_bytes, 256);
   dec->off_ops = off;
-  off = align_up(off + dec->ops.size() * sizeof(Op), 256);
+  off = align_up(off + dec->ops.size() * sizeof(OpRec), 256);
   dec->off_op_rows = off;
   off = align_up(off + dec->op_rows.size() * 4, 256);
   dec->off_chunk_off = off;
@@ -1362,7 +1399,15 @@ int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream) {
       IVB_CUDA(cudaMemcpy2DAsync(blob + c.dst, c.dpitch, c.src, c.spitch, c.width, c.rows, cudaMemcpyDeviceToDevice, s));
     }
   }
-  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_ops, dec->ops.data(), dec->ops.size() * sizeof(Op), cudaMemcpyHostToDevice, s));
+  {
+    dec->recs.assign(dec->ops.size(), OpRec{});
+    for (size_t i = 0; i < dec->ops.size(); ++i) {
+      std::memset(&dec->recs[i], 0, sizeof(OpRec));
+      dec->recs[i].op = dec->ops[i];
+      if (dec->ops[i].layer >= 0) dec->recs[i].layer = dec->layers[dec->ops[i].layer];
+    }
+    IVB_CUDA(cudaMemcpyAsync(ws + dec->off_ops, dec->recs.data(), dec->recs.size() * sizeof(OpRec), cudaMemcpyHostToDevice, s));
+  }
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_op_rows, dec->op_rows.data(), dec->op_rows.size() * 4, cudaMemcpyHostToDevice, s));
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_off, dec->chunk_off.data(), dec->chunk_off.size() * 8, cudaMemcpyHostToDevice, s));
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_bytes, dec->chunk_bytes.data(), dec->chunk_bytes.size() * 4, cudaMemcpyHostToDevice, s));
@@ -1391,7 +1436,7 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   if (feed == nullptr && !(flags & IVB_RUN_SAMPLE))
     return fail(IVB_EINVAL, "ivb_decoder_run: without fed tokens every step must sample");
   ClusterParams p{};
-  p.ops = reinterpret_cast<const Op*>(ws + dec->off_ops);
+  p.ops = reinterpret_cast<const OpRec*>(ws + dec->off_ops);
   p.op_rows = reinterpret_cast<const int32_t*>(ws + dec->off_op_rows);
   p.n_ops = static_cast<int32_t>(dec->ops.size());
   p.kc = dec->kc;
