@@ -143,6 +143,17 @@ int32_t ivb_ternary_group_dots(const IvbTernary* m, const int8_t* q8, int32_t* d
 int32_t ivb_ternary_gemv(const IvbTernary* m, const float* x, const float* norm_weight, float norm_eps,
                          float norm_clip, float act_eps, int32_t epilogue, float* out, void* stream);
 
+/* Split-K variant of ivb_ternary_gemv (same arguments, same results within fp32 rounding): the input
+ * columns are spread over more CTAs and their partial row sums are added in a static device scratch.
+ * It has no counterpart in the reference. It allocates nothing: the scratch is a file-scope
+ * __device__ array of 32768 fp32 row sums (rows > 32768 or in_features > 16384 return IVB_EINVAL);
+ * its address is looked up once per device with cudaGetSymbolAddress on the first call with that
+ * device current, so make the first call on each device outside any stream capture. Each call clears
+ * the partial sums with a memset before accumulating. Calls that overlap in time on one device (other
+ * streams or threads) share the scratch and race: serialise them. */
+int32_t ivb_ternary_gemv_splitk(const IvbTernary* m, const float* x, const float* norm_weight, float norm_eps,
+                                float norm_clip, float act_eps, int32_t epilogue, float* out, void* stream);
+
 /* Sampler over one logits row: temperature, repetition penalty, exact top-k, softmax and an
  * inverse-CDF draw with a Philox4x32-10 uniform (key rng[0], counter rng[1]++).
  * Replaces ternary.cu:1064-1337 logit_bounds + sample_token. token/history: int64 [1] each. */
