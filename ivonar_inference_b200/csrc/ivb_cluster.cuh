@@ -18,7 +18,7 @@
 namespace ivb {
 
 constexpr int kMaxCluster = 16;
-constexpr int kStages = 4;
+constexpr int kStages = 3;
 
 enum OpKind : int32_t { OP_ENTRY_MAMBA = 0, OP_ENTRY_MLA = 1, OP_ATTN = 2, OP_OUT = 3, OP_GATE_UP = 4, OP_DOWN = 5, OP_HEAD = 6 };
 enum Gather : int32_t { G_NONE = 0, G_RESID = 1, G_VEC = 2, G_LATENT = 3 };
@@ -165,8 +165,7 @@ __device__ __forceinline__ void stream_issue(const ClusterParams& p, Stream& s, 
   const unsigned bytes = s.cbytes[s.p_chunk];
   const int stage = s.issued % kStages;
   unsigned long long* bar = s.full + stage;
-  fence_proxy_async();
-  mbar_expect_tx(bar, bytes);
+  mbar_expect_tx(bar, bytes);  // the stage is only ever written by the copy engine: no proxy fence
   bulk_copy(s.ring + static_cast<size_t>(stage) * s.stage_bytes, p.stream + s.coff[s.p_chunk], bytes, bar);
   ++s.issued;
   if (++s.p_chunk == p.chunks_per_token) {
