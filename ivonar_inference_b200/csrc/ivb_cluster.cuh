@@ -4,7 +4,7 @@
 // runs the whole token loop. Activations move between CTAs through distributed shared memory: each
 // CTA publishes its slice of a vector in its own shared memory, a hardware cluster barrier orders
 // the exchange, and consumers read every slice with ld.shared::cluster. Weights reach the CTAs as a
-// per-CTA linear stream (laid out once at bind time): a 4-stage ring of cp.async.bulk copies fed
+// per-CTA linear stream (laid out once at bind time): a 3-stage ring of cp.async.bulk copies fed
 // ahead of use, each stage completing on an mbarrier. Per block the critical path is
 //   mamba: [norm+quant -> entry rows of my heads -> SSM step] | out | gate/up | down
 //   mla:   [norm+quant -> entry rows (q, k_rope of my heads, my latent rows)] | attention | out | gate/up | down
@@ -22,6 +22,8 @@ constexpr int kStages = 3;
 
 enum OpKind : int32_t { OP_ENTRY_MAMBA = 0, OP_ENTRY_MLA = 1, OP_ATTN = 2, OP_OUT = 3, OP_GATE_UP = 4, OP_DOWN = 5, OP_HEAD = 6 };
 enum Gather : int32_t { G_NONE = 0, G_RESID = 1, G_VEC = 2, G_LATENT = 3 };
+// Buffers that other CTAs fill with st.async pushes; each has a transaction-count mbarrier.
+enum XBuf : int32_t { XB_RESID = 0, XB_VEC = 1, XB_LATENT = 2, XB_CAND = 3, XB_COUNT = 4, XB_NONE = -1 };
 
 // One step of the per-token program; identical for every CTA of the cluster.
 struct Op {
@@ -31,6 +33,8 @@ struct Op {
   int32_t gather;                  // what is gathered from the cluster before the op runs
   int32_t gather_n, gather_per;    // input vector length and per-CTA slice length of its producer
   int32_t push_per;                // entry of an mla block: latent rows per CTA (output slice stride)
+  int32_t in_buf;                  // input buffer filled by the previous op's pushes (XB_*), or XB_NONE
+  int32_t in_bytes;                // bytes of that fill (all producers together)
   int32_t in_n;                    // GEMV input length
   int32_t rows_per, rows_total;    // uniform row partition across the cluster
   int32_t chunk_rows;              // rows per stream chunk
@@ -66,6 +70,7 @@ struct ClusterSmem {
   int32_t ring, stage_bytes;
   int32_t xv, act, xsum, resid, pub, pub_n, loc, red, xl;
   int32_t ctab;                    // chunk table of the CTA: [cpt] u64 offsets, then [cpt] u32 sizes
+  int32_t cand;                    // offset inside the union region of the merge arrays (keys, ids) the head pushes into
   int32_t rope_row;                // rope (cos, sin) row of the current position, prefetched by the mla entry op
   int32_t seen;                    // the CTA's slice of the repetition flags, prefetched by the head op
   int32_t u;                       // union region (attention / sampler)
@@ -131,6 +136,16 @@ __device__ __forceinline__ void st_cluster_f32(unsigned addr, float v) {
 }
 __device__ __forceinline__ void st_cluster_v4(unsigned addr, float4 v) {
   asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+               : "memory");
+}
+// st.async into another CTA's shared memory; the bytes complete a transaction on that CTA's mbarrier.
+__device__ __forceinline__ void st_async_v4(unsigned addr, float4 v, unsigned mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
+               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(mbar)
+               : "memory");
+}
+__device__ __forceinline__ void st_async_b32(unsigned addr, unsigned v, unsigned mbar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v), "r"(mbar)
                : "memory");
 }
 __device__ __forceinline__ void atom_min_cluster_u32(unsigned addr, unsigned v) {

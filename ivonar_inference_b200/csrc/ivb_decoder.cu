@@ -24,13 +24,6 @@ int ivb_lpr_log(int in_features);
 
 namespace ivb {
 
-// Thread 0 of a failing CTA: record the code and tell every CTA of the cluster to stop after cluster
-// barrier number `stop_at` (the next one). The flag keeps the minimum, so every CTA stops at the same
-// barrier even when several fail at different times; no CTA is left waiting on a barrier alone.
-__device__ __forceinline__ void raise_error(const ClusterParams& p, unsigned* err_flag, unsigned code, unsigned stop_at) {
-  atomicCAS(p.error, 0u, code);
-  for (int r = 0; r < p.d.R; ++r) atom_min_cluster_u32(map_rank(err_flag, r), stop_at);
-}
 
 // floats of the recurrent constants copied out of the constants chunk: decay, theta, skip, conv w/b
 __host__ __device__ __forceinline__ int ssm_const_floats(int nh, int S, int hd, int taps) {
@@ -68,21 +61,21 @@ __device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
   f[3] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7443)) - 8388736.0f;
 }
 
-// Store v at dst[i] in the shared memory of every CTA of the cluster (the next op's input vector is
-// replicated; the cluster barrier after the op makes the stores visible).
 // All threads: copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n)
-// in every CTA of the cluster; one (slice, rank) pair per thread, 16-byte stores when aligned.
-__device__ __forceinline__ void push_vec(float* dst, int base, const float* src, int n, int R) {
+// in every CTA of the cluster with st.async; each store completes its bytes on that CTA's mbarrier
+// `bar` (the consumer arms it with the size of the whole fill and waits). One (slice, rank) pair per
+// thread, 16-byte stores when aligned.
+__device__ __forceinline__ void push_async(float* dst, int base, const float* src, int n, int R, unsigned long long* bar) {
   if (((base | n) & 3) == 0) {
     const int n4 = n >> 2;
     for (int idx = threadIdx.x; idx < n4 * R; idx += kThreads) {
       const int r = idx / n4, i = idx - r * n4;
-      st_cluster_v4(map_rank(dst + base + 4 * i, r), reinterpret_cast<const float4*>(src)[i]);
+      st_async_v4(map_rank(dst + base + 4 * i, r), reinterpret_cast<const float4*>(src)[i], map_rank(bar, r));
     }
   } else {
     for (int idx = threadIdx.x; idx < n * R; idx += kThreads) {
       const int r = idx / n, i = idx - r * n;
-      st_cluster_f32(map_rank(dst + base + i, r), src[i]);
+      st_async_b32(map_rank(dst + base + i, r), __float_as_uint(src[i]), map_rank(bar, r));
     }
   }
 }
@@ -158,7 +151,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long full[kStages];
   __shared__ __align__(8) unsigned long long abar[2];
-  __shared__ unsigned err_flag;  // cluster barrier number after which every CTA stops (~0u: none)
+  __shared__ __align__(8) unsigned long long xbar[XB_COUNT];  // fills of the pushed buffers (transaction counts)
   __shared__ __align__(16) OpRec opbuf[2];  // the running op and the next one (descriptor + layer)
   __shared__ __align__(16) int rowsbuf[2][4];
   const unsigned rank = cluster_rank();
@@ -179,8 +172,8 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
     mbar_init(&abar[0], 1);
     mbar_init(&abar[1], 1);
+    for (int b = 0; b < XB_COUNT; ++b) mbar_init(&xbar[b], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    err_flag = 0xffffffffu;
   }
   unsigned long long* coff = reinterpret_cast<unsigned long long*>(smem + M.ctab);
   unsigned* cbytes = reinterpret_cast<unsigned*>(coff + p.chunks_per_token);
@@ -224,15 +217,23 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
   }
   bool alive = true;
-  unsigned nbar = 0;  // cluster barriers passed in this run
-  auto sync_ok = [&]() -> bool {
-    cluster_sync();
-    ++nbar;
-    return *reinterpret_cast<volatile unsigned*>(&err_flag) > nbar;
+  // Ops hand their outputs to the next op through pushed buffers: the consumer arms the buffer's
+  // mbarrier with the bytes of the whole fill (arrive + expect_tx) and waits (bounded); the
+  // producers' st.async stores complete those bytes. No cluster barrier per op: a CTA starts an op as
+  // soon as its input has landed. A CTA is never more than one op ahead of another (every op needs
+  // every CTA's output of the previous one), and every op reads its input buffer before it pushes, so
+  // a fill never overwrites a buffer that is still being read.
+  unsigned xph[XB_COUNT] = {0u, 0u, 0u, 0u};
+  auto wait_fill = [&](int b, unsigned bytes) -> bool {
+    if (tid == 0) mbar_expect_tx(&xbar[b], bytes);
+    const bool late = !mbar_wait_bounded(&xbar[b], xph[b], p.timeout_ns);
+    xph[b] ^= 1u;
+    return !__syncthreads_or(late);
   };
   auto fail_here = [&](unsigned code) {
-    if (tid == 0) raise_error(p, &err_flag, code, nbar + 1);
+    if (tid == 0) atomicCAS(p.error, 0u, code);
   };
+  bool resid_pending = false;  // the last op of the previous token pushed the residual without a head
   for (int step = 0; step < p.steps && alive; ++step) {
     if (step > 0 && p.feed != nullptr) tok = ldcg_i64(p.feed + step);
     if (pos < 0 || pos >= D.max_len || tok < 0 || tok >= D.vocab) {
@@ -242,6 +243,13 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     }
     const bool head = head_needed(p, step);
     const bool tracing = p.trace != nullptr && step == p.trace_step;
+    if (resid_pending) {
+      resid_pending = false;
+      if (!wait_fill(XB_RESID, static_cast<unsigned>(D.hidden) * 4u)) {
+        fail_here(IVB_ETIMEOUT);
+        break;
+      }
+    }
     // embedding of the token -> residual replica (every CTA computes the whole row)
     {
       const uint8_t* erow = p.head.packed + static_cast<size_t>(tok) * p.head.row_bytes;
@@ -272,6 +280,11 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
       };
       const int lo = min(op.rows_total, static_cast<int>(rank) * op.rows_per);
       bool ok = true;
+      if (op.in_buf >= 0 && !wait_fill(op.in_buf, static_cast<unsigned>(op.in_bytes))) {
+        fail_here(IVB_ETIMEOUT);
+        alive = false;
+        break;
+      }
       if (op.kind == OP_ATTN) {
         // ---------------- latent attention over the compressed cache ----------------
         const IvbLayerDesc& L = lay;
@@ -546,7 +559,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
           __syncthreads();
           tick(3);
         }
-        if (ok) push_vec(xv, first_head * D.head_dim, stg, nh * D.head_dim, R);  // stg written before the head loop's last sync
+        if (ok) push_async(xv, first_head * D.head_dim, stg, nh * D.head_dim, R, &xbar[XB_VEC]);  // stg written before the head loop's last sync
         asm volatile("fence.proxy.async.global;" ::: "memory");
         if (!ok) fail_here(IVB_ETIMEOUT);
         stream_release(p, st, rank);
@@ -636,17 +649,17 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         if (op.kind == OP_OUT || op.kind == OP_DOWN) {
           for (int r = tid; r < rows_c; r += kThreads) stg[r] = resid[lo + r] + rows_out[r];
           __syncthreads();
-          push_vec(resid, lo, stg, rows_c, R);
+          push_async(resid, lo, stg, rows_c, R, &xbar[XB_RESID]);
         } else if (op.kind == OP_GATE_UP) {
           for (int m = tid; m < rows_c / 2; m += kThreads) stg[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
           __syncthreads();
-          push_vec(xv, lo / 2, stg, rows_c / 2, R);
+          push_async(xv, lo / 2, stg, rows_c / 2, R, &xbar[XB_VEC]);
         } else if (op.kind == OP_ENTRY_MLA) {
           const int lat0 = nh * (D.head_dim + D.rope);
           const int l0 = static_cast<int>(rank) * op.push_per;  // first latent row of this CTA
           for (int r = tid; r < rows_c - lat0; r += kThreads) stg[r] = rows_out[lat0 + r];
           __syncthreads();
-          push_vec(xl, l0, stg, rows_c - lat0, R);
+          push_async(xl, l0, stg, rows_c - lat0, R, &xbar[XB_LATENT]);
         } else if (op.kind == OP_HEAD) {
           for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
         } else if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
@@ -729,15 +742,19 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             stg[cl] = y;
           }
           __syncthreads();
-          push_vec(xv, first_head * hd, stg, channels, R);
+          push_async(xv, first_head * hd, stg, channels, R, &xbar[XB_VEC]);
         }
         if (!ok) fail_here(IVB_ETIMEOUT);
         // the head ends the token: local top-k of my vocabulary slice for the sampler
         if (op.kind == OP_HEAD && sampling) {
+          // head scratch at U: keys [rows_per] | ck, ci, out keys, out ids [kc] | histogram | misc;
+          // the merge arrays that the other CTAs push into start at U + M.cand (disjoint)
           unsigned* keys = reinterpret_cast<unsigned*>(U);
           unsigned* ck = keys + op.rows_per;
           int* ci = reinterpret_cast<int*>(ck + p.kc);
-          TopkScratch ts{reinterpret_cast<unsigned*>(ci + p.kc), reinterpret_cast<int*>(ci + p.kc) + kWarps * 256};
+          unsigned* ok_key = reinterpret_cast<unsigned*>(ci + p.kc);
+          int* ok_id = reinterpret_cast<int*>(ok_key + p.kc);
+          TopkScratch ts{reinterpret_cast<unsigned*>(ok_id + p.kc), reinterpret_cast<int*>(ok_id + p.kc) + kWarps * 256};
           cp_async_wait_all();
           __syncthreads();
           const uint8_t* seen_b = reinterpret_cast<const uint8_t*>(seen_s);
@@ -746,10 +763,20 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
             keys[r] = score_key(rows_out[r], pref ? seen_b[r] : __ldcg(p.seen + lo + r), inv_t, pen, ipen);
           __syncthreads();
           const int kl = min(K, rows_c);
-          if (kl > 0)
-            topk_sorted(keys, nullptr, lo, rows_c, kl, ts, ck, ci, p.cand_key + static_cast<size_t>(rank) * p.kc,
-                        p.cand_id + static_cast<size_t>(rank) * p.kc);
-          if (tid == 0) p.cand_n[rank] = kl;
+          if (kl > 0) topk_sorted(keys, nullptr, lo, rows_c, kl, ts, ck, ci, ok_key, ok_id);
+          __syncthreads();
+          // my candidates go to offset sum_{r < rank} min(K, rows of r) of every CTA's merge arrays
+          int base = 0;
+          for (int r = 0; r < static_cast<int>(rank); ++r)
+            base += min(K, max(0, min(op.rows_total - r * op.rows_per, op.rows_per)));
+          unsigned* mk = reinterpret_cast<unsigned*>(U + M.cand);
+          int* mi = reinterpret_cast<int*>(mk + R * p.kc);
+          for (int idx = tid; idx < kl * R; idx += kThreads) {
+            const int r = idx / kl, c = idx - r * kl;
+            const unsigned bar = map_rank(&xbar[XB_CAND], r);
+            st_async_b32(map_rank(mk + base + c, r), ok_key[c], bar);
+            st_async_b32(map_rank(mi + base + c, r), static_cast<unsigned>(ok_id[c]), bar);
+          }
         }
       }
       tick(5);
@@ -758,33 +785,32 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
       mark(marks, 7);
       cp_async_wait_all();  // the next descriptor has landed
       ++opk;
-      if (!sync_ok()) {
+      __syncthreads();      // local buffers (rows, codes, staging) are reused by the next op
+      if (!ok) {
         alive = false;
         break;
       }
     }
     if (!alive) break;
+    if (!head) resid_pending = true;
     if (sampling) {
-      // every CTA merges the cluster's candidates and draws the same token
+      // every CTA merges the cluster's candidates (pushed into its merge arrays) and draws the same token
       const int kc = p.kc;
-      unsigned* mk = reinterpret_cast<unsigned*>(U);
+      const Op& hop = opbuf[(opk + 1) & 1].op;  // the head op just run (the slot before the current one)
+      unsigned* mk = reinterpret_cast<unsigned*>(U + M.cand);
       int* mi = reinterpret_cast<int*>(mk + R * kc);
-      unsigned* ck = reinterpret_cast<unsigned*>(mi + R * kc);
+      unsigned* ck = reinterpret_cast<unsigned*>(U);
       int* ci = reinterpret_cast<int*>(ck + kc);
       unsigned* sk = reinterpret_cast<unsigned*>(ci + kc);
       int* si = reinterpret_cast<int*>(sk + kc);
       float* cdf = reinterpret_cast<float*>(si + kc);
       TopkScratch ts{reinterpret_cast<unsigned*>(cdf + kc), reinterpret_cast<int*>(cdf + kc) + kWarps * 256};
       int n = 0;
-      for (int r = 0; r < R; ++r) {
-        const int cn = __ldcg(p.cand_n + r);
-        for (int c = tid; c < cn; c += kThreads) {
-          mk[n + c] = __ldcg(p.cand_key + static_cast<size_t>(r) * kc + c);
-          mi[n + c] = __ldcg(p.cand_id + static_cast<size_t>(r) * kc + c);
-        }
-        n += cn;
+      for (int r = 0; r < R; ++r) n += min(K, max(0, min(hop.rows_total - r * hop.rows_per, hop.rows_per)));
+      if (!wait_fill(XB_CAND, static_cast<unsigned>(n) * 8u)) {
+        fail_here(IVB_ETIMEOUT);
+        break;
       }
-      __syncthreads();
       const int kk = min(K, n);
       topk_sorted(mk, mi, 0, n, kk, ts, ck, ci, sk, si);
       const int chosen = draw_token(sk, si, kk, cdf, red, rkey, rctr);
@@ -803,7 +829,9 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
     ++pos;
     if (rank == 0 && tid == 0) p.position[0] = pos;
   }
-  // let every in-flight copy land before the CTA's shared memory goes away
+  // let every in-flight copy land before the CTA's shared memory goes away: a residual fill nobody
+  // consumed (the run stopped after a step without a head), the descriptor prefetch, the ring
+  if (resid_pending) wait_fill(XB_RESID, static_cast<unsigned>(D.hidden) * 4u);
   cp_async_wait_all();
   if (tid == 0) {
     while (st.consumed < st.issued) {
@@ -1123,7 +1151,39 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   for (size_t i = 0; i < plans.size(); ++i) {
     plans[i].op.first_chunk = cpt;
     cpt += plans[i].op.n_chunks;
-    dec->ops.push_back(plans[i].op);
+    // the buffer this op waits for (filled by the previous op's pushes) and the bytes of that fill
+    Op& op = plans[i].op;
+    op.in_buf = XB_NONE;
+    op.in_bytes = 0;
+    switch (op.kind) {
+      case OP_ENTRY_MAMBA:
+      case OP_ENTRY_MLA:
+        if (op.layer > 0) {
+          op.in_buf = XB_RESID;
+          op.in_bytes = d * 4;
+        }
+        break;
+      case OP_GATE_UP:
+      case OP_HEAD:
+        op.in_buf = XB_RESID;
+        op.in_bytes = d * 4;
+        break;
+      case OP_ATTN:
+        op.in_buf = XB_LATENT;
+        op.in_bytes = Lt * 4;
+        break;
+      case OP_OUT:
+        op.in_buf = XB_VEC;
+        op.in_bytes = H * hd * 4;
+        break;
+      case OP_DOWN:
+        op.in_buf = XB_VEC;
+        op.in_bytes = F * 4;
+        break;
+      default:
+        break;
+    }
+    dec->ops.push_back(op);
   }
   dec->cpt = cpt;
   dec->head_first = plans.back().op.first_chunk;
@@ -1261,8 +1321,12 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   // recurrent op: constants, coefficients, values, partial readouts, prefetched state
   size_t u_need = r16((static_cast<size_t>(ssm_const_floats(hpc, S, hd, D.taps)) + 5 * hpc * S + hpc * hd + std::max(kThreads, hpc * hd) +
                        3 * static_cast<size_t>(hpc) * S * hd + static_cast<size_t>(hpc) * hd * (D.taps - 1)) * 4);
-  u_need = std::max(u_need, r16(static_cast<size_t>(Vper) * 4) + 2 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
-  u_need = std::max(u_need, 2 * r16(static_cast<size_t>(R) * kc * 4) + 5 * r16(kc * 4) + kWarps * 256 * 4 + 64 * 4);
+  // head + sampler: the head's top-k scratch (or the merge scratch) first, then the merge arrays that
+  // the other CTAs push their candidates into
+  const size_t head_scratch = static_cast<size_t>(Vper) * 4 + 4 * static_cast<size_t>(kc) * 4 + kWarps * 256 * 4 + 16 * 4;
+  const size_t merge_scratch = 5 * static_cast<size_t>(kc) * 4 + kWarps * 256 * 4 + 16 * 4;
+  M.cand = static_cast<int>(r16(std::max(head_scratch, merge_scratch)));
+  u_need = std::max(u_need, static_cast<size_t>(M.cand) + 2 * r16(static_cast<size_t>(R) * kc * 4));
   const size_t attn_fixed = r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4) + r16((Lt + 63) / 64 * 64) +
                             static_cast<size_t>(Lt + 2 * D.rope + D.nope) * 4 + kWarps * Lt * 4 + 64;
   const size_t per_pos = static_cast<size_t>(D.lpad) + 4 + static_cast<size_t>(D.rpad) * 2;
