@@ -200,6 +200,16 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
  * records the globaltimer (ns) of step `step`, per phase and CTA: [0] work start, [1..6] marks inside
  * the phase (0 where a phase has fewer), [7] work end before the phase's barrier. NULL turns it off. */
 int32_t ivb_decoder_trace(IvbDecoder* dec, uint64_t* buffer, int32_t step);
+/* Device workspace (bytes) for one ivb_decoder_prefill call of up to max_tokens tokens. */
+uint64_t ivb_decoder_prefill_workspace_bytes(const IvbDecoder* dec, int32_t max_tokens);
+/* Prompt prefill with all `count` tokens per layer at once: device int64 tokens [count] at positions
+ * start_position.. (tcgen05 GEMMs for every projection, recurrent scan over the tokens, latent/k_rope
+ * cache fill and causal latent attention), then the head of the last token into logits; leaves caches,
+ * recurrent state, position and token where token-by-token decoding would. Chunked prompts: call again
+ * with the next tokens and start_position advanced (the recurrent state carries over). Asynchronous.
+ * Replaces kernel_decoder.py:457-479 prefill and ternary.cu:688-982 (tile GEMM/recurrence/attention). */
+int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t count, int32_t start_position, void* workspace,
+                            uint64_t workspace_bytes, void* stream);
 /* Synchronises the stream and returns IVB_ETIMEOUT/IVB_ECAPACITY if the device error word is set. */
 int32_t ivb_decoder_check(IvbDecoder* dec, void* stream);
 

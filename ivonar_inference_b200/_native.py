@@ -125,6 +125,8 @@ SIGNATURES = {
     "ivb_decoder_bind": (c_int32, [c_void_p, c_void_p, c_void_p]),
     "ivb_decoder_run": (c_int32, [c_void_p, c_int32, c_void_p, c_int32, c_uint64, c_void_p]),
     "ivb_decoder_trace": (c_int32, [c_void_p, c_void_p, c_int32]),
+    "ivb_decoder_prefill_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
+    "ivb_decoder_prefill": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_uint64, c_void_p]),
     "ivb_decoder_check": (c_int32, [c_void_p, c_void_p]),
 }
 

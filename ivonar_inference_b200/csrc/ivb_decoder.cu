@@ -40,27 +40,6 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 constexpr int kAttnPieces = 4;
 
-// The 16 two-bit codes of a packed word (input 4b + f in bits 8b + 2f) as exact floats code - 1.
-__device__ __forceinline__ void word_codes_m1(unsigned w, float* cm1) {
-#pragma unroll
-  for (int f = 0; f < 4; ++f) {
-    const unsigned m = (w >> (2 * f)) & 0x03030303u;
-#pragma unroll
-    for (int b = 0; b < 4; ++b)
-      cm1[4 * b + f] = __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7440 | b)) - 8388609.0f;
-  }
-}  // 128-wide latent pieces per attention lane (latent <= 512)
-
-// Four signed bytes to exact floats without the conversion unit: biased byte b + 128 placed in the
-// low mantissa bits of 2^23, then 2^23 + 128 subtracted (exact for every byte value).
-__device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
-  const unsigned b = w ^ 0x80808080u;
-  f[0] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440)) - 8388736.0f;
-  f[1] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7441)) - 8388736.0f;
-  f[2] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7442)) - 8388736.0f;
-  f[3] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7443)) - 8388736.0f;
-}
-
 // All threads: copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n)
 // in every CTA of the cluster with st.async; each store completes its bytes on that CTA's mbarrier
 // `bar` (the consumer arms it with the size of the whole fill and waits). One (slice, rank) pair per
@@ -1356,6 +1335,18 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   return true;
 }
 
+}  // namespace ivb
+
+namespace ivb {
+// The model description and layers a decoder was created with (for the prefill path).
+const IvbModelDesc& decoder_model(const IvbDecoder* dec, const IvbLayerDesc** layers) {
+  *layers = dec->layers.data();
+  return dec->desc;
+}
+// The device error word ivb_decoder_check reports (nullptr before bind).
+unsigned* decoder_error_word(const IvbDecoder* dec) {
+  return dec->ws == nullptr ? nullptr : reinterpret_cast<unsigned*>(dec->ws + dec->off_sync);
+}
 }  // namespace ivb
 
 extern "C" {

@@ -201,6 +201,27 @@ __device__ __forceinline__ int quant_code(float v, float scale, float rscale) {
   return near ? static_cast<int>(rintf(v / scale)) : q;
 }
 
+// The 16 two-bit codes of a packed word (input 4b + f in bits 8b + 2f) as exact floats code - 1.
+__device__ __forceinline__ void word_codes_m1(unsigned w, float* cm1) {
+#pragma unroll
+  for (int f = 0; f < 4; ++f) {
+    const unsigned m = (w >> (2 * f)) & 0x03030303u;
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      cm1[4 * b + f] = __uint_as_float(__byte_perm(m, 0x4B000000u, 0x7440 | b)) - 8388609.0f;
+  }
+}
+
+// Four signed bytes to exact floats without the conversion unit: biased byte b + 128 placed in the
+// low mantissa bits of 2^23, then 2^23 + 128 subtracted (exact for every byte value).
+__device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
+  const unsigned b = w ^ 0x80808080u;
+  f[0] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7440)) - 8388736.0f;
+  f[1] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7441)) - 8388736.0f;
+  f[2] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7442)) - 8388736.0f;
+  f[3] = __uint_as_float(__byte_perm(b, 0x4B000000u, 0x7443)) - 8388736.0f;
+}
+
 // ------------------------------------------------------------------------------------------------
 // Canonical per-token int8 quantiser (optionally with RMSNorm: clamp(x * inv_rms, +-clip) * w).
 // src holds the fp32 input (n values, shared). For the sum of squares lane t < 256 owns inputs

@@ -79,7 +79,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) ternary_gemm_kernel(const Ivb
   float* scl = reinterpret_cast<float*>(smem + 2 * kGemmTile);  // [128] group scales of the tile's rows
   __shared__ __align__(8) unsigned long long mma_bar;
   __shared__ unsigned tmem_base;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int tid = threadIdx.x, warp = tid >> 5;
   const int r0 = blockIdx.x * kGemmN, t0 = blockIdx.y * kGemmM;
   const int groups = (m.in_features + 127) >> 7;
   if (warp == 0) {

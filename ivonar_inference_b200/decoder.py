@@ -31,6 +31,7 @@ from .model import rope_table
 BURST = 16
 SELF_CHECK_TOLERANCE = 0.25
 DEFAULT_TIMEOUT_NS = 2_000_000_000
+PREFILL_CHUNK = 1024  # prompt tokens per tensor-core prefill call (workspace grows with it)
 
 
 def _pad_rows(packed: Tensor) -> Tensor:
@@ -100,6 +101,8 @@ class B200Decoder:
         ctas: int = 0,
         seed: int | None = None,
         timeout_ns: int = DEFAULT_TIMEOUT_NS,
+        prefill: str = "gemm",
+        prefill_chunk: int = PREFILL_CHUNK,
     ) -> None:
         target = model.device if device is None else torch.device(device)
         if target.type != "cuda":
@@ -110,6 +113,11 @@ class B200Decoder:
             raise ValueError("max_top_k must be positive")
         self.lib = native.library()
         self.model = model
+        if prefill not in ("gemm", "steps"):
+            raise ValueError("prefill must be 'gemm' (tensor-core prefill) or 'steps' (token by token)")
+        self.prefill_mode = prefill
+        self.prefill_chunk = max(1, int(prefill_chunk))
+        self._prefill_ws: Tensor | None = None
         self.device = target
         config = model.config
         self.max_len = int(config.seq_len if max_len is None else max_len)
@@ -368,10 +376,27 @@ class B200Decoder:
         self.position.zero_()
         self.host_position = 0
         self._feed = ids
-        self._launch(length, ids, 0)
+        if self.prefill_mode == "steps":
+            self._launch(length, ids, 0)
+        else:
+            self._prefill_gemm(ids)
         self._check()
         self.host_position = length
         return self.logits
+
+    def _prefill_gemm(self, ids: Tensor) -> None:
+        """All prompt tokens per layer at once (tcgen05 GEMMs), in chunks of prefill_chunk tokens."""
+
+        chunk = min(self.prefill_chunk, self.max_len)
+        with torch.cuda.device(self.device):
+            nbytes = int(self.lib.ivb_decoder_prefill_workspace_bytes(self._plan, chunk))
+            if self._prefill_ws is None or self._prefill_ws.numel() < nbytes:
+                self._prefill_ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            for start in range(0, int(ids.numel()), chunk):
+                part = ids[start:start + chunk]
+                rc = self.lib.ivb_decoder_prefill(self._plan, part.data_ptr(), int(part.numel()), start,
+                                                  self._prefill_ws.data_ptr(), self._prefill_ws.numel(), self._stream())
+                native.check(rc, "ivb_decoder_prefill")
 
     @torch.no_grad()
     def step(self, token: Tensor) -> Tensor:
