@@ -107,6 +107,111 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_kernel(IvbLayerDesc L, cons
     for (int k = 0; k < taps - 1; ++k) L.conv_state[static_cast<size_t>(cc_) * (taps - 1) + k] = win[k];
 }
 
+// Convolution + SiLU of every (token, channel) of a mamba block, in parallel: value[t][c] from the entry
+// rows t - taps + 1 .. t (the block's conv window before the chunk for the first tokens).
+__global__ void __launch_bounds__(kThreads) ssm_value_kernel(IvbLayerDesc L, const float* ent, int T, int d, int ld, int taps,
+                                                             float* value) {
+  const int i = blockIdx.x * kThreads + threadIdx.x;
+  if (i >= T * d) return;
+  const int t = i / d, c = i - t * d;
+  float conv = L.conv_bias[c];
+  for (int k2 = 0; k2 < taps; ++k2) {
+    const int src = t - (taps - 1) + k2;  // token index of tap k2 (negative: the stored window)
+    const float x = src >= 0 ? ent[static_cast<size_t>(src) * ld + c] : L.conv_state[static_cast<size_t>(c) * (taps - 1) + (taps - 1 + src)];
+    conv = fmaf(L.conv_weight[c * taps + k2], x, conv);
+  }
+  value[i] = silu_f(conv);
+}
+
+// Recurrent scan over the tokens with the per-(token, head, state) coefficients computed cooperatively
+// for blocks of 32 tokens into shared memory. CTA: 16 channels x 16 state lanes (lane s of a channel's
+// half-warp owns state s). The conv window of the block is advanced at the end. Same arithmetic per
+// step as the decode kernel.
+constexpr int kScanBlock = 32;
+__global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L, const float* ent, const float* value, int T,
+                                                                  int d, int H, int hd, int S, int taps, float half_dt_min,
+                                                                  float half_dt_range, float* y) {
+  extern __shared__ float sh[];
+  const int tid = threadIdx.x, sub = tid & 15, chl = tid >> 4;
+  const int c0 = blockIdx.x * 16, c = c0 + chl;
+  const bool live = c < d;
+  const int h0 = c0 / hd, nhc = (min(d, c0 + 16) - 1) / hd - h0 + 1;  // heads spanned by the CTA's channels
+  float* coef = sh;                                   // [kScanBlock][nhc][S][5]
+  float* vals = coef + kScanBlock * nhc * S * 5;      // [kScanBlock][16]
+  float* gates = vals + kScanBlock * 16;              // [kScanBlock][16]
+  const int ld = 2 * d + 3 * H * S;
+  const int h = live ? c / hd : h0, dd = live ? c - h * hd : 0;
+  const bool on = live && sub < S;
+  const int s = on ? sub : 0;
+  const size_t si_idx = (static_cast<size_t>(h) * S + s) * hd + dd;
+  float sr = on ? L.ssm_state[2 * si_idx] : 0.0f, si = on ? L.ssm_state[2 * si_idx + 1] : 0.0f;
+  float prev = on ? L.prev_force[si_idx] : 0.0f;
+  const float skip = live ? L.skip[c] : 0.0f;
+  for (int t0 = 0; t0 < T; t0 += kScanBlock) {
+    const int nt = min(kScanBlock, T - t0);
+    __syncthreads();
+    for (int idx = tid; idx < nt * nhc * S; idx += kThreads) {
+      const int tt = idx / (nhc * S), rest = idx - tt * (nhc * S), hl = rest / S, s2 = rest - hl * S;
+      const int hh = h0 + hl;
+      const float* bcdt = ent + static_cast<size_t>(t0 + tt) * ld + 2 * d + hh * 3 * S;
+      const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * half_dt_range;
+      const float mag = expf(2.0f * half_dt * L.decay[hh * S + s2]);
+      float sn, cs;
+      sincosf(2.0f * half_dt * L.theta[hh * S + s2], &sn, &cs);
+      float* cf = coef + (static_cast<size_t>(tt) * nhc * S + hl * S + s2) * 5;
+      cf[0] = tanhf(bcdt[s2]);
+      cf[1] = tanhf(bcdt[S + s2]);
+      cf[2] = half_dt;
+      cf[3] = mag * cs;
+      cf[4] = mag * sn;
+    }
+    for (int idx = tid; idx < nt * 16; idx += kThreads) {
+      const int tt = idx >> 4, ch = idx & 15;
+      const int cc2 = c0 + ch;
+      vals[idx] = cc2 < d ? value[static_cast<size_t>(t0 + tt) * d + cc2] : 0.0f;
+      gates[idx] = cc2 < d ? ent[static_cast<size_t>(t0 + tt) * ld + d + cc2] : 0.0f;
+    }
+    __syncthreads();
+    const int hl = h - h0;
+    for (int tt = 0; tt < nt; ++tt) {
+      const float v = vals[tt * 16 + chl];
+      float contrib = 0.0f;
+      if (on) {
+        const float* cf = coef + (static_cast<size_t>(tt) * nhc * S + hl * S + s) * 5;
+        const float b = cf[0], cc = cf[1], half_dt = cf[2], ar = cf[3], ai = cf[4];
+        const float force = b * v;
+        const float dr = (force + ar * prev) * half_dt;
+        const float di = (ai * prev) * half_dt;
+        const float nr = sr * ar - si * ai + dr;
+        const float ni = sr * ai + si * ar + di;
+        sr = nr;
+        si = ni;
+        prev = force;
+        contrib = cc * nr;
+      }
+#pragma unroll
+      for (int off = 8; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
+      if (live && sub == 0)
+        y[static_cast<size_t>(t0 + tt) * d + c] = (contrib + skip * v) * sigmoid_f(gates[tt * 16 + chl]);
+    }
+  }
+  if (on) {
+    L.ssm_state[2 * si_idx] = sr;
+    L.ssm_state[2 * si_idx + 1] = si;
+    L.prev_force[si_idx] = prev;
+  }
+  // the conv window after the last token: the last taps - 1 inputs (older window entries when T is short)
+  __syncthreads();
+  if (live && sub == 0) {
+    float w[kMaxTaps];
+    for (int k = 0; k < taps - 1; ++k) {
+      const int src = T - (taps - 1) + k;
+      w[k] = src >= 0 ? ent[static_cast<size_t>(src) * ld + c] : L.conv_state[static_cast<size_t>(c) * (taps - 1) + (taps - 1 + src)];
+    }
+    for (int k = 0; k < taps - 1; ++k) L.conv_state[static_cast<size_t>(c) * (taps - 1) + k] = w[k];
+  }
+}
+
 // Cache fill of one mla block for T tokens at positions pos0..: the quantised latent and the rotated,
 // fp16-rounded k_rope of every head. One CTA per token. ent [T][d + Lt + H*rope]: q | latent | k_rope.
 __global__ void __launch_bounds__(kThreads) mla_cache_kernel(IvbLayerDesc L, const float* ent, int pos0, int d, int Lt,
@@ -315,7 +420,7 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.resid = take(T * d * 4);
   L.ent = take(T * ld_ent * 4);
   L.y = take(T * d * 4);
-  L.h = take(T * F * 4);
+  L.h = take(T * std::max(F, d) * 4);  // also the mamba conv values [T][d]
   L.q8 = take(T * L.ldq);
   L.scale = take(T * 4);
   L.gsum = take(T * L.groups * 4);
@@ -382,7 +487,17 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
     const IvbLayerDesc& L = layers[li];
     if (int32_t rc = quant(resid, d, L.mixer_norm, L.mixer_norm_eps)) return rc;
     if (int32_t rc = gemm(L.entry, IVB_EPI_STORE, ent, L.entry.rows)) return rc;
-    if (L.kind == IVB_MAMBA) {
+    if (L.kind == IVB_MAMBA && hd >= 4) {
+      const int ld = 2 * d + 3 * H * S;
+      ssm_value_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, ld, L.conv_taps, hbuf);
+      IVB_CUDA(cudaGetLastError());
+      const int nhc_max = std::min(16, 15 / hd + 2);
+      const size_t smem = (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * 16) * 4;
+      IVB_CUDA(cudaFuncSetAttribute(ssm_scan_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+      ssm_scan_block_kernel<<<(d + 15) / 16, kThreads, smem, s>>>(L, ent, hbuf, count, d, H, hd, S, L.conv_taps, L.half_dt_min,
+                                                                   L.half_dt_range, y);
+      IVB_CUDA(cudaGetLastError());
+    } else if (L.kind == IVB_MAMBA) {
       const int blocks = (d * 16 + kThreads - 1) / kThreads;
       ssm_scan_kernel<<<blocks, kThreads, 0, s>>>(L, ent, count, d, H, hd, S, L.conv_taps, L.half_dt_min, L.half_dt_range, y);
       IVB_CUDA(cudaGetLastError());
