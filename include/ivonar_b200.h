@@ -144,19 +144,26 @@ int32_t ivb_ternary_gemv(const IvbTernary* m, const float* x, const float* norm_
                          float norm_clip, float act_eps, int32_t epilogue, float* out, void* stream);
 
 /* Prefill quantiser for `rows` token rows: x [rows][n] fp32 (RMSNorm first when norm_weight is given) ->
- * q8 [rows][ldq] int8 in the GEMM layout (within each 16-input block byte 4f+b holds input 4b+f; inputs
- * n..ldq-1 are zero), scale [rows], gsum [rows][ceil(n/128)] int32 sums of the codes per 128-input group.
- * ldq: a multiple of 16, at least n rounded up to 128. Replaces ternary.cu:637-668 quantize_tile_*. */
+ * q8 int8 in the tiled GEMM activation layout, scale [rows], and, when gsum is not NULL,
+ * gsum [rows][ceil(n/128)] int32 sums of the codes per 128-input group. ldq: a multiple of 128, at
+ * least n (inputs n..ldq-1 are written as zero).
+ * Tiled layout: one 16384-byte block per (token tile t/128, input group i/128) at
+ * ((t/128) * (ldq/128) + i/128) * 16384; inside it, the 16-input chunk k = (i%128)/16 of token row
+ * r = t%128 sits at (8*(r/8) + k) * 128 + (r%8) * 16, and within the chunk byte 4f+b holds input 4b+f.
+ * q8 must hold ceil(rows/128) * 128 * ldq bytes (16-byte aligned); the pad rows of the last tile are
+ * not written. Replaces ternary.cu:637-668 quantize_tile_*. */
 int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* norm_weight, float norm_eps,
                           float norm_clip, float act_eps, int8_t* q8, int32_t ldq, float* scale, int32_t* gsum,
                           void* stream);
 
-/* Prefill ternary GEMM on tcgen05 int8 MMA (TMEM accumulators), `rows_t` tokens at once:
- * out[t][r] = epilogue(scale[t] * sum_g s[r][g] * (sum_{k in g} code[r][k] * q8[t][k] - gsum[t][g]) + bias[r])
- * with q8/scale/gsum from ivb_quantize_rows; out row stride ldo (SILU_PAIR writes rows/2 outputs per token).
+/* Prefill ternary GEMM on tcgen05 int8 MMA (weights as signed codes in TMEM, activations from shared
+ * memory, TMEM accumulators), `rows_t` tokens at once:
+ * out[t][r] = epilogue(scale[t] * sum_g s[r][g] * (sum_{k in g} (code[r][k] - 1) * q8[t][k]) + bias[r])
+ * with q8 (tiled layout, same ldq)/scale from ivb_quantize_rows; out row stride ldo (SILU_PAIR writes
+ * rows/2 outputs per token). Uses all 512 TMEM columns of the SMs it runs on.
  * *error becomes IVB_ETIMEOUT if a bounded wait on the tensor core ran out. Replaces ternary.cu:688-783. */
-int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, const int32_t* gsum,
-                         int32_t rows_t, int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream);
+int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
+                         int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream);
 
 /* Split-K variant of ivb_ternary_gemv (same arguments, same results within fp32 rounding): the input
  * columns are spread over more CTAs and their partial row sums are added in a static device scratch.

@@ -1,25 +1,54 @@
 // Prefill ternary GEMM of libivonar_b200.so on the 5th-generation tensor cores (tcgen05, kind::i8).
 //
-// out[t][r] = epilogue(act_scale[t] * sum_g s[r][g] * (sum_{k in g} code[r][k] * q8[t][k] - gsum[t][g]) + bias[r])
-// for T token rows at once. codes are the 2-bit weights as unsigned bytes 0..2 (= ternary + 1), so the
-// per-group integer dot is exact in the int32 accumulator and the -1 offset is the group sum of the
-// activations. Reference: kernels/ternary.cu:688-765 gemm_tile_body (per-token int8 tiles, dp4a).
+// out[t][r] = epilogue(act_scale[t] * sum_g s[r][g] * (sum_{k in g} (code[r][k] - 1) * q8[t][k]) + bias[r])
+// for T token rows at once: the per-group integer dot is exact in the int32 accumulator, then scaled by
+// the fp16 group scale in fp32. Reference: kernels/ternary.cu:688-765 gemm_tile_body (per-token int8
+// tiles, dp4a), which subtracts the activation group sum instead of offsetting the codes.
 //
-// One CTA computes a 128-token x 128-row tile; per 128-input scale group it stages the activations
-// (already in the GEMM layout) and the unpacked weight codes in shared memory as K-major core matrices,
-// one thread issues four 128x128x32 int8 MMAs into a TMEM accumulator, and the four warps read it back
-// (tcgen05.ld), subtract the group sum, scale by the fp16 group scale and accumulate in fp32 registers.
+// One CTA computes a 128-row x 128-token tile. The weights are the MMA's A operand and live in tensor
+// memory: they never pass through shared memory as bytes. Warp-specialised roles per 128-input group g:
+//   * producer warps (4, one TMEM lane quarter each): producer 0 fetches the tile's packed weights of the
+//     group (128 rows x 32 bytes) with one TMA tensor load into a small packed ring and bulk-copies the
+//     group's 16 KB activation tile (core matrices, laid out by ivb_quantize_rows) into an operand stage;
+//     then every producer thread expands its row's 128 two-bit codes to signed bytes (code - 1) in
+//     registers and stores them into the group's A slot in TMEM (tcgen05.st, 32 columns);
+//   * one MMA thread: four 128x128x32 int8 MMAs (A from TMEM, B = activations from shared memory) into
+//     TMEM accumulator g % 3, committed to the stage's "empty" barrier and to the accumulator's "full"
+//     barrier;
+//   * epilogue warps (16; warp w reads TMEM lane quarter w % 4 = weight rows, columns 32 (w / 4).. =
+//     tokens): drain the accumulator (tcgen05.ld), scale by the row's group scale and accumulate in fp32
+//     registers, then re-arm it with the int32 0x4B400000. With that preload the accumulator holds the
+//     bit pattern of the float 12582912 + dot (exact while |dot| < 2^22), so the drain is one paired
+//     subtract and one paired multiply-add per two outputs instead of an integer conversion.
+// TMEM: 3 accumulators x 128 columns + 4 A slots x 32 columns = all 512 columns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+
+#include <algorithm>
+#include <mutex>
 
 #include "ivb_common.h"
 #include "ivb_cluster.cuh"
 
 namespace ivb {
 
-constexpr int kGemmM = 128;          // tokens per tile (TMEM lanes)
-constexpr int kGemmN = 128;          // weight rows per tile (TMEM columns)
-constexpr int kGemmThreads = 128;    // four warps: warp w owns TMEM lanes 32w..32w+31
-constexpr int kGemmTile = 16384;     // bytes of one 128 x 128 int8 operand tile
+constexpr int kGemmRows = 128;       // weight rows per tile (MMA M, TMEM lanes)
+constexpr int kGemmTok = 128;        // tokens per tile (MMA N, accumulator columns)
+constexpr int kGemmTile = 16384;     // bytes of one 128-token x 128-input activation tile
+constexpr int kGemmStages = 4;       // activation stages = TMEM A slots (groups in flight)
+constexpr int kGemmBufs = 3;         // TMEM accumulators of 128 columns
+constexpr int kGemmACol = kGemmBufs * kGemmTok;  // first TMEM column of the A slots (32 columns each)
+constexpr int kGemmEpiWarps = 16;    // warps 0-15: epilogue
+constexpr int kGemmEpiCols = 32;     // accumulator columns (tokens) per epilogue thread
+constexpr int kGemmMmaWarp = 16;     // warp 16: TMEM allocation and the MMA thread
+constexpr int kGemmProdWarps = 4;    // warps 17-20: producers (lane quarter = warp % 4)
+constexpr int kGemmProducers = 32 * kGemmProdWarps;
+constexpr int kGemmThreads = 32 * (kGemmEpiWarps + 1 + kGemmProdWarps);
+constexpr int kPackSlots = 4;                    // packed weight blocks in flight
+constexpr int kPackSlot = kGemmRows * 32;        // packed bytes of one group for the tile's 128 rows
+constexpr unsigned kGemmMagic = 0x4B400000u;     // bit pattern of 12582912.0f = 1.5 * 2^23
+constexpr float kGemmMagicF = 12582912.0f;
 
 // Position of input i inside the GEMM activation layout: each 16-input block is a 4 x 4 byte transpose
 // (byte 4f + b holds input 4b + f), which matches the codes a packed weight word yields by masking
@@ -28,22 +57,30 @@ __host__ __device__ __forceinline__ int gemm_slot(int i) { return (i & ~15) + ((
 
 // One 16-byte chunk (c) of row r in a K-major core-matrix tile: core matrices of 8 rows x 16 bytes,
 // 8 chunks (128 inputs) per row group. LBO (next K chunk) = 128 B, SBO (next 8-row group) = 1024 B.
-__device__ __forceinline__ int tile_off(int r, int c) { return (((r >> 3) << 3) + c) * 128 + ((r & 7) << 4); }
+__host__ __device__ __forceinline__ int tile_off(int r, int c) { return (((r >> 3) << 3) + c) * 128 + ((r & 7) << 4); }
+
+// Byte offset of (token t, 16-input chunk k) in the tiled activation buffer of row length ldq:
+// 16 KB blocks per (token tile, 128-input group), each a core-matrix tile.
+__host__ __device__ __forceinline__ size_t q8_chunk_offset(int t, int k, int ldq) {
+  return (static_cast<size_t>(t >> 7) * (ldq >> 7) + (k >> 3)) * kGemmTile + tile_off(t & 127, k & 7);
+}
 
 __device__ __forceinline__ uint64_t smem_desc(unsigned addr) {
   return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |
          (static_cast<uint64_t>(1024 >> 4) << 32) | (1ull << 46);
 }
 
-// kind::i8 instruction descriptor: D s32, A s8 (activations), B u8 (codes), both K-major, M 128, N 128.
-constexpr uint32_t kGemmIdesc = (2u << 4) | (1u << 7) | (0u << 10) | (static_cast<uint32_t>(kGemmN >> 3) << 17) |
-                                (static_cast<uint32_t>(kGemmM >> 4) << 24);
+// kind::i8 instruction descriptor: D s32, A s8 (weight codes - 1, TMEM), B s8 (activations, shared
+// memory), both K-major, M 128, N 128.
+constexpr uint32_t kGemmIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kGemmTok >> 3) << 17) |
+                                (static_cast<uint32_t>(kGemmRows >> 4) << 24);
 
-__device__ __forceinline__ void umma_i8(unsigned tmem_d, uint64_t da, uint64_t db, uint32_t idesc, bool accumulate) {
+// D (TMEM) += A (TMEM) x B (shared memory descriptor)
+__device__ __forceinline__ void umma_i8_ta(unsigned tmem_d, unsigned tmem_a, uint64_t db, uint32_t idesc) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "l"(da), "l"(db), "r"(idesc), "r"(accumulate ? 1u : 0u)
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(db), "r"(idesc)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
@@ -65,140 +102,283 @@ __device__ __forceinline__ void tmem_ld32(unsigned taddr, uint32_t (&v)[32]) {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Grid (row tiles, token tiles). q8 [T][ldq] int8 in gemm_slot order, gsum [T][groups], act_scale [T].
-__global__ void __launch_bounds__(kGemmThreads, 1) ternary_gemm_kernel(const IvbTernary m, const int8_t* __restrict__ q8,
-                                                                       int ldq, const float* __restrict__ act_scale,
-                                                                       const int32_t* __restrict__ gsum, int T,
-                                                                       int epilogue, float* out, int ldo,
-                                                                       unsigned long long timeout_ns, unsigned* error) {
+__device__ __forceinline__ void tmem_ld16(unsigned taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// 32 columns of this warp's lanes from 32 registers.
+__device__ __forceinline__ void tmem_st32(unsigned taddr, const uint32_t (&v)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]), "r"(v[16]), "r"(v[17]), "r"(v[18]),
+      "r"(v[19]), "r"(v[20]), "r"(v[21]), "r"(v[22]), "r"(v[23]), "r"(v[24]), "r"(v[25]), "r"(v[26]), "r"(v[27]),
+      "r"(v[28]), "r"(v[29]), "r"(v[30]), "r"(v[31])
+      : "memory");
+}
+
+// 32 columns of this warp's lanes set to one value per lane.
+__device__ __forceinline__ void tmem_fill32(unsigned taddr, uint32_t v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
+      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
+      "r"(v)
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// TMA tensor load of a 2-D box (x: byte column, y: row) of the packed weights into shared memory.
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_addr(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
+      : "memory");
+}
+__device__ __forceinline__ void mbar_expect(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
+// Grid (row tiles, token tiles). q8: the tiled activation layout (q8_chunk_offset), act_scale [T];
+// wmap: 2-D tensor map over the packed weights (row_bytes x rows bytes, box 32 x 128).
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    ternary_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const IvbTernary m, const int8_t* __restrict__ q8,
+                        int ldq, const float* __restrict__ act_scale, int T, int epilogue, float* out, int ldo,
+                        unsigned long long timeout_ns, unsigned* error) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       smem_raw + ((1024u - (static_cast<unsigned>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u);
-  unsigned char* tile_a = smem;                    // [128 tokens][128] int8, core-matrix layout
-  unsigned char* tile_b = smem + kGemmTile;        // [128 rows][128] codes
-  float* scl = reinterpret_cast<float*>(smem + 2 * kGemmTile);  // [128] group scales of the tile's rows
-  __shared__ __align__(8) unsigned long long mma_bar;
+  __shared__ __align__(8) unsigned long long full_bar[kGemmStages], empty_bar[kGemmStages];
+  __shared__ __align__(8) unsigned long long tfull_bar[kGemmBufs], tempty_bar[kGemmBufs];
+  __shared__ __align__(8) unsigned long long pk_bar[kPackSlots], pk_empty[kPackSlots];
   __shared__ unsigned tmem_base;
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int r0 = blockIdx.x * kGemmN, t0 = blockIdx.y * kGemmM;
+  __shared__ int failed;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kGemmTok;
   const int groups = (m.in_features + 127) >> 7;
-  if (warp == 0) {
+  unsigned char* pack = smem + kGemmStages * kGemmTile;           // packed ring
+  float* scale_tab = reinterpret_cast<float*>(pack + kPackSlots * kPackSlot);  // [groups][128 rows]
+  if (warp == kGemmMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
-                 "r"(kGemmN));
+                 "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  if (tid == 0) {
-    mbar_init(&mma_bar, 1);
+  const int pj = tid - 32 * (kGemmMmaWarp + 1);  // producer index 0..127 (pj == 0: the copy issuer)
+  if (pj == 0) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
+    for (int i = 0; i < kGemmStages; ++i) {
+      mbar_init(full_bar + i, kGemmProducers);
+      mbar_init(empty_bar + i, 1);
+    }
+    for (int i = 0; i < kGemmBufs; ++i) {
+      mbar_init(tfull_bar + i, 1);
+      mbar_init(tempty_bar + i, kGemmEpiWarps);
+    }
+    for (int i = 0; i < kPackSlots; ++i) {
+      mbar_init(pk_bar + i, 1);
+      mbar_init(pk_empty + i, kGemmProducers);
+    }
+    failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    for (int g = 0; g < kPackSlots && g < groups; ++g) {
+      mbar_expect_tx(pk_bar + g, kPackSlot);
+      tma_load_2d(pack + g * kPackSlot, &wmap, g << 5, r0, pk_bar + g);
+    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const unsigned tmem = tmem_base;
-  const int t = t0 + tid;                 // the token row this thread drains (TMEM lane tid)
-  const bool t_ok = t < T;
-  float acc[kGemmN];
-#pragma unroll
-  for (int n = 0; n < kGemmN; ++n) acc[n] = 0.0f;
-  unsigned parity = 0;
+  const int quarter = warp & 3;               // TMEM lane quarter this warp may access
+  const int row = 32 * quarter + lane;        // epilogue and producer warps: the weight row (TMEM lane)
+  const unsigned lane_base = tmem + (static_cast<unsigned>(32 * quarter) << 16);
+  const int col0 = (warp >> 2) * kGemmEpiCols;  // epilogue warps: first token column
+
+  float2 acc[kGemmEpiCols / 2];
   bool late = false;
-  for (int g = 0; g < groups && !late; ++g) {
-    // stage A: this thread's token row, eight 16-byte chunks of group g
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(q8 + static_cast<size_t>(t_ok ? t : 0) * ldq + (g << 7));
-      const int kin = min(128, m.in_features - (g << 7));
+  int issued = 0;                                // activation tiles bulk-copied by producer 0
+  int pk_issued = min(kPackSlots, groups);       // packed blocks requested by producer 0
+  if (warp > kGemmMmaWarp) {
+    // ---- producers ----
+    const int8_t* a_src = q8 + static_cast<size_t>(blockIdx.y) * (ldq >> 7) * kGemmTile;
+    for (int g = 0; g < groups; ++g) {
+      const int st = g % kGemmStages, slot = g % kPackSlots;
+      if (!mbar_wait_bounded(pk_bar + slot, (g / kPackSlots) & 1, timeout_ns) ||
+          (g >= kGemmStages && !mbar_wait_bounded(empty_bar + st, ((g / kGemmStages) - 1) & 1, timeout_ns))) {
+        late = true;
+        break;
+      }
+      if (pj == 0) {
+        mbar_expect(full_bar + st, kGemmTile);
+        bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(g) * kGemmTile, kGemmTile, full_bar + st);
+        issued = g + 1;
+      }
+      // row's 16 packed words -> 32 TMEM columns: column 4c + f holds the codes (w_c >> 2f) & 0x03030303
+      // (inputs 16c + 4b + f, b = 0..3), each byte turned into the signed code - 1
+      const uint4* pk = reinterpret_cast<const uint4*>(pack + slot * kPackSlot + row * 32);
+      const uint4 p0 = pk[0], p1 = pk[1];
+      const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+      uint32_t v[32];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        uint4 v = make_uint4(0u, 0u, 0u, 0u);
-        if (t_ok && (c << 4) < kin) v = __ldg(src + c);
-        *reinterpret_cast<uint4*>(tile_a + tile_off(tid, c)) = v;
+      for (int c = 0; c < 8; ++c)
+#pragma unroll
+        for (int f = 0; f < 4; ++f) v[4 * c + f] = (((words[c] >> (2 * f)) & 0x03030303u) + 0x7F7F7F7Fu) ^ 0x80808080u;
+      mbar_arrive(pk_empty + slot);
+      tmem_st32(lane_base + kGemmACol + st * 32, v);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(full_bar + st);
+      // refill the slot of group g - 1 (read by every producer by now) with group g - 1 + kPackSlots
+      const int prev = g - 1, nxt = prev + kPackSlots;
+      if (pj == 0 && prev >= 0 && nxt < groups) {
+        if (!mbar_wait_bounded(pk_empty + prev % kPackSlots, (prev / kPackSlots) & 1, timeout_ns)) {
+          late = true;
+          break;
+        }
+        mbar_expect_tx(pk_bar + prev % kPackSlots, kPackSlot);
+        tma_load_2d(pack + (prev % kPackSlots) * kPackSlot, &wmap, nxt << 5, r0, pk_bar + prev % kPackSlots);
+        pk_issued = nxt + 1;
       }
     }
-    // stage B: this thread's weight row, eight packed words -> eight 16-byte code chunks
-    {
-      const int r = r0 + tid;
-      const bool r_ok = r < m.rows;
-      const uint32_t* src = reinterpret_cast<const uint32_t*>(m.packed + static_cast<size_t>(r_ok ? r : 0) * m.row_bytes) + (g << 3);
-      const int words = min(8, (m.row_bytes >> 2) - (g << 3));
+    if (late) atomicExch(&failed, 1);
+  } else if (warp == kGemmMmaWarp) {
+    // ---- MMA issuer ----
+    if (lane == 0) {
+      for (int g = 0; g < groups; ++g) {
+        const int st = g % kGemmStages, b = g % kGemmBufs;
+        // tempty completion k of accumulator b: armed for group b + 3k (k = 0: the initial arming)
+        if (!mbar_wait_bounded(full_bar + st, (g / kGemmStages) & 1, timeout_ns) ||
+            !mbar_wait_bounded(tempty_bar + b, (g / kGemmBufs) & 1, timeout_ns)) {
+          late = true;
+          break;
+        }
+        tc_fence_after();
+        const unsigned bsm = smem_addr(smem + st * kGemmTile);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
-        const uint32_t w = (r_ok && c < words) ? __ldg(src + c) : 0u;
-        uint4 v;
-        v.x = w & 0x03030303u;
-        v.y = (w >> 2) & 0x03030303u;
-        v.z = (w >> 4) & 0x03030303u;
-        v.w = (w >> 6) & 0x03030303u;
-        *reinterpret_cast<uint4*>(tile_b + tile_off(tid, c)) = v;
+        for (int kk = 0; kk < 4; ++kk)
+          umma_i8_ta(tmem + b * kGemmTok, tmem + kGemmACol + st * 32 + kk * 8, smem_desc(bsm + kk * 256), kGemmIdesc);
+        umma_commit(empty_bar + st);
+        umma_commit(tfull_bar + b);
       }
-      scl[tid] = r_ok ? h2f(__ldg(m.scales + static_cast<size_t>(r) * m.scale_stride + g)) : 0.0f;
+      if (late) atomicExch(&failed, 1);
     }
-    const float gs = t_ok ? static_cast<float>(__ldg(gsum + static_cast<size_t>(t) * groups + g)) : 0.0f;
-    fence_proxy_async();  // the staged tiles, before the tensor core reads them
-    __syncthreads();
-    if (tid == 0) {
-      tc_fence_after();
-      const unsigned a = smem_addr(tile_a), b = smem_addr(tile_b);
-#pragma unroll
-      for (int kk = 0; kk < 4; ++kk) umma_i8(tmem, smem_desc(a + kk * 256), smem_desc(b + kk * 256), kGemmIdesc, kk > 0);
-      umma_commit(&mma_bar);
+    __syncwarp();
+  } else {
+    // ---- epilogue: drain, scale, accumulate; re-arm the accumulator for group g + 3 ----
+    for (int i = tid; i < groups * kGemmRows; i += 32 * kGemmEpiWarps) {
+      const int g = i >> 7, r = r0 + (i & 127);
+      scale_tab[i] = r < m.rows ? h2f(__ldg(m.scales + static_cast<size_t>(r) * m.scale_stride + g)) : 0.0f;
     }
-    // wait for the four MMAs (bounded), then drain this thread's lane
-    late = !mbar_wait_bounded(&mma_bar, parity, timeout_ns);
-    late = __syncthreads_or(late);
-    parity ^= 1u;
-    if (late) break;
-    tc_fence_after();
-    const unsigned lane_addr = tmem + (static_cast<unsigned>(warp * 32) << 16);
-#pragma unroll
-    for (int cb = 0; cb < kGemmN / 32; ++cb) {
-      uint32_t d[32];
-      tmem_ld32(lane_addr + cb * 32, d);
-#pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const int n = cb * 32 + j;
-        acc[n] = fmaf(static_cast<float>(static_cast<int>(d[j])) - gs, scl[n], acc[n]);
-      }
-    }
+    asm volatile("bar.sync 1, %0;" ::"n"(32 * kGemmEpiWarps) : "memory");
+    for (int b = 0; b < kGemmBufs && b < groups; ++b) tmem_fill32(lane_base + b * kGemmTok + col0, kGemmMagic);
+    tmem_wait_st();
     tc_fence_before();
-    __syncthreads();  // tiles and TMEM are rewritten by the next group
-  }
-  if (late) {
-    if (tid == 0) atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
-  } else if (t_ok) {
-    const float s = __ldg(act_scale + t);
-    float* orow = out + static_cast<size_t>(t) * ldo;
-    if (epilogue == IVB_EPI_SILU_PAIR) {
+    __syncwarp();
+    if (lane == 0)
+      for (int b = 0; b < kGemmBufs; ++b) mbar_arrive(tempty_bar + b);
 #pragma unroll
-      for (int p2 = 0; p2 < kGemmN / 2; ++p2) {
-        const int r = r0 + 2 * p2;
-        if (r + 1 < m.rows) {
-          float g = acc[2 * p2] * s, u = acc[2 * p2 + 1] * s;
-          if (m.bias != nullptr) {
-            g += __ldg(m.bias + r);
-            u += __ldg(m.bias + r + 1);
-          }
-          orow[r >> 1] = silu_f(g) * u;
-        }
+    for (int n = 0; n < kGemmEpiCols / 2; ++n) acc[n] = make_float2(0.0f, 0.0f);
+    const float2 m2 = make_float2(-kGemmMagicF, -kGemmMagicF);
+    for (int g = 0; g < groups; ++g) {
+      const int b = g % kGemmBufs;
+      late = !mbar_wait_bounded(tfull_bar + b, (g / kGemmBufs) & 1, timeout_ns);
+      if (__any_sync(kFull, late)) {
+        late = true;
+        break;
       }
-    } else {
+      tc_fence_after();
+      uint32_t d[32];
+      tmem_ld32(lane_base + b * kGemmTok + col0, d);
+      const float sv = scale_tab[g * kGemmRows + row];
+      const float2 s2 = make_float2(sv, sv);
 #pragma unroll
-      for (int n = 0; n < kGemmN; ++n) {
-        const int r = r0 + n;
-        if (r < m.rows) {
-          float v = acc[n] * s;
-          if (m.bias != nullptr) v += __ldg(m.bias + r);
-          orow[r] = epilogue == IVB_EPI_RESIDUAL ? orow[r] + v : v;
+      for (int q = 0; q < 16; ++q) {
+        const float2 x = __fadd2_rn(make_float2(__uint_as_float(d[2 * q]), __uint_as_float(d[2 * q + 1])), m2);
+        acc[q] = __ffma2_rn(x, s2, acc[q]);
+      }
+      if (g + kGemmBufs < groups) {
+        tmem_fill32(lane_base + b * kGemmTok + col0, kGemmMagic);
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar + b);
+    }
+    if (late && lane == 0) atomicExch(&failed, 1);
+  }
+  __syncthreads();
+  const bool bad = failed != 0;
+  if (bad) {
+    if (tid == 0) atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
+    // no bulk or tensor copy may still be writing this CTA's shared memory when it exits
+    if (pj == 0) {
+      for (int g = max(0, issued - kGemmStages); g < issued; ++g)
+        mbar_wait_bounded(full_bar + g % kGemmStages, (g / kGemmStages) & 1, timeout_ns);
+      for (int g = max(0, pk_issued - kPackSlots); g < pk_issued; ++g)
+        mbar_wait_bounded(pk_bar + g % kPackSlots, (g / kPackSlots) & 1, timeout_ns);
+    }
+  } else {
+    // stage the tile as [token][row] fp32 in the (now idle) stages, then write it out row by row, coalesced
+    constexpr int kLd = kGemmRows + 4;
+    float* tile = reinterpret_cast<float*>(smem);
+    if (warp < kGemmEpiWarps) {
+#pragma unroll
+      for (int q = 0; q < kGemmEpiCols / 2; ++q) {
+        tile[(col0 + 2 * q) * kLd + row] = acc[q].x;
+        tile[(col0 + 2 * q + 1) * kLd + row] = acc[q].y;
+      }
+    }
+    __syncthreads();
+    const bool vec = (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
+    for (int tr = warp; tr < kGemmTok && t0 + tr < T; tr += kGemmThreads / 32) {
+      const int tt = t0 + tr;
+      const float sc = __ldg(act_scale + tt);
+      const float4 v4 = *reinterpret_cast<const float4*>(tile + tr * kLd + 4 * lane);
+      float v[4] = {v4.x * sc, v4.y * sc, v4.z * sc, v4.w * sc};
+      const int r = r0 + 4 * lane;
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (m.bias != nullptr && r + e < m.rows) v[e] += __ldg(m.bias + r + e);
+      float* orow = out + static_cast<size_t>(tt) * ldo;
+      if (epilogue == IVB_EPI_SILU_PAIR) {
+        // rows r, r+1 (gate, up) -> output r/2; rows r+2, r+3 -> r/2 + 1 (m.rows is even)
+        if (r + 1 < m.rows) orow[r >> 1] = silu_f(v[0]) * v[1];
+        if (r + 3 < m.rows) orow[(r >> 1) + 1] = silu_f(v[2]) * v[3];
+      } else if (vec && r + 3 < m.rows) {
+        float4* o4 = reinterpret_cast<float4*>(orow + r);
+        if (epilogue == IVB_EPI_RESIDUAL) {
+          const float4 old = *o4;
+          v[0] += old.x;
+          v[1] += old.y;
+          v[2] += old.z;
+          v[3] += old.w;
         }
+        *o4 = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (r + e < m.rows) orow[r + e] = epilogue == IVB_EPI_RESIDUAL ? orow[r + e] + v[e] : v[e];
       }
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kGemmN));
+  if (warp == kGemmMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
 
-// One CTA per token row: the canonical quantiser (RMSNorm optional), codes written in gemm_slot order,
-// per-128-group sums of the codes.
+// One CTA per token row: the canonical quantiser (RMSNorm optional), codes written as 16-byte chunks of
+// the tiled GEMM activation layout (q8_chunk_offset, gemm_slot order inside a chunk), per-128-group sums
+// of the codes.
 __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x, int n, const float* norm_w, float norm_eps,
                                                                  float clip, float act_eps, int8_t* q8, int ldq,
                                                                  float* scale, int32_t* gsum) {
@@ -211,12 +391,25 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x,
   load_vector(x + static_cast<size_t>(row) * n, n, xv);
   __syncthreads();
   const float s = quantize_block(xv, n, norm_w, norm_eps, clip, act_eps, codes, false, nullptr, red);
-  int8_t* qrow = q8 + static_cast<size_t>(row) * ldq;
   const int groups = (n + 127) >> 7;
-  for (int i = threadIdx.x; i < ldq; i += kThreads) qrow[gemm_slot(i)] = i < n ? codes[i] : 0;
+  for (int k = threadIdx.x; k < (ldq >> 4); k += kThreads) {
+    // word f, byte b of chunk k holds input 16k + 4b + f
+    uint32_t o[4];
+#pragma unroll
+    for (int f = 0; f < 4; ++f) {
+      uint32_t w = 0u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int i = (k << 4) + 4 * b + f;
+        w |= (i < n ? static_cast<uint32_t>(static_cast<uint8_t>(codes[i])) : 0u) << (8 * b);
+      }
+      o[f] = w;
+    }
+    *reinterpret_cast<uint4*>(q8 + q8_chunk_offset(row, k, ldq)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
   // group sums: one warp per group, exact integers
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int g = warp; g < groups; g += kWarps) {
+  for (int g = warp; gsum != nullptr && g < groups; g += kWarps) {
     int sum = 0;
     for (int i = (g << 7) + lane; i < min(n, (g + 1) << 7); i += 32) sum += codes[i];
     sum = __reduce_add_sync(kFull, sum);
@@ -233,9 +426,8 @@ int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* 
                           float norm_clip, float act_eps, int8_t* q8, int32_t ldq, float* scale, int32_t* gsum,
                           void* stream) {
   using namespace ivb;
-  if (x == nullptr || q8 == nullptr || scale == nullptr || gsum == nullptr)
-    return fail(IVB_EINVAL, "ivb_quantize_rows: null argument");
-  if (rows < 0 || n <= 0 || ldq < (n + 127) / 128 * 128 || (ldq & 15))
+  if (x == nullptr || q8 == nullptr || scale == nullptr) return fail(IVB_EINVAL, "ivb_quantize_rows: null argument");
+  if (rows < 0 || n <= 0 || ldq < (n + 127) / 128 * 128 || (ldq & 127) || (reinterpret_cast<uintptr_t>(q8) & 15))
     return fail(IVB_EINVAL, "ivb_quantize_rows: bad shape (rows %d, n %d, ldq %d)", rows, n, ldq);
   if (rows == 0) return IVB_OK;
   const size_t pad = static_cast<size_t>((n + 63) / 64) * 64;
@@ -248,24 +440,59 @@ int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* 
   return IVB_OK;
 }
 
-int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, const int32_t* gsum,
-                         int32_t rows_t, int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream) {
+}  // extern "C"
+
+namespace ivb {
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+}  // namespace
+}  // namespace ivb
+
+extern "C" {
+
+int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
+                         int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream) {
   using namespace ivb;
-  if (m == nullptr || q8 == nullptr || act_scale == nullptr || gsum == nullptr || out == nullptr || error == nullptr)
+  if (m == nullptr || q8 == nullptr || act_scale == nullptr || out == nullptr || error == nullptr)
     return fail(IVB_EINVAL, "ivb_ternary_gemm: null argument");
   if (int32_t rc = check_ternary(*m, "ivb_ternary_gemm")) return rc;
   if (epilogue < IVB_EPI_STORE || epilogue > IVB_EPI_SILU_PAIR) return fail(IVB_EINVAL, "ivb_ternary_gemm: bad epilogue");
   if (epilogue == IVB_EPI_SILU_PAIR && (m->rows & 1)) return fail(IVB_EINVAL, "ivb_ternary_gemm: silu pairs need an even row count");
-  if (rows_t < 0 || ldq < (m->in_features + 127) / 128 * 128 || (ldq & 15) || (reinterpret_cast<uintptr_t>(q8) & 15))
+  if (rows_t < 0 || ldq < (m->in_features + 127) / 128 * 128 || (ldq & 127) || (reinterpret_cast<uintptr_t>(q8) & 15))
     return fail(IVB_EINVAL, "ivb_ternary_gemm: bad activation layout (ldq %d)", ldq);
   if (ldo < (epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows)) return fail(IVB_EINVAL, "ivb_ternary_gemm: ldo too small");
   if (rows_t == 0) return IVB_OK;
   if (!device_is_sm100()) return fail(IVB_EUNSUPPORTED, "ivb_ternary_gemm: needs an sm_100 device");
-  const size_t smem = 2 * kGemmTile + kGemmN * 4 + 1024;
+  const int groups = (m->in_features + 127) / 128;
+  constexpr size_t kSmemCap = 227 * 1024 - 2048;  // dynamic shared memory beside the static barriers
+  const size_t smem = static_cast<size_t>(kGemmStages) * kGemmTile + kPackSlots * kPackSlot +
+                      static_cast<size_t>(groups) * kGemmRows * 4 + 1024;
+  if (smem > kSmemCap) return fail(IVB_EINVAL, "ivb_ternary_gemm: %d inputs leave too little shared memory", m->in_features);
   IVB_CUDA(cudaFuncSetAttribute(ternary_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  const dim3 grid((m->rows + kGemmN - 1) / kGemmN, (rows_t + kGemmM - 1) / kGemmM);
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(IVB_EUNSUPPORTED, "ivb_ternary_gemm: cuTensorMapEncodeTiled is unavailable");
+  CUtensorMap wmap;
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(m->row_bytes), static_cast<cuuint64_t>(m->rows)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(m->row_bytes)};
+  const cuuint32_t box[2] = {32, kGemmRows}, estride[2] = {1, 1};
+  if (encode(&wmap, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<unsigned char*>(m->packed), dims, strides, box, estride,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+    return fail(IVB_EINVAL, "ivb_ternary_gemm: cannot describe the packed weights to the TMA engine");
+  const dim3 grid((m->rows + kGemmRows - 1) / kGemmRows, (rows_t + kGemmTok - 1) / kGemmTok);
   ternary_gemm_kernel<<<grid, kGemmThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      *m, q8, ldq, act_scale, gsum, rows_t, epilogue, out, ldo, 2000000000ull, error);
+      wmap, *m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, 2000000000ull, error);
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }

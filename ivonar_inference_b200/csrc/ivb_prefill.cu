@@ -15,14 +15,6 @@
 #include "ivb_common.h"
 #include "ivb_cluster.cuh"
 
-extern "C" {
-int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* norm_weight, float norm_eps,
-                          float norm_clip, float act_eps, int8_t* q8, int32_t ldq, float* scale, int32_t* gsum,
-                          void* stream);
-int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, const int32_t* gsum,
-                         int32_t rows_t, int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream);
-}
-
 namespace ivb {
 
 const IvbModelDesc& decoder_model(const IvbDecoder* dec, const IvbLayerDesc** layers);
@@ -398,7 +390,7 @@ __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_
 }
 
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, gsum, err, total;
+  size_t resid, ent, y, h, q8, scale, err, total;
   int ldq, groups, ld_ent;
 };
 
@@ -421,9 +413,8 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.ent = take(T * ld_ent * 4);
   L.y = take(T * d * 4);
   L.h = take(T * std::max(F, d) * 4);  // also the mamba conv values [T][d]
-  L.q8 = take(T * L.ldq);
+  L.q8 = take((T + 127) / 128 * 128 * L.ldq);  // whole 128-token tiles
   L.scale = take(T * 4);
-  L.gsum = take(T * L.groups * 4);
   L.err = take(16);
   L.total = o;
   return L;
@@ -469,7 +460,6 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   float* hbuf = reinterpret_cast<float*>(ws + W.h);
   int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
   float* scale = reinterpret_cast<float*>(ws + W.scale);
-  int32_t* gsum = reinterpret_cast<int32_t*>(ws + W.gsum);
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
   if (err == nullptr) return fail(IVB_EINVAL, "ivb_decoder_prefill: bind the decoder first");
   const int lpad = static_cast<int>((Lt + 15) / 16 * 16), rpad = (rope + 7) / 8 * 8;
@@ -477,11 +467,11 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   IVB_CUDA(cudaGetLastError());
   auto quant = [&](const float* x, int n, const float* norm, float eps) -> int32_t {
     const int ld = (n + 127) / 128 * 128;
-    return ivb_quantize_rows(x, count, n, norm, eps, md.norm_clip, md.act_eps, q8, ld, scale, gsum, stream);
+    return ivb_quantize_rows(x, count, n, norm, eps, md.norm_clip, md.act_eps, q8, ld, scale, nullptr, stream);
   };
   auto gemm = [&](const IvbTernary& m, int epilogue, float* out, int ldo) -> int32_t {
     const int ld = (m.in_features + 127) / 128 * 128;
-    return ivb_ternary_gemm(&m, q8, ld, scale, gsum, count, epilogue, out, ldo, err, stream);
+    return ivb_ternary_gemm(&m, q8, ld, scale, count, epilogue, out, ldo, err, stream);
   };
   for (int li = 0; li < md.num_layers; ++li) {
     const IvbLayerDesc& L = layers[li];

@@ -36,7 +36,7 @@ def _quantize_rows(x: torch.Tensor, w: torch.Tensor | None):
     nat, lib = _lib()
     rows, n = x.shape
     ldq = (n + 127) // 128 * 128
-    q8 = torch.zeros(rows, ldq, dtype=torch.int8, device="cuda")
+    q8 = torch.zeros((rows + 127) // 128 * 128, ldq, dtype=torch.int8, device="cuda")  # whole 128-token tiles
     scale = torch.empty(rows, dtype=torch.float32, device="cuda")
     gsum = torch.empty(rows, (n + 127) // 128, dtype=torch.int32, device="cuda")
     xd = x.float().cuda().contiguous()
@@ -47,8 +47,15 @@ def _quantize_rows(x: torch.Tensor, w: torch.Tensor | None):
     return q8, scale, gsum, ldq
 
 
-def _slot(i: np.ndarray) -> np.ndarray:
-    return (i & ~15) + ((i & 3) << 2) + ((i >> 2) & 3)
+def _q8_offsets(rows: int, ldq: int) -> np.ndarray:
+    """Byte offset of (token t, input i) in the tiled GEMM activation layout documented in ivonar_b200.h."""
+    t = np.arange(rows)[:, None]
+    i = np.arange(ldq)[None, :]
+    k = i >> 4
+    r = t & 127
+    tile = ((t >> 7) * (ldq >> 7) + (k >> 3)) * 16384
+    core = (((r >> 3) << 3) + (k & 7)) * 128 + ((r & 7) << 4)
+    return tile + core + ((i & 3) << 2) + ((i >> 2) & 3)
 
 
 def test_quantize_rows_matches_the_oracle_quantiser(oracle_lib) -> None:
@@ -57,13 +64,12 @@ def test_quantize_rows_matches_the_oracle_quantiser(oracle_lib) -> None:
         x = torch.randn(rows, n, generator=gen) * 2.0
         w = 1.0 + 0.1 * torch.randn(n, generator=gen)
         q8, scale, gsum, ldq = _quantize_rows(x, w if normed else None)
-        q8 = q8.cpu().numpy()
+        flat = q8.cpu().numpy().reshape(-1)
+        natural = flat[_q8_offsets(rows, ldq)]
         for t in range(rows):
             q, s, _ = oracle_lib.quantize(x[t].numpy(), w.numpy() if normed else None)
-            got = np.zeros(ldq, np.int8)
-            got[: n] = q8[t][_slot(np.arange(n))]
-            np.testing.assert_array_equal(got[:n], q)
-            assert np.all(q8[t][_slot(np.arange(n, ldq))] == 0)
+            np.testing.assert_array_equal(natural[t, :n], q)
+            assert np.all(natural[t, n:] == 0)
             assert np.float32(scale[t].item()) == s
             groups = (n + 127) // 128
             want = [int(q[g * 128:(g + 1) * 128].astype(np.int64).sum()) for g in range(groups)]
@@ -85,8 +91,8 @@ def test_gemm_matches_the_oracle_gemv_per_token(oracle_lib, epilogue: int) -> No
         out_rows = rows // 2 if epilogue == 2 else rows
         base = torch.randn(tokens, out_rows, generator=gen)
         out = base.clone().cuda()
-        nat.check(lib.ivb_ternary_gemm(ctypes.byref(desc), q8.data_ptr(), ldq, scale.data_ptr(), gsum.data_ptr(), tokens,
-                                       epilogue, out.data_ptr(), out_rows, err.data_ptr(), stream), "ivb_ternary_gemm")
+        nat.check(lib.ivb_ternary_gemm(ctypes.byref(desc), q8.data_ptr(), ldq, scale.data_ptr(), tokens, epilogue,
+                                       out.data_ptr(), out_rows, err.data_ptr(), stream), "ivb_ternary_gemm")
         torch.cuda.synchronize()
         assert int(err.item()) == 0
         got = out.cpu().numpy()
