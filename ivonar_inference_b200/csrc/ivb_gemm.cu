@@ -13,13 +13,11 @@
 //     then every producer thread expands its row's 128 two-bit codes to signed bytes (code - 1) in
 //     registers and stores them into the group's A slot in TMEM (tcgen05.st, 32 columns);
 //   * one MMA thread: four 128x128x32 int8 MMAs (A from TMEM, B = activations from shared memory) into
-//     TMEM accumulator g % 3, committed to the stage's "empty" barrier and to the accumulator's "full"
-//     barrier;
+//     TMEM accumulator g % 3 (the first one overwrites it), committed to the stage's "empty" barrier and
+//     to the accumulator's "full" barrier;
 //   * epilogue warps (16; warp w reads TMEM lane quarter w % 4 = weight rows, columns 32 (w / 4).. =
-//     tokens): drain the accumulator (tcgen05.ld), scale by the row's group scale and accumulate in fp32
-//     registers, then re-arm it with the int32 0x4B400000. With that preload the accumulator holds the
-//     bit pattern of the float 12582912 + dot (exact while |dot| < 2^22), so the drain is one paired
-//     subtract and one paired multiply-add per two outputs instead of an integer conversion.
+//     tokens): drain the accumulator (tcgen05.ld), convert the exact int32 group dots, scale them by the
+//     row's group scale and accumulate in fp32 registers (paired multiply-adds).
 // TMEM: 3 accumulators x 128 columns + 4 A slots x 32 columns = all 512 columns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -47,8 +45,6 @@ constexpr int kGemmProducers = 32 * kGemmProdWarps;
 constexpr int kGemmThreads = 32 * (kGemmEpiWarps + 1 + kGemmProdWarps);
 constexpr int kPackSlots = 4;                    // packed weight blocks in flight
 constexpr int kPackSlot = kGemmRows * 32;        // packed bytes of one group for the tile's 128 rows
-constexpr unsigned kGemmMagic = 0x4B400000u;     // bit pattern of 12582912.0f = 1.5 * 2^23
-constexpr float kGemmMagicF = 12582912.0f;
 
 // Position of input i inside the GEMM activation layout: each 16-input block is a 4 x 4 byte transpose
 // (byte 4f + b holds input 4b + f), which matches the codes a packed weight word yields by masking
@@ -76,11 +72,11 @@ constexpr uint32_t kGemmIdesc = (2u << 4) | (1u << 7) | (1u << 10) | (static_cas
                                 (static_cast<uint32_t>(kGemmRows >> 4) << 24);
 
 // D (TMEM) += A (TMEM) x B (shared memory descriptor)
-__device__ __forceinline__ void umma_i8_ta(unsigned tmem_d, unsigned tmem_a, uint64_t db, uint32_t idesc) {
+__device__ __forceinline__ void umma_i8_ta(unsigned tmem_d, unsigned tmem_a, uint64_t db, uint32_t idesc, bool accumulate) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, 1, 0;\n\t"
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], [%1], %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-      "r"(tmem_a), "l"(db), "r"(idesc)
+      "r"(tmem_a), "l"(db), "r"(idesc), "r"(accumulate ? 1u : 0u)
       : "memory");
 }
 __device__ __forceinline__ void umma_commit(unsigned long long* bar) {
@@ -124,14 +120,6 @@ __device__ __forceinline__ void tmem_st32(unsigned taddr, const uint32_t (&v)[32
       : "memory");
 }
 
-// 32 columns of this warp's lanes set to one value per lane.
-__device__ __forceinline__ void tmem_fill32(unsigned taddr, uint32_t v) {
-  asm volatile(
-      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-      "%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-      "r"(v)
-      : "memory");
-}
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // TMA tensor load of a 2-D box (x: byte column, y: row) of the packed weights into shared memory.
@@ -266,7 +254,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const unsigned bsm = smem_addr(smem + st * kGemmTile);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          umma_i8_ta(tmem + b * kGemmTok, tmem + kGemmACol + st * 32 + kk * 8, smem_desc(bsm + kk * 256), kGemmIdesc);
+          umma_i8_ta(tmem + b * kGemmTok, tmem + kGemmACol + st * 32 + kk * 8, smem_desc(bsm + kk * 256), kGemmIdesc, kk > 0);
         umma_commit(empty_bar + st);
         umma_commit(tfull_bar + b);
       }
@@ -274,21 +262,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     __syncwarp();
   } else {
-    // ---- epilogue: drain, scale, accumulate; re-arm the accumulator for group g + 3 ----
+    // ---- epilogue: drain, scale, accumulate ----
     for (int i = tid; i < groups * kGemmRows; i += 32 * kGemmEpiWarps) {
       const int g = i >> 7, r = r0 + (i & 127);
       scale_tab[i] = r < m.rows ? h2f(__ldg(m.scales + static_cast<size_t>(r) * m.scale_stride + g)) : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"n"(32 * kGemmEpiWarps) : "memory");
-    for (int b = 0; b < kGemmBufs && b < groups; ++b) tmem_fill32(lane_base + b * kGemmTok + col0, kGemmMagic);
-    tmem_wait_st();
-    tc_fence_before();
     __syncwarp();
     if (lane == 0)
       for (int b = 0; b < kGemmBufs; ++b) mbar_arrive(tempty_bar + b);
 #pragma unroll
     for (int n = 0; n < kGemmEpiCols / 2; ++n) acc[n] = make_float2(0.0f, 0.0f);
-    const float2 m2 = make_float2(-kGemmMagicF, -kGemmMagicF);
     for (int g = 0; g < groups; ++g) {
       const int b = g % kGemmBufs;
       late = !mbar_wait_bounded(tfull_bar + b, (g / kGemmBufs) & 1, timeout_ns);
@@ -303,12 +287,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       const float2 s2 = make_float2(sv, sv);
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        const float2 x = __fadd2_rn(make_float2(__uint_as_float(d[2 * q]), __uint_as_float(d[2 * q + 1])), m2);
+        const float2 x = make_float2(static_cast<float>(static_cast<int>(d[2 * q])), static_cast<float>(static_cast<int>(d[2 * q + 1])));
         acc[q] = __ffma2_rn(x, s2, acc[q]);
-      }
-      if (g + kGemmBufs < groups) {
-        tmem_fill32(lane_base + b * kGemmTok + col0, kGemmMagic);
-        tmem_wait_st();
       }
       tc_fence_before();
       __syncwarp();
