@@ -11,6 +11,10 @@ advance_many(16), host copies included. With --gpus N (torchrun) every rank deco
 independent sequences on its own GPU (data parallel, no collective on the data path); value is the
 total over ranks divided by the slowest rank's time.
 
+Secondary, rank 0: prompt prefill tok/s at 512, 2048 and 8192 tokens (b=1) through
+B200Decoder.prefill (tcgen05 GEMMs, recurrent scan, latent-cache fill and causal attention), and the
+int8 tensor-core throughput of the prefill GEMM alone on the gate/up shape at 2048 tokens.
+
 --impl reference times the reference algorithm's CPU implementation (the C port in oracle/, all host
 threads) on a bounded sample of the same workload, rank 0 only.
 """
@@ -48,6 +52,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true")
     return ap.parse_args()
 
 
@@ -189,6 +194,73 @@ def run_reference(args) -> None:
     del torch
 
 
+INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
+
+
+def prefill_measure(device) -> dict:
+    """Config 2 at b=1: prefill tok/s per prompt length, and the GEMM's int8 tensor-core throughput."""
+    import ctypes
+
+    import torch
+
+    from ivonar_inference_b200 import B200Decoder, synthetic
+    from ivonar_inference_b200 import _native as native
+
+    model = synthetic.synthetic_model(synthetic.config1(seq_len=8192), seed=0)
+    result: dict = {"batch": 1, "tok_s": {}, "ms": {}}
+    for length, reps in ((512, 3), (2048, 2), (8192, 1)):
+        dec = B200Decoder(model, max_len=length, device=device)
+        prompt = synthetic.random_prompt(32768, length, seed=length).to(device)
+        dec.prefill(prompt)
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            dec.prefill(prompt)
+        end.record()
+        torch.cuda.synchronize(device)
+        ms = start.elapsed_time(end) / reps
+        result["tok_s"][str(length)] = length / (ms / 1000.0)
+        result["ms"][str(length)] = ms
+        del dec
+    torch.cuda.empty_cache()
+    lib = native.library()
+    gen = torch.Generator().manual_seed(0)
+    rows, cols, tokens = 5632, 1024, 2048
+    packed, scales = synthetic._packed(gen, rows, cols, "baseline")
+    weights = (packed.to(device).contiguous(), scales.view(torch.int16).to(device).contiguous())
+    desc = native.ternary(weights[0], weights[1], None, rows, cols)
+    x = torch.randn(tokens, cols, device=device)
+    q8 = torch.zeros(tokens, cols, dtype=torch.int8, device=device)
+    act = torch.empty(tokens, device=device)
+    out = torch.empty(tokens, rows, device=device)
+    err = torch.zeros(1, dtype=torch.int32, device=device)
+    stream = torch.cuda.current_stream(device).cuda_stream
+    native.check(lib.ivb_quantize_rows(x.data_ptr(), tokens, cols, 0, 1e-6, 8.0, 1e-5, q8.data_ptr(), cols, act.data_ptr(),
+                                       None, stream), "ivb_quantize_rows")
+
+    def gemm() -> None:
+        native.check(lib.ivb_ternary_gemm(ctypes.byref(desc), q8.data_ptr(), cols, act.data_ptr(), tokens, 0,
+                                          out.data_ptr(), rows, err.data_ptr(), stream), "ivb_ternary_gemm")
+
+    for _ in range(3):
+        gemm()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(20):
+        gemm()
+    end.record()
+    torch.cuda.synchronize(device)
+    if int(err.item()) != 0:
+        raise RuntimeError("prefill GEMM reported a timeout")
+    us = start.elapsed_time(end) / 20 * 1000.0
+    tops = 2.0 * rows * cols * tokens / (us * 1e-6) / 1e12
+    result["gemm"] = {"shape": f"{rows}x{cols} weights x {tokens} tokens", "us": us, "tops_int8": tops,
+                      "frac_of_nominal_int8_peak": tops / INT8_NOMINAL_TOPS, "peak_tops": INT8_NOMINAL_TOPS,
+                      "peak_source": "nominal dense int8 (no measured int8 peak in MEASURED_PEAKS.json)"}
+    return result
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -290,6 +362,8 @@ def run_b200(args) -> None:
             "roofline": roofline,
             "clocks": clock_info,
         }
+        if not args.no_prefill:
+            line["prefill"] = prefill_measure(device)
         if world == 1 and not args.no_cpu_baseline:
             prompt = synthetic.random_prompt(32768, PROMPT, seed=99)[0].numpy()
             line["cpu_baseline"] = cpu_baseline(model, prompt, 32)
