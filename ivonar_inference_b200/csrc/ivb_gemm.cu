@@ -28,12 +28,12 @@
 
 #include "ivb_common.h"
 #include "ivb_cluster.cuh"
+#include "ivb_tiles.cuh"
 
 namespace ivb {
 
 constexpr int kGemmRows = 128;       // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kGemmTok = 128;        // tokens per tile (MMA N, accumulator columns)
-constexpr int kGemmTile = 16384;     // bytes of one 128-token x 128-input activation tile
 constexpr int kGemmStages = 4;       // activation stages = TMEM A slots (groups in flight)
 constexpr int kGemmBufs = 3;         // TMEM accumulators of 128 columns
 constexpr int kGemmACol = kGemmBufs * kGemmTok;  // first TMEM column of the A slots (32 columns each)
@@ -45,21 +45,6 @@ constexpr int kGemmProducers = 32 * kGemmProdWarps;
 constexpr int kGemmThreads = 32 * (kGemmEpiWarps + 1 + kGemmProdWarps);
 constexpr int kPackSlots = 4;                    // packed weight blocks in flight
 constexpr int kPackSlot = kGemmRows * 32;        // packed bytes of one group for the tile's 128 rows
-
-// Position of input i inside the GEMM activation layout: each 16-input block is a 4 x 4 byte transpose
-// (byte 4f + b holds input 4b + f), which matches the codes a packed weight word yields by masking
-// (w >> 2f) & 0x03030303 for f = 0..3.
-__host__ __device__ __forceinline__ int gemm_slot(int i) { return (i & ~15) + ((i & 3) << 2) + ((i >> 2) & 3); }
-
-// One 16-byte chunk (c) of row r in a K-major core-matrix tile: core matrices of 8 rows x 16 bytes,
-// 8 chunks (128 inputs) per row group. LBO (next K chunk) = 128 B, SBO (next 8-row group) = 1024 B.
-__host__ __device__ __forceinline__ int tile_off(int r, int c) { return (((r >> 3) << 3) + c) * 128 + ((r & 7) << 4); }
-
-// Byte offset of (token t, 16-input chunk k) in the tiled activation buffer of row length ldq:
-// 16 KB blocks per (token tile, 128-input group), each a core-matrix tile.
-__host__ __device__ __forceinline__ size_t q8_chunk_offset(int t, int k, int ldq) {
-  return (static_cast<size_t>(t >> 7) * (ldq >> 7) + (k >> 3)) * kGemmTile + tile_off(t & 127, k & 7);
-}
 
 __device__ __forceinline__ uint64_t smem_desc(unsigned addr) {
   return static_cast<uint64_t>((addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(128 >> 4) << 16) |

@@ -1,19 +1,22 @@
 // Prompt prefill of libivonar_b200.so: all prompt tokens of a chunk go through each layer together.
 //
 // Per block: quantise every token row (ivb_quantize_rows), the entry projection as one tcgen05 int8
-// GEMM over all tokens (ivb_ternary_gemm), then the mixer — the recurrent scan over the tokens for a
-// mamba block (one warp lane per state, tokens in order), or for an mla block the latent/k_rope cache
-// fill of every token followed by causal latent attention (one CTA per token and head) — then the
-// out, gate/up and down GEMMs with their residual / SwiGLU epilogues. The head runs on the last
-// token only. Caches, recurrent state, position and token end exactly where the token-by-token decode
-// kernel would leave them, so decoding continues from here. Replaces kernel_decoder.py:457-479
-// (prefill) and kernels/ternary.cu:688-982 (tile GEMM, recurrent tile, kv write, attention tile).
+// GEMM over all tokens (ivb_ternary_gemm), then the mixer, then the out, gate/up and down GEMMs with
+// their residual / SwiGLU epilogues. Mamba mixer: the convolution values of all tokens in parallel,
+// then the recurrence over the tokens with the per-token coefficients staged in shared memory for
+// blocks of 32 tokens. MLA mixer: the latent/k_rope cache fill of every token, the per-head keys and
+// values of all cached positions from the latent (two more tcgen05 GEMMs), then causal flash attention
+// on tensor cores. The head runs on the last token only. Caches, recurrent state, position and token
+// end exactly where the token-by-token decode kernel would leave them, so decoding continues from
+// here. Replaces kernel_decoder.py:457-479 (prefill) and kernels/ternary.cu:688-982 (tile GEMM,
+// recurrent tile, kv write, attention tile).
 #include <cuda_runtime.h>
 
 #include <algorithm>
 
 #include "ivb_common.h"
 #include "ivb_cluster.cuh"
+#include "ivb_tiles.cuh"
 
 namespace ivb {
 
@@ -230,157 +233,226 @@ __global__ void __launch_bounds__(kThreads) mla_cache_kernel(IvbLayerDesc L, con
   }
 }
 
-// Causal latent attention of token t (position pos0 + t) and head h over cached positions 0..pos0+t.
-// Absorbed form as in the decode kernel: s_p = a_p <qa, ql_p> + q_nope.b_k + <q_rope, k_rope_p>, online
-// softmax, u = sum p_p a_p ql_p, out = W_v u / l + b_v. 128 threads; 8 lanes per position for scores,
-// a warp per position group for u.
-constexpr int kAttnThreads = 128;
-constexpr int kAttnTile = 128;
+// ---- causal attention of the prefill on tensor cores ---------------------------------------------
+// Non-absorbed form: the cached latent of every position p (int8 codes ql_p, scale a_p) is expanded
+// by the tcgen05 GEMM into per-head keys K_nope[p] = a_p W_k ql_p + b_k and values V[p] = a_p W_v ql_p
+// + b_v, which is the same arithmetic as the decode kernel's absorbed form regrouped:
+// a_p <W_k^T q, ql_p> + q.b_k = q.K_nope[p] and W_v (sum_p w_p a_p ql_p) + b_v = sum_p w_p V[p] (the
+// weights w sum to one). Then a flash-attention kernel per (64-token query block, head) runs
+// mma.sync m16n8k16 with fp16 operands in a three-product split (x = hi + lo, x.y ~ hi.hi' + hi.lo' +
+// lo.hi'), which keeps about 22 significant bits, close to the fp32 arithmetic of the decode path.
 
-__global__ void __launch_bounds__(kAttnThreads) mla_attention_kernel(IvbLayerDesc L, const float* ent, int pos0, int d, int Lt,
-                                                                     int H, int hd, int rope, int nope, int max_len, int lpad,
-                                                                     int rpad, float* y) {
-  __shared__ float qa[512];
-  __shared__ float qn[256];
-  __shared__ float qr[128];
-  __shared__ float sc[kAttnTile];
-  __shared__ float part[4][512];
-  __shared__ float red[64];
-  const int t = blockIdx.x, h = blockIdx.y, pos = pos0 + t;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int ld = d + Lt + H * rope;
-  const float* q = ent + static_cast<size_t>(t) * ld + h * hd;
+// Latent codes of positions 0..P-1 into the tiled GEMM activation layout (ldq = latent rounded to 128).
+__global__ void latent_tile_kernel(const int8_t* latent_q, int lpad, int Lt, int P, int ldq, int8_t* q8) {
+  const int chunks = ldq >> 4;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= P * chunks) return;
+  const int p = i / chunks, k = i - p * chunks;
+  // byte 4f + b of the chunk holds input 16k + 4b + f
+  uint32_t o[4];
+#pragma unroll
+  for (int f = 0; f < 4; ++f) {
+    uint32_t w = 0u;
+#pragma unroll
+    for (int b = 0; b < 4; ++b) {
+      const int j = (k << 4) + 4 * b + f;
+      w |= (j < Lt ? static_cast<uint32_t>(static_cast<uint8_t>(latent_q[static_cast<size_t>(p) * lpad + j])) : 0u) << (8 * b);
+    }
+    o[f] = w;
+  }
+  *reinterpret_cast<uint4*>(q8 + q8_chunk_offset(p, k, ldq)) = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// x = hi + lo with hi, lo fp16 (packed pairs)
+__device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
+  const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
+  const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
+  hi = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
+  lo = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
+}
+
+constexpr int kFaTok = 64;      // query tokens per CTA (4 warps x 16)
+constexpr int kFaPos = 64;      // key positions per tile
+constexpr int kFaThreads = 128;
+
+// Grid (ceil(count / 64), heads). DK: query/key dims (nope + rope) padded to 16; DV: value dims padded to 16.
+// q from the entry rows (scaled by attn_scale, rope part rotated); keys [K_nope | k_rope cache]; values V.
+template <int DK, int DV>
+__global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDesc L, const float* ent, int ld_ent,
+                                                                     const float* knope, const float* vbuf, int start,
+                                                                     int count, int d, int H, int hd, int rope, int nope,
+                                                                     int max_len, int rpad, float* y) {
+  constexpr int kKs = DK + 8;       // key tile row stride (halves)
+  constexpr int kVs = kFaPos + 8;   // transposed value tile row stride (halves)
+  extern __shared__ __align__(16) unsigned char fa_smem[];
+  __half* k_hi = reinterpret_cast<__half*>(fa_smem);
+  __half* k_lo = k_hi + kFaPos * kKs;
+  __half* v_hi = k_lo + kFaPos * kKs;
+  __half* v_lo = v_hi + DV * kVs;
+  float* qs = reinterpret_cast<float*>(fa_smem);  // the query block, before the first key tile
+  const int h = blockIdx.y, tq0 = blockIdx.x * kFaTok;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, grp = lane >> 2, tig = lane & 3;
   const float scl = L.attn_scale;
-  const float* rtab = L.rope + static_cast<size_t>(pos) * rope;
-  for (int jr = tid; jr < rope / 2; jr += kAttnThreads) {
-    const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
-    const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
-    qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
-    qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
-  }
-  for (int e = tid; e < nope; e += kAttnThreads) qn[e] = q[e] * scl;
-  __syncthreads();
-  // absorbed query
-  const IvbTernary& kn = L.k_nope_up;
-  for (int j = tid; j < Lt; j += kAttnThreads) {
-    float acc = 0.0f;
-    for (int e = 0; e < nope; ++e) {
-      const size_t r = static_cast<size_t>(h) * nope + e;
-      acc = fmaf(qn[e], code_value(kn.packed + r * kn.row_bytes, j) * h2f(__ldg(kn.scales + r * kn.scale_stride + (j >> 7))), acc);
-    }
-    qa[j] = acc;
-  }
-  float qb = 0.0f;
-  if (kn.bias != nullptr) {
-    float pp = 0.0f;
-    for (int e = tid; e < nope; e += kAttnThreads) pp = fmaf(qn[e], __ldg(kn.bias + h * nope + e), pp);
-    pp = warp_sum(pp);
-    if (lane == 0) red[warp] = pp;
-    __syncthreads();
-    qb = red[0];
-    for (int w = 1; w < kAttnThreads / 32; ++w) qb += red[w];
-  }
-  __syncthreads();
-  const int sub = tid & 7, grp = tid >> 3;  // 16 position groups of 8 lanes
-  const int P = pos + 1;
-  float m_run = -INFINITY, l_run = 0.0f;
-  float u[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) u[i] = 0.0f;
-  for (int start = 0; start < P; start += kAttnTile) {
-    const int count = min(kAttnTile, P - start);
-    for (int k = grp; k - grp < count; k += kAttnThreads / 8) {
-      const bool valid = k < count;
-      const int p = start + (valid ? k : 0);
-      const int8_t* ql = L.latent_q + static_cast<size_t>(p) * lpad;
-      float dot = 0.0f;
-      for (int j0 = sub * 16; j0 < Lt; j0 += 128) {
-        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(ql + j0));
-        float f[16];
-        bytes_to_f32(w.x, f);
-        bytes_to_f32(w.y, f + 4);
-        bytes_to_f32(w.z, f + 8);
-        bytes_to_f32(w.w, f + 12);
-#pragma unroll
-        for (int i = 0; i < 16; ++i) dot = fmaf(qa[j0 + i], f[i], dot);
-      }
-      float rp = 0.0f;
-      const uint16_t* kr = L.k_rope_cache + (static_cast<size_t>(h) * max_len + p) * rpad;
-      for (int r = sub; r < rope; r += 8) rp = fmaf(qr[r], h2f(__ldcg(kr + r)), rp);
-      float total = fmaf(__ldcg(L.latent_scale + p), dot, rp);
-      total += __shfl_xor_sync(kFull, total, 4);
-      total += __shfl_xor_sync(kFull, total, 2);
-      total += __shfl_xor_sync(kFull, total, 1);
-      if (valid && sub == 0) sc[k] = total + qb;
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int k = tid; k < count; k += kAttnThreads) mx = fmaxf(mx, sc[k]);
-    mx = warp_max(mx);
-    if (lane == 0) red[warp] = mx;
-    __syncthreads();
-    mx = red[0];
-    for (int w = 1; w < kAttnThreads / 32; ++w) mx = fmaxf(mx, red[w]);
-    __syncthreads();
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-    float ls = 0.0f;
-    for (int k = tid; k < count; k += kAttnThreads) {
-      const float e = expf(sc[k] - m_new);
-      sc[k] = e * __ldcg(L.latent_scale + start + k);
-      ls += e;
-    }
-    ls = warp_sum(ls);
-    if (lane == 0) red[warp] = ls;
-    __syncthreads();
-    ls = red[0];
-    for (int w = 1; w < kAttnThreads / 32; ++w) ls += red[w];
-    l_run = l_run * corr + ls;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) u[i] *= corr;
-    for (int k = warp; k < count; k += kAttnThreads / 32) {
-      const int8_t* ql = L.latent_q + static_cast<size_t>(start + k) * lpad;
-      const float ea = sc[k];
-#pragma unroll
-      for (int pc = 0; pc < 2; ++pc) {
-        const int j0 = pc * 256 + lane * 8;
-        if (j0 < Lt) {
-          const uint2 w = __ldcg(reinterpret_cast<const uint2*>(ql + j0));
-          float f[8];
-          bytes_to_f32(w.x, f);
-          bytes_to_f32(w.y, f + 4);
-#pragma unroll
-          for (int i = 0; i < 8; ++i) u[pc * 8 + i] = fmaf(ea, f[i], u[pc * 8 + i]);
-        }
+  // queries of the block: [nope part * scale | rotated rope part * scale | 0 padding]
+  for (int i = tid; i < kFaTok * DK; i += kFaThreads) {
+    const int tl = i / DK, e = i - tl * DK, t = tq0 + tl;
+    float v = 0.0f;
+    if (t < count && e < nope + rope) {
+      const float* q = ent + static_cast<size_t>(t) * ld_ent + h * hd;
+      if (e < nope) {
+        v = q[e] * scl;
+      } else {
+        const int jr = (e - nope) >> 1;
+        const float* rt = L.rope + static_cast<size_t>(start + t) * rope;
+        const float cs = __ldg(rt + 2 * jr), sn = __ldg(rt + 2 * jr + 1);
+        const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
+        v = (((e - nope) & 1) == 0 ? q0 * cs - q1 * sn : q0 * sn + q1 * cs) * scl;
       }
     }
-    m_run = m_new;
+    qs[i] = v;
+  }
+  __syncthreads();
+  // this warp's 16 query rows as A fragments (hi, lo) per 16-dim step
+  uint32_t qh[DK / 16][4], ql[DK / 16][4];
+  const int r0 = 16 * warp + grp;
+#pragma unroll
+  for (int kk = 0; kk < DK / 16; ++kk) {
+    const int c = 16 * kk + 2 * tig;
+    split2(qs[r0 * DK + c], qs[r0 * DK + c + 1], qh[kk][0], ql[kk][0]);
+    split2(qs[(r0 + 8) * DK + c], qs[(r0 + 8) * DK + c + 1], qh[kk][1], ql[kk][1]);
+    split2(qs[r0 * DK + c + 8], qs[r0 * DK + c + 9], qh[kk][2], ql[kk][2]);
+    split2(qs[(r0 + 8) * DK + c + 8], qs[(r0 + 8) * DK + c + 9], qh[kk][3], ql[kk][3]);
+  }
+  float o[DV / 8][4];
+#pragma unroll
+  for (int n = 0; n < DV / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
+  const int pos_a = start + tq0 + r0, pos_b = pos_a + 8;  // positions of this thread's two query rows
+  const int t_last = min(count, tq0 + kFaTok) - 1;
+  const int p_end = start + t_last + 1;                   // keys 0..p_end-1 serve the block
+  const int warp_last = start + min(count - 1, tq0 + 16 * warp + 15);
+  for (int p0 = 0; p0 < p_end; p0 += kFaPos) {
+    __syncthreads();  // the previous tile is no longer read
+    for (int i = tid; i < kFaPos * DK; i += kFaThreads) {
+      const int pl = i / DK, e = i - pl * DK, p = p0 + pl;
+      float v = 0.0f;
+      if (p < p_end) {
+        if (e < nope) v = knope[static_cast<size_t>(p) * H * nope + h * nope + e];
+        else if (e < nope + rope) v = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + p) * rpad + (e - nope)]);
+      }
+      const __half hv = __float2half_rn(v);
+      k_hi[pl * kKs + e] = hv;
+      k_lo[pl * kKs + e] = __float2half_rn(v - __half2float(hv));
+    }
+    for (int i = tid; i < kFaPos * DV; i += kFaThreads) {
+      const int pl = i / DV, e = i - pl * DV, p = p0 + pl;
+      const float v = (p < p_end && e < hd) ? vbuf[static_cast<size_t>(p) * d + h * hd + e] : 0.0f;
+      const __half hv = __float2half_rn(v);
+      v_hi[e * kVs + pl] = hv;
+      v_lo[e * kVs + pl] = __float2half_rn(v - __half2float(hv));
+    }
     __syncthreads();
-  }
+    if (p0 > warp_last) continue;  // every key of the tile lies after this warp's queries
+    float s[kFaPos / 8][4];
 #pragma unroll
-  for (int pc = 0; pc < 2; ++pc) {
-    const int j0 = pc * 256 + lane * 8;
+    for (int n = 0; n < kFaPos / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
 #pragma unroll
-    for (int i = 0; i < 8; ++i)
-      if (j0 + i < Lt) part[warp][j0 + i] = u[pc * 8 + i];
+    for (int kk = 0; kk < DK / 16; ++kk) {
+#pragma unroll
+      for (int n = 0; n < kFaPos / 8; ++n) {
+        const int row = (8 * n + grp) * kKs + 16 * kk + 2 * tig;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + row);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + row);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
+        mma16816(s[n], qh[kk], bh0, bh1);
+        mma16816(s[n], qh[kk], bl0, bl1);
+        mma16816(s[n], ql[kk], bh0, bh1);
+      }
+    }
+    // causal mask and online softmax (rows pos_a: s[n][0..1], pos_b: s[n][2..3])
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < kFaPos / 8; ++n) {
+      const int p = p0 + 8 * n + 2 * tig;
+      if (p > pos_a) s[n][0] = -INFINITY;
+      if (p + 1 > pos_a) s[n][1] = -INFINITY;
+      if (p > pos_b) s[n][2] = -INFINITY;
+      if (p + 1 > pos_b) s[n][3] = -INFINITY;
+      mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
+      mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
+    }
+    float corr[2], sum[2] = {0.0f, 0.0f};
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
+      mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 2));
+      const float m_new = fmaxf(m_run[r], mx[r]);
+      corr[r] = m_new == -INFINITY ? 1.0f : expf(m_run[r] - m_new);
+      m_run[r] = m_new;
+    }
+    uint32_t ph[kFaPos / 16][4], pl2[kFaPos / 16][4];
+#pragma unroll
+    for (int n = 0; n < kFaPos / 8; ++n) {
+      float e[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const float m = m_run[c >> 1];
+        e[c] = (s[n][c] == -INFINITY) ? 0.0f : expf(s[n][c] - m);
+      }
+      sum[0] += e[0] + e[1];
+      sum[1] += e[2] + e[3];
+      // C fragment of position tile n -> A fragment of k-step n / 2 (regs 0, 1 or 2, 3)
+      split2(e[0], e[1], ph[n >> 1][(n & 1) * 2], pl2[n >> 1][(n & 1) * 2]);
+      split2(e[2], e[3], ph[n >> 1][(n & 1) * 2 + 1], pl2[n >> 1][(n & 1) * 2 + 1]);
+    }
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      sum[r] += __shfl_xor_sync(kFull, sum[r], 1);
+      sum[r] += __shfl_xor_sync(kFull, sum[r], 2);
+      l_run[r] = l_run[r] * corr[r] + sum[r];
+    }
+#pragma unroll
+    for (int n = 0; n < DV / 8; ++n) {
+      o[n][0] *= corr[0];
+      o[n][1] *= corr[0];
+      o[n][2] *= corr[1];
+      o[n][3] *= corr[1];
+    }
+#pragma unroll
+    for (int kk = 0; kk < kFaPos / 16; ++kk) {
+#pragma unroll
+      for (int n = 0; n < DV / 8; ++n) {
+        const int row = (8 * n + grp) * kVs + 16 * kk + 2 * tig;
+        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + row);
+        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
+        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + row);
+        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
+        mma16816(o[n], ph[kk], bh0, bh1);
+        mma16816(o[n], ph[kk], bl0, bl1);
+        mma16816(o[n], pl2[kk], bh0, bh1);
+      }
+    }
   }
-  __syncthreads();
-  for (int j = tid; j < Lt; j += kAttnThreads) {
-    float v = part[0][j];
-    for (int w = 1; w < kAttnThreads / 32; ++w) v += part[w][j];
-    qa[j] = v;  // the weighted latent sum u
-  }
-  __syncthreads();
-  const IvbTernary& vu = L.v_up;
-  const float inv_l = 1.0f / l_run;
-  for (int e = tid; e < hd; e += kAttnThreads) {
-    const size_t r = static_cast<size_t>(h) * hd + e;
-    float acc = 0.0f;
-    for (int j = 0; j < Lt; ++j)
-      acc = fmaf(code_value(vu.packed + r * vu.row_bytes, j) * h2f(__ldg(vu.scales + r * vu.scale_stride + (j >> 7))), qa[j], acc);
-    float o = acc * inv_l;
-    if (vu.bias != nullptr) o += __ldg(vu.bias + r);
-    y[static_cast<size_t>(t) * d + h * hd + e] = o;
+  const int ta = tq0 + r0, tb = ta + 8;
+  const float inv_a = 1.0f / l_run[0], inv_b = 1.0f / l_run[1];
+#pragma unroll
+  for (int n = 0; n < DV / 8; ++n) {
+    const int e = 8 * n + 2 * tig;
+    if (ta < count) {
+      if (e < hd) y[static_cast<size_t>(ta) * d + h * hd + e] = o[n][0] * inv_a;
+      if (e + 1 < hd) y[static_cast<size_t>(ta) * d + h * hd + e + 1] = o[n][1] * inv_a;
+    }
+    if (tb < count) {
+      if (e < hd) y[static_cast<size_t>(tb) * d + h * hd + e] = o[n][2] * inv_b;
+      if (e + 1 < hd) y[static_cast<size_t>(tb) * d + h * hd + e + 1] = o[n][3] * inv_b;
+    }
   }
 }
 
@@ -389,8 +461,31 @@ __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_
   position[0] = pos_end;
 }
 
+template <int DK>
+int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf, int start,
+                  int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad, float* y, cudaStream_t s) {
+  const size_t smem = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
+  IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK, DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  flash_attention_kernel<DK, DK><<<dim3((count + kFaTok - 1) / kFaTok, H), kFaThreads, smem, s>>>(
+      L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+// Query/key dims (nope + rope) and value dims (head_dim) are equal for these models; both padded to 16.
+int32_t launch_flash_attention(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf,
+                               int start, int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad,
+                               float* y, cudaStream_t s) {
+  const int dk = std::max(nope + rope, hd);
+  if (dk <= 16) return launch_fa<16>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 32) return launch_fa<32>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 64) return launch_fa<64>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 128) return launch_fa<128>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  return fail(IVB_EINVAL, "ivb_decoder_prefill: head dims %d beyond the attention kernel", dk);
+}
+
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, err, total;
+  size_t resid, ent, y, h, q8, scale, err, kvq8, knope, vbuf, total;
   int ldq, groups, ld_ent;
 };
 
@@ -416,6 +511,13 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.q8 = take((T + 127) / 128 * 128 * L.ldq);  // whole 128-token tiles
   L.scale = take(T * 4);
   L.err = take(16);
+  // latent attention: the cached latent of every position in the GEMM layout, and its keys and values
+  bool mla = false;
+  for (int i = 0; i < md.num_layers; ++i) mla = mla || layers[i].kind == IVB_MLA;
+  const size_t P = mla ? static_cast<size_t>(md.max_len) : 0;
+  L.kvq8 = take((P + 127) / 128 * 128 * ((md.latent_dim + 127) / 128 * 128));
+  L.knope = take(P * md.heads * md.nope_dim * 4);
+  L.vbuf = take(P * d * 4);
   L.total = o;
   return L;
 }
@@ -458,6 +560,9 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   float* ent = reinterpret_cast<float*>(ws + W.ent);
   float* y = reinterpret_cast<float*>(ws + W.y);
   float* hbuf = reinterpret_cast<float*>(ws + W.h);
+  int8_t* kvq8 = reinterpret_cast<int8_t*>(ws + W.kvq8);
+  float* knope = reinterpret_cast<float*>(ws + W.knope);
+  float* vbuf = reinterpret_cast<float*>(ws + W.vbuf);
   int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
   float* scale = reinterpret_cast<float*>(ws + W.scale);
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
@@ -494,9 +599,17 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
     } else {
       mla_cache_kernel<<<count, kThreads, 0, s>>>(L, ent, start_position, d, Lt, H, rope, md.max_len, lpad, rpad, md.act_eps);
       IVB_CUDA(cudaGetLastError());
-      mla_attention_kernel<<<dim3(count, H), kAttnThreads, 0, s>>>(L, ent, start_position, d, Lt, H, hd, rope, nope,
-                                                                  md.max_len, lpad, rpad, y);
+      // keys and values of positions 0..P-1 from the cached latent (earlier chunks included)
+      const int P = start_position + count, ldl = (Lt + 127) / 128 * 128;
+      const int chunks = P * (ldl >> 4);
+      latent_tile_kernel<<<(chunks + 255) / 256, 256, 0, s>>>(L.latent_q, lpad, Lt, P, ldl, kvq8);
       IVB_CUDA(cudaGetLastError());
+      if (int32_t rc = ivb_ternary_gemm(&L.k_nope_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, knope, H * nope, err, stream))
+        return rc;
+      if (int32_t rc = ivb_ternary_gemm(&L.v_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, vbuf, d, err, stream)) return rc;
+      if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, start_position, count, d, H, hd, rope, nope,
+                                              md.max_len, rpad, y, s))
+        return rc;
     }
     if (int32_t rc = quant(y, d, nullptr, 0.0f)) return rc;
     if (int32_t rc = gemm(L.out, IVB_EPI_RESIDUAL, resid, d)) return rc;
