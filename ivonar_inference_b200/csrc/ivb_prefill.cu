@@ -277,29 +277,75 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
   lo = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
 }
 
-constexpr int kFaTok = 64;      // query tokens per CTA (4 warps x 16)
+constexpr int kFaTok = 128;     // query tokens per CTA (8 warps x 16)
 constexpr int kFaPos = 64;      // key positions per tile
-constexpr int kFaThreads = 128;
+constexpr int kFaThreads = 256;
 
-// Grid (ceil(count / 64), heads). DK: query/key dims (nope + rope) padded to 16; DV: value dims padded to 16.
-// q from the entry rows (scaled by attn_scale, rope part rotated); keys [K_nope | k_rope cache]; values V.
-template <int DK, int DV>
+// Keys and values of positions 0..P-1 of one layer as fp16 hi/lo pairs, laid out for whole-tile copies:
+// kh/kl [H][Ppad][DK] (K_nope then k_rope, zero padded), vh/vl [H][DV][Ppad] (transposed, zero padded),
+// Ppad = P rounded up to kFaPos. One thread per (head, position, 8 dims).
+template <int DK>
+__global__ void kv_split_kernel(IvbLayerDesc L, const float* knope, const float* vbuf, int P, int Ppad, int d, int H,
+                                int hd, int rope, int nope, int max_len, int rpad, __half* kh, __half* kl, __half* vh,
+                                __half* vl) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_head = Ppad * (DK / 8);
+  if (i >= H * per_head) return;
+  const int h = i / per_head, rest = i - h * per_head, p = rest / (DK / 8), e0 = (rest - p * (DK / 8)) * 8;
+  uint32_t khw[4], klw[4], vhw[8], vlw[8];
+  float kv[8], vv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = e0 + j;
+    float k = 0.0f, v = 0.0f;
+    if (p < P) {
+      if (e < nope) k = knope[static_cast<size_t>(p) * H * nope + h * nope + e];
+      else if (e < nope + rope) k = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + p) * rpad + (e - nope)]);
+      if (e < hd) v = vbuf[static_cast<size_t>(p) * d + h * hd + e];
+    }
+    kv[j] = k;
+    vv[j] = v;
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) split2(kv[2 * j], kv[2 * j + 1], khw[j], klw[j]);
+  const size_t ko = (static_cast<size_t>(h) * Ppad + p) * DK + e0;
+  *reinterpret_cast<uint4*>(kh + ko) = make_uint4(khw[0], khw[1], khw[2], khw[3]);
+  *reinterpret_cast<uint4*>(kl + ko) = make_uint4(klw[0], klw[1], klw[2], klw[3]);
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (e0 + j >= DK) break;
+    const __half hv = __float2half_rn(vv[j]);
+    const size_t vo = (static_cast<size_t>(h) * DK + e0 + j) * Ppad + p;
+    vh[vo] = hv;
+    vl[vo] = __float2half_rn(vv[j] - __half2float(hv));
+  }
+  (void)vhw;
+  (void)vlw;
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// Grid (ceil(count / 128), heads). DK: query/key dims (nope + rope) padded to 16 (= value dims padded).
+// q from the entry rows (scaled by attn_scale, rope part rotated); keys and values from kv_split_kernel.
+// Tiles of 64 positions are double-buffered with cp.async.
+template <int DK>
 __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDesc L, const float* ent, int ld_ent,
-                                                                     const float* knope, const float* vbuf, int start,
-                                                                     int count, int d, int H, int hd, int rope, int nope,
-                                                                     int max_len, int rpad, float* y) {
+                                                                     const __half* kh, const __half* kl,
+                                                                     const __half* vh, const __half* vl, int Ppad,
+                                                                     int start, int count, int d, int hd, int rope,
+                                                                     int nope, float* y) {
+  constexpr int DV = DK;
   constexpr int kKs = DK + 8;       // key tile row stride (halves)
   constexpr int kVs = kFaPos + 8;   // transposed value tile row stride (halves)
+  constexpr int kTileHalves = 2 * kFaPos * kKs + 2 * DV * kVs;  // k_hi, k_lo, v_hi, v_lo
   extern __shared__ __align__(16) unsigned char fa_smem[];
-  __half* k_hi = reinterpret_cast<__half*>(fa_smem);
-  __half* k_lo = k_hi + kFaPos * kKs;
-  __half* v_hi = k_lo + kFaPos * kKs;
-  __half* v_lo = v_hi + DV * kVs;
+  __half* tiles = reinterpret_cast<__half*>(fa_smem);
   float* qs = reinterpret_cast<float*>(fa_smem);  // the query block, before the first key tile
   const int h = blockIdx.y, tq0 = blockIdx.x * kFaTok;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, grp = lane >> 2, tig = lane & 3;
   const float scl = L.attn_scale;
-  // queries of the block: [nope part * scale | rotated rope part * scale | 0 padding]
   for (int i = tid; i < kFaTok * DK; i += kFaThreads) {
     const int tl = i / DK, e = i - tl * DK, t = tq0 + tl;
     float v = 0.0f;
@@ -318,7 +364,6 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
     qs[i] = v;
   }
   __syncthreads();
-  // this warp's 16 query rows as A fragments (hi, lo) per 16-dim step
   uint32_t qh[DK / 16][4], ql[DK / 16][4];
   const int r0 = 16 * warp + grp;
 #pragma unroll
@@ -329,6 +374,31 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
     split2(qs[r0 * DK + c + 8], qs[r0 * DK + c + 9], qh[kk][2], ql[kk][2]);
     split2(qs[(r0 + 8) * DK + c + 8], qs[(r0 + 8) * DK + c + 9], qh[kk][3], ql[kk][3]);
   }
+  __syncthreads();  // qs is overwritten by the tiles
+  const __half* khh = kh + static_cast<size_t>(h) * Ppad * DK;
+  const __half* klh = kl + static_cast<size_t>(h) * Ppad * DK;
+  const __half* vhh = vh + static_cast<size_t>(h) * DV * Ppad;
+  const __half* vlh = vl + static_cast<size_t>(h) * DV * Ppad;
+  auto load_tile = [&](int buf, int p0) {
+    __half* base = tiles + buf * kTileHalves;
+    __half* khs = base;
+    __half* kls = khs + kFaPos * kKs;
+    __half* vhs = kls + kFaPos * kKs;
+    __half* vls = vhs + DV * kVs;
+    for (int i = tid; i < kFaPos * (DK / 8); i += kFaThreads) {
+      const int pl = i / (DK / 8), c = i - pl * (DK / 8);
+      const size_t src = static_cast<size_t>(p0 + pl) * DK + 8 * c;
+      cp_async16(khs + pl * kKs + 8 * c, khh + src);
+      cp_async16(kls + pl * kKs + 8 * c, klh + src);
+    }
+    for (int i = tid; i < DV * (kFaPos / 8); i += kFaThreads) {
+      const int e = i / (kFaPos / 8), c = i - e * (kFaPos / 8);
+      const size_t src = static_cast<size_t>(e) * Ppad + p0 + 8 * c;
+      cp_async16(vhs + e * kVs + 8 * c, vhh + src);
+      cp_async16(vls + e * kVs + 8 * c, vlh + src);
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
   float o[DV / 8][4];
 #pragma unroll
   for (int n = 0; n < DV / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
@@ -337,108 +407,104 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
   const int t_last = min(count, tq0 + kFaTok) - 1;
   const int p_end = start + t_last + 1;                   // keys 0..p_end-1 serve the block
   const int warp_last = start + min(count - 1, tq0 + 16 * warp + 15);
-  for (int p0 = 0; p0 < p_end; p0 += kFaPos) {
-    __syncthreads();  // the previous tile is no longer read
-    for (int i = tid; i < kFaPos * DK; i += kFaThreads) {
-      const int pl = i / DK, e = i - pl * DK, p = p0 + pl;
-      float v = 0.0f;
-      if (p < p_end) {
-        if (e < nope) v = knope[static_cast<size_t>(p) * H * nope + h * nope + e];
-        else if (e < nope + rope) v = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + p) * rpad + (e - nope)]);
-      }
-      const __half hv = __float2half_rn(v);
-      k_hi[pl * kKs + e] = hv;
-      k_lo[pl * kKs + e] = __float2half_rn(v - __half2float(hv));
-    }
-    for (int i = tid; i < kFaPos * DV; i += kFaThreads) {
-      const int pl = i / DV, e = i - pl * DV, p = p0 + pl;
-      const float v = (p < p_end && e < hd) ? vbuf[static_cast<size_t>(p) * d + h * hd + e] : 0.0f;
-      const __half hv = __float2half_rn(v);
-      v_hi[e * kVs + pl] = hv;
-      v_lo[e * kVs + pl] = __float2half_rn(v - __half2float(hv));
+  const int tiles_n = (p_end + kFaPos - 1) / kFaPos;
+  load_tile(0, 0);
+  for (int it = 0; it < tiles_n; ++it) {
+    const int p0 = it * kFaPos, buf = it & 1;
+    if (it + 1 < tiles_n) {
+      load_tile(buf ^ 1, p0 + kFaPos);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
     }
     __syncthreads();
-    if (p0 > warp_last) continue;  // every key of the tile lies after this warp's queries
-    float s[kFaPos / 8][4];
+    const __half* k_hi = tiles + buf * kTileHalves;
+    const __half* k_lo = k_hi + kFaPos * kKs;
+    const __half* v_hi = k_lo + kFaPos * kKs;
+    const __half* v_lo = v_hi + DV * kVs;
+    if (p0 <= warp_last) {
+      float s[kFaPos / 8][4];
 #pragma unroll
-    for (int n = 0; n < kFaPos / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
+      for (int n = 0; n < kFaPos / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
 #pragma unroll
-    for (int kk = 0; kk < DK / 16; ++kk) {
+      for (int kk = 0; kk < DK / 16; ++kk) {
+#pragma unroll
+        for (int n = 0; n < kFaPos / 8; ++n) {
+          const int row = (8 * n + grp) * kKs + 16 * kk + 2 * tig;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + row);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + row);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
+          mma16816(s[n], qh[kk], bh0, bh1);
+          mma16816(s[n], qh[kk], bl0, bl1);
+          mma16816(s[n], ql[kk], bh0, bh1);
+        }
+      }
+      // causal mask and online softmax (rows pos_a: s[n][0..1], pos_b: s[n][2..3])
+      float mx[2] = {-INFINITY, -INFINITY};
 #pragma unroll
       for (int n = 0; n < kFaPos / 8; ++n) {
-        const int row = (8 * n + grp) * kKs + 16 * kk + 2 * tig;
-        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + row);
-        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
-        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + row);
-        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
-        mma16816(s[n], qh[kk], bh0, bh1);
-        mma16816(s[n], qh[kk], bl0, bl1);
-        mma16816(s[n], ql[kk], bh0, bh1);
+        const int p = p0 + 8 * n + 2 * tig;
+        if (p > pos_a) s[n][0] = -INFINITY;
+        if (p + 1 > pos_a) s[n][1] = -INFINITY;
+        if (p > pos_b) s[n][2] = -INFINITY;
+        if (p + 1 > pos_b) s[n][3] = -INFINITY;
+        mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
+        mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
       }
-    }
-    // causal mask and online softmax (rows pos_a: s[n][0..1], pos_b: s[n][2..3])
-    float mx[2] = {-INFINITY, -INFINITY};
+      float corr[2], sum[2] = {0.0f, 0.0f};
 #pragma unroll
-    for (int n = 0; n < kFaPos / 8; ++n) {
-      const int p = p0 + 8 * n + 2 * tig;
-      if (p > pos_a) s[n][0] = -INFINITY;
-      if (p + 1 > pos_a) s[n][1] = -INFINITY;
-      if (p > pos_b) s[n][2] = -INFINITY;
-      if (p + 1 > pos_b) s[n][3] = -INFINITY;
-      mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
-      mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
-    }
-    float corr[2], sum[2] = {0.0f, 0.0f};
-#pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
-      mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 2));
-      const float m_new = fmaxf(m_run[r], mx[r]);
-      corr[r] = m_new == -INFINITY ? 1.0f : expf(m_run[r] - m_new);
-      m_run[r] = m_new;
-    }
-    uint32_t ph[kFaPos / 16][4], pl2[kFaPos / 16][4];
-#pragma unroll
-    for (int n = 0; n < kFaPos / 8; ++n) {
-      float e[4];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        const float m = m_run[c >> 1];
-        e[c] = (s[n][c] == -INFINITY) ? 0.0f : expf(s[n][c] - m);
+      for (int r = 0; r < 2; ++r) {
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
+        mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 2));
+        const float m_new = fmaxf(m_run[r], mx[r]);
+        corr[r] = m_new == -INFINITY ? 1.0f : expf(m_run[r] - m_new);
+        m_run[r] = m_new;
       }
-      sum[0] += e[0] + e[1];
-      sum[1] += e[2] + e[3];
-      // C fragment of position tile n -> A fragment of k-step n / 2 (regs 0, 1 or 2, 3)
-      split2(e[0], e[1], ph[n >> 1][(n & 1) * 2], pl2[n >> 1][(n & 1) * 2]);
-      split2(e[2], e[3], ph[n >> 1][(n & 1) * 2 + 1], pl2[n >> 1][(n & 1) * 2 + 1]);
-    }
+      uint32_t ph[kFaPos / 16][4], pl2[kFaPos / 16][4];
 #pragma unroll
-    for (int r = 0; r < 2; ++r) {
-      sum[r] += __shfl_xor_sync(kFull, sum[r], 1);
-      sum[r] += __shfl_xor_sync(kFull, sum[r], 2);
-      l_run[r] = l_run[r] * corr[r] + sum[r];
-    }
+      for (int n = 0; n < kFaPos / 8; ++n) {
+        float e[4];
 #pragma unroll
-    for (int n = 0; n < DV / 8; ++n) {
-      o[n][0] *= corr[0];
-      o[n][1] *= corr[0];
-      o[n][2] *= corr[1];
-      o[n][3] *= corr[1];
-    }
+        for (int c = 0; c < 4; ++c) {
+          const float m = m_run[c >> 1];
+          e[c] = (s[n][c] == -INFINITY) ? 0.0f : expf(s[n][c] - m);
+        }
+        sum[0] += e[0] + e[1];
+        sum[1] += e[2] + e[3];
+        // C fragment of position tile n -> A fragment of k-step n / 2 (regs 0, 1 or 2, 3)
+        split2(e[0], e[1], ph[n >> 1][(n & 1) * 2], pl2[n >> 1][(n & 1) * 2]);
+        split2(e[2], e[3], ph[n >> 1][(n & 1) * 2 + 1], pl2[n >> 1][(n & 1) * 2 + 1]);
+      }
 #pragma unroll
-    for (int kk = 0; kk < kFaPos / 16; ++kk) {
+      for (int r = 0; r < 2; ++r) {
+        sum[r] += __shfl_xor_sync(kFull, sum[r], 1);
+        sum[r] += __shfl_xor_sync(kFull, sum[r], 2);
+        l_run[r] = l_run[r] * corr[r] + sum[r];
+      }
 #pragma unroll
       for (int n = 0; n < DV / 8; ++n) {
-        const int row = (8 * n + grp) * kVs + 16 * kk + 2 * tig;
-        const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + row);
-        const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
-        const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + row);
-        const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
-        mma16816(o[n], ph[kk], bh0, bh1);
-        mma16816(o[n], ph[kk], bl0, bl1);
-        mma16816(o[n], pl2[kk], bh0, bh1);
+        o[n][0] *= corr[0];
+        o[n][1] *= corr[0];
+        o[n][2] *= corr[1];
+        o[n][3] *= corr[1];
+      }
+#pragma unroll
+      for (int kk = 0; kk < kFaPos / 16; ++kk) {
+#pragma unroll
+        for (int n = 0; n < DV / 8; ++n) {
+          const int row = (8 * n + grp) * kVs + 16 * kk + 2 * tig;
+          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + row);
+          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
+          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + row);
+          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
+          mma16816(o[n], ph[kk], bh0, bh1);
+          mma16816(o[n], ph[kk], bl0, bl1);
+          mma16816(o[n], pl2[kk], bh0, bh1);
+        }
       }
     }
+    __syncthreads();  // buffer buf is refilled by the next iteration's prefetch
   }
   const int ta = tq0 + r0, tb = ta + 8;
   const float inv_a = 1.0f / l_run[0], inv_b = 1.0f / l_run[1];
@@ -456,36 +522,45 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
   }
 }
 
-__global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_end, int64_t* token, int64_t* position) {
-  token[0] = tokens[count - 1];
-  position[0] = pos_end;
-}
-
 template <int DK>
-int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf, int start,
-                  int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad, float* y, cudaStream_t s) {
-  const size_t smem = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
-  IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK, DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  flash_attention_kernel<DK, DK><<<dim3((count + kFaTok - 1) / kFaTok, H), kFaThreads, smem, s>>>(
-      L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y);
+int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf,
+                  __half* kvh, int start, int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad,
+                  float* y, cudaStream_t s) {
+  const int P = start + count, Ppad = (P + kFaPos - 1) / kFaPos * kFaPos;
+  const size_t per = static_cast<size_t>(H) * Ppad * DK;  // halves per split array
+  __half *kh = kvh, *kl = kh + per, *vh = kl + per, *vl = vh + per;
+  const int threads = H * Ppad * (DK / 8);
+  kv_split_kernel<DK><<<(threads + 255) / 256, 256, 0, s>>>(L, knope, vbuf, P, Ppad, d, H, hd, rope, nope, max_len, rpad,
+                                                            kh, kl, vh, vl);
+  IVB_CUDA(cudaGetLastError());
+  const size_t tile = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
+  const size_t smem = std::max(2 * tile, static_cast<size_t>(kFaTok) * DK * 4);
+  IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  flash_attention_kernel<DK><<<dim3((count + kFaTok - 1) / kFaTok, H), kFaThreads, smem, s>>>(
+      L, ent, ld_ent, kh, kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y);
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
 
 // Query/key dims (nope + rope) and value dims (head_dim) are equal for these models; both padded to 16.
 int32_t launch_flash_attention(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf,
-                               int start, int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad,
-                               float* y, cudaStream_t s) {
+                               __half* kvh, int start, int count, int d, int H, int hd, int rope, int nope, int max_len,
+                               int rpad, float* y, cudaStream_t s) {
   const int dk = std::max(nope + rope, hd);
-  if (dk <= 16) return launch_fa<16>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 32) return launch_fa<32>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 64) return launch_fa<64>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 128) return launch_fa<128>(L, ent, ld_ent, knope, vbuf, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 16) return launch_fa<16>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 32) return launch_fa<32>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 64) return launch_fa<64>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 128) return launch_fa<128>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
   return fail(IVB_EINVAL, "ivb_decoder_prefill: head dims %d beyond the attention kernel", dk);
 }
 
+__global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_end, int64_t* token, int64_t* position) {
+  token[0] = tokens[count - 1];
+  position[0] = pos_end;
+}
+
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, err, kvq8, knope, vbuf, total;
+  size_t resid, ent, y, h, q8, scale, err, kvq8, knope, vbuf, kvh, total;
   int ldq, groups, ld_ent;
 };
 
@@ -518,6 +593,9 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.kvq8 = take((P + 127) / 128 * 128 * ((md.latent_dim + 127) / 128 * 128));
   L.knope = take(P * md.heads * md.nope_dim * 4);
   L.vbuf = take(P * d * 4);
+  const int dk_raw = std::max(md.nope_dim + md.rope_dim, md.head_dim);  // padded as launch_flash_attention does
+  const size_t dk = dk_raw <= 16 ? 16 : dk_raw <= 32 ? 32 : dk_raw <= 64 ? 64 : 128;
+  L.kvh = take(4 * static_cast<size_t>(md.heads) * ((P + 63) / 64 * 64) * dk * 2);
   L.total = o;
   return L;
 }
@@ -563,6 +641,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   int8_t* kvq8 = reinterpret_cast<int8_t*>(ws + W.kvq8);
   float* knope = reinterpret_cast<float*>(ws + W.knope);
   float* vbuf = reinterpret_cast<float*>(ws + W.vbuf);
+  __half* kvh = reinterpret_cast<__half*>(ws + W.kvh);
   int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
   float* scale = reinterpret_cast<float*>(ws + W.scale);
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
@@ -607,8 +686,8 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       if (int32_t rc = ivb_ternary_gemm(&L.k_nope_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, knope, H * nope, err, stream))
         return rc;
       if (int32_t rc = ivb_ternary_gemm(&L.v_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, vbuf, d, err, stream)) return rc;
-      if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, start_position, count, d, H, hd, rope, nope,
-                                              md.max_len, rpad, y, s))
+      if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, kvh, start_position, count, d, H, hd, rope,
+                                              nope, md.max_len, rpad, y, s))
         return rc;
     }
     if (int32_t rc = quant(y, d, nullptr, 0.0f)) return rc;
