@@ -134,6 +134,7 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
   float* coef = sh;                                   // [kScanBlock][nhc][S][5]
   float* vals = coef + kScanBlock * nhc * S * 5;      // [kScanBlock][16]
   float* gates = vals + kScanBlock * 16;              // [kScanBlock][16]
+  float* ctb = gates + kScanBlock * 16;               // [kScanBlock][256]: C * Re(state) per (channel, lane)
   const int ld = 2 * d + 3 * H * S;
   const int h = live ? c / hd : h0, dd = live ? c - h * hd : 0;
   const bool on = live && sub < S;
@@ -141,7 +142,6 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
   const size_t si_idx = (static_cast<size_t>(h) * S + s) * hd + dd;
   float sr = on ? L.ssm_state[2 * si_idx] : 0.0f, si = on ? L.ssm_state[2 * si_idx + 1] : 0.0f;
   float prev = on ? L.prev_force[si_idx] : 0.0f;
-  const float skip = live ? L.skip[c] : 0.0f;
   for (int t0 = 0; t0 < T; t0 += kScanBlock) {
     const int nt = min(kScanBlock, T - t0);
     __syncthreads();
@@ -168,6 +168,8 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
     }
     __syncthreads();
     const int hl = h - h0;
+    // the recurrence alone stays on the sequential path; the per-channel sums over the state lanes and
+    // the output gate run afterwards for the whole block
     for (int tt = 0; tt < nt; ++tt) {
       const float v = vals[tt * 16 + chl];
       float contrib = 0.0f;
@@ -184,10 +186,19 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
         prev = force;
         contrib = cc * nr;
       }
+      ctb[tt * kThreads + tid] = contrib;
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nt * 16; idx += kThreads) {
+      const int tt = idx >> 4, ch = idx & 15, cc2 = c0 + ch;
+      if (cc2 >= d) continue;
+      // the xor-butterfly order of the decode kernel's 16-lane warp sum (offsets 8, 4, 2, 1), lane 0
+      const float* v = ctb + tt * kThreads + ch * 16;
+      float a[8];
 #pragma unroll
-      for (int off = 8; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
-      if (live && sub == 0)
-        y[static_cast<size_t>(t0 + tt) * d + c] = (contrib + skip * v) * sigmoid_f(gates[tt * 16 + chl]);
+      for (int i = 0; i < 8; ++i) a[i] = v[i] + v[i + 8];
+      const float sum = ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
+      y[static_cast<size_t>(t0 + tt) * d + cc2] = (sum + L.skip[cc2] * vals[idx]) * sigmoid_f(gates[idx]);
     }
   }
   if (on) {
@@ -666,7 +677,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       ssm_value_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, ld, L.conv_taps, hbuf);
       IVB_CUDA(cudaGetLastError());
       const int nhc_max = std::min(16, 15 / hd + 2);
-      const size_t smem = (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * 16) * 4;
+      const size_t smem = (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * 16 + kScanBlock * kThreads) * 4;
       IVB_CUDA(cudaFuncSetAttribute(ssm_scan_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
       ssm_scan_block_kernel<<<(d + 15) / 16, kThreads, smem, s>>>(L, ent, hbuf, count, d, H, hd, S, L.conv_taps, L.half_dt_min,
                                                                    L.half_dt_range, y);
