@@ -53,6 +53,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--only", choices=("prefill", "gemm"), default=None,
+                    help="run one secondary measurement alone (for profiler captures): a prefill of "
+                         "--prefill-tokens tokens, or the prefill GEMM on the gate/up shape")
+    ap.add_argument("--prefill-tokens", type=int, default=2048)
     return ap.parse_args()
 
 
@@ -197,7 +201,7 @@ def run_reference(args) -> None:
 INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
 
 
-def prefill_measure(device) -> dict:
+def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps: int = 20) -> dict:
     """Config 2 at b=1: prefill tok/s per prompt length, and the GEMM's int8 tensor-core throughput."""
     import ctypes
 
@@ -208,7 +212,7 @@ def prefill_measure(device) -> dict:
 
     model = synthetic.synthetic_model(synthetic.config1(seq_len=8192), seed=0)
     result: dict = {"batch": 1, "tok_s": {}, "ms": {}}
-    for length, reps in ((512, 3), (2048, 2), (8192, 1)):
+    for length, reps in lengths:
         dec = B200Decoder(model, max_len=length, device=device)
         prompt = synthetic.random_prompt(32768, length, seed=length).to(device)
         dec.prefill(prompt)
@@ -243,17 +247,19 @@ def prefill_measure(device) -> dict:
         native.check(lib.ivb_ternary_gemm(ctypes.byref(desc), q8.data_ptr(), cols, act.data_ptr(), tokens, 0,
                                           out.data_ptr(), rows, err.data_ptr(), stream), "ivb_ternary_gemm")
 
+    if gemm_reps <= 0:
+        return result
     for _ in range(3):
         gemm()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
-    for _ in range(20):
+    for _ in range(gemm_reps):
         gemm()
     end.record()
     torch.cuda.synchronize(device)
     if int(err.item()) != 0:
         raise RuntimeError("prefill GEMM reported a timeout")
-    us = start.elapsed_time(end) / 20 * 1000.0
+    us = start.elapsed_time(end) / gemm_reps * 1000.0
     tops = 2.0 * rows * cols * tokens / (us * 1e-6) / 1e12
     result["gemm"] = {"shape": f"{rows}x{cols} weights x {tokens} tokens", "us": us, "tops_int8": tops,
                       "frac_of_nominal_int8_peak": tops / INT8_NOMINAL_TOPS, "peak_tops": INT8_NOMINAL_TOPS,
@@ -375,6 +381,16 @@ def run_b200(args) -> None:
 
 def main() -> None:
     args = parse()
+    if args.only is not None:
+        import torch
+
+        torch.cuda.set_device(0)
+        device = torch.device("cuda", 0)
+        if args.only == "prefill":
+            print(json.dumps(prefill_measure(device, lengths=((args.prefill_tokens, args.steps),), gemm_reps=0)), flush=True)
+        else:
+            print(json.dumps(prefill_measure(device, lengths=(), gemm_reps=args.steps)["gemm"]), flush=True)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:

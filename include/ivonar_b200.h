@@ -91,7 +91,7 @@ typedef struct IvbLayerDesc {
   const float* rope;          /* [max_len, rope_dim / 2, 2] (cos, sin) */
   int8_t* latent_q;           /* cache [max_len, latent] int8 codes of the quantised latent */
   float* latent_scale;        /* cache [max_len] per-position activation scale */
-  uint16_t* k_rope_cache;     /* cache [max_len, heads, rope_dim] fp16 rotated k_rope */
+  uint16_t* k_rope_cache;     /* cache [heads, max_len, rope_dim padded to 8] fp16 rotated k_rope */
   float attn_scale;           /* 1 / sqrt(head_dim) */
 } IvbLayerDesc;
 

@@ -288,9 +288,9 @@ __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_
   lo = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
 }
 
-constexpr int kFaTok = 128;     // query tokens per CTA (8 warps x 16)
+constexpr int kFaTok = 64;      // query tokens per CTA (4 warps x 16)
 constexpr int kFaPos = 64;      // key positions per tile
-constexpr int kFaThreads = 256;
+constexpr int kFaThreads = 128;
 
 // Keys and values of positions 0..P-1 of one layer as fp16 hi/lo pairs, laid out for whole-tile copies:
 // kh/kl [H][Ppad][DK] (K_nope then k_rope, zero padded), vh/vl [H][DV][Ppad] (transposed, zero padded),
@@ -338,11 +338,11 @@ __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
-// Grid (ceil(count / 128), heads). DK: query/key dims (nope + rope) padded to 16 (= value dims padded).
+// Grid (ceil(count / 64), heads). DK: query/key dims (nope + rope) padded to 16 (= value dims padded).
 // q from the entry rows (scaled by attn_scale, rope part rotated); keys and values from kv_split_kernel.
 // Tiles of 64 positions are double-buffered with cp.async.
 template <int DK>
-__global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDesc L, const float* ent, int ld_ent,
+__global__ void __launch_bounds__(kFaThreads, DK <= 64 ? 3 : 1) flash_attention_kernel(IvbLayerDesc L, const float* ent, int ld_ent,
                                                                      const __half* kh, const __half* kl,
                                                                      const __half* vh, const __half* vl, int Ppad,
                                                                      int start, int count, int d, int hd, int rope,
@@ -437,19 +437,25 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
       float s[kFaPos / 8][4];
 #pragma unroll
       for (int n = 0; n < kFaPos / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
+      // the three products of a split go to one accumulator; consecutive MMAs target different
+      // accumulators so none waits on the previous one
 #pragma unroll
       for (int kk = 0; kk < DK / 16; ++kk) {
+        uint32_t bh[kFaPos / 8][2], bl[kFaPos / 8][2];
 #pragma unroll
         for (int n = 0; n < kFaPos / 8; ++n) {
           const int row = (8 * n + grp) * kKs + 16 * kk + 2 * tig;
-          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(k_hi + row);
-          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
-          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(k_lo + row);
-          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
-          mma16816(s[n], qh[kk], bh0, bh1);
-          mma16816(s[n], qh[kk], bl0, bl1);
-          mma16816(s[n], ql[kk], bh0, bh1);
+          bh[n][0] = *reinterpret_cast<const uint32_t*>(k_hi + row);
+          bh[n][1] = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
+          bl[n][0] = *reinterpret_cast<const uint32_t*>(k_lo + row);
+          bl[n][1] = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
         }
+#pragma unroll
+        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], qh[kk], bh[n][0], bh[n][1]);
+#pragma unroll
+        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], qh[kk], bl[n][0], bl[n][1]);
+#pragma unroll
+        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], ql[kk], bh[n][0], bh[n][1]);
       }
       // causal mask and online softmax (rows pos_a: s[n][0..1], pos_b: s[n][2..3])
       float mx[2] = {-INFINITY, -INFINITY};
@@ -503,15 +509,23 @@ __global__ void __launch_bounds__(kFaThreads) flash_attention_kernel(IvbLayerDes
 #pragma unroll
       for (int kk = 0; kk < kFaPos / 16; ++kk) {
 #pragma unroll
-        for (int n = 0; n < DV / 8; ++n) {
-          const int row = (8 * n + grp) * kVs + 16 * kk + 2 * tig;
-          const uint32_t bh0 = *reinterpret_cast<const uint32_t*>(v_hi + row);
-          const uint32_t bh1 = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
-          const uint32_t bl0 = *reinterpret_cast<const uint32_t*>(v_lo + row);
-          const uint32_t bl1 = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
-          mma16816(o[n], ph[kk], bh0, bh1);
-          mma16816(o[n], ph[kk], bl0, bl1);
-          mma16816(o[n], pl2[kk], bh0, bh1);
+        for (int n0 = 0; n0 < DV / 8; n0 += 8) {  // eight value columns at a time bound the registers
+          constexpr int kG = DV / 8 < 8 ? DV / 8 : 8;
+          uint32_t bh[kG][2], bl[kG][2];
+#pragma unroll
+          for (int j = 0; j < kG; ++j) {
+            const int row = (8 * (n0 + j) + grp) * kVs + 16 * kk + 2 * tig;
+            bh[j][0] = *reinterpret_cast<const uint32_t*>(v_hi + row);
+            bh[j][1] = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
+            bl[j][0] = *reinterpret_cast<const uint32_t*>(v_lo + row);
+            bl[j][1] = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
+          }
+#pragma unroll
+          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], ph[kk], bh[j][0], bh[j][1]);
+#pragma unroll
+          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], ph[kk], bl[j][0], bl[j][1]);
+#pragma unroll
+          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], pl2[kk], bh[j][0], bh[j][1]);
         }
       }
     }

@@ -31,7 +31,7 @@ from .model import rope_table
 BURST = 16
 SELF_CHECK_TOLERANCE = 0.25
 DEFAULT_TIMEOUT_NS = 2_000_000_000
-PREFILL_CHUNK = 1024  # prompt tokens per tensor-core prefill call (workspace grows with it)
+PREFILL_CHUNK = 2048  # prompt tokens per tensor-core prefill call (workspace grows with it)
 
 
 def _pad_rows(packed: Tensor) -> Tensor:
