@@ -120,6 +120,35 @@ typedef struct IvbModelDesc {
 
 typedef struct IvbDecoder IvbDecoder; /* host-side plan; opaque */
 
+/* ---- batched decode (independent sequences, one token each per step) ---------------------------- */
+/* Per-layer recurrent state and latent caches of `batch` sequences: the pointers of sequence 0, the
+ * sequences following contiguously with the sizes of the single-sequence layout (ssm_state
+ * heads*state*head_dim*2 floats, prev_force heads*state*head_dim, conv_state hidden*(conv_taps-1),
+ * latent_q max_len*latent_pad bytes, latent_scale max_len floats, k_rope_cache heads*max_len*rope_pad
+ * halves, with latent_pad = latent rounded up to 16 and rope_pad = rope_dim rounded up to 8). */
+typedef struct IvbBatchLayer {
+  float* ssm_state;
+  float* prev_force;
+  float* conv_state;
+  int8_t* latent_q;
+  float* latent_scale;
+  uint16_t* k_rope_cache;
+} IvbBatchLayer;
+
+typedef struct IvbBatch {
+  int32_t batch;
+  const IvbBatchLayer* layers; /* host array [num_layers] */
+  int64_t* tokens;             /* [batch] token of each sequence fed this step; replaced by the sampled one */
+  int64_t* positions;          /* [batch] cache slot of that token; advanced by one per step */
+  float* logits;               /* [batch][vocab] */
+  uint8_t* seen;               /* [batch][vocab] repetition-penalty flags */
+  uint64_t* rng;               /* [batch][2] philox key (per-sequence seed), draw counter */
+  int64_t* history;            /* [batch][history_len] sampled tokens, step s in column s (may be NULL) */
+  int32_t history_len;
+  const float* sampling;       /* [3] temperature, penalty, inverse_penalty (shared) */
+  const int64_t* top_k;        /* [1] (shared) */
+} IvbBatch;
+
 /* ---- library ---------------------------------------------------------------------------------- */
 int32_t ivb_abi_version(void);
 const char* ivb_last_error(void);
@@ -182,6 +211,16 @@ int32_t ivb_ternary_gemv_splitk(const IvbTernary* m, const float* x, const float
 int32_t ivb_sample(const float* logits, uint8_t* seen, int32_t vocab, const float* sampling,
                    const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* token, int64_t* history,
                    void* stream);
+
+/* Batched decode: `steps` tokens for every sequence of `b` (each step: the decoder's layers over all
+ * sequences at once as tcgen05 GEMMs, per-sequence SSM step / latent-cache append / attention, head
+ * GEMM, per-sequence sampler). The decoder handle supplies the weights and shapes; its own
+ * single-sequence state is not touched. Workspace: ivb_batch_workspace_bytes, 256-byte aligned.
+ * Replaces StaticDecoder's batch_size > 1 step (decoder.py:67,96,387-394); the reference GPU kernels
+ * have no batched decode. */
+uint64_t ivb_batch_workspace_bytes(const IvbDecoder* dec, int32_t batch);
+int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* b, int32_t steps, void* workspace, uint64_t workspace_bytes,
+                         void* stream);
 
 /* Debug/failure-detection probe: one CTA waits for a barrier count that never arrives, with a
  * bounded spin of timeout_ns; returns IVB_ETIMEOUT and leaves the context usable. */

@@ -105,6 +105,33 @@ class IvbModelDesc(Structure):
 
 
 # (name, restype, argtypes) for every function declared in include/ivonar_b200.h
+class IvbBatchLayer(Structure):
+    _fields_ = [
+        ("ssm_state", c_void_p),
+        ("prev_force", c_void_p),
+        ("conv_state", c_void_p),
+        ("latent_q", c_void_p),
+        ("latent_scale", c_void_p),
+        ("k_rope_cache", c_void_p),
+    ]
+
+
+class IvbBatch(Structure):
+    _fields_ = [
+        ("batch", c_int32),
+        ("layers", POINTER(IvbBatchLayer)),
+        ("tokens", c_void_p),
+        ("positions", c_void_p),
+        ("logits", c_void_p),
+        ("seen", c_void_p),
+        ("rng", c_void_p),
+        ("history", c_void_p),
+        ("history_len", c_int32),
+        ("sampling", c_void_p),
+        ("top_k", c_void_p),
+    ]
+
+
 SIGNATURES = {
     "ivb_abi_version": (c_int32, []),
     "ivb_last_error": (c_char_p, []),
@@ -127,6 +154,8 @@ SIGNATURES = {
     "ivb_decoder_trace": (c_int32, [c_void_p, c_void_p, c_int32]),
     "ivb_decoder_prefill_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
     "ivb_decoder_prefill": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_uint64, c_void_p]),
+    "ivb_batch_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
+    "ivb_batch_decode": (c_int32, [c_void_p, POINTER(IvbBatch), c_int32, c_void_p, c_uint64, c_void_p]),
     "ivb_decoder_check": (c_int32, [c_void_p, c_void_p]),
 }
 

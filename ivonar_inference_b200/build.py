@@ -18,7 +18,7 @@ CSRC = PACKAGE / "csrc"
 INCLUDE = ROOT / "include"
 LIBRARY = PACKAGE / "libivonar_b200.so"
 
-SOURCES = ("ivb_unit.cu", "ivb_decoder.cu", "ivb_splitk.cu", "ivb_gemm.cu", "ivb_prefill.cu")
+SOURCES = ("ivb_unit.cu", "ivb_decoder.cu", "ivb_splitk.cu", "ivb_gemm.cu", "ivb_prefill.cu", "ivb_batch.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = (
     "-O3",

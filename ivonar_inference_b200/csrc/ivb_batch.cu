@@ -1,0 +1,429 @@
+// Batched decode of libivonar_b200.so: `batch` independent sequences advance one token per step
+// together. The projections of all sequences run as one tcgen05 GEMM per matrix (ivb_ternary_gemm over
+// `batch` token rows, so the weights stream once per step for the whole batch); the per-sequence parts
+// — SSM step, latent-cache append and absorbed latent attention over the sequence's own cache, the
+// sampler — run one CTA (or a channel slice) per sequence. The arithmetic of each part is the
+// single-sequence decode step's (kernels/ternary.cu:421-482 recurrent_step, :509-611 attention_step,
+// :1099-1337 sample_token; decoder.py:235-297 for the torch forms).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+
+#include "ivb_common.h"
+#include "ivb_cluster.cuh"
+#include "ivb_tiles.cuh"
+
+extern "C" {
+int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* norm_weight, float norm_eps,
+                          float norm_clip, float act_eps, int8_t* q8, int32_t ldq, float* scale, int32_t* gsum,
+                          void* stream);
+int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
+                         int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream);
+}
+
+namespace ivb {
+namespace {
+
+constexpr int kBatchTaps = 8;  // conv window registers (conv_taps - 1 <= 8)
+
+__global__ void __launch_bounds__(kThreads) batch_embed_kernel(IvbTernary head, const int64_t* tokens, int d, float* resid) {
+  const int b = blockIdx.x;
+  const long long tok = tokens[b];
+  const uint8_t* erow = head.packed + static_cast<size_t>(tok) * head.row_bytes;
+  const uint16_t* srow = head.scales + static_cast<size_t>(tok) * head.scale_stride;
+  for (int i = threadIdx.x; i < d; i += kThreads)
+    resid[static_cast<size_t>(b) * d + i] =
+        static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
+}
+
+// One SSM step of sequence blockIdx.y: a half-warp per channel, lane s owns state s; ent row b =
+// value | gate | per head (B, C, dt). Same arithmetic as the single-sequence decode step.
+__global__ void __launch_bounds__(kThreads) batch_ssm_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent, int ld, int d,
+                                                             int H, int hd, int S, int taps, float half_dt_min,
+                                                             float half_dt_range, float* y) {
+  const int b = blockIdx.y;
+  const int lane = threadIdx.x & 31, sub = lane & 15;
+  const int c = (blockIdx.x * kThreads + threadIdx.x) >> 4;
+  const bool live = c < d;
+  const int cc_ = live ? c : 0;
+  const int h = cc_ / hd, dd = cc_ - h * hd;
+  const bool on = live && sub < S;
+  const int s = on ? sub : 0;
+  float* ssm = B.ssm_state + static_cast<size_t>(b) * H * S * hd * 2;
+  float* prevf = B.prev_force + static_cast<size_t>(b) * H * S * hd;
+  float* conv_state = B.conv_state + static_cast<size_t>(b) * d * (taps - 1);
+  const float* row = ent + static_cast<size_t>(b) * ld;
+  const float incoming = live ? row[cc_] : 0.0f;
+  float conv = live ? L.conv_bias[cc_] : 0.0f;
+  for (int k2 = 0; k2 < taps - 1; ++k2)
+    conv = fmaf(live ? L.conv_weight[cc_ * taps + k2] : 0.0f,
+                live ? conv_state[static_cast<size_t>(cc_) * (taps - 1) + k2] : 0.0f, conv);
+  conv = fmaf(live ? L.conv_weight[cc_ * taps + taps - 1] : 0.0f, incoming, conv);
+  const float value = silu_f(conv);
+  const size_t si = (static_cast<size_t>(h) * S + s) * hd + dd;
+  float contrib = 0.0f;
+  if (on) {
+    const float* bcdt = row + 2 * d + h * 3 * S;
+    const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s]) * half_dt_range;
+    const float mag = expf(2.0f * half_dt * L.decay[h * S + s]);
+    float sn, cs;
+    sincosf(2.0f * half_dt * L.theta[h * S + s], &sn, &cs);
+    const float ar = mag * cs, ai = mag * sn;
+    const float bb = tanhf(bcdt[s]), cc = tanhf(bcdt[S + s]);
+    const float sr = ssm[2 * si], sim = ssm[2 * si + 1], prev = prevf[si];
+    const float force = bb * value;
+    const float dr = (force + ar * prev) * half_dt;
+    const float di = (ai * prev) * half_dt;
+    const float nr = sr * ar - sim * ai + dr;
+    const float ni = sr * ai + sim * ar + di;
+    ssm[2 * si] = nr;
+    ssm[2 * si + 1] = ni;
+    prevf[si] = force;
+    contrib = cc * nr;
+  }
+#pragma unroll
+  for (int off = 8; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
+  if (live && sub == 0) {
+    y[static_cast<size_t>(b) * d + cc_] = (contrib + L.skip[cc_] * value) * sigmoid_f(row[d + cc_]);
+    // shift the conv window: the oldest input leaves, this token's enters
+    float* w = conv_state + static_cast<size_t>(cc_) * (taps - 1);
+    for (int k = 0; k + 1 < taps - 1; ++k) w[k] = w[k + 1];
+    if (taps > 1) w[taps - 2] = incoming;
+  }
+}
+
+// Latent-cache append of sequence blockIdx.x at its position: quantised latent + rotated k_rope.
+__global__ void __launch_bounds__(kThreads) batch_cache_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent, int ld,
+                                                               const int64_t* positions, int d, int Lt, int H, int rope,
+                                                               int max_len, int lpad, int rpad, float act_eps,
+                                                               unsigned* error) {
+  __shared__ float xl[512 + 64];
+  __shared__ __align__(16) int8_t codes[576];
+  __shared__ float red[64];
+  const int b = blockIdx.x;
+  const long long pos = positions[b];
+  if (pos < 0 || pos >= max_len) {
+    if (threadIdx.x == 0) atomicCAS(error, 0u, static_cast<unsigned>(IVB_ECAPACITY));
+    return;
+  }
+  const float* row = ent + static_cast<size_t>(b) * ld;
+  for (int j = threadIdx.x; j < Lt; j += kThreads) xl[j] = row[d + j];
+  __syncthreads();
+  const float a = quantize_block(xl, Lt, nullptr, 0.0f, 0.0f, act_eps, codes, false, nullptr, red);
+  int8_t* latent_q = B.latent_q + static_cast<size_t>(b) * max_len * lpad;
+  for (int j = threadIdx.x; j < Lt; j += kThreads) latent_q[pos * lpad + j] = codes[j];
+  if (threadIdx.x == 0) B.latent_scale[static_cast<size_t>(b) * max_len + pos] = a;
+  const float* rtab = L.rope + pos * rope;
+  uint16_t* kcache = B.k_rope_cache + static_cast<size_t>(b) * H * max_len * rpad;
+  for (int i = threadIdx.x; i < H * (rope / 2); i += kThreads) {
+    const int h = i / (rope / 2), jr = i - h * (rope / 2);
+    const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+    const float k0 = row[d + Lt + h * rope + 2 * jr], k1 = row[d + Lt + h * rope + 2 * jr + 1];
+    uint16_t* kc = kcache + (static_cast<size_t>(h) * max_len + pos) * rpad;
+    kc[2 * jr] = f2h(k0 * cs - k1 * sn);
+    kc[2 * jr + 1] = f2h(k0 * sn + k1 * cs);
+  }
+}
+
+// Absorbed latent attention of sequence blockIdx.x, head blockIdx.y, over cached positions 0..pos:
+// s_p = a_p <qa, ql_p> + q_nope.b_k + <q_rope, k_rope_p>, online softmax, out = W_v (sum_p w_p a_p ql_p) + b_v.
+constexpr int kAttnThreads = 128;
+constexpr int kAttnTile = 128;
+
+__global__ void __launch_bounds__(kAttnThreads) batch_attention_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent,
+                                                                       int ld, const int64_t* positions, int d, int Lt, int H,
+                                                                       int hd, int rope, int nope, int max_len, int lpad,
+                                                                       int rpad, float* y) {
+  __shared__ float qa[512];
+  __shared__ float qn[256];
+  __shared__ float qr[128];
+  __shared__ float sc[kAttnTile];
+  __shared__ float part[4][512];
+  __shared__ float red[64];
+  const int t = blockIdx.x, h = blockIdx.y;
+  const long long pos_in = positions[t];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (pos_in < 0 || pos_in >= max_len) {  // capacity error, reported by the cache append
+    for (int e = tid; e < hd; e += kAttnThreads) y[static_cast<size_t>(t) * d + h * hd + e] = 0.0f;
+    return;
+  }
+  const int pos = static_cast<int>(pos_in);
+  // sequence t's caches
+  const int8_t* latent_q = B.latent_q + static_cast<size_t>(t) * max_len * lpad;
+  const float* latent_scale = B.latent_scale + static_cast<size_t>(t) * max_len;
+  const uint16_t* k_rope_cache = B.k_rope_cache + static_cast<size_t>(t) * H * max_len * rpad;
+  const float* q = ent + static_cast<size_t>(t) * ld + h * hd;
+  const float scl = L.attn_scale;
+  const float* rtab = L.rope + static_cast<size_t>(pos) * rope;
+  for (int jr = tid; jr < rope / 2; jr += kAttnThreads) {
+    const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+    const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
+    qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
+    qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+  }
+  for (int e = tid; e < nope; e += kAttnThreads) qn[e] = q[e] * scl;
+  __syncthreads();
+  // absorbed query
+  const IvbTernary& kn = L.k_nope_up;
+  for (int j = tid; j < Lt; j += kAttnThreads) {
+    float acc = 0.0f;
+    for (int e = 0; e < nope; ++e) {
+      const size_t r = static_cast<size_t>(h) * nope + e;
+      acc = fmaf(qn[e], code_value(kn.packed + r * kn.row_bytes, j) * h2f(__ldg(kn.scales + r * kn.scale_stride + (j >> 7))), acc);
+    }
+    qa[j] = acc;
+  }
+  float qb = 0.0f;
+  if (kn.bias != nullptr) {
+    float pp = 0.0f;
+    for (int e = tid; e < nope; e += kAttnThreads) pp = fmaf(qn[e], __ldg(kn.bias + h * nope + e), pp);
+    pp = warp_sum(pp);
+    if (lane == 0) red[warp] = pp;
+    __syncthreads();
+    qb = red[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) qb += red[w];
+  }
+  __syncthreads();
+  const int sub = tid & 7, grp = tid >> 3;  // 16 position groups of 8 lanes
+  const int P = pos + 1;
+  float m_run = -INFINITY, l_run = 0.0f;
+  float u[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) u[i] = 0.0f;
+  for (int start = 0; start < P; start += kAttnTile) {
+    const int count = min(kAttnTile, P - start);
+    for (int k = grp; k - grp < count; k += kAttnThreads / 8) {
+      const bool valid = k < count;
+      const int p = start + (valid ? k : 0);
+      const int8_t* ql = latent_q + static_cast<size_t>(p) * lpad;
+      float dot = 0.0f;
+      for (int j0 = sub * 16; j0 < Lt; j0 += 128) {
+        const uint4 w = __ldcg(reinterpret_cast<const uint4*>(ql + j0));
+        float f[16];
+        bytes_to_f32(w.x, f);
+        bytes_to_f32(w.y, f + 4);
+        bytes_to_f32(w.z, f + 8);
+        bytes_to_f32(w.w, f + 12);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dot = fmaf(qa[j0 + i], f[i], dot);
+      }
+      float rp = 0.0f;
+      const uint16_t* kr = k_rope_cache + (static_cast<size_t>(h) * max_len + p) * rpad;
+      for (int r = sub; r < rope; r += 8) rp = fmaf(qr[r], h2f(__ldcg(kr + r)), rp);
+      float total = fmaf(__ldcg(latent_scale + p), dot, rp);
+      total += __shfl_xor_sync(kFull, total, 4);
+      total += __shfl_xor_sync(kFull, total, 2);
+      total += __shfl_xor_sync(kFull, total, 1);
+      if (valid && sub == 0) sc[k] = total + qb;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int k = tid; k < count; k += kAttnThreads) mx = fmaxf(mx, sc[k]);
+    mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = red[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+    __syncthreads();
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+    float ls = 0.0f;
+    for (int k = tid; k < count; k += kAttnThreads) {
+      const float e = expf(sc[k] - m_new);
+      sc[k] = e * __ldcg(latent_scale + start + k);
+      ls += e;
+    }
+    ls = warp_sum(ls);
+    if (lane == 0) red[warp] = ls;
+    __syncthreads();
+    ls = red[0];
+    for (int w = 1; w < kAttnThreads / 32; ++w) ls += red[w];
+    l_run = l_run * corr + ls;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) u[i] *= corr;
+    for (int k = warp; k < count; k += kAttnThreads / 32) {
+      const int8_t* ql = latent_q + static_cast<size_t>(start + k) * lpad;
+      const float ea = sc[k];
+#pragma unroll
+      for (int pc = 0; pc < 2; ++pc) {
+        const int j0 = pc * 256 + lane * 8;
+        if (j0 < Lt) {
+          const uint2 w = __ldcg(reinterpret_cast<const uint2*>(ql + j0));
+          float f[8];
+          bytes_to_f32(w.x, f);
+          bytes_to_f32(w.y, f + 4);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) u[pc * 8 + i] = fmaf(ea, f[i], u[pc * 8 + i]);
+        }
+      }
+    }
+    m_run = m_new;
+    __syncthreads();
+  }
+#pragma unroll
+  for (int pc = 0; pc < 2; ++pc) {
+    const int j0 = pc * 256 + lane * 8;
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (j0 + i < Lt) part[warp][j0 + i] = u[pc * 8 + i];
+  }
+  __syncthreads();
+  for (int j = tid; j < Lt; j += kAttnThreads) {
+    float v = part[0][j];
+    for (int w = 1; w < kAttnThreads / 32; ++w) v += part[w][j];
+    qa[j] = v;  // the weighted latent sum u
+  }
+  __syncthreads();
+  const IvbTernary& vu = L.v_up;
+  const float inv_l = 1.0f / l_run;
+  for (int e = tid; e < hd; e += kAttnThreads) {
+    const size_t r = static_cast<size_t>(h) * hd + e;
+    float acc = 0.0f;
+    for (int j = 0; j < Lt; ++j)
+      acc = fmaf(code_value(vu.packed + r * vu.row_bytes, j) * h2f(__ldg(vu.scales + r * vu.scale_stride + (j >> 7))), qa[j], acc);
+    float o = acc * inv_l;
+    if (vu.bias != nullptr) o += __ldg(vu.bias + r);
+    y[static_cast<size_t>(t) * d + h * hd + e] = o;
+  }
+}
+
+
+// Sampler of sequence blockIdx.x (temperature, repetition penalty, top-k, Philox draw), then its
+// position advances by one.
+__global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* logits, uint8_t* seen, int vocab,
+                                                                   const float* sampling, const int64_t* top_k,
+                                                                   int max_top_k, uint64_t* rng, int64_t* tokens,
+                                                                   int64_t* positions, int64_t* history, int history_len,
+                                                                   int step) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  SampleSmem sm;
+  carve_sample(smem, vocab, sm);
+  const int b = blockIdx.x;
+  int64_t* hist = (history != nullptr && step < history_len) ? history + static_cast<size_t>(b) * history_len + step : nullptr;
+  sample_block(logits + static_cast<size_t>(b) * vocab, seen + static_cast<size_t>(b) * vocab, vocab, sampling, top_k,
+               max_top_k, rng + 2 * b, tokens + b, hist, sm);
+  if (threadIdx.x == 0) positions[b] += 1;
+}
+
+struct BatchLayout {
+  size_t resid, ent, y, h, q8, scale, total;
+  int ldq;
+};
+
+BatchLayout batch_layout(const IvbModelDesc& md, const IvbLayerDesc* layers, int batch) {
+  BatchLayout L{};
+  const int d = md.hidden, F = md.dense;
+  int ld_ent = 0;
+  for (int i = 0; i < md.num_layers; ++i) ld_ent = std::max(ld_ent, layers[i].entry.rows);
+  L.ldq = (std::max(d, F) + 127) / 128 * 128;
+  const size_t T = static_cast<size_t>(batch);
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o = align_up(o + bytes, 256);
+    return at;
+  };
+  L.resid = take(T * d * 4);
+  L.ent = take(T * ld_ent * 4);
+  L.y = take(T * d * 4);
+  L.h = take(T * std::max(F, d) * 4);
+  L.q8 = take((T + 127) / 128 * 128 * L.ldq);
+  L.scale = take(T * 4);
+  L.total = o;
+  return L;
+}
+
+}  // namespace
+}  // namespace ivb
+
+extern "C" {
+
+uint64_t ivb_batch_workspace_bytes(const IvbDecoder* dec, int32_t batch) {
+  using namespace ivb;
+  if (dec == nullptr || batch <= 0) return 0;
+  const IvbLayerDesc* layers = nullptr;
+  const IvbModelDesc& md = decoder_model(dec, &layers);
+  return batch_layout(md, layers, batch).total;
+}
+
+int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, void* workspace, uint64_t workspace_bytes,
+                         void* stream) {
+  using namespace ivb;
+  if (dec == nullptr || bt == nullptr || workspace == nullptr) return fail(IVB_EINVAL, "ivb_batch_decode: null argument");
+  if (bt->layers == nullptr || bt->tokens == nullptr || bt->positions == nullptr || bt->logits == nullptr ||
+      bt->seen == nullptr || bt->rng == nullptr || bt->sampling == nullptr || bt->top_k == nullptr)
+    return fail(IVB_EINVAL, "ivb_batch_decode: null batch buffer");
+  const int B = bt->batch;
+  if (B <= 0 || steps < 0) return fail(IVB_EINVAL, "ivb_batch_decode: batch %d, steps %d", B, steps);
+  const IvbLayerDesc* layers = nullptr;
+  const IvbModelDesc& md = decoder_model(dec, &layers);
+  const BatchLayout W = batch_layout(md, layers, B);
+  if (workspace_bytes < W.total) return fail(IVB_EINVAL, "ivb_batch_decode: workspace too small (%llu < %zu)",
+                                             static_cast<unsigned long long>(workspace_bytes), W.total);
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255) != 0) return fail(IVB_EINVAL, "ivb_batch_decode: workspace must be 256-byte aligned");
+  const int d = md.hidden, F = md.dense, H = md.heads, hd = md.head_dim, S = md.state_dim, Lt = md.latent_dim;
+  const int rope = md.rope_dim, nope = md.nope_dim, V = md.vocab;
+  if (Lt > 512 || rope > 128 || nope > 256 || S > 16) return fail(IVB_EINVAL, "ivb_batch_decode: shapes beyond the batch kernels");
+  for (int i = 0; i < md.num_layers; ++i)
+    if (layers[i].kind == IVB_MAMBA && layers[i].conv_taps > kBatchTaps + 1)
+      return fail(IVB_EINVAL, "ivb_batch_decode: conv width %d beyond the step kernel", layers[i].conv_taps);
+  uint32_t* err = decoder_error_word(dec);
+  if (err == nullptr) return fail(IVB_EINVAL, "ivb_batch_decode: bind the decoder first");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned char* ws = static_cast<unsigned char*>(workspace);
+  float* resid = reinterpret_cast<float*>(ws + W.resid);
+  float* ent = reinterpret_cast<float*>(ws + W.ent);
+  float* y = reinterpret_cast<float*>(ws + W.y);
+  float* hbuf = reinterpret_cast<float*>(ws + W.h);
+  int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
+  float* scale = reinterpret_cast<float*>(ws + W.scale);
+  const int lpad = (Lt + 15) / 16 * 16, rpad = (rope + 7) / 8 * 8;
+  const size_t sample_smem = sample_smem_bytes(V);
+  IVB_CUDA(cudaFuncSetAttribute(batch_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(sample_smem)));
+  auto quant = [&](const float* x, int n, const float* norm, float eps) -> int32_t {
+    const int ld = (n + 127) / 128 * 128;
+    return ivb_quantize_rows(x, B, n, norm, eps, md.norm_clip, md.act_eps, q8, ld, scale, nullptr, stream);
+  };
+  auto gemm = [&](const IvbTernary& m, int epilogue, float* out, int ldo) -> int32_t {
+    const int ld = (m.in_features + 127) / 128 * 128;
+    return ivb_ternary_gemm(&m, q8, ld, scale, B, epilogue, out, ldo, err, stream);
+  };
+  for (int step = 0; step < steps; ++step) {
+    batch_embed_kernel<<<B, kThreads, 0, s>>>(md.head, bt->tokens, d, resid);
+    IVB_CUDA(cudaGetLastError());
+    for (int li = 0; li < md.num_layers; ++li) {
+      const IvbLayerDesc& L = layers[li];
+      const IvbBatchLayer& BL = bt->layers[li];
+      const int ld = L.entry.rows;
+      if (int32_t rc = quant(resid, d, L.mixer_norm, L.mixer_norm_eps)) return rc;
+      if (int32_t rc = gemm(L.entry, IVB_EPI_STORE, ent, ld)) return rc;
+      if (L.kind == IVB_MAMBA) {
+        batch_ssm_kernel<<<dim3((d * 16 + kThreads - 1) / kThreads, B), kThreads, 0, s>>>(
+            L, BL, ent, ld, d, H, hd, S, L.conv_taps, L.half_dt_min, L.half_dt_range, y);
+        IVB_CUDA(cudaGetLastError());
+      } else {
+        batch_cache_kernel<<<B, kThreads, 0, s>>>(L, BL, ent, ld, bt->positions, d, Lt, H, rope, md.max_len, lpad, rpad,
+                                                  md.act_eps, err);
+        IVB_CUDA(cudaGetLastError());
+        batch_attention_kernel<<<dim3(B, H), kAttnThreads, 0, s>>>(L, BL, ent, ld, bt->positions, d, Lt, H, hd, rope, nope,
+                                                                   md.max_len, lpad, rpad, y);
+        IVB_CUDA(cudaGetLastError());
+      }
+      if (int32_t rc = quant(y, d, nullptr, 0.0f)) return rc;
+      if (int32_t rc = gemm(L.out, IVB_EPI_RESIDUAL, resid, d)) return rc;
+      if (int32_t rc = quant(resid, d, L.ffn_norm, L.ffn_norm_eps)) return rc;
+      if (int32_t rc = gemm(L.gate_up, IVB_EPI_SILU_PAIR, hbuf, F)) return rc;
+      if (int32_t rc = quant(hbuf, F, nullptr, 0.0f)) return rc;
+      if (int32_t rc = gemm(L.down, IVB_EPI_RESIDUAL, resid, d)) return rc;
+    }
+    if (int32_t rc = quant(resid, d, md.final_norm, md.final_norm_eps)) return rc;
+    if (int32_t rc = gemm(md.head, IVB_EPI_STORE, bt->logits, V)) return rc;
+    batch_sample_kernel<<<B, kThreads, sample_smem, s>>>(bt->logits, bt->seen, V, bt->sampling, bt->top_k, md.max_top_k,
+                                                         bt->rng, bt->tokens, bt->positions, bt->history, bt->history_len,
+                                                         step);
+    IVB_CUDA(cudaGetLastError());
+  }
+  return IVB_OK;
+}
+
+}  // extern "C"

@@ -34,4 +34,9 @@ int32_t check_ternary(const IvbTernary& m, const char* name);
 // True when the current device is compute capability 10.0 (B200 / sm_100a).
 bool device_is_sm100();
 
+// The model description a decoder handle was created from (layers: its host array), and the device
+// error word that ivb_decoder_check reports.
+const IvbModelDesc& decoder_model(const IvbDecoder* dec, const IvbLayerDesc** layers);
+unsigned* decoder_error_word(const IvbDecoder* dec);
+
 }  // namespace ivb

@@ -20,8 +20,6 @@
 
 namespace ivb {
 
-const IvbModelDesc& decoder_model(const IvbDecoder* dec, const IvbLayerDesc** layers);
-unsigned* decoder_error_word(const IvbDecoder* dec);
 
 constexpr int kMaxTaps = 8;
 
