@@ -36,60 +36,72 @@ __global__ void __launch_bounds__(kThreads) batch_embed_kernel(IvbTernary head, 
         static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
 }
 
-// One SSM step of sequence blockIdx.y: a half-warp per channel, lane s owns state s; ent row b =
-// value | gate | per head (B, C, dt). Same arithmetic as the single-sequence decode step.
-__global__ void __launch_bounds__(kThreads) batch_ssm_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent, int ld, int d,
-                                                             int H, int hd, int S, int taps, float half_dt_min,
-                                                             float half_dt_range, float* y) {
-  const int b = blockIdx.y;
-  const int lane = threadIdx.x & 31, sub = lane & 15;
-  const int c = (blockIdx.x * kThreads + threadIdx.x) >> 4;
-  const bool live = c < d;
-  const int cc_ = live ? c : 0;
-  const int h = cc_ / hd, dd = cc_ - h * hd;
-  const bool on = live && sub < S;
-  const int s = on ? sub : 0;
-  float* ssm = B.ssm_state + static_cast<size_t>(b) * H * S * hd * 2;
-  float* prevf = B.prev_force + static_cast<size_t>(b) * H * S * hd;
-  float* conv_state = B.conv_state + static_cast<size_t>(b) * d * (taps - 1);
+// One SSM step of sequence blockIdx.y for 128 consecutive channels (one thread each, so the state of a
+// (head, state) row is read and written contiguously across the threads); the per-(head, state)
+// coefficients of the heads the CTA touches are computed once into shared memory. ent row b = value |
+// gate | per head (B, C, dt). Same arithmetic as the single-sequence decode step, including the order
+// of the sum over the states (the xor butterfly of a 16-lane warp sum).
+constexpr int kSsmChannels = 128;
+__global__ void __launch_bounds__(kSsmChannels) batch_ssm_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent, int ld,
+                                                                 int d, int H, int hd, int S, int taps, float half_dt_min,
+                                                                 float half_dt_range, float* y) {
+  extern __shared__ float coef[];  // [heads touched][S][5]: B, C, half_dt, ar, ai
+  const int b = blockIdx.y, c0 = blockIdx.x * kSsmChannels;
+  const int c = c0 + threadIdx.x;
+  const int h0 = c0 / hd, nh = (min(d, c0 + kSsmChannels) - 1) / hd - h0 + 1;
   const float* row = ent + static_cast<size_t>(b) * ld;
-  const float incoming = live ? row[cc_] : 0.0f;
-  float conv = live ? L.conv_bias[cc_] : 0.0f;
-  for (int k2 = 0; k2 < taps - 1; ++k2)
-    conv = fmaf(live ? L.conv_weight[cc_ * taps + k2] : 0.0f,
-                live ? conv_state[static_cast<size_t>(cc_) * (taps - 1) + k2] : 0.0f, conv);
-  conv = fmaf(live ? L.conv_weight[cc_ * taps + taps - 1] : 0.0f, incoming, conv);
-  const float value = silu_f(conv);
-  const size_t si = (static_cast<size_t>(h) * S + s) * hd + dd;
-  float contrib = 0.0f;
-  if (on) {
+  for (int i = threadIdx.x; i < nh * S; i += kSsmChannels) {
+    const int h = h0 + i / S, s = i - (i / S) * S;
     const float* bcdt = row + 2 * d + h * 3 * S;
     const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s]) * half_dt_range;
     const float mag = expf(2.0f * half_dt * L.decay[h * S + s]);
     float sn, cs;
     sincosf(2.0f * half_dt * L.theta[h * S + s], &sn, &cs);
-    const float ar = mag * cs, ai = mag * sn;
-    const float bb = tanhf(bcdt[s]), cc = tanhf(bcdt[S + s]);
-    const float sr = ssm[2 * si], sim = ssm[2 * si + 1], prev = prevf[si];
-    const float force = bb * value;
-    const float dr = (force + ar * prev) * half_dt;
-    const float di = (ai * prev) * half_dt;
-    const float nr = sr * ar - sim * ai + dr;
-    const float ni = sr * ai + sim * ar + di;
-    ssm[2 * si] = nr;
-    ssm[2 * si + 1] = ni;
-    prevf[si] = force;
-    contrib = cc * nr;
+    float* cf = coef + i * 5;
+    cf[0] = tanhf(bcdt[s]);
+    cf[1] = tanhf(bcdt[S + s]);
+    cf[2] = half_dt;
+    cf[3] = mag * cs;
+    cf[4] = mag * sn;
   }
+  __syncthreads();
+  if (c >= d) return;
+  const int h = c / hd, dd = c - h * hd;
+  float* ssm = B.ssm_state + static_cast<size_t>(b) * H * S * hd * 2;
+  float* prevf = B.prev_force + static_cast<size_t>(b) * H * S * hd;
+  float* conv_state = B.conv_state + static_cast<size_t>(b) * d * (taps - 1) + static_cast<size_t>(c) * (taps - 1);
+  const float incoming = row[c];
+  float conv = L.conv_bias[c];
+  for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(L.conv_weight[c * taps + k2], conv_state[k2], conv);
+  conv = fmaf(L.conv_weight[c * taps + taps - 1], incoming, conv);
+  const float value = silu_f(conv);
+  float contrib[16];
 #pragma unroll
-  for (int off = 8; off > 0; off >>= 1) contrib += __shfl_xor_sync(kFull, contrib, off);
-  if (live && sub == 0) {
-    y[static_cast<size_t>(b) * d + cc_] = (contrib + L.skip[cc_] * value) * sigmoid_f(row[d + cc_]);
-    // shift the conv window: the oldest input leaves, this token's enters
-    float* w = conv_state + static_cast<size_t>(cc_) * (taps - 1);
-    for (int k = 0; k + 1 < taps - 1; ++k) w[k] = w[k + 1];
-    if (taps > 1) w[taps - 2] = incoming;
+  for (int s = 0; s < 16; ++s) {
+    contrib[s] = 0.0f;
+    if (s < S) {
+      const float* cf = coef + ((h - h0) * S + s) * 5;
+      const size_t si = (static_cast<size_t>(h) * S + s) * hd + dd;
+      const float sr = ssm[2 * si], sim = ssm[2 * si + 1], prev = prevf[si];
+      const float force = cf[0] * value;
+      const float dr = (force + cf[3] * prev) * cf[2];
+      const float di = (cf[4] * prev) * cf[2];
+      const float nr = sr * cf[3] - sim * cf[4] + dr;
+      const float ni = sr * cf[4] + sim * cf[3] + di;
+      ssm[2 * si] = nr;
+      ssm[2 * si + 1] = ni;
+      prevf[si] = force;
+      contrib[s] = cf[1] * nr;
+    }
   }
+  float a8[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) a8[i] = contrib[i] + contrib[i + 8];
+  const float sum = ((a8[0] + a8[4]) + (a8[2] + a8[6])) + ((a8[1] + a8[5]) + (a8[3] + a8[7]));
+  y[static_cast<size_t>(b) * d + c] = (sum + L.skip[c] * value) * sigmoid_f(row[d + c]);
+  // shift the conv window: the oldest input leaves, this token's enters
+  for (int k = 0; k + 1 < taps - 1; ++k) conv_state[k] = conv_state[k + 1];
+  if (taps > 1) conv_state[taps - 2] = incoming;
 }
 
 // Latent-cache append of sequence blockIdx.x at its position: quantised latent + rotated k_rope.
@@ -398,7 +410,8 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
       if (int32_t rc = quant(resid, d, L.mixer_norm, L.mixer_norm_eps)) return rc;
       if (int32_t rc = gemm(L.entry, IVB_EPI_STORE, ent, ld)) return rc;
       if (L.kind == IVB_MAMBA) {
-        batch_ssm_kernel<<<dim3((d * 16 + kThreads - 1) / kThreads, B), kThreads, 0, s>>>(
+        const int nh_max = std::min(H, kSsmChannels / hd + 2);
+        batch_ssm_kernel<<<dim3((d + kSsmChannels - 1) / kSsmChannels, B), kSsmChannels, nh_max * S * 5 * 4, s>>>(
             L, BL, ent, ld, d, H, hd, S, L.conv_taps, L.half_dt_min, L.half_dt_range, y);
         IVB_CUDA(cudaGetLastError());
       } else {
