@@ -143,8 +143,10 @@ typedef struct IvbBatch {
   float* logits;               /* [batch][vocab] */
   uint8_t* seen;               /* [batch][vocab] repetition-penalty flags */
   uint64_t* rng;               /* [batch][2] philox key (per-sequence seed), draw counter */
-  int64_t* history;            /* [batch][history_len] sampled tokens, step s in column s (may be NULL) */
+  int64_t* history;            /* [batch][history_len] sampled tokens (may be NULL) */
   int32_t history_len;
+  int32_t* step;               /* [1] device step counter: the step that runs writes column *step, then
+                                  advances it (the caller zeroes it at the start of a generation) */
   const float* sampling;       /* [3] temperature, penalty, inverse_penalty (shared) */
   const int64_t* top_k;        /* [1] (shared) */
 } IvbBatch;

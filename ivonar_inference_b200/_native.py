@@ -127,6 +127,7 @@ class IvbBatch(Structure):
         ("rng", c_void_p),
         ("history", c_void_p),
         ("history_len", c_int32),
+        ("step", c_void_p),
         ("sampling", c_void_p),
         ("top_k", c_void_p),
     ]

@@ -25,7 +25,7 @@ class B200BatchDecoder:
     """`batch` sequences of one model decoded together; sampling per sequence (own seed and flags)."""
 
     def __init__(self, model, batch: int, max_len: int | None = None, device: str | torch.device | None = None,
-                 max_top_k: int = 256, history_len: int = 1024) -> None:
+                 max_top_k: int = 256, history_len: int = 1024, graphs: bool = True) -> None:
         if batch <= 0:
             raise ValueError("batch must be positive")
         self.base = B200Decoder(model, max_len=max_len, device=device, sampling=True, max_top_k=max_top_k)
@@ -72,6 +72,9 @@ class B200BatchDecoder:
         self.seen = torch.zeros(batch, self.vocab, dtype=torch.uint8, device=dev)
         self.rng = torch.zeros(batch, 2, dtype=torch.int64, device=dev)
         self.history = torch.zeros(batch, int(history_len), dtype=torch.int64, device=dev)
+        self.step_counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.use_graphs = bool(graphs)
+        self._graph: torch.cuda.CUDAGraph | None = None
         self.host_positions = [0] * batch
         spec = native.IvbBatch()
         spec.batch = batch
@@ -83,6 +86,7 @@ class B200BatchDecoder:
         spec.rng = self.rng.data_ptr()
         spec.history = self.history.data_ptr()
         spec.history_len = int(history_len)
+        spec.step = self.step_counter.data_ptr()
         spec.sampling = base._sampling.data_ptr()
         spec.top_k = base.top_k.data_ptr()
         self._spec = spec
@@ -124,6 +128,7 @@ class B200BatchDecoder:
             self.rng[b].copy_(base.rng)
             self.logits[b].copy_(base.logits[0])
             self.host_positions[b] = base.host_position
+        self.step_counter.zero_()
         return first
 
     @torch.no_grad()
@@ -133,13 +138,38 @@ class B200BatchDecoder:
         steps = int(steps)
         if steps <= 0:
             return self.history[:, :0]
-        if steps > self.history.shape[1]:
-            raise ValueError("steps exceed the history length of this batch decoder")
         if max(self.host_positions) + steps > self.max_len:
             raise ValueError("the batch has no free position left (capacity)")
+        done = int(self.step_counter.item())
+        if done + steps > self.history.shape[1]:
+            raise ValueError("steps exceed the history length of this batch decoder")
+        if not self.use_graphs:
+            self._launch(steps)
+        else:
+            run = steps
+            if self._graph is None:
+                # one step runs eagerly (first-use setup happens outside capture), then one step is captured
+                self._launch(1)
+                run -= 1
+                if run > 0:
+                    self._capture()
+            for _ in range(run):
+                self._graph.replay()
+        self.base._check()
+        self.host_positions = [p + steps for p in self.host_positions]
+        return self.history[:, done:done + steps]
+
+    def _launch(self, steps: int) -> None:
         rc = self.lib.ivb_batch_decode(self.base._plan, ctypes.byref(self._spec), steps, self.workspace.data_ptr(),
                                        self.workspace.numel(), self._stream())
         native.check(rc, "ivb_batch_decode")
-        self.base._check()
-        self.host_positions = [p + steps for p in self.host_positions]
-        return self.history[:, :steps]
+
+    def _capture(self) -> None:
+        """One batched step as a CUDA graph (its launches replayed without host work per kernel)."""
+
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            rc = self.lib.ivb_batch_decode(self.base._plan, ctypes.byref(self._spec), 1, self.workspace.data_ptr(),
+                                           self.workspace.numel(), self._stream())
+        native.check(rc, "ivb_batch_decode (capture)")
+        self._graph = graph

@@ -26,8 +26,10 @@ namespace {
 
 constexpr int kBatchTaps = 8;  // conv window registers (conv_taps - 1 <= 8)
 
-__global__ void __launch_bounds__(kThreads) batch_embed_kernel(IvbTernary head, const int64_t* tokens, int d, float* resid) {
+__global__ void __launch_bounds__(kThreads) batch_embed_kernel(IvbTernary head, const int64_t* tokens, int d, float* resid,
+                                                               int32_t* step_counter) {
   const int b = blockIdx.x;
+  if (b == 0 && threadIdx.x == 0 && step_counter != nullptr) *step_counter += 1;
   const long long tok = tokens[b];
   const uint8_t* erow = head.packed + static_cast<size_t>(tok) * head.row_bytes;
   const uint16_t* srow = head.scales + static_cast<size_t>(tok) * head.scale_stride;
@@ -306,12 +308,14 @@ __global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* 
                                                                    const float* sampling, const int64_t* top_k,
                                                                    int max_top_k, uint64_t* rng, int64_t* tokens,
                                                                    int64_t* positions, int64_t* history, int history_len,
-                                                                   int step) {
+                                                                   const int32_t* step_counter) {
   extern __shared__ __align__(16) unsigned char smem[];
   SampleSmem sm;
   carve_sample(smem, vocab, sm);
   const int b = blockIdx.x;
-  int64_t* hist = (history != nullptr && step < history_len) ? history + static_cast<size_t>(b) * history_len + step : nullptr;
+  const int step = step_counter != nullptr ? *step_counter - 1 : -1;  // advanced by this step's embedding kernel
+  int64_t* hist = (history != nullptr && step >= 0 && step < history_len) ? history + static_cast<size_t>(b) * history_len + step
+                                                                         : nullptr;
   sample_block(logits + static_cast<size_t>(b) * vocab, seen + static_cast<size_t>(b) * vocab, vocab, sampling, top_k,
                max_top_k, rng + 2 * b, tokens + b, hist, sm);
   if (threadIdx.x == 0) positions[b] += 1;
@@ -401,7 +405,7 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
     return ivb_ternary_gemm(&m, q8, ld, scale, B, epilogue, out, ldo, err, stream);
   };
   for (int step = 0; step < steps; ++step) {
-    batch_embed_kernel<<<B, kThreads, 0, s>>>(md.head, bt->tokens, d, resid);
+    batch_embed_kernel<<<B, kThreads, 0, s>>>(md.head, bt->tokens, d, resid, bt->step);
     IVB_CUDA(cudaGetLastError());
     for (int li = 0; li < md.num_layers; ++li) {
       const IvbLayerDesc& L = layers[li];
@@ -433,7 +437,7 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
     if (int32_t rc = gemm(md.head, IVB_EPI_STORE, bt->logits, V)) return rc;
     batch_sample_kernel<<<B, kThreads, sample_smem, s>>>(bt->logits, bt->seen, V, bt->sampling, bt->top_k, md.max_top_k,
                                                          bt->rng, bt->tokens, bt->positions, bt->history, bt->history_len,
-                                                         step);
+                                                         bt->step);
     IVB_CUDA(cudaGetLastError());
   }
   return IVB_OK;
