@@ -15,6 +15,12 @@ Secondary, rank 0: prompt prefill tok/s at 512, 2048 and 819
 B200Decoder.prefill (tcgen05 GEMMs, recurrent scan, latent-cache fill and causal attention), and the
 int8 tensor-core throughput of the prefill GEMM alone on the gate/up shape at 2048 tokens.
 
+Secondary, every rank: batched serving, 256 independent sequences split evenly over
+the N GPUs (data parallel, no collective on the data path), each a 128-token random prompt and then
+sampled tokens (T 0.5, top-k 40, rp 1.15, per-sequence seeds) through B200BatchDecoder; `batched.value`
+is the aggregate decode tok/s (all sequences' tokens over the slowest rank's CUDA-event time of the
+timed decode steps).
+
 --impl reference times the reference algorithm's CPU implementation (the C port in oracle/, all host
 threads) on a bounded sample of the same workload, rank 0 only.
 """
@@ -53,6 +59,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--only", choices=("prefill", "gemm"), default=None,
                     help="run one secondary measurement alone (for profiler captures): a prefill of "
                          "--prefill-tokens tokens, or the prefill GEMM on the gate/up shape")
@@ -199,6 +206,32 @@ def run_reference(args) -> None:
 
 
 INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
+BATCH_SEQUENCES, BATCH_PROMPT, BATCH_TOKENS, BATCH_WARM = 256, 128, 512, 8
+
+
+def batch_measure(device, world: int, rank: int) -> dict:
+    """Config 3 on this rank: BATCH_SEQUENCES / world sequences decoded together (B200BatchDecoder)."""
+    import torch
+
+    from ivonar_inference_b200 import synthetic
+    from ivonar_inference_b200.batch import B200BatchDecoder
+
+    per_rank = max(1, BATCH_SEQUENCES // world)
+    model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
+    max_len = BATCH_PROMPT + BATCH_TOKENS + 8
+    batch = B200BatchDecoder(model, per_rank, max_len=max_len, device=device, history_len=BATCH_TOKENS)
+    first = rank * per_rank
+    prompts = [synthetic.random_prompt(32768, BATCH_PROMPT, seed=50_000 + first + i)[0] for i in range(per_rank)]
+    batch.start(prompts, [first + i for i in range(per_rank)], TEMPERATURE, TOP_K, PENALTY)
+    batch.decode(BATCH_WARM)  # includes the graph capture
+    torch.cuda.synchronize(device)
+    timed = BATCH_TOKENS - 1 - BATCH_WARM
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    batch.decode(timed)
+    end.record()
+    torch.cuda.synchronize(device)
+    return {"sequences_per_gpu": per_rank, "ms": start.elapsed_time(end), "steps": timed}
 
 
 def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps: int = 20) -> dict:
@@ -348,6 +381,21 @@ def run_b200(args) -> None:
         dist.all_reduce(e2e_total, op=dist.ReduceOp.MAX)
     e2e_value = world * args.steps * tokens / (float(e2e_total.item()) / 1000.0)
 
+    ctas, phases = dec.ctas, dec.num_phases
+    batched = None
+    if not args.no_batch:
+        del dec
+        torch.cuda.empty_cache()
+        part = batch_measure(device, world, rank)
+        batch_ms = torch.tensor([part["ms"]], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(batch_ms, op=dist.ReduceOp.MAX)
+        seqs = part["sequences_per_gpu"] * world
+        batched = {"metric": "batched decode tok/s (aggregate, config 3)", "value": seqs * part["steps"] / (float(batch_ms.item()) / 1000.0),
+                   "unit": "tok/s", "sequences": seqs, "sequences_per_gpu": part["sequences_per_gpu"],
+                   "prompt": BATCH_PROMPT, "timed_steps": part["steps"], "ms": float(batch_ms.item()),
+                   "ms_per_step": float(batch_ms.item()) / part["steps"], "parallelism": f"dp{world}"}
+
     if rank == 0:
         peak, peak_kind = measured_peaks()
         nbytes, parts = decode_bytes(model, PROMPT + 1, tokens)
@@ -362,12 +410,14 @@ def run_b200(args) -> None:
             "warmup": args.warmup, "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "int8", "data": "synthetic",
             "config": {"workload": WORKLOAD, "l2": "flushed (256 MB write) before every step", "parallelism": f"dp{world}",
-                       "ctas": dec.ctas, "phases_per_token": dec.num_phases},
+                       "ctas": ctas, "phases_per_token": phases},
             "e2e": {"value": e2e_value, "unit": "tok/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": args.steps,
             "roofline": roofline,
             "clocks": clock_info,
         }
+        if batched is not None:
+            line["batched"] = batched
         if not args.no_prefill:
             line["prefill"] = prefill_measure(device)
         if world == 1 and not args.no_cpu_baseline:
