@@ -116,23 +116,48 @@ __global__ void __launch_bounds__(kThreads) ssm_value_kernel(IvbLayerDesc L, con
   value[i] = silu_f(conv);
 }
 
-// Recurrent scan over the tokens with the per-(token, head, state) coefficients computed cooperatively
-// for blocks of 32 tokens into shared memory. CTA: 16 channels x 16 state lanes (lane s of a channel's
-// half-warp owns state s). The conv window of the block is advanced at the end. Same arithmetic per
-// step as the decode kernel.
+// Per-(token, head, state) coefficients of the recurrence, all tokens in parallel:
+// coef[t][h][s] = (tanh B, tanh C, half_dt, Re alpha, Im alpha) with alpha = exp(2 half_dt (decay + i theta)).
+__global__ void ssm_coef_kernel(IvbLayerDesc L, const float* ent, int T, int d, int H, int S, int ld, float half_dt_min,
+                                float half_dt_range, float* coefb) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * H * S) return;
+  const int t = i / (H * S), rest = i - t * (H * S), h = rest / S, s = rest - h * S;
+  const float* bcdt = ent + static_cast<size_t>(t) * ld + 2 * d + h * 3 * S;
+  const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s]) * half_dt_range;
+  const float mag = expf(2.0f * half_dt * L.decay[h * S + s]);
+  float sn, cs;
+  sincosf(2.0f * half_dt * L.theta[h * S + s], &sn, &cs);
+  float* cf = coefb + static_cast<size_t>(i) * 5;
+  cf[0] = tanhf(bcdt[s]);
+  cf[1] = tanhf(bcdt[S + s]);
+  cf[2] = half_dt;
+  cf[3] = mag * cs;
+  cf[4] = mag * sn;
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+
+// Recurrent scan over the tokens in blocks of 32: the block's coefficients (ssm_coef_kernel), conv
+// values (ssm_value_kernel) and gates are copied into shared memory with cp.async one block ahead, the
+// recurrence runs with one lane per state (nothing but the complex update on the sequential path), and
+// the 16-lane sums and the output gate run afterwards for the whole block. CTA: 16 channels x 16 state
+// lanes. Same arithmetic per step as the decode kernel.
 constexpr int kScanBlock = 32;
-__global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L, const float* ent, const float* value, int T,
-                                                                  int d, int H, int hd, int S, int taps, float half_dt_min,
-                                                                  float half_dt_range, float* y) {
+constexpr int kScanCh = 16;                // channels per CTA
+constexpr int kScanThreads = 16 * kScanCh;
+__global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDesc L, const float* ent, const float* value,
+                                                                  const float* coefb, int T, int d, int H, int hd, int S,
+                                                                  int taps, float* y) {
   extern __shared__ float sh[];
   const int tid = threadIdx.x, sub = tid & 15, chl = tid >> 4;
-  const int c0 = blockIdx.x * 16, c = c0 + chl;
+  const int c0 = blockIdx.x * kScanCh, c = c0 + chl;
   const bool live = c < d;
-  const int h0 = c0 / hd, nhc = (min(d, c0 + 16) - 1) / hd - h0 + 1;  // heads spanned by the CTA's channels
-  float* coef = sh;                                   // [kScanBlock][nhc][S][5]
-  float* vals = coef + kScanBlock * nhc * S * 5;      // [kScanBlock][16]
-  float* gates = vals + kScanBlock * 16;              // [kScanBlock][16]
-  float* ctb = gates + kScanBlock * 16;               // [kScanBlock][256]: C * Re(state) per (channel, lane)
+  const int h0 = c0 / hd, nhc = (min(d, c0 + kScanCh) - 1) / hd - h0 + 1;  // heads spanned by the CTA's channels
+  const int per_blk = kScanBlock * nhc * S * 5 + 2 * kScanBlock * kScanCh;  // coef | vals | gates
+  float* ctb = sh + 2 * per_blk;                                            // [kScanBlock][threads]: C * Re(state)
   const int ld = 2 * d + 3 * H * S;
   const int h = live ? c / hd : h0, dd = live ? c - h * hd : 0;
   const bool on = live && sub < S;
@@ -140,39 +165,49 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
   const size_t si_idx = (static_cast<size_t>(h) * S + s) * hd + dd;
   float sr = on ? L.ssm_state[2 * si_idx] : 0.0f, si = on ? L.ssm_state[2 * si_idx + 1] : 0.0f;
   float prev = on ? L.prev_force[si_idx] : 0.0f;
-  for (int t0 = 0; t0 < T; t0 += kScanBlock) {
+  auto prefetch = [&](int t0, float* buf) {
     const int nt = min(kScanBlock, T - t0);
-    __syncthreads();
-    for (int idx = tid; idx < nt * nhc * S; idx += kThreads) {
-      const int tt = idx / (nhc * S), rest = idx - tt * (nhc * S), hl = rest / S, s2 = rest - hl * S;
-      const int hh = h0 + hl;
-      const float* bcdt = ent + static_cast<size_t>(t0 + tt) * ld + 2 * d + hh * 3 * S;
-      const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * half_dt_range;
-      const float mag = expf(2.0f * half_dt * L.decay[hh * S + s2]);
-      float sn, cs;
-      sincosf(2.0f * half_dt * L.theta[hh * S + s2], &sn, &cs);
-      float* cf = coef + (static_cast<size_t>(tt) * nhc * S + hl * S + s2) * 5;
-      cf[0] = tanhf(bcdt[s2]);
-      cf[1] = tanhf(bcdt[S + s2]);
-      cf[2] = half_dt;
-      cf[3] = mag * cs;
-      cf[4] = mag * sn;
+    float* coef = buf;
+    float* vals = coef + kScanBlock * nhc * S * 5;
+    float* gates = vals + kScanBlock * kScanCh;
+    const int row = nhc * S * 5;  // coefficients of the CTA's heads for one token, contiguous
+    for (int idx = tid; idx < nt * row; idx += kScanThreads) {
+      const int tt = idx / row, k = idx - tt * row;
+      cp_async4(coef + idx, coefb + (static_cast<size_t>(t0 + tt) * H + h0) * S * 5 + k);
     }
-    for (int idx = tid; idx < nt * 16; idx += kThreads) {
-      const int tt = idx >> 4, ch = idx & 15;
-      const int cc2 = c0 + ch;
-      vals[idx] = cc2 < d ? value[static_cast<size_t>(t0 + tt) * d + cc2] : 0.0f;
-      gates[idx] = cc2 < d ? ent[static_cast<size_t>(t0 + tt) * ld + d + cc2] : 0.0f;
+    for (int idx = tid; idx < nt * kScanCh; idx += kScanThreads) {
+      const int tt = idx / kScanCh, cc2 = c0 + (idx % kScanCh);
+      if (cc2 < d) {
+        cp_async4(vals + idx, value + static_cast<size_t>(t0 + tt) * d + cc2);
+        cp_async4(gates + idx, ent + static_cast<size_t>(t0 + tt) * ld + d + cc2);
+      } else {
+        vals[idx] = 0.0f;
+        gates[idx] = 0.0f;
+      }
     }
-    __syncthreads();
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  prefetch(0, sh);
+  for (int t0 = 0, blk = 0; t0 < T; t0 += kScanBlock, ++blk) {
+    const int nt = min(kScanBlock, T - t0);
+    float* buf = sh + (blk & 1) * per_blk;
+    const float* coef = buf;
+    const float* vals = coef + kScanBlock * nhc * S * 5;
+    const float* gates = vals + kScanBlock * kScanCh;
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // this block's data has landed; the other buffer and ctb are free
+    if (t0 + kScanBlock < T) prefetch(t0 + kScanBlock, sh + ((blk + 1) & 1) * per_blk);
     const int hl = h - h0;
+    const float* cf0 = coef + (hl * S + s) * 5;
+    const int cstep = nhc * S * 5;
     // the recurrence alone stays on the sequential path; the per-channel sums over the state lanes and
     // the output gate run afterwards for the whole block
+#pragma unroll 4
     for (int tt = 0; tt < nt; ++tt) {
-      const float v = vals[tt * 16 + chl];
+      const float v = vals[tt * kScanCh + chl];
       float contrib = 0.0f;
       if (on) {
-        const float* cf = coef + (static_cast<size_t>(tt) * nhc * S + hl * S + s) * 5;
+        const float* cf = cf0 + tt * cstep;
         const float b = cf[0], cc = cf[1], half_dt = cf[2], ar = cf[3], ai = cf[4];
         const float force = b * v;
         const float dr = (force + ar * prev) * half_dt;
@@ -184,19 +219,19 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_block_kernel(IvbLayerDesc L
         prev = force;
         contrib = cc * nr;
       }
-      ctb[tt * kThreads + tid] = contrib;
+      ctb[tt * kScanThreads + tid] = contrib;
     }
     __syncthreads();
-    for (int idx = tid; idx < nt * 16; idx += kThreads) {
-      const int tt = idx >> 4, ch = idx & 15, cc2 = c0 + ch;
+    for (int idx = tid; idx < nt * kScanCh; idx += kScanThreads) {
+      const int tt = idx / kScanCh, ch = idx % kScanCh, cc2 = c0 + ch;
       if (cc2 >= d) continue;
       // the xor-butterfly order of the decode kernel's 16-lane warp sum (offsets 8, 4, 2, 1), lane 0
-      const float* v = ctb + tt * kThreads + ch * 16;
+      const float* v = ctb + tt * kScanThreads + ch * 16;
       float a[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] = v[i] + v[i + 8];
       const float sum = ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
-      y[static_cast<size_t>(t0 + tt) * d + cc2] = (sum + L.skip[cc2] * vals[idx]) * sigmoid_f(gates[idx]);
+      y[static_cast<size_t>(t0 + tt) * d + cc2] = (sum + __ldg(L.skip + cc2) * vals[idx]) * sigmoid_f(gates[idx]);
     }
   }
   if (on) {
@@ -583,7 +618,7 @@ __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_
 }
 
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, err, kvq8, knope, vbuf, kvh, total;
+  size_t resid, ent, y, h, q8, scale, err, coef, kvq8, knope, vbuf, kvh, total;
   int ldq, groups, ld_ent;
 };
 
@@ -609,6 +644,7 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.q8 = take((T + 127) / 128 * 128 * L.ldq);  // whole 128-token tiles
   L.scale = take(T * 4);
   L.err = take(16);
+  L.coef = take(T * md.heads * md.state_dim * 5 * 4);  // recurrence coefficients of a mamba block
   // latent attention: the cached latent of every position in the GEMM layout, and its keys and values
   bool mla = false;
   for (int i = 0; i < md.num_layers; ++i) mla = mla || layers[i].kind == IVB_MLA;
@@ -665,6 +701,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   float* knope = reinterpret_cast<float*>(ws + W.knope);
   float* vbuf = reinterpret_cast<float*>(ws + W.vbuf);
   __half* kvh = reinterpret_cast<__half*>(ws + W.kvh);
+  float* coefb = reinterpret_cast<float*>(ws + W.coef);
   int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
   float* scale = reinterpret_cast<float*>(ws + W.scale);
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
@@ -688,11 +725,15 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       const int ld = 2 * d + 3 * H * S;
       ssm_value_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, ld, L.conv_taps, hbuf);
       IVB_CUDA(cudaGetLastError());
-      const int nhc_max = std::min(16, 15 / hd + 2);
-      const size_t smem = (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * 16 + kScanBlock * kThreads) * 4;
+      ssm_coef_kernel<<<(count * H * S + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, H, S, ld, L.half_dt_min,
+                                                                                 L.half_dt_range, coefb);
+      IVB_CUDA(cudaGetLastError());
+      const int nhc_max = std::min(H, (kScanCh - 1) / hd + 2);
+      const size_t smem =
+          (2 * (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * kScanCh) + kScanBlock * kScanThreads) * 4;
       IVB_CUDA(cudaFuncSetAttribute(ssm_scan_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      ssm_scan_block_kernel<<<(d + 15) / 16, kThreads, smem, s>>>(L, ent, hbuf, count, d, H, hd, S, L.conv_taps, L.half_dt_min,
-                                                                   L.half_dt_range, y);
+      ssm_scan_block_kernel<<<(d + kScanCh - 1) / kScanCh, kScanThreads, smem, s>>>(L, ent, hbuf, coefb, count, d, H, hd, S,
+                                                                                  L.conv_taps, y);
       IVB_CUDA(cudaGetLastError());
     } else if (L.kind == IVB_MAMBA) {
       const int blocks = (d * 16 + kThreads - 1) / kThreads;
