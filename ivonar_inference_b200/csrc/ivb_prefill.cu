@@ -140,36 +140,54 @@ __device__ __forceinline__ void cp_async4(void* dst, const void* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
 
-// Recurrent scan over the tokens in blocks of 32: the block's coefficients (ssm_coef_kernel), conv
-// values (ssm_value_kernel) and gates are copied into shared memory with cp.async one block ahead, the
-// recurrence runs with one lane per state (nothing but the complex update on the sequential path), and
-// the 16-lane sums and the output gate run afterwards for the whole block. CTA: 16 channels x 16 state
-// lanes. Same arithmetic per step as the decode kernel.
+// Chunked scan. The recurrence is linear in the state: x_t = a_t x_{t-1} + u_t with
+// u_t = half_dt_t (f_t + a_t f_{t-1}) (f = B v, the force, an input), so the tokens split into chunks
+// of kScanChunk that run in parallel: each chunk scans from a zero state (its x~_t), the chunk-local
+// products A_t = a_first..a_t (ssm_cumprod_kernel) carry a chunk's start state to every token, a short
+// pass over the chunks (ssm_carry_kernel) finds each chunk's start state, and ssm_output_kernel adds
+// C_t Re(A_t x_start) to the chunk's partial output and applies skip and gate:
+//   x_t = x~_t + A_t x_start(chunk of t).
+// The per-step arithmetic is the decode step's; only the grouping of the state sums differs.
+//
+// Chunk scan (grid: channel groups x chunks): blocks of 32 tokens, the block's coefficients
+// (ssm_coef_kernel), conv values (ssm_value_kernel) copied into shared memory with cp.async one block
+// ahead, the recurrence with one lane per state, the 16-lane sums afterwards for the whole block
+// (written to y as the partial output). CTA: 16 channels x 16 state lanes.
 constexpr int kScanBlock = 32;
+constexpr int kScanChunk = 128;            // tokens per chunk (a multiple of kScanBlock)
 constexpr int kScanCh = 16;                // channels per CTA
 constexpr int kScanThreads = 16 * kScanCh;
 __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDesc L, const float* ent, const float* value,
                                                                   const float* coefb, int T, int d, int H, int hd, int S,
-                                                                  int taps, float* y) {
+                                                                  int taps, float* xend, float* y) {
   extern __shared__ float sh[];
   const int tid = threadIdx.x, sub = tid & 15, chl = tid >> 4;
   const int c0 = blockIdx.x * kScanCh, c = c0 + chl;
   const bool live = c < d;
   const int h0 = c0 / hd, nhc = (min(d, c0 + kScanCh) - 1) / hd - h0 + 1;  // heads spanned by the CTA's channels
-  const int per_blk = kScanBlock * nhc * S * 5 + 2 * kScanBlock * kScanCh;  // coef | vals | gates
+  const int per_blk = kScanBlock * nhc * S * 5 + kScanBlock * kScanCh;  // coef | vals
   float* ctb = sh + 2 * per_blk;                                            // [kScanBlock][threads]: C * Re(state)
   const int ld = 2 * d + 3 * H * S;
   const int h = live ? c / hd : h0, dd = live ? c - h * hd : 0;
   const bool on = live && sub < S;
   const int s = on ? sub : 0;
   const size_t si_idx = (static_cast<size_t>(h) * S + s) * hd + dd;
-  float sr = on ? L.ssm_state[2 * si_idx] : 0.0f, si = on ? L.ssm_state[2 * si_idx + 1] : 0.0f;
-  float prev = on ? L.prev_force[si_idx] : 0.0f;
+  const int t_begin = blockIdx.y * kScanChunk, t_end = min(T, t_begin + kScanChunk);
+  const bool last_chunk = t_end == T;
+  // every chunk scans from a zero state; the force before the chunk is an input (or the stored one)
+  float sr = 0.0f, si = 0.0f, prev = 0.0f;
+  if (on) {
+    if (t_begin == 0) {
+      prev = L.prev_force[si_idx];
+    } else {
+      const float* cfp = coefb + ((static_cast<size_t>(t_begin - 1) * H + h) * S + s) * 5;
+      prev = cfp[0] * value[static_cast<size_t>(t_begin - 1) * d + c];
+    }
+  }
   auto prefetch = [&](int t0, float* buf) {
     const int nt = min(kScanBlock, T - t0);
     float* coef = buf;
     float* vals = coef + kScanBlock * nhc * S * 5;
-    float* gates = vals + kScanBlock * kScanCh;
     const int row = nhc * S * 5;  // coefficients of the CTA's heads for one token, contiguous
     for (int idx = tid; idx < nt * row; idx += kScanThreads) {
       const int tt = idx / row, k = idx - tt * row;
@@ -177,26 +195,20 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDe
     }
     for (int idx = tid; idx < nt * kScanCh; idx += kScanThreads) {
       const int tt = idx / kScanCh, cc2 = c0 + (idx % kScanCh);
-      if (cc2 < d) {
-        cp_async4(vals + idx, value + static_cast<size_t>(t0 + tt) * d + cc2);
-        cp_async4(gates + idx, ent + static_cast<size_t>(t0 + tt) * ld + d + cc2);
-      } else {
-        vals[idx] = 0.0f;
-        gates[idx] = 0.0f;
-      }
+      if (cc2 < d) cp_async4(vals + idx, value + static_cast<size_t>(t0 + tt) * d + cc2);
+      else vals[idx] = 0.0f;
     }
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
-  prefetch(0, sh);
-  for (int t0 = 0, blk = 0; t0 < T; t0 += kScanBlock, ++blk) {
-    const int nt = min(kScanBlock, T - t0);
+  prefetch(t_begin, sh);
+  for (int t0 = t_begin, blk = 0; t0 < t_end; t0 += kScanBlock, ++blk) {
+    const int nt = min(kScanBlock, t_end - t0);
     float* buf = sh + (blk & 1) * per_blk;
     const float* coef = buf;
     const float* vals = coef + kScanBlock * nhc * S * 5;
-    const float* gates = vals + kScanBlock * kScanCh;
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // this block's data has landed; the other buffer and ctb are free
-    if (t0 + kScanBlock < T) prefetch(t0 + kScanBlock, sh + ((blk + 1) & 1) * per_blk);
+    if (t0 + kScanBlock < t_end) prefetch(t0 + kScanBlock, sh + ((blk + 1) & 1) * per_blk);
     const int hl = h - h0;
     const float* cf0 = coef + (hl * S + s) * 5;
     const int cstep = nhc * S * 5;
@@ -231,17 +243,18 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDe
 #pragma unroll
       for (int i = 0; i < 8; ++i) a[i] = v[i] + v[i + 8];
       const float sum = ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
-      y[static_cast<size_t>(t0 + tt) * d + cc2] = (sum + __ldg(L.skip + cc2) * vals[idx]) * sigmoid_f(gates[idx]);
+      y[static_cast<size_t>(t0 + tt) * d + cc2] = sum;  // partial output, finished by ssm_output_kernel
     }
   }
   if (on) {
-    L.ssm_state[2 * si_idx] = sr;
-    L.ssm_state[2 * si_idx + 1] = si;
-    L.prev_force[si_idx] = prev;
+    const size_t xo = (static_cast<size_t>(blockIdx.y) * H * S * hd + si_idx) * 2;
+    xend[xo] = sr;
+    xend[xo + 1] = si;
+    if (last_chunk) L.prev_force[si_idx] = prev;
   }
   // the conv window after the last token: the last taps - 1 inputs (older window entries when T is short)
   __syncthreads();
-  if (live && sub == 0) {
+  if (last_chunk && live && sub == 0) {
     float w[kMaxTaps];
     for (int k = 0; k < taps - 1; ++k) {
       const int src = T - (taps - 1) + k;
@@ -249,6 +262,79 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDe
     }
     for (int k = 0; k < taps - 1; ++k) L.conv_state[static_cast<size_t>(c) * (taps - 1) + k] = w[k];
   }
+}
+
+// Chunk-local products of the decay factors: A[t][h][s] = a_first(chunk) ... a_t (complex), one thread
+// per (chunk, head, state).
+__global__ void ssm_cumprod_kernel(const float* coefb, int T, int H, int S, float* cum) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int chunks = (T + kScanChunk - 1) / kScanChunk;
+  if (i >= chunks * H * S) return;
+  const int k = i / (H * S), hs = i - k * (H * S);
+  float pr = 1.0f, pi = 0.0f;
+  for (int t = k * kScanChunk; t < min(T, (k + 1) * kScanChunk); ++t) {
+    const float* cf = coefb + (static_cast<size_t>(t) * H * S + hs) * 5;
+    const float ar = cf[3], ai = cf[4];
+    const float nr = pr * ar - pi * ai, ni = pr * ai + pi * ar;
+    pr = nr;
+    pi = ni;
+    cum[(static_cast<size_t>(t) * H * S + hs) * 2] = pr;
+    cum[(static_cast<size_t>(t) * H * S + hs) * 2 + 1] = pi;
+  }
+}
+
+// Start state of every chunk, one thread per (head, state, channel): x_start(0) = the stored state,
+// x_start(k + 1) = x~_end(k) + A_end(k) x_start(k); the state after the last token is stored.
+__global__ void ssm_carry_kernel(IvbLayerDesc L, const float* cum, const float* xend, int T, int H, int S, int hd,
+                                 float* carry) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int lanes = H * S * hd;
+  if (i >= lanes) return;
+  const int hs = i / hd;  // (h * S + s)
+  const int chunks = (T + kScanChunk - 1) / kScanChunk;
+  float xr = L.ssm_state[2 * static_cast<size_t>(i)], xi = L.ssm_state[2 * static_cast<size_t>(i) + 1];
+  for (int k = 0; k < chunks; ++k) {
+    carry[(static_cast<size_t>(k) * lanes + i) * 2] = xr;
+    carry[(static_cast<size_t>(k) * lanes + i) * 2 + 1] = xi;
+    const int t_last = min(T, (k + 1) * kScanChunk) - 1;
+    const float ar = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2], ai = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2 + 1];
+    const float er = xend[(static_cast<size_t>(k) * lanes + i) * 2], ei = xend[(static_cast<size_t>(k) * lanes + i) * 2 + 1];
+    const float nr = er + (ar * xr - ai * xi), ni = ei + (ar * xi + ai * xr);
+    xr = nr;
+    xi = ni;
+  }
+  L.ssm_state[2 * static_cast<size_t>(i)] = xr;
+  L.ssm_state[2 * static_cast<size_t>(i) + 1] = xi;
+}
+
+// y[t][c] = (partial + sum_s C_t Re(A_t x_start) + skip v_t) * sigmoid(gate_t), one thread per (t, c);
+// the sum over the states in the decode kernel's xor-butterfly order.
+__global__ void ssm_output_kernel(IvbLayerDesc L, const float* ent, const float* value, const float* coefb, const float* cum,
+                                  const float* carry, int T, int d, int H, int hd, int S, float* y) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * d) return;
+  const int t = i / d, c = i - t * d, h = c / hd, dd = c - h * hd;
+  const int k = t / kScanChunk;
+  const int lanes = H * S * hd;
+  const int ld = 2 * d + 3 * H * S;
+  float v[16];
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    v[s] = 0.0f;
+    if (s < S) {
+      const size_t hs = static_cast<size_t>(h) * S + s;
+      const float cc = coefb[(static_cast<size_t>(t) * H * S + hs) * 5 + 1];
+      const float ar = cum[(static_cast<size_t>(t) * H * S + hs) * 2], ai = cum[(static_cast<size_t>(t) * H * S + hs) * 2 + 1];
+      const size_t ci = (static_cast<size_t>(k) * lanes + hs * hd + dd) * 2;
+      v[s] = cc * (ar * carry[ci] - ai * carry[ci + 1]);
+    }
+  }
+  float a[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) a[j] = v[j] + v[j + 8];
+  const float corr = ((a[0] + a[4]) + (a[2] + a[6])) + ((a[1] + a[5]) + (a[3] + a[7]));
+  const float* row = ent + static_cast<size_t>(t) * ld;
+  y[i] = ((y[i] + corr) + __ldg(L.skip + c) * value[i]) * sigmoid_f(row[d + c]);
 }
 
 // Cache fill of one mla block for T tokens at positions pos0..: the quantised latent and the rotated,
@@ -618,7 +704,7 @@ __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_
 }
 
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, err, coef, kvq8, knope, vbuf, kvh, total;
+  size_t resid, ent, y, h, q8, scale, err, coef, cum, xend, carry, kvq8, knope, vbuf, kvh, total;
   int ldq, groups, ld_ent;
 };
 
@@ -645,6 +731,10 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   L.scale = take(T * 4);
   L.err = take(16);
   L.coef = take(T * md.heads * md.state_dim * 5 * 4);  // recurrence coefficients of a mamba block
+  L.cum = take(T * md.heads * md.state_dim * 2 * 4);   // chunk-local decay products
+  const size_t chunks = (T + kScanChunk - 1) / kScanChunk, lanes = static_cast<size_t>(md.heads) * md.state_dim * md.head_dim;
+  L.xend = take(chunks * lanes * 2 * 4);                // chunk-end states of the zero-start scans
+  L.carry = take(chunks * lanes * 2 * 4);               // chunk start states
   // latent attention: the cached latent of every position in the GEMM layout, and its keys and values
   bool mla = false;
   for (int i = 0; i < md.num_layers; ++i) mla = mla || layers[i].kind == IVB_MLA;
@@ -702,6 +792,9 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   float* vbuf = reinterpret_cast<float*>(ws + W.vbuf);
   __half* kvh = reinterpret_cast<__half*>(ws + W.kvh);
   float* coefb = reinterpret_cast<float*>(ws + W.coef);
+  float* cumb = reinterpret_cast<float*>(ws + W.cum);
+  float* xendb = reinterpret_cast<float*>(ws + W.xend);
+  float* carryb = reinterpret_cast<float*>(ws + W.carry);
   int8_t* q8 = reinterpret_cast<int8_t*>(ws + W.q8);
   float* scale = reinterpret_cast<float*>(ws + W.scale);
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
@@ -730,10 +823,18 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       IVB_CUDA(cudaGetLastError());
       const int nhc_max = std::min(H, (kScanCh - 1) / hd + 2);
       const size_t smem =
-          (2 * (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + 2 * kScanBlock * kScanCh) + kScanBlock * kScanThreads) * 4;
+          (2 * (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + kScanBlock * kScanCh) + kScanBlock * kScanThreads) * 4;
       IVB_CUDA(cudaFuncSetAttribute(ssm_scan_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-      ssm_scan_block_kernel<<<(d + kScanCh - 1) / kScanCh, kScanThreads, smem, s>>>(L, ent, hbuf, coefb, count, d, H, hd, S,
-                                                                                  L.conv_taps, y);
+      const int chunks = (count + kScanChunk - 1) / kScanChunk;
+      ssm_cumprod_kernel<<<(chunks * H * S + 127) / 128, 128, 0, s>>>(coefb, count, H, S, cumb);
+      IVB_CUDA(cudaGetLastError());
+      ssm_scan_block_kernel<<<dim3((d + kScanCh - 1) / kScanCh, chunks), kScanThreads, smem, s>>>(
+          L, ent, hbuf, coefb, count, d, H, hd, S, L.conv_taps, xendb, y);
+      IVB_CUDA(cudaGetLastError());
+      ssm_carry_kernel<<<(H * S * hd + 127) / 128, 128, 0, s>>>(L, cumb, xendb, count, H, S, hd, carryb);
+      IVB_CUDA(cudaGetLastError());
+      ssm_output_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, hbuf, coefb, cumb, carryb, count, d,
+                                                                                  H, hd, S, y);
       IVB_CUDA(cudaGetLastError());
     } else if (L.kind == IVB_MAMBA) {
       const int blocks = (d * 16 + kThreads - 1) / kThreads;
