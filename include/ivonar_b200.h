@@ -224,6 +224,32 @@ uint64_t ivb_batch_workspace_bytes(const IvbDecoder* dec, int32_t batch);
 int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* b, int32_t steps, void* workspace, uint64_t workspace_bytes,
                          void* stream);
 
+/* Unit steps of the batched decode for callers that orchestrate the layers themselves (tensor-parallel
+ * shards: `channels` = heads * head_dim of the shard, the entry rows laid out as the shard's
+ * [value | gate | B, C, dt per head] or [q | latent | k_rope]):
+ * ivb_batch_embed: resid[b] = embedding row of tokens[b] (advances *step_counter when not NULL);
+ * ivb_batch_ssm: one SSM step per sequence (recurrent_step, ternary.cu:421-482);
+ * ivb_batch_mla: latent-cache append at positions[b] and absorbed attention (ternary.cu:509-611);
+ * ivb_batch_sample: per-sequence sampler, then positions[b] += 1 (ternary.cu:1099-1337). */
+int32_t ivb_batch_embed(const IvbTernary* head, const int64_t* tokens, int32_t batch, int32_t hidden, float* resid,
+                        int32_t* step_counter, void* stream);
+int32_t ivb_batch_ssm(const IvbLayerDesc* layer, const IvbBatchLayer* state, const float* ent, int32_t ld, int32_t batch,
+                      int32_t channels, int32_t heads, int32_t head_dim, int32_t state_dim, float* y, void* stream);
+int32_t ivb_batch_mla(const IvbLayerDesc* layer, const IvbBatchLayer* state, const float* ent, int32_t ld,
+                      const int64_t* positions, int32_t batch, int32_t channels, int32_t latent, int32_t heads,
+                      int32_t head_dim, int32_t rope, int32_t nope, int32_t max_len, float act_eps, uint32_t* error,
+                      float* y, void* stream);
+int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int32_t batch, const float* sampling,
+                         const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
+                         int64_t* history, int32_t history_len, const int32_t* step_counter, void* stream);
+
+/* Per-row max |x| (rows x n fp32) into amax [rows]; with ivb_quantize_rows_amax the quantisation of a
+ * row-parallel shard uses the amax of the whole row (after an all-reduce MAX), so every shard's codes
+ * equal the unsharded quantiser's: scale = max(amax / 127, act_eps), code = rint(x / scale). */
+int32_t ivb_rows_amax(const float* x, int32_t rows, int32_t n, float* amax, void* stream);
+int32_t ivb_quantize_rows_amax(const float* x, int32_t rows, int32_t n, const float* amax, float act_eps, int8_t* q8,
+                               int32_t ldq, float* scale, void* stream);
+
 /* Debug/failure-detection probe: one CTA waits for a barrier count that never arrives, with a
  * bounded spin of timeout_ns; returns IVB_ETIMEOUT and leaves the context usable. */
 int32_t ivb_probe_wait_timeout(uint32_t* counter, uint32_t* error_word, uint64_t timeout_ns, void* stream);

@@ -157,6 +157,15 @@ SIGNATURES = {
     "ivb_decoder_prefill": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_uint64, c_void_p]),
     "ivb_batch_workspace_bytes": (c_uint64, [c_void_p, c_int32]),
     "ivb_batch_decode": (c_int32, [c_void_p, POINTER(IvbBatch), c_int32, c_void_p, c_uint64, c_void_p]),
+    "ivb_batch_embed": (c_int32, [POINTER(IvbTernary), c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_void_p]),
+    "ivb_batch_ssm": (c_int32, [POINTER(IvbLayerDesc), POINTER(IvbBatchLayer), c_void_p, c_int32, c_int32, c_int32, c_int32,
+                                c_int32, c_int32, c_void_p, c_void_p]),
+    "ivb_batch_mla": (c_int32, [POINTER(IvbLayerDesc), POINTER(IvbBatchLayer), c_void_p, c_int32, c_void_p, c_int32, c_int32,
+                                c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
+    "ivb_batch_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
+                                   c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
+    "ivb_rows_amax": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
+    "ivb_quantize_rows_amax": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_float, c_void_p, c_int32, c_void_p, c_void_p]),
     "ivb_decoder_check": (c_int32, [c_void_p, c_void_p]),
 }
 

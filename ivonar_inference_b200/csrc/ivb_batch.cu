@@ -443,4 +443,63 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
   return IVB_OK;
 }
 
+// ---- unit steps, for callers that orchestrate the layers themselves (tensor parallel) -----------
+
+int32_t ivb_batch_embed(const IvbTernary* head, const int64_t* tokens, int32_t batch, int32_t hidden, float* resid,
+                        int32_t* step_counter, void* stream) {
+  using namespace ivb;
+  if (head == nullptr || tokens == nullptr || resid == nullptr || batch <= 0 || hidden <= 0)
+    return fail(IVB_EINVAL, "ivb_batch_embed: bad argument");
+  batch_embed_kernel<<<batch, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(*head, tokens, hidden, resid, step_counter);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_batch_ssm(const IvbLayerDesc* L, const IvbBatchLayer* B, const float* ent, int32_t ld, int32_t batch,
+                      int32_t channels, int32_t heads, int32_t head_dim, int32_t state_dim, float* y, void* stream) {
+  using namespace ivb;
+  if (L == nullptr || B == nullptr || ent == nullptr || y == nullptr || batch <= 0 || channels != heads * head_dim ||
+      state_dim > 16 || L->conv_taps > kBatchTaps + 1)
+    return fail(IVB_EINVAL, "ivb_batch_ssm: bad argument");
+  const int nh_max = std::min(heads, kSsmChannels / head_dim + 2);
+  batch_ssm_kernel<<<dim3((channels + kSsmChannels - 1) / kSsmChannels, batch), kSsmChannels,
+                     nh_max * state_dim * 5 * 4, static_cast<cudaStream_t>(stream)>>>(
+      *L, *B, ent, ld, channels, heads, head_dim, state_dim, L->conv_taps, L->half_dt_min, L->half_dt_range, y);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_batch_mla(const IvbLayerDesc* L, const IvbBatchLayer* B, const float* ent, int32_t ld, const int64_t* positions,
+                      int32_t batch, int32_t channels, int32_t latent, int32_t heads, int32_t head_dim, int32_t rope,
+                      int32_t nope, int32_t max_len, float act_eps, uint32_t* error, float* y, void* stream) {
+  using namespace ivb;
+  if (L == nullptr || B == nullptr || ent == nullptr || positions == nullptr || y == nullptr || error == nullptr ||
+      batch <= 0 || channels != heads * head_dim || latent > 512 || rope > 128 || nope > 256)
+    return fail(IVB_EINVAL, "ivb_batch_mla: bad argument");
+  const int lpad = (latent + 15) / 16 * 16, rpad = (rope + 7) / 8 * 8;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  batch_cache_kernel<<<batch, kThreads, 0, s>>>(*L, *B, ent, ld, positions, channels, latent, heads, rope, max_len, lpad, rpad,
+                                                act_eps, error);
+  IVB_CUDA(cudaGetLastError());
+  batch_attention_kernel<<<dim3(batch, heads), kAttnThreads, 0, s>>>(*L, *B, ent, ld, positions, channels, latent, heads,
+                                                                     head_dim, rope, nope, max_len, lpad, rpad, y);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int32_t batch, const float* sampling,
+                         const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
+                         int64_t* history, int32_t history_len, const int32_t* step_counter, void* stream) {
+  using namespace ivb;
+  if (logits == nullptr || seen == nullptr || sampling == nullptr || top_k == nullptr || rng == nullptr ||
+      tokens == nullptr || positions == nullptr || batch <= 0 || vocab <= 0)
+    return fail(IVB_EINVAL, "ivb_batch_sample: bad argument");
+  const size_t smem = sample_smem_bytes(vocab);
+  IVB_CUDA(cudaFuncSetAttribute(batch_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  batch_sample_kernel<<<batch, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      logits, seen, vocab, sampling, top_k, max_top_k, rng, tokens, positions, history, history_len, step_counter);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
 }  // extern "C"

@@ -383,6 +383,56 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x,
   if (threadIdx.x == 0) scale[row] = s;
 }
 
+// Per-row max |x|.
+__global__ void __launch_bounds__(kThreads) rows_amax_kernel(const float* x, int n, float* amax) {
+  __shared__ float red[64];
+  const float* row = x + static_cast<size_t>(blockIdx.x) * n;
+  float am = 0.0f;
+  for (int i = threadIdx.x; i < n; i += kThreads) am = fmaxf(am, fabsf(row[i]));
+  const float m = block_max_nonneg(am, red);
+  if (threadIdx.x == 0) amax[blockIdx.x] = m;
+}
+
+// The quantiser without RMSNorm for a given amax per row (the whole row's, for a shard), codes in the
+// tiled GEMM layout: scale = max(amax / 127, act_eps), code = rint(x / scale) (the decode quantiser's
+// fast reciprocal path with its exact fallback near half-integers).
+__global__ void __launch_bounds__(kThreads) quantize_rows_amax_kernel(const float* x, int n, const float* amax_in,
+                                                                      float act_eps, int8_t* q8, int ldq, float* scale) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int pad = ((n + 63) >> 6) << 6;
+  int8_t* codes = reinterpret_cast<int8_t*>(smem);
+  const int row = blockIdx.x;
+  const float* xr = x + static_cast<size_t>(row) * n;
+  const float sc = fmaxf(amax_in[row] / 127.0f, act_eps);
+  const float rscale = 1.0f / sc;
+  for (int i = threadIdx.x; i < pad; i += kThreads) {
+    int q = 0;
+    if (i < n) {
+      const float v = xr[i];
+      bool nr = false;
+      q = quant_code_fast(v, rscale, nr);
+      if (nr) q = static_cast<int>(rintf(v / sc));
+    }
+    codes[i] = static_cast<int8_t>(q);
+  }
+  __syncthreads();
+  for (int k = threadIdx.x; k < (ldq >> 4); k += kThreads) {
+    uint32_t o[4];
+#pragma unroll
+    for (int f = 0; f < 4; ++f) {
+      uint32_t w = 0u;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        const int i = (k << 4) + 4 * b + f;
+        w |= (i < n ? static_cast<uint32_t>(static_cast<uint8_t>(codes[i])) : 0u) << (8 * b);
+      }
+      o[f] = w;
+    }
+    *reinterpret_cast<uint4*>(q8 + q8_chunk_offset(row, k, ldq)) = make_uint4(o[0], o[1], o[2], o[3]);
+  }
+  if (threadIdx.x == 0) scale[row] = sc;
+}
+
 }  // namespace ivb
 
 extern "C" {
@@ -458,6 +508,30 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
   const dim3 grid((m->rows + kGemmRows - 1) / kGemmRows, (rows_t + kGemmTok - 1) / kGemmTok);
   ternary_gemm_kernel<<<grid, kGemmThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       wmap, *m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, 2000000000ull, error);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_rows_amax(const float* x, int32_t rows, int32_t n, float* amax, void* stream) {
+  using namespace ivb;
+  if (x == nullptr || amax == nullptr || rows < 0 || n <= 0) return fail(IVB_EINVAL, "ivb_rows_amax: bad argument");
+  if (rows == 0) return IVB_OK;
+  rows_amax_kernel<<<rows, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, n, amax);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_quantize_rows_amax(const float* x, int32_t rows, int32_t n, const float* amax, float act_eps, int8_t* q8,
+                               int32_t ldq, float* scale, void* stream) {
+  using namespace ivb;
+  if (x == nullptr || amax == nullptr || q8 == nullptr || scale == nullptr) return fail(IVB_EINVAL, "ivb_quantize_rows_amax: null argument");
+  if (rows < 0 || n <= 0 || ldq < (n + 127) / 128 * 128 || (ldq & 127) || (reinterpret_cast<uintptr_t>(q8) & 15))
+    return fail(IVB_EINVAL, "ivb_quantize_rows_amax: bad shape (rows %d, n %d, ldq %d)", rows, n, ldq);
+  if (rows == 0) return IVB_OK;
+  const size_t smem = static_cast<size_t>((n + 63) / 64) * 64 + 64;
+  if (smem > 200 * 1024) return fail(IVB_EINVAL, "ivb_quantize_rows_amax: n %d too large", n);
+  IVB_CUDA(cudaFuncSetAttribute(quantize_rows_amax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  quantize_rows_amax_kernel<<<rows, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, n, amax, act_eps, q8, ldq, scale);
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
