@@ -21,6 +21,10 @@ sampled tokens (T 0.5, top-k 40, rp 1.15, per-sequence seeds) through B200BatchD
 is the aggregate decode tok/s (all sequences' tokens over the slowest rank's CUDA-event time of the
 timed decode steps).
 
+Secondary, every rank: the 7B-shaped model (weights drawn on the GPU) tensor
+parallel over the N ranks (`tp`): a 512-token random prompt teacher-forced, then sampled decode at batch
+1 and batch 32, tok/s over the slowest rank's CUDA-event time.
+
 --impl reference times the reference algorithm's CPU implementation (the C port in oracle/, all host
 threads) on a bounded sample of the same workload, rank 0 only.
 """
@@ -60,7 +64,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-clocks", action="store_true")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
-    ap.add_argument("--only", choices=("prefill", "gemm"), default=None,
+    ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks)")
+    ap.add_argument("--only", choices=("prefill", "gemm", "tp"), default=None,
                     help="run one secondary measurement alone (for profiler captures): a prefill of "
                          "--prefill-tokens tokens, or the prefill GEMM on the gate/up shape")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
@@ -300,6 +305,44 @@ def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps:
     return result
 
 
+TP_PROMPT, TP_TOKENS, TP_WARM = 512, 256, 4
+
+
+def tp_measure(device, world: int, rank: int) -> dict:
+    """Config 4 on this rank's shard: B200TensorParallel at batch 1 and 32, `world`-way tensor parallel."""
+    import torch
+    import torch.distributed as dist
+
+    from ivonar_inference_b200 import synthetic
+    from ivonar_inference_b200.tp import B200TensorParallel
+
+    model = synthetic.synthetic_model(synthetic.config4(seq_len=TP_PROMPT + TP_TOKENS + 16), seed=0, style="fast")
+    out: dict = {"metric": "decode tok/s, config 4 (7B-shaped), tensor parallel", "unit": "tok/s", "tp": world,
+                 "prompt": TP_PROMPT}
+    for batch in (1, 32):
+        tp = B200TensorParallel(model, rank, world, None, batch=batch, max_len=TP_PROMPT + TP_TOKENS + 8, device=device,
+                                history_len=TP_TOKENS)
+        prompts = synthetic.random_prompt(32768, TP_PROMPT, seed=777)[0].repeat(batch, 1)
+        prompts[:, -1] = torch.arange(batch) % 32768  # distinct last tokens
+        tp.start(prompts, list(range(batch)), TEMPERATURE, TOP_K, PENALTY)
+        tp.decode(TP_WARM)
+        torch.cuda.synchronize(device)
+        timed = TP_TOKENS - 1 - TP_WARM
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        tp.decode(timed)
+        end.record()
+        torch.cuda.synchronize(device)
+        ms = torch.tensor([start.elapsed_time(end)], dtype=torch.float64, device=device)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        out[f"b{batch}"] = {"value": batch * timed / (float(ms.item()) / 1000.0), "ms_per_step": float(ms.item()) / timed,
+                            "timed_steps": timed}
+        del tp
+        torch.cuda.empty_cache()
+    return out
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -382,6 +425,9 @@ def run_b200(args) -> None:
     e2e_value = world * args.steps * tokens / (float(e2e_total.item()) / 1000.0)
 
     ctas, phases = dec.ctas, dec.num_phases
+    tp_line = None
+    if args.tp:
+        tp_line = tp_measure(device, world, rank)
     batched = None
     if not args.no_batch:
         del dec
@@ -418,6 +464,8 @@ def run_b200(args) -> None:
         }
         if batched is not None:
             line["batched"] = batched
+        if tp_line is not None:
+            line["tp"] = tp_line
         if not args.no_prefill:
             line["prefill"] = prefill_measure(device)
         if world == 1 and not args.no_cpu_baseline:
@@ -431,6 +479,26 @@ def run_b200(args) -> None:
 
 def main() -> None:
     args = parse()
+    if args.only == "tp":
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        local = int(os.environ.get("LOCAL_RANK", "0"))
+        torch.cuda.set_device(local)
+        device = torch.device("cuda", local)
+        if world > 1:
+            dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
+        result = tp_measure(device, world, rank)
+        if rank == 0:
+            print(json.dumps(result), flush=True)
+        if world > 1:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.only is not None:
         import torch
 

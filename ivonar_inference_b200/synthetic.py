@@ -64,6 +64,9 @@ def tiny(hidden: int = 16, heads: int = 4, state_dim: int = 3, latent: int = 8, 
 def _codes(gen: torch.Generator, rows: int, cols: int, style: str) -> torch.Tensor:
     if style == "reference_tests":
         return torch.randint(0, 3, (rows, cols), generator=gen, dtype=torch.uint8)
+    if style == "fast":  # the same code distribution, drawn on the generator's device
+        r = torch.randint(0, 10, (rows, cols), generator=gen, dtype=torch.uint8, device=gen.device)
+        return (r >= 3).to(torch.uint8) + (r >= 7).to(torch.uint8)
     r = torch.rand(rows, cols, generator=gen)
     return (r >= 0.3).to(torch.uint8) + (r >= 0.7).to(torch.uint8)
 
@@ -76,8 +79,8 @@ def _packed(gen: torch.Generator, rows: int, cols: int, style: str) -> tuple[tor
     if style == "reference_tests":
         scales = (torch.rand(rows, groups, generator=gen) * 0.05 + 0.01).half()
     else:
-        scales = torch.exp(math.log(0.02) + 0.3 * torch.randn(rows, groups, generator=gen)).half()
-    return packed.contiguous(), scales
+        scales = torch.exp(math.log(0.02) + 0.3 * torch.randn(rows, groups, generator=gen, device=gen.device)).half()
+    return packed.contiguous().cpu(), scales.cpu()
 
 
 def synthetic_state(payload: dict, seed: int = 0, style: str = "baseline") -> dict[str, torch.Tensor]:
@@ -85,10 +88,14 @@ def synthetic_state(payload: dict, seed: int = 0, style: str = "baseline") -> di
 
     config = ModelConfig.from_payload(payload)
     gen = torch.Generator().manual_seed(int(seed))
+    # "fast": the packed matrices are drawn on the GPU when there is one (the 7B-shaped model in seconds)
+    big = gen
+    if style == "fast" and torch.cuda.is_available():
+        big = torch.Generator(device="cuda").manual_seed(int(seed))
     state: dict[str, torch.Tensor] = {}
 
     def linear(prefix: str, rows: int, cols: int, bias: bool = True) -> None:
-        packed, scales = _packed(gen, rows, cols, style)
+        packed, scales = _packed(big, rows, cols, style)
         state[f"{prefix}.packed_weight"] = packed
         state[f"{prefix}.weight_scales"] = scales
         if bias:

@@ -71,7 +71,8 @@ class B200TensorParallel:
     """`batch` sequences decoded with the blocks sharded over `world` ranks (this process is `rank`)."""
 
     def __init__(self, model, rank: int, world: int, group=None, batch: int = 1, max_len: int = 1024,
-                 device: str | torch.device | None = None, max_top_k: int = 256, history_len: int = 1024) -> None:
+                 device: str | torch.device | None = None, max_top_k: int = 256, history_len: int = 1024,
+                 graphs: bool = True) -> None:
         dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
         self.device, self.rank, self.world, self.group = dev, int(rank), int(world), group
         self.batch, self.max_len, self.max_top_k = int(batch), int(max_len), int(max_top_k)
@@ -196,6 +197,8 @@ class B200TensorParallel:
         self.top_k = torch.ones(1, dtype=torch.int64, device=dev)
         self.error = torch.zeros(1, dtype=torch.int32, device=dev)
         self.host_position = 0
+        self.use_graphs = bool(graphs)
+        self._graph: torch.cuda.CUDAGraph | None = None
 
     # ------------------------------------------------------------------------------------------
     def _stream(self) -> int:
@@ -311,11 +314,30 @@ class B200TensorParallel:
 
     @torch.no_grad()
     def decode(self, steps: int) -> Tensor:
-        """`steps` sampled tokens per sequence (each fed back); returns them [batch, steps]."""
+        """`steps` sampled tokens per sequence (each fed back); returns them [batch, steps]. After one eager
+        step, a whole step (kernels and NCCL all-reduces) is captured once as a CUDA graph and replayed."""
 
+        steps = int(steps)
         done = int(self.step_counter.item())
-        for _ in range(int(steps)):
+        if self.host_position + steps > self.max_len:
+            raise ValueError("the decoder has no free position left (capacity)")
+        run = steps
+        if self.use_graphs and run > 0 and self._graph is None:
             self.step()
+            run -= 1
+            if run > 0:
+                graph = torch.cuda.CUDAGraph()
+                position = self.host_position
+                with torch.cuda.graph(graph):
+                    self.step()
+                self.host_position = position  # capture records the step without running it
+                self._graph = graph
+        for _ in range(run):
+            if self._graph is not None:
+                self._graph.replay()
+                self.host_position += 1
+            else:
+                self.step()
         if int(self.error.item()) != 0:
             raise native.KernelError(f"tensor-parallel step reported error {int(self.error.item())}")
         return self.history[:, done:done + int(steps)]
