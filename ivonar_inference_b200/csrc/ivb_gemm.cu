@@ -127,7 +127,7 @@ __device__ __forceinline__ void mbar_arrive(unsigned long long* bar) {
 __global__ void __launch_bounds__(kGemmThreads, 1)
     ternary_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const IvbTernary m, const int8_t* __restrict__ q8,
                         int ldq, const float* __restrict__ act_scale, int T, int epilogue, float* out, int ldo,
-                        unsigned long long timeout_ns, unsigned* error) {
+                        int g_per, float* partial, unsigned long long timeout_ns, unsigned* error) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       smem_raw + ((1024u - (static_cast<unsigned>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u);
@@ -138,7 +138,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ int failed;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kGemmTok;
-  const int groups = (m.in_features + 127) >> 7;
+  const int groups_all = (m.in_features + 127) >> 7;
+  // split-K: this CTA's groups [g_lo, g_lo + groups); loop indices below are local to the split
+  const int g_lo = blockIdx.z * g_per;
+  const int groups = max(0, min(groups_all, g_lo + g_per) - g_lo);
   unsigned char* pack = smem + kGemmStages * kGemmTile;           // packed ring
   float* scale_tab = reinterpret_cast<float*>(pack + kPackSlots * kPackSlot);  // [groups][128 rows]
   if (warp == kGemmMmaWarp) {
@@ -165,7 +168,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int g = 0; g < kPackSlots && g < groups; ++g) {
       mbar_expect_tx(pk_bar + g, kPackSlot);
-      tma_load_2d(pack + g * kPackSlot, &wmap, g << 5, r0, pk_bar + g);
+      tma_load_2d(pack + g * kPackSlot, &wmap, (g_lo + g) << 5, r0, pk_bar + g);
     }
   }
   tc_fence_before();
@@ -193,7 +196,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (pj == 0) {
         mbar_expect(full_bar + st, kGemmTile);
-        bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(g) * kGemmTile, kGemmTile, full_bar + st);
+        bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(g_lo + g) * kGemmTile, kGemmTile, full_bar + st);
         issued = g + 1;
       }
       // row's 16 packed words -> 32 TMEM columns: column 4c + f holds the codes (w_c >> 2f) & 0x03030303
@@ -219,7 +222,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           break;
         }
         mbar_expect_tx(pk_bar + prev % kPackSlots, kPackSlot);
-        tma_load_2d(pack + (prev % kPackSlots) * kPackSlot, &wmap, nxt << 5, r0, pk_bar + prev % kPackSlots);
+        tma_load_2d(pack + (prev % kPackSlots) * kPackSlot, &wmap, (g_lo + nxt) << 5, r0, pk_bar + prev % kPackSlots);
         pk_issued = nxt + 1;
       }
     }
@@ -249,7 +252,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   } else {
     // ---- epilogue: drain, scale, accumulate ----
     for (int i = tid; i < groups * kGemmRows; i += 32 * kGemmEpiWarps) {
-      const int g = i >> 7, r = r0 + (i & 127);
+      const int g = g_lo + (i >> 7), r = r0 + (i & 127);
       scale_tab[i] = r < m.rows ? h2f(__ldg(m.scales + static_cast<size_t>(r) * m.scale_stride + g)) : 0.0f;
     }
     asm volatile("bar.sync 1, %0;" ::"n"(32 * kGemmEpiWarps) : "memory");
@@ -307,6 +310,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const bool vec = (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
     for (int tr = warp; tr < kGemmTok && t0 + tr < T; tr += kGemmThreads / 32) {
       const int tt = t0 + tr;
+      if (partial != nullptr) {  // split-K: this split's raw sums; scale, bias and epilogue in the reduction
+        const float4 v4 = *reinterpret_cast<const float4*>(tile + tr * kLd + 4 * lane);
+        const float pv[4] = {v4.x, v4.y, v4.z, v4.w};
+        float* prow = partial + (static_cast<size_t>(blockIdx.z) * T + tt) * m.rows;
+        const int r = r0 + 4 * lane;
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (r + e < m.rows) prow[r + e] = pv[e];
+        continue;
+      }
       const float sc = __ldg(act_scale + tt);
       const float4 v4 = *reinterpret_cast<const float4*>(tile + tr * kLd + 4 * lane);
       float v[4] = {v4.x * sc, v4.y * sc, v4.z * sc, v4.w * sc};
@@ -340,6 +353,35 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __syncthreads();
   if (warp == kGemmMmaWarp) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
 }
+
+// Split-K reduction: out = epilogue(act_scale[t] * sum_z partial[z][t][r] + bias[r]), splits summed in order.
+__global__ void gemm_splitk_reduce_kernel(const float* partial, int splits, int T, int rows, const float* act_scale,
+                                          const float* bias, int epilogue, float* out, int ldo) {
+  const int per_row = epilogue == IVB_EPI_SILU_PAIR ? rows / 2 : rows;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= T * per_row) return;
+  const int t = i / per_row, j = i - t * per_row;
+  const float sc = __ldg(act_scale + t);
+  auto value = [&](int r) {
+    float v = 0.0f;
+    for (int z = 0; z < splits; ++z) v += partial[(static_cast<size_t>(z) * T + t) * rows + r];
+    v *= sc;
+    if (bias != nullptr) v += __ldg(bias + r);
+    return v;
+  };
+  float* orow = out + static_cast<size_t>(t) * ldo;
+  if (epilogue == IVB_EPI_SILU_PAIR) {
+    orow[j] = silu_f(value(2 * j)) * value(2 * j + 1);
+  } else {
+    const float v = value(j);
+    orow[j] = epilogue == IVB_EPI_RESIDUAL ? orow[j] + v : v;
+  }
+}
+
+// Partial sums of split-K GEMM calls (token counts too small to fill the GPU with row tiles): a file-scope
+// device scratch, so the library allocates nothing; calls on one device use it one at a time.
+constexpr size_t kGemmScratch = size_t(1) << 22;  // floats
+static __device__ __align__(256) float g_gemm_partial[kGemmScratch];
 
 // One CTA per token row: the canonical quantiser (RMSNorm optional), codes written as 16-byte chunks of
 // the tiled GEMM activation layout (q8_chunk_offset, gemm_slot order inside a chunk), per-128-group sums
@@ -476,6 +518,28 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 
 extern "C" {
 
+}  // extern "C"
+
+namespace ivb {
+namespace {
+int32_t gemm_scratch(int dev, float** out) {
+  static std::mutex lock;
+  static float* table[64] = {};
+  if (dev < 0 || dev >= 64) return fail(IVB_EINVAL, "ivb_ternary_gemm: device %d out of range", dev);
+  std::lock_guard<std::mutex> guard(lock);
+  if (table[dev] == nullptr) {
+    void* p = nullptr;
+    IVB_CUDA(cudaGetSymbolAddress(&p, g_gemm_partial));
+    table[dev] = static_cast<float*>(p);
+  }
+  *out = table[dev];
+  return IVB_OK;
+}
+}  // namespace
+}  // namespace ivb
+
+extern "C" {
+
 int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
                          int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream) {
   using namespace ivb;
@@ -505,10 +569,34 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return fail(IVB_EINVAL, "ivb_ternary_gemm: cannot describe the packed weights to the TMA engine");
-  const dim3 grid((m->rows + kGemmRows - 1) / kGemmRows, (rows_t + kGemmTok - 1) / kGemmTok);
-  ternary_gemm_kernel<<<grid, kGemmThreads, smem, static_cast<cudaStream_t>(stream)>>>(
-      wmap, *m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, 2000000000ull, error);
+  // split-K when the row and token tiles leave most SMs idle (decode-sized token counts): at least four
+  // groups per split, at most 8 splits, the partials within the device scratch
+  const int row_tiles = (m->rows + kGemmRows - 1) / kGemmRows, tok_tiles = (rows_t + kGemmTok - 1) / kGemmTok;
+  int splits = 1;
+  if (groups >= 8 && row_tiles * tok_tiles < 96) {
+    splits = std::min({groups / 4, std::max(1, 148 / (row_tiles * tok_tiles)), 8});
+    while (splits > 1 && static_cast<size_t>(splits) * rows_t * m->rows > kGemmScratch) --splits;
+  }
+  const int g_per = (groups + splits - 1) / splits;
+  splits = (groups + g_per - 1) / g_per;
+  float* partial = nullptr;
+  if (splits > 1) {
+    int dev = 0;
+    IVB_CUDA(cudaGetDevice(&dev));
+    if (int32_t rc = gemm_scratch(dev, &partial)) return rc;
+  }
+  const dim3 grid(row_tiles, tok_tiles, splits);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  ternary_gemm_kernel<<<grid, kGemmThreads, smem, s>>>(wmap, *m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, g_per,
+                                                        partial, 2000000000ull, error);
   IVB_CUDA(cudaGetLastError());
+  if (splits > 1) {
+    const int per_row = epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows;
+    const int n = rows_t * per_row;
+    gemm_splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial, splits, rows_t, m->rows, act_scale, m->bias, epilogue,
+                                                            out, ldo);
+    IVB_CUDA(cudaGetLastError());
+  }
   return IVB_OK;
 }
 
