@@ -177,15 +177,36 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attention_kernel(IvbLayerD
   }
   for (int e = tid; e < nope; e += kAttnThreads) qn[e] = q[e] * scl;
   __syncthreads();
-  // absorbed query
+  // absorbed query qa[j] = sum_e qn[e] W_k[h nope + e][j]: thread = (e-group, 16-input word of the
+  // latent row), the e-groups summed in order through shared memory
   const IvbTernary& kn = L.k_nope_up;
-  for (int j = tid; j < Lt; j += kAttnThreads) {
-    float acc = 0.0f;
-    for (int e = 0; e < nope; ++e) {
-      const size_t r = static_cast<size_t>(h) * nope + e;
-      acc = fmaf(qn[e], code_value(kn.packed + r * kn.row_bytes, j) * h2f(__ldg(kn.scales + r * kn.scale_stride + (j >> 7))), acc);
+  {
+    const int words = (Lt + 15) >> 4, n_eg = kAttnThreads / words;  // n_eg * Lt <= 2048 = part
+    float* pe = &part[0][0];
+    const int wd = tid % words, eg = tid / words;
+    if (eg < n_eg) {
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+      for (int e = eg; e < nope; e += n_eg) {
+        const size_t r = static_cast<size_t>(h) * nope + e;
+        const unsigned w = __ldg(reinterpret_cast<const unsigned*>(kn.packed + r * kn.row_bytes) + wd);
+        const float qs = qn[e] * h2f(__ldg(kn.scales + r * kn.scale_stride + (wd >> 3)));
+        float cm1[16];
+        word_codes_m1(w, cm1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(qs, cm1[i], acc[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (wd * 16 + i < Lt) pe[eg * Lt + wd * 16 + i] = acc[i];
     }
-    qa[j] = acc;
+    __syncthreads();
+    for (int j = tid; j < Lt; j += kAttnThreads) {
+      float v = pe[j];
+      for (int g2 = 1; g2 < n_eg; ++g2) v += pe[g2 * Lt + j];
+      qa[j] = v;
+    }
   }
   float qb = 0.0f;
   if (kn.bias != nullptr) {
@@ -288,16 +309,39 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attention_kernel(IvbLayerD
     qa[j] = v;  // the weighted latent sum u
   }
   __syncthreads();
+  // out[e] = W_v[h hd + e] . u / l + b_v: thread = (output e, slice of the latent in 16-input words),
+  // the slices of an output in adjacent lanes, summed by shuffles
   const IvbTernary& vu = L.v_up;
   const float inv_l = 1.0f / l_run;
-  for (int e = tid; e < hd; e += kAttnThreads) {
-    const size_t r = static_cast<size_t>(h) * hd + e;
+  const int words = (Lt + 15) >> 4;
+  int slices = kAttnThreads / hd;
+  slices = slices < 1 ? 1 : (slices > 32 ? 32 : slices);
+  while (slices & (slices - 1)) slices &= slices - 1;  // a power of two: lanes of one output stay in a warp
+  const int per = (words + slices - 1) / slices;
+  for (int base = 0; base < hd * slices; base += kAttnThreads) {
+    const int item = base + tid, e = item / slices, sl = item % slices;
     float acc = 0.0f;
-    for (int j = 0; j < Lt; ++j)
-      acc = fmaf(code_value(vu.packed + r * vu.row_bytes, j) * h2f(__ldg(vu.scales + r * vu.scale_stride + (j >> 7))), qa[j], acc);
-    float o = acc * inv_l;
-    if (vu.bias != nullptr) o += __ldg(vu.bias + r);
-    y[static_cast<size_t>(t) * d + h * hd + e] = o;
+    if (e < hd) {
+      const size_t r = static_cast<size_t>(h) * hd + e;
+      const unsigned* row = reinterpret_cast<const unsigned*>(vu.packed + r * vu.row_bytes);
+      for (int wd = sl * per; wd < min(words, (sl + 1) * per); ++wd) {
+        const unsigned w = __ldg(row + wd);
+        const float sc = h2f(__ldg(vu.scales + r * vu.scale_stride + (wd >> 3)));
+        float cm1[16];
+        word_codes_m1(w, cm1);
+        float part_sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          if (wd * 16 + i < Lt) part_sum = fmaf(cm1[i], qa[wd * 16 + i], part_sum);
+        acc = fmaf(sc, part_sum, acc);
+      }
+    }
+    for (int off = 1; off < slices; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
+    if (e < hd && sl == 0) {
+      float o = acc * inv_l;
+      if (vu.bias != nullptr) o += __ldg(vu.bias + static_cast<size_t>(h) * hd + e);
+      y[static_cast<size_t>(t) * d + h * hd + e] = o;
+    }
   }
 }
 
