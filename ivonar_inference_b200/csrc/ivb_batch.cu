@@ -346,6 +346,214 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attention_kernel(IvbLayerD
 }
 
 
+// Absorbed latent attention of every head of sequence blockIdx.x (one warp per head): the sequence's
+// cached latent tiles (64 positions) are copied into shared memory once for all heads (cp.async, double
+// buffered); lane l scores positions l, l + 32 of a tile against the head's absorbed query (shared
+// memory broadcast), the online softmax runs per warp, and lane l accumulates latent dims 8l.. of the
+// weighted sum. Then out[e] = W_v[h hd + e] . u / l + b_v with lanes over e. Same formulas as the
+// per-head kernel above: s_p = a_p <qa, ql_p> + q_nope.b_k + <q_rope, k_rope_p>.
+constexpr int kSeqWarps = 16;
+constexpr int kSeqTile = 64;
+__global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent,
+                                                                            int ld, const int64_t* positions, int d, int Lt,
+                                                                            int H, int hd, int rope, int nope, int max_len,
+                                                                            int lpad, int rpad, float* y) {
+  extern __shared__ __align__(16) unsigned char att_smem[];
+  const int b = blockIdx.x;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int Lp = lpad;       // latent rows padded to 16 (the pad codes are zero)
+  const int lstr = Lp + 16;  // padded tile row: lanes reading different rows hit different banks
+  float* qa_s = reinterpret_cast<float*>(att_smem);                      // [H][Lp]
+  float* qr_s = qa_s + H * Lt;                                            // [H][rope]
+  float* w_s = qr_s + H * rope;                                           // [H][kSeqTile] softmax weights
+  float* lsc_s = w_s + H * kSeqTile;                                      // [2][kSeqTile]
+  int8_t* lat_s = reinterpret_cast<int8_t*>(lsc_s + 2 * kSeqTile);        // [2][kSeqTile][lstr]
+  const long long pos_in = positions[b];
+  if (pos_in < 0 || pos_in >= max_len) {  // capacity error, reported by the cache append
+    for (int i = tid; i < H * hd; i += blockDim.x) y[static_cast<size_t>(b) * d + i] = 0.0f;
+    return;
+  }
+  const int pos = static_cast<int>(pos_in), P = pos + 1;
+  const int8_t* latent_q = B.latent_q + static_cast<size_t>(b) * max_len * lpad;
+  const float* latent_scale = B.latent_scale + static_cast<size_t>(b) * max_len;
+  const uint16_t* k_rope_cache = B.k_rope_cache + static_cast<size_t>(b) * H * max_len * rpad;
+  const int n_tiles = (P + kSeqTile - 1) / kSeqTile;
+  auto load_tile = [&](int ti) {
+    const int p0 = ti * kSeqTile, cnt = min(kSeqTile, P - p0);
+    int8_t* dst = lat_s + (ti & 1) * kSeqTile * lstr;
+    const int chunks = Lp >> 4;  // 16-byte pieces per row
+    for (int i = tid; i < cnt * chunks; i += blockDim.x) {
+      const int r = i / chunks, c = i - r * chunks;
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst + r * lstr + 16 * c)),
+                   "l"(latent_q + static_cast<size_t>(p0 + r) * lpad + 16 * c)
+                   : "memory");
+    }
+    for (int i = tid; i < cnt; i += blockDim.x)
+      asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(lsc_s + (ti & 1) * kSeqTile + i)),
+                   "l"(latent_scale + p0 + i)
+                   : "memory");
+    asm volatile("cp.async.commit_group;" ::: "memory");
+  };
+  load_tile(0);
+  // absorbed queries and rotated rope queries of every head (warp per head)
+  const float scl = L.attn_scale;
+  const float* rtab = L.rope + static_cast<size_t>(pos) * rope;
+  const IvbTernary& kn = L.k_nope_up;
+  const int words = Lp >> 4;  // 16-input words (inputs beyond Lt meet zero codes in the cache)
+  for (int h = warp; h < H; h += kSeqWarps) {
+    const float* q = ent + static_cast<size_t>(b) * ld + h * hd;
+    for (int jr = lane; jr < rope / 2; jr += 32) {
+      const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+      const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
+      qr_s[h * rope + 2 * jr] = (q0 * cs - q1 * sn) * scl;
+      qr_s[h * rope + 2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+    }
+    for (int wd = lane; wd < words; wd += 32) {
+      float acc[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+      for (int e = 0; e < nope; ++e) {
+        const size_t r = static_cast<size_t>(h) * nope + e;
+        const unsigned w = __ldg(reinterpret_cast<const unsigned*>(kn.packed + r * kn.row_bytes) + wd);
+        const float qs = q[e] * scl * h2f(__ldg(kn.scales + r * kn.scale_stride + (wd >> 3)));
+        float cm1[16];
+        word_codes_m1(w, cm1);
+#pragma unroll
+        for (int i = 0; i < 16; ++i) acc[i] = fmaf(qs, cm1[i], acc[i]);
+      }
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qa_s[h * Lp + wd * 16 + i] = acc[i];
+    }
+  }
+  __syncthreads();
+  // per-warp state: the head's running max, sum and latent accumulator (8 dims per lane, up to 2 slices)
+  constexpr int kU = 16;  // Lt <= 512
+  {  // H <= kSeqWarps: one warp per head
+    const int h = warp;
+    const bool live = h < H;
+    float qb = 0.0f;
+    if (live && kn.bias != nullptr) {
+      const float* q = ent + static_cast<size_t>(b) * ld + h * hd;
+      float pp = 0.0f;
+      for (int e = lane; e < nope; e += 32) pp = fmaf(q[e] * scl, __ldg(kn.bias + h * nope + e), pp);
+      qb = warp_sum(pp);
+    }
+    float m_run = -INFINITY, l_run = 0.0f, u[kU];
+#pragma unroll
+    for (int i = 0; i < kU; ++i) u[i] = 0.0f;
+    for (int ti = 0; ti < n_tiles; ++ti) {
+      if (ti > 0) __syncthreads();  // the other buffer is free (its tile was used by every warp)
+      if (ti + 1 < n_tiles) {
+        load_tile(ti + 1);
+        asm volatile("cp.async.wait_group 1;" ::: "memory");
+      } else {
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+      }
+      __syncthreads();
+      const int p0 = ti * kSeqTile, cnt = min(kSeqTile, P - p0);
+      const int8_t* tile = lat_s + (ti & 1) * kSeqTile * lstr;
+      const float* lsc = lsc_s + (ti & 1) * kSeqTile;
+      if (live) {
+        float s2[2];
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int pl = lane + 32 * k;
+          s2[k] = -INFINITY;
+          if (pl < cnt) {
+            const int8_t* ql = tile + pl * lstr;
+            const float* qa = qa_s + h * Lp;
+            float d0 = 0.0f, d1 = 0.0f;
+            for (int j0 = 0; j0 < Lp; j0 += 16) {
+              const uint4 wv = *reinterpret_cast<const uint4*>(ql + j0);
+              float f[16];
+              bytes_to_f32(wv.x, f);
+              bytes_to_f32(wv.y, f + 4);
+              bytes_to_f32(wv.z, f + 8);
+              bytes_to_f32(wv.w, f + 12);
+#pragma unroll
+              for (int i = 0; i < 16; i += 2) {
+                d0 = fmaf(qa[j0 + i], f[i], d0);
+                d1 = fmaf(qa[j0 + i + 1], f[i + 1], d1);
+              }
+            }
+            float rp = 0.0f;
+            const uint16_t* kr = k_rope_cache + (static_cast<size_t>(h) * max_len + p0 + pl) * rpad;
+            for (int r = 0; r < rope; ++r) rp = fmaf(qr_s[h * rope + r], h2f(__ldg(kr + r)), rp);
+            s2[k] = fmaf(lsc[pl], d0 + d1, rp) + qb;
+          }
+        }
+        float mx = fmaxf(s2[0], s2[1]);
+        mx = warp_max(mx);
+        const float m_new = fmaxf(m_run, mx);
+        const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+        float ls = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 2; ++k) {
+          const int pl = lane + 32 * k;
+          if (pl < cnt) {
+            const float e = expf(s2[k] - m_new);
+            ls += e;
+            w_s[h * kSeqTile + pl] = e * lsc[pl];
+          }
+        }
+        ls = warp_sum(ls);
+        l_run = l_run * corr + ls;
+#pragma unroll
+        for (int i = 0; i < kU; ++i) u[i] *= corr;
+        m_run = m_new;
+        __syncwarp();
+        for (int pl = 0; pl < cnt; ++pl) {
+          const float wgt = w_s[h * kSeqTile + pl];
+          const int8_t* ql = tile + pl * lstr;
+#pragma unroll
+          for (int pc = 0; pc < kU / 8; ++pc) {
+            const int j0 = pc * 256 + lane * 8;
+            if (j0 < Lp) {
+              const uint2 wv = *reinterpret_cast<const uint2*>(ql + j0);
+              float f[8];
+              bytes_to_f32(wv.x, f);
+              bytes_to_f32(wv.y, f + 4);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) u[pc * 8 + i] = fmaf(wgt, f[i], u[pc * 8 + i]);
+            }
+          }
+        }
+        __syncwarp();
+      }
+    }
+    // u / l into this head's query row (no longer needed), then out = W_v u + b_v, lanes over outputs
+    if (live) {
+      const float inv_l = 1.0f / l_run;
+      float* us = qa_s + h * Lp;
+#pragma unroll
+      for (int pc = 0; pc < kU / 8; ++pc) {
+        const int j0 = pc * 256 + lane * 8;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (j0 + i < Lp) us[j0 + i] = u[pc * 8 + i] * inv_l;
+      }
+      __syncwarp();
+      const IvbTernary& vu = L.v_up;
+      for (int e = lane; e < hd; e += 32) {
+        const size_t r = static_cast<size_t>(h) * hd + e;
+        const unsigned* row = reinterpret_cast<const unsigned*>(vu.packed + r * vu.row_bytes);
+        float acc = 0.0f;
+        for (int wd = 0; wd < words; ++wd) {
+          const unsigned w = __ldg(row + wd);
+          float cm1[16];
+          word_codes_m1(w, cm1);
+          float part_sum = 0.0f;
+#pragma unroll
+          for (int i = 0; i < 16; ++i) part_sum = fmaf(cm1[i], us[wd * 16 + i], part_sum);
+          acc = fmaf(h2f(__ldg(vu.scales + r * vu.scale_stride + (wd >> 3))), part_sum, acc);
+        }
+        if (vu.bias != nullptr) acc += __ldg(vu.bias + r);
+        y[static_cast<size_t>(b) * d + h * hd + e] = acc;
+      }
+    }
+  }
+}
+
 // Sampler of sequence blockIdx.x (temperature, repetition penalty, top-k, Philox draw), then its
 // position advances by one.
 __global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* logits, uint8_t* seen, int vocab,
@@ -363,6 +571,25 @@ __global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* 
   sample_block(logits + static_cast<size_t>(b) * vocab, seen + static_cast<size_t>(b) * vocab, vocab, sampling, top_k,
                max_top_k, rng + 2 * b, tokens + b, hist, sm);
   if (threadIdx.x == 0) positions[b] += 1;
+}
+
+// One CTA per sequence (a warp per head, the latent tiles shared) when there are enough sequences to fill
+// the SMs and the heads fit in one CTA; else one CTA per (sequence, head), more parallel for few sequences.
+int32_t launch_batch_attention(const IvbLayerDesc& L, const IvbBatchLayer& BL, const float* ent, int ld, const int64_t* positions,
+                               int batch, int d, int Lt, int H, int hd, int rope, int nope, int max_len, int lpad, int rpad,
+                               float* y, cudaStream_t s) {
+  if (H <= kSeqWarps && Lt <= 512 && batch >= 128) {
+    const size_t smem = (static_cast<size_t>(H) * lpad + static_cast<size_t>(H) * rope + static_cast<size_t>(H) * kSeqTile +
+                         2 * kSeqTile) * 4 + 2 * static_cast<size_t>(kSeqTile) * (lpad + 16);
+    IVB_CUDA(cudaFuncSetAttribute(batch_attention_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+    batch_attention_seq_kernel<<<batch, 32 * kSeqWarps, smem, s>>>(L, BL, ent, ld, positions, d, Lt, H, hd, rope, nope, max_len,
+                                                                   lpad, rpad, y);
+  } else {
+    batch_attention_kernel<<<dim3(batch, H), kAttnThreads, 0, s>>>(L, BL, ent, ld, positions, d, Lt, H, hd, rope, nope, max_len,
+                                                                   lpad, rpad, y);
+  }
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
 }
 
 struct BatchLayout {
@@ -466,9 +693,9 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
         batch_cache_kernel<<<B, kThreads, 0, s>>>(L, BL, ent, ld, bt->positions, d, Lt, H, rope, md.max_len, lpad, rpad,
                                                   md.act_eps, err);
         IVB_CUDA(cudaGetLastError());
-        batch_attention_kernel<<<dim3(B, H), kAttnThreads, 0, s>>>(L, BL, ent, ld, bt->positions, d, Lt, H, hd, rope, nope,
-                                                                   md.max_len, lpad, rpad, y);
-        IVB_CUDA(cudaGetLastError());
+        if (int32_t rc = launch_batch_attention(L, BL, ent, ld, bt->positions, B, d, Lt, H, hd, rope, nope, md.max_len, lpad,
+                                                rpad, y, s))
+          return rc;
       }
       if (int32_t rc = quant(y, d, nullptr, 0.0f)) return rc;
       if (int32_t rc = gemm(L.out, IVB_EPI_RESIDUAL, resid, d)) return rc;
@@ -525,9 +752,9 @@ int32_t ivb_batch_mla(const IvbLayerDesc* L, const IvbBatchLayer* B, const float
   batch_cache_kernel<<<batch, kThreads, 0, s>>>(*L, *B, ent, ld, positions, channels, latent, heads, rope, max_len, lpad, rpad,
                                                 act_eps, error);
   IVB_CUDA(cudaGetLastError());
-  batch_attention_kernel<<<dim3(batch, heads), kAttnThreads, 0, s>>>(*L, *B, ent, ld, positions, channels, latent, heads,
-                                                                     head_dim, rope, nope, max_len, lpad, rpad, y);
-  IVB_CUDA(cudaGetLastError());
+  if (int32_t rc = launch_batch_attention(*L, *B, ent, ld, positions, batch, channels, latent, heads, head_dim, rope, nope,
+                                          max_len, lpad, rpad, y, s))
+    return rc;
   return IVB_OK;
 }
 
