@@ -75,3 +75,20 @@ def test_batch_capacity_is_refused() -> None:
     batch.decode(2)
     with pytest.raises(ValueError, match="capacity"):
         batch.decode(1)
+
+
+def test_large_batch_streams_equal_single_sequence_streams() -> None:
+    """128 sequences: the per-sequence attention kernel (latent tiles shared by the heads) is in use."""
+    from ivonar_inference_b200 import synthetic
+    from ivonar_inference_b200.batch import B200BatchDecoder
+
+    model = synthetic.synthetic_model(synthetic.config0(), 0)
+    batch, count, max_len = 128, 20, 64
+    prompts = [synthetic.random_prompt(512, 8 + (i % 11), seed=100 + i)[0] for i in range(batch)]
+    seeds = list(range(batch))
+    dec = B200BatchDecoder(model, batch, max_len=max_len, device="cuda")
+    first = dec.start(prompts, seeds, 1.0, 1, 4.0)
+    rest = dec.decode(count - 1).cpu().numpy()
+    for b in (0, 57, 127):
+        want, _ = _run_single(model, prompts[b], seeds[b], 1.0, 1, 4.0, count, max_len)
+        assert [first[b]] + rest[b].tolist() == want, b
