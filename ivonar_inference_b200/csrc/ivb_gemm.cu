@@ -273,9 +273,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tmem_ld32(lane_base + b * kGemmTok + col0, d);
       const float sv = scale_tab[g * kGemmRows + row];
       const float2 s2 = make_float2(sv, sv);
+      // exact int32 -> float without the conversion unit: the bits of 0x4B400000 + dot are the float
+      // 12582912 + dot (|dot| < 2^22), and one paired subtract leaves dot
+      const float2 m2 = make_float2(-12582912.0f, -12582912.0f);
 #pragma unroll
       for (int q = 0; q < 16; ++q) {
-        const float2 x = make_float2(static_cast<float>(static_cast<int>(d[2 * q])), static_cast<float>(static_cast<int>(d[2 * q + 1])));
+        const float2 x = __fadd2_rn(make_float2(__int_as_float(static_cast<int>(d[2 * q]) + 0x4B400000),
+                                                __int_as_float(static_cast<int>(d[2 * q + 1]) + 0x4B400000)), m2);
         acc[q] = __ffma2_rn(x, s2, acc[q]);
       }
       tc_fence_before();
