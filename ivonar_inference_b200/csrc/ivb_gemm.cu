@@ -7,10 +7,11 @@
 //
 // One CTA computes a 128-row x 128-token tile. The weights are the MMA's A operand and live in tensor
 // memory: they never pass through shared memory as bytes. Warp-specialised roles per 128-input group g:
-//   * producer warps (4, one TMEM lane quarter each): producer 0 fetches the tile's packed weights of the
-//     group (128 rows x 32 bytes) with one TMA tensor load into a small packed ring and bulk-copies the
-//     group's 16 KB activation tile (core matrices, laid out by ivb_quantize_rows) into an operand stage;
-//     then every producer thread expands its row's 128 two-bit codes to signed bytes (code - 1) in
+//   * two producer teams of 4 warps (one TMEM lane quarter each), team t taking the groups g = t (mod 2)
+//     so two groups are staged at once: the team's leader fetches the tile's packed weights of the group
+//     (128 rows x 32 bytes) with one TMA tensor load into a small packed ring and bulk-copies the group's
+//     16 KB activation tile (core matrices, laid out by ivb_quantize_rows) into an operand stage; then
+//     every thread of the team expands its row's 128 two-bit codes to signed bytes (code - 1) in
 //     registers and stores them into the group's A slot in TMEM (tcgen05.st, 32 columns);
 //   * one MMA thread: four 128x128x32 int8 MMAs (A from TMEM, B = activations from shared memory) into
 //     TMEM accumulator g % 3 (the first one overwrites it), committed to the stage's "empty" barrier and
@@ -40,8 +41,9 @@ constexpr int kGemmACol = kGemmBufs * kGemmTok;  // first TMEM column of the A s
 constexpr int kGemmEpiWarps = 16;    // warps 0-15: epilogue
 constexpr int kGemmEpiCols = 32;     // accumulator columns (tokens) per epilogue thread
 constexpr int kGemmMmaWarp = 16;     // warp 16: TMEM allocation and the MMA thread
-constexpr int kGemmProdWarps = 4;    // warps 17-20: producers (lane quarter = warp % 4)
-constexpr int kGemmProducers = 32 * kGemmProdWarps;
+constexpr int kGemmTeams = 2;        // producer teams: team t stages the groups g = t (mod 2)
+constexpr int kGemmProdWarps = 4 * kGemmTeams;  // warps 17-24: producers (lane quarter = warp % 4)
+constexpr int kGemmProducers = 128;  // threads of one team (one per weight row / TMEM lane)
 constexpr int kGemmThreads = 32 * (kGemmEpiWarps + 1 + kGemmProdWarps);
 constexpr int kPackSlots = 4;                    // packed weight blocks in flight
 constexpr int kPackSlot = kGemmRows * 32;        // packed bytes of one group for the tile's 128 rows
@@ -136,6 +138,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   __shared__ __align__(8) unsigned long long pk_bar[kPackSlots], pk_empty[kPackSlots];
   __shared__ unsigned tmem_base;
   __shared__ int failed;
+  __shared__ int stage_group[kGemmStages], slot_group[kPackSlots];  // last group copied into each (error drain)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kGemmTok;
   const int groups_all = (m.in_features + 127) >> 7;
@@ -149,7 +152,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  const int pj = tid - 32 * (kGemmMmaWarp + 1);  // producer index 0..127 (pj == 0: the copy issuer)
+  const int pj = tid - 32 * (kGemmMmaWarp + 1);  // producer index 0..255
+  const int team = pj >> 7, tj = pj & 127;        // tj == 0: the team's copy issuer
   if (pj == 0) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
     for (int i = 0; i < kGemmStages; ++i) {
@@ -165,8 +169,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       mbar_init(pk_empty + i, kGemmProducers);
     }
     failed = 0;
+    for (int i = 0; i < kGemmStages; ++i) stage_group[i] = -1;
+    for (int i = 0; i < kPackSlots; ++i) slot_group[i] = -1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     for (int g = 0; g < kPackSlots && g < groups; ++g) {
+      slot_group[g] = g;
       mbar_expect_tx(pk_bar + g, kPackSlot);
       tma_load_2d(pack + g * kPackSlot, &wmap, (g_lo + g) << 5, r0, pk_bar + g);
     }
@@ -182,22 +189,20 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
   float2 acc[kGemmEpiCols / 2];
   bool late = false;
-  int issued = 0;                                // activation tiles bulk-copied by producer 0
-  int pk_issued = min(kPackSlots, groups);       // packed blocks requested by producer 0
   if (warp > kGemmMmaWarp) {
-    // ---- producers ----
+    // ---- producers: team `team` stages groups team, team + 2, ... ----
     const int8_t* a_src = q8 + static_cast<size_t>(blockIdx.y) * (ldq >> 7) * kGemmTile;
-    for (int g = 0; g < groups; ++g) {
+    for (int g = team; g < groups; g += kGemmTeams) {
       const int st = g % kGemmStages, slot = g % kPackSlots;
       if (!mbar_wait_bounded(pk_bar + slot, (g / kPackSlots) & 1, timeout_ns) ||
           (g >= kGemmStages && !mbar_wait_bounded(empty_bar + st, ((g / kGemmStages) - 1) & 1, timeout_ns))) {
         late = true;
         break;
       }
-      if (pj == 0) {
+      if (tj == 0) {
+        stage_group[st] = g;
         mbar_expect(full_bar + st, kGemmTile);
         bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(g_lo + g) * kGemmTile, kGemmTile, full_bar + st);
-        issued = g + 1;
       }
       // row's 16 packed words -> 32 TMEM columns: column 4c + f holds the codes (w_c >> 2f) & 0x03030303
       // (inputs 16c + 4b + f, b = 0..3), each byte turned into the signed code - 1
@@ -214,16 +219,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(full_bar + st);
-      // refill the slot of group g - 1 (read by every producer by now) with group g - 1 + kPackSlots
-      const int prev = g - 1, nxt = prev + kPackSlots;
-      if (pj == 0 && prev >= 0 && nxt < groups) {
+      // refill the slot of the team's previous group (read by the whole team by now) with that group
+      // + kPackSlots (the same team's)
+      const int prev = g - kGemmTeams, nxt = prev + kPackSlots;
+      if (tj == 0 && prev >= 0 && nxt < groups) {
         if (!mbar_wait_bounded(pk_empty + prev % kPackSlots, (prev / kPackSlots) & 1, timeout_ns)) {
           late = true;
           break;
         }
+        slot_group[prev % kPackSlots] = nxt;
         mbar_expect_tx(pk_bar + prev % kPackSlots, kPackSlot);
         tma_load_2d(pack + (prev % kPackSlots) * kPackSlot, &wmap, (g_lo + nxt) << 5, r0, pk_bar + prev % kPackSlots);
-        pk_issued = nxt + 1;
       }
     }
     if (late) atomicExch(&failed, 1);
@@ -294,10 +300,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (tid == 0) atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
     // no bulk or tensor copy may still be writing this CTA's shared memory when it exits
     if (pj == 0) {
-      for (int g = max(0, issued - kGemmStages); g < issued; ++g)
-        mbar_wait_bounded(full_bar + g % kGemmStages, (g / kGemmStages) & 1, timeout_ns);
-      for (int g = max(0, pk_issued - kPackSlots); g < pk_issued; ++g)
-        mbar_wait_bounded(pk_bar + g % kPackSlots, (g / kPackSlots) & 1, timeout_ns);
+      for (int i = 0; i < kGemmStages; ++i)
+        if (stage_group[i] >= 0) mbar_wait_bounded(full_bar + i, (stage_group[i] / kGemmStages) & 1, timeout_ns);
+      for (int i = 0; i < kPackSlots; ++i)
+        if (slot_group[i] >= 0) mbar_wait_bounded(pk_bar + i, (slot_group[i] / kPackSlots) & 1, timeout_ns);
     }
   } else {
     // stage the tile as [token][row] fp32 in the (now idle) stages, then write it out row by row, coalesced
