@@ -40,16 +40,20 @@ __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wai
 
 constexpr int kAttnPieces = 4;
 
-// All threads: copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n)
-// in every CTA of the cluster with st.async; each store completes its bytes on that CTA's mbarrier
-// `bar` (the consumer arms it with the size of the whole fill and waits). One (slice, rank) pair per
-// thread, 16-byte stores when aligned.
+// Copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n) in every
+// CTA of the cluster; the bytes complete on that CTA's mbarrier `bar` (the consumer arms it with the
+// size of the whole fill and waits). Aligned slices go as one bulk shared-to-shared copy per CTA,
+// issued by thread r for CTA r (the copy engine reads src; push_drain() waits for those reads before
+// src is written again); other slices as one st.async per (word, rank).
 __device__ __forceinline__ void push_async(float* dst, int base, const float* src, int n, int R, unsigned long long* bar) {
   if (((base | n) & 3) == 0) {
-    const int n4 = n >> 2;
-    for (int idx = threadIdx.x; idx < n4 * R; idx += kThreads) {
-      const int r = idx / n4, i = idx - r * n4;
-      st_async_v4(map_rank(dst + base + 4 * i, r), reinterpret_cast<const float4*>(src)[i], map_rank(bar, r));
+    if (static_cast<int>(threadIdx.x) < R && n > 0) {
+      fence_proxy_async();  // the generic writes of src (ordered by the barrier) before the async-proxy read
+      asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                       map_rank(dst + base, threadIdx.x)),
+                   "r"(smem_addr(src)), "r"(static_cast<unsigned>(n) * 4u), "r"(map_rank(bar, threadIdx.x))
+                   : "memory");
+      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
     }
   } else {
     for (int idx = threadIdx.x; idx < n * R; idx += kThreads) {
@@ -58,6 +62,8 @@ __device__ __forceinline__ void push_async(float* dst, int base, const float* sr
     }
   }
 }
+// Every thread: wait until the bulk pushes this thread issued have read their source.
+__device__ __forceinline__ void push_drain() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // Bounded wait on an attention tile mbarrier; the verdict is uniform across the CTA.
 __device__ __forceinline__ bool tile_wait(unsigned long long* bar, unsigned parity, unsigned long long timeout_ns) {
@@ -763,6 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
         for (int k = 0; k < 6; ++k) marks[1 + k] = static_cast<unsigned long long>(prof[k]);
       mark(marks, 7);
       cp_async_wait_all();  // the next descriptor has landed
+      push_drain();         // the staging slice has been read by this op's pushes
       ++opk;
       __syncthreads();      // local buffers (rows, codes, staging) are reused by the next op
       if (!ok) {
@@ -812,6 +819,7 @@ __global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __gri
   // consumed (the run stopped after a step without a head), the descriptor prefetch, the ring
   if (resid_pending) wait_fill(XB_RESID, static_cast<unsigned>(D.hidden) * 4u);
   cp_async_wait_all();
+  push_drain();
   if (tid == 0) {
     while (st.consumed < st.issued) {
       if (!mbar_wait_bounded(st.full + st.consumed % kStages, (st.consumed / kStages) & 1u, p.timeout_ns)) break;

@@ -235,8 +235,11 @@ __device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
 // bit-identically in each pass. src is only read (it may be a push target of a later op).
 static __device__ float quantize_block(const float* src, int n, const float* norm_w, float norm_eps, float clip,
                                        float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
-  const int tid = threadIdx.x, lane = tid & 31;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int chunks = (n + 63) >> 6, padded = chunks << 6;
+  // red[0, kWarps): warp partial sums of squares; red[16, 16 + kWarps): warp maxima. Each slot range is
+  // written before one barrier and read after it by every thread, and the next write to either range
+  // comes after a later barrier of this function, so one barrier per reduction suffices.
   float inv = 0.0f;
   if (norm_w != nullptr) {
     float p = 0.0f;
@@ -247,7 +250,12 @@ static __device__ float quantize_block(const float* src, int n, const float* nor
         p = fmaf(x, x, p);
       }
     }
-    const float ss = block_sum(p, red);  // warps beyond the canonical lanes add exact zeros
+    p = warp_sum(p);  // warps beyond the canonical lanes add exact zeros
+    if (lane == 0) red[warp] = p;
+    __syncthreads();
+    float ss = red[0];
+#pragma unroll
+    for (int w = 1; w < kWarps; ++w) ss += red[w];
     inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
   }
   auto value = [&](int i) -> float {
@@ -259,7 +267,17 @@ static __device__ float quantize_block(const float* src, int n, const float* nor
   for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(value(i)));
   if (xsum != nullptr)
     for (int u = tid; u < chunks; u += kThreads) xsum[u] = 0;
-  const float amax = block_max_nonneg(am, red);
+  // non-negative floats order like their bit patterns: one redux per warp, the warps meet in shared slots
+  unsigned* wmax = reinterpret_cast<unsigned*>(red) + 16;
+  {
+    const unsigned m = __reduce_max_sync(kFull, __float_as_uint(am));
+    if (lane == 0) wmax[warp] = m;
+  }
+  __syncthreads();
+  unsigned mbits = wmax[0];
+#pragma unroll
+  for (int w = 1; w < kWarps; ++w) mbits = max(mbits, wmax[w]);
+  const float amax = __uint_as_float(mbits);
   const float scale = fmaxf(amax / 127.0f, act_eps);
   const float rscale = 1.0f / scale;
   // codes; each warp's 32 consecutive inputs of one pass share a 64-input chunk, so the chunk sums are
