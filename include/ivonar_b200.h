@@ -198,7 +198,10 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
 
 /* Split-K variant of ivb_ternary_gemv (same arguments, same results within fp32 rounding): the input
  * columns are spread over more CTAs and their partial row sums are added in a static device scratch.
- * It has no counterpart in the reference. It allocates nothing: the scratch is a file-scope
+ * It has no counterpart in the reference. It is for callers that may not allocate device memory at call
+ * time: a serving process whose pool already holds the GPU's memory (a cudaMalloc there fails or waits
+ * for the whole device), or code on a latency-bound path where cudaMalloc's implicit device
+ * synchronisation is not acceptable. It allocates nothing: the scratch is a file-scope
  * __device__ array of 32768 fp32 row sums (rows > 32768 or in_features > 16384 return IVB_EINVAL);
  * its address is looked up once per device with cudaGetSymbolAddress on the first call with that
  * device current, so make the first call on each device outside any stream capture. Each call clears

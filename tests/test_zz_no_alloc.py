@@ -1,5 +1,8 @@
 """ivb_ternary_gemv_splitk (static scratch, no allocation) against ivb_ternary_gemv on a B200.
 
+The split-K entry point serves callers that may not allocate device memory when they call it (a server
+whose memory pool already holds the GPU, or a path that cannot take cudaMalloc's synchronisation).
+
 Collected last on purpose: it must pass alone and after the other GPU tests, which exercises the
 once-per-device scratch lookup both cold and after other kernels ran.
 """
