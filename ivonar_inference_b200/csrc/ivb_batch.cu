@@ -346,14 +346,64 @@ __global__ void __launch_bounds__(kAttnThreads) batch_attention_kernel(IvbLayerD
 }
 
 
-// Absorbed latent attention of every head of sequence blockIdx.x (one warp per head): the sequence's
-// cached latent tiles (64 positions) are copied into shared memory once for all heads (cp.async, double
-// buffered); lane l scores positions l, l + 32 of a tile against the head's absorbed query (shared
-// memory broadcast), the online softmax runs per warp, and lane l accumulates latent dims 8l.. of the
-// weighted sum. Then out[e] = W_v[h hd + e] . u / l + b_v with lanes over e. Same formulas as the
-// per-head kernel above: s_p = a_p <qa, ql_p> + q_nope.b_k + <q_rope, k_rope_p>.
+// Absorbed latent attention of every head of sequence blockIdx.x on the tensor cores: one CTA per
+// sequence, 16 warps, the heads as the 16 MMA rows (heads beyond H are zero rows). Per tile of 64 cached
+// positions (copied into shared memory once for all heads, cp.async, double buffered):
+//   S[h][p] = <qa_h, ql_p>   (M 16 heads, N 64 positions, K latent)
+//   U[h][:] = corr_h U[h][:] + sum_p w[h][p] ql_p   (M 16 heads, N latent, K 64 positions)
+// with mma.sync m16n8k8 tf32: the latent codes are exact in tf32, and each fp32 operand (qa, w) is split
+// into tf32 hi + lo (two MMAs), so the products keep ~21 significant bits. Between the two, warp h runs
+// head h's online softmax: s_p = a_p S[h][p] + q_nope.b_k + <q_rope, k_rope_p>, w = exp(s - m) a_p.
+// Then out[e] = W_v[h hd + e] . U[h] / l_h + b_v with lanes over e. Same formulas as the per-head kernel.
 constexpr int kSeqWarps = 16;
 constexpr int kSeqTile = 64;
+constexpr int kSeqMaxNb = 4;  // latent n-blocks of 8 per warp: Lt <= 512
+
+__device__ __forceinline__ uint32_t tf32_bits(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+__device__ __forceinline__ void mma_tf32(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// an int8 code as the tf32 (= fp32) bits of its exact value
+__device__ __forceinline__ uint32_t code_tf32(int8_t v) { return __float_as_uint(static_cast<float>(v)); }
+
+struct SeqSmem {
+  int ldq;  // floats per row of qa / u (Lp + 4)
+  size_t qa_hi, qa_lo, qr, qb, tiles, lsc, s_part, w_hi, w_lo, corr, l, u, total;
+};
+__host__ __device__ inline SeqSmem seq_smem(int Lp, int rope) {
+  SeqSmem m;
+  m.ldq = Lp + 4;
+  const int lstr = Lp + 16;
+  size_t o = 0;
+  auto take = [&](size_t bytes) {
+    const size_t at = o;
+    o += (bytes + 15) / 16 * 16;
+    return at;
+  };
+  m.qa_hi = take(static_cast<size_t>(16) * m.ldq * 4);
+  m.qa_lo = take(static_cast<size_t>(16) * m.ldq * 4);
+  m.qr = take(static_cast<size_t>(16) * rope * 4);
+  m.qb = take(16 * 4);
+  m.tiles = take(static_cast<size_t>(2) * kSeqTile * lstr);
+  m.lsc = take(2 * kSeqTile * 4);
+  m.s_part = take(static_cast<size_t>(2) * 16 * (kSeqTile + 4) * 4);
+  m.w_hi = take(static_cast<size_t>(16) * (kSeqTile + 4) * 4);
+  m.w_lo = take(static_cast<size_t>(16) * (kSeqTile + 4) * 4);
+  m.corr = take(16 * 4);
+  m.l = take(16 * 4);
+  m.u = take(static_cast<size_t>(16) * m.ldq * 4);
+  m.total = o;
+  return m;
+}
+
 __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(IvbLayerDesc L, IvbBatchLayer B, const float* ent,
                                                                             int ld, const int64_t* positions, int d, int Lt,
                                                                             int H, int hd, int rope, int nope, int max_len,
@@ -361,13 +411,24 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
   extern __shared__ __align__(16) unsigned char att_smem[];
   const int b = blockIdx.x;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int Lp = lpad;       // latent rows padded to 16 (the pad codes are zero)
-  const int lstr = Lp + 16;  // padded tile row: lanes reading different rows hit different banks
-  float* qa_s = reinterpret_cast<float*>(att_smem);                      // [H][Lp]
-  float* qr_s = qa_s + H * Lt;                                            // [H][rope]
-  float* w_s = qr_s + H * rope;                                           // [H][kSeqTile] softmax weights
-  float* lsc_s = w_s + H * kSeqTile;                                      // [2][kSeqTile]
-  int8_t* lat_s = reinterpret_cast<int8_t*>(lsc_s + 2 * kSeqTile);        // [2][kSeqTile][lstr]
+  const int g = lane >> 2, t = lane & 3;  // MMA fragment coordinates
+  const int Lp = lpad;                    // latent rows padded to 16 (the pad codes are zero)
+  const int lstr = Lp + 16;               // padded tile row
+  const SeqSmem M = seq_smem(Lp, rope);
+  const int lq = M.ldq;
+  float* qa_hi = reinterpret_cast<float*>(att_smem + M.qa_hi);  // [16][lq] tf32 hi of the absorbed queries
+  float* qa_lo = reinterpret_cast<float*>(att_smem + M.qa_lo);
+  float* qr_s = reinterpret_cast<float*>(att_smem + M.qr);      // [16][rope]
+  float* qb_s = reinterpret_cast<float*>(att_smem + M.qb);      // [16]
+  int8_t* lat_s = reinterpret_cast<int8_t*>(att_smem + M.tiles);  // [2][kSeqTile][lstr]
+  float* lsc_s = reinterpret_cast<float*>(att_smem + M.lsc);      // [2][kSeqTile]
+  float* s_part = reinterpret_cast<float*>(att_smem + M.s_part);  // [2][16][kSeqTile + 4] (two K halves)
+  float* w_hi = reinterpret_cast<float*>(att_smem + M.w_hi);      // [16][kSeqTile + 4]
+  float* w_lo = reinterpret_cast<float*>(att_smem + M.w_lo);
+  float* corr_s = reinterpret_cast<float*>(att_smem + M.corr);    // [16]
+  float* l_s = reinterpret_cast<float*>(att_smem + M.l);          // [16]
+  float* u_s = reinterpret_cast<float*>(att_smem + M.u);          // [16][lq]
+  constexpr int kSt = kSeqTile + 4;
   const long long pos_in = positions[b];
   if (pos_in < 0 || pos_in >= max_len) {  // capacity error, reported by the cache append
     for (int i = tid; i < H * hd; i += blockDim.x) y[static_cast<size_t>(b) * d + i] = 0.0f;
@@ -395,24 +456,39 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
     asm volatile("cp.async.commit_group;" ::: "memory");
   };
   load_tile(0);
-  // absorbed queries and rotated rope queries of every head (warp per head)
+  // rows of heads >= H stay zero: no score, no weight
+  for (int i = tid; i < 16 * kSt; i += blockDim.x) {
+    w_hi[i] = 0.0f;
+    w_lo[i] = 0.0f;
+  }
+  // absorbed queries (tf32 hi/lo), rotated rope queries and q_nope . b_k of every head (warp per head);
+  // lane = (e slice, 16-input word): slices of the nope inputs meet by shuffles
   const float scl = L.attn_scale;
   const float* rtab = L.rope + static_cast<size_t>(pos) * rope;
   const IvbTernary& kn = L.k_nope_up;
-  const int words = Lp >> 4;  // 16-input words (inputs beyond Lt meet zero codes in the cache)
-  for (int h = warp; h < H; h += kSeqWarps) {
-    const float* q = ent + static_cast<size_t>(b) * ld + h * hd;
-    for (int jr = lane; jr < rope / 2; jr += 32) {
-      const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
-      const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
-      qr_s[h * rope + 2 * jr] = (q0 * cs - q1 * sn) * scl;
-      qr_s[h * rope + 2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
-    }
-    for (int wd = lane; wd < words; wd += 32) {
-      float acc[16];
+  const int words = Lp >> 4;
+  const int slices = words >= 32 ? 1 : 32 / words;  // words is a power of two <= 32 (Lp <= 512)
+  // the queries of all heads into shared memory (the u rows are free until the end)
+  for (int i = tid; i < H * hd; i += blockDim.x) u_s[i] = ent[static_cast<size_t>(b) * ld + i];
+  __syncthreads();
+  {
+    const int h = warp;
+    const bool live = h < H;
+    const float* q = u_s + h * hd;
+    if (live)
+      for (int jr = lane; jr < rope / 2; jr += 32) {
+        const float cs = __ldg(rtab + 2 * jr), sn = __ldg(rtab + 2 * jr + 1);
+        const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
+        qr_s[h * rope + 2 * jr] = (q0 * cs - q1 * sn) * scl;
+        qr_s[h * rope + 2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+      }
+    const int wd = lane % words, sl = lane / words;
+    float acc[16];
 #pragma unroll
-      for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-      for (int e = 0; e < nope; ++e) {
+    for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+    if (live && sl < slices) {
+#pragma unroll 8
+      for (int e = sl; e < nope; e += slices) {
         const size_t r = static_cast<size_t>(h) * nope + e;
         const unsigned w = __ldg(reinterpret_cast<const unsigned*>(kn.packed + r * kn.row_bytes) + wd);
         const float qs = q[e] * scl * h2f(__ldg(kn.scales + r * kn.scale_stride + (wd >> 3)));
@@ -421,135 +497,196 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
 #pragma unroll
         for (int i = 0; i < 16; ++i) acc[i] = fmaf(qs, cm1[i], acc[i]);
       }
+    }
+    for (int off = words; off < 32; off <<= 1)
 #pragma unroll
-      for (int i = 0; i < 16; ++i) qa_s[h * Lp + wd * 16 + i] = acc[i];
+      for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], off);
+    if (sl == 0)
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float v = live ? acc[i] : 0.0f;
+        const uint32_t hi = tf32_bits(v);
+        qa_hi[h * lq + wd * 16 + i] = __uint_as_float(hi);
+        qa_lo[h * lq + wd * 16 + i] = __uint_as_float(tf32_bits(v - __uint_as_float(hi)));
+      }
+    float pp = 0.0f;
+    if (live && kn.bias != nullptr)
+      for (int e = lane; e < nope; e += 32) pp = fmaf(q[e] * scl, __ldg(kn.bias + h * nope + e), pp);
+    pp = warp_sum(pp);
+    if (lane == 0) qb_s[h] = pp;
+  }
+  // head h's softmax state (warp h); U accumulators of latent n-blocks warp, warp + 16, ...
+  float m_run = -INFINITY, l_run = 0.0f;
+  float uacc[kSeqMaxNb][4];
+#pragma unroll
+  for (int j = 0; j < kSeqMaxNb; ++j)
+#pragma unroll
+    for (int c = 0; c < 4; ++c) uacc[j][c] = 0.0f;
+  const int ksteps = Lp >> 3, khalf = (ksteps + 1) >> 1;
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    __syncthreads();  // the previous tile's buffer, scores and weights are no longer read
+    if (ti + 1 < n_tiles) {
+      load_tile(ti + 1);
+      asm volatile("cp.async.wait_group 1;" ::: "memory");
+    } else {
+      asm volatile("cp.async.wait_group 0;" ::: "memory");
+    }
+    __syncthreads();
+    const int p0 = ti * kSeqTile, cnt = min(kSeqTile, P - p0);
+    const int8_t* tile = lat_s + (ti & 1) * kSeqTile * lstr;
+    const float* lsc = lsc_s + (ti & 1) * kSeqTile;
+    // head warp's rotated keys of its two positions, issued together before the score MMAs (rpad <= 32:
+    // up to four 16-byte loads per position), so their latency is paid once and hidden
+    constexpr int kKrVec = 4;
+    uint4 krv[2][kKrVec];
+    const bool kr_vec = rpad <= 8 * kKrVec;
+#pragma unroll
+    for (int k = 0; k < 2; ++k) {
+      const int pl = lane + 32 * k;
+      const uint4* kr4 = reinterpret_cast<const uint4*>(k_rope_cache + (static_cast<size_t>(warp) * max_len + p0 + pl) * rpad);
+      const bool ok = kr_vec && warp < H && pl < cnt;
+#pragma unroll
+      for (int v = 0; v < kKrVec; ++v) krv[k][v] = ok && 8 * v < rpad ? __ldg(kr4 + v) : make_uint4(0u, 0u, 0u, 0u);
+    }
+    // ---- S = QA x tile^T: warp -> positions 8 (warp % 8).., K half warp / 8 ----
+    {
+      const int nb = warp & 7, half = warp >> 3;
+      const int k_lo = half * khalf, k_hi = min(ksteps, k_lo + khalf);
+      float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      const int8_t* prow = tile + (8 * nb + g) * lstr;
+      for (int ks = k_lo; ks < k_hi; ++ks) {
+        const int k0 = 8 * ks;
+        const uint32_t b0 = code_tf32(prow[k0 + t]), b1 = code_tf32(prow[k0 + t + 4]);
+        mma_tf32(c, __float_as_uint(qa_hi[g * lq + k0 + t]), __float_as_uint(qa_hi[(g + 8) * lq + k0 + t]),
+                 __float_as_uint(qa_hi[g * lq + k0 + t + 4]), __float_as_uint(qa_hi[(g + 8) * lq + k0 + t + 4]), b0, b1);
+        mma_tf32(c, __float_as_uint(qa_lo[g * lq + k0 + t]), __float_as_uint(qa_lo[(g + 8) * lq + k0 + t]),
+                 __float_as_uint(qa_lo[g * lq + k0 + t + 4]), __float_as_uint(qa_lo[(g + 8) * lq + k0 + t + 4]), b0, b1);
+      }
+      float* sp = s_part + half * 16 * kSt;
+      sp[g * kSt + 8 * nb + 2 * t] = c[0];
+      sp[g * kSt + 8 * nb + 2 * t + 1] = c[1];
+      sp[(g + 8) * kSt + 8 * nb + 2 * t] = c[2];
+      sp[(g + 8) * kSt + 8 * nb + 2 * t + 1] = c[3];
+    }
+    __syncthreads();
+    // ---- online softmax of head h = warp over the tile's positions ----
+    if (warp < H) {
+      const int h = warp;
+      const float qb = qb_s[h];
+      float s2[2];
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int pl = lane + 32 * k;
+        s2[k] = -INFINITY;
+        if (pl < cnt) {
+          const float dot = s_part[h * kSt + pl] + s_part[16 * kSt + h * kSt + pl];
+          float rp = 0.0f;
+          if (kr_vec) {
+#pragma unroll
+            for (int v = 0; v < kKrVec; ++v) {
+              const uint32_t kw[4] = {krv[k][v].x, krv[k][v].y, krv[k][v].z, krv[k][v].w};  // halves 8v .. 8v + 7
+#pragma unroll
+              for (int r2 = 0; r2 < 8; ++r2) {
+                const int r = 8 * v + r2;
+                if (r < rope) rp = fmaf(qr_s[h * rope + r], h2f(static_cast<uint16_t>(kw[r2 >> 1] >> (16 * (r2 & 1)))), rp);
+              }
+            }
+          } else {
+            const uint16_t* kr = k_rope_cache + (static_cast<size_t>(h) * max_len + p0 + pl) * rpad;
+            for (int r = 0; r < rope; ++r) rp = fmaf(qr_s[h * rope + r], h2f(__ldg(kr + r)), rp);
+          }
+          s2[k] = fmaf(lsc[pl], dot, rp) + qb;
+        }
+      }
+      const float mx = warp_max(fmaxf(s2[0], s2[1]));
+      const float m_new = fmaxf(m_run, mx);
+      const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+      float ls = 0.0f;
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int pl = lane + 32 * k;
+        float wgt = 0.0f;
+        if (pl < cnt) {
+          const float e = expf(s2[k] - m_new);
+          ls += e;
+          wgt = e * lsc[pl];
+        }
+        const uint32_t hi = tf32_bits(wgt);
+        w_hi[h * kSt + pl] = __uint_as_float(hi);
+        w_lo[h * kSt + pl] = __uint_as_float(tf32_bits(wgt - __uint_as_float(hi)));
+      }
+      ls = warp_sum(ls);
+      l_run = l_run * corr + ls;
+      m_run = m_new;
+      if (lane == 0) corr_s[h] = corr;
+    } else if (warp < 16 && lane == 0) {
+      corr_s[warp] = 1.0f;
+    }
+    __syncthreads();
+    // ---- U = corr U + W x tile: warp -> latent n-blocks warp, warp + 16, ... ----
+    {
+      const float c_lo = corr_s[g], c_hi = corr_s[g + 8];
+      const int nbs = Lp >> 3;
+#pragma unroll
+      for (int j = 0; j < kSeqMaxNb; ++j) {
+        const int nb = warp + 16 * j;
+        if (nb < nbs) {
+          uacc[j][0] *= c_lo;
+          uacc[j][1] *= c_lo;
+          uacc[j][2] *= c_hi;
+          uacc[j][3] *= c_hi;
+#pragma unroll
+          for (int ks = 0; ks < kSeqTile / 8; ++ks) {
+            const int k0 = 8 * ks;
+            const uint32_t b0 = code_tf32(tile[(k0 + t) * lstr + 8 * nb + g]);
+            const uint32_t b1 = code_tf32(tile[(k0 + t + 4) * lstr + 8 * nb + g]);
+            mma_tf32(uacc[j], __float_as_uint(w_hi[g * kSt + k0 + t]), __float_as_uint(w_hi[(g + 8) * kSt + k0 + t]),
+                     __float_as_uint(w_hi[g * kSt + k0 + t + 4]), __float_as_uint(w_hi[(g + 8) * kSt + k0 + t + 4]), b0, b1);
+            mma_tf32(uacc[j], __float_as_uint(w_lo[g * kSt + k0 + t]), __float_as_uint(w_lo[(g + 8) * kSt + k0 + t]),
+                     __float_as_uint(w_lo[g * kSt + k0 + t + 4]), __float_as_uint(w_lo[(g + 8) * kSt + k0 + t + 4]), b0, b1);
+          }
+        }
+      }
+    }
+  }
+  if (warp < H && lane == 0) l_s[warp] = l_run;
+  __syncthreads();
+  {
+    const int nbs = Lp >> 3;
+    const float il_lo = g < H ? 1.0f / l_s[g] : 0.0f, il_hi = g + 8 < H ? 1.0f / l_s[g + 8] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < kSeqMaxNb; ++j) {
+      const int nb = warp + 16 * j;
+      if (nb < nbs) {
+        u_s[g * lq + 8 * nb + 2 * t] = uacc[j][0] * il_lo;
+        u_s[g * lq + 8 * nb + 2 * t + 1] = uacc[j][1] * il_lo;
+        u_s[(g + 8) * lq + 8 * nb + 2 * t] = uacc[j][2] * il_hi;
+        u_s[(g + 8) * lq + 8 * nb + 2 * t + 1] = uacc[j][3] * il_hi;
+      }
     }
   }
   __syncthreads();
-  // per-warp state: the head's running max, sum and latent accumulator (8 dims per lane, up to 2 slices)
-  constexpr int kU = 16;  // Lt <= 512
-  {  // H <= kSeqWarps: one warp per head
+  // out = W_v u / l + b_v: warp per head, lanes over the outputs e
+  if (warp < H) {
     const int h = warp;
-    const bool live = h < H;
-    float qb = 0.0f;
-    if (live && kn.bias != nullptr) {
-      const float* q = ent + static_cast<size_t>(b) * ld + h * hd;
-      float pp = 0.0f;
-      for (int e = lane; e < nope; e += 32) pp = fmaf(q[e] * scl, __ldg(kn.bias + h * nope + e), pp);
-      qb = warp_sum(pp);
-    }
-    float m_run = -INFINITY, l_run = 0.0f, u[kU];
+    const float* us = u_s + h * lq;
+    const IvbTernary& vu = L.v_up;
+    for (int e = lane; e < hd; e += 32) {
+      const size_t r = static_cast<size_t>(h) * hd + e;
+      const unsigned* row = reinterpret_cast<const unsigned*>(vu.packed + r * vu.row_bytes);
+      float acc = 0.0f;
+#pragma unroll 8
+      for (int wd = 0; wd < words; ++wd) {
+        const unsigned w = __ldg(row + wd);
+        float cm1[16];
+        word_codes_m1(w, cm1);
+        float part_sum = 0.0f;
 #pragma unroll
-    for (int i = 0; i < kU; ++i) u[i] = 0.0f;
-    for (int ti = 0; ti < n_tiles; ++ti) {
-      if (ti > 0) __syncthreads();  // the other buffer is free (its tile was used by every warp)
-      if (ti + 1 < n_tiles) {
-        load_tile(ti + 1);
-        asm volatile("cp.async.wait_group 1;" ::: "memory");
-      } else {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        for (int i = 0; i < 16; ++i) part_sum = fmaf(cm1[i], us[wd * 16 + i], part_sum);
+        acc = fmaf(h2f(__ldg(vu.scales + r * vu.scale_stride + (wd >> 3))), part_sum, acc);
       }
-      __syncthreads();
-      const int p0 = ti * kSeqTile, cnt = min(kSeqTile, P - p0);
-      const int8_t* tile = lat_s + (ti & 1) * kSeqTile * lstr;
-      const float* lsc = lsc_s + (ti & 1) * kSeqTile;
-      if (live) {
-        float s2[2];
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int pl = lane + 32 * k;
-          s2[k] = -INFINITY;
-          if (pl < cnt) {
-            const int8_t* ql = tile + pl * lstr;
-            const float* qa = qa_s + h * Lp;
-            float d0 = 0.0f, d1 = 0.0f;
-            for (int j0 = 0; j0 < Lp; j0 += 16) {
-              const uint4 wv = *reinterpret_cast<const uint4*>(ql + j0);
-              float f[16];
-              bytes_to_f32(wv.x, f);
-              bytes_to_f32(wv.y, f + 4);
-              bytes_to_f32(wv.z, f + 8);
-              bytes_to_f32(wv.w, f + 12);
-#pragma unroll
-              for (int i = 0; i < 16; i += 2) {
-                d0 = fmaf(qa[j0 + i], f[i], d0);
-                d1 = fmaf(qa[j0 + i + 1], f[i + 1], d1);
-              }
-            }
-            float rp = 0.0f;
-            const uint16_t* kr = k_rope_cache + (static_cast<size_t>(h) * max_len + p0 + pl) * rpad;
-            for (int r = 0; r < rope; ++r) rp = fmaf(qr_s[h * rope + r], h2f(__ldg(kr + r)), rp);
-            s2[k] = fmaf(lsc[pl], d0 + d1, rp) + qb;
-          }
-        }
-        float mx = fmaxf(s2[0], s2[1]);
-        mx = warp_max(mx);
-        const float m_new = fmaxf(m_run, mx);
-        const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-        float ls = 0.0f;
-#pragma unroll
-        for (int k = 0; k < 2; ++k) {
-          const int pl = lane + 32 * k;
-          if (pl < cnt) {
-            const float e = expf(s2[k] - m_new);
-            ls += e;
-            w_s[h * kSeqTile + pl] = e * lsc[pl];
-          }
-        }
-        ls = warp_sum(ls);
-        l_run = l_run * corr + ls;
-#pragma unroll
-        for (int i = 0; i < kU; ++i) u[i] *= corr;
-        m_run = m_new;
-        __syncwarp();
-        for (int pl = 0; pl < cnt; ++pl) {
-          const float wgt = w_s[h * kSeqTile + pl];
-          const int8_t* ql = tile + pl * lstr;
-#pragma unroll
-          for (int pc = 0; pc < kU / 8; ++pc) {
-            const int j0 = pc * 256 + lane * 8;
-            if (j0 < Lp) {
-              const uint2 wv = *reinterpret_cast<const uint2*>(ql + j0);
-              float f[8];
-              bytes_to_f32(wv.x, f);
-              bytes_to_f32(wv.y, f + 4);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) u[pc * 8 + i] = fmaf(wgt, f[i], u[pc * 8 + i]);
-            }
-          }
-        }
-        __syncwarp();
-      }
-    }
-    // u / l into this head's query row (no longer needed), then out = W_v u + b_v, lanes over outputs
-    if (live) {
-      const float inv_l = 1.0f / l_run;
-      float* us = qa_s + h * Lp;
-#pragma unroll
-      for (int pc = 0; pc < kU / 8; ++pc) {
-        const int j0 = pc * 256 + lane * 8;
-#pragma unroll
-        for (int i = 0; i < 8; ++i)
-          if (j0 + i < Lp) us[j0 + i] = u[pc * 8 + i] * inv_l;
-      }
-      __syncwarp();
-      const IvbTernary& vu = L.v_up;
-      for (int e = lane; e < hd; e += 32) {
-        const size_t r = static_cast<size_t>(h) * hd + e;
-        const unsigned* row = reinterpret_cast<const unsigned*>(vu.packed + r * vu.row_bytes);
-        float acc = 0.0f;
-        for (int wd = 0; wd < words; ++wd) {
-          const unsigned w = __ldg(row + wd);
-          float cm1[16];
-          word_codes_m1(w, cm1);
-          float part_sum = 0.0f;
-#pragma unroll
-          for (int i = 0; i < 16; ++i) part_sum = fmaf(cm1[i], us[wd * 16 + i], part_sum);
-          acc = fmaf(h2f(__ldg(vu.scales + r * vu.scale_stride + (wd >> 3))), part_sum, acc);
-        }
-        if (vu.bias != nullptr) acc += __ldg(vu.bias + r);
-        y[static_cast<size_t>(b) * d + h * hd + e] = acc;
-      }
+      if (vu.bias != nullptr) acc += __ldg(vu.bias + r);
+      y[static_cast<size_t>(b) * d + h * hd + e] = acc;
     }
   }
 }
@@ -578,9 +715,9 @@ __global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* 
 int32_t launch_batch_attention(const IvbLayerDesc& L, const IvbBatchLayer& BL, const float* ent, int ld, const int64_t* positions,
                                int batch, int d, int Lt, int H, int hd, int rope, int nope, int max_len, int lpad, int rpad,
                                float* y, cudaStream_t s) {
-  if (H <= kSeqWarps && Lt <= 512 && batch >= 128) {
-    const size_t smem = (static_cast<size_t>(H) * lpad + static_cast<size_t>(H) * rope + static_cast<size_t>(H) * kSeqTile +
-                         2 * kSeqTile) * 4 + 2 * static_cast<size_t>(kSeqTile) * (lpad + 16);
+  const int words = lpad / 16;
+  if (H <= kSeqWarps && Lt <= 512 && (words & (words - 1)) == 0 && batch >= 128) {
+    const size_t smem = seq_smem(lpad, rope).total;
     IVB_CUDA(cudaFuncSetAttribute(batch_attention_seq_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
     batch_attention_seq_kernel<<<batch, 32 * kSeqWarps, smem, s>>>(L, BL, ent, ld, positions, d, Lt, H, hd, rope, nope, max_len,
                                                                    lpad, rpad, y);
