@@ -52,13 +52,32 @@ __global__ void __launch_bounds__(kSsmChannels) batch_ssm_kernel(IvbLayerDesc L,
   const int c = c0 + threadIdx.x;
   const int h0 = c0 / hd, nh = (min(d, c0 + kSsmChannels) - 1) / hd - h0 + 1;
   const float* row = ent + static_cast<size_t>(b) * ld;
+  const bool live = c < d;
+  const int h = live ? c / hd : h0, dd = live ? c - h * hd : 0;
+  float* ssm = B.ssm_state + static_cast<size_t>(b) * H * S * hd * 2;
+  float* prevf = B.prev_force + static_cast<size_t>(b) * H * S * hd;
+  // this channel's states (every one loaded before the first store, so the loads overlap) and inputs,
+  // issued before the coefficients so their latency hides behind the transcendental functions
+  float st_r[16], st_i[16], st_p[16];
+#pragma unroll
+  for (int s = 0; s < 16; ++s) {
+    st_r[s] = st_i[s] = st_p[s] = 0.0f;
+    if (live && s < S) {
+      const size_t si = (static_cast<size_t>(h) * S + s) * hd + dd;
+      const float2 v = reinterpret_cast<const float2*>(ssm)[si];
+      st_r[s] = v.x;
+      st_i[s] = v.y;
+      st_p[s] = prevf[si];
+    }
+  }
+  const float incoming = live ? row[c] : 0.0f, gate = live ? row[d + c] : 0.0f;
   for (int i = threadIdx.x; i < nh * S; i += kSsmChannels) {
-    const int h = h0 + i / S, s = i - (i / S) * S;
-    const float* bcdt = row + 2 * d + h * 3 * S;
+    const int hh = h0 + i / S, s = i - (i / S) * S;
+    const float* bcdt = row + 2 * d + hh * 3 * S;
     const float half_dt = half_dt_min + sigmoid_f(bcdt[2 * S + s]) * half_dt_range;
-    const float mag = expf(2.0f * half_dt * L.decay[h * S + s]);
+    const float mag = expf(2.0f * half_dt * L.decay[hh * S + s]);
     float sn, cs;
-    sincosf(2.0f * half_dt * L.theta[h * S + s], &sn, &cs);
+    sincosf(2.0f * half_dt * L.theta[hh * S + s], &sn, &cs);
     float* cf = coef + i * 5;
     cf[0] = tanhf(bcdt[s]);
     cf[1] = tanhf(bcdt[S + s]);
@@ -67,12 +86,8 @@ __global__ void __launch_bounds__(kSsmChannels) batch_ssm_kernel(IvbLayerDesc L,
     cf[4] = mag * sn;
   }
   __syncthreads();
-  if (c >= d) return;
-  const int h = c / hd, dd = c - h * hd;
-  float* ssm = B.ssm_state + static_cast<size_t>(b) * H * S * hd * 2;
-  float* prevf = B.prev_force + static_cast<size_t>(b) * H * S * hd;
+  if (!live) return;
   float* conv_state = B.conv_state + static_cast<size_t>(b) * d * (taps - 1) + static_cast<size_t>(c) * (taps - 1);
-  const float incoming = row[c];
   float conv = L.conv_bias[c];
   for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(L.conv_weight[c * taps + k2], conv_state[k2], conv);
   conv = fmaf(L.conv_weight[c * taps + taps - 1], incoming, conv);
@@ -84,14 +99,13 @@ __global__ void __launch_bounds__(kSsmChannels) batch_ssm_kernel(IvbLayerDesc L,
     if (s < S) {
       const float* cf = coef + ((h - h0) * S + s) * 5;
       const size_t si = (static_cast<size_t>(h) * S + s) * hd + dd;
-      const float sr = ssm[2 * si], sim = ssm[2 * si + 1], prev = prevf[si];
+      const float sr = st_r[s], sim = st_i[s], prev = st_p[s];
       const float force = cf[0] * value;
       const float dr = (force + cf[3] * prev) * cf[2];
       const float di = (cf[4] * prev) * cf[2];
       const float nr = sr * cf[3] - sim * cf[4] + dr;
       const float ni = sr * cf[4] + sim * cf[3] + di;
-      ssm[2 * si] = nr;
-      ssm[2 * si + 1] = ni;
+      reinterpret_cast<float2*>(ssm)[si] = make_float2(nr, ni);
       prevf[si] = force;
       contrib[s] = cf[1] * nr;
     }
@@ -100,7 +114,7 @@ __global__ void __launch_bounds__(kSsmChannels) batch_ssm_kernel(IvbLayerDesc L,
 #pragma unroll
   for (int i = 0; i < 8; ++i) a8[i] = contrib[i] + contrib[i + 8];
   const float sum = ((a8[0] + a8[4]) + (a8[2] + a8[6])) + ((a8[1] + a8[5]) + (a8[3] + a8[7]));
-  y[static_cast<size_t>(b) * d + c] = (sum + L.skip[c] * value) * sigmoid_f(row[d + c]);
+  y[static_cast<size_t>(b) * d + c] = (sum + L.skip[c] * value) * sigmoid_f(gate);
   // shift the conv window: the oldest input leaves, this token's enters
   for (int k = 0; k + 1 < taps - 1; ++k) conv_state[k] = conv_state[k + 1];
   if (taps > 1) conv_state[taps - 2] = incoming;
