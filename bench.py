@@ -65,10 +65,12 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks)")
-    ap.add_argument("--only", choices=("prefill", "gemm", "tp"), default=None,
+    ap.add_argument("--only", choices=("prefill", "gemm", "tp", "batch"), default=None,
                     help="run one secondary measurement alone (for profiler captures): a prefill of "
-                         "--prefill-tokens tokens, or the prefill GEMM on the gate/up shape")
+                         "--prefill-tokens tokens, the prefill GEMM on the gate/up shape, config 4, or "
+                         "config 3 (--batch-tokens decode tokens per sequence)")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
+    ap.add_argument("--batch-tokens", type=int, default=512, help="decode tokens per sequence of --only batch")
     return ap.parse_args()
 
 
@@ -214,8 +216,9 @@ INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
 BATCH_SEQUENCES, BATCH_PROMPT, BATCH_TOKENS, BATCH_WARM = 256, 128, 512, 8
 
 
-def batch_measure(device, world: int, rank: int) -> dict:
-    """Config 3 on this rank: BATCH_SEQUENCES / world sequences decoded together (B200BatchDecoder)."""
+def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS) -> dict:
+    """Config 3 on this rank: BATCH_SEQUENCES / world sequences decoded together (B200BatchDecoder);
+    `tokens` decode tokens per sequence (config 3: 512; fewer only for profiler captures)."""
     import torch
 
     from ivonar_inference_b200 import synthetic
@@ -223,14 +226,14 @@ def batch_measure(device, world: int, rank: int) -> dict:
 
     per_rank = max(1, BATCH_SEQUENCES // world)
     model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
-    max_len = BATCH_PROMPT + BATCH_TOKENS + 8
-    batch = B200BatchDecoder(model, per_rank, max_len=max_len, device=device, history_len=BATCH_TOKENS)
+    max_len = BATCH_PROMPT + tokens + 8
+    batch = B200BatchDecoder(model, per_rank, max_len=max_len, device=device, history_len=tokens)
     first = rank * per_rank
     prompts = [synthetic.random_prompt(32768, BATCH_PROMPT, seed=50_000 + first + i)[0] for i in range(per_rank)]
     batch.start(prompts, [first + i for i in range(per_rank)], TEMPERATURE, TOP_K, PENALTY)
     batch.decode(BATCH_WARM)  # includes the graph capture
     torch.cuda.synchronize(device)
-    timed = BATCH_TOKENS - 1 - BATCH_WARM
+    timed = tokens - 1 - BATCH_WARM
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     start.record()
     batch.decode(timed)
@@ -506,6 +509,10 @@ def main() -> None:
         device = torch.device("cuda", 0)
         if args.only == "prefill":
             print(json.dumps(prefill_measure(device, lengths=((args.prefill_tokens, args.steps),), gemm_reps=0)), flush=True)
+        elif args.only == "batch":
+            r = batch_measure(device, 1, 0, tokens=args.batch_tokens)
+            r["tok_s"] = r["sequences_per_gpu"] * r["steps"] / (r["ms"] / 1000.0)
+            print(json.dumps(r), flush=True)
         else:
             print(json.dumps(prefill_measure(device, lengths=(), gemm_reps=args.steps)["gemm"]), flush=True)
         return

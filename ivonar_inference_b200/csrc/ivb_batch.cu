@@ -390,7 +390,7 @@ __device__ __forceinline__ uint32_t code_tf32(int8_t v) { return __float_as_uint
 
 struct SeqSmem {
   int ldq;  // floats per row of qa / u (Lp + 4)
-  size_t qa_hi, qa_lo, qr, qb, tiles, lsc, s_part, w_hi, w_lo, corr, l, u, total;
+  size_t qa_hl, qr, qb, tiles, lsc, s_part, w_hl, corr, l, u, total;
 };
 __host__ __device__ inline SeqSmem seq_smem(int Lp, int rope) {
   SeqSmem m;
@@ -402,15 +402,13 @@ __host__ __device__ inline SeqSmem seq_smem(int Lp, int rope) {
     o += (bytes + 15) / 16 * 16;
     return at;
   };
-  m.qa_hi = take(static_cast<size_t>(16) * m.ldq * 4);
-  m.qa_lo = take(static_cast<size_t>(16) * m.ldq * 4);
+  m.qa_hl = take(static_cast<size_t>(16) * m.ldq * 8);
   m.qr = take(static_cast<size_t>(16) * rope * 4);
   m.qb = take(16 * 4);
   m.tiles = take(static_cast<size_t>(2) * kSeqTile * lstr);
   m.lsc = take(2 * kSeqTile * 4);
   m.s_part = take(static_cast<size_t>(2) * 16 * (kSeqTile + 4) * 4);
-  m.w_hi = take(static_cast<size_t>(16) * (kSeqTile + 4) * 4);
-  m.w_lo = take(static_cast<size_t>(16) * (kSeqTile + 4) * 4);
+  m.w_hl = take(static_cast<size_t>(16) * (kSeqTile + 4) * 8);
   m.corr = take(16 * 4);
   m.l = take(16 * 4);
   m.u = take(static_cast<size_t>(16) * m.ldq * 4);
@@ -430,15 +428,15 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
   const int lstr = Lp + 16;               // padded tile row
   const SeqSmem M = seq_smem(Lp, rope);
   const int lq = M.ldq;
-  float* qa_hi = reinterpret_cast<float*>(att_smem + M.qa_hi);  // [16][lq] tf32 hi of the absorbed queries
-  float* qa_lo = reinterpret_cast<float*>(att_smem + M.qa_lo);
+  // tf32 (hi, lo) pairs, one 8-byte load per fragment element pair; the row strides (lq, kSt pairs,
+  // both 4 mod 16) keep the fragment loads of a half-warp on distinct banks
+  float2* qa_hl = reinterpret_cast<float2*>(att_smem + M.qa_hl);  // [16][lq] absorbed queries
   float* qr_s = reinterpret_cast<float*>(att_smem + M.qr);      // [16][rope]
   float* qb_s = reinterpret_cast<float*>(att_smem + M.qb);      // [16]
   int8_t* lat_s = reinterpret_cast<int8_t*>(att_smem + M.tiles);  // [2][kSeqTile][lstr]
   float* lsc_s = reinterpret_cast<float*>(att_smem + M.lsc);      // [2][kSeqTile]
   float* s_part = reinterpret_cast<float*>(att_smem + M.s_part);  // [2][16][kSeqTile + 4] (two K halves)
-  float* w_hi = reinterpret_cast<float*>(att_smem + M.w_hi);      // [16][kSeqTile + 4]
-  float* w_lo = reinterpret_cast<float*>(att_smem + M.w_lo);
+  float2* w_hl = reinterpret_cast<float2*>(att_smem + M.w_hl);    // [16][kSeqTile + 4] softmax weights
   float* corr_s = reinterpret_cast<float*>(att_smem + M.corr);    // [16]
   float* l_s = reinterpret_cast<float*>(att_smem + M.l);          // [16]
   float* u_s = reinterpret_cast<float*>(att_smem + M.u);          // [16][lq]
@@ -472,8 +470,7 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
   load_tile(0);
   // rows of heads >= H stay zero: no score, no weight
   for (int i = tid; i < 16 * kSt; i += blockDim.x) {
-    w_hi[i] = 0.0f;
-    w_lo[i] = 0.0f;
+    w_hl[i] = make_float2(0.0f, 0.0f);
   }
   // absorbed queries (tf32 hi/lo), rotated rope queries and q_nope . b_k of every head (warp per head);
   // lane = (e slice, 16-input word): slices of the nope inputs meet by shuffles
@@ -520,8 +517,7 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
       for (int i = 0; i < 16; ++i) {
         const float v = live ? acc[i] : 0.0f;
         const uint32_t hi = tf32_bits(v);
-        qa_hi[h * lq + wd * 16 + i] = __uint_as_float(hi);
-        qa_lo[h * lq + wd * 16 + i] = __uint_as_float(tf32_bits(v - __uint_as_float(hi)));
+        qa_hl[h * lq + wd * 16 + i] = make_float2(__uint_as_float(hi), __uint_as_float(tf32_bits(v - __uint_as_float(hi))));
       }
     float pp = 0.0f;
     if (live && kn.bias != nullptr)
@@ -571,10 +567,10 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
       for (int ks = k_lo; ks < k_hi; ++ks) {
         const int k0 = 8 * ks;
         const uint32_t b0 = code_tf32(prow[k0 + t]), b1 = code_tf32(prow[k0 + t + 4]);
-        mma_tf32(c, __float_as_uint(qa_hi[g * lq + k0 + t]), __float_as_uint(qa_hi[(g + 8) * lq + k0 + t]),
-                 __float_as_uint(qa_hi[g * lq + k0 + t + 4]), __float_as_uint(qa_hi[(g + 8) * lq + k0 + t + 4]), b0, b1);
-        mma_tf32(c, __float_as_uint(qa_lo[g * lq + k0 + t]), __float_as_uint(qa_lo[(g + 8) * lq + k0 + t]),
-                 __float_as_uint(qa_lo[g * lq + k0 + t + 4]), __float_as_uint(qa_lo[(g + 8) * lq + k0 + t + 4]), b0, b1);
+        const float2 a0 = qa_hl[g * lq + k0 + t], a1 = qa_hl[(g + 8) * lq + k0 + t];
+        const float2 a2 = qa_hl[g * lq + k0 + t + 4], a3 = qa_hl[(g + 8) * lq + k0 + t + 4];
+        mma_tf32(c, __float_as_uint(a0.x), __float_as_uint(a1.x), __float_as_uint(a2.x), __float_as_uint(a3.x), b0, b1);
+        mma_tf32(c, __float_as_uint(a0.y), __float_as_uint(a1.y), __float_as_uint(a2.y), __float_as_uint(a3.y), b0, b1);
       }
       float* sp = s_part + half * 16 * kSt;
       sp[g * kSt + 8 * nb + 2 * t] = c[0];
@@ -626,8 +622,7 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
           wgt = e * lsc[pl];
         }
         const uint32_t hi = tf32_bits(wgt);
-        w_hi[h * kSt + pl] = __uint_as_float(hi);
-        w_lo[h * kSt + pl] = __uint_as_float(tf32_bits(wgt - __uint_as_float(hi)));
+        w_hl[h * kSt + pl] = make_float2(__uint_as_float(hi), __uint_as_float(tf32_bits(wgt - __uint_as_float(hi))));
       }
       ls = warp_sum(ls);
       l_run = l_run * corr + ls;
@@ -654,10 +649,10 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
             const int k0 = 8 * ks;
             const uint32_t b0 = code_tf32(tile[(k0 + t) * lstr + 8 * nb + g]);
             const uint32_t b1 = code_tf32(tile[(k0 + t + 4) * lstr + 8 * nb + g]);
-            mma_tf32(uacc[j], __float_as_uint(w_hi[g * kSt + k0 + t]), __float_as_uint(w_hi[(g + 8) * kSt + k0 + t]),
-                     __float_as_uint(w_hi[g * kSt + k0 + t + 4]), __float_as_uint(w_hi[(g + 8) * kSt + k0 + t + 4]), b0, b1);
-            mma_tf32(uacc[j], __float_as_uint(w_lo[g * kSt + k0 + t]), __float_as_uint(w_lo[(g + 8) * kSt + k0 + t]),
-                     __float_as_uint(w_lo[g * kSt + k0 + t + 4]), __float_as_uint(w_lo[(g + 8) * kSt + k0 + t + 4]), b0, b1);
+            const float2 a0 = w_hl[g * kSt + k0 + t], a1 = w_hl[(g + 8) * kSt + k0 + t];
+            const float2 a2 = w_hl[g * kSt + k0 + t + 4], a3 = w_hl[(g + 8) * kSt + k0 + t + 4];
+            mma_tf32(uacc[j], __float_as_uint(a0.x), __float_as_uint(a1.x), __float_as_uint(a2.x), __float_as_uint(a3.x), b0, b1);
+            mma_tf32(uacc[j], __float_as_uint(a0.y), __float_as_uint(a1.y), __float_as_uint(a2.y), __float_as_uint(a3.y), b0, b1);
           }
         }
       }
@@ -692,11 +687,13 @@ __global__ void __launch_bounds__(32 * kSeqWarps) batch_attention_seq_kernel(Ivb
 #pragma unroll 8
       for (int wd = 0; wd < words; ++wd) {
         const unsigned w = __ldg(row + wd);
-        float cm1[16];
+        float cm1[16], uv[16];
         word_codes_m1(w, cm1);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) *reinterpret_cast<float4*>(uv + 4 * i) = reinterpret_cast<const float4*>(us + wd * 16)[i];
         float part_sum = 0.0f;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) part_sum = fmaf(cm1[i], us[wd * 16 + i], part_sum);
+        for (int i = 0; i < 16; ++i) part_sum = fmaf(cm1[i], uv[i], part_sum);
         acc = fmaf(h2f(__ldg(vu.scales + r * vu.scale_stride + (wd >> 3))), part_sum, acc);
       }
       if (vu.bias != nullptr) acc += __ldg(vu.bias + r);
