@@ -71,6 +71,7 @@ def parse() -> argparse.Namespace:
                          "config 3 (--batch-tokens decode tokens per sequence)")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--batch-tokens", type=int, default=512, help="decode tokens per sequence of --only batch")
+    ap.add_argument("--kernel-table", action="store_true", help="--only batch: per-kernel device time of a step")
     return ap.parse_args()
 
 
@@ -216,9 +217,11 @@ INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
 BATCH_SEQUENCES, BATCH_PROMPT, BATCH_TOKENS, BATCH_WARM = 256, 128, 512, 8
 
 
-def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS) -> dict:
+def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS, kernel_table: bool = False) -> dict:
     """Config 3 on this rank: BATCH_SEQUENCES / world sequences decoded together (B200BatchDecoder);
-    `tokens` decode tokens per sequence (config 3: 512; fewer only for profiler captures)."""
+    `tokens` decode tokens per sequence (config 3: 512; fewer only for profiler captures). kernel_table:
+    after the timed steps, 4 more steps under the torch profiler (CUPTI) give the device time per kernel
+    of a step (in `kernels`), outside the timed region."""
     import torch
 
     from ivonar_inference_b200 import synthetic
@@ -226,8 +229,9 @@ def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS) -> 
 
     per_rank = max(1, BATCH_SEQUENCES // world)
     model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
-    max_len = BATCH_PROMPT + tokens + 8
-    batch = B200BatchDecoder(model, per_rank, max_len=max_len, device=device, history_len=tokens)
+    room = 8 if kernel_table else 0  # positions and history slots for the profiled steps
+    max_len = BATCH_PROMPT + tokens + 8 + room
+    batch = B200BatchDecoder(model, per_rank, max_len=max_len, device=device, history_len=tokens + room)
     first = rank * per_rank
     prompts = [synthetic.random_prompt(32768, BATCH_PROMPT, seed=50_000 + first + i)[0] for i in range(per_rank)]
     batch.start(prompts, [first + i for i in range(per_rank)], TEMPERATURE, TOP_K, PENALTY)
@@ -239,7 +243,18 @@ def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS) -> 
     batch.decode(timed)
     end.record()
     torch.cuda.synchronize(device)
-    return {"sequences_per_gpu": per_rank, "ms": start.elapsed_time(end), "steps": timed}
+    out = {"sequences_per_gpu": per_rank, "ms": start.elapsed_time(end), "steps": timed}
+    if kernel_table:
+        from torch.profiler import ProfilerActivity, profile
+
+        extra = 4
+        with profile(activities=[ProfilerActivity.CUDA]) as prof:
+            batch.decode(extra)
+            torch.cuda.synchronize(device)
+        rows = [(e.key, e.count // extra, e.device_time_total / extra) for e in prof.key_averages() if e.device_time_total > 0]
+        out["kernels"] = [{"kernel": k.replace("(anonymous namespace)::", "").split("(")[0], "launches_per_step": c, "us_per_step": round(t, 1)}
+                          for k, c, t in sorted(rows, key=lambda r: -r[2])]
+    return out
 
 
 def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps: int = 20) -> dict:
@@ -510,7 +525,7 @@ def main() -> None:
         if args.only == "prefill":
             print(json.dumps(prefill_measure(device, lengths=((args.prefill_tokens, args.steps),), gemm_reps=0)), flush=True)
         elif args.only == "batch":
-            r = batch_measure(device, 1, 0, tokens=args.batch_tokens)
+            r = batch_measure(device, 1, 0, tokens=args.batch_tokens, kernel_table=args.kernel_table)
             r["tok_s"] = r["sequences_per_gpu"] * r["steps"] / (r["ms"] / 1000.0)
             print(json.dumps(r), flush=True)
         else:
