@@ -272,14 +272,33 @@ __global__ void ssm_cumprod_kernel(const float* coefb, int T, int H, int S, floa
   if (i >= chunks * H * S) return;
   const int k = i / (H * S), hs = i - k * (H * S);
   float pr = 1.0f, pi = 0.0f;
-  for (int t = k * kScanChunk; t < min(T, (k + 1) * kScanChunk); ++t) {
-    const float* cf = coefb + (static_cast<size_t>(t) * H * S + hs) * 5;
-    const float ar = cf[3], ai = cf[4];
-    const float nr = pr * ar - pi * ai, ni = pr * ai + pi * ar;
-    pr = nr;
-    pi = ni;
-    cum[(static_cast<size_t>(t) * H * S + hs) * 2] = pr;
-    cum[(static_cast<size_t>(t) * H * S + hs) * 2 + 1] = pi;
+  const int t_end = min(T, (k + 1) * kScanChunk);
+  // the coefficients of 16 tokens are loaded before their products are stored, so the loads overlap
+  // (stores into cum could alias coefb as far as the compiler knows)
+  constexpr int kBatch = 16;
+  for (int t0 = k * kScanChunk; t0 < t_end; t0 += kBatch) {
+    float ar[kBatch], ai[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int t = t0 + j;
+      ar[j] = ai[j] = 0.0f;
+      if (t < t_end) {
+        const float* cf = coefb + (static_cast<size_t>(t) * H * S + hs) * 5;
+        ar[j] = cf[3];
+        ai[j] = cf[4];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int t = t0 + j;
+      if (t < t_end) {
+        const float nr = pr * ar[j] - pi * ai[j], ni = pr * ai[j] + pi * ar[j];
+        pr = nr;
+        pi = ni;
+        cum[(static_cast<size_t>(t) * H * S + hs) * 2] = pr;
+        cum[(static_cast<size_t>(t) * H * S + hs) * 2 + 1] = pi;
+      }
+    }
   }
 }
 
@@ -293,15 +312,33 @@ __global__ void ssm_carry_kernel(IvbLayerDesc L, const float* cum, const float* 
   const int hs = i / hd;  // (h * S + s)
   const int chunks = (T + kScanChunk - 1) / kScanChunk;
   float xr = L.ssm_state[2 * static_cast<size_t>(i)], xi = L.ssm_state[2 * static_cast<size_t>(i) + 1];
-  for (int k = 0; k < chunks; ++k) {
-    carry[(static_cast<size_t>(k) * lanes + i) * 2] = xr;
-    carry[(static_cast<size_t>(k) * lanes + i) * 2 + 1] = xi;
-    const int t_last = min(T, (k + 1) * kScanChunk) - 1;
-    const float ar = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2], ai = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2 + 1];
-    const float er = xend[(static_cast<size_t>(k) * lanes + i) * 2], ei = xend[(static_cast<size_t>(k) * lanes + i) * 2 + 1];
-    const float nr = er + (ar * xr - ai * xi), ni = ei + (ar * xi + ai * xr);
-    xr = nr;
-    xi = ni;
+  // the inputs of 8 chunks are loaded before their carries are stored, so the loads overlap
+  constexpr int kBatch = 8;
+  for (int k0 = 0; k0 < chunks; k0 += kBatch) {
+    float ar[kBatch], ai[kBatch], er[kBatch], ei[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int k = k0 + j;
+      ar[j] = ai[j] = er[j] = ei[j] = 0.0f;
+      if (k < chunks) {
+        const int t_last = min(T, (k + 1) * kScanChunk) - 1;
+        ar[j] = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2];
+        ai[j] = cum[(static_cast<size_t>(t_last) * H * S + hs) * 2 + 1];
+        er[j] = xend[(static_cast<size_t>(k) * lanes + i) * 2];
+        ei[j] = xend[(static_cast<size_t>(k) * lanes + i) * 2 + 1];
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      const int k = k0 + j;
+      if (k < chunks) {
+        carry[(static_cast<size_t>(k) * lanes + i) * 2] = xr;
+        carry[(static_cast<size_t>(k) * lanes + i) * 2 + 1] = xi;
+        const float nr = er[j] + (ar[j] * xr - ai[j] * xi), ni = ei[j] + (ar[j] * xi + ai[j] * xr);
+        xr = nr;
+        xi = ni;
+      }
+    }
   }
   L.ssm_state[2 * static_cast<size_t>(i)] = xr;
   L.ssm_state[2 * static_cast<size_t>(i) + 1] = xi;
