@@ -181,6 +181,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  // launched as a programmatic dependent: everything above (TMEM, barriers, the first packed-weight
+  // copies) may overlap the previous kernel; its outputs (activations, scales, a residual to add to)
+  // are read only after this wait
+  asm volatile("griddepcontrol.wait;" ::: "memory");
   const unsigned tmem = tmem_base;
   const int quarter = warp & 3;               // TMEM lane quarter this warp may access
   const int row = 32 * quarter + lane;        // epilogue and producer warps: the weight row (TMEM lane)
@@ -399,6 +403,9 @@ static __device__ __align__(256) float g_gemm_partial[kGemmScratch];
 __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x, int n, const float* norm_w, float norm_eps,
                                                                  float clip, float act_eps, int8_t* q8, int ldq,
                                                                  float* scale, int32_t* gsum) {
+  // a GEMM launched after this kernel as a programmatic dependent may start its set-up now (it waits
+  // for this grid's completion before it reads the codes)
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   extern __shared__ __align__(16) unsigned char smem[];
   const int pad = ((n + 63) >> 6) << 6;
   float* xv = reinterpret_cast<float*>(smem);
@@ -597,9 +604,21 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
   }
   const dim3 grid(row_tiles, tok_tiles, splits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  ternary_gemm_kernel<<<grid, kGemmThreads, smem, s>>>(wmap, *m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, g_per,
-                                                        partial, 2000000000ull, error);
-  IVB_CUDA(cudaGetLastError());
+  // programmatic dependent launch: the kernel's set-up overlaps the tail of the previous kernel on the
+  // stream (the kernel waits for that grid with griddepcontrol.wait before reading its outputs)
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kGemmThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  const IvbTernary mv = *m;
+  IVB_CUDA(cudaLaunchKernelEx(&cfg, ternary_gemm_kernel, wmap, mv, q8, ldq, act_scale, static_cast<int>(rows_t), static_cast<int>(epilogue),
+                              out, static_cast<int>(ldo), g_per, partial, 2000000000ull, error));
   if (splits > 1) {
     const int per_row = epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows;
     const int n = rows_t * per_row;
