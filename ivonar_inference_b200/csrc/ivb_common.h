@@ -6,6 +6,7 @@
 #include <cstdarg>
 #include <cstdint>
 #include <cstdio>
+#include <utility>
 
 #include "ivonar_b200.h"
 
@@ -26,6 +27,25 @@ inline int32_t cuda_fail(cudaError_t err, const char* what) {
   } while (0)
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Programmatic dependent launch: the grid may be scheduled while the previous kernel on the stream is
+// still running (once that kernel's CTAs have all triggered, or exited). The kernel must run
+// pdl_enter() (or griddepcontrol.wait) before it reads anything an earlier kernel wrote.
+template <typename... Params, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // Checks the layout contract of one ternary matrix (row_bytes 16-aligned and wide enough,
 // scale_stride covers ceil(in/128) groups, 16-byte aligned base pointer).

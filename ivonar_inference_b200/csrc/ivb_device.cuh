@@ -83,6 +83,12 @@ __device__ __forceinline__ void bulk_copy(void* dst, const void* src, unsigned b
       "l"(src), "r"(bytes), "r"(smem_addr(bar))
       : "memory");
 }
+// First statement of a kernel launched with launch_pdl: wait until the previous grid on the stream has
+// completed and its writes are visible, then let the next grid be scheduled (it waits the same way).
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned parity) {
   unsigned ok;

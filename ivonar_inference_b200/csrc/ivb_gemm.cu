@@ -185,6 +185,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   // copies) may overlap the previous kernel; its outputs (activations, scales, a residual to add to)
   // are read only after this wait
   asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const unsigned tmem = tmem_base;
   const int quarter = warp & 3;               // TMEM lane quarter this warp may access
   const int row = 32 * quarter + lane;        // epilogue and producer warps: the weight row (TMEM lane)
@@ -371,6 +372,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // Split-K reduction: out = epilogue(act_scale[t] * sum_z partial[z][t][r] + bias[r]), splits summed in order.
 __global__ void gemm_splitk_reduce_kernel(const float* partial, int splits, int T, int rows, const float* act_scale,
                                           const float* bias, int epilogue, float* out, int ldo) {
+  pdl_enter();
   const int per_row = epilogue == IVB_EPI_SILU_PAIR ? rows / 2 : rows;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * per_row) return;
@@ -403,9 +405,7 @@ static __device__ __align__(256) float g_gemm_partial[kGemmScratch];
 __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x, int n, const float* norm_w, float norm_eps,
                                                                  float clip, float act_eps, int8_t* q8, int ldq,
                                                                  float* scale, int32_t* gsum) {
-  // a GEMM launched after this kernel as a programmatic dependent may start its set-up now (it waits
-  // for this grid's completion before it reads the codes)
-  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  pdl_enter();  // the next kernel (a GEMM) may start its set-up now; it waits for this grid's completion
   extern __shared__ __align__(16) unsigned char smem[];
   const int pad = ((n + 63) >> 6) << 6;
   float* xv = reinterpret_cast<float*>(smem);
@@ -444,6 +444,7 @@ __global__ void __launch_bounds__(kThreads) quantize_rows_kernel(const float* x,
 
 // Per-row max |x|.
 __global__ void __launch_bounds__(kThreads) rows_amax_kernel(const float* x, int n, float* amax) {
+  pdl_enter();
   __shared__ float red[64];
   const float* row = x + static_cast<size_t>(blockIdx.x) * n;
   float am = 0.0f;
@@ -457,6 +458,7 @@ __global__ void __launch_bounds__(kThreads) rows_amax_kernel(const float* x, int
 // fast reciprocal path with its exact fallback near half-integers).
 __global__ void __launch_bounds__(kThreads) quantize_rows_amax_kernel(const float* x, int n, const float* amax_in,
                                                                       float act_eps, int8_t* q8, int ldq, float* scale) {
+  pdl_enter();
   extern __shared__ __align__(16) unsigned char smem[];
   const int pad = ((n + 63) >> 6) << 6;
   int8_t* codes = reinterpret_cast<int8_t*>(smem);
@@ -508,8 +510,8 @@ int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* 
   const size_t smem = pad * 4 + pad + 64 * 4;
   if (smem > 200 * 1024) return fail(IVB_EINVAL, "ivb_quantize_rows: n %d too large", n);
   IVB_CUDA(cudaFuncSetAttribute(quantize_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  quantize_rows_kernel<<<rows, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, n, norm_weight, norm_eps, norm_clip,
-                                                                                   act_eps, q8, ldq, scale, gsum);
+  IVB_CUDA(launch_pdl(quantize_rows_kernel, dim3(rows), dim3(kThreads), smem, static_cast<cudaStream_t>(stream), x, n, norm_weight, norm_eps, norm_clip,
+                                                                                   act_eps, q8, ldq, scale, gsum));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
@@ -622,8 +624,8 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
   if (splits > 1) {
     const int per_row = epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows;
     const int n = rows_t * per_row;
-    gemm_splitk_reduce_kernel<<<(n + 255) / 256, 256, 0, s>>>(partial, splits, rows_t, m->rows, act_scale, m->bias, epilogue,
-                                                            out, ldo);
+    IVB_CUDA(launch_pdl(gemm_splitk_reduce_kernel, dim3((n + 255) / 256), dim3(256), 0, s, partial, splits, rows_t, m->rows, act_scale, m->bias, epilogue,
+                                                            out, ldo));
     IVB_CUDA(cudaGetLastError());
   }
   return IVB_OK;
@@ -633,7 +635,7 @@ int32_t ivb_rows_amax(const float* x, int32_t rows, int32_t n, float* amax, void
   using namespace ivb;
   if (x == nullptr || amax == nullptr || rows < 0 || n <= 0) return fail(IVB_EINVAL, "ivb_rows_amax: bad argument");
   if (rows == 0) return IVB_OK;
-  rows_amax_kernel<<<rows, kThreads, 0, static_cast<cudaStream_t>(stream)>>>(x, n, amax);
+  IVB_CUDA(launch_pdl(rows_amax_kernel, dim3(rows), dim3(kThreads), 0, static_cast<cudaStream_t>(stream), x, n, amax));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
@@ -648,7 +650,7 @@ int32_t ivb_quantize_rows_amax(const float* x, int32_t rows, int32_t n, const fl
   const size_t smem = static_cast<size_t>((n + 63) / 64) * 64 + 64;
   if (smem > 200 * 1024) return fail(IVB_EINVAL, "ivb_quantize_rows_amax: n %d too large", n);
   IVB_CUDA(cudaFuncSetAttribute(quantize_rows_amax_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  quantize_rows_amax_kernel<<<rows, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(x, n, amax, act_eps, q8, ldq, scale);
+  IVB_CUDA(launch_pdl(quantize_rows_amax_kernel, dim3(rows), dim3(kThreads), smem, static_cast<cudaStream_t>(stream), x, n, amax, act_eps, q8, ldq, scale));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
