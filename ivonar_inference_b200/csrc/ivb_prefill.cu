@@ -25,6 +25,7 @@ constexpr int kMaxTaps = 8;
 
 // Embedding rows of the prompt tokens (the tied head): resid[t][i] = (code - 1) * scale.
 __global__ void __launch_bounds__(kThreads) embed_rows_kernel(IvbTernary head, const int64_t* tokens, int d, float* resid) {
+  pdl_enter();
   const int t = blockIdx.x;
   const long long tok = tokens[t];
   const uint8_t* erow = head.packed + static_cast<size_t>(tok) * head.row_bytes;
@@ -39,6 +40,7 @@ __global__ void __launch_bounds__(kThreads) embed_rows_kernel(IvbTernary head, c
 __global__ void __launch_bounds__(kThreads) ssm_scan_kernel(IvbLayerDesc L, const float* ent, int T, int d, int H, int hd,
                                                             int S, int taps, float half_dt_min, float half_dt_range,
                                                             float* y) {
+  pdl_enter();
   const int lane = threadIdx.x & 31, sub = lane & 15;
   const int c = (blockIdx.x * kThreads + threadIdx.x) >> 4;  // channel
   const bool live = c < d;
@@ -104,6 +106,7 @@ __global__ void __launch_bounds__(kThreads) ssm_scan_kernel(IvbLayerDesc L, cons
 // rows t - taps + 1 .. t (the block's conv window before the chunk for the first tokens).
 __global__ void __launch_bounds__(kThreads) ssm_value_kernel(IvbLayerDesc L, const float* ent, int T, int d, int ld, int taps,
                                                              float* value) {
+  pdl_enter();
   const int i = blockIdx.x * kThreads + threadIdx.x;
   if (i >= T * d) return;
   const int t = i / d, c = i - t * d;
@@ -120,6 +123,7 @@ __global__ void __launch_bounds__(kThreads) ssm_value_kernel(IvbLayerDesc L, con
 // coef[t][h][s] = (tanh B, tanh C, half_dt, Re alpha, Im alpha) with alpha = exp(2 half_dt (decay + i theta)).
 __global__ void ssm_coef_kernel(IvbLayerDesc L, const float* ent, int T, int d, int H, int S, int ld, float half_dt_min,
                                 float half_dt_range, float* coefb) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * H * S) return;
   const int t = i / (H * S), rest = i - t * (H * S), h = rest / S, s = rest - h * S;
@@ -160,6 +164,7 @@ constexpr int kScanThreads = 16 * kScanCh;
 __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDesc L, const float* ent, const float* value,
                                                                   const float* coefb, int T, int d, int H, int hd, int S,
                                                                   int taps, float* xend, float* y) {
+  pdl_enter();
   extern __shared__ float sh[];
   const int tid = threadIdx.x, sub = tid & 15, chl = tid >> 4;
   const int c0 = blockIdx.x * kScanCh, c = c0 + chl;
@@ -267,6 +272,7 @@ __global__ void __launch_bounds__(kScanThreads) ssm_scan_block_kernel(IvbLayerDe
 // Chunk-local products of the decay factors: A[t][h][s] = a_first(chunk) ... a_t (complex), one thread
 // per (chunk, head, state).
 __global__ void ssm_cumprod_kernel(const float* coefb, int T, int H, int S, float* cum) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int chunks = (T + kScanChunk - 1) / kScanChunk;
   if (i >= chunks * H * S) return;
@@ -306,6 +312,7 @@ __global__ void ssm_cumprod_kernel(const float* coefb, int T, int H, int S, floa
 // x_start(k + 1) = x~_end(k) + A_end(k) x_start(k); the state after the last token is stored.
 __global__ void ssm_carry_kernel(IvbLayerDesc L, const float* cum, const float* xend, int T, int H, int S, int hd,
                                  float* carry) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int lanes = H * S * hd;
   if (i >= lanes) return;
@@ -348,6 +355,7 @@ __global__ void ssm_carry_kernel(IvbLayerDesc L, const float* cum, const float* 
 // the sum over the states in the decode kernel's xor-butterfly order.
 __global__ void ssm_output_kernel(IvbLayerDesc L, const float* ent, const float* value, const float* coefb, const float* cum,
                                   const float* carry, int T, int d, int H, int hd, int S, float* y) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= T * d) return;
   const int t = i / d, c = i - t * d, h = c / hd, dd = c - h * hd;
@@ -378,6 +386,7 @@ __global__ void ssm_output_kernel(IvbLayerDesc L, const float* ent, const float*
 // fp16-rounded k_rope of every head. One CTA per token. ent [T][d + Lt + H*rope]: q | latent | k_rope.
 __global__ void __launch_bounds__(kThreads) mla_cache_kernel(IvbLayerDesc L, const float* ent, int pos0, int d, int Lt,
                                                              int H, int rope, int max_len, int lpad, int rpad, float act_eps) {
+  pdl_enter();
   __shared__ float xl[512 + 64];
   __shared__ __align__(16) int8_t codes[576];
   __shared__ float red[64];
@@ -411,6 +420,7 @@ __global__ void __launch_bounds__(kThreads) mla_cache_kernel(IvbLayerDesc L, con
 
 // Latent codes of positions 0..P-1 into the tiled GEMM activation layout (ldq = latent rounded to 128).
 __global__ void latent_tile_kernel(const int8_t* latent_q, int lpad, int Lt, int P, int ldq, int8_t* q8) {
+  pdl_enter();
   const int chunks = ldq >> 4;
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= P * chunks) return;
@@ -455,6 +465,7 @@ template <int DK>
 __global__ void kv_split_kernel(IvbLayerDesc L, const float* knope, const float* vbuf, int P, int Ppad, int d, int H,
                                 int hd, int rope, int nope, int max_len, int rpad, __half* kh, __half* kl, __half* vh,
                                 __half* vl) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   const int per_head = Ppad * (DK / 8);
   if (i >= H * per_head) return;
@@ -503,6 +514,7 @@ __global__ void __launch_bounds__(kFaThreads, DK <= 64 ? 3 : 1) flash_attention_
                                                                      const __half* vh, const __half* vl, int Ppad,
                                                                      int start, int count, int d, int hd, int rope,
                                                                      int nope, float* y) {
+  pdl_enter();
   constexpr int DV = DK;
   constexpr int kKs = DK + 8;       // key tile row stride (halves)
   constexpr int kVs = kFaPos + 8;   // transposed value tile row stride (halves)
@@ -711,14 +723,14 @@ int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const flo
   const size_t per = static_cast<size_t>(H) * Ppad * DK;  // halves per split array
   __half *kh = kvh, *kl = kh + per, *vh = kl + per, *vl = vh + per;
   const int threads = H * Ppad * (DK / 8);
-  kv_split_kernel<DK><<<(threads + 255) / 256, 256, 0, s>>>(L, knope, vbuf, P, Ppad, d, H, hd, rope, nope, max_len, rpad,
-                                                            kh, kl, vh, vl);
+  IVB_CUDA(launch_pdl(kv_split_kernel<DK>, dim3((threads + 255) / 256), dim3(256), 0, s, L, knope, vbuf, P, Ppad, d, H, hd, rope, nope, max_len, rpad,
+                                                            kh, kl, vh, vl));
   IVB_CUDA(cudaGetLastError());
   const size_t tile = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
   const size_t smem = std::max(2 * tile, static_cast<size_t>(kFaTok) * DK * 4);
   IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  flash_attention_kernel<DK><<<dim3((count + kFaTok - 1) / kFaTok, H), kFaThreads, smem, s>>>(
-      L, ent, ld_ent, kh, kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y);
+  IVB_CUDA(launch_pdl(flash_attention_kernel<DK>, dim3(dim3((count + kFaTok - 1) / kFaTok, H)), dim3(kFaThreads), smem, s, 
+      L, ent, ld_ent, kh, kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
@@ -736,6 +748,7 @@ int32_t launch_flash_attention(const IvbLayerDesc& L, const float* ent, int ld_e
 }
 
 __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_end, int64_t* token, int64_t* position) {
+  pdl_enter();
   token[0] = tokens[count - 1];
   position[0] = pos_end;
 }
@@ -837,7 +850,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   uint32_t* err = decoder_error_word(dec);  // reported by ivb_decoder_check
   if (err == nullptr) return fail(IVB_EINVAL, "ivb_decoder_prefill: bind the decoder first");
   const int lpad = static_cast<int>((Lt + 15) / 16 * 16), rpad = (rope + 7) / 8 * 8;
-  embed_rows_kernel<<<count, kThreads, 0, s>>>(md.head, tokens, d, resid);
+  IVB_CUDA(launch_pdl(embed_rows_kernel, dim3(count), dim3(kThreads), 0, s, md.head, tokens, d, resid));
   IVB_CUDA(cudaGetLastError());
   auto quant = [&](const float* x, int n, const float* norm, float eps) -> int32_t {
     const int ld = (n + 127) / 128 * 128;
@@ -853,37 +866,37 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
     if (int32_t rc = gemm(L.entry, IVB_EPI_STORE, ent, L.entry.rows)) return rc;
     if (L.kind == IVB_MAMBA && hd >= 4) {
       const int ld = 2 * d + 3 * H * S;
-      ssm_value_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, ld, L.conv_taps, hbuf);
+      IVB_CUDA(launch_pdl(ssm_value_kernel, dim3((count * d + kThreads - 1) / kThreads), dim3(kThreads), 0, s, L, ent, count, d, ld, L.conv_taps, hbuf));
       IVB_CUDA(cudaGetLastError());
-      ssm_coef_kernel<<<(count * H * S + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, count, d, H, S, ld, L.half_dt_min,
-                                                                                 L.half_dt_range, coefb);
+      IVB_CUDA(launch_pdl(ssm_coef_kernel, dim3((count * H * S + kThreads - 1) / kThreads), dim3(kThreads), 0, s, L, ent, count, d, H, S, ld, L.half_dt_min,
+                                                                                 L.half_dt_range, coefb));
       IVB_CUDA(cudaGetLastError());
       const int nhc_max = std::min(H, (kScanCh - 1) / hd + 2);
       const size_t smem =
           (2 * (static_cast<size_t>(kScanBlock) * nhc_max * S * 5 + kScanBlock * kScanCh) + kScanBlock * kScanThreads) * 4;
       IVB_CUDA(cudaFuncSetAttribute(ssm_scan_block_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
       const int chunks = (count + kScanChunk - 1) / kScanChunk;
-      ssm_cumprod_kernel<<<(chunks * H * S + 127) / 128, 128, 0, s>>>(coefb, count, H, S, cumb);
+      IVB_CUDA(launch_pdl(ssm_cumprod_kernel, dim3((chunks * H * S + 127) / 128), dim3(128), 0, s, coefb, count, H, S, cumb));
       IVB_CUDA(cudaGetLastError());
-      ssm_scan_block_kernel<<<dim3((d + kScanCh - 1) / kScanCh, chunks), kScanThreads, smem, s>>>(
-          L, ent, hbuf, coefb, count, d, H, hd, S, L.conv_taps, xendb, y);
+      IVB_CUDA(launch_pdl(ssm_scan_block_kernel, dim3(dim3((d + kScanCh - 1) / kScanCh, chunks)), dim3(kScanThreads), smem, s, 
+          L, ent, hbuf, coefb, count, d, H, hd, S, L.conv_taps, xendb, y));
       IVB_CUDA(cudaGetLastError());
-      ssm_carry_kernel<<<(H * S * hd + 127) / 128, 128, 0, s>>>(L, cumb, xendb, count, H, S, hd, carryb);
+      IVB_CUDA(launch_pdl(ssm_carry_kernel, dim3((H * S * hd + 127) / 128), dim3(128), 0, s, L, cumb, xendb, count, H, S, hd, carryb));
       IVB_CUDA(cudaGetLastError());
-      ssm_output_kernel<<<(count * d + kThreads - 1) / kThreads, kThreads, 0, s>>>(L, ent, hbuf, coefb, cumb, carryb, count, d,
-                                                                                  H, hd, S, y);
+      IVB_CUDA(launch_pdl(ssm_output_kernel, dim3((count * d + kThreads - 1) / kThreads), dim3(kThreads), 0, s, L, ent, hbuf, coefb, cumb, carryb, count, d,
+                                                                                  H, hd, S, y));
       IVB_CUDA(cudaGetLastError());
     } else if (L.kind == IVB_MAMBA) {
       const int blocks = (d * 16 + kThreads - 1) / kThreads;
-      ssm_scan_kernel<<<blocks, kThreads, 0, s>>>(L, ent, count, d, H, hd, S, L.conv_taps, L.half_dt_min, L.half_dt_range, y);
+      IVB_CUDA(launch_pdl(ssm_scan_kernel, dim3(blocks), dim3(kThreads), 0, s, L, ent, count, d, H, hd, S, L.conv_taps, L.half_dt_min, L.half_dt_range, y));
       IVB_CUDA(cudaGetLastError());
     } else {
-      mla_cache_kernel<<<count, kThreads, 0, s>>>(L, ent, start_position, d, Lt, H, rope, md.max_len, lpad, rpad, md.act_eps);
+      IVB_CUDA(launch_pdl(mla_cache_kernel, dim3(count), dim3(kThreads), 0, s, L, ent, start_position, d, Lt, H, rope, md.max_len, lpad, rpad, md.act_eps));
       IVB_CUDA(cudaGetLastError());
       // keys and values of positions 0..P-1 from the cached latent (earlier chunks included)
       const int P = start_position + count, ldl = (Lt + 127) / 128 * 128;
       const int chunks = P * (ldl >> 4);
-      latent_tile_kernel<<<(chunks + 255) / 256, 256, 0, s>>>(L.latent_q, lpad, Lt, P, ldl, kvq8);
+      IVB_CUDA(launch_pdl(latent_tile_kernel, dim3((chunks + 255) / 256), dim3(256), 0, s, L.latent_q, lpad, Lt, P, ldl, kvq8));
       IVB_CUDA(cudaGetLastError());
       if (int32_t rc = ivb_ternary_gemm(&L.k_nope_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, knope, H * nope, err, stream))
         return rc;
@@ -903,7 +916,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   if (int32_t rc = ivb_ternary_gemv(&md.head, resid + static_cast<size_t>(count - 1) * d, md.final_norm, md.final_norm_eps,
                                     md.norm_clip, md.act_eps, IVB_EPI_STORE, md.logits, stream))
     return rc;
-  prefill_finish_kernel<<<1, 1, 0, s>>>(tokens, count, start_position + count, md.token, md.position);
+  IVB_CUDA(launch_pdl(prefill_finish_kernel, dim3(1), dim3(1), 0, s, tokens, count, start_position + count, md.token, md.position));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
