@@ -522,7 +522,9 @@ __global__ void __launch_bounds__(kFaThreads, DK <= 64 ? 3 : 1) flash_attention_
   extern __shared__ __align__(16) unsigned char fa_smem[];
   __half* tiles = reinterpret_cast<__half*>(fa_smem);
   float* qs = reinterpret_cast<float*>(fa_smem);  // the query block, before the first key tile
-  const int h = blockIdx.y, tq0 = blockIdx.x * kFaTok;
+  // grid (heads, query tiles) with the last query tile first: the causal tiles with the most keys start
+  // in the first wave and the short ones fill the tail
+  const int h = blockIdx.x, tq0 = (gridDim.y - 1 - blockIdx.y) * kFaTok;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, grp = lane >> 2, tig = lane & 3;
   const float scl = L.attn_scale;
   for (int i = tid; i < kFaTok * DK; i += kFaThreads) {
@@ -729,7 +731,7 @@ int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const flo
   const size_t tile = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
   const size_t smem = std::max(2 * tile, static_cast<size_t>(kFaTok) * DK * 4);
   IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  IVB_CUDA(launch_pdl(flash_attention_kernel<DK>, dim3(dim3((count + kFaTok - 1) / kFaTok, H)), dim3(kFaThreads), smem, s, 
+  IVB_CUDA(launch_pdl(flash_attention_kernel<DK>, dim3(H, (count + kFaTok - 1) / kFaTok), dim3(kFaThreads), smem, s, 
       L, ent, ld_ent, kh, kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
