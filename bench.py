@@ -37,6 +37,7 @@ import os
 import statistics
 import subprocess
 import sys
+import tempfile
 import time
 from pathlib import Path
 
@@ -125,9 +126,7 @@ class ClockSampler:
         self.index, self.proc, self.path = index, None, None
         if not enabled:
             return
-        out = ROOT / "gpurun_out"
-        out.mkdir(exist_ok=True)
-        self.path = out / f"clocks_rank{index}.csv"
+        self.path = Path(tempfile.mkdtemp(prefix="ivb_clocks_")) / f"clocks_rank{index}.csv"
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200"],

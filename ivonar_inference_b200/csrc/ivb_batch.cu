@@ -10,7 +10,7 @@
 #include <algorithm>
 
 #include "ivb_common.h"
-#include "ivb_cluster.cuh"
+#include "ivb_decode.cuh"
 #include "ivb_tiles.cuh"
 
 extern "C" {

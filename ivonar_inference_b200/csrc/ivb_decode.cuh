@@ -1,15 +1,21 @@
-// Cluster decode kernel of libivonar_b200.so.
+// Whole-GPU decode kernel of libivonar_b200.so: device-side structures and helpers.
 //
-// One thread-block cluster of R CTAs (R = 16 for the Nano shape, one attention/SSM head per CTA)
-// runs the whole token loop. Activations move between CTAs through distributed shared memory: each
-// CTA publishes its slice of a vector in its own shared memory, a hardware cluster barrier orders
-// the exchange, and consumers read every slice with ld.shared::cluster. Weights reach the CTAs as a
-// per-CTA linear stream (laid out once at bind time): a 3-stage ring of cp.async.bulk copies fed
-// ahead of use, each stage completing on an mbarrier. Per block the critical path is
-//   mamba: [norm+quant -> entry rows of my heads -> SSM step] | out | gate/up | down
-//   mla:   [norm+quant -> entry rows (q, k_rope of my heads, my latent rows)] | attention | out | gate/up | down
-// with one cluster barrier after each bracket; the head and a distributed top-k sampler end the token.
-// Replaces the reference's per-token launch list and its 16-token CUDA graph
+// One cooperative launch of G CTAs (one per SM) runs the whole token loop: R GEMV CTAs run every
+// projection (and the recurrent step of their channels), and one attention CTA per head runs that
+// head's latent attention, so each CTA executes a small set of code that stays in the instruction cache.
+// Every op of the per-token program is a dependent phase across the GPU: each producer CTA writes
+// its slice of the op's output vector as 8-byte words {value, token epoch} into a global buffer
+// owned by that op, and each consumer CTA gathers the whole vector by polling those words until
+// every one carries the current epoch (the flag travels inside the data word, so one L2 round trip
+// both synchronises and delivers; no fence and no counter). Weights reach the CTAs as a per-CTA
+// linear stream (laid out once at bind time): a ring of cp.async.bulk copies fed ahead of use, each
+// stage completing on an mbarrier, so the weight stream overlaps the handoff latency. Per block:
+//   mamba: [norm+quant -> entry rows of my channels (value, gate) and of their head (B, C, dt) -> SSM
+//           step of my channels] | out | gate/up | down
+//   mla:   [norm+quant -> entry rows (q, latent, k_rope slices)] | attention (one dedicated CTA per
+//           head) | out | gate/up | down
+// then the LM head with a local top-k per CTA, a merge by group leaders and a final merge that every
+// CTA runs identically. Replaces the reference's per-token launch list and its 16-token CUDA graph
 // (kernel_decoder.py:179-283, 683-735).
 #pragma once
 
@@ -17,33 +23,31 @@
 
 namespace ivb {
 
-constexpr int kMaxCluster = 16;
-constexpr int kStages = 3;
+constexpr int kStages = 6;
 
-enum OpKind : int32_t { OP_ENTRY_MAMBA = 0, OP_ENTRY_MLA = 1, OP_ATTN = 2, OP_OUT = 3, OP_GATE_UP = 4, OP_DOWN = 5, OP_HEAD = 6 };
-enum Gather : int32_t { G_NONE = 0, G_RESID = 1, G_VEC = 2, G_LATENT = 3 };
-// Buffers that other CTAs fill with st.async pushes; each has a transaction-count mbarrier.
-enum XBuf : int32_t { XB_RESID = 0, XB_VEC = 1, XB_LATENT = 2, XB_CAND = 3, XB_COUNT = 4, XB_NONE = -1 };
+enum OpKind : int32_t {
+  OP_ENTRY_MAMBA = 0, OP_ENTRY_MLA = 1, OP_ATTN = 2, OP_OUT = 3, OP_GATE_UP = 4, OP_DOWN = 5, OP_HEAD = 6, OP_MERGE = 7
+};
+// Where a gathered input vector lands in shared memory.
+enum InDst : int32_t { IN_NONE = 0, IN_RESID = 1, IN_VEC = 2, IN_LATENT = 3, IN_CAND = 4, IN_PARTS = 5 };
 
-// One step of the per-token program; identical for every CTA of the cluster.
+// One step of the per-token program; identical for every CTA.
 struct Op {
   int32_t kind, layer;
-  int32_t first_chunk, n_chunks;  // chunks of the weight stream this op consumes (constants chunk first)
-  int32_t has_const;
-  int32_t gather;                  // what is gathered from the cluster before the op runs
-  int32_t gather_n, gather_per;    // input vector length and per-CTA slice length of its producer
+  int32_t first_chunk, n_chunks;  // chunks of the weight stream this op consumes (norm chunk, constants chunk, rows)
+  int32_t has_norm_chunk, has_const;
+  int32_t in_dst;                  // InDst of the gathered input
+  int32_t ll_in, ll_in_words;      // input: word offset of the previous op's output buffer and its length (-1: none)
+  int32_t ll_out;                  // word offset of this op's output buffer
   int32_t push_per;                // entry of an mla block: latent rows per CTA (output slice stride)
-  int32_t in_buf;                  // input buffer filled by the previous op's pushes (XB_*), or XB_NONE
-  int32_t in_bytes;                // bytes of that fill (all producers together)
   int32_t in_n;                    // GEMV input length
-  int32_t rows_per, rows_total;    // uniform row partition across the cluster
+  int32_t rows_per, rows_total;    // uniform row partition across the CTAs
   int32_t chunk_rows;              // rows per stream chunk
   int32_t row_bytes, scale_stride, has_bias, lpr_log;
-  int32_t epilogue;
   int32_t has_norm;
   float norm_eps;
   // constants chunk: byte offsets of its arrays
-  int32_t c_norm, c_decay, c_theta, c_skip, c_convw, c_convb;
+  int32_t c_decay, c_theta, c_skip, c_convw, c_convb;
   int32_t c_wkn, c_skn, c_bkn, c_wv, c_sv, c_bv;
 };
 
@@ -54,43 +58,52 @@ struct __align__(16) OpRec {
   IvbLayerDesc layer;  // zero for the head
 };
 
-struct ClusterDims {
+struct DecodeDims {
   int32_t vocab, hidden, heads, head_dim, state_dim, latent, rope, nope, dense, max_len, max_top_k;
-  int32_t R, hpc;                  // cluster size, heads per CTA
+  int32_t R;                       // GEMV CTAs (ranks 0 .. R-1); ranks R .. R+heads-1 are the attention CTAs
+  int32_t cpc;                     // recurrent channels per GEMV CTA (hidden / R, within one head)
+  int32_t A;                       // attention CTAs (heads, or 0 without attention blocks)
   int32_t taps;                    // conv taps
   int32_t lpad, rpad;              // latent cache row stride (bytes), k_rope cache row stride (halves)
   int32_t rb_lat, ss_lat;          // row bytes / scale stride of latent-input matrices
   int32_t tile;                    // cached positions per attention tile
+  int32_t group;                   // CTAs per candidate-merge group (the group's first CTA merges)
+  int32_t cand_cap;                // candidates one merge can hold in shared memory
   float act_eps, clip;
   float half_dt_min, half_dt_range;
 };
 
 // Shared-memory map (byte offsets from the dynamic shared memory base).
-struct ClusterSmem {
+struct DecodeSmem {
   int32_t ring, stage_bytes;
-  int32_t xv, act, xsum, resid, pub, pub_n, loc, red, xl;
-  int32_t ctab;                    // chunk table of the CTA: [cpt] u64 offsets, then [cpt] u32 sizes
-  int32_t cand;                    // offset inside the union region of the merge arrays (keys, ids) the head pushes into
+  int32_t xv, act, xsum, resid, pub, pub_n, loc, red, xl;  // xl: the attention op's gathered [q_h | latent | k_rope_h]
+  int32_t ctab;                    // chunk table of the CTA: [cpt] u64 addresses, then [cpt] u32 sizes
+  int32_t cand;                    // offset inside the union region of the gathered candidate arrays (keys, ids)
   int32_t rope_row;                // rope (cos, sin) row of the current position, prefetched by the mla entry op
   int32_t seen;                    // the CTA's slice of the repetition flags, prefetched by the head op
-  int32_t u;                       // union region (attention / sampler)
+  int32_t u;                       // union region (attention / SSM / sampler)
   int32_t total;
 };
 
-struct ClusterParams {
+struct DecodeParams {
   const OpRec* ops;
   const int32_t* op_rows;          // [n_ops][R] output rows of each CTA
   int32_t n_ops;
   int32_t kc;                      // candidate slots per CTA (>= top-k)
+  int32_t head_op;                 // index of the head op (the ops from it on run only when a head is needed)
   int32_t head_first;              // first stream chunk of the head op
   int32_t chunks_per_token;
   int32_t steps;
-  const unsigned long long* chunk_off;  // [R][chunks_per_token] byte offsets into the stream
-  const unsigned* chunk_bytes;          // [R][chunks_per_token]
-  const unsigned char* stream;
-  ClusterDims d;
-  ClusterSmem sm;
-  const IvbLayerDesc* layers;
+  const unsigned long long* chunk_addr;  // [R][chunks_per_token] device addresses of the GEMV CTAs' stream chunks
+  const unsigned* chunk_bytes;           // [R][chunks_per_token]
+  const unsigned long long* attn_addr;   // [heads][n_mla] the attention CTAs' chunks (one per attention op)
+  const unsigned* attn_bytes;            // [heads][n_mla]
+  const int32_t* attn_ops;               // [n_mla] indices of the attention ops in `ops`
+  int32_t n_mla;
+  unsigned long long* ll;          // flag-word buffers of all ops (one token's worth, reused every token)
+  unsigned* epoch;                 // [1] last token epoch used by any run; flags are epoch + 1, + 2, ...
+  DecodeDims d;
+  DecodeSmem sm;
   IvbTernary head;                 // original head matrix (embedding rows)
   float* logits;
   int64_t* token;
@@ -101,9 +114,6 @@ struct ClusterParams {
   const float* sampling;
   const int64_t* top_k;
   uint64_t* rng;
-  unsigned* cand_key;              // [R][K] local top-k candidates of each CTA
-  int* cand_id;
-  int* cand_n;                     // [R]
   unsigned* error;
   const int64_t* feed;
   unsigned long long timeout_ns;
@@ -112,80 +122,148 @@ struct ClusterParams {
   int32_t flags;
 };
 
-// ---- cluster primitives -------------------------------------------------------------------------
-__device__ __forceinline__ unsigned cluster_rank() {
-  unsigned r;
-  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-  return r;
-}
-__device__ __forceinline__ void cluster_sync() {
-  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-__device__ __forceinline__ unsigned map_rank(const void* local, unsigned rank) {
-  unsigned r;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr(local)), "r"(rank));
-  return r;
-}
-__device__ __forceinline__ float ld_cluster_f32(unsigned addr) {
-  float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-  return v;
-}
-__device__ __forceinline__ void st_cluster_f32(unsigned addr, float v) {
-  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
-}
-__device__ __forceinline__ void st_cluster_v4(unsigned addr, float4 v) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
-               : "memory");
-}
-// st.async into another CTA's shared memory; the bytes complete a transaction on that CTA's mbarrier.
-__device__ __forceinline__ void st_async_v4(unsigned addr, float4 v, unsigned mbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(addr),
-               "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(mbar)
-               : "memory");
-}
-__device__ __forceinline__ void st_async_b32(unsigned addr, unsigned v, unsigned mbar) {
-  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];" ::"r"(addr), "r"(v), "r"(mbar)
-               : "memory");
-}
-__device__ __forceinline__ void atom_min_cluster_u32(unsigned addr, unsigned v) {
-  asm volatile("red.shared::cluster.min.u32 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-
 __device__ __forceinline__ int part_lo(int n, int per, int c) { return min(n, c * per); }
 __device__ __forceinline__ int part_hi(int n, int per, int c) { return min(n, (c + 1) * per); }
 
+// ---- flag words: {payload in the low 32 bits, token epoch in the high 32 bits} ------------------
+// A 64-bit aligned relaxed access at gpu scope is single-copy atomic, so a consumer that sees the
+// epoch also sees the payload written with it.
+__device__ __forceinline__ void ll_store(unsigned long long* w, unsigned payload, unsigned flag) {
+  const unsigned long long v = (static_cast<unsigned long long>(flag) << 32) | payload;
+  asm volatile("st.relaxed.gpu.global.b64 [%0], %1;" ::"l"(w), "l"(v) : "memory");
+}
+__device__ __forceinline__ void ll_load2(const unsigned long long* w, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.gpu.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(w) : "memory");
+}
+__device__ __forceinline__ unsigned long long ll_load1(const unsigned long long* w) {
+  unsigned long long a;
+  asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(a) : "l"(w) : "memory");
+  return a;
+}
+
+// Producer side: words [base, base + n) of buffer `buf` <- src[0, n) (any CTA threads).
+__device__ __forceinline__ void ll_put(unsigned long long* buf, int base, const float* src, int n, unsigned flag) {
+  for (int i = threadIdx.x; i < n; i += kThreads) ll_store(buf + base + i, __float_as_uint(src[i]), flag);
+}
+
+// Consumer side, every thread of the CTA: dst <- the payloads of words [0, n1) of src1, then [0, n2) of
+// src2, then [0, n3) of src3, once every word carries `flag`. The pairs of words are loaded all at once
+// (kLLPairs per thread per pass) and only the missing ones are polled again. Bounded: returns false in
+// every thread if some word did not arrive within timeout_ns (the verdict is uniform across the CTA).
+// The sources are 16-byte aligned; n1 and n2 are even (an odd word may end the last range only).
+constexpr int kLLPairs = 9;
+static __device__ __noinline__ bool ll_gather3(const unsigned long long* src1, int n1, const unsigned long long* src2, int n2,
+                                               const unsigned long long* src3, int n3, unsigned flag, unsigned* dst,
+                                               unsigned long long timeout_ns) {
+  const int p1 = n1 >> 1, p2 = p1 + (n2 >> 1), pairs = p2 + (n3 >> 1);
+  bool late = false;
+  for (int base = 0; base < pairs; base += kLLPairs * kThreads) {
+    unsigned long long a[kLLPairs], b[kLLPairs];
+    const unsigned long long* w[kLLPairs];
+#pragma unroll
+    for (int j = 0; j < kLLPairs; ++j) {
+      const int q = base + j * kThreads + static_cast<int>(threadIdx.x);
+      w[j] = q < p1 ? src1 + 2 * q : q < p2 ? src2 + 2 * (q - p1) : src3 + 2 * (q - p2);
+      if (q < pairs) {
+        ll_load2(w[j], a[j], b[j]);
+      } else {
+        a[j] = static_cast<unsigned long long>(flag) << 32;
+        b[j] = a[j];
+      }
+    }
+    unsigned long long t0 = 0ull;
+    unsigned spins = 0u;
+    while (!late) {
+      bool miss = false;
+#pragma unroll
+      for (int j = 0; j < kLLPairs; ++j) {
+        if (static_cast<unsigned>(a[j] >> 32) != flag || static_cast<unsigned>(b[j] >> 32) != flag) {
+          miss = true;
+          ll_load2(w[j], a[j], b[j]);
+        }
+      }
+      if (!miss) break;
+      if ((++spins & 63u) == 0u) {
+        const unsigned long long t = global_ns();
+        if (t0 == 0ull) t0 = t;
+        else if (t - t0 > timeout_ns) late = true;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kLLPairs; ++j) {
+      const int q = base + j * kThreads + static_cast<int>(threadIdx.x);
+      if (q < pairs) {
+        dst[2 * q] = static_cast<unsigned>(a[j]);
+        dst[2 * q + 1] = static_cast<unsigned>(b[j]);
+      }
+    }
+  }
+  // an odd last word of the last non-empty range
+  const int odd_n = n3 > 0 ? n3 : n2 > 0 ? n2 : n1;
+  if ((odd_n & 1) && threadIdx.x == 0 && !late) {
+    const unsigned long long* last = n3 > 0 ? src3 + n3 - 1 : n2 > 0 ? src2 + n2 - 1 : src1 + n1 - 1;
+    unsigned long long v = ll_load1(last);
+    const unsigned long long t0 = global_ns();
+    while (static_cast<unsigned>(v >> 32) != flag) {
+      if (global_ns() - t0 > timeout_ns) {
+        late = true;
+        break;
+      }
+      v = ll_load1(last);
+    }
+    dst[n1 + n2 + n3 - 1] = static_cast<unsigned>(v);
+  }
+  return !__syncthreads_or(late);
+}
+__device__ __forceinline__ bool ll_gather2(const unsigned long long* src1, int n1, const unsigned long long* src2, int n2,
+                                           unsigned flag, unsigned* dst, unsigned long long timeout_ns) {
+  return ll_gather3(src1, n1, src2, n2, src2, 0, flag, dst, timeout_ns);
+}
+__device__ __forceinline__ bool ll_gather(const unsigned long long* buf, int n, unsigned flag, unsigned* dst,
+                                          unsigned long long timeout_ns) {
+  return ll_gather3(buf, n, buf, 0, buf, 0, flag, dst, timeout_ns);
+}
+
 // ---- weight stream ------------------------------------------------------------------------------
+// Lives in shared memory. The producer cursor (issued, p_step, p_chunk) belongs to thread 0; the
+// consumers address chunk number `idx` of the run (every thread knows it: the chunks consumed by
+// earlier tokens plus the op's first chunk), so no per-thread counter travels between routines.
 struct Stream {
   unsigned long long* full;  // [kStages] mbarriers
   unsigned char* ring;
   int stage_bytes;
-  const unsigned long long* coff;  // this CTA's chunk table (shared copy): byte offsets into the stream
-  const unsigned* cbytes;          // chunk sizes
-  unsigned consumed, issued;
+  const unsigned long long* caddr;  // this CTA's chunk table (shared copy): device addresses
+  const unsigned* cbytes;           // chunk sizes
+  int cpt, head_first;       // chunks per token, first chunk of the head (skipped by tokens without one)
+  unsigned issued;
   int p_step, p_chunk;       // producer cursor
 };
 
-__device__ __forceinline__ bool head_needed(const ClusterParams& p, int step) {
+__device__ __forceinline__ bool head_needed(const DecodeParams& p, int step) {
   return (p.flags & (IVB_RUN_SAMPLE | IVB_RUN_HEAD_ALL)) != 0 || step == p.steps - 1;
+}
+// chunks a token consumes: all of them, or those before the head's when it computes no head
+__device__ __forceinline__ int chunks_of_step(const DecodeParams& p, const Stream* s, int step) {
+  return head_needed(p, step) ? s->cpt : s->head_first;
 }
 
 // thread 0 only: queue the next chunk of this CTA's stream into the next ring stage
-__device__ __forceinline__ void stream_issue(const ClusterParams& p, Stream& s, unsigned rank) {
-  if (s.p_step >= p.steps) return;
-  if (s.p_chunk == p.head_first && !head_needed(p, s.p_step)) {
-    s.p_chunk = 0;
-    if (++s.p_step >= p.steps) return;
+static __device__ __noinline__ void stream_issue(const DecodeParams& p, Stream* s) {
+  if (s->p_step >= p.steps) return;
+  if (s->p_chunk == s->head_first && !head_needed(p, s->p_step)) {
+    s->p_chunk = 0;
+    if (++s->p_step >= p.steps) return;
   }
-  const unsigned bytes = s.cbytes[s.p_chunk];
-  const int stage = s.issued % kStages;
-  unsigned long long* bar = s.full + stage;
+  const unsigned bytes = s->cbytes[s->p_chunk];
+  const int stage = s->issued % kStages;
+  unsigned long long* bar = s->full + stage;
   mbar_expect_tx(bar, bytes);  // the stage is only ever written by the copy engine: no proxy fence
-  bulk_copy(s.ring + static_cast<size_t>(stage) * s.stage_bytes, p.stream + s.coff[s.p_chunk], bytes, bar);
-  ++s.issued;
-  if (++s.p_chunk == p.chunks_per_token) {
-    s.p_chunk = 0;
-    ++s.p_step;
+  bulk_copy(s->ring + static_cast<size_t>(stage) * s->stage_bytes, reinterpret_cast<const void*>(s->caddr[s->p_chunk]), bytes,
+            bar);
+  ++s->issued;
+  if (++s->p_chunk == s->cpt) {
+    s->p_chunk = 0;
+    ++s->p_step;
   }
 }
 
@@ -203,21 +281,20 @@ __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsig
   return true;
 }
 
-// all threads: wait until the next chunk has landed; returns its stage base, or nullptr in every
-// thread when any thread's bounded wait ran out (the verdict is uniform across the CTA)
-__device__ __forceinline__ const unsigned char* stream_acquire(const ClusterParams& p, Stream& s) {
-  const int stage = s.consumed % kStages;
-  const unsigned parity = (s.consumed / kStages) & 1u;
-  const bool late = !mbar_wait_bounded(s.full + stage, parity, p.timeout_ns);
-  if (__syncthreads_or(late)) return nullptr;
-  return s.ring + static_cast<size_t>(stage) * s.stage_bytes;
+// every thread: wait until chunk `idx` of the run has landed in its ring stage (each thread's own
+// mbarrier wait makes the copied bytes visible to it; no CTA barrier). Returns the stage base, or
+// nullptr when this thread's bounded wait ran out (the op reports it after its closing barrier).
+__device__ __forceinline__ const unsigned char* stream_acquire(const DecodeParams& p, const Stream* s, unsigned idx) {
+  const int stage = idx % kStages;
+  const unsigned parity = (idx / kStages) & 1u;
+  if (!mbar_wait_bounded(s->full + stage, parity, p.timeout_ns)) return nullptr;
+  return s->ring + static_cast<size_t>(stage) * s->stage_bytes;
 }
 
-// all threads: the chunk is no longer read; refill its stage with a later chunk
-__device__ __forceinline__ void stream_release(const ClusterParams& p, Stream& s, unsigned rank) {
-  __syncthreads();
-  if (threadIdx.x == 0) stream_issue(p, s, rank);
-  ++s.consumed;
+// thread 0, after a CTA barrier that follows the last read of the stages: refill every stage freed
+// since the last call (chunks below `consumed` are no longer read), keeping the ring full.
+__device__ __forceinline__ void stream_refill(const DecodeParams& p, Stream* s, unsigned consumed) {
+  while (s->issued < consumed + kStages && s->p_step < p.steps) stream_issue(p, s);
 }
 
 // ---- GEMV rows from a ring stage ----------------------------------------------------------------
@@ -411,6 +488,53 @@ __device__ __forceinline__ void rows_stage_ct(const ActChunk (&a)[KPL], const bo
   }
 }
 
+// Rows [0, k) of one stream chunk laid out [k x row_bytes packed][k x sstride fp16 (16B pad)][k x fp32
+// bias] against the quantised input `act` (transposed GEMV layout, in_n inputs): 2^lg lanes per row
+// (lg <= 5), lane `sub` owning the 64-input chunks sub + j * 2^lg (j < 4, so in_n <= 256 * 2^lg), their
+// activations held in registers; every row is one chain of fmaf over the lane's chunks followed by
+// an xor butterfly over the lanes. The plan picks lg per op so that the CTA's rows take one pass
+// where the registers allow. One small routine serves every GEMV of the decode kernel.
+constexpr int kRowsKPL = 4;
+static __device__ __noinline__ void rows_generic(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias,
+                                                 float act_scale, const int8_t* act, int in_n, int lg, float* out) {
+  const int lpr = 1 << lg, rpi = kThreads >> lg;
+  const int chunks = (in_n + 63) >> 6;
+  const int sub = threadIdx.x & (lpr - 1);
+  if (static_cast<int>(threadIdx.x >> lg) >= k) return;  // lanes without a row in any pass (rpi > k)
+  ActChunk a[kRowsKPL];
+  bool have[kRowsKPL];
+#pragma unroll
+  for (int j = 0; j < kRowsKPL; ++j) {
+    const int u = sub + (j << lg);
+    have[j] = u < chunks;
+    if (have[j]) {
+      a[j] = load_act_chunk(act, nullptr, u);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a[j].q[q] = make_int4(0, 0, 0, 0);
+      a[j].xsum = 0;
+    }
+  }
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
+  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
+  const unsigned mask = lpr >= 32 ? kFull : (((1u << lpr) - 1u) << (threadIdx.x & 31 & ~(lpr - 1)));
+#pragma unroll 1
+  for (int base = 0; base < k; base += rpi) {
+    const int r = base + (static_cast<int>(threadIdx.x) >> lg);
+    if (r >= k) break;  // the row group's lanes leave together
+    const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * row_bytes);
+    const uint16_t* srow = scales + r * sstride;
+    float acc = 0.0f;
+#pragma unroll
+    for (int j = 0; j < kRowsKPL; ++j) {
+      const int u = sub + (j << lg);
+      if (have[j]) acc = fmaf(static_cast<float>(chunk_dot64(wr[u], a[j])), h2f(srow[u >> 1]) * (1.0f / 64.0f), acc);
+    }
+    for (int off = 1; off < lpr; off <<= 1) acc += __shfl_xor_sync(mask, acc, off);
+    if (sub == 0) out[r] = has_bias ? acc * act_scale + bias[r] : acc * act_scale;
+  }
+}
+
 // Fallback for inputs with more than three chunks per lane: activations re-read from shared memory,
 // chunk sums from xsum (the quantiser fills it for these ops).
 __device__ __forceinline__ void chunk_rows_wide(const Op& op, const unsigned char* stage, int k, const int8_t* act,
@@ -457,8 +581,8 @@ struct TopkScratch {
   int* misc;       // [16]
 };
 
-static __device__ int topk_digit(const TopkScratch& ts, const unsigned* keys, int n, int shift, unsigned& prefix,
-                                 unsigned& mask, int& remaining) {
+static __device__ __noinline__ void topk_digit(const TopkScratch ts, const unsigned* keys, int n, int shift, unsigned prefix,
+                                              unsigned mask, int remaining) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   for (int b = tid; b < kWarps * 256; b += kThreads) ts.hist[b] = 0u;
   __syncthreads();
@@ -496,21 +620,22 @@ static __device__ int topk_digit(const TopkScratch& ts, const unsigned* keys, in
     ts.misc[9] = remaining - static_cast<int>(above);
   }
   __syncthreads();
-  prefix |= static_cast<unsigned>(ts.misc[8]) << shift;
-  mask |= 255u << shift;
-  remaining = ts.misc[9];
-  __syncthreads();
-  return 0;
 }
 
 // The K best of keys[0, n) by (key desc, id asc); ids[i] (or id_base + i when ids == nullptr) must
 // increase with i among equal keys. Writes them sorted into out_key / out_id (K <= kMaxTopK).
-static __device__ void topk_sorted(const unsigned* keys, const int* ids, int id_base, int n, int K, const TopkScratch& ts,
+static __device__ __noinline__ void topk_sorted(const unsigned* keys, const int* ids, int id_base, int n, int K, const TopkScratch ts,
                                    unsigned* ck, int* ci, unsigned* out_key, int* out_id) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   unsigned prefix = 0u, mask = 0u;
   int remaining = K;
-  for (int shift = 24; shift >= 0; shift -= 8) topk_digit(ts, keys, n, shift, prefix, mask, remaining);
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    topk_digit(ts, keys, n, shift, prefix, mask, remaining);
+    prefix |= static_cast<unsigned>(ts.misc[8]) << shift;  // the digit of the K-th key and what is left below it
+    mask |= 255u << shift;
+    remaining = ts.misc[9];
+    __syncthreads();
+  }
   const unsigned thr = prefix;
   if (tid == 0) {
     ts.misc[10] = 0;
@@ -570,7 +695,7 @@ static __device__ void topk_sorted(const unsigned* keys, const int* ids, int id_
 
 // p_c = exp(s_c - s_0) over sorted keys, canonical CDF (32-candidate Hillis-Steele chunks, carries
 // in order), u = philox(key, counter), token = #(cdf <= u * total) clamped to K - 1.
-static __device__ int draw_token(const unsigned* sorted_key, const int* sorted_id, int K, float* cdf, float* red,
+static __device__ __noinline__ int draw_token(const unsigned* sorted_key, const int* sorted_id, int K, float* cdf, float* red,
                                  uint64_t key, uint64_t counter) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float top = key_value(sorted_key[0]);

@@ -1,12 +1,14 @@
-// Persistent multi-layer decode kernel of libivonar_b200.so.
+// Whole-GPU persistent decode kernel of libivonar_b200.so.
 //
-// One cooperative launch runs `steps` tokens: for every token the CTAs (one per SM) walk a phase
-// program built on the host — per block: fused norm+quantise+GEMV entry projection, the recurrent
-// step or latent attention, the out projection with residual add, the SwiGLU gate/up GEMV and the
-// down GEMV with residual add — then the LM head and the sampler. Phases are separated by a bounded
-// grid barrier; each CTA loads the first weight chunks of its next GEMV slice into registers before
-// it waits, so the weight stream overlaps the barrier latency. This replaces the reference's 131-137
-// launches per token and its 16-token CUDA graph (kernel_decoder.py:179-283, 683-735).
+// One cooperative launch of G CTAs (one per SM) runs `steps` tokens: for every token the CTAs walk an
+// op program built on the host — per block: fused norm+quantise+GEMV entry projection (with the
+// recurrent step of the CTA's head for mamba blocks), the latent attention of the CTA's head (mla
+// blocks), the out projection with residual add, the SwiGLU gate/up GEMV and the down GEMV with
+// residual add — then the LM head and the sampler. Consecutive ops hand their outputs over through
+// flag words in global memory (ivb_decode.cuh: the payload and the token epoch in one 8-byte word,
+// gathered by polling), and each CTA's weights stream into a shared-memory ring ahead of use, so the
+// weight traffic overlaps the handoff latency. This replaces the reference's 131-137 launches per
+// token and its 16-token CUDA graph (kernel_decoder.py:179-283, 683-735).
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -16,7 +18,7 @@
 #include <vector>
 
 #include "ivb_common.h"
-#include "ivb_cluster.cuh"
+#include "ivb_decode.cuh"
 
 size_t ivb_sample_smem_bytes(int vocab);
 size_t ivb_gemv_smem_bytes(int n);
@@ -24,11 +26,6 @@ int ivb_lpr_log(int in_features);
 
 namespace ivb {
 
-
-// floats of the recurrent constants copied out of the constants chunk: decay, theta, skip, conv w/b
-__host__ __device__ __forceinline__ int ssm_const_floats(int nh, int S, int hd, int taps) {
-  return 2 * nh * S + nh * hd * (2 + taps);
-}
 __device__ __forceinline__ void cp_async_f32(float* dst, const float* src) {
   asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
@@ -38,32 +35,6 @@ __device__ __forceinline__ void cp_async_16(void* dst, const void* src) {
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-constexpr int kAttnPieces = 4;
-
-// Copy src[0, n) (local shared memory, written before a __syncthreads) to dst[base, base + n) in every
-// CTA of the cluster; the bytes complete on that CTA's mbarrier `bar` (the consumer arms it with the
-// size of the whole fill and waits). Aligned slices go as one bulk shared-to-shared copy per CTA,
-// issued by thread r for CTA r (the copy engine reads src; push_drain() waits for those reads before
-// src is written again); other slices as one st.async per (word, rank).
-__device__ __forceinline__ void push_async(float* dst, int base, const float* src, int n, int R, unsigned long long* bar) {
-  if (((base | n) & 3) == 0) {
-    if (static_cast<int>(threadIdx.x) < R && n > 0) {
-      fence_proxy_async();  // the generic writes of src (ordered by the barrier) before the async-proxy read
-      asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                       map_rank(dst + base, threadIdx.x)),
-                   "r"(smem_addr(src)), "r"(static_cast<unsigned>(n) * 4u), "r"(map_rank(bar, threadIdx.x))
-                   : "memory");
-      asm volatile("cp.async.bulk.commit_group;" ::: "memory");
-    }
-  } else {
-    for (int idx = threadIdx.x; idx < n * R; idx += kThreads) {
-      const int r = idx / n, i = idx - r * n;
-      st_async_b32(map_rank(dst + base + i, r), __float_as_uint(src[i]), map_rank(bar, r));
-    }
-  }
-}
-// Every thread: wait until the bulk pushes this thread issued have read their source.
-__device__ __forceinline__ void push_drain() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
 
 // Bounded wait on an attention tile mbarrier; the verdict is uniform across the CTA.
 __device__ __forceinline__ bool tile_wait(unsigned long long* bar, unsigned parity, unsigned long long timeout_ns) {
@@ -77,7 +48,7 @@ struct TileBuf {
   uint16_t* kr;     // [tile][rpad]
 };
 
-__device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const ClusterDims& D, int b) {
+__device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const DecodeDims& D, int b) {
   const size_t one = round16(D.tile * D.lpad) + round16(D.tile * 4) + round16(D.tile * D.rpad * 2);
   unsigned char* t = base + b * one;
   TileBuf tb;
@@ -87,9 +58,15 @@ __device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const ClusterDi
   return tb;
 }
 
-// thread 0: bulk-copy cached positions [start, start + count) of head h into tile buffer b
-__device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const ClusterDims& D, const TileBuf& tb, int h,
-                                           int start, int count, unsigned long long* bar) {
+// thread 0: bulk-copy cached positions [start, start + count) of head h into tile buffer b. The copies
+// need 16-byte aligned sources: start must be a multiple of 4 (scale entries are 4 bytes); a call that
+// breaks this records IVB_EINVAL in *error and copies nothing (its wait then runs out and reports).
+__device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const DecodeDims& D, const TileBuf& tb, int h,
+                                           int start, int count, unsigned long long* bar, unsigned* error) {
+  if ((start & 3) != 0) {
+    atomicCAS(error, 0u, static_cast<unsigned>(IVB_EINVAL));
+    return;
+  }
   const unsigned lat = count * D.lpad, lsc = round16(count * 4), kr = count * D.rpad * 2;
   asm volatile("fence.proxy.async.global;" ::: "memory");
   fence_proxy_async();
@@ -99,741 +76,1082 @@ __device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const ClusterD
   bulk_copy(tb.kr, L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + start) * D.rpad, kr, bar);
 }
 
-// Rows of all stages of a GEMV op with compile-time lane geometry; the lane's activation chunks are
-// loaded once and stay in registers across the stages. Returns false when a stage wait ran out.
-template <int LG, int KPL, int RPT, typename Tick>
-__device__ __forceinline__ bool rows_ct(const ClusterParams& p, Stream& st, unsigned rank, const Op& op, int rows_c,
-                                        const int8_t* act, float act_scale, float* rows_out, Tick& tick) {
-  const int chunks = (op.in_n + 63) >> 6;
-  const int row_bytes = op.row_bytes, sstride = op.scale_stride;
-  const bool has_bias = op.has_bias != 0;
-  const int n_row_chunks = op.n_chunks - op.has_const, crows = op.chunk_rows;
-  ActChunk a[KPL];
-  bool have[KPL];
-  load_act_ct<LG, KPL>(act, chunks, a, have);
-  bool ok = true;
-  for (int c = 0; c < n_row_chunks; ++c) {
-    const unsigned char* stage = stream_acquire(p, st);
-    tick(2);
-    if (stage == nullptr) {
-      ok = false;
-    } else {
-      const int r0 = c * crows;
-      rows_stage_ct<LG, KPL, RPT>(a, have, stage, max(0, min(crows, rows_c - r0)), row_bytes, sstride, has_bias, act_scale,
-                                  rows_out + r0);
-    }
-    tick(3);
-    stream_release(p, st, rank);
-    tick(4);
+// Candidate slots of the sampler: every CTA of the head op publishes exactly kp (even) candidates,
+// padded with key 0 (below every real score key) where it has fewer rows; the head op's buffer holds
+// all CTAs' keys first ([R][kp]) and then all their ids, so a merge gathers straight into a key array
+// and an id array. Merge leaders publish kq candidates each the same way.
+__device__ __forceinline__ int cand_slots(int K, int rows_per) { return (min(K, max(rows_per, 1)) + 1) & ~1; }
+
+// Publish the first k of (keys, ids) into slots [0, kp) of key_dst and id_dst, padding the rest with
+// key 0 and distinct ids pad_id + j (beyond any vocabulary index, so a merge's (key, id) order stays
+// total). A final merge always holds at least K real candidates, so padding is never drawn.
+__device__ __forceinline__ void cand_put(unsigned long long* key_dst, unsigned long long* id_dst, const unsigned* keys,
+                                        const int* ids, int k, int kp, unsigned pad_id, unsigned flag) {
+  for (int j = threadIdx.x; j < kp; j += kThreads) {
+    ll_store(key_dst + j, j < k ? keys[j] : 0u, flag);
+    ll_store(id_dst + j, j < k ? static_cast<unsigned>(ids[j]) : pad_id + static_cast<unsigned>(j), flag);
   }
+}
+
+// The decode kernel's quantiser for vectors already in shared memory (the latent of the attention op):
+// one out-of-line copy of quantize_block (bit-identical codes).
+static __device__ __noinline__ float quantize_ni(const float* src, int n, const float* norm_w, float norm_eps, float clip,
+                                                 float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
+  return quantize_block(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
+}
+
+// Gather + (RMSNorm +) quantise of an input of at most 1024 values, all in registers: thread t polls
+// the words t, t + 256, t + 512, t + 768 of the input's flag-word buffer, exactly the elements the
+// canonical quantiser assigns to lane t, so the sum of squares (fmaf in that order, warp butterfly,
+// warps in order), the amax and the codes (rint(v / scale), transposed GEMV layout, zero padding to a
+// 64-input chunk) equal quantize_block's bit for bit. buf == nullptr: the values are read from `keep`;
+// otherwise they are also stored there. Returns the activation scale, or -1 in every thread when a
+// word did not arrive within timeout_ns.
+static __device__ __noinline__ float gather_quantize_1k(const unsigned long long* buf, int n, unsigned flag, float* keep,
+                                                        const float* norm_w, float norm_eps, float clip, float act_eps,
+                                                        int8_t* codes, float* red, unsigned long long timeout_ns,
+                                                        long long* t_arrived) {
+  constexpr int E = 4;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  float x[E];
+  bool late = false;
+  if (buf != nullptr) {
+    unsigned long long w[E];
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      const int i = tid + k * kThreads;
+      w[k] = i < n ? ll_load1(buf + i) : static_cast<unsigned long long>(flag) << 32;
+    }
+    unsigned long long t0 = 0ull;
+    unsigned spins = 0u;
+    while (!late) {
+      bool miss = false;
+#pragma unroll
+      for (int k = 0; k < E; ++k) {
+        if (static_cast<unsigned>(w[k] >> 32) != flag) {
+          miss = true;
+          w[k] = ll_load1(buf + tid + k * kThreads);
+        }
+      }
+      if (!miss) break;
+      if ((++spins & 63u) == 0u) {
+        const unsigned long long t = global_ns();
+        if (t0 == 0ull) t0 = t;
+        else if (t - t0 > timeout_ns) late = true;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      const int i = tid + k * kThreads;
+      x[k] = __uint_as_float(static_cast<unsigned>(w[k]));
+      if (keep != nullptr && i < n) keep[i] = x[k];
+    }
+  } else {
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      const int i = tid + k * kThreads;
+      x[k] = i < n ? keep[i] : 0.0f;
+    }
+  }
+  float inv = 0.0f;
+  if (norm_w != nullptr) {
+    float p2 = 0.0f;
+#pragma unroll
+    for (int k = 0; k < E; ++k)
+      if (tid + k * kThreads < n) p2 = fmaf(x[k], x[k], p2);
+    p2 = warp_sum(p2);
+    if (lane == 0) red[warp] = p2;
+  }
+  if (__syncthreads_or(late)) return -1.0f;
+  if (t_arrived != nullptr && threadIdx.x == 0) *t_arrived = clock64();  // tracing: the whole input is here
+  if (norm_w != nullptr) {
+    float ss = red[0];
+#pragma unroll
+    for (int w2 = 1; w2 < kWarps; ++w2) ss += red[w2];
+    inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
+  }
+  float v[E];
+  float am = 0.0f;
+#pragma unroll
+  for (int k = 0; k < E; ++k) {
+    const int i = tid + k * kThreads;
+    v[k] = 0.0f;
+    if (i < n) v[k] = norm_w != nullptr ? __fmul_rn(fminf(fmaxf(__fmul_rn(x[k], inv), -clip), clip), norm_w[i]) : x[k];
+    am = fmaxf(am, fabsf(v[k]));
+  }
+  unsigned* wmax = reinterpret_cast<unsigned*>(red) + 16;
+  {
+    const unsigned m = __reduce_max_sync(kFull, __float_as_uint(am));
+    if (lane == 0) wmax[warp] = m;
+  }
+  __syncthreads();
+  unsigned mbits = wmax[0];
+#pragma unroll
+  for (int w2 = 1; w2 < kWarps; ++w2) mbits = max(mbits, wmax[w2]);
+  const float scale = fmaxf(__uint_as_float(mbits) / 127.0f, act_eps);
+  const float rscale = 1.0f / scale;
+  const int padded = (n + 63) & ~63;
+  bool near = false;
+  int q[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) {
+    const int i = tid + k * kThreads;
+    bool nr = false;
+    q[k] = i < n ? quant_code_fast(v[k], rscale, nr) : 0;
+    near |= nr;
+    if (i < padded) codes[act_slot(i)] = static_cast<int8_t>(q[k]);
+  }
+  if (__syncthreads_or(near)) {
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      const int i = tid + k * kThreads;
+      if (i < n) {
+        bool nr = false;
+        quant_code_fast(v[k], rscale, nr);
+        if (nr) {
+          const int qe = static_cast<int>(rintf(v[k] / scale));
+          if (qe != q[k]) codes[act_slot(i)] = static_cast<int8_t>(qe);
+        }
+      }
+    }
+    __syncthreads();
+  }
+  return scale;
+}
+
+// Gather + (RMSNorm +) quantise of an op's input vector: thread t polls the words t, t + 256, ... of
+// the input's flag-word buffer (all loads in flight at once) and stores the values to `keep` (shared);
+// the quantiser then walks the same elements per thread in the canonical order (sum of squares with
+// fmaf over t, t + 256, ..., warp butterfly, warps in order; amax; codes rint(v / scale) in the
+// transposed GEMV layout, zero padding to a 64-input chunk), so the codes equal quantize_block's bit
+// for bit. One compact routine serves every input width (n <= 3072). buf == nullptr: the values are
+// already in `keep`. Returns the activation scale (> 0), or -1 in every thread when a word did not
+// arrive within timeout_ns.
+constexpr int kMaxEPT = 12;  // input elements per thread: n <= 3072
+static __device__ __noinline__ float gather_quantize(const unsigned long long* buf, int n, unsigned flag, float* keep,
+                                                     const float* norm_w, float norm_eps, float clip, float act_eps,
+                                                     int8_t* codes, float* red, unsigned long long timeout_ns,
+                                                     long long* t_arrived) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  bool late = false;
+  if (buf != nullptr) {
+    unsigned long long w[kMaxEPT];
+#pragma unroll
+    for (int k = 0; k < kMaxEPT; ++k) {
+      const int i = tid + k * kThreads;
+      w[k] = i < n ? ll_load1(buf + i) : static_cast<unsigned long long>(flag) << 32;
+    }
+    unsigned long long t0 = 0ull;
+    unsigned spins = 0u;
+    while (!late) {
+      bool miss = false;
+#pragma unroll
+      for (int k = 0; k < kMaxEPT; ++k) {
+        if (static_cast<unsigned>(w[k] >> 32) != flag) {
+          miss = true;
+          w[k] = ll_load1(buf + tid + k * kThreads);
+        }
+      }
+      if (!miss) break;
+      if ((++spins & 63u) == 0u) {
+        const unsigned long long t = global_ns();
+        if (t0 == 0ull) t0 = t;
+        else if (t - t0 > timeout_ns) late = true;
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < kMaxEPT; ++k) {
+      const int i = tid + k * kThreads;
+      if (i < n) keep[i] = __uint_as_float(static_cast<unsigned>(w[k]));
+    }
+  }
+  float inv = 0.0f;
+  if (norm_w != nullptr) {
+    float p2 = 0.0f;
+    for (int i = tid; i < n; i += kThreads) p2 = fmaf(keep[i], keep[i], p2);  // this thread's own stores
+    p2 = warp_sum(p2);
+    if (lane == 0) red[warp] = p2;
+  }
+  if (__syncthreads_or(late)) return -1.0f;
+  if (t_arrived != nullptr && threadIdx.x == 0) *t_arrived = clock64();  // tracing: the whole input is here
+  if (norm_w != nullptr) {
+    float ss = red[0];
+#pragma unroll
+    for (int w2 = 1; w2 < kWarps; ++w2) ss += red[w2];
+    inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
+  }
+  auto value = [&](int i) -> float {
+    const float x = keep[i];
+    return norm_w != nullptr ? __fmul_rn(fminf(fmaxf(__fmul_rn(x, inv), -clip), clip), norm_w[i]) : x;
+  };
+  float am = 0.0f;
+  for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(value(i)));
+  unsigned* wmax = reinterpret_cast<unsigned*>(red) + 16;
+  {
+    const unsigned m = __reduce_max_sync(kFull, __float_as_uint(am));
+    if (lane == 0) wmax[warp] = m;
+  }
+  __syncthreads();
+  unsigned mbits = wmax[0];
+#pragma unroll
+  for (int w2 = 1; w2 < kWarps; ++w2) mbits = max(mbits, wmax[w2]);
+  const float scale = fmaxf(__uint_as_float(mbits) / 127.0f, act_eps);
+  const float rscale = 1.0f / scale;
+  const int padded = (n + 63) & ~63;
+  bool near = false;
+  for (int i = tid; i < padded; i += kThreads) {
+    bool nr = false;
+    const int q = i < n ? quant_code_fast(value(i), rscale, nr) : 0;
+    near |= nr;
+    codes[act_slot(i)] = static_cast<int8_t>(q);
+  }
+  if (__syncthreads_or(near)) {
+    // rare: values within rounding distance of a half-integer take the IEEE division
+    for (int i = tid; i < n; i += kThreads) {
+      const float v = value(i);
+      bool nr = false;
+      const int q = quant_code_fast(v, rscale, nr);
+      if (nr) {
+        const int qe = static_cast<int>(rintf(v / scale));
+        if (qe != q) codes[act_slot(i)] = static_cast<int8_t>(qe);
+      }
+    }
+    __syncthreads();
+  }
+  return scale;
+}
+
+// Per-CTA state of the decode kernel that the op routines share. It lives in shared memory (thread 0
+// writes it, barriers publish it), so the routines compiled out of line read it without touching the
+// thread stack, whose local-memory traffic would go to L2 (shared memory takes nearly all of L1 here).
+struct Ctx {
+  const DecodeParams* p;
+  Stream* st;
+  unsigned chunk_base;  // stream chunks consumed by the tokens before this one
+  unsigned rank;
+  float *xv, *resid, *loc, *red, *xl, *stg, *rope_s, *seen_s;
+  int8_t* act;
+  int* xsum;
+  unsigned char* U;
+  unsigned long long* abar;
+  unsigned apar[2];     // phase parities of the two attention tile barriers (flipped by thread 0)
+  long long pos;
+  unsigned flag;
+  int K, kp, kq, n_groups;
+  bool two_level, sampling;
+  float inv_t, pen, ipen;
+  // tracing (thread 0): slots 1..6 of the op's record sum SM cycles spent in six parts of the op
+  unsigned long long* marks;
+  long long prof[6];
+  long long prof_t, prof_t2;
+  __device__ __forceinline__ void tick(int part) {
+    if (threadIdx.x == 0 && marks != nullptr) {
+      const long long now = clock64();
+      prof[part] += now - prof_t;
+      prof_t = now;
+    }
+  }
+  __device__ __forceinline__ void fail(unsigned code) {
+    if (threadIdx.x == 0) atomicCAS(p->error, 0u, code);
+  }
+};
+
+// Shared-memory layout of the attention op inside the union region (the plan sizes it the same way):
+// current latent codes [round64(latent)] | qa [round32(latent)] | qr, krc [rope] | qn [nope] |
+// u [round32(latent)] | scores [tile + 4] | 16-byte aligned double tile buffer.
+struct AttnSmem {
+  int8_t* qlc;
+  float *qa, *qr, *krc, *qn, *u, *sc;
+  unsigned char* tiles;
+};
+__host__ __device__ __forceinline__ size_t attn_fixed_bytes(int latent, int rope, int nope, int tile) {
+  const int l64 = (latent + 63) / 64 * 64, l32 = (latent + 31) / 32 * 32;
+  return round16(l64) + static_cast<size_t>(2 * l32 + 2 * rope + nope + tile + 4) * 4 + 16;
+}
+__device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims& D) {
+  const int l64 = (D.latent + 63) / 64 * 64, l32 = (D.latent + 31) / 32 * 32;
+  AttnSmem a;
+  a.qlc = reinterpret_cast<int8_t*>(U);
+  a.qa = reinterpret_cast<float*>(U + round16(l64));
+  a.qr = a.qa + l32;
+  a.krc = a.qr + D.rope;
+  a.qn = a.krc + D.rope;
+  a.u = a.qn + D.nope;
+  a.sc = a.u + l32;
+  unsigned char* t = reinterpret_cast<unsigned char*>(a.sc + D.tile + 4);
+  a.tiles = t + ((16 - (reinterpret_cast<uintptr_t>(t) & 15)) & 15);
+  return a;
+}
+// (code - 1) of input j of a packed row
+__device__ __forceinline__ float code_m1(const unsigned char* row, int j) {
+  return static_cast<float>(((row[j >> 2] >> ((j & 3) << 1)) & 3) - 1);
+}
+
+// Latent attention of head h over the compressed cache, absorbed form, after the head's q, the latent
+// and the head's k_rope were gathered into xl. Reference: ternary.cu:509-611, decoder.py:271-297,
+// attention.py:136-151, with k_nope = W_k(latent) and v = W_v(latent) absorbed:
+//   score_t = a_t <qa, ql_t> + <q_rope, k_rope_t> + q_nope.b_k     (qa = W_k^T q_nope)
+//   out     = W_v (sum_t p_t a_t ql_t) / l + b_v
+// The latent of this position is quantised and appended to the cache, the rotated k_rope of the head
+// too; every attention CTA writes the same latent bytes, so each one later reads cache rows it wrote
+// itself. Cached positions arrive in tiles by bulk copy (double buffered), the current one is scored
+// from shared memory; the caller issues the first tile before this call. Publishes the head's outputs.
+// `chunk`: the op's constants chunk in the ring.
+static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
+  // every field used in a loop is read once into a register: the loops store to shared memory, where
+  // the context, the op record and the parameters also live, so reads through them would repeat
+  const DecodeParams& p = *c.p;
+  const DecodeDims D = p.d;
+  const int c_wkn = opr.c_wkn, c_skn = opr.c_skn, c_bkn = opr.c_bkn, c_wv = opr.c_wv, c_sv = opr.c_sv, c_bv = opr.c_bv;
+  const int ll_out = opr.ll_out;
+  int8_t* const lat_q = L.latent_q;
+  float* const lat_s = L.latent_scale;
+  uint16_t* const kr_cache = L.k_rope_cache;
+  const bool kn_bias = L.k_nope_up.bias != nullptr, v_bias = L.v_up.bias != nullptr;
+  float* const red = c.red;
+  float* const stg = c.stg;
+  unsigned long long* const abar = c.abar;
+  const unsigned flag = c.flag;
+  const int tid = threadIdx.x, sub = tid & 7, grp = tid >> 3;
+  const int Lt = D.latent, l32 = (Lt + 31) / 32 * 32;
+  const int P = static_cast<int>(c.pos);
+  bool ok = true;
+  const unsigned char* cst = stream_acquire(p, c.st, chunk);
+  if (__syncthreads_or(cst == nullptr)) ok = false;
+  const AttnSmem A = attn_smem(c.U, D);
+  const float* qh = c.xl;                 // gathered q of the head
+  const float* lat = c.xl + D.head_dim;   // the latent
+  const float* kh = lat + Lt;             // k_rope of the head
+  const float a_cur = quantize_ni(lat, Lt, nullptr, 0.0f, 0.0f, D.act_eps, A.qlc, false, nullptr, red);
+  for (int j = tid; j < Lt; j += kThreads) lat_q[static_cast<size_t>(P) * D.lpad + j] = A.qlc[j];
+  if (tid == 0) lat_s[P] = a_cur;
+  const float scl = L.attn_scale;
+  cp_async_wait_all();  // the rope row of this position
+  __syncthreads();
+  c.tick(0);
+  for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
+    const float cs = c.rope_s[2 * jr], sn = c.rope_s[2 * jr + 1];
+    const float q0 = qh[D.nope + 2 * jr], q1 = qh[D.nope + 2 * jr + 1];
+    const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
+    A.qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
+    A.qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+    const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
+    A.krc[2 * jr] = kr0;
+    A.krc[2 * jr + 1] = kr1;
+    uint16_t* kc = kr_cache + (static_cast<size_t>(h) * D.max_len + P) * D.rpad;
+    kc[2 * jr] = f2h(kr0);
+    kc[2 * jr + 1] = f2h(kr1);
+  }
+  for (int e = tid; e < D.nope; e += kThreads) A.qn[e] = qh[e] * scl;
+  // cached positions 0..P-1 in tiles, then the current one
+  const int lo = 0, cached = P;
+  const bool has_cur = true;
+  const int n_tiles = cached == 0 ? 1 : (cached + D.tile - 1) / D.tile;
+  // the first tile (positions 0 .. min(P, tile) - 1) was issued before the op's input arrived
+  __syncthreads();
+  // absorbed query qa[j] = sum_e qn[e] * W_knope[h][e][j] (weights from the constants chunk)
+  const unsigned char* wkn = cst + c_wkn;
+  const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + c_skn);
+  for (int j = tid; j < l32; j += kThreads) {
+    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent chains over e (e mod 4), added in order
+    if (j < Lt) {
+      const int sh = (j & 3) << 1, bj = j >> 2, gj = j >> 7;
+      int e = 0;
+      for (; e + 4 <= D.nope; e += 4)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int ee = e + q;
+          const float cm = static_cast<float>(((wkn[ee * D.rb_lat + bj] >> sh) & 3) - 1);
+          acc[q] = fmaf(A.qn[ee], cm * h2f(skn[ee * D.ss_lat + gj]), acc[q]);
+        }
+      for (; e < D.nope; ++e)
+        acc[0] = fmaf(A.qn[e], static_cast<float>(((wkn[e * D.rb_lat + bj] >> sh) & 3) - 1) * h2f(skn[e * D.ss_lat + gj]), acc[0]);
+    }
+    A.qa[j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);  // zero beyond the latent width (the score loop reads whole words)
+  }
+  float qb = 0.0f;
+  if (kn_bias) {
+    const float* bkn = reinterpret_cast<const float*>(cst + c_bkn);
+    float pp = 0.0f;
+    for (int e = tid; e < D.nope; e += kThreads) pp = fmaf(A.qn[e], bkn[e], pp);
+    qb = block_sum(pp, red);
+  } else {
+    __syncthreads();
+  }
+  c.tick(1);
+  // online softmax over the tiles, the current position last
+  float m_run = -INFINITY, l_run = 0.0f, u0 = 0.0f, u1 = 0.0f;
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    const int start = lo + ti * D.tile;
+    const int count = max(0, min(D.tile, lo + cached - start));
+    const bool last = ti == n_tiles - 1;
+    const TileBuf tb = tile_buf(A.tiles, D, ti & 1);
+    if (tid == 0 && ti + 1 < n_tiles && count == D.tile && start + D.tile < lo + cached)
+      tile_issue(L, D, tile_buf(A.tiles, D, (ti + 1) & 1), h, start + D.tile, min(D.tile, lo + cached - start - D.tile),
+                 &abar[(ti + 1) & 1], p.error);
+    if (count > 0) {
+      if (!tile_wait(&abar[ti & 1], c.apar[ti & 1], p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      if (tid == 0) c.apar[ti & 1] ^= 1u;  // every thread read it before the wait's barrier
+    }
+    const int npos = count + (last && has_cur ? 1 : 0);
+    // scores: 8 lanes per position, lane `sub` takes latent words sub, sub + 8, ... and rope entries sub, sub + 8, ...
+#pragma unroll 1
+    for (int k0 = 0; k0 < npos; k0 += kThreads / 8) {
+      const int k = k0 + grp;
+      const bool valid = k < npos, cur = k == count;
+      const int8_t* ql = cur ? A.qlc : tb.lat + (valid ? k : 0) * D.lpad;
+      float dot = 0.0f, rp = 0.0f;
+      if (valid) {
+        float dot1 = 0.0f;
+#pragma unroll 2
+        for (int i = 4 * sub; i < Lt; i += 32) {
+          float f[4];
+          bytes_to_f32(*reinterpret_cast<const unsigned*>(ql + i), f);
+          const float4 q = *reinterpret_cast<const float4*>(A.qa + i);
+          dot = fmaf(q.x, f[0], fmaf(q.y, f[1], dot));
+          dot1 = fmaf(q.z, f[2], fmaf(q.w, f[3], dot1));
+        }
+        dot += dot1;
+        for (int r = sub; r < D.rope; r += 8) rp = fmaf(A.qr[r], cur ? A.krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
+      }
+      float total = valid ? fmaf(cur ? a_cur : tb.lsc[k], dot, rp) : 0.0f;
+      total += __shfl_xor_sync(kFull, total, 4);
+      total += __shfl_xor_sync(kFull, total, 2);
+      total += __shfl_xor_sync(kFull, total, 1);
+      if (valid && sub == 0) A.sc[k] = total + qb;
+    }
+    __syncthreads();
+    float mx = -INFINITY;
+    for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, A.sc[k]);
+    mx = block_max(mx, red);
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+    float ls = 0.0f;
+    for (int k = tid; k < npos; k += kThreads) {
+      const float e = expf(A.sc[k] - m_new);
+      A.sc[k] = e * (k == count ? a_cur : tb.lsc[k]);  // softmax weight times the latent scale
+      ls += e;
+    }
+    ls = block_sum(ls, red);  // its barrier also orders the weights above before the sums below
+    l_run = l_run * corr + ls;
+    u0 *= corr;
+    u1 *= corr;
+    // weighted latent sum: thread j owns latent entries j and j + 256; even and odd positions in
+    // separate chains, added at the end of the tile
+    {
+      float v0 = 0.0f, v1 = 0.0f, w0 = 0.0f, w1 = 0.0f;
+      const bool in0 = tid < Lt, in1 = tid + kThreads < Lt;
+#pragma unroll 2
+      for (int k = 0; k < npos; k += 2) {
+        const int8_t* qa0 = k == count ? A.qlc : tb.lat + k * D.lpad;
+        const float wa = A.sc[k];
+        const bool has_b = k + 1 < npos;
+        const int8_t* qb0 = k + 1 == count ? A.qlc : tb.lat + (has_b ? k + 1 : k) * D.lpad;
+        const float wb = has_b ? A.sc[k + 1] : 0.0f;
+        if (in0) {
+          v0 = fmaf(wa, static_cast<float>(qa0[tid]), v0);
+          w0 = fmaf(wb, static_cast<float>(qb0[tid]), w0);
+        }
+        if (in1) {
+          v1 = fmaf(wa, static_cast<float>(qa0[tid + kThreads]), v1);
+          w1 = fmaf(wb, static_cast<float>(qb0[tid + kThreads]), w1);
+        }
+      }
+      u0 += v0 + w0;
+      u1 += v1 + w1;
+    }
+    m_run = m_new;
+    __syncthreads();  // the tile buffer and the weights are reused
+  }
+  c.tick(2);
+  if (ok) {
+    if (tid < l32) A.u[tid] = tid < Lt ? u0 : 0.0f;
+    if (tid + kThreads < l32) A.u[tid + kThreads] = tid + kThreads < Lt ? u1 : 0.0f;
+    __syncthreads();
+    // out[e] = W_v[h][e] . u / l + b_v[h][e] (four lanes per output, lane q taking a quarter of the latent)
+    const unsigned char* wv = cst + c_wv;
+    const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + c_sv);
+    const float* bv = reinterpret_cast<const float*>(cst + c_bv);
+    const float inv_l = 1.0f / l_run;
+    const int q4 = tid & 3;
+    for (int e0 = 0; e0 < D.head_dim; e0 += kThreads / 4) {
+      const int e = e0 + (tid >> 2);
+      float acc = 0.0f;
+      if (e < D.head_dim) {
+        // lane q4 takes the packed bytes q4, q4 + 4, ... of the row (4 inputs each), four chains
+        const unsigned char* row = wv + e * D.rb_lat;
+        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        for (int b4 = q4; 4 * b4 < Lt; b4 += 4) {
+          const int byte = row[b4];  // signed: (code & 3) - 1 must reach -1
+          const float sc = h2f(sv[e * D.ss_lat + (b4 >> 5)]);
+#pragma unroll
+          for (int f = 0; f < 4; ++f) {
+            const int j = 4 * b4 + f;
+            if (j < Lt) a4[f] = fmaf(static_cast<float>(((byte >> (2 * f)) & 3) - 1) * sc, A.u[j], a4[f]);
+          }
+        }
+        acc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
+      }
+      acc += __shfl_xor_sync(kFull, acc, 1);
+      acc += __shfl_xor_sync(kFull, acc, 2);
+      if (e < D.head_dim && q4 == 0) stg[e] = acc * inv_l + (v_bias ? bv[e] : 0.0f);
+    }
+    __syncthreads();
+    ll_put(p.ll + ll_out, h * D.head_dim, stg, D.head_dim, flag);
+    c.tick(3);
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  if (!ok) c.fail(IVB_ETIMEOUT);
   return ok;
 }
 
-// rope table of an mla block (the entry op's layer description)
-__device__ __forceinline__ const float* L_entry_rope(const IvbLayerDesc& L) { return L.rope; }
+// Recurrent step of the CTA's cpc channels (one head h) after their entry rows: rows_out = [value cpc |
+// gate cpc | B, C, dt of the head 3S]. Causal conv + SiLU per channel, per-state coefficients, the
+// complex state update per (channel, state), the readout C.Re(state) summed over the states in order,
+// skip and output gate; publishes y of the CTA's channels. Reference: ternary.cu:421-482,
+// cpu_decoder.py:137-183, decoder.py:235-264.
+// ssmc: [decay S | theta S | skip cpc | conv w cpc*taps | conv b cpc] from the constants chunk, then
+// scratch [coef 5S | vals cpc | cpart cpc*S], then the prefetched state [cpc per state: S x cpc x 2 |
+// S x cpc prev force | cpc x (taps - 1) conv window].
+__host__ __device__ __forceinline__ int ssm_smem_floats(int cpc, int S, int taps) {
+  return 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S + 3 * S * cpc + cpc * (taps - 1);
+}
+static __device__ __noinline__ void ssm_step(Ctx& c, const Op& op, const IvbLayerDesc& L, const float* rows_out, float* ssmc) {
+  const DecodeParams& p = *c.p;
+  const DecodeDims D = p.d;  // registers: the loops below store to shared memory, where p lives
+  const int tid = threadIdx.x;
+  const int S = D.state_dim, hd = D.head_dim, taps = D.taps, cpc = D.cpc;
+  const int ch0 = c.rank * cpc, h = ch0 / hd, dd0 = ch0 - h * hd;
+  const float* decay = ssmc;
+  const float* theta = decay + S;
+  const float* skip = theta + S;
+  const float* convw = skip + cpc;
+  const float* convb = convw + cpc * taps;
+  float* coef = ssmc + 2 * S + cpc * (2 + taps);  // [5][S]: b, c, half_dt, a_re, a_im
+  float* vals = coef + 5 * S;                    // [cpc] conv + SiLU values
+  float* cpart = vals + cpc;                     // [cpc][S] readout terms
+  const float* s_state = cpart + cpc * S;        // [S][cpc][2]
+  const float* s_prev = s_state + 2 * S * cpc;   // [S][cpc]
+  const float* s_conv = s_prev + S * cpc;        // [cpc][taps - 1]
+  const float* bcdt = rows_out + 2 * cpc;
+  for (int s2 = tid; s2 < S; s2 += kThreads) {
+    const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
+    const float mag = expf(2.0f * half_dt * decay[s2]);
+    float sn, cs;
+    sincosf(2.0f * half_dt * theta[s2], &sn, &cs);
+    coef[s2] = tanhf(bcdt[s2]);
+    coef[S + s2] = tanhf(bcdt[S + s2]);
+    coef[2 * S + s2] = half_dt;
+    coef[3 * S + s2] = mag * cs;
+    coef[4 * S + s2] = mag * sn;
+  }
+  float* const conv_state = L.conv_state;
+  float2* const ssm_state = reinterpret_cast<float2*>(L.ssm_state);
+  float* const prev_force = L.prev_force;
+  float* const stg = c.stg;
+  for (int cl = tid; cl < cpc; cl += kThreads) {
+    const float* win = s_conv + cl * (taps - 1);
+    float* gwin = conv_state + static_cast<size_t>(ch0 + cl) * (taps - 1);
+    const float incoming = rows_out[cl];
+    float conv = convb[cl];
+    for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
+    conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
+    for (int k2 = 0; k2 + 1 < taps - 1; ++k2) gwin[k2] = win[k2 + 1];
+    if (taps > 1) gwin[taps - 2] = incoming;
+    vals[cl] = silu_f(conv);
+  }
+  __syncthreads();
+  // one (channel, state) pair per thread: lanes run along the channels of a state (contiguous state memory)
+  for (int it = tid; it < cpc * S; it += kThreads) {
+    const int s2 = it / cpc, cl = it - s2 * cpc;
+    const int li = s2 * cpc + cl;
+    const size_t gi = static_cast<size_t>(h * S + s2) * hd + dd0 + cl;
+    const float b = coef[s2], cc = coef[S + s2], half_dt = coef[2 * S + s2];
+    const float ar = coef[3 * S + s2], ai = coef[4 * S + s2];
+    const float prev = s_prev[li];
+    const float sr = s_state[2 * li], si = s_state[2 * li + 1];
+    const float force = b * vals[cl];
+    const float dr = (force + ar * prev) * half_dt;
+    const float di = (ai * prev) * half_dt;
+    const float nr = sr * ar - si * ai + dr;
+    const float ni = sr * ai + si * ar + di;
+    ssm_state[gi] = make_float2(nr, ni);
+    prev_force[gi] = force;
+    cpart[cl * S + s2] = cc * nr;
+  }
+  __syncthreads();
+  for (int cl = tid; cl < cpc; cl += kThreads) {
+    float contrib = 0.0f;
+    for (int s2 = 0; s2 < S; ++s2) contrib += cpart[cl * S + s2];
+    stg[cl] = (contrib + skip[cl] * vals[cl]) * sigmoid_f(rows_out[cpc + cl]);
+  }
+  __syncthreads();
+  ll_put(p.ll + op.ll_out, ch0, stg, cpc, c.flag);
+}
 
-__global__ void __launch_bounds__(kThreads, 1) cluster_decode_kernel(const __grid_constant__ ClusterParams p) {
+// Local top-k of the head op: keys[0, n) (n <= 256, one per thread) ranked by (key desc, index asc);
+// those of rank < k go to out_key/out_id in order. Every thread counts the keys above its own.
+static __device__ __noinline__ void topk_by_rank(const unsigned* keys, int n, int k, int id_base, unsigned* out_key, int* out_id) {
+  const int tid = threadIdx.x;
+  if (tid < n) {
+    const unsigned mine = keys[tid];
+    int rank = 0;
+    for (int o = 0; o < n; ++o) {
+      const unsigned ko = keys[o];
+      rank += (ko > mine || (ko == mine && o < tid)) ? 1 : 0;
+    }
+    if (rank < k) {
+      out_key[rank] = mine;
+      out_id[rank] = id_base + tid;
+    }
+  }
+  __syncthreads();
+}
+
+// Every GEMV op (entry projections, out, gate/up, down, head) of one CTA: prefetches for the op's
+// epilogue, the gathered and (normed) quantised input, its rows chunk by chunk from the weight ring,
+// and the epilogue (publish the output slice, residual add, SwiGLU, the recurrent step, or the head's
+// logits and local top-k candidates).
+static __device__ __noinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDesc& lay, int rows_c) {
+  // the op record, the dimensions and the context fields used below are read once into registers (the
+  // op stores to shared memory, where all three live)
+  const DecodeParams& p = *c.p;
+  const Op op = opr;
+  Stream* st = c.st;
+  unsigned idx = c.chunk_base + op.first_chunk;  // the op's chunks: [norm] [constants] rows...
+  const DecodeDims D = p.d;
+  unsigned char* U = c.U;
+  const int tid = threadIdx.x;
+  const unsigned flag = c.flag;
+  const int lo = min(op.rows_total, static_cast<int>(c.rank) * op.rows_per);
+  float* rows_out = c.loc;
+  bool ok = true;
+  const unsigned char* cst = nullptr;
+  float* ssmc = reinterpret_cast<float*>(U);
+  const int S = D.state_dim, taps = D.taps, cpc = D.cpc;
+  if (op.kind == OP_HEAD && c.sampling && ((lo | rows_c) & 3) == 0) {
+    // the repetition flags of my vocabulary slice, for the local top-k
+    const float* src = reinterpret_cast<const float*>(p.seen + lo);
+    for (int i = tid; i < rows_c / 4; i += kThreads) cp_async_f32(c.seen_s + i, src + i);
+    cp_async_commit();
+  } else if (op.kind == OP_ENTRY_MAMBA) {
+    // the recurrent state of my channels streams into shared memory while the rows are computed:
+    // per state s the cpc complex values and previous forces of my channels, then the conv windows
+    const int hd = D.head_dim, ch0 = c.rank * cpc, h = ch0 / hd, dd0 = ch0 - h * hd;
+    float* dst = ssmc + 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S;
+    const int l0 = 2 * S * cpc, l1 = S * cpc, l2 = cpc * (taps - 1);
+    for (int i = tid; i < l0 + l1 + l2; i += kThreads) {
+      const float* src;
+      if (i < l0) {
+        const int s2 = i / (2 * cpc), r = i - s2 * 2 * cpc;
+        src = lay.ssm_state + (static_cast<size_t>(h * S + s2) * hd + dd0) * 2 + r;
+      } else if (i < l0 + l1) {
+        const int s2 = (i - l0) / cpc, r = (i - l0) - s2 * cpc;
+        src = lay.prev_force + static_cast<size_t>(h * S + s2) * hd + dd0 + r;
+      } else {
+        src = lay.conv_state + static_cast<size_t>(ch0) * (taps - 1) + (i - l0 - l1);
+      }
+      cp_async_f32(dst + i, src);
+    }
+    cp_async_commit();
+  }
+  c.tick(0);
+  // the input: the previous op's output gathered from its flag words (or the embedding / combined
+  // attention already in shared memory), normed with the weights of its own stream chunk, quantised
+  const unsigned char* nrm = nullptr;
+  if (op.has_norm_chunk) {
+    nrm = stream_acquire(p, st, idx++);
+    if (nrm == nullptr) ok = false;
+  }
+  const bool from_smem = op.ll_in < 0;
+  float* keep = op.in_dst == IN_RESID ? c.resid : c.xv;
+  long long* t_arr = c.marks != nullptr ? &c.prof_t2 : nullptr;
+  const unsigned long long* src = from_smem ? nullptr : p.ll + op.ll_in;
+  const float* nw = op.has_norm ? reinterpret_cast<const float*>(nrm) : nullptr;
+  const float act_scale =
+      op.in_n <= 4 * kThreads
+          ? gather_quantize_1k(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.red, p.timeout_ns, t_arr)
+          : gather_quantize(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.red, p.timeout_ns, t_arr);
+  if (act_scale < 0.0f) ok = false;
+  if (tid == 0 && c.marks != nullptr && !from_smem) {  // split the wait for the input from the quantiser
+    c.prof[1] += c.prof_t2 - c.prof_t;
+    c.prof_t = c.prof_t2;
+  }
+  if (op.has_const) {
+    cst = stream_acquire(p, st, idx++);
+    if (cst == nullptr) ok = false;
+  }
+  c.tick(2);
+  // SSM constants leave the stage before it is recycled
+  if (op.kind == OP_ENTRY_MAMBA && cst != nullptr) {
+    const int e0 = S, e1 = 2 * S, e2 = e1 + cpc, e3 = e2 + cpc * taps, e4 = e3 + cpc;
+    for (int i = tid; i < e4; i += kThreads) {
+      const float* src = i < e0   ? reinterpret_cast<const float*>(cst + op.c_decay) + i
+                         : i < e1 ? reinterpret_cast<const float*>(cst + op.c_theta) + (i - e0)
+                         : i < e2 ? reinterpret_cast<const float*>(cst + op.c_skip) + (i - e1)
+                         : i < e3 ? reinterpret_cast<const float*>(cst + op.c_convw) + (i - e2)
+                                  : reinterpret_cast<const float*>(cst + op.c_convb) + (i - e3);
+      ssmc[i] = *src;
+    }
+  }
+  // rows of this CTA, chunk by chunk (a warp skips a chunk whose wait ran out in any of its lanes)
+  const int n_row_chunks = op.n_chunks - op.has_const - op.has_norm_chunk;
+  for (int ch = 0; ch < n_row_chunks; ++ch) {
+    const unsigned char* stage = stream_acquire(p, st, idx++);
+    if (!__all_sync(kFull, stage != nullptr)) {
+      ok = false;
+    } else {
+      const int r0 = ch * op.chunk_rows;
+      const int k = max(0, min(op.chunk_rows, rows_c - r0));
+      if (k > 0) rows_generic(stage, k, op.row_bytes, op.scale_stride, op.has_bias, act_scale, c.act, op.in_n, op.lpr_log, rows_out + r0);
+    }
+  }
+  __syncthreads();  // every row of this CTA is in rows_out
+  c.tick(3);
+  float* stg = c.stg;
+  // epilogues
+  if (op.kind == OP_OUT || op.kind == OP_DOWN) {
+    for (int r = tid; r < rows_c; r += kThreads) stg[r] = c.resid[lo + r] + rows_out[r];
+    __syncthreads();
+    ll_put(p.ll + op.ll_out, lo, stg, rows_c, flag);
+  } else if (op.kind == OP_GATE_UP) {
+    for (int m = tid; m < rows_c / 2; m += kThreads) stg[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
+    __syncthreads();
+    ll_put(p.ll + op.ll_out, lo / 2, stg, rows_c / 2, flag);
+  } else if (op.kind == OP_ENTRY_MLA) {
+    ll_put(p.ll + op.ll_out, lo, rows_out, rows_c, flag);
+  } else if (op.kind == OP_HEAD) {
+    for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
+    if (c.sampling) {
+      // local top-k of my vocabulary slice (rows_c <= 256, one key per thread) for the sampler
+      unsigned* keys = reinterpret_cast<unsigned*>(U);
+      unsigned* ok_key = keys + kThreads;
+      int* ok_id = reinterpret_cast<int*>(ok_key + p.kc);
+      cp_async_wait_all();
+      __syncthreads();
+      const uint8_t* seen_b = reinterpret_cast<const uint8_t*>(c.seen_s);
+      const bool pref = ((lo | rows_c) & 3) == 0;
+      for (int r = tid; r < rows_c; r += kThreads)
+        keys[r] = score_key(rows_out[r], pref ? seen_b[r] : __ldcg(p.seen + lo + r), c.inv_t, c.pen, c.ipen);
+      __syncthreads();
+      const int kl = min(c.K, rows_c);
+      topk_by_rank(keys, rows_c, kl, lo, ok_key, ok_id);
+      const int R = D.R, kp = c.kp;
+      cand_put(p.ll + op.ll_out + static_cast<size_t>(c.rank) * kp, p.ll + op.ll_out + static_cast<size_t>(R) * kp + static_cast<size_t>(c.rank) * kp,
+               ok_key, ok_id, kl, kp, 0x40000000u + c.rank * static_cast<unsigned>(kp), flag);
+    }
+  } else if (op.kind == OP_ENTRY_MAMBA) {
+    cp_async_wait_all();
+    __syncthreads();
+    ssm_step(c, opr, lay, rows_out, ssmc);
+  }
+  c.tick(4);
+  if (!ok) atomicCAS(p.error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
+  return ok;
+}
+
+// Group leaders (two-level merges only): the top-k of their group's head candidates, published as kq slots.
+static __device__ __noinline__ bool op_merge(Ctx& c, const Op& op) {
+  const DecodeParams& p = *c.p;
+  const DecodeDims& D = p.d;
+  const int R = D.R;
+  if (!c.sampling || !c.two_level || c.rank % D.group != 0) return true;  // candidates exist only when sampling
+  const int g = c.rank / D.group;
+  const int nblk = min(D.group, R - g * D.group);
+  const int kp = c.kp, kq = c.kq;
+  const unsigned long long* hbuf = p.ll + op.ll_in;
+  unsigned* mk = reinterpret_cast<unsigned*>(c.U + p.sm.cand);
+  int* mi = reinterpret_cast<int*>(mk + nblk * kp);
+  unsigned* ck = reinterpret_cast<unsigned*>(c.U);
+  int* ci = reinterpret_cast<int*>(ck + p.kc);
+  unsigned* sk = reinterpret_cast<unsigned*>(ci + p.kc);
+  int* si = reinterpret_cast<int*>(sk + p.kc);
+  TopkScratch ts{reinterpret_cast<unsigned*>(si + p.kc), reinterpret_cast<int*>(si + p.kc) + kWarps * 256};
+  const size_t first = static_cast<size_t>(g) * D.group * kp;
+  if (!ll_gather2(hbuf + first, nblk * kp, hbuf + static_cast<size_t>(R) * kp + first, nblk * kp, c.flag, mk, p.timeout_ns)) {
+    c.fail(IVB_ETIMEOUT);
+    return false;
+  }
+  const int kk = min(c.K, nblk * kp);
+  topk_sorted(mk, mi, 0, nblk * kp, kk, ts, ck, ci, sk, si);
+  cand_put(p.ll + op.ll_out + static_cast<size_t>(g) * kq, p.ll + op.ll_out + static_cast<size_t>(c.n_groups) * kq + static_cast<size_t>(g) * kq,
+           sk, si, kk, kq, 0x60000000u + static_cast<unsigned>(g * kq), c.flag);
+  return true;
+}
+
+// Every CTA: merge the candidates (of the group leaders, or of every head CTA) and draw the same token
+// with the Philox uniform of counter rctr. Returns the token, or -1 when a wait ran out.
+static __device__ __noinline__ int draw_next(Ctx& c, uint64_t rkey, uint64_t rctr) {
+  const DecodeParams& p = *c.p;
+  const int kc = p.kc, R = p.d.R;
+  const int nblk = c.two_level ? c.n_groups : R;
+  const int kb = c.two_level ? c.kq : c.kp;
+  const unsigned long long* src = p.ll + (c.two_level ? p.ops[p.n_ops - 1].op.ll_out : p.ops[p.head_op].op.ll_out);
+  unsigned* mk = reinterpret_cast<unsigned*>(c.U + p.sm.cand);
+  int* mi = reinterpret_cast<int*>(mk + nblk * kb);
+  unsigned* ck = reinterpret_cast<unsigned*>(c.U);
+  int* ci = reinterpret_cast<int*>(ck + kc);
+  unsigned* sk = reinterpret_cast<unsigned*>(ci + kc);
+  int* si = reinterpret_cast<int*>(sk + kc);
+  float* cdf = reinterpret_cast<float*>(si + kc);
+  TopkScratch ts{reinterpret_cast<unsigned*>(cdf + kc), reinterpret_cast<int*>(cdf + kc) + kWarps * 256};
+  if (!ll_gather(src, nblk * 2 * kb, c.flag, mk, p.timeout_ns)) {
+    c.fail(IVB_ETIMEOUT);
+    return -1;
+  }
+  const int n = nblk * kb;
+  const int kk = min(c.K, n);
+  topk_sorted(mk, mi, 0, n, kk, ts, ck, ci, sk, si);
+  return draw_token(sk, si, kk, cdf, c.red, rkey, rctr);
+}
+
+__global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long full[kStages];
   __shared__ __align__(8) unsigned long long abar[2];
-  __shared__ __align__(8) unsigned long long xbar[XB_COUNT];  // fills of the pushed buffers (transaction counts)
   __shared__ __align__(16) OpRec opbuf[2];  // the running op and the next one (descriptor + layer)
   __shared__ __align__(16) int rowsbuf[2][4];
-  const unsigned rank = cluster_rank();
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const ClusterDims& D = p.d;
-  const ClusterSmem& M = p.sm;
+  __shared__ Ctx c;
+  __shared__ Stream st;
+  __shared__ __align__(16) DecodeParams ps;  // the parameters, read by the op routines from shared memory
+  const unsigned rank = blockIdx.x;
+  const int tid = threadIdx.x;
+  const DecodeDims& D = p.d;
+  const DecodeSmem& M = p.sm;
   const int R = D.R;
-  float* xv = reinterpret_cast<float*>(smem + M.xv);
-  int8_t* act = reinterpret_cast<int8_t*>(smem + M.act);
-  int* xsum = reinterpret_cast<int*>(smem + M.xsum);
-  float* resid = reinterpret_cast<float*>(smem + M.resid);
-  float* loc = reinterpret_cast<float*>(smem + M.loc);
-  float* red = reinterpret_cast<float*>(smem + M.red);
-  float* xl = reinterpret_cast<float*>(smem + M.xl);
-  float* stg = reinterpret_cast<float*>(smem + M.pub);  // this op's output slice before it is pushed
-  unsigned char* U = smem + M.u;
-  if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&full[s], 1);
-    mbar_init(&abar[0], 1);
-    mbar_init(&abar[1], 1);
-    for (int b = 0; b < XB_COUNT; ++b) mbar_init(&xbar[b], 1);
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  const bool attn_cta = static_cast<int>(rank) >= R;  // one per head: runs only the attention ops
+  const int cpt = attn_cta ? p.n_mla : p.chunks_per_token;
+  const unsigned long long* my_addr =
+      attn_cta ? p.attn_addr + static_cast<size_t>(rank - R) * p.n_mla : p.chunk_addr + static_cast<size_t>(rank) * cpt;
+  const unsigned* my_bytes =
+      attn_cta ? p.attn_bytes + static_cast<size_t>(rank - R) * p.n_mla : p.chunk_bytes + static_cast<size_t>(rank) * cpt;
+  unsigned long long* caddr = reinterpret_cast<unsigned long long*>(smem + M.ctab);
+  unsigned* cbytes = reinterpret_cast<unsigned*>(caddr + p.chunks_per_token);
+  for (int k = tid; k < cpt; k += kThreads) {
+    caddr[k] = my_addr[k];
+    cbytes[k] = my_bytes[k];
   }
-  unsigned long long* coff = reinterpret_cast<unsigned long long*>(smem + M.ctab);
-  unsigned* cbytes = reinterpret_cast<unsigned*>(coff + p.chunks_per_token);
-  for (int c = tid; c < p.chunks_per_token; c += kThreads) {
-    coff[c] = p.chunk_off[static_cast<size_t>(rank) * p.chunks_per_token + c];
-    cbytes[c] = p.chunk_bytes[static_cast<size_t>(rank) * p.chunks_per_token + c];
-  }
-  float* rope_s = reinterpret_cast<float*>(smem + M.rope_row);
-  float* seen_s = reinterpret_cast<float*>(smem + M.seen);  // bytes; float* for the 4-byte copies
-  __syncthreads();
-  cluster_sync();
-  Stream st{full, smem + M.ring, M.stage_bytes, coff, cbytes, 0u, 0u, 0, 0};
+  for (int i = tid; i < static_cast<int>(sizeof(DecodeParams) / 4); i += kThreads)
+    reinterpret_cast<unsigned*>(&ps)[i] = reinterpret_cast<const unsigned*>(&p)[i];
   // op descriptors travel through a two-slot shared buffer: op k+1 is fetched while op k runs
   auto fetch_op = [&](int oi, int slot) {
     if (tid < static_cast<int>(sizeof(OpRec) / 16))
       cp_async_16(reinterpret_cast<unsigned char*>(&opbuf[slot]) + 16 * tid,
                   reinterpret_cast<const unsigned char*>(p.ops + oi) + 16 * tid);
-    else if (tid == kThreads - 1)
+    else if (tid == kThreads - 1 && !attn_cta)
       cp_async_f32(reinterpret_cast<float*>(&rowsbuf[slot][0]), reinterpret_cast<const float*>(p.op_rows + oi * R + rank));
     cp_async_commit();
   };
-  fetch_op(0, 0);
+  fetch_op(attn_cta ? (p.n_mla > 0 ? p.attn_ops[0] : 0) : 0, 0);
+  long long tok = p.feed != nullptr ? ldcg_i64(p.feed) : ldcg_i64(p.token);
+  const unsigned epoch0 = __ldcg(p.epoch);
+  const uint64_t rkey = p.rng[0];
+  uint64_t rctr = p.rng[1];
+  if (tid == 0) {
+    for (int s2 = 0; s2 < kStages; ++s2) mbar_init(&full[s2], 1);
+    mbar_init(&abar[0], 1);
+    mbar_init(&abar[1], 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    st.full = full;
+    st.ring = smem + M.ring;
+    st.stage_bytes = M.stage_bytes;
+    st.caddr = caddr;
+    st.cbytes = cbytes;
+    st.cpt = cpt;
+    st.head_first = attn_cta ? cpt : p.head_first;  // the attention CTAs' chunks never belong to a head
+    st.issued = 0u;
+    st.p_step = 0;
+    st.p_chunk = 0;
+    c.p = &ps;
+    c.st = &st;
+    c.chunk_base = 0u;
+    c.rank = rank;
+    c.xv = reinterpret_cast<float*>(smem + M.xv);
+    c.resid = reinterpret_cast<float*>(smem + M.resid);
+    c.loc = reinterpret_cast<float*>(smem + M.loc);
+    c.red = reinterpret_cast<float*>(smem + M.red);
+    c.xl = reinterpret_cast<float*>(smem + M.xl);
+    c.stg = reinterpret_cast<float*>(smem + M.pub);  // this op's output slice before it is published
+    c.rope_s = reinterpret_cast<float*>(smem + M.rope_row);
+    c.seen_s = reinterpret_cast<float*>(smem + M.seen);  // bytes; float* for the 4-byte copies
+    c.act = reinterpret_cast<int8_t*>(smem + M.act);
+    c.xsum = reinterpret_cast<int*>(smem + M.xsum);
+    c.U = smem + M.u;
+    c.abar = abar;
+    c.apar[0] = c.apar[1] = 0u;
+    c.marks = nullptr;
+    c.pos = ldcg_i64(p.position);
+    c.inv_t = 1.0f / __ldcg(p.sampling);
+    c.pen = __ldcg(p.sampling + 1);
+    c.ipen = __ldcg(p.sampling + 2);
+    c.sampling = (p.flags & IVB_RUN_SAMPLE) != 0;
+    const long long kreq = ldcg_i64(p.top_k);
+    const int cap = min(min(D.max_top_k, D.vocab), kMaxTopK);
+    c.K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
+    // candidate layout of this run (uniform across the CTAs): kp slots per GEMV CTA; when they do not
+    // all fit one merge, group leaders first reduce their groups to kq slots each
+    c.kp = cand_slots(c.K, p.ops[p.head_op].op.rows_per);
+    c.n_groups = (R + D.group - 1) / D.group;
+    c.two_level = c.n_groups > 1 && R * c.kp > D.cand_cap;
+    c.kq = (min(c.K, D.group * c.kp) + 1) & ~1;
+    for (int k = 0; k < kStages; ++k) stream_issue(p, &st);
+  }
   cp_async_wait_all();
   __syncthreads();
   unsigned opk = 0;  // ops run so far (selects the descriptor slot)
-  if (tid == 0)
-    for (int k = 0; k < kStages; ++k) stream_issue(p, st, rank);
-  unsigned apar[2] = {0u, 0u};
-  const int first_head = static_cast<int>(rank) * D.hpc;
-  const int nh = max(0, min(D.heads - first_head, D.hpc));
-  long long pos = ldcg_i64(p.position);
-  long long tok = p.feed != nullptr ? ldcg_i64(p.feed) : ldcg_i64(p.token);
-  uint64_t rkey = p.rng[0], rctr = p.rng[1];
-  const float inv_t = 1.0f / __ldcg(p.sampling);
-  const float pen = __ldcg(p.sampling + 1), ipen = __ldcg(p.sampling + 2);
-  const bool sampling = (p.flags & IVB_RUN_SAMPLE) != 0;
-  int K = 1;
-  {
-    const long long kreq = ldcg_i64(p.top_k);
-    const int cap = min(min(D.max_top_k, D.vocab), kMaxTopK);
-    K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
-  }
   bool alive = true;
-  // Ops hand their outputs to the next op through pushed buffers: the consumer arms the buffer's
-  // mbarrier with the bytes of the whole fill (arrive + expect_tx) and waits (bounded); the
-  // producers' st.async stores complete those bytes. No cluster barrier per op: a CTA starts an op as
-  // soon as its input has landed. A CTA is never more than one op ahead of another (every op needs
-  // every CTA's output of the previous one), and every op reads its input buffer before it pushes, so
-  // a fill never overwrites a buffer that is still being read.
-  unsigned xph[XB_COUNT] = {0u, 0u, 0u, 0u};
-  auto wait_fill = [&](int b, unsigned bytes) -> bool {
-    if (tid == 0) mbar_expect_tx(&xbar[b], bytes);
-    const bool late = !mbar_wait_bounded(&xbar[b], xph[b], p.timeout_ns);
-    xph[b] ^= 1u;
-    return !__syncthreads_or(late);
-  };
-  auto fail_here = [&](unsigned code) {
-    if (tid == 0) atomicCAS(p.error, 0u, code);
-  };
-  bool resid_pending = false;  // the last op of the previous token pushed the residual without a head
-  for (int step = 0; step < p.steps && alive; ++step) {
-    if (step > 0 && p.feed != nullptr) tok = ldcg_i64(p.feed + step);
-    if (pos < 0 || pos >= D.max_len || tok < 0 || tok >= D.vocab) {
-      // every CTA sees the same values: stop together
-      if (rank == 0 && tid == 0) atomicCAS(p.error, 0u, static_cast<unsigned>(pos >= D.max_len ? IVB_ECAPACITY : IVB_EINVAL));
-      break;
-    }
-    const bool head = head_needed(p, step);
-    const bool tracing = p.trace != nullptr && step == p.trace_step;
-    if (resid_pending) {
-      resid_pending = false;
-      if (!wait_fill(XB_RESID, static_cast<unsigned>(D.hidden) * 4u)) {
-        fail_here(IVB_ETIMEOUT);
-        break;
+  if (attn_cta) {
+    // ---------------- attention CTA of head h: the attention op of every mla block ----------------
+    const int h = static_cast<int>(rank) - R;
+    for (int step = 0; step < p.steps && alive; ++step) {
+      const long long pos = c.pos;
+      if (pos < 0 || pos >= D.max_len) break;  // GEMV CTA 0 reports it
+      const unsigned flag = epoch0 + static_cast<unsigned>(step) + 1u;
+      const bool tracing = p.trace != nullptr && step == p.trace_step;
+      if (tid == 0) c.flag = flag;
+      for (int mi = 0; mi < p.n_mla && alive; ++mi) {
+        const int oi = p.attn_ops[mi];
+        const Op& op = opbuf[opk & 1].op;
+        const IvbLayerDesc& lay = opbuf[opk & 1].layer;
+        fetch_op(p.attn_ops[mi + 1 < p.n_mla ? mi + 1 : 0], (opk + 1) & 1);
+        if (tid == 0) {
+          c.marks = tracing ? p.trace + (static_cast<size_t>(oi) * (R + D.A) + rank) * 8 : nullptr;
+          for (int k = 0; k < 6; ++k) c.prof[k] = 0;
+          c.prof_t = c.marks != nullptr ? clock64() : 0;
+          mark(c.marks, 0);
+        }
+        // the first tile of cached positions (independent of this token) before the input arrives
+        if (tid == 0 && pos > 0)
+          tile_issue(lay, D, tile_buf(attn_smem(c.U, D).tiles, D, 0), h, 0, min(static_cast<int>(pos), D.tile), &abar[0],
+                     p.error);
+        // the rope row of this position (waited for inside), and the head's q, the latent and the
+        // head's k_rope from the entry op's output [q | latent | k_rope]
+        const float* rrow = lay.rope + static_cast<size_t>(pos) * D.rope;
+        for (int i = tid; i < D.rope; i += kThreads) cp_async_f32(c.rope_s + i, rrow + i);
+        cp_async_commit();
+        const unsigned long long* src = p.ll + op.ll_in;
+        bool ok = ll_gather3(src + h * D.head_dim, D.head_dim, src + D.hidden, D.latent, src + D.hidden + D.latent + h * D.rope,
+                             D.rope, flag, reinterpret_cast<unsigned*>(c.xl), p.timeout_ns);
+        c.tick(5);
+        const unsigned chunk = c.chunk_base + static_cast<unsigned>(mi);
+        if (ok) ok = op_attention(c, op, lay, h, chunk);
+        else c.fail(IVB_ETIMEOUT);
+        if (tid == 0 && c.marks != nullptr) {
+          for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
+          mark(c.marks, 7);
+        }
+        cp_async_wait_all();
+        ++opk;
+        const bool failed = __syncthreads_or(!ok);
+        if (tid == 0) stream_refill(p, &st, chunk + 1);
+        if (failed) alive = false;
       }
-    }
-    // embedding of the token -> residual replica (every CTA computes the whole row)
-    {
-      const uint8_t* erow = p.head.packed + static_cast<size_t>(tok) * p.head.row_bytes;
-      const uint16_t* srow = p.head.scales + static_cast<size_t>(tok) * p.head.scale_stride;
-      for (int i = tid; i < D.hidden; i += kThreads)
-        resid[i] = static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
-    }
-    __syncthreads();
-    const int n_run = head ? p.n_ops : p.n_ops - 1;  // the head is the last op of the program
-    for (int oi = 0; oi < n_run && alive; ++oi) {
-      const Op& op = opbuf[opk & 1].op;  // fields are read from shared memory where used
-      const IvbLayerDesc& lay = opbuf[opk & 1].layer;
-      const int rows_c = rowsbuf[opk & 1][0];
-      fetch_op(oi + 1 < n_run ? oi + 1 : 0, (opk + 1) & 1);  // the op after this one (op 0 of the next token)
-      unsigned long long* marks = tracing ? p.trace + (static_cast<size_t>(oi) * R + rank) * 8 : nullptr;
-      mark(marks, 0);
-      // the input of this op (resid, xv or xl) was pushed into this CTA by every producer of the
-      // previous op before the cluster barrier
-      // tracing: slots 1..6 sum the SM cycles spent in six parts of the op (thread 0's view)
-      long long prof[6] = {0, 0, 0, 0, 0, 0};
-      long long prof_t = marks != nullptr ? clock64() : 0;
-      auto tick = [&](int part) {
-        if (marks != nullptr) {
-          const long long now = clock64();
-          prof[part] += now - prof_t;
-          prof_t = now;
-        }
-      };
-      const int lo = min(op.rows_total, static_cast<int>(rank) * op.rows_per);
-      bool ok = true;
-      if (op.in_buf >= 0 && !wait_fill(op.in_buf, static_cast<unsigned>(op.in_bytes))) {
-        fail_here(IVB_ETIMEOUT);
-        alive = false;
-        break;
-      }
-      if (op.kind == OP_ATTN) {
-        // ---------------- latent attention over the compressed cache ----------------
-        const IvbLayerDesc& L = lay;
-        const unsigned char* cst = stream_acquire(p, st);
-        if (cst == nullptr) ok = false;
-        float* qlat_f = reinterpret_cast<float*>(U);  // [latent] quantiser scratch
-        int8_t* qlc = reinterpret_cast<int8_t*>(U + round16(((D.latent + 63) / 64 * 64) * 4));
-        float* qa = reinterpret_cast<float*>(reinterpret_cast<unsigned char*>(qlc) + round16((D.latent + 63) / 64 * 64));
-        float* qr = qa + D.latent;
-        float* krc = qr + D.rope;
-        float* qn = krc + D.rope;
-        float* sc = qn + D.nope;
-        float* part = sc + D.tile + 4;
-        unsigned char* tiles = reinterpret_cast<unsigned char*>(part + kWarps * D.latent);
-        tiles += (16 - (reinterpret_cast<uintptr_t>(tiles) & 15)) & 15;
-        const float a_cur = quantize_block(xl, D.latent, nullptr, 0.0f, 0.0f, D.act_eps, qlc, false, nullptr, red);
-        if (rank == 0) {
-          for (int j = tid; j < D.latent; j += kThreads) L.latent_q[static_cast<size_t>(pos) * D.lpad + j] = qlc[j];
-          if (tid == 0) L.latent_scale[pos] = a_cur;
-        }
-        const int P = static_cast<int>(pos);
-        const int n_tiles = P == 0 ? 1 : (P + D.tile - 1) / D.tile;
-        tick(0);
-        for (int hl = 0; hl < nh && ok; ++hl) {
-          const int h = first_head + hl;
-          const float* qh = loc + hl * D.head_dim;
-          const float* kh = loc + nh * D.head_dim + hl * D.rope;
-          const float scl = L.attn_scale;
-          for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
-            const float cs = rope_s[2 * jr], sn = rope_s[2 * jr + 1];  // prefetched by the entry op
-            const float q0 = qh[D.nope + 2 * jr], q1 = qh[D.nope + 2 * jr + 1];
-            const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
-            qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
-            qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
-            const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
-            krc[2 * jr] = kr0;
-            krc[2 * jr + 1] = kr1;
-            uint16_t* kc = L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + P) * D.rpad;
-            kc[2 * jr] = f2h(kr0);
-            kc[2 * jr + 1] = f2h(kr1);
-          }
-          for (int e = tid; e < D.nope; e += kThreads) qn[e] = qh[e] * scl;
-          // first tile of this head
-          if (tid == 0 && P > 0) tile_issue(L, D, tile_buf(tiles, D, 0), h, 0, min(P, D.tile), &abar[0]);
-          __syncthreads();
-          // absorbed query qa[j] = sum_e qn[e] * W_knope[h][e][j] (weights in the constants chunk)
-          const unsigned char* wkn = cst + op.c_wkn + static_cast<size_t>(hl) * D.nope * D.rb_lat;
-          const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + op.c_skn) + hl * D.nope * D.ss_lat;
-          const int words = (D.latent + 15) >> 4;  // 16-input words of a latent row
-          if ((words & (words - 1)) == 0) {
-            // thread: word wd of e-group eg; the e-groups of a warp meet by shuffles, the warps in `part`
-            const int wd = tid & (words - 1), eg = tid / words, n_eg = kThreads / words;
-            float acc[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-            for (int e = eg; e < D.nope; e += n_eg) {
-              const unsigned w = *reinterpret_cast<const unsigned*>(wkn + e * D.rb_lat + wd * 4);
-              const float sc_e = h2f(skn[e * D.ss_lat + (wd >> 3)]), q_e = qn[e];
-              float cm1[16];
-              word_codes_m1(w, cm1);
-#pragma unroll
-              for (int i = 0; i < 16; ++i) acc[i] = fmaf(q_e, cm1[i] * sc_e, acc[i]);
-            }
-            for (int off = words; off < 32; off <<= 1)
-#pragma unroll
-              for (int i = 0; i < 16; ++i) acc[i] += __shfl_xor_sync(kFull, acc[i], off);
-            if (lane < words)
-#pragma unroll
-              for (int i = 0; i < 16; ++i)
-                if (wd * 16 + i < D.latent) part[warp * D.latent + wd * 16 + i] = acc[i];
-            __syncthreads();
-            for (int j = tid; j < D.latent; j += kThreads) {
-              float v = part[j];
-#pragma unroll
-              for (int w2 = 1; w2 < kWarps; ++w2) v += part[w2 * D.latent + j];
-              qa[j] = v;
-            }
-          } else {
-            for (int j = tid; j < D.latent; j += kThreads) {
-              float acc = 0.0f;
-              for (int e = 0; e < D.nope; ++e)
-                acc = fmaf(qn[e], code_value(wkn + e * D.rb_lat, j) * h2f(skn[e * D.ss_lat + (j >> 7)]), acc);
-              qa[j] = acc;
-            }
-          }
-          float qb = 0.0f;
-          if (L.k_nope_up.bias != nullptr) {
-            const float* bkn = reinterpret_cast<const float*>(cst + op.c_bkn) + hl * D.nope;
-            float pp = 0.0f;
-            for (int e = tid; e < D.nope; e += kThreads) pp = fmaf(qn[e], bkn[e], pp);
-            qb = block_sum(pp, red);
-          } else {
-            __syncthreads();
-          }
-          // Tiles of cached positions (plus the current one, last): scores with 8 lanes per position
-          // (lane `sub` owns latent pieces p * 128 + sub * 16 .. + 16, the absorbed query slice kept in
-          // registers), an online softmax, and the weighted latent sum u with one warp per position
-          // group (lane owns latent lane * 8 + 256 * p2 .. + 8).
-          tick(1);
-          const int sub = tid & 7, grp = tid >> 3;
-          float qa_r[kAttnPieces][16];
-#pragma unroll
-          for (int pc = 0; pc < kAttnPieces; ++pc)
-#pragma unroll
-            for (int i = 0; i < 16; ++i) {
-              const int j = pc * 128 + sub * 16 + i;
-              qa_r[pc][i] = j < D.latent ? qa[j] : 0.0f;
-            }
-          float u[kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1][8];
-#pragma unroll
-          for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc)
-#pragma unroll
-            for (int i = 0; i < 8; ++i) u[pc][i] = 0.0f;
-          float m_run = -INFINITY, l_run = 0.0f;
-          for (int ti = 0; ti < n_tiles; ++ti) {
-            tick(5);
-            const int start = ti * D.tile;
-            const int count = max(0, min(D.tile, P - start));
-            const bool last = ti == n_tiles - 1;
-            const TileBuf tb = tile_buf(tiles, D, ti & 1);
-            if (tid == 0 && ti + 1 < n_tiles)
-              tile_issue(L, D, tile_buf(tiles, D, (ti + 1) & 1), h, start + D.tile, min(D.tile, P - start - D.tile),
-                         &abar[(ti + 1) & 1]);
-            if (count > 0) {
-              if (!tile_wait(&abar[ti & 1], apar[ti & 1], p.timeout_ns)) {
-                ok = false;
-                break;
-              }
-              apar[ti & 1] ^= 1u;
-            }
-            tick(4);
-            const int npos = count + (last ? 1 : 0);
-            for (int k = grp; k - grp < npos; k += kThreads / 8) {
-              const bool valid = k < npos;
-              const bool cur = k == count;
-              const int8_t* ql = cur ? qlc : tb.lat + (valid ? k : 0) * D.lpad;
-              float dot0 = 0.0f, dot1 = 0.0f;
-#pragma unroll
-              for (int pc = 0; pc < kAttnPieces; ++pc) {
-                const int j0 = pc * 128 + sub * 16;
-                if (valid && j0 < D.latent) {
-                  const uint4 w = *reinterpret_cast<const uint4*>(ql + j0);
-                  float f[16];
-                  bytes_to_f32(w.x, f);
-                  bytes_to_f32(w.y, f + 4);
-                  bytes_to_f32(w.z, f + 8);
-                  bytes_to_f32(w.w, f + 12);
-#pragma unroll
-                  for (int i = 0; i < 16; i += 2) {
-                    dot0 = fmaf(qa_r[pc][i], f[i], dot0);
-                    dot1 = fmaf(qa_r[pc][i + 1], f[i + 1], dot1);
-                  }
-                }
-              }
-              float rp = 0.0f;
-              if (valid)
-                for (int r = sub; r < D.rope; r += 8) rp = fmaf(qr[r], cur ? krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
-              const float at = valid ? (cur ? a_cur : tb.lsc[k]) : 0.0f;
-              float total = fmaf(at, dot0 + dot1, rp);
-              total += __shfl_xor_sync(kFull, total, 4);
-              total += __shfl_xor_sync(kFull, total, 2);
-              total += __shfl_xor_sync(kFull, total, 1);
-              if (valid && sub == 0) sc[k] = total + qb;
-            }
-            __syncthreads();
-            tick(2);
-            float mx = -INFINITY;
-            for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, sc[k]);
-            mx = block_max(mx, red);
-            const float m_new = fmaxf(m_run, mx);
-            const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-            float ls = 0.0f;
-            for (int k = tid; k < npos; k += kThreads) {
-              const float e = expf(sc[k] - m_new);
-              sc[k] = e * (k == count ? a_cur : tb.lsc[k]);  // softmax weight times the latent scale
-              ls += e;
-            }
-            ls = block_sum(ls, red);
-            l_run = l_run * corr + ls;
-#pragma unroll
-            for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) u[pc][i] *= corr;
-            for (int k = warp; k < npos; k += kWarps) {
-              const int8_t* ql = k == count ? qlc : tb.lat + k * D.lpad;
-              const float ea = sc[k];
-#pragma unroll
-              for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc) {
-                const int j0 = pc * 256 + lane * 8;
-                if (j0 < D.latent) {
-                  const uint2 w = *reinterpret_cast<const uint2*>(ql + j0);
-                  float f[8];
-                  bytes_to_f32(w.x, f);
-                  bytes_to_f32(w.y, f + 4);
-#pragma unroll
-                  for (int i = 0; i < 8; ++i) u[pc][i] = fmaf(ea, f[i], u[pc][i]);
-                }
-              }
-            }
-            m_run = m_new;
-            __syncthreads();
-          }
-          if (!ok) break;
-          tick(5);
-#pragma unroll
-          for (int pc = 0; pc < (kAttnPieces / 2 > 0 ? kAttnPieces / 2 : 1); ++pc) {
-            const int j0 = pc * 256 + lane * 8;
-#pragma unroll
-            for (int i = 0; i < 8; ++i)
-              if (j0 + i < D.latent) part[warp * D.latent + j0 + i] = u[pc][i];
-          }
-          __syncthreads();
-          for (int j = tid; j < D.latent; j += kThreads) {
-            float v = part[j];
-#pragma unroll
-            for (int w = 1; w < kWarps; ++w) v += part[w * D.latent + j];
-            qlat_f[j] = v;
-          }
-          __syncthreads();
-          // out_h[e] = W_v[h][e] . u / l + b_v
-          const unsigned char* wv = cst + op.c_wv + static_cast<size_t>(hl) * D.head_dim * D.rb_lat;
-          const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + op.c_sv) + hl * D.head_dim * D.ss_lat;
-          const float* bv = reinterpret_cast<const float*>(cst + op.c_bv) + hl * D.head_dim;
-          const float inv_l = 1.0f / l_run;
-          if ((words & (words - 1)) == 0) {
-            // lanes of a row own its 16-input words (the u slice in registers); rows step by kThreads/words
-            const int wd = tid & (words - 1);
-            float uj[16], cm1[16];
-#pragma unroll
-            for (int i = 0; i < 16; ++i) uj[i] = wd * 16 + i < D.latent ? qlat_f[wd * 16 + i] : 0.0f;
-            for (int e0 = 0; e0 < D.head_dim; e0 += kThreads / words) {
-              const int e = e0 + tid / words;
-              float acc = 0.0f;
-              if (e < D.head_dim) {
-                const unsigned w = *reinterpret_cast<const unsigned*>(wv + e * D.rb_lat + wd * 4);
-                const float sc_e = h2f(sv[e * D.ss_lat + (wd >> 3)]);
-                word_codes_m1(w, cm1);
-#pragma unroll
-                for (int i = 0; i < 16; ++i) acc = fmaf(cm1[i] * sc_e, uj[i], acc);
-              }
-              for (int off = 1; off < words; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
-              if (e < D.head_dim && wd == 0) {
-                float o = acc * inv_l;
-                if (L.v_up.bias != nullptr) o += bv[e];
-                stg[hl * D.head_dim + e] = o;
-              }
-            }
-          } else {
-          int tpr = kThreads / D.head_dim;
-          if (tpr > 32) tpr = 32;
-          int tpr_log = 0;
-          while ((2 << tpr_log) <= tpr) ++tpr_log;
-          tpr = 1 << tpr_log;
-          for (int base = 0; base < D.head_dim; base += kThreads >> tpr_log) {
-            const int e = base + (tid >> tpr_log);
-            const int pid = tid & (tpr - 1);
-            float acc = 0.0f;
-            if (e < D.head_dim) {
-              const unsigned char* row = wv + e * D.rb_lat;
-              const int span = (D.latent + tpr - 1) / tpr;
-              const int j0 = pid * span, j1 = min(D.latent, j0 + span);
-              for (int j = j0; j < j1; ++j) acc = fmaf(code_value(row, j) * h2f(sv[e * D.ss_lat + (j >> 7)]), qlat_f[j], acc);
-            }
-            for (int off = 1; off < tpr; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
-            if (e < D.head_dim && pid == 0) {
-              float o = acc * inv_l;
-              if (L.v_up.bias != nullptr) o += bv[e];
-              stg[hl * D.head_dim + e] = o;
-            }
-          }
-          }
-          __syncthreads();
-          tick(3);
-        }
-        if (ok) push_async(xv, first_head * D.head_dim, stg, nh * D.head_dim, R, &xbar[XB_VEC]);  // stg written before the head loop's last sync
-        asm volatile("fence.proxy.async.global;" ::: "memory");
-        if (!ok) fail_here(IVB_ETIMEOUT);
-        stream_release(p, st, rank);
-      } else {
-        // ---------------- GEMV ops ----------------
-        const unsigned char* cst = nullptr;
-        float act_scale = 0.0f;
-        float* ssmc = reinterpret_cast<float*>(U);
-        const int S = D.state_dim, hd = D.head_dim, taps = D.taps;
-        if (op.kind == OP_ENTRY_MLA) {
-          // the rope row of this position, for the attention op that follows
-          const float* rrow = L_entry_rope(lay) + static_cast<size_t>(pos) * D.rope;
-          for (int i = tid; i < D.rope; i += kThreads) cp_async_f32(rope_s + i, rrow + i);
-          cp_async_commit();
-        } else if (op.kind == OP_HEAD && sampling && ((lo | rows_c) & 3) == 0) {
-          // the repetition flags of my vocabulary slice, for the local top-k
-          const float* src = reinterpret_cast<const float*>(p.seen + lo);
-          for (int i = tid; i < rows_c / 4; i += kThreads) cp_async_f32(seen_s + i, src + i);
-          cp_async_commit();
-        }
-        if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
-          // the recurrent state of my heads streams into shared memory while the rows are computed
-          const IvbLayerDesc& L = lay;
-          const int nhs = nh * S, channels = nh * hd;
-          float* dst = ssmc + ssm_const_floats(nh, S, hd, taps) + 5 * nhs + channels + max(kThreads, channels);
-          const float* src[3] = {L.ssm_state + static_cast<size_t>(first_head) * S * hd * 2,
-                                 L.prev_force + static_cast<size_t>(first_head) * S * hd,
-                                 L.conv_state + static_cast<size_t>(first_head) * hd * (taps - 1)};
-          const int len[3] = {2 * nhs * hd, nhs * hd, channels * (taps - 1)};
-          for (int a2 = 0; a2 < 3; ++a2) {
-            for (int i = tid; i < len[a2]; i += kThreads) cp_async_f32(dst + i, src[a2] + i);
-            dst += len[a2];
-          }
-          cp_async_commit();
-        }
-        if (op.has_const) {
-          cst = stream_acquire(p, st);
-          if (cst == nullptr) ok = false;
-        }
-        tick(0);
-        // quantiser input: the residual replica (entry, gate/up, head) or the pushed vector (out, down)
-        const bool from_resid =
-            op.kind == OP_ENTRY_MAMBA || op.kind == OP_ENTRY_MLA || op.kind == OP_GATE_UP || op.kind == OP_HEAD;
-        const float* norm_w = (op.has_norm && cst != nullptr) ? reinterpret_cast<const float*>(cst + op.c_norm) : nullptr;
-        act_scale = quantize_block(from_resid ? resid : xv, op.in_n, norm_w, op.norm_eps, D.clip, D.act_eps, act, true,
-                                   op_needs_xsum(op) ? xsum : nullptr, red);
-        tick(1);
-        // SSM constants leave the stage before it is recycled
-        if (op.kind == OP_ENTRY_MAMBA && cst != nullptr) {
-          const float* src[5] = {reinterpret_cast<const float*>(cst + op.c_decay), reinterpret_cast<const float*>(cst + op.c_theta),
-                                 reinterpret_cast<const float*>(cst + op.c_skip), reinterpret_cast<const float*>(cst + op.c_convw),
-                                 reinterpret_cast<const float*>(cst + op.c_convb)};
-          const int len[5] = {nh * S, nh * S, nh * hd, nh * hd * taps, nh * hd};
-          int off = 0;
-          for (int a = 0; a < 5; ++a) {
-            for (int i = tid; i < len[a]; i += kThreads) ssmc[off + i] = src[a][i];
-            off += len[a];
-          }
-        }
-        if (op.has_const) stream_release(p, st, rank);
-        // rows of this CTA, chunk by chunk
-        float* rows_out = loc;
-        const int n_row_chunks = op.n_chunks - op.has_const;
-        const int kpl = (((op.in_n + 63) >> 6) + (1 << op.lpr_log) - 1) >> op.lpr_log;
-        const int geo = op.lpr_log * 8 + kpl;
-        bool done_ct = true;
-        if (geo == 3 * 8 + 2) ok &= rows_ct<3, 2, 4>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
-        else if (geo == 4 * 8 + 3) ok &= rows_ct<4, 3, 3>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
-        else if (geo == 5 * 8 + 2) ok &= rows_ct<5, 2, 4>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
-        else if (geo == 5 * 8 + 3) ok &= rows_ct<5, 3, 2>(p, st, rank, op, rows_c, act, act_scale, rows_out, tick);
-        else done_ct = false;
-        for (int c = 0; c < (done_ct ? 0 : n_row_chunks); ++c) {
-          const unsigned char* stage = stream_acquire(p, st);
-          tick(2);
-          if (stage == nullptr) {
-            ok = false;
-          } else {
-            const int r0 = c * op.chunk_rows;
-            const int k = max(0, min(op.chunk_rows, rows_c - r0));
-            chunk_rows(op, stage, k, act, xsum, act_scale, rows_out + r0);
-          }
-          tick(3);
-          stream_release(p, st, rank);
-          tick(4);
-        }
-        // epilogues
-        if (op.kind == OP_OUT || op.kind == OP_DOWN) {
-          for (int r = tid; r < rows_c; r += kThreads) stg[r] = resid[lo + r] + rows_out[r];
-          __syncthreads();
-          push_async(resid, lo, stg, rows_c, R, &xbar[XB_RESID]);
-        } else if (op.kind == OP_GATE_UP) {
-          for (int m = tid; m < rows_c / 2; m += kThreads) stg[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
-          __syncthreads();
-          push_async(xv, lo / 2, stg, rows_c / 2, R, &xbar[XB_VEC]);
-        } else if (op.kind == OP_ENTRY_MLA) {
-          const int lat0 = nh * (D.head_dim + D.rope);
-          const int l0 = static_cast<int>(rank) * op.push_per;  // first latent row of this CTA
-          for (int r = tid; r < rows_c - lat0; r += kThreads) stg[r] = rows_out[lat0 + r];
-          __syncthreads();
-          push_async(xl, l0, stg, rows_c - lat0, R, &xbar[XB_LATENT]);
-        } else if (op.kind == OP_HEAD) {
-          for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
-        } else if (op.kind == OP_ENTRY_MAMBA && nh > 0) {
-          // recurrent step for the channels of my heads; rows_out = per head [value hd | gate hd | bc_dt 3S]
-          const IvbLayerDesc& L = lay;
-          const float* decay = ssmc;
-          const float* theta = decay + nh * S;
-          const float* skip = theta + nh * S;
-          const float* convw = skip + nh * hd;
-          const float* convb = convw + nh * hd * taps;
-          const int channels = nh * hd, nhs = nh * S;
-          float* coef = ssmc + ssm_const_floats(nh, S, hd, taps);  // [5][nh*S]: b, c, half_dt, a_re, a_im
-          float* vals = coef + 5 * nhs;                            // [channels] conv + SiLU values
-          float* cpart = vals + channels;                          // [max(kThreads, channels)] partial readouts
-          const float* s_state = cpart + max(kThreads, channels);  // prefetched [nh][S][hd][2]
-          const float* s_prev = s_state + 2 * nhs * hd;             // [nh][S][hd]
-          const float* s_conv = s_prev + nhs * hd;                  // [channels][taps - 1]
-          cp_async_wait_all();
-          __syncthreads();
-          for (int t = tid; t < nhs; t += kThreads) {
-            const int hl = t / S, s2 = t - hl * S;
-            const float* bcdt = rows_out + hl * (2 * hd + 3 * S) + 2 * hd;
-            const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
-            const float mag = expf(2.0f * half_dt * decay[t]);
-            float sn, cs;
-            sincosf(2.0f * half_dt * theta[t], &sn, &cs);
-            coef[t] = tanhf(bcdt[s2]);
-            coef[nhs + t] = tanhf(bcdt[S + s2]);
-            coef[2 * nhs + t] = half_dt;
-            coef[3 * nhs + t] = mag * cs;
-            coef[4 * nhs + t] = mag * sn;
-          }
-          for (int cl = tid; cl < channels; cl += kThreads) {
-            const int hl = cl / hd, dd = cl - hl * hd;
-            const float* win = s_conv + cl * (taps - 1);
-            float* gwin = L.conv_state + static_cast<size_t>(first_head * hd + cl) * (taps - 1);
-            const float incoming = rows_out[hl * (2 * hd + 3 * S) + dd];
-            float conv = convb[cl];
-            for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
-            conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
-            for (int k2 = 0; k2 + 1 < taps - 1; ++k2) gwin[k2] = win[k2 + 1];
-            if (taps > 1) gwin[taps - 2] = incoming;
-            vals[cl] = silu_f(conv);
-          }
-          __syncthreads();
-          // thread (group g, channel cl) advances states g*spt .. of channel cl; lanes run along the
-          // channels so the state loads and stores are contiguous
-          const int groups = max(1, min(S, kThreads / channels));
-          const int spt = (S + groups - 1) / groups;
-          for (int it = tid; it < groups * channels; it += kThreads) {
-            const int g = it / channels, cl = it - g * channels;
-            const int hl = cl / hd, dd = cl - hl * hd;
-            const float value = vals[cl];
-            float contrib = 0.0f;
-            for (int s2 = g * spt; s2 < min(S, (g + 1) * spt); ++s2) {
-              const int t = hl * S + s2;
-              const int li = t * hd + dd;  // local state index
-              const size_t gi = static_cast<size_t>(first_head * S + t) * hd + dd;
-              const float b = coef[t], cc = coef[nhs + t], half_dt = coef[2 * nhs + t];
-              const float ar = coef[3 * nhs + t], ai = coef[4 * nhs + t];
-              const float prev = s_prev[li];
-              const float sr = s_state[2 * li], si = s_state[2 * li + 1];
-              const float force = b * value;
-              const float dr = (force + ar * prev) * half_dt;
-              const float di = (ai * prev) * half_dt;
-              const float nr = sr * ar - si * ai + dr;
-              const float ni = sr * ai + si * ar + di;
-              reinterpret_cast<float2*>(L.ssm_state)[gi] = make_float2(nr, ni);
-              L.prev_force[gi] = force;
-              contrib = fmaf(cc, nr, contrib);
-            }
-            cpart[it] = contrib;
-          }
-          __syncthreads();
-          for (int cl = tid; cl < channels; cl += kThreads) {
-            const int hl = cl / hd, dd = cl - hl * hd;
-            float contrib = 0.0f;
-            for (int g = 0; g < groups; ++g) contrib += cpart[g * channels + cl];
-            const float y = (contrib + skip[cl] * vals[cl]) * sigmoid_f(rows_out[hl * (2 * hd + 3 * S) + hd + dd]);
-            stg[cl] = y;
-          }
-          __syncthreads();
-          push_async(xv, first_head * hd, stg, channels, R, &xbar[XB_VEC]);
-        }
-        if (!ok) fail_here(IVB_ETIMEOUT);
-        // the head ends the token: local top-k of my vocabulary slice for the sampler
-        if (op.kind == OP_HEAD && sampling) {
-          // head scratch at U: keys [rows_per] | ck, ci, out keys, out ids [kc] | histogram | misc;
-          // the merge arrays that the other CTAs push into start at U + M.cand (disjoint)
-          unsigned* keys = reinterpret_cast<unsigned*>(U);
-          unsigned* ck = keys + op.rows_per;
-          int* ci = reinterpret_cast<int*>(ck + p.kc);
-          unsigned* ok_key = reinterpret_cast<unsigned*>(ci + p.kc);
-          int* ok_id = reinterpret_cast<int*>(ok_key + p.kc);
-          TopkScratch ts{reinterpret_cast<unsigned*>(ok_id + p.kc), reinterpret_cast<int*>(ok_id + p.kc) + kWarps * 256};
-          cp_async_wait_all();
-          __syncthreads();
-          const uint8_t* seen_b = reinterpret_cast<const uint8_t*>(seen_s);
-          const bool pref = ((lo | rows_c) & 3) == 0;
-          for (int r = tid; r < rows_c; r += kThreads)
-            keys[r] = score_key(rows_out[r], pref ? seen_b[r] : __ldcg(p.seen + lo + r), inv_t, pen, ipen);
-          __syncthreads();
-          const int kl = min(K, rows_c);
-          if (kl > 0) topk_sorted(keys, nullptr, lo, rows_c, kl, ts, ck, ci, ok_key, ok_id);
-          __syncthreads();
-          // my candidates go to offset sum_{r < rank} min(K, rows of r) of every CTA's merge arrays
-          int base = 0;
-          for (int r = 0; r < static_cast<int>(rank); ++r)
-            base += min(K, max(0, min(op.rows_total - r * op.rows_per, op.rows_per)));
-          unsigned* mk = reinterpret_cast<unsigned*>(U + M.cand);
-          int* mi = reinterpret_cast<int*>(mk + R * p.kc);
-          for (int idx = tid; idx < kl * R; idx += kThreads) {
-            const int r = idx / kl, c = idx - r * kl;
-            const unsigned bar = map_rank(&xbar[XB_CAND], r);
-            st_async_b32(map_rank(mk + base + c, r), ok_key[c], bar);
-            st_async_b32(map_rank(mi + base + c, r), static_cast<unsigned>(ok_id[c]), bar);
-          }
-        }
-      }
-      tick(5);
-      if (marks != nullptr && tid == 0)
-        for (int k = 0; k < 6; ++k) marks[1 + k] = static_cast<unsigned long long>(prof[k]);
-      mark(marks, 7);
-      cp_async_wait_all();  // the next descriptor has landed
-      push_drain();         // the staging slice has been read by this op's pushes
-      ++opk;
-      __syncthreads();      // local buffers (rows, codes, staging) are reused by the next op
-      if (!ok) {
-        alive = false;
-        break;
-      }
-    }
-    if (!alive) break;
-    if (!head) resid_pending = true;
-    if (sampling) {
-      // every CTA merges the cluster's candidates (pushed into its merge arrays) and draws the same token
-      const int kc = p.kc;
-      const Op& hop = opbuf[(opk + 1) & 1].op;  // the head op just run (the slot before the current one)
-      unsigned* mk = reinterpret_cast<unsigned*>(U + M.cand);
-      int* mi = reinterpret_cast<int*>(mk + R * kc);
-      unsigned* ck = reinterpret_cast<unsigned*>(U);
-      int* ci = reinterpret_cast<int*>(ck + kc);
-      unsigned* sk = reinterpret_cast<unsigned*>(ci + kc);
-      int* si = reinterpret_cast<int*>(sk + kc);
-      float* cdf = reinterpret_cast<float*>(si + kc);
-      TopkScratch ts{reinterpret_cast<unsigned*>(cdf + kc), reinterpret_cast<int*>(cdf + kc) + kWarps * 256};
-      int n = 0;
-      for (int r = 0; r < R; ++r) n += min(K, max(0, min(hop.rows_total - r * hop.rows_per, hop.rows_per)));
-      if (!wait_fill(XB_CAND, static_cast<unsigned>(n) * 8u)) {
-        fail_here(IVB_ETIMEOUT);
-        break;
-      }
-      const int kk = min(K, n);
-      topk_sorted(mk, mi, 0, n, kk, ts, ck, ci, sk, si);
-      const int chosen = draw_token(sk, si, kk, cdf, red, rkey, rctr);
-      ++rctr;
-      tok = chosen;
       if (tid == 0) {
-        const int per = (D.vocab + R - 1) / R;
-        if (chosen / per == static_cast<int>(rank)) p.seen[chosen] = 1;
-        if (rank == 0) {
-          p.token[0] = chosen;
-          p.rng[1] = rctr;
-          if (p.history != nullptr && step < p.history_len) p.history[step] = chosen;
+        c.pos = pos + 1;
+        c.chunk_base += static_cast<unsigned>(p.n_mla);
+      }
+      __syncthreads();
+    }
+  } else {
+    // ---------------- GEMV CTA: every projection op of the token program ----------------
+    for (int step = 0; step < p.steps && alive; ++step) {
+      if (step > 0 && p.feed != nullptr) tok = ldcg_i64(p.feed + step);
+      const long long pos = c.pos;
+      if (pos < 0 || pos >= D.max_len || tok < 0 || tok >= D.vocab) {
+        // every CTA sees the same values: stop together
+        if (rank == 0 && tid == 0) atomicCAS(p.error, 0u, static_cast<unsigned>(pos >= D.max_len ? IVB_ECAPACITY : IVB_EINVAL));
+        break;
+      }
+      const bool head = head_needed(p, step);
+      const bool tracing = p.trace != nullptr && step == p.trace_step;
+      if (tid == 0) c.flag = epoch0 + static_cast<unsigned>(step) + 1u;
+      // embedding of the token -> residual replica (every GEMV CTA computes the whole row)
+      {
+        const uint8_t* erow = p.head.packed + static_cast<size_t>(tok) * p.head.row_bytes;
+        const uint16_t* srow = p.head.scales + static_cast<size_t>(tok) * p.head.scale_stride;
+        float* resid = reinterpret_cast<float*>(smem + M.resid);
+        for (int i = tid; i < D.hidden; i += kThreads)
+          resid[i] = static_cast<float>(((__ldg(erow + (i >> 2)) >> ((i & 3) << 1)) & 3) - 1) * h2f(__ldg(srow + (i >> 7)));
+      }
+      __syncthreads();
+      const int n_run = head ? p.n_ops : p.head_op;  // the head (and the candidate merge) end the program
+      for (int oi = 0; oi < n_run && alive; ++oi) {
+        const Op& op = opbuf[opk & 1].op;  // fields are read from shared memory where used
+        const IvbLayerDesc& lay = opbuf[opk & 1].layer;
+        const int rows_c = rowsbuf[opk & 1][0];
+        fetch_op(oi + 1 < n_run ? oi + 1 : 0, (opk + 1) & 1);  // the op after this one (op 0 of the next token)
+        if (tid == 0) {
+          c.marks = tracing && op.kind != OP_ATTN ? p.trace + (static_cast<size_t>(oi) * (R + D.A) + rank) * 8 : nullptr;
+          for (int k = 0; k < 6; ++k) c.prof[k] = 0;
+          c.prof_t = c.marks != nullptr ? clock64() : 0;
+          mark(c.marks, 0);
+        }
+        bool ok = true;
+        if (op.kind == OP_MERGE) {
+          ok = op_merge(c, op);
+        } else if (op.kind != OP_ATTN) {  // the attention CTAs run the attention ops
+          ok = op_gemv(c, op, lay, rows_c);
+        }
+        c.tick(5);
+        if (tid == 0 && c.marks != nullptr) {
+          for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
+          mark(c.marks, 7);
+        }
+        cp_async_wait_all();  // the next descriptor has landed
+        ++opk;
+        // local buffers (rows, codes, staging) are reused by the next op, and the op's ring stages are free
+        const bool failed = __syncthreads_or(!ok);
+        if (tid == 0) stream_refill(p, &st, c.chunk_base + op.first_chunk + op.n_chunks);
+        if (failed) {
+          alive = false;
+          break;
         }
       }
+      if (!alive) break;
+      if (c.sampling) {
+        const int chosen = draw_next(c, rkey, rctr);
+        if (chosen < 0) break;
+        ++rctr;
+        tok = chosen;
+        if (tid == 0) {
+          // the CTA whose vocabulary slice holds the token sets its flag (it alone reads that slice)
+          const int per = p.ops[p.head_op].op.rows_per;
+          if (chosen / per == static_cast<int>(rank)) p.seen[chosen] = 1;
+          if (rank == 0) {
+            p.token[0] = chosen;
+            p.rng[1] = rctr;
+            if (p.history != nullptr && step < p.history_len) p.history[step] = chosen;
+          }
+        }
+      }
+      if (tid == 0) {
+        c.pos = pos + 1;
+        c.chunk_base += static_cast<unsigned>(chunks_of_step(p, &st, step));
+        if (rank == 0) p.position[0] = pos + 1;
+      }
+      __syncthreads();
     }
-    ++pos;
-    if (rank == 0 && tid == 0) p.position[0] = pos;
+    // every flag of this run is at most epoch0 + steps: the next run starts above it
+    if (rank == 0 && tid == 0) *p.epoch = epoch0 + static_cast<unsigned>(p.steps);
   }
-  // let every in-flight copy land before the CTA's shared memory goes away: a residual fill nobody
-  // consumed (the run stopped after a step without a head), the descriptor prefetch, the ring
-  if (resid_pending) wait_fill(XB_RESID, static_cast<unsigned>(D.hidden) * 4u);
+  // let every in-flight copy land before the CTA's shared memory goes away: the descriptor prefetch,
+  // and the ring (at most the last kStages chunks issued can still be in flight)
   cp_async_wait_all();
-  push_drain();
   if (tid == 0) {
-    while (st.consumed < st.issued) {
-      if (!mbar_wait_bounded(st.full + st.consumed % kStages, (st.consumed / kStages) & 1u, p.timeout_ns)) break;
-      ++st.consumed;
-    }
+    const unsigned issued = st.issued;
+    for (unsigned k = issued > kStages ? issued - kStages : 0u; k < issued; ++k)
+      if (!mbar_wait_bounded(full + k % kStages, (k / kStages) & 1u, p.timeout_ns)) break;
   }
   __syncthreads();
-  cluster_sync();
 }
 
 }  // namespace ivb
 
 // ------------------------------------------------------------------------------------------------
-// host plan: per-CTA weight streams, op program, shared-memory map
+// host plan: per-CTA weight streams, op program, flag-word buffers, shared-memory map
 // ------------------------------------------------------------------------------------------------
 namespace {
 
@@ -857,18 +1175,24 @@ size_t r16(size_t v) { return (v + 15) / 16 * 16; }
 struct IvbDecoder {
   IvbModelDesc desc;
   std::vector<IvbLayerDesc> layers;
-  ivb::ClusterDims d;
-  ivb::ClusterSmem sm;
+  ivb::DecodeDims d;
+  ivb::DecodeSmem sm;
   std::vector<ivb::Op> ops;
   std::vector<ivb::OpRec> recs;  // device op records, kept alive until the upload completes
   std::vector<int32_t> op_rows;
-  std::vector<unsigned long long> chunk_off;
+  std::vector<unsigned long long> chunk_off;  // byte offset into the stream blob, or ~0 for a pointer chunk
+  std::vector<unsigned long long> chunk_ptr;  // device address of a pointer chunk (a shared array read in place)
+  std::vector<unsigned long long> chunk_addr; // device addresses (filled at bind)
   std::vector<unsigned> chunk_bytes;
+  std::vector<unsigned long long> attn_off;   // [A][n_mla] blob offsets of the attention CTAs' chunks
+  std::vector<unsigned long long> attn_addr;  // device addresses (filled at bind)
+  std::vector<unsigned> attn_bytes;
+  std::vector<int32_t> attn_ops;              // indices of the attention ops
   std::vector<CopyOp> copies;
-  int32_t R, cpt, head_first, kc;
-  size_t stream_bytes, smem;
-  size_t off_stream, off_ops, off_op_rows, off_chunk_off, off_chunk_bytes, off_layers, off_cand_key, off_cand_id,
-      off_cand_n, off_sync, total;
+  int32_t R, A, cpt, head_first, head_op, kc;
+  size_t stream_bytes, smem, ll_words;
+  size_t off_stream, off_ops, off_op_rows, off_chunk_addr, off_chunk_bytes, off_attn_addr, off_attn_bytes, off_attn_ops, off_ll,
+      off_sync, total;
   unsigned char* ws;
   unsigned long long* trace;
   int32_t trace_step;
@@ -884,6 +1208,7 @@ static int32_t validate(const IvbModelDesc& d) {
   if (d.state_dim > kMaxStateDim) return fail(IVB_EINVAL, "state_dim %d > %d", d.state_dim, kMaxStateDim);
   if (d.latent_dim > 32 * kMaxLatentPerLane) return fail(IVB_EINVAL, "latent_dim %d > %d", d.latent_dim, 32 * kMaxLatentPerLane);
   if (d.rope_dim + d.nope_dim != d.head_dim || (d.rope_dim & 1)) return fail(IVB_EINVAL, "rope_dim + nope_dim must equal head_dim");
+  if ((d.head_dim & 1) || (d.latent_dim & 1)) return fail(IVB_EINVAL, "head_dim and latent_dim must be even");
   if (d.max_top_k <= 0) return fail(IVB_EINVAL, "max_top_k must be positive");
   if (!d.layers || !d.logits || !d.token || !d.position || !d.seen || !d.sampling || !d.top_k || !d.rng || !d.final_norm)
     return fail(IVB_EINVAL, "null state pointer in the model description");
@@ -936,11 +1261,19 @@ static int32_t validate(const IvbModelDesc& d) {
   return IVB_OK;
 }
 
-// Builds the stream, op program and shared-memory map for a cluster of R CTAs; false if it does not fit.
+// True when every one of R CTAs gets at least one of n rows under the uniform partition ceil(n / R):
+// then the gather of such an op waits for every CTA, which is what lets each op's flag-word buffer be
+// reused every token (no CTA can be a whole token ahead of another one still reading it).
+static bool every_cta_has_rows(int n, int R) {
+  const int per = (n + R - 1) / R;
+  return R <= n && per * (R - 1) < n;
+}
+
+// Builds the stream, op program, flag-word buffers and shared-memory map for R CTAs; false if it does not fit.
 static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   const IvbModelDesc& md = dec->desc;
-  ClusterDims& D = dec->d;
-  D = ClusterDims{};
+  DecodeDims& D = dec->d;
+  D = DecodeDims{};
   D.vocab = md.vocab;
   D.hidden = md.hidden;
   D.heads = md.heads;
@@ -953,7 +1286,6 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   D.max_len = md.max_len;
   D.max_top_k = md.max_top_k;
   D.R = R;
-  D.hpc = (md.heads + R - 1) / R;
   D.taps = 1;
   D.act_eps = md.act_eps;
   D.clip = md.norm_clip;
@@ -969,212 +1301,332 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     }
   }
   const int d = md.hidden, F = md.dense, Lt = md.latent_dim, hd = md.head_dim, S = md.state_dim, H = md.heads;
-  const int hpc = D.hpc;
-  const int dper = (d + R - 1) / R, Fper = (F + R - 1) / R, Lper = (Lt + R - 1) / R, Vper = (md.vocab + R - 1) / R;
-  auto heads_of = [&](int c) { return std::max(0, std::min(H - c * hpc, hpc)); };
+  // every GEMV CTA owns hidden / R recurrent channels inside one head and rows of every hidden/FFN projection
+  if (d % R != 0 || R % H != 0 || !every_cta_has_rows(F, R)) {
+    why = "the CTA count must divide the hidden width, be a multiple of the heads and leave every CTA FFN rows";
+    return false;
+  }
+  if (d > kMaxEPT * kThreads || F > kMaxEPT * kThreads) {
+    why = "hidden and FFN widths above 3072 are not supported by the decode kernel";
+    return false;
+  }
+  D.cpc = d / R;
+  D.A = 0;
+  for (const IvbLayerDesc& L : dec->layers)
+    if (L.kind == IVB_MLA) D.A = H;
+  const int cpc = D.cpc;
+  const int dper = d / R, Fper = (F + R - 1) / R, Vper = (md.vocab + R - 1) / R;
+  const int ent_mla = d + Lt + H * D.rope;  // rows of the mla entry matrix: [q | latent | k_rope]
+  const int Eper = (ent_mla + R - 1) / R;
   auto part = [&](int n, int per, int c) { return std::max(0, std::min(n, (c + 1) * per) - std::min(n, c * per)); };
-  const size_t stage = 36 * 1024;
+  const size_t stage = 20 * 1024;
   dec->kc = std::min(std::min(md.max_top_k, md.vocab), kMaxTopK);
+  if (Vper > kThreads) {
+    why = "more than 256 vocabulary rows per CTA";
+    return false;
+  }
   // ---- op program and per-CTA segments ------------------------------------------------------------
   struct OpPlan {
     Op op;
     std::vector<std::vector<Segment>> segs;  // [R] row segments of each CTA
-    int const_kind;                           // 0 none, 1 norm, 2 mamba (norm + ssm), 3 attention
+    int const_kind;                           // 0 none, 2 mamba (ssm constants), 3 attention
     const float* norm;
     const IvbLayerDesc* layer;
+    int out_words;                            // flag words of the op's output vector
   };
   std::vector<OpPlan> plans;
-  auto gemv_op = [&](int kind, int layer, const IvbTernary& m, int in_n, int rows_per, int rows_total, int gather,
-                     int gather_n, int gather_per, const float* norm, float eps) {
+  auto gemv_op = [&](int kind, int layer, const IvbTernary& m, int in_n, int rows_per, int rows_total, int in_dst,
+                     const float* norm, float eps) {
     OpPlan pl{};
     pl.op.kind = kind;
     pl.op.layer = layer;
-    pl.op.gather = gather;
-    pl.op.gather_n = gather_n;
-    pl.op.gather_per = gather_per;
+    pl.op.in_dst = in_dst;
     pl.op.in_n = in_n;
     pl.op.rows_per = rows_per;
     pl.op.rows_total = rows_total;
-    pl.op.row_bytes = m.row_bytes;
+    // the chunk's row stride: the packed row, plus 16 bytes when it is a multiple of 128 bytes, so the
+    // rows of one warp's 16-byte weight loads fall on different shared-memory banks
+    pl.op.row_bytes = m.row_bytes % 128 == 0 ? m.row_bytes + 16 : m.row_bytes;
     pl.op.scale_stride = ((m.in_features + 127) / 128 + 7) / 8 * 8;
     pl.op.has_bias = m.bias != nullptr;
+    // lanes per row: at most kRowsKPL chunks per lane, then as many lanes as keep the CTA's rows in one
+    // pass of rows_generic (rows x lanes <= 256) without idle lanes (lanes <= chunks)
     const int chunks = (in_n + 63) / 64;
     int lg = 0;
-    while ((1 << lg) < (chunks + 2) / 3 && lg < 5) ++lg;  // at most three chunks per lane when possible
+    while (lg < 5 && ((chunks + (1 << lg) - 1) >> lg) > kRowsKPL) ++lg;
+    while (lg < 5 && (1 << (lg + 1)) <= chunks && (std::max(rows_per, 1) << (lg + 1)) <= kThreads) ++lg;
     pl.op.lpr_log = lg;
     pl.op.has_norm = norm != nullptr;
+    pl.op.has_norm_chunk = norm != nullptr;
     pl.op.norm_eps = eps;
     pl.norm = norm;
-    pl.const_kind = norm != nullptr ? 1 : 0;
+    pl.const_kind = 0;
     pl.segs.assign(R, {});
     return pl;
   };
   for (int li = 0; li < static_cast<int>(dec->layers.size()); ++li) {
     const IvbLayerDesc& L = dec->layers[li];
-    const int gather0 = li == 0 ? G_NONE : G_RESID;
     if (L.kind == IVB_MAMBA) {
-      OpPlan e = gemv_op(OP_ENTRY_MAMBA, li, L.entry, d, hpc * (2 * hd + 3 * S), H * (2 * hd + 3 * S), gather0, d, dper,
-                         L.mixer_norm, L.mixer_norm_eps);
+      // value and gate rows of my channels, then the B, C, dt rows of their head
+      OpPlan e = gemv_op(OP_ENTRY_MAMBA, li, L.entry, d, 2 * cpc + 3 * S, R * (2 * cpc + 3 * S), IN_RESID, L.mixer_norm,
+                         L.mixer_norm_eps);
       e.const_kind = 2;
       e.layer = &L;
-      for (int c = 0; c < R; ++c)
-        for (int hl = 0; hl < heads_of(c); ++hl) {
-          const int h = c * hpc + hl;
-          e.segs[c].push_back({&L.entry, h * hd, hd});
-          e.segs[c].push_back({&L.entry, d + h * hd, hd});
-          e.segs[c].push_back({&L.entry, 2 * d + h * 3 * S, 3 * S});
-        }
+      e.out_words = d;
+      for (int c = 0; c < R; ++c) {
+        const int ch0 = c * cpc, h = ch0 / hd;
+        e.segs[c].push_back({&L.entry, ch0, cpc});
+        e.segs[c].push_back({&L.entry, d + ch0, cpc});
+        e.segs[c].push_back({&L.entry, 2 * d + h * 3 * S, 3 * S});
+      }
       plans.push_back(e);
     } else {
-      OpPlan e = gemv_op(OP_ENTRY_MLA, li, L.entry, d, hpc * (hd + D.rope) + Lper, H * (hd + D.rope) + Lt, gather0, d,
-                         dper, L.mixer_norm, L.mixer_norm_eps);
+      OpPlan e = gemv_op(OP_ENTRY_MLA, li, L.entry, d, Eper, ent_mla, IN_RESID, L.mixer_norm, L.mixer_norm_eps);
       e.layer = &L;
-      e.op.push_per = Lper;
-      for (int c = 0; c < R; ++c) {
-        for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, (c * hpc + hl) * hd, hd});
-        for (int hl = 0; hl < heads_of(c); ++hl) e.segs[c].push_back({&L.entry, d + Lt + (c * hpc + hl) * D.rope, D.rope});
-        const int l0 = std::min(Lt, c * Lper), ln = part(Lt, Lper, c);
-        if (ln > 0) e.segs[c].push_back({&L.entry, d + l0, ln});
-      }
+      e.out_words = ent_mla;
+      for (int c = 0; c < R; ++c)
+        if (part(ent_mla, Eper, c) > 0) e.segs[c].push_back({&L.entry, c * Eper, part(ent_mla, Eper, c)});
       plans.push_back(e);
       OpPlan a{};
       a.op.kind = OP_ATTN;
       a.op.layer = li;
-      a.op.gather = G_LATENT;
-      a.op.gather_n = Lt;
-      a.op.gather_per = Lper;
+      a.op.in_dst = IN_LATENT;
       a.op.in_n = Lt;
-      a.op.rows_per = hpc * hd;
-      a.op.rows_total = d;
-      a.op.lpr_log = 0;
+      a.op.rows_per = 0;
+      a.op.rows_total = 0;
       a.const_kind = 3;
       a.layer = &L;
+      a.out_words = d;  // the heads' outputs, written by the attention CTAs
       a.segs.assign(R, {});
       plans.push_back(a);
     }
-    const int ygather_per = hpc * hd;
-    OpPlan o = gemv_op(OP_OUT, li, L.out, d, dper, d, G_VEC, d, ygather_per, nullptr, 0.0f);
-    for (int c = 0; c < R; ++c)
-      if (part(d, dper, c) > 0) o.segs[c].push_back({&L.out, c * dper, part(d, dper, c)});
+    OpPlan o = gemv_op(OP_OUT, li, L.out, d, dper, d, IN_VEC, nullptr, 0.0f);
+    o.out_words = d;
+    for (int c = 0; c < R; ++c) o.segs[c].push_back({&L.out, c * dper, dper});
     plans.push_back(o);
-    OpPlan g = gemv_op(OP_GATE_UP, li, L.gate_up, d, 2 * Fper, 2 * F, G_RESID, d, dper, L.ffn_norm, L.ffn_norm_eps);
+    OpPlan g = gemv_op(OP_GATE_UP, li, L.gate_up, d, 2 * Fper, 2 * F, IN_RESID, L.ffn_norm, L.ffn_norm_eps);
+    g.out_words = F;
     for (int c = 0; c < R; ++c)
       if (part(F, Fper, c) > 0) g.segs[c].push_back({&L.gate_up, 2 * c * Fper, 2 * part(F, Fper, c)});
     plans.push_back(g);
-    OpPlan dn = gemv_op(OP_DOWN, li, L.down, F, dper, d, G_VEC, F, Fper, nullptr, 0.0f);
-    for (int c = 0; c < R; ++c)
-      if (part(d, dper, c) > 0) dn.segs[c].push_back({&L.down, c * dper, part(d, dper, c)});
+    OpPlan dn = gemv_op(OP_DOWN, li, L.down, F, dper, d, IN_VEC, nullptr, 0.0f);
+    dn.out_words = d;
+    for (int c = 0; c < R; ++c) dn.segs[c].push_back({&L.down, c * dper, dper});
     plans.push_back(dn);
   }
+  const int kp_max = (std::min(dec->kc, std::max(Vper, 1)) + 1) & ~1;  // candidate slots per CTA (cand_slots)
   {
-    OpPlan hp = gemv_op(OP_HEAD, -1, md.head, d, Vper, md.vocab, G_RESID, d, dper, md.final_norm, md.final_norm_eps);
+    OpPlan hp = gemv_op(OP_HEAD, -1, md.head, d, Vper, md.vocab, IN_RESID, md.final_norm, md.final_norm_eps);
+    hp.out_words = 2 * R * kp_max;
     for (int c = 0; c < R; ++c)
       if (part(md.vocab, Vper, c) > 0) hp.segs[c].push_back({&md.head, c * Vper, part(md.vocab, Vper, c)});
     plans.push_back(hp);
+    OpPlan mg{};
+    mg.op.kind = OP_MERGE;
+    mg.op.layer = -1;
+    mg.op.in_dst = IN_CAND;
+    mg.const_kind = 0;
+    mg.out_words = 0;  // set with the group size below
+    mg.segs.assign(R, {});
+    plans.push_back(mg);
   }
   // ---- constants-chunk layouts (identical offsets for every CTA) ----------------------------------
+  // The norm weights are their own chunk, read in place from the model's array when it is 16-byte
+  // aligned (one shared copy for all CTAs instead of one per CTA); the per-CTA constants of the
+  // recurrent step (its head's decay/theta, its channels' skip and conv) and of the attention (its
+  // head's up-projection rows) live in a constants chunk of the stream.
+  const bool norm_in_place = (d * 4) % 16 == 0;
   size_t max_const = 16;
   for (OpPlan& pl : plans) {
     Op& op = pl.op;
     size_t off = 0;
-    if (pl.const_kind == 1 || pl.const_kind == 2) {
-      op.c_norm = static_cast<int>(off);
-      off += r16(static_cast<size_t>(d) * 4);
-    }
     if (pl.const_kind == 2) {
       op.c_decay = static_cast<int>(off);
-      off += r16(hpc * S * 4);
+      off += r16(S * 4);
       op.c_theta = static_cast<int>(off);
-      off += r16(hpc * S * 4);
+      off += r16(S * 4);
       op.c_skip = static_cast<int>(off);
-      off += r16(hpc * hd * 4);
+      off += r16(cpc * 4);
       op.c_convw = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hpc) * hd * D.taps * 4);
+      off += r16(static_cast<size_t>(cpc) * D.taps * 4);
       op.c_convb = static_cast<int>(off);
-      off += r16(hpc * hd * 4);
+      off += r16(cpc * 4);
     }
     if (pl.const_kind == 3) {
       op.c_wkn = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hpc) * D.nope * D.rb_lat);
+      off += r16(static_cast<size_t>(D.nope) * D.rb_lat);
       op.c_skn = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hpc) * D.nope * D.ss_lat * 2);
+      off += r16(static_cast<size_t>(D.nope) * D.ss_lat * 2);
       op.c_bkn = static_cast<int>(off);
-      off += r16(hpc * D.nope * 4);
+      off += r16(D.nope * 4);
       op.c_wv = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hpc) * hd * D.rb_lat);
+      off += r16(static_cast<size_t>(hd) * D.rb_lat);
       op.c_sv = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hpc) * hd * D.ss_lat * 2);
+      off += r16(static_cast<size_t>(hd) * D.ss_lat * 2);
       op.c_bv = static_cast<int>(off);
-      off += r16(hpc * hd * 4);
+      off += r16(hd * 4);
     }
     op.has_const = pl.const_kind != 0;
     max_const = std::max(max_const, off);
+    if (op.has_norm_chunk) max_const = std::max(max_const, r16(static_cast<size_t>(d) * 4));
     pl.op.n_chunks = 0;
   }
   if (max_const > stage) {
     why = "a constants chunk does not fit a stream stage";
     return false;
   }
-  // ---- chunk the rows, lay out every CTA's stream ---------------------------------------------------
+  // ---- chunk the rows ---------------------------------------------------------------------------
   for (OpPlan& pl : plans) {
     Op& op = pl.op;
-    if (op.kind == OP_ATTN) {
+    if (op.kind == OP_ATTN) {  // its constants chunk is in the attention CTAs' own streams
       op.chunk_rows = 0;
-      op.n_chunks = 1;
+      op.n_chunks = 0;
+      op.has_const = 0;
+      continue;
+    }
+    if (op.kind == OP_MERGE) {
+      op.chunk_rows = 0;
+      op.n_chunks = 0;
       continue;
     }
     const size_t per_row = op.row_bytes + op.scale_stride * 2 + 4;
     int cr = static_cast<int>((stage - 64) / per_row);
-    const int rpi = kThreads >> op.lpr_log;  // rows one thread-row of chunk_rows covers
+    const int rpi = kThreads >> op.lpr_log;  // rows one pass of rows_generic covers
     if (cr >= rpi) cr = cr / rpi * rpi;
     if (op.kind == OP_GATE_UP) cr &= ~1;
     cr = std::max(2, std::min(cr, std::max(2, op.rows_per)));
     op.chunk_rows = cr;
-    op.n_chunks = op.has_const + (op.rows_per + cr - 1) / cr;
+    op.n_chunks = op.has_norm_chunk + op.has_const + (op.rows_per + cr - 1) / cr;
   }
+  // ---- shared memory map ----------------------------------------------------------------------------
+  DecodeSmem& M = dec->sm;
+  size_t o = 0;
+  M.ring = 0;
+  M.stage_bytes = static_cast<int>(stage);
+  o += kStages * stage;
+  const int max_in = std::max(d, F);
+  const int pad_in = (max_in + 63) / 64 * 64;
+  M.xv = static_cast<int>(o);
+  o += r16(static_cast<size_t>(pad_in) * 4);
+  M.act = static_cast<int>(o);
+  o += r16(pad_in);
+  M.xsum = static_cast<int>(o);
+  o += r16(pad_in / 64 * 4);
+  M.resid = static_cast<int>(o);
+  o += r16(static_cast<size_t>(d) * 4);
+  int pub_n = std::max(std::max(cpc, hd + 2), std::max(dper, Fper));
+  M.pub_n = pub_n;
+  M.pub = static_cast<int>(o);
+  o += r16(static_cast<size_t>(pub_n) * 4);  // staging of the op's output slice
+  int loc_n = 0;
+  for (const OpPlan& pl : plans) loc_n = std::max(loc_n, pl.op.rows_per);
+  M.loc = static_cast<int>(o);
+  o += r16(static_cast<size_t>(loc_n) * 4);
+  M.red = static_cast<int>(o);
+  o += r16(64 * 4);
+  M.xl = static_cast<int>(o);
+  o += r16(static_cast<size_t>((hd + Lt + D.rope + 63) / 64 * 64) * 4);
+  int cpt = 0;
+  for (const OpPlan& pl : plans) cpt += pl.op.n_chunks;
+  M.ctab = static_cast<int>(o);
+  o += r16(static_cast<size_t>(cpt) * 8) + r16(static_cast<size_t>(cpt) * 4);
+  M.rope_row = static_cast<int>(o);
+  o += r16(static_cast<size_t>(std::max(md.rope_dim, 1)) * 4);
+  M.seen = static_cast<int>(o);
+  o += r16(static_cast<size_t>(Vper));
+  M.u = static_cast<int>(o);
+  if (o >= smem_cap) {
+    why = "the decoder's fixed shared-memory regions exceed a CTA's shared memory";
+    return false;
+  }
+  const int kc = dec->kc;
+  const size_t room = smem_cap - o;  // for the union region
+  // recurrent op: constants, scratch and prefetched state of the CTA's channels
+  size_t u_need = r16(static_cast<size_t>(ssm_smem_floats(cpc, S, D.taps)) * 4);
+  // head: keys [256] and its candidates [kc]; merges: scratch, then the gathered candidate arrays
+  const size_t head_scratch = static_cast<size_t>(kThreads) * 4 + 2 * static_cast<size_t>(kc) * 4;
+  const size_t merge_scratch = 5 * static_cast<size_t>(kc) * 4 + kWarps * 256 * 4 + 16 * 4;
+  M.cand = static_cast<int>(r16(std::max(head_scratch, merge_scratch)));
+  if (static_cast<size_t>(M.cand) + 16 * 8 > room) {
+    why = "no room for the sampler's candidates in shared memory";
+    return false;
+  }
+  // candidates one merge can hold: all of them when they fit, else groups of CTAs whose leaders merge first
+  const size_t cap_c = std::min<size_t>((room - M.cand) / 8, static_cast<size_t>(R) * kp_max);
+  D.cand_cap = static_cast<int>(cap_c);
+  D.group = R;
+  if (static_cast<size_t>(R) * kp_max > cap_c) {
+    int g = static_cast<int>(cap_c / kp_max);
+    for (; g >= 1; --g) {
+      const int ng = (R + g - 1) / g;
+      const int kq = (std::min(kc, g * kp_max) + 1) & ~1;
+      if (static_cast<size_t>(ng) * kq <= cap_c) break;
+    }
+    if (g < 1) {
+      why = "the sampler's candidate merge does not fit shared memory";
+      return false;
+    }
+    D.group = g;
+  }
+  {
+    const int ng = (R + D.group - 1) / D.group;
+    const int kq = (std::min(kc, D.group * kp_max) + 1) & ~1;
+    plans.back().out_words = 2 * ng * kq;
+  }
+  u_need = std::max(u_need, static_cast<size_t>(M.cand) + r16(cap_c * 8));
+  const size_t per_pos = static_cast<size_t>(D.lpad) + 4 + static_cast<size_t>(D.rpad) * 2;
+  bool any_mla = false;
+  for (const IvbLayerDesc& L : dec->layers) any_mla |= L.kind == IVB_MLA;
+  int tile = 0;
+  if (any_mla) {
+    const size_t fixed = attn_fixed_bytes(Lt, D.rope, D.nope, 0);
+    const size_t troom = room > fixed ? room - fixed : 0;
+    tile = static_cast<int>(troom / (2 * per_pos + 8)) / 16 * 16;
+    tile = std::min(tile, (md.max_len + 15) / 16 * 16);
+    if (tile < 16) {
+      why = "no room for an attention tile in shared memory";
+      return false;
+    }
+    tile = std::min(tile, 256);
+    u_need = std::max(u_need, attn_fixed_bytes(Lt, D.rope, D.nope, tile) + 2 * (r16(static_cast<size_t>(tile) * D.lpad) +
+                                                                                 r16(tile * 4) + r16(static_cast<size_t>(tile) * D.rpad * 2)));
+  }
+  D.tile = std::max(tile, 16);
+  o += r16(u_need);
+  M.total = static_cast<int>(o);
+  if (o > smem_cap) {
+    why = "the decoder needs more shared memory than a CTA has";
+    return false;
+  }
+  dec->smem = o;
+  // ---- op records: chunks, flag-word buffers ---------------------------------------------------------
   dec->ops.clear();
   dec->op_rows.assign(plans.size() * R, 0);
-  int cpt = 0;
+  cpt = 0;
+  size_t llw = 0;
   for (size_t i = 0; i < plans.size(); ++i) {
-    plans[i].op.first_chunk = cpt;
-    cpt += plans[i].op.n_chunks;
-    // the buffer this op waits for (filled by the previous op's pushes) and the bytes of that fill
     Op& op = plans[i].op;
-    op.in_buf = XB_NONE;
-    op.in_bytes = 0;
-    switch (op.kind) {
-      case OP_ENTRY_MAMBA:
-      case OP_ENTRY_MLA:
-        if (op.layer > 0) {
-          op.in_buf = XB_RESID;
-          op.in_bytes = d * 4;
-        }
-        break;
-      case OP_GATE_UP:
-      case OP_HEAD:
-        op.in_buf = XB_RESID;
-        op.in_bytes = d * 4;
-        break;
-      case OP_ATTN:
-        op.in_buf = XB_LATENT;
-        op.in_bytes = Lt * 4;
-        break;
-      case OP_OUT:
-        op.in_buf = XB_VEC;
-        op.in_bytes = H * hd * 4;
-        break;
-      case OP_DOWN:
-        op.in_buf = XB_VEC;
-        op.in_bytes = F * 4;
-        break;
-      default:
-        break;
+    op.first_chunk = cpt;
+    cpt += op.n_chunks;
+    op.ll_out = static_cast<int32_t>(llw);
+    llw += (static_cast<size_t>(plans[i].out_words) + 15) / 16 * 16;  // whole 128-byte lines per buffer
+    const bool first_entry = (op.kind == OP_ENTRY_MAMBA || op.kind == OP_ENTRY_MLA) && op.layer == 0;
+    if (i == 0 || first_entry) {
+      op.ll_in = -1;
+      op.ll_in_words = 0;
+    } else {
+      op.ll_in = plans[i - 1].op.ll_out;
+      op.ll_in_words = plans[i - 1].out_words;
     }
+    if (op.kind == OP_HEAD) dec->head_op = static_cast<int32_t>(i);
     dec->ops.push_back(op);
   }
+  dec->ll_words = llw;
   dec->cpt = cpt;
-  dec->head_first = plans.back().op.first_chunk;
+  dec->head_first = plans[dec->head_op].op.first_chunk;
+  // ---- every CTA's stream ---------------------------------------------------------------------------
   dec->chunk_off.assign(static_cast<size_t>(R) * cpt, 0);
+  dec->chunk_ptr.assign(static_cast<size_t>(R) * cpt, 0);
   dec->chunk_bytes.assign(static_cast<size_t>(R) * cpt, 0);
   dec->copies.clear();
   size_t cursor = 0;
@@ -1189,53 +1641,41 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
       const Op& op = pl.op;
       int rows_c = 0;
       for (const Segment& sg : pl.segs[c]) rows_c += sg.count;
-      if (op.kind == OP_ATTN) rows_c = heads_of(c) * hd;
       dec->op_rows[i * R + c] = rows_c;
+      if (op.has_norm_chunk) {
+        const size_t nb = r16(static_cast<size_t>(d) * 4);
+        if (norm_in_place && (reinterpret_cast<uintptr_t>(pl.norm) & 15) == 0) {
+          dec->chunk_off[static_cast<size_t>(c) * cpt + ci] = ~0ull;
+          dec->chunk_ptr[static_cast<size_t>(c) * cpt + ci] = reinterpret_cast<uintptr_t>(pl.norm);
+        } else {
+          add(cursor, pl.norm, static_cast<size_t>(d) * 4, 1, 0, 0);
+          dec->chunk_off[static_cast<size_t>(c) * cpt + ci] = cursor;
+          cursor = r16(cursor + nb);
+        }
+        dec->chunk_bytes[static_cast<size_t>(c) * cpt + ci] = static_cast<unsigned>(nb);
+        ++ci;
+      }
       if (op.has_const) {
         const size_t base = cursor;
         size_t bytes = 16;
-        if (pl.const_kind == 1 || pl.const_kind == 2) {
-          add(base + op.c_norm, pl.norm, static_cast<size_t>(d) * 4, 1, 0, 0);
-          bytes = std::max(bytes, static_cast<size_t>(op.c_norm) + r16(static_cast<size_t>(d) * 4));
-        }
         if (pl.const_kind == 2) {
           const IvbLayerDesc& L = *pl.layer;
-          const int nh = heads_of(c), h0 = c * hpc;
-          if (nh > 0) {
-            add(base + op.c_decay, L.decay + h0 * S, nh * S * 4, 1, 0, 0);
-            add(base + op.c_theta, L.theta + h0 * S, nh * S * 4, 1, 0, 0);
-            add(base + op.c_skip, L.skip + h0 * hd, nh * hd * 4, 1, 0, 0);
-            add(base + op.c_convw, L.conv_weight + static_cast<size_t>(h0) * hd * D.taps, static_cast<size_t>(nh) * hd * D.taps * 4, 1, 0, 0);
-            add(base + op.c_convb, L.conv_bias + h0 * hd, nh * hd * 4, 1, 0, 0);
-          }
-          bytes = std::max(bytes, static_cast<size_t>(op.c_convb) + r16(hpc * hd * 4));
-        }
-        if (pl.const_kind == 3) {
-          const IvbLayerDesc& L = *pl.layer;
-          const int nh = heads_of(c), h0 = c * hpc;
-          const IvbTernary& kn = L.k_nope_up;
-          const IvbTernary& vu = L.v_up;
-          const size_t sgroups = static_cast<size_t>((Lt + 127) / 128) * 2;
-          if (nh > 0) {
-            add(base + op.c_wkn, kn.packed + static_cast<size_t>(h0) * D.nope * kn.row_bytes, D.rb_lat, nh * D.nope, kn.row_bytes, D.rb_lat);
-            add(base + op.c_skn, kn.scales + static_cast<size_t>(h0) * D.nope * kn.scale_stride, sgroups, nh * D.nope,
-                static_cast<size_t>(kn.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
-            add(base + op.c_bkn, kn.bias ? static_cast<const void*>(kn.bias + h0 * D.nope) : nullptr, nh * D.nope * 4, 1, 0, 0);
-            add(base + op.c_wv, vu.packed + static_cast<size_t>(h0) * hd * vu.row_bytes, D.rb_lat, nh * hd, vu.row_bytes, D.rb_lat);
-            add(base + op.c_sv, vu.scales + static_cast<size_t>(h0) * hd * vu.scale_stride, sgroups, nh * hd,
-                static_cast<size_t>(vu.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
-            add(base + op.c_bv, vu.bias ? static_cast<const void*>(vu.bias + h0 * hd) : nullptr, nh * hd * 4, 1, 0, 0);
-          }
-          bytes = std::max(bytes, static_cast<size_t>(op.c_bv) + r16(hpc * hd * 4));
+          const int ch0 = c * cpc, h = ch0 / hd;
+          add(base + op.c_decay, L.decay + h * S, S * 4, 1, 0, 0);
+          add(base + op.c_theta, L.theta + h * S, S * 4, 1, 0, 0);
+          add(base + op.c_skip, L.skip + ch0, cpc * 4, 1, 0, 0);
+          add(base + op.c_convw, L.conv_weight + static_cast<size_t>(ch0) * D.taps, static_cast<size_t>(cpc) * D.taps * 4, 1, 0, 0);
+          add(base + op.c_convb, L.conv_bias + ch0, cpc * 4, 1, 0, 0);
+          bytes = std::max(bytes, static_cast<size_t>(op.c_convb) + r16(cpc * 4));
         }
         dec->chunk_off[static_cast<size_t>(c) * cpt + ci] = base;
         dec->chunk_bytes[static_cast<size_t>(c) * cpt + ci] = static_cast<unsigned>(r16(bytes));
         cursor = r16(base + bytes);
         ++ci;
       }
-      if (op.kind == OP_ATTN) continue;
+      if (op.kind == OP_ATTN || op.kind == OP_MERGE) continue;
       // row chunks: [k x row_bytes][k x scale_stride fp16, 16B pad][k x fp32 bias, 16B pad]
-      const int n_row_chunks = op.n_chunks - op.has_const;
+      const int n_row_chunks = op.n_chunks - op.has_const - op.has_norm_chunk;
       for (int rc = 0; rc < n_row_chunks; ++rc) {
         const int r0 = rc * op.chunk_rows;
         const int k = std::max(0, std::min(op.chunk_rows, rows_c - r0));
@@ -1252,7 +1692,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
             const int n = b - a;
             const IvbTernary& m = *sg.m;
             const size_t dr = static_cast<size_t>(a - r0);
-            add(base + dr * op.row_bytes, m.packed + static_cast<size_t>(src_row) * m.row_bytes, op.row_bytes, n, m.row_bytes,
+            add(base + dr * op.row_bytes, m.packed + static_cast<size_t>(src_row) * m.row_bytes, m.row_bytes, n, m.row_bytes,
                 op.row_bytes);
             add(base + sc_off + dr * op.scale_stride * 2, m.scales + static_cast<size_t>(src_row) * m.scale_stride,
                 static_cast<size_t>((m.in_features + 127) / 128) * 2, n, static_cast<size_t>(m.scale_stride) * 2,
@@ -1268,78 +1708,73 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
       }
     }
   }
+  // the attention CTAs' streams: per head, one constants chunk per attention op (the head's k_nope and
+  // v up-projection rows, scales and biases)
+  dec->attn_ops.clear();
+  for (size_t i = 0; i < plans.size(); ++i)
+    if (plans[i].op.kind == OP_ATTN) dec->attn_ops.push_back(static_cast<int32_t>(i));
+  const int n_mla = static_cast<int>(dec->attn_ops.size());
+  dec->A = n_mla > 0 ? H : 0;
+  dec->attn_off.assign(static_cast<size_t>(dec->A) * n_mla, 0);
+  dec->attn_bytes.assign(static_cast<size_t>(dec->A) * n_mla, 16);
+  for (int h = 0; h < dec->A; ++h)
+    for (int mi = 0; mi < n_mla; ++mi) {
+      const OpPlan& pl = plans[dec->attn_ops[mi]];
+      const Op& op = pl.op;
+      const IvbLayerDesc& L = *pl.layer;
+      const IvbTernary& kn = L.k_nope_up;
+      const IvbTernary& vu = L.v_up;
+      const size_t sgroups = static_cast<size_t>((Lt + 127) / 128) * 2;
+      const size_t base = cursor;
+      add(base + op.c_wkn, kn.packed + static_cast<size_t>(h) * D.nope * kn.row_bytes, D.rb_lat, D.nope, kn.row_bytes, D.rb_lat);
+      add(base + op.c_skn, kn.scales + static_cast<size_t>(h) * D.nope * kn.scale_stride, sgroups, D.nope,
+          static_cast<size_t>(kn.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
+      add(base + op.c_bkn, kn.bias ? static_cast<const void*>(kn.bias + h * D.nope) : nullptr, D.nope * 4, 1, 0, 0);
+      add(base + op.c_wv, vu.packed + static_cast<size_t>(h) * hd * vu.row_bytes, D.rb_lat, hd, vu.row_bytes, D.rb_lat);
+      add(base + op.c_sv, vu.scales + static_cast<size_t>(h) * hd * vu.scale_stride, sgroups, hd,
+          static_cast<size_t>(vu.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
+      add(base + op.c_bv, vu.bias ? static_cast<const void*>(vu.bias + h * hd) : nullptr, hd * 4, 1, 0, 0);
+      const size_t bytes = r16(static_cast<size_t>(op.c_bv) + r16(hd * 4));
+      dec->attn_off[static_cast<size_t>(h) * n_mla + mi] = base;
+      dec->attn_bytes[static_cast<size_t>(h) * n_mla + mi] = static_cast<unsigned>(bytes);
+      cursor = r16(base + bytes);
+    }
   dec->stream_bytes = r16(cursor) + 256;
-  // ---- shared memory map ----------------------------------------------------------------------------
-  ClusterSmem& M = dec->sm;
-  size_t o = 0;
-  M.ring = 0;
-  M.stage_bytes = static_cast<int>(stage);
-  o += kStages * stage;
-  const int max_in = std::max(d, F);
-  const int pad_in = (max_in + 63) / 64 * 64;
-  M.xv = static_cast<int>(o);
-  o += r16(static_cast<size_t>(pad_in) * 4);
-  M.act = static_cast<int>(o);
-  o += r16(pad_in);
-  M.xsum = static_cast<int>(o);
-  o += r16(pad_in / 64 * 4);
-  M.resid = static_cast<int>(o);
-  o += r16(static_cast<size_t>(d) * 4);
-  int pub_n = std::max(std::max(hpc * hd, Lper), std::max(dper, Fper));
-  M.pub_n = pub_n;
-  M.pub = static_cast<int>(o);
-  o += r16(static_cast<size_t>(pub_n) * 4);  // staging of the op's output slice
-  int loc_n = 0;
-  for (const Op& op : dec->ops) loc_n = std::max(loc_n, op.kind == OP_ATTN ? 0 : op.rows_per);
-  M.loc = static_cast<int>(o);
-  o += r16(static_cast<size_t>(loc_n) * 4);
-  M.red = static_cast<int>(o);
-  o += r16(64 * 4);
-  M.xl = static_cast<int>(o);
-  o += r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4);
-  M.ctab = static_cast<int>(o);
-  o += r16(static_cast<size_t>(dec->cpt) * 8) + r16(static_cast<size_t>(dec->cpt) * 4);
-  M.rope_row = static_cast<int>(o);
-  o += r16(static_cast<size_t>(std::max(md.rope_dim, 1)) * 4);
-  M.seen = static_cast<int>(o);
-  o += r16(static_cast<size_t>(Vper));
-  M.u = static_cast<int>(o);
-  const int kc = dec->kc;
-  // recurrent op: constants, coefficients, values, partial readouts, prefetched state
-  size_t u_need = r16((static_cast<size_t>(ssm_const_floats(hpc, S, hd, D.taps)) + 5 * hpc * S + hpc * hd + std::max(kThreads, hpc * hd) +
-                       3 * static_cast<size_t>(hpc) * S * hd + static_cast<size_t>(hpc) * hd * (D.taps - 1)) * 4);
-  // head + sampler: the head's top-k scratch (or the merge scratch) first, then the merge arrays that
-  // the other CTAs push their candidates into
-  const size_t head_scratch = static_cast<size_t>(Vper) * 4 + 4 * static_cast<size_t>(kc) * 4 + kWarps * 256 * 4 + 16 * 4;
-  const size_t merge_scratch = 5 * static_cast<size_t>(kc) * 4 + kWarps * 256 * 4 + 16 * 4;
-  M.cand = static_cast<int>(r16(std::max(head_scratch, merge_scratch)));
-  u_need = std::max(u_need, static_cast<size_t>(M.cand) + 2 * r16(static_cast<size_t>(R) * kc * 4));
-  const size_t attn_fixed = r16(static_cast<size_t>((Lt + 63) / 64 * 64) * 4) + r16((Lt + 63) / 64 * 64) +
-                            static_cast<size_t>(Lt + 2 * D.rope + D.nope) * 4 + kWarps * Lt * 4 + 64;
-  const size_t per_pos = static_cast<size_t>(D.lpad) + 4 + static_cast<size_t>(D.rpad) * 2;
-  bool any_mla = false;
-  for (const IvbLayerDesc& L : dec->layers) any_mla |= L.kind == IVB_MLA;
-  int tile = 0;
-  if (any_mla) {
-    const size_t room = smem_cap > o + attn_fixed ? smem_cap - o - attn_fixed : 0;
-    tile = static_cast<int>(room / (2 * per_pos + 8)) / 16 * 16;
-    tile = std::min(tile, (md.max_len + 15) / 16 * 16);
-    if (tile < 16) {
-      why = "no room for an attention tile in shared memory";
+  // ---- consistency of the plan (checked here so that a planning error is an error code, not a fault) --
+  for (size_t i = 0; i < dec->attn_bytes.size(); ++i)
+    if (dec->attn_bytes[i] > stage || dec->attn_off[i] + dec->attn_bytes[i] > dec->stream_bytes) {
+      why = "an attention constants chunk does not fit a ring stage";
       return false;
     }
-    tile = std::min(tile, 512);
-    u_need = std::max(u_need, attn_fixed + static_cast<size_t>(tile) * 4 + 64 + 2 * (r16(static_cast<size_t>(tile) * D.lpad) +
-                                                                                  r16(tile * 4) + r16(static_cast<size_t>(tile) * D.rpad * 2)));
+  for (size_t i = 0; i < dec->chunk_bytes.size(); ++i) {
+    const unsigned b = dec->chunk_bytes[i];
+    if (b == 0 || b > stage || (b & 15) != 0) {
+      why = "a stream chunk does not fit a ring stage";
+      return false;
+    }
+    if (dec->chunk_off[i] != ~0ull && dec->chunk_off[i] + b > dec->stream_bytes) {
+      why = "a stream chunk lies outside the stream";
+      return false;
+    }
   }
-  D.tile = std::max(tile, 16);
-  o += r16(u_need);
-  M.total = static_cast<int>(o);
-  if (o > smem_cap) {
-    why = "the cluster decoder needs more shared memory than a CTA has";
-    return false;
+  for (size_t i = 0; i < plans.size(); ++i) {
+    const Op& op = dec->ops[i];
+    if (op.n_chunks > kStages) {
+      why = "an op needs more stream chunks than the ring holds";
+      return false;
+    }
+    if (static_cast<size_t>(op.ll_out) + plans[i].out_words > dec->ll_words) {
+      why = "a flag-word buffer lies outside its region";
+      return false;
+    }
+    for (int c = 0; c < R; ++c) {
+      const int rows_c = dec->op_rows[i * R + c];
+      if (op.kind != OP_ATTN && op.kind != OP_MERGE && (rows_c > op.rows_per || rows_c > loc_n)) {
+        why = "a CTA's rows exceed its row buffer";
+        return false;
+      }
+    }
   }
-  dec->smem = o;
   return true;
 }
 
@@ -1372,33 +1807,28 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
   dec->ws = nullptr;
   dec->trace = nullptr;
   dec->trace_step = 0;
-  int dev = 0, optin = 0;
+  int dev = 0, optin = 0, sms = 0;
   IVB_CUDA(cudaGetDevice(&dev));
   IVB_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+  IVB_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
   const size_t cap = static_cast<size_t>(optin) - 4096;  // static shared memory of the kernel
-  IVB_CUDA(cudaFuncSetAttribute(cluster_decode_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1));
-  std::string why = "no cluster size fits";
+  // CTA count: the request (default 128: the flag-word handoff measured fastest there on B200), at
+  // most one CTA per SM, lowered until every CTA has rows of every hidden/FFN projection and the
+  // plan fits a CTA's shared memory
+  const int want = std::min(ctas > 0 ? ctas : 128, sms - desc->heads);  // the attention CTAs take one SM per head
+  std::string why = "no CTA count fits";
   bool planned = false;
-  for (int R : {16, 8, 4, 2, 1}) {
-    if (ctas > 0 && R > ctas) continue;
-    if (!plan(dec, R, cap, why)) continue;
-    IVB_CUDA(cudaFuncSetAttribute(cluster_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(R);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = dec->smem;
-    cudaLaunchAttribute at[1];
-    at[0].id = cudaLaunchAttributeClusterDimension;
-    at[0].val.clusterDim.x = R;
-    at[0].val.clusterDim.y = 1;
-    at[0].val.clusterDim.z = 1;
-    cfg.attrs = at;
-    cfg.numAttrs = 1;
-    int clusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&clusters, reinterpret_cast<const void*>(cluster_decode_kernel), &cfg) != cudaSuccess ||
-        clusters < 1) {
-      cudaGetLastError();
-      why = "the device cannot schedule the cluster";
+  for (int R = want; R >= 1; --R) {
+    std::string w;
+    if (!plan(dec, R, cap, w)) {
+      if (why == "no CTA count fits") why = w;
+      continue;
+    }
+    IVB_CUDA(cudaFuncSetAttribute(grid_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
+    int per_sm = 0;
+    IVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_decode_kernel, kThreads, dec->smem));
+    if (per_sm < 1 || per_sm * sms < R + dec->A) {
+      why = "the device cannot hold every CTA of the decode kernel at once";
       continue;
     }
     dec->R = R;
@@ -1409,7 +1839,6 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
     delete dec;
     return fail(IVB_EINVAL, "ivb_decoder_create: %s", why.c_str());
   }
-  const int R = dec->R;
   size_t off = 0;
   dec->off_stream = off;
   off = align_up(off + dec->stream_bytes, 256);
@@ -1417,19 +1846,19 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
   off = align_up(off + dec->ops.size() * sizeof(OpRec), 256);
   dec->off_op_rows = off;
   off = align_up(off + dec->op_rows.size() * 4, 256);
-  dec->off_chunk_off = off;
+  dec->off_chunk_addr = off;
   off = align_up(off + dec->chunk_off.size() * 8, 256);
   dec->off_chunk_bytes = off;
   off = align_up(off + dec->chunk_bytes.size() * 4, 256);
-  dec->off_layers = off;
-  off = align_up(off + dec->layers.size() * sizeof(IvbLayerDesc), 256);
-  dec->off_cand_key = off;
-  off = align_up(off + static_cast<size_t>(R) * dec->kc * 4, 256);
-  dec->off_cand_id = off;
-  off = align_up(off + static_cast<size_t>(R) * dec->kc * 4, 256);
-  dec->off_cand_n = off;
-  off = align_up(off + R * 4, 256);
-  dec->off_sync = off;
+  dec->off_attn_addr = off;
+  off = align_up(off + dec->attn_off.size() * 8 + 8, 256);
+  dec->off_attn_bytes = off;
+  off = align_up(off + dec->attn_bytes.size() * 4 + 4, 256);
+  dec->off_attn_ops = off;
+  off = align_up(off + dec->attn_ops.size() * 4 + 4, 256);
+  dec->off_ll = off;
+  off = align_up(off + dec->ll_words * 8, 256);
+  dec->off_sync = off;  // [0] error word, [4] token epoch
   off = align_up(off + 256, 256);
   dec->total = off;
   *out = dec;
@@ -1442,7 +1871,7 @@ uint64_t ivb_decoder_workspace_bytes(const IvbDecoder* dec) { return dec ? dec->
 
 int32_t ivb_decoder_num_phases(const IvbDecoder* dec) { return dec ? static_cast<int32_t>(dec->ops.size()) : 0; }
 
-int32_t ivb_decoder_ctas(const IvbDecoder* dec) { return dec ? dec->R : 0; }
+int32_t ivb_decoder_ctas(const IvbDecoder* dec) { return dec ? dec->R + dec->A : 0; }
 
 int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream) {
   using namespace ivb;
@@ -1471,12 +1900,22 @@ int32_t ivb_decoder_bind(IvbDecoder* dec, void* workspace, void* stream) {
     }
     IVB_CUDA(cudaMemcpyAsync(ws + dec->off_ops, dec->recs.data(), dec->recs.size() * sizeof(OpRec), cudaMemcpyHostToDevice, s));
   }
+  dec->chunk_addr.resize(dec->chunk_off.size());
+  for (size_t i = 0; i < dec->chunk_off.size(); ++i)
+    dec->chunk_addr[i] = dec->chunk_off[i] == ~0ull ? dec->chunk_ptr[i]
+                                                    : static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(blob)) + dec->chunk_off[i];
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_op_rows, dec->op_rows.data(), dec->op_rows.size() * 4, cudaMemcpyHostToDevice, s));
-  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_off, dec->chunk_off.data(), dec->chunk_off.size() * 8, cudaMemcpyHostToDevice, s));
+  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_addr, dec->chunk_addr.data(), dec->chunk_addr.size() * 8, cudaMemcpyHostToDevice, s));
   IVB_CUDA(cudaMemcpyAsync(ws + dec->off_chunk_bytes, dec->chunk_bytes.data(), dec->chunk_bytes.size() * 4, cudaMemcpyHostToDevice, s));
-  IVB_CUDA(cudaMemcpyAsync(ws + dec->off_layers, dec->layers.data(), dec->layers.size() * sizeof(IvbLayerDesc),
-                           cudaMemcpyHostToDevice, s));
-  IVB_CUDA(cudaMemsetAsync(ws + dec->off_cand_n, 0, dec->R * 4, s));
+  dec->attn_addr.resize(dec->attn_off.size());
+  for (size_t i = 0; i < dec->attn_off.size(); ++i)
+    dec->attn_addr[i] = static_cast<unsigned long long>(reinterpret_cast<uintptr_t>(blob)) + dec->attn_off[i];
+  if (!dec->attn_addr.empty()) {
+    IVB_CUDA(cudaMemcpyAsync(ws + dec->off_attn_addr, dec->attn_addr.data(), dec->attn_addr.size() * 8, cudaMemcpyHostToDevice, s));
+    IVB_CUDA(cudaMemcpyAsync(ws + dec->off_attn_bytes, dec->attn_bytes.data(), dec->attn_bytes.size() * 4, cudaMemcpyHostToDevice, s));
+    IVB_CUDA(cudaMemcpyAsync(ws + dec->off_attn_ops, dec->attn_ops.data(), dec->attn_ops.size() * 4, cudaMemcpyHostToDevice, s));
+  }
+  IVB_CUDA(cudaMemsetAsync(ws + dec->off_ll, 0, dec->ll_words * 8, s));  // every flag word starts at epoch 0
   IVB_CUDA(cudaMemsetAsync(ws + dec->off_sync, 0, 256, s));
   IVB_CUDA(cudaStreamSynchronize(s));
   return IVB_OK;
@@ -1498,20 +1937,25 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   if (steps == 0) return IVB_OK;
   if (feed == nullptr && !(flags & IVB_RUN_SAMPLE))
     return fail(IVB_EINVAL, "ivb_decoder_run: without fed tokens every step must sample");
-  ClusterParams p{};
+  DecodeParams p{};
   p.ops = reinterpret_cast<const OpRec*>(ws + dec->off_ops);
   p.op_rows = reinterpret_cast<const int32_t*>(ws + dec->off_op_rows);
   p.n_ops = static_cast<int32_t>(dec->ops.size());
   p.kc = dec->kc;
+  p.head_op = dec->head_op;
   p.head_first = dec->head_first;
   p.chunks_per_token = dec->cpt;
   p.steps = steps;
-  p.chunk_off = reinterpret_cast<const unsigned long long*>(ws + dec->off_chunk_off);
+  p.chunk_addr = reinterpret_cast<const unsigned long long*>(ws + dec->off_chunk_addr);
   p.chunk_bytes = reinterpret_cast<const unsigned*>(ws + dec->off_chunk_bytes);
-  p.stream = ws + dec->off_stream;
+  p.attn_addr = reinterpret_cast<const unsigned long long*>(ws + dec->off_attn_addr);
+  p.attn_bytes = reinterpret_cast<const unsigned*>(ws + dec->off_attn_bytes);
+  p.attn_ops = reinterpret_cast<const int32_t*>(ws + dec->off_attn_ops);
+  p.n_mla = static_cast<int32_t>(dec->attn_ops.size());
+  p.ll = reinterpret_cast<unsigned long long*>(ws + dec->off_ll);
+  p.epoch = reinterpret_cast<unsigned*>(ws + dec->off_sync + 4);
   p.d = dec->d;
   p.sm = dec->sm;
-  p.layers = reinterpret_cast<const IvbLayerDesc*>(ws + dec->off_layers);
   p.head = md.head;
   p.logits = md.logits;
   p.token = md.token;
@@ -1522,9 +1966,6 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   p.sampling = md.sampling;
   p.top_k = md.top_k;
   p.rng = md.rng;
-  p.cand_key = reinterpret_cast<unsigned*>(ws + dec->off_cand_key);
-  p.cand_id = reinterpret_cast<int*>(ws + dec->off_cand_id);
-  p.cand_n = reinterpret_cast<int*>(ws + dec->off_cand_n);
   p.error = error;
   p.feed = feed;
   p.timeout_ns = timeout_ns == 0 ? 1000000000ull : timeout_ns;
@@ -1532,19 +1973,18 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   p.trace_step = dec->trace_step;
   p.flags = flags;
   IVB_CUDA(cudaMemsetAsync(error, 0, 4, s));
+  // cooperative: every CTA is resident at once (they wait on one another's flag words)
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(dec->R);
+  cfg.gridDim = dim3(dec->R + dec->A);
   cfg.blockDim = dim3(kThreads);
   cfg.dynamicSmemBytes = dec->smem;
   cfg.stream = s;
   cudaLaunchAttribute at[1];
-  at[0].id = cudaLaunchAttributeClusterDimension;
-  at[0].val.clusterDim.x = dec->R;
-  at[0].val.clusterDim.y = 1;
-  at[0].val.clusterDim.z = 1;
+  at[0].id = cudaLaunchAttributeCooperative;
+  at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  IVB_CUDA(cudaLaunchKernelEx(&cfg, cluster_decode_kernel, p));
+  IVB_CUDA(cudaLaunchKernelEx(&cfg, grid_decode_kernel, p));
   return IVB_OK;
 }
 

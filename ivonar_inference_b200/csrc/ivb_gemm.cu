@@ -28,7 +28,7 @@
 #include <mutex>
 
 #include "ivb_common.h"
-#include "ivb_cluster.cuh"
+#include "ivb_decode.cuh"
 #include "ivb_tiles.cuh"
 
 namespace ivb {

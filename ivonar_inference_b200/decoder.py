@@ -329,7 +329,7 @@ class B200Decoder:
                 kinds += [f"L{index}.entry_ssm", f"L{index}.out", f"L{index}.gate_up", f"L{index}.down"]
             else:
                 kinds += [f"L{index}.entry", f"L{index}.attention", f"L{index}.out", f"L{index}.gate_up", f"L{index}.down"]
-        return kinds + ["head"]
+        return kinds + ["head", "merge"]
 
     @property
     def weight_bytes(self) -> int:

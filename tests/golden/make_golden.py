@@ -1,9 +1,12 @@
 """Generate the golden vectors that pin the CPU oracle to the reference implementation.
 
-Run in a container where the reference package is importable (it is not available on the GPU
-hosts, so its outputs travel as these fixtures):
+Run where the reference package (ivonar_inference) is importable, for example after installing it
+under baseline/_ref as bench.py's reference arm does; IVONAR_HOME must name a writable directory
+for its numba cache:
 
-    IVONAR_HOME=/tmp/ivh PYTHONPATH=/root/reference/src python tests/golden/make_golden.py
+    IVONAR_HOME=<writable dir> PYTHONPATH=<reference install or its src/> python tests/golden/make_golden.py
+
+The generated fixtures are committed, so the tests need only this repository.
 
 It imports LuisOezdem/ivonar-inference unmodified and records, on seeded synthetic inputs:
   quantizer.npz   numba norm_quantize / quantize_into (cpu_decoder.py:30-70)
