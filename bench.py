@@ -99,7 +99,9 @@ def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
     """
     cfg = model.config
     weights = 0
-    for proj in model.projections():
+    for proj in model.modules():
+        if getattr(proj, "packed_weight", None) is None:
+            continue
         weights += proj.packed_weight.numel() + proj.weight_scales.numel() * 2
         if proj.bias is not None:
             weights += proj.bias.numel() * 4

@@ -1,32 +1,35 @@
-"""B200Decoder: the reference decoder interface over the sm_100a persistent decode kernel.
+"""B200Decoder: the reference decoder interface over the sm_100a whole-GPU decode kernel.
 
-Drop-in for ``ivonar_inference.kernel_decoder.KernelDecoder`` behind ``build_decoder``
-(reference src/ivonar_inference/decoder.py:61-466 for the interface, 479-529 for the dispatch):
-same constructor arguments, attributes (device, max_len, batch_size, burst_size, position,
-host_position, logits, token, seen, graph, graphs, attention_lengths) and methods (prefill, step,
-configure_sampling, sample, advance, advance_many, capture, reset, self_check, attention_length),
-same errors (ValueError "capacity" / "no free position left", RuntimeError without sampling).
+Drop-in for ``ivonar_inference.kernel_decoder.KernelDecoder`` behind ``build_decoder`` (reference
+src/ivonar_inference/decoder.py:61-466 for the interface, 479-529 for the dispatch). Like the
+reference's own GPU decoder it is a subclass of the reference's ``StaticDecoder``
+(kernel_decoder.py:145-170): the constructor, attributes (device, max_len, batch_size, burst_size,
+position, host_position, logits, token, seen, graph, graphs, attention_lengths), ``step``,
+``advance``, ``configure_sampling``, ``reset`` and ``attention_length`` are the reference's own; this
+class overrides what the kernels run (``prefill``, the per-token ``_step`` and ``_sample``,
+``advance_many``, ``capture``, ``self_check``).
 
-The model can be the reference ``IvonarModel`` or this package's ``PackedModel``; only their
-packed tensors are read. Weights stay in the q2_g128 format; rows are stacked per fused projection
-(entry, gate/up interleaved) and padded to 16-byte rows, as the reference Matrix does
-(kernel_decoder.py:84-142). The attention cache is the compressed latent (int8 codes + scale per
-position, fp16 rotated k_rope) instead of the reference's decompressed fp16 K/V.
+The model is the reference ``IvonarModel``; only its packed tensors are read. Weights stay in the
+q2_g128 format; rows are stacked per fused projection (entry, gate/up interleaved) and padded to
+16-byte rows, as the reference Matrix does (kernel_decoder.py:84-142). The attention cache is the
+compressed latent (int8 codes + scale per position, fp16 rotated k_rope) instead of the reference's
+decompressed fp16 K/V.
 """
 
 from __future__ import annotations
 
 import ctypes
 import math
-from collections.abc import Iterable
 
 import torch
 import torch.nn.functional as F
 from torch import Tensor
 
 from . import _native as native
+from . import _reference
 from ._native import KernelError
-from .model import rope_table
+
+StaticDecoder = _reference.module("decoder").StaticDecoder
 
 BURST = 16
 SELF_CHECK_TOLERANCE = 0.25
@@ -86,7 +89,17 @@ class DeviceMatrix:
         return self.packed.numel() + self.scales.numel() * 2 + (0 if self.bias is None else self.bias.numel() * 4)
 
 
-class B200Decoder:
+def rope_from_rotary(rotary, max_len: int) -> Tensor:
+    """[max_len, rope_dim/2, 2] (cos, sin) of one attention layer, computed by the reference's own
+    ``Rotary.rotate`` on unit vectors (as StaticDecoder._prepare_attention does, decoder.py:177-181)."""
+
+    dim = int(rotary.head_dim)
+    unit = torch.zeros(1, max_len, 1, dim, dtype=torch.float32)
+    unit[..., 0::2] = 1.0
+    return rotary.rotate(unit, offset=0).reshape(max_len, dim // 2, 2).contiguous()
+
+
+class B200Decoder(StaticDecoder):
     """Batch-1 decoder whose whole token step is one persistent sm_100a kernel launch."""
 
     backend_name = "ternary-b200"
@@ -109,48 +122,35 @@ class B200Decoder:
             raise KernelError("ternary kernels need a CUDA device")
         if target.index is None:
             target = torch.device("cuda", torch.cuda.current_device())
-        if max_top_k <= 0:
-            raise ValueError("max_top_k must be positive")
-        self.lib = native.library()
-        self.model = model
         if prefill not in ("gemm", "steps"):
             raise ValueError("prefill must be 'gemm' (tensor-core prefill) or 'steps' (token by token)")
-        self.prefill_mode = prefill
-        self.prefill_chunk = max(1, int(prefill_chunk))
-        self._prefill_ws: Tensor | None = None
-        self.device = target
-        config = model.config
-        self.max_len = int(config.seq_len if max_len is None else max_len)
-        if self.max_len <= 0 or self.max_len > int(config.seq_len):
-            raise ValueError("max_len must lie within the model context")
+        self.lib = native.library()
         with torch.cuda.device(target):
             if not self.lib.ivb_device_supported():
                 raise KernelError(f"{torch.cuda.get_device_name(target)} is not an sm_100 GPU this build runs on")
-        self.batch_size = 1
-        self.sampling = bool(sampling)
-        vocab = int(config.vocab_size)
-        self.vocab = vocab
-        self.max_top_k = min(int(max_top_k), vocab)
-        self.attention_lengths = (self.max_len,)
-        self.host_position = 0
-        self.burst_size = 1
-        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        capacity = int(model.config.seq_len if max_len is None else max_len)
+        super().__init__(model, max_len=capacity, batch_size=1, device=target, sampling=sampling, max_top_k=max_top_k,
+                         attention_lengths=(capacity,), fuse_projections=False)
+        # the kernels keep their own compressed latent cache: the reference's fp16 K/V caches go
+        self.attention_caches = {}
+        self.prefill_mode = prefill
+        self.prefill_chunk = max(1, int(prefill_chunk))
+        self._prefill_ws: Tensor | None = None
+        self.vocab = int(model.config.vocab_size)
         self._burst_graph: torch.cuda.CUDAGraph | None = None
         self.timeout_ns = int(timeout_ns)
-        dev = target
-        self.token = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.position = torch.zeros(1, dtype=torch.int64, device=dev)
-        self.logits = torch.zeros(1, vocab, dtype=torch.float32, device=dev)
-        self.seen = torch.zeros(1, vocab, dtype=torch.bool, device=dev)
+        dev = self.device
+        # temperature, penalty and inverse penalty side by side (the kernels read one [3] array); the
+        # reference's configure_sampling fills these views
         self._sampling = torch.ones(3, dtype=torch.float32, device=dev)
         self.temperature = self._sampling[0:1]
         self.penalty = self._sampling[1:2]
         self.inverse_penalty = self._sampling[2:3]
-        self.top_k = torch.full((1,), self.max_top_k, dtype=torch.int64, device=dev)
         self.history = torch.zeros(max(self.max_len, BURST), dtype=torch.int64, device=dev)
         if seed is None:
             seed = int(torch.randint(0, 2**62, (1,)).item())
         self.rng = torch.tensor([int(seed), 0], dtype=torch.int64, device=dev)
+        self._ctas_request = int(ctas)
         self._build(model, dev)
 
     # ------------------------------------------------------------------------------------------
@@ -161,7 +161,6 @@ class B200Decoder:
         self.head = DeviceMatrix([model.token_io.projection], dev)
         self.final_norm = model.final_norm.weight.float().to(dev).contiguous()
         self.layer_matrices: list[dict[str, DeviceMatrix]] = []
-        self.recurrent_states: dict[int, dict[str, Tensor]] = {}
         self.latent_caches: dict[int, tuple[Tensor, Tensor, Tensor]] = {}
         self._keep: list[Tensor] = []
         layers = (native.IvbLayerDesc * len(model.blocks))()
@@ -194,12 +193,11 @@ class B200Decoder:
                 }
                 consts = {k: v.to(dev) for k, v in consts.items()}
                 self._keep += list(consts.values())
-                state = {
-                    "ssm_state": torch.zeros(1, mixer.num_heads, mixer.state_dim, mixer.head_dim, 2, device=dev),
-                    "prev_force": torch.zeros(1, mixer.num_heads, mixer.state_dim, mixer.head_dim, device=dev),
-                    "conv_state": torch.zeros(1, hidden, max(taps - 1, 1), device=dev),
-                }
-                self.recurrent_states[index] = state
+                # the reference's recurrent state buffers (StaticDecoder._prepare_recurrent): [1, H, S, hd, 2],
+                # [1, H, S, hd], [1, hidden, taps - 1] fp32, the layout the kernels read
+                state = self.recurrent_states[index]
+                if taps < 2:
+                    raise KernelError("the B200 kernels need a causal convolution of at least 2 taps")
                 for key in ("decay", "theta", "skip", "conv_weight", "conv_bias"):
                     setattr(desc, key, consts[key].data_ptr())
                 desc.ssm_state = state["ssm_state"].data_ptr()
@@ -216,7 +214,7 @@ class B200Decoder:
                 # up-projections are read by bulk copies: 16-byte scale rows
                 mats["k_nope_up"] = DeviceMatrix([mixer.k_nope_up_proj], dev, scale_align=8)
                 mats["v_up"] = DeviceMatrix([mixer.v_up_proj], dev, scale_align=8)
-                rope = rope_table(mixer.rope, self.max_len).to(dev)
+                rope = rope_from_rotary(mixer.rope, self.max_len).to(dev)
                 # compressed cache: int8 latent codes (rows padded to 16 bytes), one scale per
                 # position (padded to a multiple of 4), head-major fp16 k_rope (rows padded to 8)
                 lpad = (int(mixer.latent_dim) + 15) // 16 * 16
@@ -277,7 +275,8 @@ class B200Decoder:
         self._desc = md
         handle = ctypes.c_void_p()
         with torch.cuda.device(dev):
-            native.check(self.lib.ivb_decoder_create(ctypes.byref(md), 0, ctypes.byref(handle)), "ivb_decoder_create")
+            native.check(self.lib.ivb_decoder_create(ctypes.byref(md), self._ctas_request, ctypes.byref(handle)),
+                         "ivb_decoder_create")
             self._plan = handle
             self.workspace = torch.zeros(int(self.lib.ivb_decoder_workspace_bytes(handle)), dtype=torch.uint8, device=dev)
             native.check(self.lib.ivb_decoder_bind(handle, self.workspace.data_ptr(), self._stream()), "ivb_decoder_bind")
@@ -346,19 +345,10 @@ class B200Decoder:
     def persisted_bytes(self) -> int:
         return 0
 
-    @property
-    def graph(self) -> torch.cuda.CUDAGraph | None:
-        return self.graphs.get(self.max_len)
-
-    def attention_length(self, position: int) -> int:
-        if position < self.max_len:
-            return self.max_len
-        raise ValueError("the decoder has no free position left")
-
     # ------------------------------------------------------------------------------------------
     @torch.no_grad()
     def prefill(self, input_ids: Tensor) -> Tensor:
-        """Run the prompt (teacher-forced through the persistent kernel) and return its last logits."""
+        """Run the prompt and return its last logits (tensor-core prefill, or token by token)."""
 
         if input_ids.ndim != 2 or input_ids.shape[0] != self.batch_size:
             raise ValueError(f"input_ids must have shape [{self.batch_size}, seq_len]")
@@ -398,61 +388,22 @@ class B200Decoder:
                                                   self._prefill_ws.data_ptr(), self._prefill_ws.numel(), self._stream())
                 native.check(rc, "ivb_decoder_prefill")
 
-    @torch.no_grad()
-    def step(self, token: Tensor) -> Tensor:
-        """Feed one token and return the next logits (samples too when the decoder samples)."""
+    def _step(self, length: int) -> None:
+        """One token through the kernel (the reference step's contract, decoder.py:307-322): feeds
+        self.token, advances self.position and, when sampling, samples the next token into it."""
 
-        if token.ndim == 2:
-            token = token[:, 0]
-        if token.shape != (self.batch_size,):
-            raise ValueError(f"token must have shape [{self.batch_size}]")
-        self.attention_length(self.host_position)
-        self.token.copy_(token.to(device=self.device, dtype=torch.int64))
-        graph = self.graphs.get(self.max_len)
-        if graph is not None:
-            graph.replay()
-        else:
-            self._launch(1, self.token, native.IVB_RUN_SAMPLE if self.sampling else 0)
-        self._check()
-        self.host_position += 1
-        return self.logits
+        self._launch(1, self.token, native.IVB_RUN_SAMPLE if self.sampling else 0)
+        if not torch.cuda.is_current_stream_capturing():
+            self._check()
 
-    def configure_sampling(self, temperature: float, top_k: int, repetition_penalty: float = 1.0,
-                           penalized_ids: Iterable[int] = ()) -> None:
-        """Set the sampling rule for the answer that starts now (reference decoder.py:335-361)."""
+    def _run_step(self) -> None:
+        super()._run_step()
+        self._check()  # errors of a replayed graph surface here
 
-        if not self.sampling:
-            raise RuntimeError("this decoder was created without sampling")
-        if temperature <= 0 or repetition_penalty <= 0:
-            raise ValueError("temperature and repetition_penalty must be positive")
-        effective = int(top_k) if 0 < int(top_k) <= self.max_top_k else self.max_top_k
-        self.temperature.fill_(float(temperature))
-        self.penalty.fill_(float(repetition_penalty))
-        self.inverse_penalty.fill_(1.0 / float(repetition_penalty))
-        self.top_k.fill_(effective)
-        self.seen.zero_()
-        seeds = [int(t) for t in penalized_ids if 0 <= int(t) < self.seen.shape[1]]
-        if seeds:
-            index = torch.tensor(sorted(set(seeds)), dtype=torch.int64, device=self.device)
-            self.seen.index_fill_(1, index, True)
-
-    @torch.no_grad()
-    def sample(self) -> int:
-        """Sample from the logits the last prefill or step produced."""
-
-        if not self.sampling:
-            raise RuntimeError("this decoder was created without sampling")
+    def _sample(self) -> None:
         self._launch(0, None, native.IVB_RUN_SAMPLE_ONLY)
-        self._check()
-        return int(self.token[0])
-
-    @torch.no_grad()
-    def advance(self) -> int:
-        """Feed the sampled token, run one step and return the token sampled from it."""
-
-        if not self.sampling:
-            raise RuntimeError("this decoder was created without sampling")
-        return self.advance_many(1)[0]
+        if not torch.cuda.is_current_stream_capturing():
+            self._check()
 
     @torch.no_grad()
     def advance_many(self, count: int) -> list[int]:
@@ -480,45 +431,35 @@ class B200Decoder:
 
     @torch.no_grad()
     def capture(self, warmup_steps: int = 2) -> bool:
-        """Record the one-step launch (and the 16-token burst when sampling) as CUDA graphs."""
+        """The reference's one-step graph (decoder.py:403-433) plus a 16-token burst graph when sampling
+        (as kernel_decoder.py:482-512 adds); the decoder state the warm-up steps touch is restored."""
 
         if self.device.type != "cuda" or not torch.cuda.is_available():
             return False
-        saved_position = int(self.position)
-        saved_token = self.token.clone()
         saved_rng = self.rng.clone()
         saved_seen = self.seen.clone()
         saved_states = {i: {k: v.clone() for k, v in s.items()} for i, s in self.recurrent_states.items()}
-        graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        saved_position = int(self.position)
+        saved_token = self.token.clone()
+        captured = super().capture(warmup_steps)
         burst = None
-        flags = native.IVB_RUN_SAMPLE if self.sampling else 0
-        try:
-            stream = torch.cuda.Stream(device=self.device)
-            stream.wait_stream(torch.cuda.current_stream(self.device))
-            with torch.cuda.stream(stream):
-                for _ in range(max(1, warmup_steps)):
+        if captured and self.sampling and self.max_len >= BURST:
+            try:
+                stream = torch.cuda.Stream(device=self.device)
+                stream.wait_stream(torch.cuda.current_stream(self.device))
+                with torch.cuda.stream(stream):
                     self.position.zero_()
-                    self._launch(1, self.token, flags)
-                torch.cuda.synchronize(self.device)
-                graph = torch.cuda.CUDAGraph()
-                self.position.zero_()
-                with torch.cuda.graph(graph, stream=stream):
-                    self._launch(1, self.token, flags)
-                graphs[self.max_len] = graph
-                if self.sampling and self.max_len >= BURST:
-                    self.position.zero_()
-                    self._launch(BURST, None, flags)
+                    self._launch(BURST, None, native.IVB_RUN_SAMPLE)
                     torch.cuda.synchronize(self.device)
-                    burst = torch.cuda.CUDAGraph()
+                    graph = torch.cuda.CUDAGraph()
                     self.position.zero_()
-                    with torch.cuda.graph(burst, stream=stream):
-                        self._launch(BURST, None, flags)
-            torch.cuda.synchronize(self.device)
-            self._check()
-        except Exception:
-            graphs = {}
-            burst = None
-        self.graphs = graphs
+                    with torch.cuda.graph(graph, stream=stream):
+                        self._launch(BURST, None, native.IVB_RUN_SAMPLE)
+                torch.cuda.synchronize(self.device)
+                self._check()
+                burst = graph
+            except Exception:
+                burst = None
         self._burst_graph = burst
         self.burst_size = BURST if burst is not None else 1
         self.position.fill_(saved_position)
@@ -528,7 +469,7 @@ class B200Decoder:
         for i, state in saved_states.items():
             for key, value in state.items():
                 self.recurrent_states[i][key].copy_(value)
-        return bool(graphs)
+        return captured
 
     @torch.no_grad()
     def self_check(self) -> None:
@@ -553,32 +494,19 @@ class B200Decoder:
         if not 0 <= sampled < vocab:
             raise KernelError("the B200 sampler returned an invalid token on this GPU")
 
-    def reset(self) -> None:
-        self.position.zero_()
-        self.host_position = 0
-        self.seen.zero_()
-
-
-def _reference_static_decoder():
-    try:
-        from ivonar_inference.decoder import StaticDecoder  # type: ignore
-
-        return StaticDecoder
-    except Exception:
-        return None
-
 
 def build_decoder(model, device: str | torch.device, sampling: bool = False, max_top_k: int = 256,
                   kernels: bool = True) -> tuple[object, str, str | None]:
-    """The decoder the engine serves: the B200 kernels where they run (reference decoder.py:479-507).
+    """The decoder the engine serves (reference decoder.py:479-507 with its CUDA kernel slot,
+    ``_kernel_decoder`` at :518-529, filled by B200Decoder).
 
-    Returns ``(decoder, backend, note)`` with backend "ternary" for the kernel path, as the
-    reference does. When the kernels cannot run, the reference torch decoder is used if the
-    reference package is importable; otherwise the error is raised.
+    CUDA with kernels: a self-checked B200Decoder, backend "ternary". When it cannot run there, or for
+    any other device, the reference's own ``build_decoder`` decides (its numba CPU decoder or its torch
+    decoder), with the B200 failure as the note.
     """
 
     target = torch.device(device)
-    note = None
+    reference_build = _reference.module("decoder").build_decoder
     if kernels and target.type == "cuda":
         try:
             decoder = B200Decoder(model, device=target, sampling=sampling, max_top_k=max_top_k)
@@ -586,11 +514,6 @@ def build_decoder(model, device: str | torch.device, sampling: bool = False, max
             return decoder, "ternary", None
         except Exception as exc:
             note = f"B200 ternary kernels unavailable, using the torch decoder: {exc}"
-            fallback = _reference_static_decoder()
-            if fallback is None:
-                raise
-    fallback = _reference_static_decoder()
-    if fallback is None:
-        raise KernelError("no decoder for this device: the B200 kernels need an sm_100 GPU")
-    decoder = fallback(model, device=target, sampling=sampling, max_top_k=max_top_k)
-    return decoder, "torch", note
+        decoder, backend, _ = reference_build(model, target, sampling=sampling, max_top_k=max_top_k, kernels=False)
+        return decoder, backend, note
+    return reference_build(model, target, sampling=sampling, max_top_k=max_top_k, kernels=kernels)

@@ -8,7 +8,10 @@ of the named shapes, built as packed state dicts with the reference key layout (
   SSM constants as the reference tests build them (tests/conftest.py:88-94).
 ``style="reference_tests"`` reproduces the reference test distribution instead (uniform codes,
 scales U(0.01, 0.06)). Generation uses one CPU torch.Generator, so a (config, seed) pair gives
-the same bytes on every machine with the same torch build.
+the same bytes on every machine with the same torch build. The models are the reference's own
+``IvonarModel`` objects: the payload is parsed by the reference's ``ModelConfig.from_payload`` and the
+state dict assembled (and validated) by its ``build_model`` (src/ivonar_inference/config.py:39,
+loader.py:146).
 """
 
 from __future__ import annotations
@@ -17,13 +20,28 @@ import math
 
 import torch
 
-from .model import REQUIRED_CONTRACT, ModelConfig, PackedModel, build_model
+from . import _reference
+
+# The checkpoint contract every Ivonar packed checkpoint declares (the keys and values the reference
+# loader requires, src/ivonar_inference/config.py:6-17): a format, restated here as data only.
+CONTRACT = {
+    "architecture": "ivonar_native_ternary",
+    "architecture_version": 1,
+    "ternary_group_size": 128,
+    "ternary_storage": "q2_g128",
+    "activation_quantization": "int8_per_token",
+    "output_head_type": "tied_ternary_embedding_head",
+    "mla_rope_layout": "decoupled_direct_rope",
+    "mamba_implementation": "ivonar_mamba3_conv_et_mimo",
+    "mamba_variant": "MIMO",
+    "tie_embeddings": True,
+}
 
 
 def config_payload(name: str, vocab: int, hidden: int, layers: list[str], heads: int, state_dim: int, latent: int,
                    dense: int, seq_len: int) -> dict:
     return {
-        **REQUIRED_CONTRACT,
+        **CONTRACT,
         "name": name,
         "vocab_size": vocab,
         "seq_len": seq_len,
@@ -86,7 +104,7 @@ def _packed(gen: torch.Generator, rows: int, cols: int, style: str) -> tuple[tor
 def synthetic_state(payload: dict, seed: int = 0, style: str = "baseline") -> dict[str, torch.Tensor]:
     """A packed state dict for ``payload`` (see the module docstring for the distributions)."""
 
-    config = ModelConfig.from_payload(payload)
+    config = _reference.module("config").ModelConfig.from_payload(payload)
     gen = torch.Generator().manual_seed(int(seed))
     # "fast": the packed matrices are drawn on the GPU when there is one (the 7B-shaped model in seconds)
     big = gen
@@ -135,8 +153,12 @@ def synthetic_state(payload: dict, seed: int = 0, style: str = "baseline") -> di
     return state
 
 
-def synthetic_model(payload: dict, seed: int = 0, style: str = "baseline") -> PackedModel:
-    return build_model(payload, synthetic_state(payload, seed, style), validate=False)
+def synthetic_model(payload: dict, seed: int = 0, style: str = "baseline"):
+    """The reference ``IvonarModel`` of ``payload`` with the synthetic weights (on the CPU)."""
+
+    config = _reference.module("config").ModelConfig.from_payload(payload)
+    model = _reference.module("loader").build_model(config, synthetic_state(payload, seed, style))
+    return model.eval()
 
 
 def random_prompt(vocab: int, length: int, seed: int = 0, low: int = 0) -> torch.Tensor:

@@ -29,8 +29,7 @@ import torch.nn.functional as F
 from torch import Tensor
 
 from . import _native as native
-from .decoder import DeviceMatrix
-from .model import Ternary, rope_table
+from .decoder import DeviceMatrix, rope_from_rotary
 
 
 def split_even(total: int, parts: int, unit: int = 1) -> list[tuple[int, int]]:
@@ -48,12 +47,27 @@ def split_even(total: int, parts: int, unit: int = 1) -> list[tuple[int, int]]:
     return out
 
 
-def row_slice(t: Ternary, r0: int, r1: int) -> Ternary:
+class Shard:
+    """A slice of a packed projection: the attributes DeviceMatrix reads (packed uint8 rows, fp16 group
+    scales, optional fp32 bias, widths), in the checkpoint's q2_g128 layout."""
+
+    def __init__(self, packed_weight: Tensor, weight_scales: Tensor, in_features: int, bias: Tensor | None,
+                 group_size: int = 128, eps: float = 1e-5) -> None:
+        self.packed_weight = packed_weight
+        self.weight_scales = weight_scales
+        self.in_features = int(in_features)
+        self.out_features = int(packed_weight.shape[0])
+        self.bias = bias
+        self.group_size = int(group_size)
+        self.eps = float(eps)
+
+
+def row_slice(t, r0: int, r1: int) -> Shard:
     bias = None if t.bias is None else t.bias[r0:r1]
-    return Ternary(t.packed_weight[r0:r1], t.weight_scales[r0:r1], t.in_features, bias, group_size=t.group_size, eps=t.eps)
+    return Shard(t.packed_weight[r0:r1], t.weight_scales[r0:r1], t.in_features, bias, group_size=t.group_size, eps=t.eps)
 
 
-def col_slice(t: Ternary, k0: int, k1: int, keep_bias: bool) -> Ternary:
+def col_slice(t, k0: int, k1: int, keep_bias: bool) -> Shard:
     """Inputs [k0, k1) of a matrix. The shard keeps the q2_g128 layout: either it starts on a 128-input
     group boundary (and ends on one, or at the end), or it lies inside one group (its one scale column)."""
 
@@ -63,8 +77,8 @@ def col_slice(t: Ternary, k0: int, k1: int, keep_bias: bool) -> Ternary:
         raise ValueError("column shards must follow the 128-input scale groups")
     packed = t.packed_weight[:, k0 // 4: (k1 + 3) // 4]
     scales = t.weight_scales[:, k0 // 128: (k1 - 1) // 128 + 1]
-    return Ternary(packed.contiguous(), scales.contiguous(), k1 - k0, t.bias if keep_bias else None,
-                   group_size=t.group_size, eps=t.eps)
+    return Shard(packed.contiguous(), scales.contiguous(), k1 - k0, t.bias if keep_bias else None,
+                 group_size=t.group_size, eps=t.eps)
 
 
 class B200TensorParallel:
@@ -152,7 +166,7 @@ class B200TensorParallel:
                 entry = DeviceMatrix([q, mixer.kv_down_proj, k_rope], dev)
                 kn = DeviceMatrix([row_slice(mixer.k_nope_up_proj, h0 * nope, h1 * nope)], dev, scale_align=8)
                 vu = DeviceMatrix([row_slice(mixer.v_up_proj, c0, c1)], dev, scale_align=8)
-                table = rope_table(mixer.rope, self.max_len).to(dev)
+                table = rope_from_rotary(mixer.rope, self.max_len).to(dev)
                 lpad, rpad = (Lt + 15) // 16 * 16, (rope + 7) // 8 * 8
                 cache = (
                     torch.zeros(B, self.max_len, lpad, dtype=torch.int8, device=dev),

@@ -143,7 +143,8 @@ def _torch():
 
 
 def rope_table_np(rotary, max_len: int) -> np.ndarray:
-    """Same table as ivonar_inference_b200.model.rope_table (the oracle keeps its own copy)."""
+    """[max_len, head_dim/2, (cos, sin)] of the reference RotaryEmbedding (attention.py:41-72: scaled
+    inverse frequencies and positions, then cos/sin of their outer product)."""
     torch = _torch()
     dim = int(rotary.head_dim)
     inv_freq = 1.0 / (float(rotary.rope_base) ** (torch.arange(0, dim, 2, dtype=torch.float32) / dim))

@@ -69,48 +69,29 @@ def test_last_error_reports_bad_arguments() -> None:
     assert lib.ivb_decoder_create(None, 0, ctypes.byref(handle)) == _native.IVB_EINVAL
 
 
-def test_build_model_uses_every_state_entry() -> None:
-    from ivonar_inference_b200 import model as M
-    from ivonar_inference_b200 import synthetic
+def test_synthetic_models_are_the_reference_model_built_by_its_loader(tmp_path: Path) -> None:
+    from ivonar_inference_b200 import _reference, synthetic
 
     payload = synthetic.tiny()
+    model = synthetic.synthetic_model(payload, 0, "reference_tests")
+    assert isinstance(model, _reference.module("model").IvonarModel)
+    assert [b.mixer_type for b in model.blocks] == ["mamba", "mla", "mamba"]
+    assert model.blocks[1].mixer.rope_dim == 2 and model.blocks[1].mixer.nope_dim == 2
+    # the reference loader validates what the generator emits: no reserved code 3, positive scales
     state = synthetic.synthetic_state(payload, 0, "reference_tests")
-    built = M.build_model(payload, state)
-    assert [b.mixer_type for b in built.blocks] == ["mamba", "mla", "mamba"]
-    assert built.blocks[1].mixer.rope_dim == 2 and built.blocks[1].mixer.nope_dim == 2
-    extra = dict(state)
-    extra["blocks.0.mixer.unknown"] = torch.zeros(1)
-    with pytest.raises(RuntimeError, match="does not use"):
-        M.build_model(payload, extra)
-    missing = dict(state)
-    del missing["final_norm.weight"]
-    with pytest.raises(RuntimeError, match="missing final_norm.weight"):
-        M.build_model(payload, missing)
     bad = dict(state)
     bad["blocks.0.ffn.down_proj.packed_weight"] = bad["blocks.0.ffn.down_proj.packed_weight"].clone()
     bad["blocks.0.ffn.down_proj.packed_weight"][0, 0] = 0xFF
-    with pytest.raises(RuntimeError, match="reserved code 3"):
-        M.build_model(payload, bad)
-    with pytest.raises(ValueError, match="incompatible"):
-        M.ModelConfig.from_payload({**payload, "architecture_version": 2})
-    with pytest.raises(ValueError, match="mixture-of-experts"):
-        M.ModelConfig.from_payload({**payload, "num_experts": 4})
-
-
-def test_checkpoint_round_trip(tmp_path: Path) -> None:
-    from ivonar_inference_b200 import model as M
-    from ivonar_inference_b200 import synthetic
-
-    payload = synthetic.config0()
-    state = synthetic.synthetic_state(payload, 1)
+    config = _reference.module("config").ModelConfig.from_payload(payload)
+    with pytest.raises(RuntimeError, match="code 3"):
+        _reference.module("loader").build_model(config, bad)
+    # a packed checkpoint of it loads through the reference's load_model unchanged
     path = tmp_path / "packed.pt"
-    torch.save({"format": M.PACKED_FORMAT, "schema_version": 1, "config": payload, "model_state": state}, path)
-    loaded = M.load_checkpoint(path)
-    assert loaded.config.vocab_size == 512 and len(loaded.blocks) == 4
+    loader = _reference.module("loader")
+    torch.save({"format": loader.PACKED_FORMAT, "schema_version": loader.PACKED_SCHEMA_VERSION, "config": payload,
+                "model_state": state}, path)
+    loaded = loader.load_model(path, materialize=False).model
     assert torch.equal(loaded.token_io.projection.packed_weight, state["token_io.projection.packed_weight"])
-    torch.save({"format": "other", "schema_version": 1, "config": payload, "model_state": state}, path)
-    with pytest.raises(RuntimeError, match="unsupported checkpoint format"):
-        M.load_checkpoint(path)
 
 
 def test_synthetic_models_are_reproducible_and_follow_the_distribution() -> None:
@@ -128,18 +109,17 @@ def test_synthetic_models_are_reproducible_and_follow_the_distribution() -> None
     assert abs(float(scales.log().mean()) - torch.log(torch.tensor(0.02)).item()) < 0.05
 
 
-def test_rope_table_matches_the_reference_rotary_layout() -> None:
-    from ivonar_inference_b200.model import Rotary, rope_table
+def test_rope_table_is_the_reference_decoders_rotary_table() -> None:
+    from ivonar_inference_b200 import _reference, synthetic
+    from ivonar_inference_b200.decoder import rope_from_rotary
 
-    rot = Rotary(16, base_context=32, active_context=64, scaling_strategy="linear")
-    table = rope_table(rot, 64)
-    assert table.shape == (64, 8, 2)
-    inv = 1.0 / (10000.0 ** (torch.arange(0, 16, 2, dtype=torch.float32) / 16))
-    pos = torch.arange(64, dtype=torch.float32) / 2.0
-    torch.testing.assert_close(table[..., 0], torch.cos(pos[:, None] * inv), rtol=0, atol=0)
-    yarn = rope_table(Rotary(16, 32, 64, scaling_strategy="yarn_like"), 4)
-    none = rope_table(Rotary(16, 32, 64, scaling_strategy="none"), 4)
-    assert not torch.equal(yarn, none)
+    model = synthetic.synthetic_model(synthetic.tiny(hidden=64, latent=24, dense=96, seq_len=64), 0, "reference_tests")
+    static = _reference.module("decoder").StaticDecoder(model, device="cpu")
+    mixer = model.blocks[1].mixer
+    table = rope_from_rotary(mixer.rope, 64)
+    assert table.shape == (64, mixer.rope_dim // 2, 2)
+    reference = torch.view_as_real(static.rope_tables[1][:, mixer.nope_dim // 2:])
+    torch.testing.assert_close(table, reference, rtol=0, atol=0)
 
 
 def test_the_b200_decoder_refuses_a_cpu_device() -> None:
@@ -150,10 +130,9 @@ def test_the_b200_decoder_refuses_a_cpu_device() -> None:
         B200Decoder(model, device="cpu")
 
 
-def test_build_decoder_has_no_cpu_fallback_without_the_reference(monkeypatch) -> None:
-    from ivonar_inference_b200 import KernelError, decoder, synthetic
+def test_build_decoder_leaves_other_devices_to_the_reference_dispatch() -> None:
+    from ivonar_inference_b200 import _reference, decoder, synthetic
 
-    monkeypatch.setattr(decoder, "_reference_static_decoder", lambda: None)
     model = synthetic.synthetic_model(synthetic.tiny(), 0, "reference_tests")
-    with pytest.raises(KernelError):
-        decoder.build_decoder(model, "cpu")
+    dec, backend, note = decoder.build_decoder(model, "cpu", kernels=False)
+    assert isinstance(dec, _reference.module("decoder").StaticDecoder) and backend == "torch" and note is None
