@@ -25,8 +25,14 @@ Secondary, every rank: the 7B-shaped model (weights drawn on
 parallel over the N ranks (`tp`): a 512-token random prompt teacher-forced, then sampled decode at batch
 1 and batch 32, tok/s over the slowest rank's CUDA-event time.
 
---impl reference times the reference algorithm's CPU implementation (the C port in oracle/, all host
-threads) on a bounded sample of the same workload, rank 0 only.
+Secondary, rank 0 (`gpu_reference`): the reference's own GPU decoder (KernelDecoder, NVRTC-compiled CUDA,
+installed unmodified in baseline/_ref) and B200Decoder timed by the same procedure through the reference
+API on the same GPU: prefill, configure_sampling, sample, then CUDA events around advance_many bursts that
+produce the 256 decode tokens (the reference eager and with its CUDA graphs captured).
+
+--impl reference times the reference's own CPU decoder (the numba CpuDecoder chosen by the reference's
+build_decoder for device "cpu", installed unmodified in baseline/_ref) on this host's cores, rank 0 only:
+each timed step decodes the workload's 256 sampled tokens after an untimed prefill.
 """
 
 from __future__ import annotations
@@ -63,6 +69,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--tokens", type=int, default=TOKENS)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-clocks", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true", help="skip the reference KernelDecoder on this GPU")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks)")
@@ -164,20 +171,63 @@ class ClockSampler:
         }
 
 
-def cpu_baseline(model, prompt, tokens: int, threads: int = 0) -> dict:
-    """The C port of the reference token loop on this host's cores (bounded sample)."""
-    from oracle import oracle
+def reference_environment() -> None:
+    """The reference keeps its numba and NVRTC caches under IVONAR_HOME: a temporary directory, set before
+    its modules are imported."""
+    os.environ.setdefault("IVONAR_HOME", str(Path(tempfile.gettempdir()) / "ivb_reference_home"))
 
-    dec = oracle.OracleDecoder(model, max_len=PROMPT + tokens + 1, threads=threads, seed=7)
-    dec.prefill(prompt)
-    dec.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
-    first = dec.sample()
+
+def host_cpu() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
+def reference_cpu_decoder(model):
+    """The decoder the reference serves on device "cpu": its build_decoder picks the numba CpuDecoder
+    after that decoder's self-check (the torch StaticDecoder when the check fails)."""
+    reference_environment()
+    from ivonar_inference_b200 import _reference
+
+    decoder, backend, note = _reference.module("decoder").build_decoder(model, "cpu", sampling=True, kernels=True)
+    if backend == "ternary":
+        import numba
+
+        threads = int(numba.get_num_threads())
+        label = "reference CpuDecoder (numba)"
+    else:
+        import torch
+
+        threads = int(torch.get_num_threads())
+        label = f"reference torch StaticDecoder ({note})"
+    return decoder, threads, label
+
+
+def reference_cpu_rate(decoder, prompt, tokens: int) -> float:
+    """Seconds for `tokens` sampled decode tokens after an untimed prefill (reference decoder API)."""
+    decoder.prefill(prompt)
+    decoder.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
+    decoder.sample()
     start = time.perf_counter()
-    dec.generate(first, tokens)
-    seconds = time.perf_counter() - start
-    return {"value": tokens / seconds, "unit": "tok/s", "cores": dec.threads, "kind": "port",
-            "sample": f"config1 model, {PROMPT}-token prompt prefilled, {tokens} sampled decode tokens timed "
-                      f"(C port of the reference numba/GPU decode step, OpenMP, {dec.threads} threads)",
+    decoder.advance_many(tokens)
+    return time.perf_counter() - start
+
+
+def cpu_baseline(model, tokens: int) -> dict:
+    """The reference's CPU decoder on this host's cores, on a bounded sample (rank 0, N=1)."""
+    from ivonar_inference_b200 import synthetic
+
+    decoder, threads, label = reference_cpu_decoder(model)
+    reference_cpu_rate(decoder, synthetic.random_prompt(32768, PROMPT, seed=98), 4)  # numba warm-up
+    seconds = reference_cpu_rate(decoder, synthetic.random_prompt(32768, PROMPT, seed=99), tokens)
+    return {"value": tokens / seconds, "unit": "tok/s", "cores": threads, "kind": "reference",
+            "cpu": host_cpu(),
+            "sample": f"config1 model, {PROMPT}-token prompt prefilled (untimed), {tokens} sampled decode tokens "
+                      f"timed; {label}, {threads} threads, from baseline/_ref",
             "seconds": seconds}
 
 
@@ -185,33 +235,81 @@ def run_reference(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    import torch
-
     from ivonar_inference_b200 import synthetic
 
+    tokens = int(args.tokens)
     model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0)
-    sample_tokens = 16
+    decoder, threads, label = reference_cpu_decoder(model)
     times = []
-    threads = 0
     for step in range(args.warmup + args.steps):
-        prompt = synthetic.random_prompt(32768, PROMPT, seed=100 + step)[0].numpy()
-        result = cpu_baseline(model, prompt, sample_tokens)
-        threads = result["cores"]
+        prompt = synthetic.random_prompt(32768, PROMPT, seed=100 + step)
+        seconds = reference_cpu_rate(decoder, prompt, tokens if step >= args.warmup else 8)
         if step >= args.warmup:
-            times.append(result["seconds"])
-    value = args.steps * sample_tokens / sum(times)
-    sample = (f"each step: config1 model, {PROMPT}-token prompt prefilled (untimed), {sample_tokens} sampled decode "
-              f"tokens timed; C port of the reference decode step, OpenMP {threads} threads")
+            times.append(seconds)
+    value = args.steps * tokens / sum(times)
+    sample = (f"each step: config1 model, {PROMPT}-token prompt prefilled (untimed), {tokens} sampled decode tokens "
+              f"timed (warm-up steps decode 8); {label}, {threads} threads, from baseline/_ref")
     line = {
         "impl": "reference", "metric": "decode tok/s (b=1)", "value": value, "unit": "tok/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000 * sum(times) / len(times),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
         "data": "synthetic", "config": {"workload": WORKLOAD, "runs_on": "host CPU"},
-        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "port", "sample": sample},
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample,
+                         "cpu": host_cpu()},
         "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
-    del torch
+
+
+def api_decode_rate(decoder, prompt, tokens: int) -> float:
+    """Decode tok/s through the reference decoder API: prefill, configure_sampling, sample and 16 warm
+    tokens untimed, then CUDA events around the advance_many bursts that produce `tokens` tokens."""
+    import torch
+
+    decoder.prefill(prompt)
+    decoder.configure_sampling(TEMPERATURE, TOP_K, PENALTY)
+    decoder.sample()
+    decoder.advance_many(16)
+    torch.cuda.synchronize(decoder.device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    done = 0
+    while done < tokens:
+        done += len(decoder.advance_many(min(decoder.burst_size, tokens - done)))
+    end.record()
+    torch.cuda.synchronize(decoder.device)
+    return tokens / (start.elapsed_time(end) / 1000.0)
+
+
+def gpu_reference(device, tokens: int) -> dict:
+    """The reference KernelDecoder and B200Decoder on this GPU, timed by the same procedure."""
+    import torch
+
+    reference_environment()
+    from ivonar_inference_b200 import B200Decoder, _reference, synthetic
+
+    model = synthetic.synthetic_model(synthetic.config1(seq_len=2048), seed=0).to(device)
+    prompt = synthetic.random_prompt(32768, PROMPT, seed=4242).to(device)
+    max_len = PROMPT + tokens + 64
+    out: dict = {"procedure": f"{PROMPT}-token prompt, then {tokens} sampled tokens through advance_many bursts "
+                              "(CUDA events), reference decoder API", "unit": "tok/s"}
+    try:
+        kernel_decoder = _reference.module("kernel_decoder").KernelDecoder
+        ref = kernel_decoder(model, max_len=max_len, device=device, sampling=True)
+        ref.self_check()
+        out["reference_kernel_decoder"] = {"eager": api_decode_rate(ref, prompt, tokens)}
+        out["reference_kernel_decoder"]["graph_captured"] = bool(ref.capture())
+        out["reference_kernel_decoder"]["graph"] = max(api_decode_rate(ref, prompt, tokens) for _ in range(2))
+        out["reference_kernel_decoder"]["burst"] = int(ref.burst_size)
+        del ref
+    except Exception as exc:  # the reference's NVRTC build can be missing on a box
+        out["reference_kernel_decoder"] = {"unavailable": f"{type(exc).__name__}: {exc}"[:300]}
+    torch.cuda.empty_cache()
+    ours = B200Decoder(model, max_len=max_len, device=device, sampling=True, seed=5)
+    ours.capture()
+    out["b200_decoder"] = {"graph": max(api_decode_rate(ours, prompt, tokens) for _ in range(2)),
+                           "burst": int(ours.burst_size)}
+    return out
 
 
 INT8_NOMINAL_TOPS = 4500.0  # B200 dense int8 tensor-core peak (nominal)
@@ -468,7 +566,7 @@ def run_b200(args) -> None:
         achieved = nbytes / launch_s / 1e9
         roofline = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                     "traffic": NCU_DRAM_BYTES_PER_TOKEN * tokens, "traffic_source": TRAFFIC_SOURCE,
-                    "peak_source": peak_kind, "kernel": "ivb::cluster_decode_kernel",
+                    "peak_source": peak_kind, "kernel": "ivb::grid_decode_kernel",
                     "algorithmic_bytes_per_launch": nbytes, **parts}
         line = {
             "metric": "decode tok/s (b=1)", "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -487,9 +585,10 @@ def run_b200(args) -> None:
             line["tp"] = tp_line
         if not args.no_prefill:
             line["prefill"] = prefill_measure(device)
+        if not args.no_gpu_reference:
+            line["gpu_reference"] = gpu_reference(device, tokens)
         if world == 1 and not args.no_cpu_baseline:
-            prompt = synthetic.random_prompt(32768, PROMPT, seed=99)[0].numpy()
-            line["cpu_baseline"] = cpu_baseline(model, prompt, 32)
+            line["cpu_baseline"] = cpu_baseline(model, 32)
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

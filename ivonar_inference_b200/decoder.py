@@ -495,10 +495,21 @@ class B200Decoder(StaticDecoder):
             raise KernelError("the B200 sampler returned an invalid token on this GPU")
 
 
+def kernel_decoder(model, target: torch.device, sampling: bool, max_top_k: int) -> tuple[B200Decoder, str | None]:
+    """Drop-in for the reference's CUDA slot ``_kernel_decoder(model, target, sampling, max_top_k)``
+    (decoder.py:518-529): a self-checked decoder and no note (prompts always run through the tensor-core
+    prefill, so no torch weights are materialised). Binding it there makes the reference's build_decoder,
+    Engine.load, verify_model and run_benchmark serve B200Decoder."""
+
+    decoder = B200Decoder(model, device=target, sampling=sampling, max_top_k=max_top_k)
+    decoder.self_check()
+    return decoder, None
+
+
 def build_decoder(model, device: str | torch.device, sampling: bool = False, max_top_k: int = 256,
                   kernels: bool = True) -> tuple[object, str, str | None]:
     """The decoder the engine serves (reference decoder.py:479-507 with its CUDA kernel slot,
-    ``_kernel_decoder`` at :518-529, filled by B200Decoder).
+    ``_kernel_decoder`` at :518-529, filled by ``kernel_decoder``).
 
     CUDA with kernels: a self-checked B200Decoder, backend "ternary". When it cannot run there, or for
     any other device, the reference's own ``build_decoder`` decides (its numba CPU decoder or its torch
@@ -509,9 +520,8 @@ def build_decoder(model, device: str | torch.device, sampling: bool = False, max
     reference_build = _reference.module("decoder").build_decoder
     if kernels and target.type == "cuda":
         try:
-            decoder = B200Decoder(model, device=target, sampling=sampling, max_top_k=max_top_k)
-            decoder.self_check()
-            return decoder, "ternary", None
+            decoder, note = kernel_decoder(model, target, sampling, max_top_k)
+            return decoder, "ternary", note
         except Exception as exc:
             note = f"B200 ternary kernels unavailable, using the torch decoder: {exc}"
         decoder, backend, _ = reference_build(model, target, sampling=sampling, max_top_k=max_top_k, kernels=False)
