@@ -49,12 +49,13 @@ struct TileBuf {
 };
 
 __device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const DecodeDims& D, int b) {
-  const size_t one = round16(D.tile * D.lpad) + round16(D.tile * 4) + round16(D.tile * D.rpad * 2);
+  const int rows = D.tile + 1;  // the last tile also holds the current position
+  const size_t one = round16(rows * D.lpad) + round16(rows * 4) + round16(rows * D.rpad * 2);
   unsigned char* t = base + b * one;
   TileBuf tb;
   tb.lat = reinterpret_cast<int8_t*>(t);
-  tb.lsc = reinterpret_cast<float*>(t + round16(D.tile * D.lpad));
-  tb.kr = reinterpret_cast<uint16_t*>(t + round16(D.tile * D.lpad) + round16(D.tile * 4));
+  tb.lsc = reinterpret_cast<float*>(t + round16(rows * D.lpad));
+  tb.kr = reinterpret_cast<uint16_t*>(t + round16(rows * D.lpad) + round16(rows * 4));
   return tb;
 }
 
@@ -358,15 +359,19 @@ struct Ctx {
 
 // Shared-memory layout of the attention op inside the union region (the plan sizes it the same way):
 // current latent codes [round64(latent)] | qa [round32(latent)] | qr, krc [rope] | qn [nope] |
-// u [round32(latent)] | scores [tile + 4] | 16-byte aligned double tile buffer.
+// u [round32(latent)] | scores [tile + 4] | partial sums [1024] | 16-byte aligned double tile buffer
+// (each buffer tile + 1 rows: the last tile also holds the current position).
 struct AttnSmem {
   int8_t* qlc;
-  float *qa, *qr, *krc, *qn, *u, *sc;
+  float *qa, *qr, *krc, *qn, *u, *sc, *scr;
   unsigned char* tiles;
 };
+constexpr int kAttnScratch = 1024;  // floats of partial sums (absorbed query)
+// every array starts on a 16-byte boundary (qa and u are read as float4)
+__host__ __device__ __forceinline__ int r4(int n) { return (n + 3) & ~3; }
 __host__ __device__ __forceinline__ size_t attn_fixed_bytes(int latent, int rope, int nope, int tile) {
   const int l64 = (latent + 63) / 64 * 64, l32 = (latent + 31) / 32 * 32;
-  return round16(l64) + static_cast<size_t>(2 * l32 + 2 * rope + nope + tile + 4) * 4 + 16;
+  return round16(l64) + static_cast<size_t>(2 * l32 + 2 * r4(rope) + r4(nope) + r4(tile + 4) + kAttnScratch) * 4 + 16;
 }
 __device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims& D) {
   const int l64 = (D.latent + 63) / 64 * 64, l32 = (D.latent + 31) / 32 * 32;
@@ -374,17 +379,144 @@ __device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims
   a.qlc = reinterpret_cast<int8_t*>(U);
   a.qa = reinterpret_cast<float*>(U + round16(l64));
   a.qr = a.qa + l32;
-  a.krc = a.qr + D.rope;
-  a.qn = a.krc + D.rope;
-  a.u = a.qn + D.nope;
+  a.krc = a.qr + r4(D.rope);
+  a.qn = a.krc + r4(D.rope);
+  a.u = a.qn + r4(D.nope);
   a.sc = a.u + l32;
-  unsigned char* t = reinterpret_cast<unsigned char*>(a.sc + D.tile + 4);
+  a.scr = a.sc + r4(D.tile + 4);
+  unsigned char* t = reinterpret_cast<unsigned char*>(a.scr + kAttnScratch);
   a.tiles = t + ((16 - (reinterpret_cast<uintptr_t>(t) & 15)) & 15);
   return a;
 }
-// (code - 1) of input j of a packed row
-__device__ __forceinline__ float code_m1(const unsigned char* row, int j) {
-  return static_cast<float>(((row[j >> 2] >> ((j & 3) << 1)) & 3) - 1);
+
+// The tile loop of the attention op: online softmax over the cached positions, tile by tile, the current
+// position as the extra last row of the last tile. Scores: a thread pair per position, thread h taking the
+// 16-byte chunks of the row with parity h, rotated by the position so that the 8 lanes of a shared-memory
+// phase read 8 different banks groups. Weighted latent sum: lane group g = lane / 8 of warp w takes the
+// positions 4w + g + 32i, lane s = lane % 8 owns the chunks s, s + 8, ... (CPL of them, 16 latent
+// entries each) in registers. Returns false when a tile's wait ran out; m_run, l_run and the per-lane
+// partial sums `acc` (scaled by exp(-m_run)) are the results.
+template <int CPL>
+__device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const DecodeDims& D, const IvbLayerDesc& L,
+                                           const AttnSmem& A, int h, int P, float a_cur, float qb, float& m_run,
+                                           float& l_run, float (&acc)[16 * CPL]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sub = lane & 7, grp = lane >> 3;
+  const int lc = D.lpad >> 4;  // 16-byte chunks per cached row (<= 8 * CPL)
+  const bool pow2 = (lc & (lc - 1)) == 0;
+  const int rope = D.rope, rpad = D.rpad, lpad = D.lpad, tile = D.tile;
+  float* const red = c.red;
+  unsigned long long* const abar = c.abar;
+  const int n_tiles = P == 0 ? 1 : (P + tile - 1) / tile;
+  bool ok = true;
+#pragma unroll
+  for (int i = 0; i < 16 * CPL; ++i) acc[i] = 0.0f;
+  m_run = -INFINITY;
+  l_run = 0.0f;
+  for (int ti = 0; ti < n_tiles; ++ti) {
+    const int start = ti * tile;
+    const int count = max(0, min(tile, P - start));
+    const bool last = ti == n_tiles - 1;
+    const TileBuf tb = tile_buf(A.tiles, D, ti & 1);
+    if (tid == 0 && !last)
+      tile_issue(L, D, tile_buf(A.tiles, D, (ti + 1) & 1), h, start + tile, min(tile, P - start - tile), &abar[(ti + 1) & 1],
+                 p.error);
+    if (last) {
+      // the current position as row `count` (the bulk copy writes rows below it); its scale after the wait
+      for (int j = tid; j < lpad / 4; j += kThreads)
+        reinterpret_cast<unsigned*>(tb.lat + count * lpad)[j] = reinterpret_cast<const unsigned*>(A.qlc)[j];
+      for (int r = tid; r < rope; r += kThreads) tb.kr[count * rpad + r] = f2h(A.krc[r]);
+    }
+    if (count > 0) {
+      if (!tile_wait(&abar[ti & 1], c.apar[ti & 1], p.timeout_ns)) {
+        ok = false;
+        break;
+      }
+      if (tid == 0) c.apar[ti & 1] ^= 1u;  // every thread read it before the wait's barrier
+    }
+    if (last) {
+      if (tid == 0) tb.lsc[count] = a_cur;
+      __syncthreads();
+    }
+    const int npos = count + (last ? 1 : 0);
+    // scores
+    float wmax = -INFINITY;
+    for (int k0 = 0; k0 < npos; k0 += kThreads / 2) {
+      const int k = k0 + (tid >> 1), hh = tid & 1;
+      float s = -INFINITY, dot = 0.0f;
+      if (k < npos) {
+        const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
+        const int skew = pow2 ? ((2 * k) & (lc - 1)) : 0;
+        float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+        for (int i = 0; i < 4 * CPL; ++i) {
+          if (2 * i + hh < lc) {
+            const int ch = pow2 ? ((2 * i + hh + skew) & (lc - 1)) : 2 * i + hh;
+            const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * ch);
+            const float4* q = reinterpret_cast<const float4*>(A.qa + 16 * ch);
+            const unsigned wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+            for (int t = 0; t < 4; ++t) {
+              const float4 qq = q[t];
+              float f[4];
+              bytes_to_f32(wv[t], f);
+              d0 = fmaf(qq.x, f[0], d0);
+              d1 = fmaf(qq.y, f[1], d1);
+              d2 = fmaf(qq.z, f[2], d2);
+              d3 = fmaf(qq.w, f[3], d3);
+            }
+          }
+        }
+        dot = (d0 + d1) + (d2 + d3);
+      }
+      dot += __shfl_xor_sync(kFull, dot, 1);  // both threads of a pair are in or out of range together
+      if (k < npos) {
+        float rp = 0.0f;
+        for (int r = 0; r < rope; ++r) rp = fmaf(A.qr[r], h2f(tb.kr[k * rpad + r]), rp);
+        s = fmaf(tb.lsc[k], dot, rp) + qb;
+        if (hh == 0) A.sc[k] = s;
+      }
+      wmax = fmaxf(wmax, s);
+    }
+    wmax = warp_max(wmax);
+    if (lane == 0) red[32 + warp] = wmax;  // block_sum below uses red[0 .. kWarps)
+    __syncthreads();
+    float mx = red[32];
+    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red[32 + w]);
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+    float ls = 0.0f;
+    for (int k = tid; k < npos; k += kThreads) {
+      const float e = expf(A.sc[k] - m_new);
+      A.sc[k] = e * tb.lsc[k];  // softmax weight times the latent scale
+      ls += e;
+    }
+    ls = block_sum(ls, red);  // its barrier also orders the weights above before the sums below
+    l_run = l_run * corr + ls;
+#pragma unroll
+    for (int i = 0; i < 16 * CPL; ++i) acc[i] *= corr;
+    // weighted latent sum
+    for (int k = 4 * warp + grp; k < npos; k += 4 * kWarps) {
+      const float wk = A.sc[k];
+      const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
+#pragma unroll
+      for (int j = 0; j < CPL; ++j) {
+        if (sub + 8 * j < lc) {
+          const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * (sub + 8 * j));
+          const unsigned wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            float f[4];
+            bytes_to_f32(wv[t], f);
+#pragma unroll
+            for (int b = 0; b < 4; ++b) acc[16 * j + 4 * t + b] = fmaf(wk, f[b], acc[16 * j + 4 * t + b]);
+          }
+        }
+      }
+    }
+    m_run = m_new;
+    __syncthreads();  // the tile buffer and the weights are reused
+  }
+  return ok;
 }
 
 // Latent attention of head h over the compressed cache, absorbed form, after the head's q, the latent
@@ -393,9 +525,9 @@ __device__ __forceinline__ float code_m1(const unsigned char* row, int j) {
 //   score_t = a_t <qa, ql_t> + <q_rope, k_rope_t> + q_nope.b_k     (qa = W_k^T q_nope)
 //   out     = W_v (sum_t p_t a_t ql_t) / l + b_v
 // The latent of this position is quantised and appended to the cache, the rotated k_rope of the head
-// too; every attention CTA writes the same latent bytes, so each one later reads cache rows it wrote
-// itself. Cached positions arrive in tiles by bulk copy (double buffered), the current one is scored
-// from shared memory; the caller issues the first tile before this call. Publishes the head's outputs.
+// too (fp16, as the position's own score uses it); every attention CTA writes the same latent bytes, so
+// each one later reads cache rows it wrote itself. Cached positions arrive in tiles by bulk copy (double
+// buffered); the caller issues the first tile before this call. Publishes the head's outputs.
 // `chunk`: the op's constants chunk in the ring.
 static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
@@ -407,23 +539,22 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
   int8_t* const lat_q = L.latent_q;
   float* const lat_s = L.latent_scale;
   uint16_t* const kr_cache = L.k_rope_cache;
-  const bool kn_bias = L.k_nope_up.bias != nullptr, v_bias = L.v_up.bias != nullptr;
   float* const red = c.red;
   float* const stg = c.stg;
-  unsigned long long* const abar = c.abar;
   const unsigned flag = c.flag;
-  const int tid = threadIdx.x, sub = tid & 7, grp = tid >> 3;
-  const int Lt = D.latent, l32 = (Lt + 31) / 32 * 32;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int Lt = D.latent, nope = D.nope, hd = D.head_dim, rb = D.rb_lat, ss = D.ss_lat;
   const int P = static_cast<int>(c.pos);
   bool ok = true;
   const unsigned char* cst = stream_acquire(p, c.st, chunk);
   if (__syncthreads_or(cst == nullptr)) ok = false;
   const AttnSmem A = attn_smem(c.U, D);
   const float* qh = c.xl;                 // gathered q of the head
-  const float* lat = c.xl + D.head_dim;   // the latent
+  const float* lat = c.xl + hd;           // the latent
   const float* kh = lat + Lt;             // k_rope of the head
   const float a_cur = quantize_ni(lat, Lt, nullptr, 0.0f, 0.0f, D.act_eps, A.qlc, false, nullptr, red);
   for (int j = tid; j < Lt; j += kThreads) lat_q[static_cast<size_t>(P) * D.lpad + j] = A.qlc[j];
+  for (int j = Lt + tid; j < D.lpad; j += kThreads) A.qlc[j] = 0;  // the row's padding (read as whole chunks)
   if (tid == 0) lat_s[P] = a_cur;
   const float scl = L.attn_scale;
   cp_async_wait_all();  // the rope row of this position
@@ -431,7 +562,7 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
   c.tick(0);
   for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
     const float cs = c.rope_s[2 * jr], sn = c.rope_s[2 * jr + 1];
-    const float q0 = qh[D.nope + 2 * jr], q1 = qh[D.nope + 2 * jr + 1];
+    const float q0 = qh[nope + 2 * jr], q1 = qh[nope + 2 * jr + 1];
     const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
     A.qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
     A.qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
@@ -442,165 +573,124 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
     kc[2 * jr] = f2h(kr0);
     kc[2 * jr + 1] = f2h(kr1);
   }
-  for (int e = tid; e < D.nope; e += kThreads) A.qn[e] = qh[e] * scl;
-  // cached positions 0..P-1 in tiles, then the current one
-  const int lo = 0, cached = P;
-  const bool has_cur = true;
-  const int n_tiles = cached == 0 ? 1 : (cached + D.tile - 1) / D.tile;
-  // the first tile (positions 0 .. min(P, tile) - 1) was issued before the op's input arrived
+  for (int e = tid; e < nope; e += kThreads) A.qn[e] = qh[e] * scl;
   __syncthreads();
-  // absorbed query qa[j] = sum_e qn[e] * W_knope[h][e][j] (weights from the constants chunk)
-  const unsigned char* wkn = cst + c_wkn;
-  const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + c_skn);
-  for (int j = tid; j < l32; j += kThreads) {
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};  // independent chains over e (e mod 4), added in order
-    if (j < Lt) {
-      const int sh = (j & 3) << 1, bj = j >> 2, gj = j >> 7;
-      int e = 0;
-      for (; e + 4 <= D.nope; e += 4)
+  float qb;  // q_nope . b_k
+  // absorbed query qa[j] = sum_e qn[e] s[e] (W_knope[h][e][j]): thread (byte jb, group eg) takes the four
+  // latent entries of packed byte jb over the rows e = eg, eg + G, ...; the G group sums are added in order
+  {
+    const int nb = (Lt + 3) >> 2, G = kThreads / nb;
+    const unsigned char* wkn = cst + c_wkn;
+    const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + c_skn);
+    const int jb = tid % nb, eg = tid / nb;
+    if (eg < G) {
+      float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int e = eg; e < nope; e += G) {
+        const int byte = wkn[e * rb + jb];
+        const float q = A.qn[e] * h2f(skn[e * ss + (jb >> 5)]);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int ee = e + q;
-          const float cm = static_cast<float>(((wkn[ee * D.rb_lat + bj] >> sh) & 3) - 1);
-          acc[q] = fmaf(A.qn[ee], cm * h2f(skn[ee * D.ss_lat + gj]), acc[q]);
-        }
-      for (; e < D.nope; ++e)
-        acc[0] = fmaf(A.qn[e], static_cast<float>(((wkn[e * D.rb_lat + bj] >> sh) & 3) - 1) * h2f(skn[e * D.ss_lat + gj]), acc[0]);
+        for (int f = 0; f < 4; ++f) a4[f] = fmaf(q, static_cast<float>(((byte >> (2 * f)) & 3) - 1), a4[f]);
+      }
+#pragma unroll
+      for (int f = 0; f < 4; ++f) A.scr[eg * 4 * nb + 4 * jb + f] = a4[f];
     }
-    A.qa[j] = (acc[0] + acc[1]) + (acc[2] + acc[3]);  // zero beyond the latent width (the score loop reads whole words)
-  }
-  float qb = 0.0f;
-  if (kn_bias) {
-    const float* bkn = reinterpret_cast<const float*>(cst + c_bkn);
     float pp = 0.0f;
-    for (int e = tid; e < D.nope; e += kThreads) pp = fmaf(A.qn[e], bkn[e], pp);
-    qb = block_sum(pp, red);
-  } else {
-    __syncthreads();
+    const float* bkn = reinterpret_cast<const float*>(cst + c_bkn);
+    for (int e = tid; e < nope; e += kThreads) pp = fmaf(A.qn[e], bkn[e], pp);
+    qb = block_sum(pp, red);  // its barrier also orders the partial sums above
+    const int l32 = (Lt + 31) / 32 * 32;
+    for (int j = tid; j < l32; j += kThreads) {
+      float s = 0.0f;
+      if (j < Lt)
+        for (int g = 0; g < G; ++g) s += A.scr[g * 4 * nb + j];
+      A.qa[j] = s;  // zero beyond the latent width (the score loop reads whole chunks)
+    }
   }
+  __syncthreads();
   c.tick(1);
-  // online softmax over the tiles, the current position last
-  float m_run = -INFINITY, l_run = 0.0f, u0 = 0.0f, u1 = 0.0f;
-  for (int ti = 0; ti < n_tiles; ++ti) {
-    const int start = lo + ti * D.tile;
-    const int count = max(0, min(D.tile, lo + cached - start));
-    const bool last = ti == n_tiles - 1;
-    const TileBuf tb = tile_buf(A.tiles, D, ti & 1);
-    if (tid == 0 && ti + 1 < n_tiles && count == D.tile && start + D.tile < lo + cached)
-      tile_issue(L, D, tile_buf(A.tiles, D, (ti + 1) & 1), h, start + D.tile, min(D.tile, lo + cached - start - D.tile),
-                 &abar[(ti + 1) & 1], p.error);
-    if (count > 0) {
-      if (!tile_wait(&abar[ti & 1], c.apar[ti & 1], p.timeout_ns)) {
-        ok = false;
-        break;
-      }
-      if (tid == 0) c.apar[ti & 1] ^= 1u;  // every thread read it before the wait's barrier
-    }
-    const int npos = count + (last && has_cur ? 1 : 0);
-    // scores: 8 lanes per position, lane `sub` takes latent words sub, sub + 8, ... and rope entries sub, sub + 8, ...
-#pragma unroll 1
-    for (int k0 = 0; k0 < npos; k0 += kThreads / 8) {
-      const int k = k0 + grp;
-      const bool valid = k < npos, cur = k == count;
-      const int8_t* ql = cur ? A.qlc : tb.lat + (valid ? k : 0) * D.lpad;
-      float dot = 0.0f, rp = 0.0f;
-      if (valid) {
-        float dot1 = 0.0f;
-#pragma unroll 2
-        for (int i = 4 * sub; i < Lt; i += 32) {
-          float f[4];
-          bytes_to_f32(*reinterpret_cast<const unsigned*>(ql + i), f);
-          const float4 q = *reinterpret_cast<const float4*>(A.qa + i);
-          dot = fmaf(q.x, f[0], fmaf(q.y, f[1], dot));
-          dot1 = fmaf(q.z, f[2], fmaf(q.w, f[3], dot1));
-        }
-        dot += dot1;
-        for (int r = sub; r < D.rope; r += 8) rp = fmaf(A.qr[r], cur ? A.krc[r] : h2f(tb.kr[k * D.rpad + r]), rp);
-      }
-      float total = valid ? fmaf(cur ? a_cur : tb.lsc[k], dot, rp) : 0.0f;
-      total += __shfl_xor_sync(kFull, total, 4);
-      total += __shfl_xor_sync(kFull, total, 2);
-      total += __shfl_xor_sync(kFull, total, 1);
-      if (valid && sub == 0) A.sc[k] = total + qb;
-    }
-    __syncthreads();
-    float mx = -INFINITY;
-    for (int k = tid; k < npos; k += kThreads) mx = fmaxf(mx, A.sc[k]);
-    mx = block_max(mx, red);
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-    float ls = 0.0f;
-    for (int k = tid; k < npos; k += kThreads) {
-      const float e = expf(A.sc[k] - m_new);
-      A.sc[k] = e * (k == count ? a_cur : tb.lsc[k]);  // softmax weight times the latent scale
-      ls += e;
-    }
-    ls = block_sum(ls, red);  // its barrier also orders the weights above before the sums below
-    l_run = l_run * corr + ls;
-    u0 *= corr;
-    u1 *= corr;
-    // weighted latent sum: thread j owns latent entries j and j + 256; even and odd positions in
-    // separate chains, added at the end of the tile
-    {
-      float v0 = 0.0f, v1 = 0.0f, w0 = 0.0f, w1 = 0.0f;
-      const bool in0 = tid < Lt, in1 = tid + kThreads < Lt;
-#pragma unroll 2
-      for (int k = 0; k < npos; k += 2) {
-        const int8_t* qa0 = k == count ? A.qlc : tb.lat + k * D.lpad;
-        const float wa = A.sc[k];
-        const bool has_b = k + 1 < npos;
-        const int8_t* qb0 = k + 1 == count ? A.qlc : tb.lat + (has_b ? k + 1 : k) * D.lpad;
-        const float wb = has_b ? A.sc[k + 1] : 0.0f;
-        if (in0) {
-          v0 = fmaf(wa, static_cast<float>(qa0[tid]), v0);
-          w0 = fmaf(wb, static_cast<float>(qb0[tid]), w0);
-        }
-        if (in1) {
-          v1 = fmaf(wa, static_cast<float>(qa0[tid + kThreads]), v1);
-          w1 = fmaf(wb, static_cast<float>(qb0[tid + kThreads]), w1);
-        }
-      }
-      u0 += v0 + w0;
-      u1 += v1 + w1;
-    }
-    m_run = m_new;
-    __syncthreads();  // the tile buffer and the weights are reused
+  float m_run, l_run;
+  float u_acc[16 * kMaxLatentPerLane / 16 * 4];
+  const int lc = D.lpad >> 4;
+  bool tiles_ok;
+  if (lc <= 8) {
+    float acc[16];
+    tiles_ok = attn_tiles<1>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) u_acc[i] = acc[i];
+  } else if (lc <= 16) {
+    float acc[32];
+    tiles_ok = attn_tiles<2>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) u_acc[i] = acc[i];
+  } else {
+    float acc[64];
+    tiles_ok = attn_tiles<4>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) u_acc[i] = acc[i];
   }
+  ok &= tiles_ok;
   c.tick(2);
   if (ok) {
-    if (tid < l32) A.u[tid] = tid < Lt ? u0 : 0.0f;
-    if (tid + kThreads < l32) A.u[tid + kThreads] = tid + kThreads < Lt ? u1 : 0.0f;
+    // the four lane groups of a warp hold the same chunks: add them, then the warps' sums in warp order
+    const int sub = lane & 7, cpl = (lc + 7) >> 3;
+    float* part = reinterpret_cast<float*>(A.tiles);  // [kWarps][lpad] (both tile buffers are free now)
+#pragma unroll
+    for (int j = 0; j < kMaxLatentPerLane / 4; ++j) {
+      if (j < cpl) {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          float v = u_acc[16 * j + e];
+          v += __shfl_xor_sync(kFull, v, 8);
+          v += __shfl_xor_sync(kFull, v, 16);
+          if (lane < 8 && sub + 8 * j < lc) part[warp * D.lpad + 16 * (sub + 8 * j) + e] = v;
+        }
+      }
+    }
     __syncthreads();
-    // out[e] = W_v[h][e] . u / l + b_v[h][e] (four lanes per output, lane q taking a quarter of the latent)
+    for (int j = tid; j < D.lpad; j += kThreads) {
+      float s = 0.0f;
+      for (int w = 0; w < kWarps; ++w) s += part[w * D.lpad + j];
+      A.u[j] = j < Lt ? s : 0.0f;
+    }
+    __syncthreads();
+    // out[e] = s[e] (W_v[h][e] . u) / l + b_v[e]: LP lanes per output, lane q taking the packed words
+    // q, q + LP, ... of the row (16 latent entries, one scale group each)
     const unsigned char* wv = cst + c_wv;
     const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + c_sv);
     const float* bv = reinterpret_cast<const float*>(cst + c_bv);
     const float inv_l = 1.0f / l_run;
-    const int q4 = tid & 3;
-    for (int e0 = 0; e0 < D.head_dim; e0 += kThreads / 4) {
-      const int e = e0 + (tid >> 2);
-      float acc = 0.0f;
-      if (e < D.head_dim) {
-        // lane q4 takes the packed bytes q4, q4 + 4, ... of the row (4 inputs each), four chains
-        const unsigned char* row = wv + e * D.rb_lat;
-        float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        for (int b4 = q4; 4 * b4 < Lt; b4 += 4) {
-          const int byte = row[b4];  // signed: (code & 3) - 1 must reach -1
-          const float sc = h2f(sv[e * D.ss_lat + (b4 >> 5)]);
+    int LP = 32;
+    while (LP > 1 && LP * hd > kThreads) LP >>= 1;
+    const int q = tid & (LP - 1), nw = (Lt + 15) >> 4;
+    for (int e0 = 0; e0 < hd; e0 += kThreads / LP) {
+      const int e = e0 + tid / LP;
+      float acc0 = 0.0f, acc1 = 0.0f;
+      if (e < hd) {
+        const unsigned* row = reinterpret_cast<const unsigned*>(wv + e * rb);
+        for (int w = q; w < nw; w += LP) {
+          const unsigned bits = row[w];
+          const float4* uu = reinterpret_cast<const float4*>(A.u + 16 * w);
+          float t0 = 0.0f, t1 = 0.0f;
 #pragma unroll
-          for (int f = 0; f < 4; ++f) {
-            const int j = 4 * b4 + f;
-            if (j < Lt) a4[f] = fmaf(static_cast<float>(((byte >> (2 * f)) & 3) - 1) * sc, A.u[j], a4[f]);
+          for (int t = 0; t < 4; ++t) {
+            const float4 u4 = uu[t];
+            const unsigned b = bits >> (8 * t);
+            t0 = fmaf(static_cast<float>(static_cast<int>(b & 3u) - 1), u4.x, t0);
+            t1 = fmaf(static_cast<float>(static_cast<int>((b >> 2) & 3u) - 1), u4.y, t1);
+            t0 = fmaf(static_cast<float>(static_cast<int>((b >> 4) & 3u) - 1), u4.z, t0);
+            t1 = fmaf(static_cast<float>(static_cast<int>((b >> 6) & 3u) - 1), u4.w, t1);
           }
+          const float sc = h2f(sv[e * ss + (w >> 3)]);
+          if (w & 1) acc1 = fmaf(sc, t0 + t1, acc1);
+          else acc0 = fmaf(sc, t0 + t1, acc0);
         }
-        acc = (a4[0] + a4[1]) + (a4[2] + a4[3]);
       }
-      acc += __shfl_xor_sync(kFull, acc, 1);
-      acc += __shfl_xor_sync(kFull, acc, 2);
-      if (e < D.head_dim && q4 == 0) stg[e] = acc * inv_l + (v_bias ? bv[e] : 0.0f);
+      float acc = acc0 + acc1;
+      for (int o = 1; o < LP; o <<= 1) acc += __shfl_xor_sync(kFull, acc, o);
+      if (e < hd && q == 0) stg[e] = acc * inv_l + bv[e];
     }
     __syncthreads();
-    ll_put(p.ll + ll_out, h * D.head_dim, stg, D.head_dim, flag);
+    ll_put(p.ll + ll_out, h * hd, stg, hd, flag);
     c.tick(3);
   }
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -1574,22 +1664,22 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     plans.back().out_words = 2 * ng * kq;
   }
   u_need = std::max(u_need, static_cast<size_t>(M.cand) + r16(cap_c * 8));
-  const size_t per_pos = static_cast<size_t>(D.lpad) + 4 + static_cast<size_t>(D.rpad) * 2;
   bool any_mla = false;
   for (const IvbLayerDesc& L : dec->layers) any_mla |= L.kind == IVB_MLA;
   int tile = 0;
   if (any_mla) {
-    const size_t fixed = attn_fixed_bytes(Lt, D.rope, D.nope, 0);
-    const size_t troom = room > fixed ? room - fixed : 0;
-    tile = static_cast<int>(troom / (2 * per_pos + 8)) / 16 * 16;
-    tile = std::min(tile, (md.max_len + 15) / 16 * 16);
+    // two tile buffers of tile + 1 rows (the last tile also holds the current position)
+    auto attn_bytes = [&](int t) {
+      const size_t rows = static_cast<size_t>(t) + 1;
+      return attn_fixed_bytes(Lt, D.rope, D.nope, t) + 2 * (r16(rows * D.lpad) + r16(rows * 4) + r16(rows * D.rpad * 2));
+    };
+    tile = std::min(256, (md.max_len + 15) / 16 * 16);
+    while (tile >= 16 && attn_bytes(tile) > room) tile -= 16;
     if (tile < 16) {
       why = "no room for an attention tile in shared memory";
       return false;
     }
-    tile = std::min(tile, 256);
-    u_need = std::max(u_need, attn_fixed_bytes(Lt, D.rope, D.nope, tile) + 2 * (r16(static_cast<size_t>(tile) * D.lpad) +
-                                                                                 r16(tile * 4) + r16(static_cast<size_t>(tile) * D.rpad * 2)));
+    u_need = std::max(u_need, attn_bytes(tile));
   }
   D.tile = std::max(tile, 16);
   o += r16(u_need);
