@@ -311,8 +311,9 @@ struct ActChunk {
   int xsum;
 };
 
-// xsum == nullptr: the chunk sum of the codes is computed here (sixteen dp4a with ones).
-__device__ __forceinline__ ActChunk load_act_chunk(const int8_t* act, const int* xsum, int u) {
+// The chunk sum of the codes: xsum[u], or the two half sums xhalf[2u], xhalf[2u + 1], or (both null)
+// computed here with sixteen dp4a with ones.
+__device__ __forceinline__ ActChunk load_act_chunk(const int8_t* act, const int* xsum, int u, const int* xhalf = nullptr) {
   ActChunk c;
   const int rot = (u >> 1) & 3;
   const char* base = reinterpret_cast<const char*>(act) + (u << 6);
@@ -320,6 +321,8 @@ __device__ __forceinline__ ActChunk load_act_chunk(const int8_t* act, const int*
   for (int k = 0; k < 4; ++k) c.q[k] = *reinterpret_cast<const int4*>(base + (((k + rot) & 3) << 4));
   if (xsum != nullptr) {
     c.xsum = xsum[u];
+  } else if (xhalf != nullptr) {
+    c.xsum = xhalf[2 * u] + xhalf[2 * u + 1];
   } else {
     int t = 0;
 #pragma unroll
@@ -334,24 +337,10 @@ __device__ __forceinline__ ActChunk load_act_chunk(const int8_t* act, const int*
   return c;
 }
 
-// Exact integer sum over the chunk of (code - 1) * q8. The two-bit field f of every weight byte is
-// masked in place (value code << 2f) and dotted with the activations of field f; the four partial
-// sums are exact multiples of 1, 4, 16 and 64, so the shifts below are exact.
-__device__ __forceinline__ int chunk_dot_regs(const uint4 w, const ActChunk& a) {
-  const unsigned ws[4] = {w.x, w.y, w.z, w.w};
-  int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
-#pragma unroll
-  for (int k = 0; k < 4; ++k) {
-    s0 = dp4a_us(ws[k] & 0x03030303u, a.q[k].x, s0);
-    s1 = dp4a_us(ws[k] & 0x0C0C0C0Cu, a.q[k].y, s1);
-    s2 = dp4a_us(ws[k] & 0x30303030u, a.q[k].z, s2);
-    s3 = dp4a_us(ws[k] & 0xC0C0C0C0u, a.q[k].w, s3);
-  }
-  return (s0 + (s1 >> 2)) + ((s2 >> 4) + (s3 >> 6)) - a.xsum;
-}
-
-// The same sum times 64, combined with shift-adds (64 s0 + 16 s1 + 4 s2 + s3 - 64 xsum); exact, and
-// the factor 64 is folded into the group scale by the caller (|result| < 2^23, so its float is exact).
+// 64 times the exact integer sum over the chunk of (code - 1) * q8. The two-bit field f of every weight
+// byte is masked in place (value code << 2f) and dotted with the activations of field f; the partial
+// sums are combined with shift-adds (64 s0 + 16 s1 + 4 s2 + s3 - 64 xsum), and the factor 64 is folded
+// into the group scale by the caller (|result| < 2^23, so its float is exact).
 __device__ __forceinline__ int chunk_dot64(const uint4 w, const ActChunk& a) {
   const unsigned ws[4] = {w.x, w.y, w.z, w.w};
   int s0 = 0, s1 = 0, s2 = 0, s3 = 0;
@@ -365,138 +354,22 @@ __device__ __forceinline__ int chunk_dot64(const uint4 w, const ActChunk& a) {
   return ((((s0 << 2) + s1) << 2) + s2) * 4 + s3 - (a.xsum << 6);
 }
 
-// rows [0, k) of a chunk laid out [k x row_bytes packed][k x scale_stride fp16 (16B pad)][k x fp32 bias]
-// Lane group of 2^lpr_log lanes per row; lane `sub` owns chunks sub + j * 2^lpr_log (j < KPL), whose
-// activations stay in registers for all rows. Every thread runs RPT rows per pass. Results of row r
-// go to out[r] (after the lane reduction).
-template <int KPL, int RPT>
-__device__ __forceinline__ void chunk_rows_kpl(const Op& op, const unsigned char* stage, int k, const int8_t* act,
-                                               const int* xsum, float act_scale, float* out) {
-  const int tid = threadIdx.x;
-  const int lg = op.lpr_log;
-  const int lpr = 1 << lg;
-  const int rpi = kThreads >> lg;
-  const int chunks = (op.in_n + 63) >> 6;
-  const int row_bytes = op.row_bytes, sstride = op.scale_stride;  // op lives in shared memory
-  const bool has_bias = op.has_bias != 0;
-  const int sub = tid & (lpr - 1);
-  ActChunk a[KPL];
-  bool have[KPL];
-#pragma unroll
-  for (int j = 0; j < KPL; ++j) {
-    const int u = sub + (j << lg);
-    have[j] = u < chunks;
-    if (have[j]) a[j] = load_act_chunk(act, nullptr, u);
-  }
-  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
-  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
-  for (int base = 0; base < k; base += RPT * rpi) {
-    int r[RPT];
-    bool v[RPT];
-    uint4 w[RPT][KPL];
-#pragma unroll
-    for (int t = 0; t < RPT; ++t) {
-      r[t] = base + t * rpi + (tid >> lg);
-      v[t] = r[t] < k;
-      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r[t]) * row_bytes);
-#pragma unroll
-      for (int j = 0; j < KPL; ++j) {
-        const int u = sub + (j << lg);
-        w[t][j] = (have[j] && v[t]) ? wr[u] : make_uint4(0u, 0u, 0u, 0u);
-      }
-    }
-    float acc[RPT];
-#pragma unroll
-    for (int t = 0; t < RPT; ++t) {
-      acc[t] = 0.0f;
-#pragma unroll
-      for (int j = 0; j < KPL; ++j) {
-        const int u = sub + (j << lg);
-        if (have[j] && v[t])
-          acc[t] = fmaf(static_cast<float>(chunk_dot_regs(w[t][j], a[j])), h2f(scales[r[t] * sstride + (u >> 1)]),
-                        acc[t]);
-      }
-    }
-    for (int off = 1; off < lpr; off <<= 1) {
-#pragma unroll
-      for (int t = 0; t < RPT; ++t) acc[t] += __shfl_xor_sync(kFull, acc[t], off);
-    }
-    if (sub == 0) {
-#pragma unroll
-      for (int t = 0; t < RPT; ++t)
-        if (v[t]) out[r[t]] = has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
-    }
-  }
-}
-
-// Compile-time lane geometry for the common shapes: LG = log2 lanes per row, KPL chunks per lane,
-// RPT rows per thread per pass. The lane's activation chunks (a, have) are loaded once per op by
-// load_act_ct and stay in registers for every stage of the op.
-template <int LG, int KPL>
-__device__ __forceinline__ void load_act_ct(const int8_t* act, int chunks, ActChunk (&a)[KPL], bool (&have)[KPL]) {
-  const int sub = threadIdx.x & ((1 << LG) - 1);
-#pragma unroll
-  for (int j = 0; j < KPL; ++j) {
-    const int u = sub + (j << LG);
-    have[j] = u < chunks;
-    if (have[j]) {
-      a[j] = load_act_chunk(act, nullptr, u);
-    } else {
-#pragma unroll
-      for (int q = 0; q < 4; ++q) a[j].q[q] = make_int4(0, 0, 0, 0);
-      a[j].xsum = 0;
-    }
-  }
-}
-
-template <int LG, int KPL, int RPT>
-__device__ __forceinline__ void rows_stage_ct(const ActChunk (&a)[KPL], const bool (&have)[KPL], const unsigned char* stage,
-                                              int k, int row_bytes, int sstride, bool has_bias, float act_scale, float* out) {
-  constexpr int LPR = 1 << LG, RPI = kThreads >> LG;
-  const int tid = threadIdx.x, sub = tid & (LPR - 1);
-  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
-  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
-  for (int base = 0; base < k; base += RPT * RPI) {
-    int r[RPT];
-    uint4 w[RPT][KPL];
-#pragma unroll
-    for (int t = 0; t < RPT; ++t) {
-      r[t] = base + t * RPI + (tid >> LG);
-      const uint4* wr = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(min(r[t], k - 1)) * row_bytes);
-#pragma unroll
-      for (int j = 0; j < KPL; ++j) w[t][j] = have[j] ? wr[sub + (j << LG)] : make_uint4(0u, 0u, 0u, 0u);
-    }
-    float acc[RPT];
-#pragma unroll
-    for (int t = 0; t < RPT; ++t) {
-      acc[t] = 0.0f;
-      const uint16_t* srow = scales + min(r[t], k - 1) * sstride;
-#pragma unroll
-      for (int j = 0; j < KPL; ++j) {
-        const float sc = have[j] ? h2f(srow[(sub + (j << LG)) >> 1]) * (1.0f / 64.0f) : 0.0f;
-        acc[t] = fmaf(static_cast<float>(chunk_dot64(w[t][j], a[j])), sc, acc[t]);
-      }
-    }
-#pragma unroll
-    for (int off = 1; off < LPR; off <<= 1)
-#pragma unroll
-      for (int t = 0; t < RPT; ++t) acc[t] += __shfl_xor_sync(kFull, acc[t], off);
-    if (sub == 0)
-#pragma unroll
-      for (int t = 0; t < RPT; ++t)
-        if (r[t] < k) out[r[t]] = has_bias ? acc[t] * act_scale + bias[r[t]] : acc[t] * act_scale;
-  }
-}
+// What rows_generic does with a finished row value v (row r of the chunk): store it to out[r] (shared,
+// for an epilogue that needs every row), or publish it as a flag word: resid[r] + v at ll[r] (out and
+// down projections), v at ll[r] (mla entry), or silu(v_r) * v_{r+1} at ll[r / 2] for even r (gate/up
+// rows interleaved; the two rows' lane groups sit in one warp, lg <= 4).
+enum RowsEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_PUBLISH = 2, EPI_SWIGLU = 3 };
 
 // Rows [0, k) of one stream chunk laid out [k x row_bytes packed][k x sstride fp16 (16B pad)][k x fp32
 // bias] against the quantised input `act` (transposed GEMV layout, in_n inputs): 2^lg lanes per row
 // (lg <= 5), lane `sub` owning the 64-input chunks sub + j * 2^lg (j < 4, so in_n <= 256 * 2^lg), their
 // activations held in registers; every row is one chain of fmaf over the lane's chunks followed by
-// an xor butterfly over the lanes. The plan picks lg per op so that the CTA's rows take one pass
-// where the registers allow. One small routine serves every GEMV of the decode kernel.
+// an xor butterfly over the lanes, then the epilogue `epi`. The plan picks lg per op so that the CTA's
+// rows take one pass where the registers allow. One small routine serves every GEMV of the decode kernel.
 constexpr int kRowsKPL = 4;
-static __device__ __noinline__ void rows_generic(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias,
-                                                 float act_scale, const int8_t* act, int in_n, int lg, float* out) {
+__device__ __forceinline__ void rows_generic(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias,
+                                             float act_scale, const int8_t* act, const int* xhalf, int in_n, int lg, float* out,
+                                             int epi, unsigned long long* ll, const float* resid, unsigned flag) {
   const int lpr = 1 << lg, rpi = kThreads >> lg;
   const int chunks = (in_n + 63) >> 6;
   const int sub = threadIdx.x & (lpr - 1);
@@ -508,7 +381,7 @@ static __device__ __noinline__ void rows_generic(const unsigned char* stage, int
     const int u = sub + (j << lg);
     have[j] = u < chunks;
     if (have[j]) {
-      a[j] = load_act_chunk(act, nullptr, u);
+      a[j] = load_act_chunk(act, nullptr, u, xhalf);
     } else {
 #pragma unroll
       for (int q = 0; q < 4; ++q) a[j].q[q] = make_int4(0, 0, 0, 0);
@@ -531,47 +404,17 @@ static __device__ __noinline__ void rows_generic(const unsigned char* stage, int
       if (have[j]) acc = fmaf(static_cast<float>(chunk_dot64(wr[u], a[j])), h2f(srow[u >> 1]) * (1.0f / 64.0f), acc);
     }
     for (int off = 1; off < lpr; off <<= 1) acc += __shfl_xor_sync(mask, acc, off);
-    if (sub == 0) out[r] = has_bias ? acc * act_scale + bias[r] : acc * act_scale;
-  }
-}
-
-// Fallback for inputs with more than three chunks per lane: activations re-read from shared memory,
-// chunk sums from xsum (the quantiser fills it for these ops).
-__device__ __forceinline__ void chunk_rows_wide(const Op& op, const unsigned char* stage, int k, const int8_t* act,
-                                                const int* xsum, float act_scale, float* out) {
-  const int tid = threadIdx.x;
-  const int lg = op.lpr_log;
-  const int lpr = 1 << lg;
-  const int rpi = kThreads >> lg;
-  const int chunks = (op.in_n + 63) >> 6;
-  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * op.row_bytes);
-  const float* bias =
-      reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * op.row_bytes + round16(k * op.scale_stride * 2));
-  const int sub = tid & (lpr - 1);
-  for (int base = 0; base < k; base += rpi) {
-    const int r = base + (tid >> lg);
-    float acc = 0.0f;
-    if (r < k) {
-      const uint4* wrow = reinterpret_cast<const uint4*>(stage + static_cast<size_t>(r) * op.row_bytes);
-      const uint16_t* srow = scales + r * op.scale_stride;
-#pragma unroll 2
-      for (int u = sub; u < chunks; u += lpr)
-        acc = fmaf(static_cast<float>(chunk_dot_regs(wrow[u], load_act_chunk(act, xsum, u))), h2f(srow[u >> 1]), acc);
+    const float v = has_bias ? acc * act_scale + bias[r] : acc * act_scale;
+    if (epi == EPI_SWIGLU) {
+      // rows r (gate, even) and r + 1 (up) are adjacent lane groups of one warp; k is even
+      const unsigned pmask = 2 * lpr >= 32 ? kFull : ((1u << (2 * lpr)) - 1u) << (threadIdx.x & 31 & ~(2 * lpr - 1));
+      const float up = __shfl_down_sync(pmask, v, lpr);
+      if (sub == 0 && (r & 1) == 0) ll_store(ll + (r >> 1), __float_as_uint(silu_f(v) * up), flag);
+    } else if (sub == 0) {
+      if (epi == EPI_STORE) out[r] = v;
+      else if (epi == EPI_RESID) ll_store(ll + r, __float_as_uint(resid[r] + v), flag);
+      else ll_store(ll + r, __float_as_uint(v), flag);
     }
-    for (int off = 1; off < lpr; off <<= 1) acc += __shfl_xor_sync(kFull, acc, off);
-    if (r < k && sub == 0) out[r] = op.has_bias ? acc * act_scale + bias[r] : acc * act_scale;
-  }
-}
-
-__device__ __forceinline__ void chunk_rows(const Op& op, const unsigned char* stage, int k, const int8_t* act, const int* xsum,
-                           float act_scale, float* out) {
-  const int chunks = (op.in_n + 63) >> 6;
-  const int kpl = (chunks + (1 << op.lpr_log) - 1) >> op.lpr_log;
-  switch (kpl) {
-    case 1: chunk_rows_kpl<1, 4>(op, stage, k, act, xsum, act_scale, out); break;
-    case 2: chunk_rows_kpl<2, 4>(op, stage, k, act, xsum, act_scale, out); break;
-    case 3: chunk_rows_kpl<3, 2>(op, stage, k, act, xsum, act_scale, out); break;
-    default: chunk_rows_wide(op, stage, k, act, xsum, act_scale, out); break;
   }
 }
 
@@ -726,10 +569,3 @@ static __device__ __noinline__ int draw_token(const unsigned* sorted_key, const 
 
 }  // namespace ivb
 
-namespace ivb {
-// true when chunk_rows reads the quantiser's chunk sums (more than three chunks per lane)
-__host__ __device__ __forceinline__ bool op_needs_xsum(const Op& op) {
-  const int chunks = (op.in_n + 63) >> 6;
-  return ((chunks + (1 << op.lpr_log) - 1) >> op.lpr_log) > 3;
-}
-}  // namespace ivb

@@ -101,18 +101,20 @@ static __device__ __noinline__ float quantize_ni(const float* src, int n, const 
   return quantize_block(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
 }
 
-// Gather + (RMSNorm +) quantise of an input of at most 1024 values, all in registers: thread t polls
-// the words t, t + 256, t + 512, t + 768 of the input's flag-word buffer, exactly the elements the
-// canonical quantiser assigns to lane t, so the sum of squares (fmaf in that order, warp butterfly,
-// warps in order), the amax and the codes (rint(v / scale), transposed GEMV layout, zero padding to a
-// 64-input chunk) equal quantize_block's bit for bit. buf == nullptr: the values are read from `keep`;
-// otherwise they are also stored there. Returns the activation scale, or -1 in every thread when a
-// word did not arrive within timeout_ns.
-static __device__ __noinline__ float gather_quantize_1k(const unsigned long long* buf, int n, unsigned flag, float* keep,
-                                                        const float* norm_w, float norm_eps, float clip, float act_eps,
-                                                        int8_t* codes, float* red, unsigned long long timeout_ns,
-                                                        long long* t_arrived) {
-  constexpr int E = 4;
+// Gather + (RMSNorm +) quantise of an input of at most E * 256 values, all in registers: thread t polls
+// the words t, t + 256, t + 512, ... of the input's flag-word buffer, exactly the elements the canonical
+// quantiser assigns to lane t, so the sum of squares (fmaf in that order, warp butterfly, warps in
+// order), the amax and the codes (rint(v / scale), transposed GEMV layout, zero padding to a 64-input
+// chunk) equal quantize_block's bit for bit. buf == nullptr: the values are read from `keep`; otherwise
+// they are also stored there. Returns the activation scale, or -1 in every thread when a word did not
+// arrive within timeout_ns. E = 4 serves inputs up to 1024 values, E = 12 up to 3072. xhalf[2u + h] gets
+// the sum of the codes of half h of 64-input chunk u (the row dots subtract the chunk's sum).
+constexpr int kMaxEPT = 12;  // input elements per thread: n <= 3072
+template <int E>
+__device__ __forceinline__ float gather_quantize_reg(const unsigned long long* buf, int n, unsigned flag, float* keep,
+                                                     const float* norm_w, float norm_eps, float clip, float act_eps,
+                                                     int8_t* codes, int* xhalf, float* red, unsigned long long timeout_ns,
+                                                     long long* t_arrived) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   float x[E];
   bool late = false;
@@ -192,133 +194,21 @@ static __device__ __noinline__ float gather_quantize_1k(const unsigned long long
   const float scale = fmaxf(__uint_as_float(mbits) / 127.0f, act_eps);
   const float rscale = 1.0f / scale;
   const int padded = (n + 63) & ~63;
-  bool near = false;
-  int q[E];
 #pragma unroll
   for (int k = 0; k < E; ++k) {
     const int i = tid + k * kThreads;
-    bool nr = false;
-    q[k] = i < n ? quant_code_fast(v[k], rscale, nr) : 0;
-    near |= nr;
-    if (i < padded) codes[act_slot(i)] = static_cast<int8_t>(q[k]);
-  }
-  if (__syncthreads_or(near)) {
-#pragma unroll
-    for (int k = 0; k < E; ++k) {
-      const int i = tid + k * kThreads;
-      if (i < n) {
-        bool nr = false;
-        quant_code_fast(v[k], rscale, nr);
-        if (nr) {
-          const int qe = static_cast<int>(rintf(v[k] / scale));
-          if (qe != q[k]) codes[act_slot(i)] = static_cast<int8_t>(qe);
-        }
-      }
+    int q = 0;
+    if (i < n) {
+      bool nr = false;
+      q = quant_code_fast(v[k], rscale, nr);
+      if (nr) q = static_cast<int>(rintf(v[k] / scale));  // within rounding distance of a half: the IEEE division
     }
-    __syncthreads();
-  }
-  return scale;
-}
-
-// Gather + (RMSNorm +) quantise of an op's input vector: thread t polls the words t, t + 256, ... of
-// the input's flag-word buffer (all loads in flight at once) and stores the values to `keep` (shared);
-// the quantiser then walks the same elements per thread in the canonical order (sum of squares with
-// fmaf over t, t + 256, ..., warp butterfly, warps in order; amax; codes rint(v / scale) in the
-// transposed GEMV layout, zero padding to a 64-input chunk), so the codes equal quantize_block's bit
-// for bit. One compact routine serves every input width (n <= 3072). buf == nullptr: the values are
-// already in `keep`. Returns the activation scale (> 0), or -1 in every thread when a word did not
-// arrive within timeout_ns.
-constexpr int kMaxEPT = 12;  // input elements per thread: n <= 3072
-static __device__ __noinline__ float gather_quantize(const unsigned long long* buf, int n, unsigned flag, float* keep,
-                                                     const float* norm_w, float norm_eps, float clip, float act_eps,
-                                                     int8_t* codes, float* red, unsigned long long timeout_ns,
-                                                     long long* t_arrived) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  bool late = false;
-  if (buf != nullptr) {
-    unsigned long long w[kMaxEPT];
-#pragma unroll
-    for (int k = 0; k < kMaxEPT; ++k) {
-      const int i = tid + k * kThreads;
-      w[k] = i < n ? ll_load1(buf + i) : static_cast<unsigned long long>(flag) << 32;
-    }
-    unsigned long long t0 = 0ull;
-    unsigned spins = 0u;
-    while (!late) {
-      bool miss = false;
-#pragma unroll
-      for (int k = 0; k < kMaxEPT; ++k) {
-        if (static_cast<unsigned>(w[k] >> 32) != flag) {
-          miss = true;
-          w[k] = ll_load1(buf + tid + k * kThreads);
-        }
-      }
-      if (!miss) break;
-      if ((++spins & 63u) == 0u) {
-        const unsigned long long t = global_ns();
-        if (t0 == 0ull) t0 = t;
-        else if (t - t0 > timeout_ns) late = true;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < kMaxEPT; ++k) {
-      const int i = tid + k * kThreads;
-      if (i < n) keep[i] = __uint_as_float(static_cast<unsigned>(w[k]));
-    }
-  }
-  float inv = 0.0f;
-  if (norm_w != nullptr) {
-    float p2 = 0.0f;
-    for (int i = tid; i < n; i += kThreads) p2 = fmaf(keep[i], keep[i], p2);  // this thread's own stores
-    p2 = warp_sum(p2);
-    if (lane == 0) red[warp] = p2;
-  }
-  if (__syncthreads_or(late)) return -1.0f;
-  if (t_arrived != nullptr && threadIdx.x == 0) *t_arrived = clock64();  // tracing: the whole input is here
-  if (norm_w != nullptr) {
-    float ss = red[0];
-#pragma unroll
-    for (int w2 = 1; w2 < kWarps; ++w2) ss += red[w2];
-    inv = 1.0f / sqrtf(ss / static_cast<float>(n) + norm_eps);
-  }
-  auto value = [&](int i) -> float {
-    const float x = keep[i];
-    return norm_w != nullptr ? __fmul_rn(fminf(fmaxf(__fmul_rn(x, inv), -clip), clip), norm_w[i]) : x;
-  };
-  float am = 0.0f;
-  for (int i = tid; i < n; i += kThreads) am = fmaxf(am, fabsf(value(i)));
-  unsigned* wmax = reinterpret_cast<unsigned*>(red) + 16;
-  {
-    const unsigned m = __reduce_max_sync(kFull, __float_as_uint(am));
-    if (lane == 0) wmax[warp] = m;
+    if (i < padded) codes[act_slot(i)] = static_cast<int8_t>(q);
+    // the code sum of the half chunk this warp holds (64-input chunk u = 4k + warp / 2), for the row dots
+    const int hs = __reduce_add_sync(kFull, q);
+    if (lane == 0 && k * kThreads + warp * 32 < padded) xhalf[2 * (4 * k + (warp >> 1)) + (warp & 1)] = hs;
   }
   __syncthreads();
-  unsigned mbits = wmax[0];
-#pragma unroll
-  for (int w2 = 1; w2 < kWarps; ++w2) mbits = max(mbits, wmax[w2]);
-  const float scale = fmaxf(__uint_as_float(mbits) / 127.0f, act_eps);
-  const float rscale = 1.0f / scale;
-  const int padded = (n + 63) & ~63;
-  bool near = false;
-  for (int i = tid; i < padded; i += kThreads) {
-    bool nr = false;
-    const int q = i < n ? quant_code_fast(value(i), rscale, nr) : 0;
-    near |= nr;
-    codes[act_slot(i)] = static_cast<int8_t>(q);
-  }
-  if (__syncthreads_or(near)) {
-    // rare: values within rounding distance of a half-integer take the IEEE division
-    for (int i = tid; i < n; i += kThreads) {
-      const float v = value(i);
-      bool nr = false;
-      const int q = quant_code_fast(v, rscale, nr);
-      if (nr) {
-        const int qe = static_cast<int>(rintf(v / scale));
-        if (qe != q) codes[act_slot(i)] = static_cast<int8_t>(qe);
-      }
-    }
-    __syncthreads();
-  }
   return scale;
 }
 
@@ -805,7 +695,7 @@ static __device__ __noinline__ void topk_by_rank(const unsigned* keys, int n, in
 // epilogue, the gathered and (normed) quantised input, its rows chunk by chunk from the weight ring,
 // and the epilogue (publish the output slice, residual add, SwiGLU, the recurrent step, or the head's
 // logits and local top-k candidates).
-static __device__ __noinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDesc& lay, int rows_c) {
+__device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDesc& lay, int rows_c) {
   // the op record, the dimensions and the context fields used below are read once into registers (the
   // op stores to shared memory, where all three live)
   const DecodeParams& p = *c.p;
@@ -863,8 +753,9 @@ static __device__ __noinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLaye
   const float* nw = op.has_norm ? reinterpret_cast<const float*>(nrm) : nullptr;
   const float act_scale =
       op.in_n <= 4 * kThreads
-          ? gather_quantize_1k(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.red, p.timeout_ns, t_arr)
-          : gather_quantize(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.red, p.timeout_ns, t_arr);
+          ? gather_quantize_reg<4>(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.xsum, c.red, p.timeout_ns, t_arr)
+          : gather_quantize_reg<kMaxEPT>(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.xsum, c.red, p.timeout_ns,
+                                         t_arr);
   if (act_scale < 0.0f) ok = false;
   if (tid == 0 && c.marks != nullptr && !from_smem) {  // split the wait for the input from the quantiser
     c.prof[1] += c.prof_t2 - c.prof_t;
@@ -887,7 +778,14 @@ static __device__ __noinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLaye
       ssmc[i] = *src;
     }
   }
-  // rows of this CTA, chunk by chunk (a warp skips a chunk whose wait ran out in any of its lanes)
+  // rows of this CTA, chunk by chunk (a warp skips a chunk whose wait ran out in any of its lanes); the
+  // out, down, gate/up and mla entry projections publish each row as it finishes
+  const int epi = op.kind == OP_OUT || op.kind == OP_DOWN           ? EPI_RESID
+                  : op.kind == OP_GATE_UP && op.lpr_log <= 4          ? EPI_SWIGLU
+                  : op.kind == OP_ENTRY_MLA                           ? EPI_PUBLISH
+                                                                      : EPI_STORE;
+  unsigned long long* const ll_out = p.ll + op.ll_out + (epi == EPI_SWIGLU ? lo / 2 : lo);
+  const float* const resid = c.resid + lo;
   const int n_row_chunks = op.n_chunks - op.has_const - op.has_norm_chunk;
   for (int ch = 0; ch < n_row_chunks; ++ch) {
     const unsigned char* stage = stream_acquire(p, st, idx++);
@@ -896,23 +794,19 @@ static __device__ __noinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLaye
     } else {
       const int r0 = ch * op.chunk_rows;
       const int k = max(0, min(op.chunk_rows, rows_c - r0));
-      if (k > 0) rows_generic(stage, k, op.row_bytes, op.scale_stride, op.has_bias, act_scale, c.act, op.in_n, op.lpr_log, rows_out + r0);
+      if (k > 0)
+        rows_generic(stage, k, op.row_bytes, op.scale_stride, op.has_bias, act_scale, c.act, c.xsum, op.in_n, op.lpr_log,
+                     rows_out + r0, epi, ll_out + (epi == EPI_SWIGLU ? r0 / 2 : r0), resid + r0, flag);
     }
   }
-  __syncthreads();  // every row of this CTA is in rows_out
+  if (epi == EPI_STORE) __syncthreads();  // every row of this CTA is in rows_out
   c.tick(3);
   float* stg = c.stg;
-  // epilogues
-  if (op.kind == OP_OUT || op.kind == OP_DOWN) {
-    for (int r = tid; r < rows_c; r += kThreads) stg[r] = c.resid[lo + r] + rows_out[r];
-    __syncthreads();
-    ll_put(p.ll + op.ll_out, lo, stg, rows_c, flag);
-  } else if (op.kind == OP_GATE_UP) {
+  // epilogues that need every row of the CTA
+  if (op.kind == OP_GATE_UP && epi == EPI_STORE) {
     for (int m = tid; m < rows_c / 2; m += kThreads) stg[m] = silu_f(rows_out[2 * m]) * rows_out[2 * m + 1];
     __syncthreads();
     ll_put(p.ll + op.ll_out, lo / 2, stg, rows_c / 2, flag);
-  } else if (op.kind == OP_ENTRY_MLA) {
-    ll_put(p.ll + op.ll_out, lo, rows_out, rows_c, flag);
   } else if (op.kind == OP_HEAD) {
     for (int r = tid; r < rows_c; r += kThreads) p.logits[lo + r] = rows_out[r];
     if (c.sampling) {
@@ -1440,11 +1334,12 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     pl.op.scale_stride = ((m.in_features + 127) / 128 + 7) / 8 * 8;
     pl.op.has_bias = m.bias != nullptr;
     // lanes per row: at most kRowsKPL chunks per lane, then as many lanes as keep the CTA's rows in one
-    // pass of rows_generic (rows x lanes <= 256) without idle lanes (lanes <= chunks)
+    // pass of rows_generic (rows x lanes <= 256) without idle lanes (lanes <= chunks), at most 16 (the
+    // lane butterfly stays at four steps, and gate/up row pairs share a warp)
     const int chunks = (in_n + 63) / 64;
     int lg = 0;
     while (lg < 5 && ((chunks + (1 << lg) - 1) >> lg) > kRowsKPL) ++lg;
-    while (lg < 5 && (1 << (lg + 1)) <= chunks && (std::max(rows_per, 1) << (lg + 1)) <= kThreads) ++lg;
+    while (lg < 4 && (1 << (lg + 1)) <= chunks && (std::max(rows_per, 1) << (lg + 1)) <= kThreads) ++lg;
     pl.op.lpr_log = lg;
     pl.op.has_norm = norm != nullptr;
     pl.op.has_norm_chunk = norm != nullptr;
@@ -1601,7 +1496,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   M.act = static_cast<int>(o);
   o += r16(pad_in);
   M.xsum = static_cast<int>(o);
-  o += r16(pad_in / 64 * 4);
+  o += r16(pad_in / 64 * 8);  // two half-chunk code sums per 64-input chunk
   M.resid = static_cast<int>(o);
   o += r16(static_cast<size_t>(d) * 4);
   int pub_n = std::max(std::max(cpc, hd + 2), std::max(dper, Fper));
