@@ -542,7 +542,7 @@ static __device__ __noinline__ int draw_token(const unsigned* sorted_key, const 
                                  uint64_t key, uint64_t counter) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float top = key_value(sorted_key[0]);
-  for (int c = tid; c < K; c += kThreads) cdf[c] = expf(key_value(sorted_key[c]) - top);
+  for (int c = tid; c < K; c += kThreads) cdf[c] = sample_exp(key_value(sorted_key[c]) - top);
   __syncthreads();
   if (warp == 0) {
     float carry = 0.0f;

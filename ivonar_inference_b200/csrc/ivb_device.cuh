@@ -819,6 +819,26 @@ __device__ __forceinline__ unsigned order_key(float v) {
   const unsigned b = __float_as_uint(v);
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
+// e^x (x <= 0) for the sampler's candidate weights, written the same way in the kernels and in the CPU
+// oracle so that both weigh the candidates bit for bit alike (the libraries' expf differ in the last
+// bits, which moves draws that land next to a CDF boundary). Cody-Waite reduction x = n ln2 + r with
+// ln2 split into a 12-bit head (n * head is exact) and a tail, e^r by its degree-7 Taylor polynomial in
+// Horner form with fused multiply-adds (|r| <= ln2 / 2: truncation below 6e-9 relative), then 2^n
+// from the exponent field. Inputs below -87 (weights under 2^-125 against the top candidate's 1) give 0.
+__device__ __forceinline__ float sample_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f;
+  const float n = rintf(__fmul_rn(x, 0x1.715476p+0f));
+  const float r = fmaf(-n, 0x1.0bfbe8p-15f, fmaf(-n, 0x1.62ep-1f, x));
+  float p = 0x1.a01a02p-13f;
+  p = fmaf(p, r, 0x1.6c16c2p-10f);
+  p = fmaf(p, r, 0x1.111112p-7f);
+  p = fmaf(p, r, 0x1.555556p-5f);
+  p = fmaf(p, r, 0x1.555556p-3f);
+  p = fmaf(p, r, 0x1p-1f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  return __fmul_rn(p, __int_as_float((static_cast<int>(n) + 127) << 23));
+}
 __device__ __forceinline__ float key_value(unsigned k) {
   return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
@@ -1033,7 +1053,7 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
   __syncthreads();
   mark(marks, 5);
   const float top = key_value(sm.hist[0]);
-  for (int c = tid; c < K; c += kThreads) sm.cprob[c] = expf(key_value(sm.hist[c]) - top);
+  for (int c = tid; c < K; c += kThreads) sm.cprob[c] = sample_exp(key_value(sm.hist[c]) - top);
   __syncthreads();
   // canonical CDF: per 32-chunk Hillis-Steele inclusive scan, chunk carries added sequentially
   if (warp == 0) {

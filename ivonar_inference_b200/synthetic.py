@@ -58,9 +58,9 @@ def config_payload(name: str, vocab: int, hidden: int, layers: list[str], heads:
     }
 
 
-def config0() -> dict:
+def config0(seq_len: int = 64) -> dict:
     """Benchmark config 0: tiny CPU-runnable hybrid (vocab 512, d 128, 4 blocks)."""
-    return config_payload("CONFIG0", 512, 128, ["mamba", "mla"] * 2, 4, 16, 64, 384, 64)
+    return config_payload("CONFIG0", 512, 128, ["mamba", "mla"] * 2, 4, 16, 64, 384, seq_len)
 
 
 def config1(seq_len: int = 8192) -> dict:

@@ -357,6 +357,29 @@ static inline uint32_t order_key(float v) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+/* e^x (x <= 0) for the sampler's candidate weights, the same operations as the kernels' sample_exp
+ * (csrc/ivb_device.cuh), so the oracle weighs candidates bit for bit as the GPU does: Cody-Waite
+ * reduction x = n ln2 + r with ln2 split into a 12-bit head (n * head exact) and a tail, e^r by the
+ * degree-7 Taylor polynomial in Horner form with fmaf (|r| <= ln2/2), 2^n from the exponent field;
+ * inputs below -87 give 0. */
+static float sample_exp(float x) {
+  if (!(x >= -87.0f)) return 0.0f;
+  const float n = rintf(x * 0x1.715476p+0f);
+  const float r = fmaf(-n, 0x1.0bfbe8p-15f, fmaf(-n, 0x1.62ep-1f, x));
+  float p = 0x1.a01a02p-13f;
+  p = fmaf(p, r, 0x1.6c16c2p-10f);
+  p = fmaf(p, r, 0x1.111112p-7f);
+  p = fmaf(p, r, 0x1.555556p-5f);
+  p = fmaf(p, r, 0x1.555556p-3f);
+  p = fmaf(p, r, 0x1p-1f);
+  p = fmaf(p, r, 1.0f);
+  p = fmaf(p, r, 1.0f);
+  const uint32_t bits = (uint32_t)((int)n + 127) << 23;
+  float scale;
+  memcpy(&scale, &bits, 4);
+  return p * scale;
+}
+
 typedef struct {
   uint32_t key;
   int32_t idx;
@@ -371,7 +394,7 @@ static int cand_cmp(const void* a, const void* b) {
 
 /* score = logit * (1/T); seen: score *= score > 0 ? ipen : pen (reference ternary.cu:989-995).
  * The K = clamp(top_k, 1, min(max_top_k, vocab, 1024)) best by (score desc, index asc);
- * p_c = exp(s_c - s_0); cdf in 32-candidate chunks (Hillis-Steele inclusive scan inside a chunk,
+ * p_c = sample_exp(s_c - s_0); cdf in 32-candidate chunks (Hillis-Steele inclusive scan inside a chunk,
  * chunk totals carried in order); u = philox(rng[0], rng[1]) (counter then incremented),
  * target = min(u, 0.99999994) * cdf[K-1], token = #(cdf <= target) clamped to K - 1.
  * Sets seen[token] = 1 and returns the token. */
@@ -401,7 +424,7 @@ int64_t orc_sample(const float* logits, uint8_t* seen, int vocab, float temperat
     const uint32_t b = (k & 0x80000000u) ? (k & 0x7fffffffu) : ~k;
     float s;
     memcpy(&s, &b, 4);
-    cdf[c] = expf(s - top);
+    cdf[c] = sample_exp(s - top);
   }
   float carry = 0.0f;
   for (int base = 0; base < K; base += 32) {

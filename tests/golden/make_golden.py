@@ -16,8 +16,9 @@ It imports LuisOezdem/ivonar-inference unmodified and records, on seeded synthet
   attention.npz   numba attention_step (cpu_decoder.py:186-231) over 6 positions
   sampler.npz     greedy (top_k = 1) picks of the torch sampler with a repetition penalty
                   (decoder.py:324-333)
-  model_*.npz     whole-model runs: torch StaticDecoder (fp32) prefill logits and greedy stream
-                  with per-step logits, numba CpuDecoder greedy stream
+  model_*.npz     whole-model runs: torch StaticDecoder (fp32) prefill logits and 256-token greedy and
+                  penalised-greedy streams (config 0 and tiny: the penalised stream's per-step logits),
+                  numba CpuDecoder greedy streams (from the torch prefill, and stepped through the prompt)
 Everything is generated from this repository's synthetic models (ivonar_inference_b200.synthetic),
 whose state dicts the reference loader reads as-is.
 """
@@ -31,6 +32,8 @@ import numpy as np
 import torch
 
 ROOT = Path(__file__).resolve().parents[2]
+STREAM = 256           # tokens of every recorded greedy stream
+STREAM_CONTEXT = 288   # context of the config-0 and tiny models the streams run on
 sys.path.insert(0, str(ROOT))
 OUT = Path(__file__).resolve().parent
 
@@ -199,10 +202,11 @@ def model_run(ref, payload: dict, seed: int, style: str, prompt_len: int, steps:
         logits = []
         for _ in range(steps - 1):
             tokens.append(dec.advance())
-            if keep_logits:
+            if keep_logits and tag == "greedy_rp":
                 logits.append(dec.logits[0].clone().numpy())
         out[f"torch_{tag}"] = np.array(tokens, np.int64)
-        if keep_logits:
+        if logits:
+            # logits after each fed token: step_logits[i] chose stream[i + 1] (prefill_logits chose stream[0])
             out[f"torch_{tag}_step_logits"] = np.stack(logits)
     if numba:
         cdec = cpu.CpuDecoder(model, max_len=payload["seq_len"], sampling=True)
@@ -227,14 +231,15 @@ def main() -> None:
     np.savez_compressed(OUT / "ternary.npz", **ternary_vectors(cpu, TernaryLinear))
     np.savez_compressed(OUT / "ssm.npz", **ssm_vectors(cpu))
     np.savez_compressed(OUT / "attention.npz", **attention_vectors(cpu))
-    data, model0 = model_run(ref, synthetic.config0(), 0, "baseline", 16, 32, True, True)
-    np.savez_compressed(OUT / "model_config0.npz", **data)
+    # 256-token streams; the models' contexts hold the prompt and every generated token
+    data, model0 = model_run(ref, synthetic.config0(seq_len=STREAM_CONTEXT), 0, "baseline", 16, STREAM, True, True)
+    np.savez_compressed(OUT / "model_config0.npz", seq_len=np.int64(STREAM_CONTEXT), **data)
     np.savez_compressed(OUT / "sampler.npz", **sampler_vectors(StaticDecoder, model0))
-    data, _ = model_run(ref, synthetic.tiny(seq_len=64), 3, "reference_tests", 8, 24, True, True)
-    np.savez_compressed(OUT / "model_tiny.npz", **data)
+    data, _ = model_run(ref, synthetic.tiny(seq_len=STREAM_CONTEXT), 3, "reference_tests", 8, STREAM, True, True)
+    np.savez_compressed(OUT / "model_tiny.npz", seq_len=np.int64(STREAM_CONTEXT), **data)
     if "--no-nano" not in sys.argv:
-        data, _ = model_run(ref, synthetic.config1(seq_len=2048), 0, "baseline", 36, 48, False, True)
-        np.savez_compressed(OUT / "model_config1.npz", **data)
+        data, _ = model_run(ref, synthetic.config1(seq_len=2048), 0, "baseline", 36, STREAM, False, True)
+        np.savez_compressed(OUT / "model_config1.npz", seq_len=np.int64(2048), **data)
     for path in sorted(OUT.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size} bytes")
 

@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden
+from conftest import check_greedy_stream, first_difference, golden, penalised_scores
 
 pytestmark = pytest.mark.gpu
 
@@ -17,16 +17,16 @@ def _model(payload, seed=0, style="baseline"):
     return synthetic.synthetic_model(payload, seed, style)
 
 
-def _first_difference(a, b) -> int:
-    return next((i for i, (x, y) in enumerate(zip(a, b)) if x != y), min(len(a), len(b)))
-
-
 @pytest.mark.parametrize("name", ["model_config0", "model_tiny"])
 def test_decoder_matches_the_oracle_and_the_reference(oracle_lib, name: str) -> None:
+    """256-token penalised greedy stream of the reference's torch decoder (fp32): prefill logits, then
+    every one of the 255 teacher-forced steps against the reference's step logits and the oracle, then
+    the free-running stream (identical, or parting only at a near-tie of the reference's own scores)."""
     from ivonar_inference_b200 import B200Decoder, synthetic
 
     g = golden(name)
-    payload = synthetic.config0() if name == "model_config0" else synthetic.tiny(seq_len=64)
+    seq_len = int(g["seq_len"])
+    payload = synthetic.config0(seq_len=seq_len) if name == "model_config0" else synthetic.tiny(seq_len=seq_len)
     style = "baseline" if name == "model_config0" else "reference_tests"
     model = _model(payload, int(g["seed"]), style)
     dec = B200Decoder(model, device="cuda", sampling=True)
@@ -34,23 +34,33 @@ def test_decoder_matches_the_oracle_and_the_reference(oracle_lib, name: str) -> 
     prompt = torch.from_numpy(g["prompt"]).view(1, -1)
     gpu = dec.prefill(prompt)[0].cpu().numpy()
     cpu = ora.prefill(g["prompt"]).copy()
+    # tolerances: GPU vs oracle 0.02 (same algorithm, different fp32 order and fp16 rope keys), GPU vs
+    # the reference's fp32 torch decoder 0.05 (its decompressed K/V path); a greedy pick may differ only
+    # where the reference's top two scores are within twice that (0.1)
     assert float(np.abs(gpu - cpu).max()) < 0.02
     assert float(np.abs(gpu - g["prefill_logits"]).max()) < 0.05
     assert dec.host_position == len(g["prompt"]) and int(dec.position) == len(g["prompt"])
-    # teacher forcing along the reference's penalized greedy stream
     stream = g["torch_greedy_rp"]
+    steps = g["torch_greedy_rp_step_logits"]
+    assert len(stream) == 256 and len(steps) == 255
     worst_oracle = worst_ref = 0.0
     for i, tok in enumerate(stream[:-1]):
         out = dec.step(torch.tensor([int(tok)]))[0].cpu().numpy()
         ref = ora.step(int(tok))
         worst_oracle = max(worst_oracle, float(np.abs(out - ref).max()))
-        worst_ref = max(worst_ref, float(np.abs(out - g["torch_greedy_rp_step_logits"][i]).max()))
-    assert worst_oracle < 0.02 and worst_ref < 0.05
-    # free-running penalized greedy: the reference's tokens
+        worst_ref = max(worst_ref, float(np.abs(out - steps[i]).max()))
+        ours = penalised_scores(out, stream[: i + 1], 4.0)
+        theirs = penalised_scores(steps[i], stream[: i + 1], 4.0)
+        pick = int(ours.argmax())
+        if pick != int(stream[i + 1]):
+            assert float(theirs[int(stream[i + 1])] - theirs[pick]) < 0.1, (i, pick, int(stream[i + 1]))
+    assert worst_oracle < 0.02 and worst_ref < 0.05, (worst_oracle, worst_ref)
+    # free-running penalised greedy, all 256 tokens through the kernel's own sampler
     dec.prefill(prompt)
     dec.configure_sampling(temperature=1.0, top_k=1, repetition_penalty=4.0)
     tokens = [dec.sample()] + dec.advance_many(len(stream) - 1)
-    assert tokens == stream.tolist()
+    agree = check_greedy_stream(tokens, stream, g["prefill_logits"], steps, 4.0, 0.1)
+    print(f"{name}: {agree}/256 tokens identical to the reference stream")
 
 
 @pytest.mark.parametrize("layers", [("mamba",), ("mla",), ("mla", "mamba")])
@@ -81,64 +91,75 @@ def test_nano_width_blocks_match_the_oracle_closely(oracle_lib, layers) -> None:
 
 
 def test_nano_decoder_matches_the_oracle(oracle_lib) -> None:
+    """Config 1 (24 blocks at the Nano width): the prefill and 255 teacher-forced steps along the
+    reference's 256-token greedy stream against the oracle, then the free-running greedy stream against
+    the reference's numba decoder, whose first divergence must be a near-tie of the oracle's logits."""
     from ivonar_inference_b200 import B200Decoder, synthetic
 
     g = golden("model_config1")
-    model = _model(synthetic.config1(seq_len=2048), 0)
-    dec = B200Decoder(model, max_len=256, device="cuda", sampling=True)
-    ora = oracle_lib.OracleDecoder(model, max_len=256)
+    model = _model(synthetic.config1(seq_len=int(g["seq_len"])), 0)
+    dec = B200Decoder(model, max_len=320, device="cuda", sampling=True)
+    ora = oracle_lib.OracleDecoder(model, max_len=320)
     prompt = torch.from_numpy(g["prompt"]).view(1, -1)
     gpu = dec.prefill(prompt)[0].cpu().numpy()
     cpu = ora.prefill(g["prompt"]).copy()
+    # 24 quantised blocks amplify rounding-order differences chaotically: at the end of this prompt the
+    # reference's own torch forward and numba decoder differ by up to 0.39 max / 0.048 mean |dlogit|
+    # (two numba runs by 0.27 / 0.047; logit std 0.54), which is the bar for every step here
     diff = np.abs(gpu - cpu)
-    # 24 quantised blocks amplify rounding-order differences chaotically; the reference's own torch
-    # and numba paths differ by 0.21 max / 0.033 mean on this model, which is the bar here.
     assert float(diff.max()) < 0.25 and float(diff.mean()) < 0.04, (float(diff.max()), float(diff.mean()))
-    # The argmax itself may land on either side of a near-tie (on this prompt the oracle's two leading
-    # logits are 0.008 apart): the GPU's pick must be within the same spread of the oracle's maximum.
-    assert float(cpu.max() - cpu[int(gpu.argmax())]) < 0.25
+    stream = g["torch_greedy"]
+    assert len(stream) == 256
+    maxes, means = [], []
+    for tok in stream[:-1]:
+        out = dec.step(torch.tensor([int(tok)]))[0].cpu().numpy()
+        ref = ora.step(int(tok))
+        d = np.abs(out - ref)
+        maxes.append(float(d.max()))
+        means.append(float(d.mean()))
+    print(f"nano teacher-forced: worst max {max(maxes):.3f}, worst mean {max(means):.4f}, average mean {np.mean(means):.4f}")
+    assert max(maxes) < 0.4 and max(means) < 0.05, (max(maxes), max(means))
+    # over the whole stream the typical step sits inside the reference's own mean spread (0.033-0.048)
+    assert float(np.mean(means)) < 0.045, float(np.mean(means))
+    # free-running greedy on the GPU; the oracle follows the GPU's tokens to price the first split
+    dec.prefill(prompt)
     dec.configure_sampling(1.0, 1, 1.0)
-    tokens = [dec.sample()] + dec.advance_many(47)
-    # Every greedy token of the GPU must be a near-argmax of the oracle's logits when the oracle is
-    # teacher-forced along the GPU's own stream (streams may split at near-ties, as the reference's
-    # own torch and numba paths do after 8 tokens on this model).
-    worst_gap = 0.0
-    gaps = []
-    logits = cpu
-    for i, tok in enumerate(tokens):
-        gap = float(logits.max() - logits[tok])
-        gaps.append(gap)
-        worst_gap = max(worst_gap, gap)
-        if i + 1 < len(tokens):
-            logits = ora.step(tok)
-    agree = _first_difference(tokens, g["numba_stepped_greedy"].tolist())
-    print(f"nano greedy: agreement with reference numba {agree}/48, worst oracle gap {worst_gap:.3e}, "
-          f"exact argmax {sum(x == 0.0 for x in gaps)}/48")
-    stats = (agree, worst_gap, sum(x == 0.0 for x in gaps))
-    # bound: the reference's own torch/numba logit spread on this model (0.21 max)
-    assert worst_gap < 0.25, stats
-    # most picks are the oracle's exact argmax; the rest are near-ties inside the bound above. The count
-    # moves with the prefill's fp32 order (tensor-core prefill vs oracle: max 0.219 / mean 0.036, the
-    # token-by-token prefill: max 0.202 / mean 0.033), so it is held to two thirds of the stream.
-    assert sum(x == 0.0 for x in gaps) >= 32, stats
+    tokens = [dec.sample()] + dec.advance_many(255)
+    numba = g["numba_stepped_greedy"].tolist()
+    d = first_difference(tokens, numba)
+    if d < 256:
+        logits = ora.prefill(g["prompt"]).copy()
+        for tok in tokens[:d]:
+            logits = ora.step(int(tok))
+        gap = abs(float(logits[tokens[d]] - logits[numba[d]]))
+        print(f"nano greedy: {d}/256 identical to the reference numba stream; split at an oracle margin of {gap:.4f}")
+        assert gap < 0.25, (d, gap)
 
 
-def test_sampled_stream_matches_the_oracle_with_the_same_seed(oracle_lib) -> None:
+def test_decode_kernel_sampler_draws_the_oracle_token_on_its_own_logits(oracle_lib) -> None:
+    """The decode kernel's distributed sampler (local top-k in every head CTA, the group merge, the
+    draw) against the oracle's sampler on the very logits the kernel produced, step by step: the same
+    Philox state and repetition flags must give the same token every time (no tolerance). Config 0
+    (single-level merge) for 256 tokens and config 1 (two-level merge over 128 CTAs) for 64."""
     from ivonar_inference_b200 import B200Decoder, synthetic
 
-    model = _model(synthetic.config0(), 3)
-    dec = B200Decoder(model, device="cuda", sampling=True, seed=1234)
-    ora = oracle_lib.OracleDecoder(model, seed=1234)
-    prompt = synthetic.random_prompt(512, 16, seed=3)
-    dec.prefill(prompt)
-    ora.prefill(prompt[0].numpy())
-    dec.configure_sampling(0.5, 40, 1.15)
-    ora.configure_sampling(0.5, 40, 1.15)
-    tokens = [dec.sample()] + dec.advance_many(31)
-    ref = [ora.sample()]
-    ref += ora.generate(ref[0], 31)
-    assert _first_difference(tokens, ref) >= 16, (tokens, ref)
-    assert int(dec.rng[1]) == 32
+    for payload, seed, count, (T, K, rp) in ((synthetic.config0(seq_len=288), 3, 256, (0.5, 40, 1.15)),
+                                             (synthetic.config1(seq_len=2048), 0, 64, (0.7, 256, 1.3))):
+        model = _model(payload, seed)
+        vocab = int(payload["vocab_size"])
+        dec = B200Decoder(model, max_len=count + 24, device="cuda", sampling=True, seed=1234 + seed)
+        dec.prefill(synthetic.random_prompt(vocab, 16, seed=seed))
+        dec.configure_sampling(T, K, rp)
+        seen = np.zeros(vocab, np.uint8)
+        rng = (oracle_lib.c_uint64 * 2)(int(dec.rng[0]), int(dec.rng[1]))
+        for i in range(count):
+            tok = dec.sample() if i == 0 else dec.advance()
+            logits = dec.logits[0].cpu().numpy()
+            want = oracle_lib.lib().orc_sample(oracle_lib._p(logits), oracle_lib._p(seen), vocab, T, rp,
+                                               float(np.float32(1.0 / rp)), K, dec.max_top_k, rng)
+            assert tok == want, (vocab, i, tok, want)
+        assert int(dec.rng[1]) == int(rng[1])
+        assert int(dec.seen[0].sum()) == int(seen.sum())
 
 
 def test_bursts_produce_the_same_tokens_as_single_steps() -> None:

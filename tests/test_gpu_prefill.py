@@ -6,7 +6,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden
+from conftest import check_greedy_stream, golden
 
 pytestmark = pytest.mark.gpu
 
@@ -22,7 +22,8 @@ def test_gemm_prefill_matches_the_step_prefill_and_the_oracle(oracle_lib, name: 
     from ivonar_inference_b200 import B200Decoder, synthetic
 
     g = golden(name)
-    payload = synthetic.config0() if name == "model_config0" else synthetic.tiny(seq_len=64)
+    seq_len = int(g["seq_len"])
+    payload = synthetic.config0(seq_len=seq_len) if name == "model_config0" else synthetic.tiny(seq_len=seq_len)
     model = _model(payload, int(g["seed"]), "baseline" if name == "model_config0" else "reference_tests")
     prompt = torch.from_numpy(g["prompt"]).view(1, -1)
     fast = B200Decoder(model, device="cuda", sampling=True)
@@ -36,11 +37,12 @@ def test_gemm_prefill_matches_the_step_prefill_and_the_oracle(oracle_lib, name: 
     assert float(np.abs(a - ref).max()) < 0.02
     assert fast.host_position == slow.host_position == len(g["prompt"])
     assert int(fast.position) == int(slow.position) and int(fast.token) == int(prompt[0, -1])
-    # decoding continues from the prefilled caches and state: the reference's penalised greedy stream
+    # decoding continues from the prefilled caches and state: the reference's 256-token penalised greedy
+    # stream (identical, or parting only at a near-tie of the reference's scores, as in the decode tests)
     stream = g["torch_greedy_rp"]
     fast.configure_sampling(temperature=1.0, top_k=1, repetition_penalty=4.0)
     tokens = [fast.sample()] + fast.advance_many(len(stream) - 1)
-    assert tokens == stream.tolist()
+    check_greedy_stream(tokens, stream, g["prefill_logits"], g["torch_greedy_rp_step_logits"], 4.0, 0.1)
 
 
 def test_chunked_prefill_equals_one_call() -> None:

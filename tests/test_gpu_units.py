@@ -174,11 +174,12 @@ def test_sampler_draws_the_oracle_token_for_the_same_philox_state(oracle_lib) ->
                                                float(np.float32(1.0 / rp)), top_k, 256, rng_o)
             assert rng_after == [key, trial + 1]
             assert hist == tok and seen_after[tok] == 1
-            if top_k == 1:
-                assert tok == want
+            # the kernel and the oracle weigh the candidates with the same exponential and add them in
+            # the same order: the same Philox state draws the same token, every time
+            assert tok == want, (vocab, trial, tok, want)
             same += int(tok == want)
             total += 1
-    assert same >= total - 1
+    assert same == total == 36
 
 
 def test_sampler_follows_the_top_k_distribution() -> None:

@@ -10,7 +10,7 @@ import numpy as np
 import pytest
 import torch
 
-from conftest import golden
+from conftest import check_greedy_stream, first_difference, golden
 
 
 def test_plain_quantizer_is_bit_exact_with_the_reference(oracle_lib) -> None:
@@ -148,7 +148,8 @@ def test_oracle_decoder_matches_the_reference_model(oracle_lib, name: str, style
     from ivonar_inference_b200 import synthetic
 
     g = golden(name)
-    payload = synthetic.config0() if name == "model_config0" else synthetic.tiny(seq_len=64)
+    seq_len = int(g["seq_len"])
+    payload = synthetic.config0(seq_len=seq_len) if name == "model_config0" else synthetic.tiny(seq_len=seq_len)
     model = _model(payload, int(g["seed"]), style)
     dec = oracle_lib.OracleDecoder(model)
     logits = dec.prefill(g["prompt"]).copy()
@@ -163,20 +164,21 @@ def test_oracle_decoder_matches_the_reference_model(oracle_lib, name: str, style
         out = dec.step(int(tok))
         worst = max(worst, float(np.abs(out - steps[i]).max()))
     assert worst < 0.05
-    # free-running penalized greedy stream: same tokens as the reference
+    # free-running penalized greedy stream (256 tokens): the reference's tokens, or a split only at a
+    # near-tie of the reference's own scores (within twice the 0.05 logit bar)
     dec.prefill(g["prompt"])
     dec.configure_sampling(1.0, 1, 4.0)
     tokens = [dec.sample()]
     tokens += dec.generate(tokens[0], len(stream) - 1)
-    assert tokens == stream.tolist()
+    check_greedy_stream(tokens, stream, g["prefill_logits"], steps, 4.0, 0.1)
 
 
 def test_oracle_decoder_on_the_nano_shape(oracle_lib) -> None:
     from ivonar_inference_b200 import synthetic
 
     g = golden("model_config1")
-    model = _model(synthetic.config1(seq_len=2048), 0, "baseline")
-    dec = oracle_lib.OracleDecoder(model, max_len=128)
+    model = _model(synthetic.config1(seq_len=int(g["seq_len"])), 0, "baseline")
+    dec = oracle_lib.OracleDecoder(model, max_len=320)
     logits = dec.prefill(g["prompt"]).copy()
     ref = g["prefill_logits"]
     # 24 quantised blocks amplify rounding-order differences: on this model the reference's own
@@ -185,12 +187,24 @@ def test_oracle_decoder_on_the_nano_shape(oracle_lib) -> None:
     diff = np.abs(logits - ref)
     assert float(diff.max()) < 0.25 and float(diff.mean()) < 0.04
     assert int(logits.argmax()) == int(ref.argmax())
-    # like for like: the reference numba decoder stepping through the prompt as the oracle does
+    # like for like: the reference numba decoder stepping through the prompt as the oracle does. Its
+    # parallel fastmath reductions depend on the thread count: two runs of it on this prompt differ by
+    # 0.27 max / 0.047 mean, and it differs from its own torch forward by up to 0.39 / 0.048, so that
+    # spread is the bar.
     stepped = g["numba_stepped_logits"]
-    assert float(np.abs(logits - stepped).max()) < 0.15
-    assert float(np.abs(logits - stepped).mean()) < 0.03
+    assert float(np.abs(logits - stepped).max()) < 0.4
+    assert float(np.abs(logits - stepped).mean()) < 0.05
+    # the 256-token greedy stream against the reference numba decoder's: identical up to a split whose
+    # margin on the oracle's own logits is within the reference's torch/numba spread (0.25)
+    numba = g["numba_stepped_greedy"].tolist()
+    assert len(numba) == 256
     dec.configure_sampling(1.0, 1, 1.0)
     tokens = [dec.sample()]
-    tokens += dec.generate(tokens[0], len(g["numba_stepped_greedy"]) - 1)
-    agree = next((i for i, (a, b) in enumerate(zip(tokens, g["numba_stepped_greedy"])) if a != b), len(tokens))
-    assert agree >= 16, (agree, tokens[:24], g["numba_stepped_greedy"][:24].tolist())
+    tokens += dec.generate(tokens[0], len(numba) - 1)
+    d = first_difference(tokens, numba)
+    if d < len(numba):
+        at = dec.prefill(g["prompt"]).copy()
+        for tok in tokens[:d]:
+            at = dec.step(int(tok)).copy()
+        gap = abs(float(at[tokens[d]] - at[numba[d]]))
+        assert gap < 0.25, (d, gap)
