@@ -192,20 +192,27 @@ int32_t ivb_quantize_rows(const float* x, int32_t rows, int32_t n, const float* 
  * out[t][r] = epilogue(scale[t] * sum_g s[r][g] * (sum_{k in g} (code[r][k] - 1) * q8[t][k]) + bias[r])
  * with q8 (tiled layout, same ldq)/scale from ivb_quantize_rows; out row stride ldo (SILU_PAIR writes
  * rows/2 outputs per token). Uses all 512 TMEM columns of the SMs it runs on.
- * *error becomes IVB_ETIMEOUT if a bounded wait on the tensor core ran out. Replaces ternary.cu:688-783. */
+ * *error becomes IVB_ETIMEOUT if a bounded wait on the tensor core ran out. Replaces ternary.cu:688-783.
+ * Few tokens (too few row x token tiles to fill the GPU) split the inputs across CTAs; the split
+ * partial sums of this entry point live in a file-scope device scratch (16 MB) shared by every call on
+ * the device, so calls on one device must not overlap in time: issue them on one stream or order them
+ * with events. ivb_decoder_prefill and ivb_batch_decode keep their partial sums in their own workspace
+ * and share nothing. */
 int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
                          int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream);
 
 /* Split-K variant of ivb_ternary_gemv (same arguments, same results within fp32 rounding): the input
- * columns are spread over more CTAs and their partial row sums are added in a static device scratch.
- * It has no counterpart in the reference. It is for callers that may not allocate device memory at call
- * time: a serving process whose pool already holds the GPU's memory (a cudaMalloc there fails or waits
- * for the whole device), or code on a latency-bound path where cudaMalloc's implicit device
- * synchronisation is not acceptable. It allocates nothing: the scratch is a file-scope
- * __device__ array of 32768 fp32 row sums (rows > 32768 or in_features > 16384 return IVB_EINVAL);
- * its address is looked up once per device with cudaGetSymbolAddress on the first call with that
- * device current, so make the first call on each device outside any stream capture. Each call clears
- * the partial sums with a memset before accumulating. Calls that overlap in time on one device (other
+ * columns are spread over more CTAs, each column block's partial row sums go to a static device
+ * scratch, and a second kernel adds them in column-block order, so two calls on the same inputs give
+ * the same bits. It has no counterpart in the reference. It is for callers that may not allocate
+ * device memory at call time: a serving process whose pool already holds the GPU's memory (a
+ * cudaMalloc there fails or waits for the whole device), or code on a latency-bound path where
+ * cudaMalloc's implicit device synchronisation is not acceptable. It allocates nothing: the scratch is
+ * a file-scope __device__ array of 16 column blocks x 32768 fp32 row sums (rows > 32768 or
+ * in_features > 16384 return IVB_EINVAL); its address is looked up, and the kernel's shared-memory
+ * limit set, once per device on the first call with that device current, so make the first call on
+ * each device outside any stream capture. The cached address belongs to the device's primary context:
+ * do not use the library across a cudaDeviceReset. Calls that overlap in time on one device (other
  * streams or threads) share the scratch and race: serialise them. */
 int32_t ivb_ternary_gemv_splitk(const IvbTernary* m, const float* x, const float* norm_weight, float norm_eps,
                                 float norm_clip, float act_eps, int32_t epilogue, float* out, void* stream);
@@ -252,6 +259,16 @@ int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int3
 int32_t ivb_rows_amax(const float* x, int32_t rows, int32_t n, float* amax, void* stream);
 int32_t ivb_quantize_rows_amax(const float* x, int32_t rows, int32_t n, const float* amax, float act_eps, int8_t* q8,
                                int32_t ldq, float* scale, void* stream);
+
+/* Unit probe of the decode kernel's GEMV row routine (the hot path of every projection op of
+ * ivb_decoder_run; replaces the reference's gemv_prequant_store row loop, kernels/ternary.cu:302-354,
+ * and the CPU decoder's row_dot, cpu_decoder.py:73-86). `stage` (device) is one weight-stream chunk:
+ * [k rows x row_bytes packed q2 codes][k x scale_stride fp16 group scales, padded to 16 bytes]
+ * [k fp32 biases when has_bias]; q8 (device) the in_n int8 activation codes. out[r] = act_scale *
+ * sum_g scale[r][g] * sum_{j in g} (code[r][j] - 1) q8[j] (+ bias[r]), computed with 2^lanes_log lanes
+ * per row exactly as in the decode kernel (integer 64-input chunk dots, fp32 over the chunks). */
+int32_t ivb_decode_rows(const uint8_t* stage, int32_t k, int32_t row_bytes, int32_t scale_stride, int32_t has_bias,
+                        float act_scale, const int8_t* q8, int32_t in_n, int32_t lanes_log, float* out, void* stream);
 
 /* Debug/failure-detection probe: one CTA waits for a barrier count that never arrives, with a
  * bounded spin of timeout_ns; returns IVB_ETIMEOUT and leaves the context usable. */

@@ -142,6 +142,7 @@ SIGNATURES = {
     "ivb_ternary_gemv": (c_int32, [POINTER(IvbTernary), c_void_p, c_void_p, c_float, c_float, c_float, c_int32, c_void_p, c_void_p]),
     "ivb_quantize_rows": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_float, c_float, c_float, c_void_p, c_int32, c_void_p, c_void_p, c_void_p]),
     "ivb_ternary_gemm": (c_int32, [POINTER(IvbTernary), c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p, c_int32, c_void_p, c_void_p]),
+    "ivb_decode_rows": (c_int32, [c_void_p, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "ivb_ternary_gemv_splitk": (c_int32, [POINTER(IvbTernary), c_void_p, c_void_p, c_float, c_float, c_float, c_int32, c_void_p, c_void_p]),
     "ivb_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p]),
     "ivb_probe_wait_timeout": (c_int32, [c_void_p, c_void_p, c_uint64, c_void_p]),

@@ -741,7 +741,7 @@ int32_t launch_batch_attention(const IvbLayerDesc& L, const IvbBatchLayer& BL, c
 }
 
 struct BatchLayout {
-  size_t resid, ent, y, h, q8, scale, total;
+  size_t resid, ent, y, h, q8, scale, partial, total;
   int ldq;
 };
 
@@ -764,6 +764,7 @@ BatchLayout batch_layout(const IvbModelDesc& md, const IvbLayerDesc* layers, int
   L.h = take(T * std::max(F, d) * 4);
   L.q8 = take((T + 127) / 128 * 128 * L.ldq);
   L.scale = take(T * 4);
+  L.partial = take(kGemmPartialFloats * 4);  // split-K partial sums of this call's GEMMs
   L.total = o;
   return L;
 }
@@ -819,9 +820,10 @@ int32_t ivb_batch_decode(IvbDecoder* dec, const IvbBatch* bt, int32_t steps, voi
     const int ld = (n + 127) / 128 * 128;
     return ivb_quantize_rows(x, B, n, norm, eps, md.norm_clip, md.act_eps, q8, ld, scale, nullptr, stream);
   };
+  float* partial = reinterpret_cast<float*>(static_cast<unsigned char*>(workspace) + W.partial);
   auto gemm = [&](const IvbTernary& m, int epilogue, float* out, int ldo) -> int32_t {
     const int ld = (m.in_features + 127) / 128 * 128;
-    return ivb_ternary_gemm(&m, q8, ld, scale, B, epilogue, out, ldo, err, stream);
+    return ternary_gemm_into(&m, q8, ld, scale, B, epilogue, out, ldo, err, partial, kGemmPartialFloats, stream);
   };
   for (int step = 0; step < steps; ++step) {
     batch_embed_kernel<<<B, kThreads, 0, s>>>(md.head, bt->tokens, d, resid, bt->step);

@@ -54,6 +54,14 @@ int32_t check_ternary(const IvbTernary& m, const char* name);
 // True when the current device is compute capability 10.0 (B200 / sm_100a).
 bool device_is_sm100();
 
+// ivb_ternary_gemm with the split-K partial sums in `partial` (partial_floats floats of device memory;
+// nullptr: no split): ivb_decoder_prefill and ivb_batch_decode pass a slice of their own workspace, so
+// their calls share nothing with other calls on the device.
+constexpr size_t kGemmPartialFloats = size_t(1) << 22;
+int32_t ternary_gemm_into(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
+                          int32_t epilogue, float* out, int32_t ldo, uint32_t* error, float* partial, size_t partial_floats,
+                          void* stream);
+
 // The model description a decoder handle was created from (layers: its host array), and the device
 // error word that ivb_decoder_check reports.
 const IvbModelDesc& decoder_model(const IvbDecoder* dec, const IvbLayerDesc** layers);

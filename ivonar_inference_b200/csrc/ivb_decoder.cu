@@ -1132,6 +1132,31 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
   __syncthreads();
 }
 
+// Unit probe of the decode kernel's row routine: the stage (one stream chunk, k rows) goes to shared
+// memory, the int8 codes into the transposed GEMV layout with their half-chunk sums (what the quantiser
+// of the decode kernel writes), then rows_generic with 2^lg lanes per row stores the k row values.
+__global__ void __launch_bounds__(kThreads, 1) rows_probe_kernel(const unsigned char* stage, int stage_bytes, int k, int row_bytes,
+                                                                 int sstride, int has_bias, float act_scale, const int8_t* q8,
+                                                                 int in_n, int lg, float* out) {
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int padded = (in_n + 63) & ~63, chunks = padded >> 6;
+  unsigned char* st = smem;
+  int8_t* act = reinterpret_cast<int8_t*>(smem + round16(stage_bytes));
+  int* xhalf = reinterpret_cast<int*>(act + padded);
+  float* res = reinterpret_cast<float*>(xhalf + 2 * chunks);
+  for (int i = threadIdx.x; i < stage_bytes; i += kThreads) st[i] = stage[i];
+  for (int i = threadIdx.x; i < padded; i += kThreads) act[act_slot(i)] = i < in_n ? q8[i] : static_cast<int8_t>(0);
+  for (int h = threadIdx.x; h < 2 * chunks; h += kThreads) {
+    int sum = 0;
+    for (int i = 32 * h; i < 32 * h + 32; ++i) sum += i < in_n ? q8[i] : 0;
+    xhalf[h] = sum;
+  }
+  __syncthreads();
+  rows_generic(st, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, lg, res, EPI_STORE, nullptr, nullptr, 0u);
+  __syncthreads();
+  for (int r = threadIdx.x; r < k; r += kThreads) out[r] = res[r];
+}
+
 }  // namespace ivb
 
 // ------------------------------------------------------------------------------------------------
@@ -1778,6 +1803,28 @@ unsigned* decoder_error_word(const IvbDecoder* dec) {
 }  // namespace ivb
 
 extern "C" {
+
+int32_t ivb_decode_rows(const uint8_t* stage, int32_t k, int32_t row_bytes, int32_t scale_stride, int32_t has_bias,
+                        float act_scale, const int8_t* q8, int32_t in_n, int32_t lanes_log, float* out, void* stream) {
+  using namespace ivb;
+  if (stage == nullptr || q8 == nullptr || out == nullptr) return fail(IVB_EINVAL, "ivb_decode_rows: null argument");
+  if (k <= 0 || in_n <= 0 || lanes_log < 0 || lanes_log > 5 || scale_stride <= 0)
+    return fail(IVB_EINVAL, "ivb_decode_rows: bad shape");
+  if ((row_bytes & 15) != 0 || row_bytes < (in_n + 3) / 4)
+    return fail(IVB_EINVAL, "ivb_decode_rows: row_bytes must be a multiple of 16 holding the row");
+  const int chunks = (in_n + 63) / 64;
+  if (chunks > (kRowsKPL << lanes_log)) return fail(IVB_EINVAL, "ivb_decode_rows: more than %d chunks per lane", kRowsKPL);
+  const size_t stage_bytes = static_cast<size_t>(k) * row_bytes + round16(static_cast<size_t>(k) * scale_stride * 2) +
+                             (has_bias ? static_cast<size_t>(k) * 4 : 0);
+  const size_t smem = round16(stage_bytes) + static_cast<size_t>(chunks) * 64 + static_cast<size_t>(chunks) * 8 + static_cast<size_t>(k) * 4;
+  if (smem > 200 * 1024) return fail(IVB_EINVAL, "ivb_decode_rows: the chunk does not fit shared memory");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  IVB_CUDA(cudaFuncSetAttribute(rows_probe_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  rows_probe_kernel<<<1, kThreads, smem, s>>>(stage, static_cast<int>(stage_bytes), k, row_bytes, scale_stride, has_bias,
+                                              act_scale, q8, in_n, lanes_log, out);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
 
 int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** out) {
   using namespace ivb;

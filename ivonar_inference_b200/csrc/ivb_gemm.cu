@@ -394,10 +394,10 @@ __global__ void gemm_splitk_reduce_kernel(const float* partial, int splits, int 
   }
 }
 
-// Partial sums of split-K GEMM calls (token counts too small to fill the GPU with row tiles): a file-scope
-// device scratch, so the library allocates nothing; calls on one device use it one at a time.
-constexpr size_t kGemmScratch = size_t(1) << 22;  // floats
-static __device__ __align__(256) float g_gemm_partial[kGemmScratch];
+// Partial sums of split-K calls of the public ivb_ternary_gemm (token counts too small to fill the GPU
+// with row tiles): a file-scope device scratch, so the entry point allocates nothing; calls on one device
+// use it one at a time. The prefill and the batched decode bring their own (ternary_gemm_into).
+static __device__ __align__(256) float g_gemm_partial[kGemmPartialFloats];
 
 // One CTA per token row: the canonical quantiser (RMSNorm optional), codes written as 16-byte chunks of
 // the tiled GEMM activation layout (q8_chunk_offset, gemm_slot order inside a chunk), per-128-group sums
@@ -548,7 +548,7 @@ int32_t gemm_scratch(int dev, float** out) {
   std::lock_guard<std::mutex> guard(lock);
   if (table[dev] == nullptr) {
     void* p = nullptr;
-    IVB_CUDA(cudaGetSymbolAddress(&p, g_gemm_partial));
+    IVB_CUDA(cudaGetSymbolAddress(&p, g_gemm_partial));  // once per device
     table[dev] = static_cast<float*>(p);
   }
   *out = table[dev];
@@ -561,6 +561,19 @@ extern "C" {
 
 int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
                          int32_t epilogue, float* out, int32_t ldo, uint32_t* error, void* stream) {
+  using namespace ivb;
+  int dev = 0;
+  IVB_CUDA(cudaGetDevice(&dev));
+  float* partial = nullptr;
+  if (int32_t rc = gemm_scratch(dev, &partial)) return rc;
+  return ternary_gemm_into(m, q8, ldq, act_scale, rows_t, epilogue, out, ldo, error, partial, kGemmPartialFloats, stream);
+}
+
+}  // extern "C"
+
+int32_t ivb::ternary_gemm_into(const IvbTernary* m, const int8_t* q8, int32_t ldq, const float* act_scale, int32_t rows_t,
+                               int32_t epilogue, float* out, int32_t ldo, uint32_t* error, float* partial, size_t partial_floats,
+                               void* stream) {
   using namespace ivb;
   if (m == nullptr || q8 == nullptr || act_scale == nullptr || out == nullptr || error == nullptr)
     return fail(IVB_EINVAL, "ivb_ternary_gemm: null argument");
@@ -589,21 +602,16 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
     return fail(IVB_EINVAL, "ivb_ternary_gemm: cannot describe the packed weights to the TMA engine");
   // split-K when the row and token tiles leave most SMs idle (decode-sized token counts): at least four
-  // groups per split, at most 8 splits, the partials within the device scratch
+  // groups per split, at most 8 splits, the partials within the caller's scratch
   const int row_tiles = (m->rows + kGemmRows - 1) / kGemmRows, tok_tiles = (rows_t + kGemmTok - 1) / kGemmTok;
   int splits = 1;
-  if (groups >= 8 && row_tiles * tok_tiles < 96) {
+  if (partial != nullptr && groups >= 8 && row_tiles * tok_tiles < 96) {
     splits = std::min({groups / 4, std::max(1, 148 / (row_tiles * tok_tiles)), 8});
-    while (splits > 1 && static_cast<size_t>(splits) * rows_t * m->rows > kGemmScratch) --splits;
+    while (splits > 1 && static_cast<size_t>(splits) * rows_t * m->rows > partial_floats) --splits;
   }
   const int g_per = (groups + splits - 1) / splits;
   splits = (groups + g_per - 1) / g_per;
-  float* partial = nullptr;
-  if (splits > 1) {
-    int dev = 0;
-    IVB_CUDA(cudaGetDevice(&dev));
-    if (int32_t rc = gemm_scratch(dev, &partial)) return rc;
-  }
+  if (splits == 1) partial = nullptr;
   const dim3 grid(row_tiles, tok_tiles, splits);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // programmatic dependent launch: the kernel's set-up overlaps the tail of the previous kernel on the
@@ -630,6 +638,8 @@ int32_t ivb_ternary_gemm(const IvbTernary* m, const int8_t* q8, int32_t ldq, con
   }
   return IVB_OK;
 }
+
+extern "C" {
 
 int32_t ivb_rows_amax(const float* x, int32_t rows, int32_t n, float* amax, void* stream) {
   using namespace ivb;

@@ -756,7 +756,7 @@ __global__ void prefill_finish_kernel(const int64_t* tokens, int count, int pos_
 }
 
 struct PrefillLayout {
-  size_t resid, ent, y, h, q8, scale, err, coef, cum, xend, carry, kvq8, knope, vbuf, kvh, total;
+  size_t resid, ent, y, h, q8, scale, err, coef, cum, xend, carry, kvq8, knope, vbuf, kvh, partial, total;
   int ldq, groups, ld_ent;
 };
 
@@ -797,6 +797,7 @@ static PrefillLayout prefill_layout(const IvbModelDesc& md, const IvbLayerDesc* 
   const int dk_raw = std::max(md.nope_dim + md.rope_dim, md.head_dim);  // padded as launch_flash_attention does
   const size_t dk = dk_raw <= 16 ? 16 : dk_raw <= 32 ? 32 : dk_raw <= 64 ? 64 : 128;
   L.kvh = take(4 * static_cast<size_t>(md.heads) * ((P + 63) / 64 * 64) * dk * 2);
+  L.partial = take(kGemmPartialFloats * 4);  // split-K partial sums of this call's GEMMs
   L.total = o;
   return L;
 }
@@ -843,6 +844,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   float* knope = reinterpret_cast<float*>(ws + W.knope);
   float* vbuf = reinterpret_cast<float*>(ws + W.vbuf);
   __half* kvh = reinterpret_cast<__half*>(ws + W.kvh);
+  float* partial = reinterpret_cast<float*>(ws + W.partial);
   float* coefb = reinterpret_cast<float*>(ws + W.coef);
   float* cumb = reinterpret_cast<float*>(ws + W.cum);
   float* xendb = reinterpret_cast<float*>(ws + W.xend);
@@ -860,7 +862,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
   };
   auto gemm = [&](const IvbTernary& m, int epilogue, float* out, int ldo) -> int32_t {
     const int ld = (m.in_features + 127) / 128 * 128;
-    return ivb_ternary_gemm(&m, q8, ld, scale, count, epilogue, out, ldo, err, stream);
+    return ternary_gemm_into(&m, q8, ld, scale, count, epilogue, out, ldo, err, partial, kGemmPartialFloats, stream);
   };
   for (int li = 0; li < md.num_layers; ++li) {
     const IvbLayerDesc& L = layers[li];
@@ -900,9 +902,12 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       const int chunks = P * (ldl >> 4);
       IVB_CUDA(launch_pdl(latent_tile_kernel, dim3((chunks + 255) / 256), dim3(256), 0, s, L.latent_q, lpad, Lt, P, ldl, kvq8));
       IVB_CUDA(cudaGetLastError());
-      if (int32_t rc = ivb_ternary_gemm(&L.k_nope_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, knope, H * nope, err, stream))
+      if (int32_t rc = ternary_gemm_into(&L.k_nope_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, knope, H * nope, err, partial,
+                                         kGemmPartialFloats, stream))
         return rc;
-      if (int32_t rc = ivb_ternary_gemm(&L.v_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, vbuf, d, err, stream)) return rc;
+      if (int32_t rc = ternary_gemm_into(&L.v_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, vbuf, d, err, partial,
+                                         kGemmPartialFloats, stream))
+        return rc;
       if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, kvh, start_position, count, d, H, hd, rope,
                                               nope, md.max_len, rpad, y, s))
         return rc;

@@ -1,7 +1,9 @@
 // Split-K ternary GEMV of libivonar_b200.so: a variant of ivb_ternary_gemv for long inputs that
-// spreads the input columns over more CTAs and adds their partial row sums in a static device
-// scratch. The entry point allocates nothing: the scratch is a file-scope __device__ array whose
-// address is looked up once per device (cudaGetSymbolAddress) and cleared with a memset per call.
+// spreads the input columns over more CTAs. Each CTA writes the partial row sums of its column block
+// to a static device scratch (one slot per column block and row, so nothing is accumulated in place),
+// and the epilogue adds a row's partials in column-block order: the result does not depend on which
+// CTA finishes first. The entry point allocates nothing: the scratch is a file-scope __device__ array
+// whose address is looked up once per device (cudaGetSymbolAddress).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -13,17 +15,19 @@ size_t ivb_gemv_smem_bytes(int n);
 
 namespace ivb {
 
-constexpr int kSplitMaxRows = 32768;    // rows of the scratch: 128 KB of fp32 partial sums
+constexpr int kSplitMaxRows = 32768;    // rows of the scratch
 constexpr int kSplitMaxIn = 16384;      // input length (each CTA quantises it in shared memory)
 constexpr int kSplitChunks = 16;        // 64-input chunks per CTA column block (1024 inputs)
 constexpr int kSplitRows = 64;          // rows per CTA row block
+constexpr int kSplitMaxBlocks = (kSplitMaxIn / 64 + kSplitChunks - 1) / kSplitChunks;  // column blocks (16)
 
-static __device__ __align__(256) float g_split_acc[kSplitMaxRows];  // partial row sums (start at zero)
-static __device__ __align__(256) float g_split_scale[4];            // [0]: activation scale of the call
+// partial row sums [column block][row] (2 MB of fp32), and [0]: the activation scale of the call
+static __device__ __align__(256) float g_split_part[kSplitMaxBlocks * kSplitMaxRows];
+static __device__ __align__(256) float g_split_scale[4];
 
 // Grid (row blocks, column blocks). Every CTA quantises the whole input (the scale needs the
-// whole vector; same canonical quantiser as ivb_ternary_gemv), then adds, for each of its rows,
-// sum over its chunks of (integer chunk dot) * group scale into g_split_acc[row].
+// whole vector; same canonical quantiser as ivb_ternary_gemv), then writes, for each of its rows,
+// the sum over its chunks of (integer chunk dot) * group scale to g_split_part[column block][row].
 __global__ void __launch_bounds__(kThreads) splitk_partial_kernel(const IvbTernary m, const float* x, const float* norm_w,
                                                                   float norm_eps, float clip, float act_eps) {
   extern __shared__ __align__(16) unsigned char smem[];
@@ -55,16 +59,20 @@ __global__ void __launch_bounds__(kThreads) splitk_partial_kernel(const IvbTerna
     }
 #pragma unroll
     for (int off = 8; off > 0; off >>= 1) part += __shfl_xor_sync(kFull, part, off);
-    if (hl == 0 && r < r1) atomicAdd(g_split_acc + r, part);
+    if (hl == 0 && r < r1) g_split_part[static_cast<size_t>(blockIdx.y) * kSplitMaxRows + r] = part;
   }
 }
 
-// out[r] from the partial sums: act_scale, bias and the epilogue of ivb_ternary_gemv.
-__global__ void __launch_bounds__(kThreads) splitk_epilogue_kernel(const float* bias, int rows, int epilogue, float* out) {
+// out[r] from the partial sums (added in column-block order): act_scale, bias and the epilogue of
+// ivb_ternary_gemv.
+__global__ void __launch_bounds__(kThreads) splitk_epilogue_kernel(const float* bias, int rows, int blocks, int epilogue,
+                                                                   float* out) {
   const int i = blockIdx.x * kThreads + threadIdx.x;
   const float s = g_split_scale[0];
   auto value = [&](int r) {
-    float v = g_split_acc[r] * s;
+    float acc = g_split_part[r];
+    for (int b = 1; b < blocks; ++b) acc += g_split_part[static_cast<size_t>(b) * kSplitMaxRows + r];
+    float v = acc * s;
     if (bias != nullptr) v += __ldg(bias + r);
     return v;
   };
@@ -75,24 +83,27 @@ __global__ void __launch_bounds__(kThreads) splitk_epilogue_kernel(const float* 
   }
 }
 
-struct SplitSymbols {
-  float* acc = nullptr;
+struct SplitDevice {
+  float* part = nullptr;
   bool ready = false;
 };
 
-// Device addresses of the scratch, looked up once per device with that device current.
-static int32_t split_symbols(int dev, float** acc) {
+// Once per device, with that device current: the scratch address (the first call also loads the
+// module there) and the partial kernel's shared-memory limit for the longest input it accepts.
+static int32_t split_device(int dev, float** part) {
   static std::mutex lock;
-  static SplitSymbols table[64];
+  static SplitDevice table[64];
   if (dev < 0 || dev >= 64) return fail(IVB_EINVAL, "ivb_ternary_gemv_splitk: device %d out of range", dev);
   std::lock_guard<std::mutex> guard(lock);
   if (!table[dev].ready) {
     void* p = nullptr;
-    IVB_CUDA(cudaGetSymbolAddress(&p, g_split_acc));
-    table[dev].acc = static_cast<float*>(p);
+    IVB_CUDA(cudaGetSymbolAddress(&p, g_split_part));
+    IVB_CUDA(cudaFuncSetAttribute(splitk_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(ivb_gemv_smem_bytes(kSplitMaxIn))));
+    table[dev].part = static_cast<float*>(p);
     table[dev].ready = true;
   }
-  *acc = table[dev].acc;
+  *part = table[dev].part;
   return IVB_OK;
 }
 
@@ -115,18 +126,17 @@ int32_t ivb_ternary_gemv_splitk(const IvbTernary* m, const float* x, const float
     return fail(IVB_EINVAL, "ivb_ternary_gemv_splitk: %d inputs exceed the %d-input limit", m->in_features, kSplitMaxIn);
   int dev = 0;
   IVB_CUDA(cudaGetDevice(&dev));
-  float* acc = nullptr;
-  if (int32_t rc = split_symbols(dev, &acc)) return rc;
+  float* part = nullptr;
+  if (int32_t rc = split_device(dev, &part)) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const size_t smem = ivb_gemv_smem_bytes(m->in_features);
-  IVB_CUDA(cudaFuncSetAttribute(splitk_partial_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  IVB_CUDA(cudaMemsetAsync(acc, 0, static_cast<size_t>(m->rows) * sizeof(float), s));
   const int chunks = (m->in_features + 63) / 64;
-  const dim3 grid((m->rows + kSplitRows - 1) / kSplitRows, (chunks + kSplitChunks - 1) / kSplitChunks);
+  const int blocks = (chunks + kSplitChunks - 1) / kSplitChunks;
+  const dim3 grid((m->rows + kSplitRows - 1) / kSplitRows, blocks);
   splitk_partial_kernel<<<grid, kThreads, smem, s>>>(*m, x, norm_weight, norm_eps, norm_clip, act_eps);
   IVB_CUDA(cudaGetLastError());
   const int outs = epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows;
-  splitk_epilogue_kernel<<<(outs + kThreads - 1) / kThreads, kThreads, 0, s>>>(m->bias, m->rows, epilogue, out);
+  splitk_epilogue_kernel<<<(outs + kThreads - 1) / kThreads, kThreads, 0, s>>>(m->bias, m->rows, blocks, epilogue, out);
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }

@@ -92,3 +92,37 @@ def test_large_batch_streams_equal_single_sequence_streams() -> None:
     for b in (0, 57, 127):
         want, _ = _run_single(model, prompts[b], seeds[b], 1.0, 1, 4.0, count, max_len)
         assert [first[b]] + rest[b].tolist() == want, b
+
+
+def test_batched_greedy_streams_match_the_oracle(oracle_lib) -> None:
+    """Every sequence of a batch against the CPU oracle decoding it alone: 48-token penalised greedy
+    streams, identical or parting only where the oracle's own top two scores (teacher-forced along the
+    common prefix) are within twice the decoder-vs-oracle bar of 0.02."""
+    from conftest import first_difference, penalised_scores
+    from ivonar_inference_b200 import synthetic
+    from ivonar_inference_b200.batch import B200BatchDecoder
+
+    model = synthetic.synthetic_model(synthetic.config0(seq_len=96), 0)
+    prompts = [synthetic.random_prompt(512, n, seed=s)[0] for n, s in ((16, 1), (9, 2), (23, 3), (16, 4), (31, 5))]
+    count = 48
+    batch = B200BatchDecoder(model, len(prompts), max_len=96, device="cuda")
+    first = batch.start(prompts, list(range(len(prompts))), 1.0, 1, 4.0)
+    rest = batch.decode(count - 1).cpu().numpy()
+    ora = oracle_lib.OracleDecoder(model, max_len=96)
+    identical = 0
+    for b, prompt in enumerate(prompts):
+        got = [int(first[b])] + rest[b].tolist()
+        ora.prefill(prompt.numpy())
+        ora.configure_sampling(1.0, 1, 4.0)
+        want = [ora.sample()]
+        want += ora.generate(want[0], count - 1)
+        d = first_difference(got, want)
+        if d < count:
+            logits = ora.prefill(prompt.numpy()).copy()
+            for tok in want[:d]:
+                logits = ora.step(int(tok)).copy()
+            s = penalised_scores(logits, want[:d], 4.0)
+            assert float(s[want[d]] - s[got[d]]) < 0.04, (b, d)
+        else:
+            identical += 1
+    assert identical >= len(prompts) - 1

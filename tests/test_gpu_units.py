@@ -226,3 +226,79 @@ def test_a_wait_that_never_completes_gives_up_and_the_gpu_stays_usable() -> None
     assert int(counter.item()) == 1
     x = torch.arange(10, device="cuda", dtype=torch.float32)
     assert float((x * 2).sum()) == 90.0
+
+
+def _stream_chunk(packed: np.ndarray, scales_u16: np.ndarray, bias, in_n: int) -> tuple[torch.Tensor, int, int]:
+    """One weight-stream chunk of the decode kernel: packed rows padded to 16 bytes (plus 16 when a
+    multiple of 128, as the plan lays them out), the fp16 scale rows padded to 8 entries, the biases."""
+    rows = packed.shape[0]
+    rb = (packed.shape[1] + 15) // 16 * 16
+    if rb % 128 == 0:
+        rb += 16
+    stride = ((in_n + 127) // 128 + 7) // 8 * 8
+    w = np.zeros((rows, rb), np.uint8)
+    w[:, : packed.shape[1]] = packed
+    sc = np.zeros((rows, stride), np.uint16)
+    sc[:, : scales_u16.shape[1]] = scales_u16
+    blob = w.tobytes() + sc.tobytes()
+    blob += b"\0" * ((-len(blob)) % 16)
+    if bias is not None:
+        blob += np.asarray(bias, np.float32).tobytes()
+    return torch.from_numpy(np.frombuffer(blob, np.uint8).copy()).cuda(), rb, stride
+
+
+def _decode_rows(chunk, rows, rb, stride, has_bias, act_scale, q8, in_n, lg) -> np.ndarray:
+    nat = _native()
+    q = torch.from_numpy(np.ascontiguousarray(q8, np.int8)).cuda()
+    out = torch.zeros(rows, dtype=torch.float32, device="cuda")
+    nat.check(nat.library().ivb_decode_rows(chunk.data_ptr(), rows, rb, stride, int(has_bias), float(act_scale), q.data_ptr(),
+                                            in_n, lg, out.data_ptr(), _stream()), "ivb_decode_rows")
+    torch.cuda.synchronize()
+    return out.cpu().numpy()
+
+
+def test_decode_row_routine_gives_the_reference_integer_dots() -> None:
+    """The decode kernel's GEMV row routine at every lane width it can run with: with a one-hot group
+    scale (1.0) and act_scale 1 each output is the exact integer dot of one 128-input group, equal bit
+    for bit to the reference's numba row_dot on the same codes (tests/golden/ternary.npz)."""
+    g = golden("ternary")
+    checked = 0
+    for k in range(int(g["count"])):
+        packed, scales, q8, dots = g[f"packed{k}"], g[f"scales{k}"], g[f"q8_{k}"], g[f"dots{k}"]
+        rows, groups = dots.shape
+        in_n = int(g[f"in{k}"])
+        chunks = (in_n + 63) // 64
+        for lg in range(5):
+            if chunks > 4 << lg:
+                continue
+            for grp in range(groups):
+                onehot = np.zeros_like(scales)
+                onehot[:, grp] = 0x3C00  # fp16 1.0
+                chunk, rb, stride = _stream_chunk(packed, onehot, None, in_n)
+                out = _decode_rows(chunk, rows, rb, stride, False, 1.0, q8, in_n, lg)
+                assert np.array_equal(out, dots[:, grp].astype(np.float32)), (k, lg, grp)
+                checked += 1
+    assert checked == 76  # every group of the six golden shapes at every lane width that holds them
+
+
+def test_decode_row_routine_matches_the_reference_gemv(oracle_lib) -> None:
+    """With the real group scales and biases the row routine equals the reference's numba gemv output
+    (its fp32 sum over groups, here over 64-input chunks: same float tolerance as the unit GEMV) and the
+    oracle's GEMV, for every lane width."""
+    g = golden("ternary")
+    for k in range(int(g["count"])):
+        packed, scales, q8, bias = g[f"packed{k}"], g[f"scales{k}"], g[f"q8_{k}"], g[f"bias{k}"]
+        in_n = int(g[f"in{k}"])
+        rows = packed.shape[0]
+        act_scale = float(g[f"act_scale{k}"])
+        mat = oracle_lib.Matrix.raw(packed, scales, in_n, bias)
+        want = np.zeros(rows, np.float32)
+        mat.gemv(np.ascontiguousarray(q8, np.int8), act_scale, want)
+        chunks = (in_n + 63) // 64
+        chunk, rb, stride = _stream_chunk(packed, scales, bias, in_n)
+        for lg in range(5):
+            if chunks > 4 << lg:
+                continue
+            out = _decode_rows(chunk, rows, rb, stride, True, act_scale, q8, in_n, lg)
+            np.testing.assert_allclose(out, g[f"gemv{k}"], rtol=1e-5, atol=1e-6)
+            np.testing.assert_allclose(out, want, rtol=1e-5, atol=1e-6)

@@ -1,4 +1,4 @@
-"""ivb_ternary_gemv_splitk (static scratch, no allocation) against ivb_ternary_gemv on a B200.
+"""ivb_ternary_gemv_splitk (static scratch, no allocation) against the CPU oracle on a B200.
 
 The split-K entry point serves callers that may not allocate device memory when they call it (a server
 whose memory pool already holds the GPU, or a path that cannot take cudaMalloc's synchronisation).
@@ -38,29 +38,35 @@ def _matrix(gen, rows: int, cols: int):
 
 @pytest.mark.parametrize("epilogue", [0, 1, 2])
 @pytest.mark.parametrize("normed", [False, True])
-def test_splitk_matches_the_gemv_entry_point_on_two_calls_in_a_row(epilogue: int, normed: bool) -> None:
+def test_splitk_matches_the_oracle_and_repeats_bit_for_bit(oracle_lib, epilogue: int, normed: bool) -> None:
+    """Against the CPU oracle's quantiser and GEMV (same codes, fp32 sums in another order), up to the
+    largest input the scratch takes (16384); two calls in a row give the same bits (the column blocks'
+    partial sums are added in a fixed order)."""
     nat, lib = _lib()
     gen = torch.Generator().manual_seed(70 + 3 * epilogue + int(normed))
     stream = torch.cuda.current_stream().cuda_stream
-    for rows, cols in ((1024, 2816), (64, 100), (5632, 1024), (32768, 1024), (8, 11008)):
-        desc, keep = _matrix(gen, rows, cols)
-        x = torch.randn(cols, generator=gen).cuda()
-        w = (1.0 + 0.1 * torch.randn(cols, generator=gen)).cuda()
+    for rows, cols in ((1024, 2816), (64, 100), (5632, 1024), (32768, 1024), (8, 11008), (64, 16384)):
+        desc, (p, sc, b) = _matrix(gen, rows, cols)
+        x = torch.randn(cols, generator=gen)
+        w = 1.0 + 0.1 * torch.randn(cols, generator=gen)
         out_rows = rows // 2 if epilogue == 2 else rows
-        base = torch.randn(out_rows, generator=gen).cuda()
-        want = base.clone()
-        nat.check(lib.ivb_ternary_gemv(ctypes.byref(desc), x.data_ptr(), w.data_ptr() if normed else 0, 1e-6, 8.0,
-                                       1e-5, epilogue, want.data_ptr(), stream), "ivb_ternary_gemv")
+        base = torch.randn(out_rows, generator=gen)
+        q8, act_scale, _ = oracle_lib.quantize(x.numpy(), w.numpy() if normed else None, 1e-6, 8.0, 1e-5)
+        mat = oracle_lib.Matrix.raw(p.cpu().numpy(), sc.cpu().numpy().view(np.uint16), cols, b.cpu().numpy())
+        want = base.numpy().copy()
+        mat.gemv(q8, act_scale, want, epilogue)
+        results = []
+        xd, wd = x.cuda(), w.cuda()  # kept alive until the kernels ran (the allocator reuses freed blocks)
         for call in range(2):
-            got = base.clone()
-            nat.check(lib.ivb_ternary_gemv_splitk(ctypes.byref(desc), x.data_ptr(), w.data_ptr() if normed else 0, 1e-6,
-                                                  8.0, 1e-5, epilogue, got.data_ptr(), stream), "ivb_ternary_gemv_splitk")
+            got = base.cuda()
+            nat.check(lib.ivb_ternary_gemv_splitk(ctypes.byref(desc), xd.data_ptr(), wd.data_ptr() if normed else 0,
+                                                  1e-6, 8.0, 1e-5, epilogue, got.data_ptr(), stream), "ivb_ternary_gemv_splitk")
             torch.cuda.synchronize()
-            ref = want.cpu().numpy()
-            scale = float(np.abs(ref).max()) + 1e-6
-            # the tolerance of the GEMV parity test (accumulation order differs)
-            np.testing.assert_allclose(got.cpu().numpy(), ref, rtol=2e-5, atol=2e-5 * scale,
-                                       err_msg=f"{rows}x{cols} call {call}")
+            results.append(got.cpu().numpy())
+        assert np.array_equal(results[0], results[1]), f"{rows}x{cols}: two calls differ"
+        scale = float(np.abs(want).max()) + 1e-6
+        # same integer chunk dots; fp32 group sums in another order (and CUDA's expf in the SwiGLU)
+        np.testing.assert_allclose(results[0], want, rtol=2e-5, atol=2e-5 * scale, err_msg=f"{rows}x{cols}")
 
 
 def test_splitk_rejects_inputs_larger_than_its_scratch() -> None:
