@@ -72,7 +72,8 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-gpu-reference", action="store_true", help="skip the reference KernelDecoder on this GPU")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
-    ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks)")
+    ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks) at N=1")
+    ap.add_argument("--no-tp", action="store_true", help="skip config 4, which runs by default on more than one GPU")
     ap.add_argument("--only", choices=("prefill", "gemm", "tp", "batch"), default=None,
                     help="run one secondary measurement alone (for profiler captures): a prefill of "
                          "--prefill-tokens tokens, the prefill GEMM on the gate/up shape, config 4, or "
@@ -124,6 +125,21 @@ def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
     kv = sum(per_pos * (p + 1) for p in range(first_position, first_position + tokens)) + per_pos * tokens
     total = tokens * (weights + state) + kv
     return float(total), {"weights_per_token": weights, "state_per_token": state, "kv_bytes_per_position": per_pos}
+
+
+def batch_roofline(model, sequences: int, first_position: int, steps: int, ms: float) -> dict:
+    """Per-GPU HBM roofline of config 3's timed decode steps: every step reads the packed weights once
+    for all of the GPU's sequences, and each sequence's recurrent state (read and written) and latent
+    cache up to its position."""
+    per_step_weights, parts = decode_bytes(model, first_position, 1)
+    weights, state, per_pos = parts["weights_per_token"], parts["state_per_token"], parts["kv_bytes_per_position"]
+    kv = sum(per_pos * (p + 2) for p in range(first_position, first_position + steps))
+    total = steps * (weights + sequences * state) + sequences * kv
+    peak, peak_kind = measured_peaks()
+    achieved = total / (ms / 1000.0) / 1e9
+    return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+            "peak_source": peak_kind, "bytes_per_gpu": total,
+            "bytes": "per step: packed weights once + per sequence (SSM state read+write + latent cache to its position)"}
 
 
 class ClockSampler:
@@ -356,8 +372,13 @@ def batch_measure(device, world: int, rank: int, tokens: int = BATCH_TOKENS, ker
     return out
 
 
-def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps: int = 20) -> dict:
-    """Config 2 at b=1: prefill tok/s per prompt length, and the GEMM's int8 tensor-core throughput."""
+PREFILL_BATCH = 8
+
+
+def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps: int = 20, batch: int = PREFILL_BATCH) -> dict:
+    """Config 2: prefill tok/s per prompt length at batch 1 and at batch `batch` (that many independent
+    requests, each its own B200Decoder prefilling its own prompt on its own stream, so their kernels
+    overlap), and the GEMM's int8 tensor-core throughput."""
     import ctypes
 
     import torch
@@ -366,22 +387,47 @@ def prefill_measure(device, lengths=((512, 3), (2048, 2), (8192, 1)), gemm_reps:
     from ivonar_inference_b200 import _native as native
 
     model = synthetic.synthetic_model(synthetic.config1(seq_len=8192), seed=0)
-    result: dict = {"batch": 1, "tok_s": {}, "ms": {}}
+    result: dict = {"batch": [1, batch], "tok_s": {}, "ms": {}, "tok_s_batch": {}, "ms_batch": {},
+                    "batch_note": f"{batch} independent prompts of the same length, one decoder and one CUDA stream each, "
+                                  "timed together (CUDA events on the launching stream, all streams joined)"}
+    longest = max((length for length, _ in lengths), default=0)
+    decs = [B200Decoder(model, max_len=longest, device=device) for _ in range(batch)] if lengths else []
+    streams = [torch.cuda.Stream(device=device) for _ in range(batch)]
     for length, reps in lengths:
-        dec = B200Decoder(model, max_len=length, device=device)
-        prompt = synthetic.random_prompt(32768, length, seed=length).to(device)
-        dec.prefill(prompt)
+        prompts = [synthetic.random_prompt(32768, length, seed=length + i).to(device) for i in range(batch)]
+        decs[0].prefill(prompts[0])
         torch.cuda.synchronize(device)
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record()
         for _ in range(reps):
-            dec.prefill(prompt)
+            decs[0].prefill(prompts[0])
         end.record()
         torch.cuda.synchronize(device)
         ms = start.elapsed_time(end) / reps
         result["tok_s"][str(length)] = length / (ms / 1000.0)
         result["ms"][str(length)] = ms
-        del dec
+        main = torch.cuda.current_stream(device)
+
+        def all_prefills() -> None:
+            for dec, prompt, st in zip(decs, prompts, streams):
+                st.wait_stream(main)
+                with torch.cuda.stream(st):
+                    dec.prefill(prompt)
+            for st in streams:
+                main.wait_stream(st)
+
+        all_prefills()  # warm-up (workspaces, tensor maps)
+        torch.cuda.synchronize(device)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record()
+        for _ in range(reps):
+            all_prefills()
+        end.record()
+        torch.cuda.synchronize(device)
+        ms_b = start.elapsed_time(end) / reps
+        result["tok_s_batch"][str(length)] = batch * length / (ms_b / 1000.0)
+        result["ms_batch"][str(length)] = ms_b
+    del decs
     torch.cuda.empty_cache()
     lib = native.library()
     gen = torch.Generator().manual_seed(0)
@@ -543,7 +589,7 @@ def run_b200(args) -> None:
 
     ctas, phases = dec.ctas, dec.num_phases
     tp_line = None
-    if args.tp:
+    if args.tp or (world > 1 and not args.no_tp):
         tp_line = tp_measure(device, world, rank)
     batched = None
     if not args.no_batch:
@@ -558,6 +604,8 @@ def run_b200(args) -> None:
                    "unit": "tok/s", "sequences": seqs, "sequences_per_gpu": part["sequences_per_gpu"],
                    "prompt": BATCH_PROMPT, "timed_steps": part["steps"], "ms": float(batch_ms.item()),
                    "ms_per_step": float(batch_ms.item()) / part["steps"], "parallelism": f"dp{world}"}
+        batched["roofline"] = batch_roofline(model, part["sequences_per_gpu"], BATCH_PROMPT + 1 + BATCH_WARM, part["steps"],
+                                             float(batch_ms.item()))
 
     if rank == 0:
         peak, peak_kind = measured_peaks()

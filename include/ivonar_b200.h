@@ -265,8 +265,9 @@ int32_t ivb_quantize_rows_amax(const float* x, int32_t rows, int32_t n, const fl
  * and the CPU decoder's row_dot, cpu_decoder.py:73-86). `stage` (device) is one weight-stream chunk:
  * [k rows x row_bytes packed q2 codes][k x scale_stride fp16 group scales, padded to 16 bytes]
  * [k fp32 biases when has_bias]; q8 (device) the in_n int8 activation codes. out[r] = act_scale *
- * sum_g scale[r][g] * sum_{j in g} (code[r][j] - 1) q8[j] (+ bias[r]), computed with 2^lanes_log lanes
- * per row exactly as in the decode kernel (integer 64-input chunk dots, fp32 over the chunks). */
+ * sum_g scale[r][g] * sum_{j in g} (code[r][j] - 1) q8[j] (+ bias[r]), computed as in the decode kernel
+ * (integer 64-input chunk dots, fp32 over the chunks): lanes_log = -1 runs the kernel's own choice of
+ * routine for the shape; 0..5 the general routine with 2^lanes_log lanes per row. */
 int32_t ivb_decode_rows(const uint8_t* stage, int32_t k, int32_t row_bytes, int32_t scale_stride, int32_t has_bias,
                         float act_scale, const int8_t* q8, int32_t in_n, int32_t lanes_log, float* out, void* stream);
 

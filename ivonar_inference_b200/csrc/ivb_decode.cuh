@@ -360,6 +360,75 @@ __device__ __forceinline__ int chunk_dot64(const uint4 w, const ActChunk& a) {
 // rows interleaved; the two rows' lane groups sit in one warp, lg <= 4).
 enum RowsEpi { EPI_STORE = 0, EPI_RESID = 1, EPI_PUBLISH = 2, EPI_SWIGLU = 3 };
 
+// rows_generic with the lane geometry fixed at compile time (2^LG lanes per row, KPL chunks per lane,
+// RPT rows per lane group in one pass, interleaved): every thread of the CTA runs every pass (a lane
+// group past the last row recomputes row k - 1 and stores nothing), so the lane butterflies are
+// full-warp shuffles of a fixed length; each chunk's product has its own accumulator (added in chunk
+// order at the end), so the chunk dots of a lane run side by side.
+template <int LG, int KPL, int RPT>
+__device__ __forceinline__ void rows_ct(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias, float act_scale,
+                                        const int8_t* act, const int* xhalf, int in_n, float* out, int epi, unsigned long long* ll,
+                                        const float* resid, unsigned flag) {
+  constexpr int kLpr = 1 << LG, kRpi = kThreads >> LG;
+  const int chunks = (in_n + 63) >> 6;
+  const int sub = threadIdx.x & (kLpr - 1), grp = threadIdx.x >> LG;
+  ActChunk a[KPL];
+  bool have[KPL];
+#pragma unroll
+  for (int j = 0; j < KPL; ++j) {
+    const int u = sub + (j << LG);
+    have[j] = u < chunks;
+    if (have[j]) {
+      a[j] = load_act_chunk(act, nullptr, u, xhalf);
+    } else {
+#pragma unroll
+      for (int q = 0; q < 4; ++q) a[j].q[q] = make_int4(0, 0, 0, 0);
+      a[j].xsum = 0;
+    }
+  }
+  const uint16_t* scales = reinterpret_cast<const uint16_t*>(stage + static_cast<size_t>(k) * row_bytes);
+  const float* bias = reinterpret_cast<const float*>(stage + static_cast<size_t>(k) * row_bytes + round16(k * sstride * 2));
+  const int passes = (k + kRpi * RPT - 1) / (kRpi * RPT);
+  for (int pass = 0; pass < passes; ++pass) {
+    float v[RPT];
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      const int rr = min(pass * kRpi * RPT + t * kRpi + grp, k - 1);
+      const uint4* wr = reinterpret_cast<const uint4*>(stage + rr * row_bytes);
+      const uint16_t* srow = scales + rr * sstride;
+      float part[KPL];
+#pragma unroll
+      for (int j = 0; j < KPL; ++j) {
+        const int u = sub + (j << LG);
+        part[j] = have[j] ? static_cast<float>(chunk_dot64(wr[u], a[j])) * (h2f(srow[u >> 1]) * (1.0f / 64.0f)) : 0.0f;
+      }
+      float acc = part[0];
+#pragma unroll
+      for (int j = 1; j < KPL; ++j) acc += part[j];
+      v[t] = acc;
+    }
+#pragma unroll
+    for (int off = 1; off < kLpr; off <<= 1)
+#pragma unroll
+      for (int t = 0; t < RPT; ++t) v[t] += __shfl_xor_sync(kFull, v[t], off);
+#pragma unroll
+    for (int t = 0; t < RPT; ++t) {
+      const int r = pass * kRpi * RPT + t * kRpi + grp;
+      const bool valid = r < k;
+      const int rr = valid ? r : k - 1;
+      const float x = has_bias ? v[t] * act_scale + bias[rr] : v[t] * act_scale;
+      if (epi == EPI_SWIGLU) {
+        const float up = __shfl_down_sync(kFull, x, kLpr);  // row r + 1 (up) is the next lane group of the warp
+        if (valid && sub == 0 && (r & 1) == 0) ll_store(ll + (r >> 1), __float_as_uint(silu_f(x) * up), flag);
+      } else if (valid && sub == 0) {
+        if (epi == EPI_STORE) out[r] = x;
+        else if (epi == EPI_RESID) ll_store(ll + r, __float_as_uint(resid[r] + x), flag);
+        else ll_store(ll + r, __float_as_uint(x), flag);
+      }
+    }
+  }
+}
+
 // Rows [0, k) of one stream chunk laid out [k x row_bytes packed][k x sstride fp16 (16B pad)][k x fp32
 // bias] against the quantised input `act` (transposed GEMV layout, in_n inputs): 2^lg lanes per row
 // (lg <= 5), lane `sub` owning the 64-input chunks sub + j * 2^lg (j < 4, so in_n <= 256 * 2^lg), their
@@ -416,6 +485,24 @@ __device__ __forceinline__ void rows_generic(const unsigned char* stage, int k, 
       else ll_store(ll + r, __float_as_uint(v), flag);
     }
   }
+}
+
+// The row routine the decode kernel runs on a chunk of k rows: the compile-time geometries for the
+// Nano shapes (1024 inputs: 16 lanes per row for up to 16 rows, 8 lanes x 2 rows for up to 64, 8 lanes
+// x 8 rows for up to 256; 2049-4096 inputs and up to 8 rows outside gate/up: 32 lanes), rows_generic
+// with 2^lg lanes per row for every other shape.
+__device__ __forceinline__ void rows_decode(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias,
+                                            float act_scale, const int8_t* act, const int* xhalf, int in_n, int lg, float* out,
+                                            int epi, unsigned long long* ll, const float* resid, unsigned flag) {
+  const int chunks = (in_n + 63) >> 6;
+  if (chunks == 16) {
+    if (k <= 16) return rows_ct<4, 1, 1>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
+    if (k <= 64) return rows_ct<3, 2, 2>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
+    if (k <= 256) return rows_ct<3, 2, 8>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
+  } else if (chunks > 32 && chunks <= 64 && k <= 8 && epi != EPI_SWIGLU) {
+    return rows_ct<5, 2, 1>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
+  }
+  rows_generic(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, lg, out, epi, ll, resid, flag);
 }
 
 // ---- top-k selection (radix select over order-preserving keys) ----------------------------------

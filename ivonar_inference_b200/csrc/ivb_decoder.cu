@@ -279,20 +279,70 @@ __device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims
   return a;
 }
 
+// Scores of the npos positions of a tile: LPP lanes per position, lane q taking the 16-byte chunks q,
+// q + LPP, ... of the position's latent row and of qa (all positions read the same qa chunk at the same
+// time, so those reads are broadcasts), the lane sums added by a butterfly over the LPP lanes; the
+// score (a_t dot + rope term + qb) goes to A.sc[k]. Returns the thread's maximum score. LC: chunks per
+// row when known at compile time (0: lc chunks).
+template <int LPP, int LC>
+__device__ __forceinline__ float attn_scores(const AttnSmem& A, const TileBuf& tb, int lc_rt, int npos, int lpad, int rope, int rpad,
+                                             float qb) {
+  constexpr int kPerPass = kThreads / LPP;
+  constexpr int kIters = (LC > 0 ? LC : 32) / LPP;  // chunks per lane (rows hold at most 32 chunks)
+  const int lc = LC > 0 ? LC : lc_rt;
+  const int tid = threadIdx.x, q = tid & (LPP - 1);
+  float wmax = -INFINITY;
+  for (int k0 = 0; k0 < npos; k0 += kPerPass) {
+    const int k = k0 + tid / LPP;
+    float dot = 0.0f;
+    if (k < npos) {
+      const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
+      float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+#pragma unroll
+      for (int i = 0; i < kIters; ++i) {
+        const int ch = q + LPP * i;
+        if (LC > 0 || ch < lc) {
+          const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * ch);
+          const float4* qa = reinterpret_cast<const float4*>(A.qa + 16 * ch);
+          const unsigned wv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float4 qq = qa[t];
+            float f[4];
+            bytes_to_f32(wv[t], f);
+            d0 = fmaf(qq.x, f[0], d0);
+            d1 = fmaf(qq.y, f[1], d1);
+            d2 = fmaf(qq.z, f[2], d2);
+            d3 = fmaf(qq.w, f[3], d3);
+          }
+        }
+      }
+      dot = (d0 + d1) + (d2 + d3);
+    }
+#pragma unroll
+    for (int o = 1; o < LPP; o <<= 1) dot += __shfl_xor_sync(kFull, dot, o);  // a position's lanes are in or out together
+    if (k < npos) {
+      float rp = 0.0f;
+      for (int r = 0; r < rope; ++r) rp = fmaf(A.qr[r], h2f(tb.kr[k * rpad + r]), rp);
+      const float sc = fmaf(tb.lsc[k], dot, rp) + qb;
+      if (q == 0) A.sc[k] = sc;
+      wmax = fmaxf(wmax, sc);
+    }
+  }
+  return wmax;
+}
+
 // The tile loop of the attention op: online softmax over the cached positions, tile by tile, the current
-// position as the extra last row of the last tile. Scores: a thread pair per position, thread h taking the
-// 16-byte chunks of the row with parity h, rotated by the position so that the 8 lanes of a shared-memory
-// phase read 8 different banks groups. Weighted latent sum: lane group g = lane / 8 of warp w takes the
-// positions 4w + g + 32i, lane s = lane % 8 owns the chunks s, s + 8, ... (CPL of them, 16 latent
-// entries each) in registers. Returns false when a tile's wait ran out; m_run, l_run and the per-lane
+// position as the extra last row of the last tile. Scores: attn_scores. Weighted latent sum: lane group
+// g = lane / 8 of warp w takes the positions 4w + g + 32i, lane s = lane % 8 owns the chunks s, s + 8,
+// ... (CPL of them, 16 latent entries each) in registers. Returns false when a tile's wait ran out; m_run, l_run and the per-lane
 // partial sums `acc` (scaled by exp(-m_run)) are the results.
-template <int CPL>
+template <int CPL, int LC>
 __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const DecodeDims& D, const IvbLayerDesc& L,
                                            const AttnSmem& A, int h, int P, float a_cur, float qb, float& m_run,
                                            float& l_run, float (&acc)[16 * CPL]) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sub = lane & 7, grp = lane >> 3;
-  const int lc = D.lpad >> 4;  // 16-byte chunks per cached row (<= 8 * CPL)
-  const bool pow2 = (lc & (lc - 1)) == 0;
+  const int lc = LC > 0 ? LC : D.lpad >> 4;  // 16-byte chunks per cached row (<= 8 * CPL)
   const int rope = D.rope, rpad = D.rpad, lpad = D.lpad, tile = D.tile;
   float* const red = c.red;
   unsigned long long* const abar = c.abar;
@@ -328,47 +378,13 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
       __syncthreads();
     }
     const int npos = count + (last ? 1 : 0);
-    // scores
-    float wmax = -INFINITY;
-    for (int k0 = 0; k0 < npos; k0 += kThreads / 2) {
-      const int k = k0 + (tid >> 1), hh = tid & 1;
-      float s = -INFINITY, dot = 0.0f;
-      if (k < npos) {
-        const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
-        const int skew = pow2 ? ((2 * k) & (lc - 1)) : 0;
-        float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
-#pragma unroll
-        for (int i = 0; i < 4 * CPL; ++i) {
-          if (2 * i + hh < lc) {
-            const int ch = pow2 ? ((2 * i + hh + skew) & (lc - 1)) : 2 * i + hh;
-            const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * ch);
-            const float4* q = reinterpret_cast<const float4*>(A.qa + 16 * ch);
-            const unsigned wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const float4 qq = q[t];
-              float f[4];
-              bytes_to_f32(wv[t], f);
-              d0 = fmaf(qq.x, f[0], d0);
-              d1 = fmaf(qq.y, f[1], d1);
-              d2 = fmaf(qq.z, f[2], d2);
-              d3 = fmaf(qq.w, f[3], d3);
-            }
-          }
-        }
-        dot = (d0 + d1) + (d2 + d3);
-      }
-      dot += __shfl_xor_sync(kFull, dot, 1);  // both threads of a pair are in or out of range together
-      if (k < npos) {
-        float rp = 0.0f;
-        for (int r = 0; r < rope; ++r) rp = fmaf(A.qr[r], h2f(tb.kr[k * rpad + r]), rp);
-        s = fmaf(tb.lsc[k], dot, rp) + qb;
-        if (hh == 0) A.sc[k] = s;
-      }
-      wmax = fmaxf(wmax, s);
-    }
-    wmax = warp_max(wmax);
-    if (lane == 0) red[32 + warp] = wmax;  // block_sum below uses red[0 .. kWarps)
+    // scores: 8, 4 or 2 lanes per position as the tile is short or long (a short tile's single pass
+    // is latency-bound; a long one is bound by the shared-memory reads)
+    const float wmax = npos <= kThreads / 8   ? attn_scores<8, LC>(A, tb, lc, npos, lpad, rope, rpad, qb)
+                       : npos <= kThreads / 4 ? attn_scores<4, LC>(A, tb, lc, npos, lpad, rope, rpad, qb)
+                                              : attn_scores<2, LC>(A, tb, lc, npos, lpad, rope, rpad, qb);
+    const float wm = warp_max(wmax);  // every lane takes part in the shuffles
+    if (lane == 0) red[32 + warp] = wm;  // block_sum below uses red[0 .. kWarps)
     __syncthreads();
     float mx = red[32];
     for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red[32 + w]);
@@ -504,17 +520,19 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
   bool tiles_ok;
   if (lc <= 8) {
     float acc[16];
-    tiles_ok = attn_tiles<1>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+    tiles_ok = attn_tiles<1, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
 #pragma unroll
     for (int i = 0; i < 16; ++i) u_acc[i] = acc[i];
   } else if (lc <= 16) {
     float acc[32];
-    tiles_ok = attn_tiles<2>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+    // the Nano latent (256: 16 chunks) with its row shape fixed at compile time
+    tiles_ok = lc == 16 ? attn_tiles<2, 16>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc)
+                        : attn_tiles<2, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
 #pragma unroll
     for (int i = 0; i < 32; ++i) u_acc[i] = acc[i];
   } else {
     float acc[64];
-    tiles_ok = attn_tiles<4>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
+    tiles_ok = attn_tiles<4, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
 #pragma unroll
     for (int i = 0; i < 64; ++i) u_acc[i] = acc[i];
   }
@@ -795,8 +813,8 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
       const int r0 = ch * op.chunk_rows;
       const int k = max(0, min(op.chunk_rows, rows_c - r0));
       if (k > 0)
-        rows_generic(stage, k, op.row_bytes, op.scale_stride, op.has_bias, act_scale, c.act, c.xsum, op.in_n, op.lpr_log,
-                     rows_out + r0, epi, ll_out + (epi == EPI_SWIGLU ? r0 / 2 : r0), resid + r0, flag);
+        rows_decode(stage, k, op.row_bytes, op.scale_stride, op.has_bias, act_scale, c.act, c.xsum, op.in_n, op.lpr_log,
+                    rows_out + r0, epi, ll_out + (epi == EPI_SWIGLU ? r0 / 2 : r0), resid + r0, flag);
     }
   }
   if (epi == EPI_STORE) __syncthreads();  // every row of this CTA is in rows_out
@@ -1152,7 +1170,8 @@ __global__ void __launch_bounds__(kThreads, 1) rows_probe_kernel(const unsigned 
     xhalf[h] = sum;
   }
   __syncthreads();
-  rows_generic(st, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, lg, res, EPI_STORE, nullptr, nullptr, 0u);
+  if (lg < 0) rows_decode(st, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, 4, res, EPI_STORE, nullptr, nullptr, 0u);
+  else rows_generic(st, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, lg, res, EPI_STORE, nullptr, nullptr, 0u);
   __syncthreads();
   for (int r = threadIdx.x; r < k; r += kThreads) out[r] = res[r];
 }
@@ -1808,12 +1827,13 @@ int32_t ivb_decode_rows(const uint8_t* stage, int32_t k, int32_t row_bytes, int3
                         float act_scale, const int8_t* q8, int32_t in_n, int32_t lanes_log, float* out, void* stream) {
   using namespace ivb;
   if (stage == nullptr || q8 == nullptr || out == nullptr) return fail(IVB_EINVAL, "ivb_decode_rows: null argument");
-  if (k <= 0 || in_n <= 0 || lanes_log < 0 || lanes_log > 5 || scale_stride <= 0)
+  if (k <= 0 || in_n <= 0 || lanes_log < -1 || lanes_log > 5 || scale_stride <= 0)
     return fail(IVB_EINVAL, "ivb_decode_rows: bad shape");
   if ((row_bytes & 15) != 0 || row_bytes < (in_n + 3) / 4)
     return fail(IVB_EINVAL, "ivb_decode_rows: row_bytes must be a multiple of 16 holding the row");
   const int chunks = (in_n + 63) / 64;
-  if (chunks > (kRowsKPL << lanes_log)) return fail(IVB_EINVAL, "ivb_decode_rows: more than %d chunks per lane", kRowsKPL);
+  if (chunks > (kRowsKPL << (lanes_log < 0 ? 4 : lanes_log)))
+    return fail(IVB_EINVAL, "ivb_decode_rows: more than %d chunks per lane", kRowsKPL);
   const size_t stage_bytes = static_cast<size_t>(k) * row_bytes + round16(static_cast<size_t>(k) * scale_stride * 2) +
                              (has_bias ? static_cast<size_t>(k) * 4 : 0);
   const size_t smem = round16(stage_bytes) + static_cast<size_t>(chunks) * 64 + static_cast<size_t>(chunks) * 8 + static_cast<size_t>(k) * 4;

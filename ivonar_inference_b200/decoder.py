@@ -151,6 +151,7 @@ class B200Decoder(StaticDecoder):
             seed = int(torch.randint(0, 2**62, (1,)).item())
         self.rng = torch.tensor([int(seed), 0], dtype=torch.int64, device=dev)
         self._ctas_request = int(ctas)
+        self._pending_check = False
         self._build(model, dev)
 
     # ------------------------------------------------------------------------------------------
@@ -305,6 +306,7 @@ class B200Decoder(StaticDecoder):
             native.check(rc, "ivb_decoder_run")
 
     def _check(self) -> None:
+        self._pending_check = False
         with torch.cuda.device(self.device):
             native.check(self.lib.ivb_decoder_check(self._plan, self._stream()), "decode kernel")
 
@@ -370,7 +372,9 @@ class B200Decoder(StaticDecoder):
             self._launch(length, ids, 0)
         else:
             self._prefill_gemm(ids)
-        self._check()
+        # the device error word is read by the next step or sample (as the reference's prefill, this
+        # call does not wait for the GPU, so prefills of several decoders on their own streams overlap)
+        self._pending_check = True
         self.host_position = length
         return self.logits
 
@@ -392,6 +396,8 @@ class B200Decoder(StaticDecoder):
         """One token through the kernel (the reference step's contract, decoder.py:307-322): feeds
         self.token, advances self.position and, when sampling, samples the next token into it."""
 
+        if self._pending_check and not torch.cuda.is_current_stream_capturing():
+            self._check()  # a failed prefill is reported before anything runs on its state
         self._launch(1, self.token, native.IVB_RUN_SAMPLE if self.sampling else 0)
         if not torch.cuda.is_current_stream_capturing():
             self._check()
@@ -401,6 +407,8 @@ class B200Decoder(StaticDecoder):
         self._check()  # errors of a replayed graph surface here
 
     def _sample(self) -> None:
+        if self._pending_check and not torch.cuda.is_current_stream_capturing():
+            self._check()
         self._launch(0, None, native.IVB_RUN_SAMPLE_ONLY)
         if not torch.cuda.is_current_stream_capturing():
             self._check()
@@ -479,6 +487,7 @@ class B200Decoder(StaticDecoder):
         length = min(32 + 16 + 1, self.max_len)
         ids = torch.randint(2, vocab, (1, length), generator=torch.Generator().manual_seed(0))
         whole = self.prefill(ids).clone()
+        self._check()
         self.prefill(ids[:, :1])
         for index in range(1, length):
             self.step(ids[:, index])

@@ -268,8 +268,8 @@ def test_decode_row_routine_gives_the_reference_integer_dots() -> None:
         rows, groups = dots.shape
         in_n = int(g[f"in{k}"])
         chunks = (in_n + 63) // 64
-        for lg in range(5):
-            if chunks > 4 << lg:
+        for lg in (-1, 0, 1, 2, 3, 4):  # -1: the routine the decode kernel picks for the shape
+            if chunks > 4 << max(lg, 4 if lg < 0 else lg):
                 continue
             for grp in range(groups):
                 onehot = np.zeros_like(scales)
@@ -278,7 +278,7 @@ def test_decode_row_routine_gives_the_reference_integer_dots() -> None:
                 out = _decode_rows(chunk, rows, rb, stride, False, 1.0, q8, in_n, lg)
                 assert np.array_equal(out, dots[:, grp].astype(np.float32)), (k, lg, grp)
                 checked += 1
-    assert checked == 76  # every group of the six golden shapes at every lane width that holds them
+    assert checked == 112  # every group of the six golden shapes, every lane width that holds them and the kernel's pick
 
 
 def test_decode_row_routine_matches_the_reference_gemv(oracle_lib) -> None:
@@ -296,9 +296,30 @@ def test_decode_row_routine_matches_the_reference_gemv(oracle_lib) -> None:
         mat.gemv(np.ascontiguousarray(q8, np.int8), act_scale, want)
         chunks = (in_n + 63) // 64
         chunk, rb, stride = _stream_chunk(packed, scales, bias, in_n)
-        for lg in range(5):
-            if chunks > 4 << lg:
+        for lg in (-1, 0, 1, 2, 3, 4):
+            if chunks > 4 << max(lg, 4 if lg < 0 else lg):
                 continue
             out = _decode_rows(chunk, rows, rb, stride, True, act_scale, q8, in_n, lg)
             np.testing.assert_allclose(out, g[f"gemv{k}"], rtol=1e-5, atol=1e-6)
             np.testing.assert_allclose(out, want, rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("rows,cols", [(8, 1024), (16, 1024), (64, 1024), (200, 1024), (8, 2816), (6, 2816), (10, 1024)])
+def test_decode_row_geometries_give_the_oracle_integer_dots(oracle_lib, rows: int, cols: int) -> None:
+    """Every compile-time row geometry of the decode kernel (16 lanes x 1 row, 8 lanes x 2 and x 8 rows,
+    32 lanes for long inputs) against the oracle's exact integer group dots (one-hot group scales)."""
+    from ivonar_inference_b200 import synthetic
+
+    gen = torch.Generator().manual_seed(rows * 7 + cols)
+    packed, scales = synthetic._packed(gen, rows, cols, "baseline")
+    packed = packed.numpy()
+    scales = scales.view(torch.int16).numpy().view(np.uint16)
+    x = torch.randn(cols, generator=gen).numpy()
+    q8, _, _ = oracle_lib.quantize(x)
+    want = oracle_lib.Matrix.raw(packed, scales, cols).group_dots(q8)
+    for grp in range(want.shape[1]):
+        onehot = np.zeros_like(scales)
+        onehot[:, grp] = 0x3C00
+        chunk, rb, stride = _stream_chunk(packed, onehot, None, cols)
+        out = _decode_rows(chunk, rows, rb, stride, False, 1.0, q8, cols, -1)
+        assert np.array_equal(out, want[:, grp].astype(np.float32)), (rows, cols, grp)
