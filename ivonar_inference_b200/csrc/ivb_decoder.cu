@@ -94,13 +94,6 @@ __device__ __forceinline__ void cand_put(unsigned long long* key_dst, unsigned l
   }
 }
 
-// The decode kernel's quantiser for vectors already in shared memory (the latent of the attention op):
-// one out-of-line copy of quantize_block (bit-identical codes).
-static __device__ __noinline__ float quantize_ni(const float* src, int n, const float* norm_w, float norm_eps, float clip,
-                                                 float act_eps, int8_t* codes, bool transposed, int* xsum, float* red) {
-  return quantize_block(src, n, norm_w, norm_eps, clip, act_eps, codes, transposed, xsum, red);
-}
-
 // Gather + (RMSNorm +) quantise of an input of at most E * 256 values, all in registers: thread t polls
 // the words t, t + 256, t + 512, ... of the input's flag-word buffer, exactly the elements the canonical
 // quantiser assigns to lane t, so the sum of squares (fmaf in that order, warp butterfly, warps in
@@ -435,7 +428,7 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
 // each one later reads cache rows it wrote itself. Cached positions arrive in tiles by bulk copy (double
 // buffered); the caller issues the first tile before this call. Publishes the head's outputs.
 // `chunk`: the op's constants chunk in the ring.
-static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
+__device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
   // the context, the op record and the parameters also live, so reads through them would repeat
   const DecodeParams& p = *c.p;
@@ -458,7 +451,7 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
   const float* qh = c.xl;                 // gathered q of the head
   const float* lat = c.xl + hd;           // the latent
   const float* kh = lat + Lt;             // k_rope of the head
-  const float a_cur = quantize_ni(lat, Lt, nullptr, 0.0f, 0.0f, D.act_eps, A.qlc, false, nullptr, red);
+  const float a_cur = quantize_block(lat, Lt, nullptr, 0.0f, 0.0f, D.act_eps, A.qlc, false, nullptr, red);
   for (int j = tid; j < Lt; j += kThreads) lat_q[static_cast<size_t>(P) * D.lpad + j] = A.qlc[j];
   for (int j = Lt + tid; j < D.lpad; j += kThreads) A.qlc[j] = 0;  // the row's padding (read as whole chunks)
   if (tid == 0) lat_s[P] = a_cur;
@@ -495,7 +488,7 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
         const int byte = wkn[e * rb + jb];
         const float q = A.qn[e] * h2f(skn[e * ss + (jb >> 5)]);
 #pragma unroll
-        for (int f = 0; f < 4; ++f) a4[f] = fmaf(q, static_cast<float>(((byte >> (2 * f)) & 3) - 1), a4[f]);
+        for (int f = 0; f < 4; ++f) a4[f] = fmaf(q, code_m1(static_cast<unsigned>(byte) >> (2 * f)), a4[f]);
       }
 #pragma unroll
       for (int f = 0; f < 4; ++f) A.scr[eg * 4 * nb + 4 * jb + f] = a4[f];
@@ -583,10 +576,10 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
           for (int t = 0; t < 4; ++t) {
             const float4 u4 = uu[t];
             const unsigned b = bits >> (8 * t);
-            t0 = fmaf(static_cast<float>(static_cast<int>(b & 3u) - 1), u4.x, t0);
-            t1 = fmaf(static_cast<float>(static_cast<int>((b >> 2) & 3u) - 1), u4.y, t1);
-            t0 = fmaf(static_cast<float>(static_cast<int>((b >> 4) & 3u) - 1), u4.z, t0);
-            t1 = fmaf(static_cast<float>(static_cast<int>((b >> 6) & 3u) - 1), u4.w, t1);
+            t0 = fmaf(code_m1(b), u4.x, t0);
+            t1 = fmaf(code_m1(b >> 2), u4.y, t1);
+            t0 = fmaf(code_m1(b >> 4), u4.z, t0);
+            t1 = fmaf(code_m1(b >> 6), u4.w, t1);
           }
           const float sc = h2f(sv[e * ss + (w >> 3)]);
           if (w & 1) acc1 = fmaf(sc, t0 + t1, acc1);
@@ -617,7 +610,7 @@ static __device__ __noinline__ bool op_attention(Ctx& c, const Op& opr, const Iv
 __host__ __device__ __forceinline__ int ssm_smem_floats(int cpc, int S, int taps) {
   return 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S + 3 * S * cpc + cpc * (taps - 1);
 }
-static __device__ __noinline__ void ssm_step(Ctx& c, const Op& op, const IvbLayerDesc& L, const float* rows_out, float* ssmc) {
+__device__ __forceinline__ void ssm_step(Ctx& c, const Op& op, const IvbLayerDesc& L, const float* rows_out, float* ssmc) {
   const DecodeParams& p = *c.p;
   const DecodeDims D = p.d;  // registers: the loops below store to shared memory, where p lives
   const int tid = threadIdx.x;

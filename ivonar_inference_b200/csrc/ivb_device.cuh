@@ -218,6 +218,10 @@ __device__ __forceinline__ void word_codes_m1(unsigned w, float* cm1) {
   }
 }
 
+// A two-bit ternary code c (0, 1, 2) as the exact float c - 1 without the conversion unit: c placed in
+// the low mantissa bits of 2^23, then 2^23 + 1 subtracted.
+__device__ __forceinline__ float code_m1(unsigned c) { return __uint_as_float(0x4B000000u | (c & 3u)) - 8388609.0f; }
+
 // Four signed bytes to exact floats without the conversion unit: biased byte b + 128 placed in the
 // low mantissa bits of 2^23, then 2^23 + 128 subtracted (exact for every byte value).
 __device__ __forceinline__ void bytes_to_f32(unsigned w, float* f) {
