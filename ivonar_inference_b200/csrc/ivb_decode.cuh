@@ -152,7 +152,7 @@ __device__ __forceinline__ void ll_put(unsigned long long* buf, int base, const 
 // every thread if some word did not arrive within timeout_ns (the verdict is uniform across the CTA).
 // The sources are 16-byte aligned; n1 and n2 are even (an odd word may end the last range only).
 constexpr int kLLPairs = 9;
-static __device__ __noinline__ bool ll_gather3(const unsigned long long* src1, int n1, const unsigned long long* src2, int n2,
+__device__ __forceinline__ bool ll_gather3(const unsigned long long* src1, int n1, const unsigned long long* src2, int n2,
                                                const unsigned long long* src3, int n3, unsigned flag, unsigned* dst,
                                                unsigned long long timeout_ns) {
   const int p1 = n1 >> 1, p2 = p1 + (n2 >> 1), pairs = p2 + (n3 >> 1);
@@ -248,7 +248,7 @@ __device__ __forceinline__ int chunks_of_step(const DecodeParams& p, const Strea
 }
 
 // thread 0 only: queue the next chunk of this CTA's stream into the next ring stage
-static __device__ __noinline__ void stream_issue(const DecodeParams& p, Stream* s) {
+__device__ __forceinline__ void stream_issue(const DecodeParams& p, Stream* s) {
   if (s->p_step >= p.steps) return;
   if (s->p_chunk == s->head_first && !head_needed(p, s->p_step)) {
     s->p_chunk = 0;
