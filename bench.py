@@ -92,10 +92,12 @@ def measured_peaks() -> tuple[float, str]:
     return 6650.0, "fallback"
 
 
-# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture (--set full) of a 16-token decode launch
-# of this workload (795,531,264 + 22,050,048 bytes), per token; scaled to a launch by the tokens it runs.
-NCU_DRAM_BYTES_PER_TOKEN = (795_531_264 + 22_050_048) / 16
-TRAFFIC_SOURCE = "ncu capture of a 16-token decode launch at positions 37-52, scaled by tokens per launch"
+# dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture (--set full) of a 16-token
+# grid_decode_kernel launch of this workload (1,815,794,944 + 64,375,040 bytes), per token; scaled to a
+# launch by the tokens it runs.
+NCU_DRAM_BYTES_PER_TOKEN = (1_815_794_944 + 64_375_040) / 16
+TRAFFIC_SOURCE = ("ncu --set full capture of a 16-token grid_decode_kernel launch at positions 37-52 "
+                  "(python bench.py --steps 1 --warmup 1 --tokens 16 ...), scaled by tokens per launch")
 
 
 def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
