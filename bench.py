@@ -11,9 +11,10 @@ advance_many(16), host copies included. With --gpus N (torchrun) every rank deco
 independent sequences on its own GPU (data parallel, no collective on the data path); value is the
 total over ranks divided by the slowest rank's time.
 
-Secondary, rank 0: prompt prefill tok/s at 512, 2048 and 8192 tokens (b=1) through
-B200Decoder.prefill (tcgen05 GEMMs, recurrent scan, latent-cache fill and causal attention), and the
-int8 tensor-core throughput of the prefill GEMM alone on the gate/up shape at 2048 tokens.
+Secondary, rank 0: prompt prefill tok/s at 512, 2048 and 8192 tokens through
+B200Decoder.prefill (tcgen05 GEMMs, recurrent scan, latent-cache fill and causal attention) at batch 1
+and at batch 8 (eight independent prompts, one decoder and one CUDA stream each, timed together), and
+the int8 tensor-core throughput of the prefill GEMM alone on the gate/up shape at 2048 tokens.
 
 Secondary, every rank: batched serving, 256 independent sequences split evenly over
 the N GPUs (data parallel, no collective on the data path), each a 128-token random prompt and then
