@@ -101,12 +101,14 @@ TRAFFIC_SOURCE = ("ncu --set full capture of a 16-token grid_decode_kernel launc
                   "(python bench.py --steps 1 --warmup 1 --tokens 16 ...), scaled by tokens per launch")
 
 
-def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
+def decode_bytes(model, first_position: int, tokens: int, cache: str = "kv") -> tuple[float, dict]:
     """Algorithmic HBM bytes of `tokens` decode steps starting at `first_position`.
 
     Per token: every packed ternary byte + fp16 scale + fp32 bias once, the recurrent state read and
-    written, and the compressed latent cache read up to the current position (latent codes + scale +
-    fp16 k_rope per position per attention layer) plus its append.
+    written, and the attention cache read up to the current position plus its append. cache "kv": the
+    single-sequence decoder's fp32 key and value rows (heads x 2 x head_dim padded to 4 floats per
+    position per attention layer); "latent": the batched decoder's compressed cache (latent codes +
+    scale + fp16 k_rope).
     """
     cfg = model.config
     weights = 0
@@ -123,6 +125,8 @@ def decode_bytes(model, first_position: int, tokens: int) -> tuple[float, dict]:
         if block.mixer_type == "mamba":
             hsd = m.num_heads * m.state_dim * m.head_dim
             state += 2 * 4 * (2 * hsd + hsd + cfg.hidden_dim * (m.conv_kernel_size - 1))
+        elif cache == "kv":
+            per_pos += m.num_heads * 2 * ((m.head_dim + 3) // 4 * 4) * 4
         else:
             per_pos += m.latent_dim + 4 + m.num_heads * m.rope_dim * 2
     kv = sum(per_pos * (p + 1) for p in range(first_position, first_position + tokens)) + per_pos * tokens
@@ -134,7 +138,7 @@ def batch_roofline(model, sequences: int, first_position: int, steps: int, ms: f
     """Per-GPU HBM roofline of config 3's timed decode steps: every step reads the packed weights once
     for all of the GPU's sequences, and each sequence's recurrent state (read and written) and latent
     cache up to its position."""
-    per_step_weights, parts = decode_bytes(model, first_position, 1)
+    per_step_weights, parts = decode_bytes(model, first_position, 1, cache="latent")
     weights, state, per_pos = parts["weights_per_token"], parts["state_per_token"], parts["kv_bytes_per_position"]
     kv = sum(per_pos * (p + 2) for p in range(first_position, first_position + steps))
     total = steps * (weights + sequences * state) + sequences * kv

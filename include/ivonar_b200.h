@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define IVB_ABI_VERSION 1
+#define IVB_ABI_VERSION 2
 
 enum {
   IVB_OK = 0,
@@ -93,6 +93,12 @@ typedef struct IvbLayerDesc {
   float* latent_scale;        /* cache [max_len] per-position activation scale */
   uint16_t* k_rope_cache;     /* cache [heads, max_len, rope_dim padded to 8] fp16 rotated k_rope */
   float attn_scale;           /* 1 / sqrt(head_dim) */
+  /* mla: the decompressed cache the decode kernel attends over (rows of head_dim rounded up to 4 floats,
+   * zero padded; 16-byte aligned). Keys: k_nope = W_k(latent) + b_k, then the rotated k_rope as stored
+   * in k_rope_cache; values: W_v(latent) + b_v. The single-sequence decoder and its prefill write them;
+   * null in descriptions used only by the batched kernels. */
+  float* k_cache;             /* [heads, max_len, head_dim padded to 4] fp32 */
+  float* v_cache;             /* [heads, max_len, head_dim padded to 4] fp32 */
 } IvbLayerDesc;
 
 /* The whole model plus the decoder state buffers. Reference: kernel_decoder.py:179-283. */

@@ -16,7 +16,7 @@ from pathlib import Path
 PACKAGE = Path(__file__).resolve().parent
 LIBRARY = PACKAGE / "libivonar_b200.so"
 
-IVB_ABI_VERSION = 1
+IVB_ABI_VERSION = 2
 IVB_OK, IVB_EINVAL, IVB_ECUDA, IVB_ETIMEOUT, IVB_ECAPACITY, IVB_EUNSUPPORTED = range(6)
 IVB_EPI_STORE, IVB_EPI_RESIDUAL, IVB_EPI_SILU_PAIR = range(3)
 IVB_MAMBA, IVB_MLA = 0, 1
@@ -68,6 +68,8 @@ class IvbLayerDesc(Structure):
         ("latent_scale", c_void_p),
         ("k_rope_cache", c_void_p),
         ("attn_scale", c_float),
+        ("k_cache", c_void_p),
+        ("v_cache", c_void_p),
     ]
 
 

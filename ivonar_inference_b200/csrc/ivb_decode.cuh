@@ -41,14 +41,13 @@ struct Op {
   int32_t ll_out;                  // word offset of this op's output buffer
   int32_t push_per;                // entry of an mla block: latent rows per CTA (output slice stride)
   int32_t in_n;                    // GEMV input length
-  int32_t rows_per, rows_total;    // uniform row partition across the CTAs
+  int32_t rows_per, rows_total;    // uniform row partition across the CTAs (attention: the head's kv rows)
   int32_t chunk_rows;              // rows per stream chunk
   int32_t row_bytes, scale_stride, has_bias, lpr_log;
   int32_t has_norm;
   float norm_eps;
   // constants chunk: byte offsets of its arrays
   int32_t c_decay, c_theta, c_skip, c_convw, c_convb;
-  int32_t c_wkn, c_skn, c_bkn, c_wv, c_sv, c_bv;
 };
 
 // Device record of one op: its descriptor and a copy of its block's layer description, so one
@@ -65,6 +64,7 @@ struct DecodeDims {
   int32_t A;                       // attention CTAs (heads, or 0 without attention blocks)
   int32_t taps;                    // conv taps
   int32_t lpad, rpad;              // latent cache row stride (bytes), k_rope cache row stride (halves)
+  int32_t kvpad;                   // key / value cache row stride (floats): head_dim rounded up to 4
   int32_t rb_lat, ss_lat;          // row bytes / scale stride of latent-input matrices
   int32_t tile;                    // cached positions per attention tile
   int32_t group;                   // CTAs per candidate-merge group (the group's first CTA merges)
@@ -489,8 +489,8 @@ __device__ __forceinline__ void rows_generic(const unsigned char* stage, int k, 
 
 // The row routine the decode kernel runs on a chunk of k rows: the compile-time geometries for the
 // Nano shapes (1024 inputs: 16 lanes per row for up to 16 rows, 8 lanes x 2 rows for up to 64, 8 lanes
-// x 8 rows for up to 256; 2049-4096 inputs and up to 8 rows outside gate/up: 32 lanes), rows_generic
-// with 2^lg lanes per row for every other shape.
+// x 8 rows for up to 256; 256 inputs: 4 lanes x 2 rows for up to 128; 2049-4096 inputs and up to 8 rows
+// outside gate/up: 32 lanes), rows_generic with 2^lg lanes per row for every other shape.
 __device__ __forceinline__ void rows_decode(const unsigned char* stage, int k, int row_bytes, int sstride, int has_bias,
                                             float act_scale, const int8_t* act, const int* xhalf, int in_n, int lg, float* out,
                                             int epi, unsigned long long* ll, const float* resid, unsigned flag) {
@@ -499,6 +499,8 @@ __device__ __forceinline__ void rows_decode(const unsigned char* stage, int k, i
     if (k <= 16) return rows_ct<4, 1, 1>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
     if (k <= 64) return rows_ct<3, 2, 2>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
     if (k <= 256) return rows_ct<3, 2, 8>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
+  } else if (chunks == 4 && k <= 128 && epi != EPI_SWIGLU) {  // 256 inputs: the attention's kv rows
+    return rows_ct<2, 1, 2>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
   } else if (chunks > 32 && chunks <= 64 && k <= 8 && epi != EPI_SWIGLU) {
     return rows_ct<5, 2, 1>(stage, k, row_bytes, sstride, has_bias, act_scale, act, xhalf, in_n, out, epi, ll, resid, flag);
   }

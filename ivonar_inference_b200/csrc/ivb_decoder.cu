@@ -42,39 +42,38 @@ __device__ __forceinline__ bool tile_wait(unsigned long long* bar, unsigned pari
   return !__syncthreads_or(late);
 }
 
+// Tile buffer b of the attention op: tile + 1 key rows, then tile + 1 value rows (head_dim padded to
+// kvpad floats); the last tile also holds the current position.
 struct TileBuf {
-  int8_t* lat;      // [tile][lpad]
-  float* lsc;       // [tile]
-  uint16_t* kr;     // [tile][rpad]
+  float* k;  // [tile + 1][kvpad]
+  float* v;  // [tile + 1][kvpad]
 };
 
+__host__ __device__ __forceinline__ size_t tile_bytes(int tile, int kvpad) {
+  return (static_cast<size_t>(tile + 1) * kvpad * 4 + 15) / 16 * 16;
+}
+
 __device__ __forceinline__ TileBuf tile_buf(unsigned char* base, const DecodeDims& D, int b) {
-  const int rows = D.tile + 1;  // the last tile also holds the current position
-  const size_t one = round16(rows * D.lpad) + round16(rows * 4) + round16(rows * D.rpad * 2);
-  unsigned char* t = base + b * one;
+  const size_t one = tile_bytes(D.tile, D.kvpad);
   TileBuf tb;
-  tb.lat = reinterpret_cast<int8_t*>(t);
-  tb.lsc = reinterpret_cast<float*>(t + round16(rows * D.lpad));
-  tb.kr = reinterpret_cast<uint16_t*>(t + round16(rows * D.lpad) + round16(rows * 4));
+  tb.k = reinterpret_cast<float*>(base + 2 * b * one);
+  tb.v = reinterpret_cast<float*>(base + (2 * b + 1) * one);
   return tb;
 }
 
-// thread 0: bulk-copy cached positions [start, start + count) of head h into tile buffer b. The copies
-// need 16-byte aligned sources: start must be a multiple of 4 (scale entries are 4 bytes); a call that
-// breaks this records IVB_EINVAL in *error and copies nothing (its wait then runs out and reports).
-__device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const DecodeDims& D, const TileBuf& tb, int h,
-                                           int start, int count, unsigned long long* bar, unsigned* error) {
-  if ((start & 3) != 0) {
-    atomicCAS(error, 0u, static_cast<unsigned>(IVB_EINVAL));
-    return;
-  }
-  const unsigned lat = count * D.lpad, lsc = round16(count * 4), kr = count * D.rpad * 2;
+// thread 0: bulk-copy the cached keys and values of positions [start, start + count) of head h into
+// tile buffer b (rows of kvpad floats, a multiple of 16 bytes at 16-byte aligned addresses), and mark
+// the buffer's copy pending. The rows were written by generic stores of earlier tokens (or kernels).
+__device__ __forceinline__ void tile_issue(const IvbLayerDesc& L, const DecodeDims& D, const TileBuf& tb, int h, int start,
+                                           int count, unsigned long long* bar, unsigned& pending, int b) {
+  const unsigned bytes = static_cast<unsigned>(count) * static_cast<unsigned>(D.kvpad) * 4u;
+  const size_t row0 = (static_cast<size_t>(h) * D.max_len + start) * D.kvpad;
   asm volatile("fence.proxy.async.global;" ::: "memory");
   fence_proxy_async();
-  mbar_expect_tx(bar, lat + lsc + kr);
-  bulk_copy(tb.lat, L.latent_q + static_cast<size_t>(start) * D.lpad, lat, bar);
-  bulk_copy(tb.lsc, L.latent_scale + start, lsc, bar);
-  bulk_copy(tb.kr, L.k_rope_cache + (static_cast<size_t>(h) * D.max_len + start) * D.rpad, kr, bar);
+  mbar_expect_tx(bar, 2u * bytes);
+  bulk_copy(tb.k, L.k_cache + row0, bytes, bar);
+  bulk_copy(tb.v, L.v_cache + row0, bytes, bar);
+  pending |= 1u << b;
 }
 
 // Candidate slots of the sampler: every CTA of the head op publishes exactly kp (even) candidates,
@@ -219,6 +218,7 @@ struct Ctx {
   unsigned char* U;
   unsigned long long* abar;
   unsigned apar[2];     // phase parities of the two attention tile barriers (flipped by thread 0)
+  unsigned apend;       // bit b: a copy into tile buffer b was issued and not yet waited for (thread 0)
   long long pos;
   unsigned flag;
   int K, kp, kq, n_groups;
@@ -241,110 +241,99 @@ struct Ctx {
 };
 
 // Shared-memory layout of the attention op inside the union region (the plan sizes it the same way):
-// current latent codes [round64(latent)] | qa [round32(latent)] | qr, krc [rope] | qn [nope] |
-// u [round32(latent)] | scores [tile + 4] | partial sums [1024] | 16-byte aligned double tile buffer
-// (each buffer tile + 1 rows: the last tile also holds the current position).
+// kv rows of this position [nope + head_dim] | scaled query, rope pairs rotated [kvpad] | this
+// position's key row [kvpad] | scores [tile + 4] | partial value sums [4 * kThreads] | 16-byte aligned
+// double tile buffer (tile_buf).
 struct AttnSmem {
-  int8_t* qlc;
-  float *qa, *qr, *krc, *qn, *u, *sc, *scr;
+  float *kv, *q, *kcur, *sc, *part;
   unsigned char* tiles;
 };
-constexpr int kAttnScratch = 1024;  // floats of partial sums (absorbed query)
-// every array starts on a 16-byte boundary (qa and u are read as float4)
 __host__ __device__ __forceinline__ int r4(int n) { return (n + 3) & ~3; }
-__host__ __device__ __forceinline__ size_t attn_fixed_bytes(int latent, int rope, int nope, int tile) {
-  const int l64 = (latent + 63) / 64 * 64, l32 = (latent + 31) / 32 * 32;
-  return round16(l64) + static_cast<size_t>(2 * l32 + 2 * r4(rope) + r4(nope) + r4(tile + 4) + kAttnScratch) * 4 + 16;
+__host__ __device__ __forceinline__ size_t attn_fixed_bytes(int nope, int hd, int tile) {
+  const int kvpad = r4(hd);
+  return static_cast<size_t>(r4(nope + hd) + 2 * kvpad + r4(tile + 4) + 4 * kThreads) * 4 + 16;
 }
 __device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims& D) {
-  const int l64 = (D.latent + 63) / 64 * 64, l32 = (D.latent + 31) / 32 * 32;
   AttnSmem a;
-  a.qlc = reinterpret_cast<int8_t*>(U);
-  a.qa = reinterpret_cast<float*>(U + round16(l64));
-  a.qr = a.qa + l32;
-  a.krc = a.qr + r4(D.rope);
-  a.qn = a.krc + r4(D.rope);
-  a.u = a.qn + r4(D.nope);
-  a.sc = a.u + l32;
-  a.scr = a.sc + r4(D.tile + 4);
-  unsigned char* t = reinterpret_cast<unsigned char*>(a.scr + kAttnScratch);
+  a.kv = reinterpret_cast<float*>(U);
+  a.q = a.kv + r4(D.nope + D.head_dim);
+  a.kcur = a.q + D.kvpad;
+  a.sc = a.kcur + D.kvpad;
+  a.part = a.sc + r4(D.tile + 4);
+  unsigned char* t = reinterpret_cast<unsigned char*>(a.part + 4 * kThreads);
   a.tiles = t + ((16 - (reinterpret_cast<uintptr_t>(t) & 15)) & 15);
   return a;
 }
 
-// Scores of the npos positions of a tile: LPP lanes per position, lane q taking the 16-byte chunks q,
-// q + LPP, ... of the position's latent row and of qa (all positions read the same qa chunk at the same
-// time, so those reads are broadcasts), the lane sums added by a butterfly over the LPP lanes; the
-// score (a_t dot + rope term + qb) goes to A.sc[k]. Returns the thread's maximum score. LC: chunks per
-// row when known at compile time (0: lc chunks).
-template <int LPP, int LC>
-__device__ __forceinline__ float attn_scores(const AttnSmem& A, const TileBuf& tb, int lc_rt, int npos, int lpad, int rope, int rpad,
-                                             float qb) {
-  constexpr int kPerPass = kThreads / LPP;
-  constexpr int kIters = (LC > 0 ? LC : 32) / LPP;  // chunks per lane (rows hold at most 32 chunks)
-  const int lc = LC > 0 ? LC : lc_rt;
-  const int tid = threadIdx.x, q = tid & (LPP - 1);
+// thread 0, after a failed wait: let the tile copies still in flight land (bounded) before the shared
+// memory they write is reused or released.
+__device__ __forceinline__ void attn_drain(Ctx& c, unsigned long long timeout_ns) {
+  for (int b = 0; b < 2; ++b)
+    if (c.apend & (1u << b)) {
+      if (mbar_wait_bounded(&c.abar[b], c.apar[b], timeout_ns)) c.apar[b] ^= 1u;
+      c.apend &= ~(1u << b);
+    }
+}
+
+// Scores of the npos positions of a tile (keys K [npos][kq float4]): 8 lanes per position, lane q
+// taking the quads q, q + 8, ... of the key row against the query quads it holds in qv; the lane sums
+// are added by a butterfly and the score goes to sc[k]. One phase of a 16-byte load is one position's
+// 128 contiguous bytes, free of bank conflicts. Returns the thread's maximum score.
+template <int NQ>
+__device__ __forceinline__ float attn_scores(const float4 (&qv)[NQ], const float* K, int kq, int npos, float* sc) {
+  const int tid = threadIdx.x, q = tid & 7;
   float wmax = -INFINITY;
-  for (int k0 = 0; k0 < npos; k0 += kPerPass) {
-    const int k = k0 + tid / LPP;
-    float dot = 0.0f;
+  for (int k0 = 0; k0 < npos; k0 += kThreads / 8) {
+    const int k = k0 + (tid >> 3);
+    float d0 = 0.0f, d1 = 0.0f;
     if (k < npos) {
-      const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
-      float d0 = 0.0f, d1 = 0.0f, d2 = 0.0f, d3 = 0.0f;
+      const float4* row = reinterpret_cast<const float4*>(K) + static_cast<size_t>(k) * kq;
 #pragma unroll
-      for (int i = 0; i < kIters; ++i) {
-        const int ch = q + LPP * i;
-        if (LC > 0 || ch < lc) {
-          const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * ch);
-          const float4* qa = reinterpret_cast<const float4*>(A.qa + 16 * ch);
-          const unsigned wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float4 qq = qa[t];
-            float f[4];
-            bytes_to_f32(wv[t], f);
-            d0 = fmaf(qq.x, f[0], d0);
-            d1 = fmaf(qq.y, f[1], d1);
-            d2 = fmaf(qq.z, f[2], d2);
-            d3 = fmaf(qq.w, f[3], d3);
-          }
+      for (int j = 0; j < NQ; ++j) {
+        if (q + 8 * j < kq) {
+          const float4 kk = row[q + 8 * j];
+          d0 = fmaf(qv[j].x, kk.x, d0);
+          d1 = fmaf(qv[j].y, kk.y, d1);
+          d0 = fmaf(qv[j].z, kk.z, d0);
+          d1 = fmaf(qv[j].w, kk.w, d1);
         }
       }
-      dot = (d0 + d1) + (d2 + d3);
     }
+    float dot = d0 + d1;
 #pragma unroll
-    for (int o = 1; o < LPP; o <<= 1) dot += __shfl_xor_sync(kFull, dot, o);  // a position's lanes are in or out together
+    for (int o = 1; o < 8; o <<= 1) dot += __shfl_xor_sync(kFull, dot, o);  // a position's lanes are in or out together
     if (k < npos) {
-      float rp = 0.0f;
-      for (int r = 0; r < rope; ++r) rp = fmaf(A.qr[r], h2f(tb.kr[k * rpad + r]), rp);
-      const float sc = fmaf(tb.lsc[k], dot, rp) + qb;
-      if (q == 0) A.sc[k] = sc;
-      wmax = fmaxf(wmax, sc);
+      if (q == 0) sc[k] = dot;
+      wmax = fmaxf(wmax, dot);
     }
   }
   return wmax;
 }
 
-// The tile loop of the attention op: online softmax over the cached positions, tile by tile, the current
-// position as the extra last row of the last tile. Scores: attn_scores. Weighted latent sum: lane group
-// g = lane / 8 of warp w takes the positions 4w + g + 32i, lane s = lane % 8 owns the chunks s, s + 8,
-// ... (CPL of them, 16 latent entries each) in registers. Returns false when a tile's wait ran out; m_run, l_run and the per-lane
-// partial sums `acc` (scaled by exp(-m_run)) are the results.
-template <int CPL, int LC>
+// The tile loop of the attention op: online softmax over positions 0..P, tile by tile, the current
+// position as the extra last row of the last tile. Value sum: thread (quad dq = tid % kq, group
+// pg = tid / kq) adds the weighted quad dq of the positions pg, pg + G, ... (G = kThreads / kq groups).
+// Returns false when a tile's wait ran out; l_run (the softmax total, scaled by exp(-max)) and the
+// thread's partial value quad `acc` are the results.
+template <int NQ>
 __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const DecodeDims& D, const IvbLayerDesc& L,
-                                           const AttnSmem& A, int h, int P, float a_cur, float qb, float& m_run,
-                                           float& l_run, float (&acc)[16 * CPL]) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, sub = lane & 7, grp = lane >> 3;
-  const int lc = LC > 0 ? LC : D.lpad >> 4;  // 16-byte chunks per cached row (<= 8 * CPL)
-  const int rope = D.rope, rpad = D.rpad, lpad = D.lpad, tile = D.tile;
+                                           const AttnSmem& A, int h, int P, float& l_run, float4& acc) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int kq = D.kvpad >> 2, tile = D.tile, kvpad = D.kvpad, hd = D.head_dim, nope = D.nope;
+  const int G = kThreads / kq, dq = tid % kq, pg = tid / kq;
   float* const red = c.red;
   unsigned long long* const abar = c.abar;
+  float4 qv[NQ];
+#pragma unroll
+  for (int j = 0; j < NQ; ++j) {
+    const int qi = (tid & 7) + 8 * j;
+    qv[j] = qi < kq ? reinterpret_cast<const float4*>(A.q)[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
   const int n_tiles = P == 0 ? 1 : (P + tile - 1) / tile;
   bool ok = true;
-#pragma unroll
-  for (int i = 0; i < 16 * CPL; ++i) acc[i] = 0.0f;
-  m_run = -INFINITY;
+  float m_run = -INFINITY;
   l_run = 0.0f;
+  acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   for (int ti = 0; ti < n_tiles; ++ti) {
     const int start = ti * tile;
     const int count = max(0, min(tile, P - start));
@@ -352,30 +341,27 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
     const TileBuf tb = tile_buf(A.tiles, D, ti & 1);
     if (tid == 0 && !last)
       tile_issue(L, D, tile_buf(A.tiles, D, (ti + 1) & 1), h, start + tile, min(tile, P - start - tile), &abar[(ti + 1) & 1],
-                 p.error);
+                 c.apend, (ti + 1) & 1);
     if (last) {
-      // the current position as row `count` (the bulk copy writes rows below it); its scale after the wait
-      for (int j = tid; j < lpad / 4; j += kThreads)
-        reinterpret_cast<unsigned*>(tb.lat + count * lpad)[j] = reinterpret_cast<const unsigned*>(A.qlc)[j];
-      for (int r = tid; r < rope; r += kThreads) tb.kr[count * rpad + r] = f2h(A.krc[r]);
+      // the current position as row `count` (the bulk copy writes the rows below it)
+      for (int e = tid; e < kvpad; e += kThreads) {
+        tb.k[count * kvpad + e] = A.kcur[e];
+        tb.v[count * kvpad + e] = e < hd ? A.kv[nope + e] : 0.0f;
+      }
     }
     if (count > 0) {
       if (!tile_wait(&abar[ti & 1], c.apar[ti & 1], p.timeout_ns)) {
         ok = false;
         break;
       }
-      if (tid == 0) c.apar[ti & 1] ^= 1u;  // every thread read it before the wait's barrier
+      if (tid == 0) {  // every thread read the parity before the wait's barrier
+        c.apar[ti & 1] ^= 1u;
+        c.apend &= ~(1u << (ti & 1));
+      }
     }
-    if (last) {
-      if (tid == 0) tb.lsc[count] = a_cur;
-      __syncthreads();
-    }
+    if (last) __syncthreads();
     const int npos = count + (last ? 1 : 0);
-    // scores: 8, 4 or 2 lanes per position as the tile is short or long (a short tile's single pass
-    // is latency-bound; a long one is bound by the shared-memory reads)
-    const float wmax = npos <= kThreads / 8   ? attn_scores<8, LC>(A, tb, lc, npos, lpad, rope, rpad, qb)
-                       : npos <= kThreads / 4 ? attn_scores<4, LC>(A, tb, lc, npos, lpad, rope, rpad, qb)
-                                              : attn_scores<2, LC>(A, tb, lc, npos, lpad, rope, rpad, qb);
+    const float wmax = attn_scores<NQ>(qv, tb.k, kq, npos, A.sc);
     const float wm = warp_max(wmax);  // every lane takes part in the shuffles
     if (lane == 0) red[32 + warp] = wm;  // block_sum below uses red[0 .. kWarps)
     __syncthreads();
@@ -386,30 +372,24 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
     float ls = 0.0f;
     for (int k = tid; k < npos; k += kThreads) {
       const float e = expf(A.sc[k] - m_new);
-      A.sc[k] = e * tb.lsc[k];  // softmax weight times the latent scale
+      A.sc[k] = e;
       ls += e;
     }
     ls = block_sum(ls, red);  // its barrier also orders the weights above before the sums below
     l_run = l_run * corr + ls;
-#pragma unroll
-    for (int i = 0; i < 16 * CPL; ++i) acc[i] *= corr;
-    // weighted latent sum
-    for (int k = 4 * warp + grp; k < npos; k += 4 * kWarps) {
-      const float wk = A.sc[k];
-      const unsigned char* row = reinterpret_cast<const unsigned char*>(tb.lat) + k * lpad;
-#pragma unroll
-      for (int j = 0; j < CPL; ++j) {
-        if (sub + 8 * j < lc) {
-          const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * (sub + 8 * j));
-          const unsigned wv[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            float f[4];
-            bytes_to_f32(wv[t], f);
-#pragma unroll
-            for (int b = 0; b < 4; ++b) acc[16 * j + 4 * t + b] = fmaf(wk, f[b], acc[16 * j + 4 * t + b]);
-          }
-        }
+    acc.x *= corr;
+    acc.y *= corr;
+    acc.z *= corr;
+    acc.w *= corr;
+    if (pg < G) {
+      const float4* V = reinterpret_cast<const float4*>(tb.v);
+      for (int k = pg; k < npos; k += G) {
+        const float wk = A.sc[k];
+        const float4 v = V[k * kq + dq];
+        acc.x = fmaf(wk, v.x, acc.x);
+        acc.y = fmaf(wk, v.y, acc.y);
+        acc.z = fmaf(wk, v.z, acc.z);
+        acc.w = fmaf(wk, v.w, acc.w);
       }
     }
     m_run = m_new;
@@ -418,181 +398,103 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
   return ok;
 }
 
-// Latent attention of head h over the compressed cache, absorbed form, after the head's q, the latent
-// and the head's k_rope were gathered into xl. Reference: ternary.cu:509-611, decoder.py:271-297,
-// attention.py:136-151, with k_nope = W_k(latent) and v = W_v(latent) absorbed:
-//   score_t = a_t <qa, ql_t> + <q_rope, k_rope_t> + q_nope.b_k     (qa = W_k^T q_nope)
-//   out     = W_v (sum_t p_t a_t ql_t) / l + b_v
-// The latent of this position is quantised and appended to the cache, the rotated k_rope of the head
-// too (fp16, as the position's own score uses it); every attention CTA writes the same latent bytes, so
-// each one later reads cache rows it wrote itself. Cached positions arrive in tiles by bulk copy (double
-// buffered); the caller issues the first tile before this call. Publishes the head's outputs.
-// `chunk`: the op's constants chunk in the ring.
+// Latent attention of head h after the head's q, the latent and the head's k_rope were gathered into
+// xl, in the reference decoder's form (cpu_decoder.py:186-231, ternary.cu:509-611, decoder.py:271-297):
+// the latent is quantised (codes and scale appended to the compressed cache), the head's up-projection
+// rows give this position's k_nope = W_k(latent) + b_k and v = W_v(latent) + b_v, the key row
+// [k_nope | rotated k_rope] and the value row are appended to the head's fp32 cache, and the scaled
+// query (rope pairs rotated) attends over positions 0..P with an online softmax. Cached positions
+// arrive in tiles by bulk copy (double buffered); the caller issues the first tile before this call.
+// Publishes the head's outputs. `chunk`: the op's stream chunk (the head's kv rows, a GEMV row chunk).
 __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
   // the context, the op record and the parameters also live, so reads through them would repeat
   const DecodeParams& p = *c.p;
   const DecodeDims D = p.d;
-  const int c_wkn = opr.c_wkn, c_skn = opr.c_skn, c_bkn = opr.c_bkn, c_wv = opr.c_wv, c_sv = opr.c_sv, c_bv = opr.c_bv;
-  const int ll_out = opr.ll_out;
+  const int ll_out = opr.ll_out, kv_rows = opr.rows_per, kv_rb = opr.row_bytes, kv_ss = opr.scale_stride, kv_lg = opr.lpr_log;
   int8_t* const lat_q = L.latent_q;
   float* const lat_s = L.latent_scale;
   uint16_t* const kr_cache = L.k_rope_cache;
+  float* const k_cache = L.k_cache;
+  float* const v_cache = L.v_cache;
   float* const red = c.red;
   float* const stg = c.stg;
   const unsigned flag = c.flag;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int Lt = D.latent, nope = D.nope, hd = D.head_dim, rb = D.rb_lat, ss = D.ss_lat;
+  const int tid = threadIdx.x;
+  const int Lt = D.latent, nope = D.nope, hd = D.head_dim, kvpad = D.kvpad;
   const int P = static_cast<int>(c.pos);
-  bool ok = true;
   const unsigned char* cst = stream_acquire(p, c.st, chunk);
-  if (__syncthreads_or(cst == nullptr)) ok = false;
-  const AttnSmem A = attn_smem(c.U, D);
-  const float* qh = c.xl;                 // gathered q of the head
-  const float* lat = c.xl + hd;           // the latent
-  const float* kh = lat + Lt;             // k_rope of the head
-  const float a_cur = quantize_block(lat, Lt, nullptr, 0.0f, 0.0f, D.act_eps, A.qlc, false, nullptr, red);
-  for (int j = tid; j < Lt; j += kThreads) lat_q[static_cast<size_t>(P) * D.lpad + j] = A.qlc[j];
-  for (int j = Lt + tid; j < D.lpad; j += kThreads) A.qlc[j] = 0;  // the row's padding (read as whole chunks)
-  if (tid == 0) lat_s[P] = a_cur;
-  const float scl = L.attn_scale;
-  cp_async_wait_all();  // the rope row of this position
-  __syncthreads();
-  c.tick(0);
-  for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
-    const float cs = c.rope_s[2 * jr], sn = c.rope_s[2 * jr + 1];
-    const float q0 = qh[nope + 2 * jr], q1 = qh[nope + 2 * jr + 1];
-    const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
-    A.qr[2 * jr] = (q0 * cs - q1 * sn) * scl;
-    A.qr[2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
-    const float kr0 = k0 * cs - k1 * sn, kr1 = k0 * sn + k1 * cs;
-    A.krc[2 * jr] = kr0;
-    A.krc[2 * jr + 1] = kr1;
-    uint16_t* kc = kr_cache + (static_cast<size_t>(h) * D.max_len + P) * D.rpad;
-    kc[2 * jr] = f2h(kr0);
-    kc[2 * jr + 1] = f2h(kr1);
-  }
-  for (int e = tid; e < nope; e += kThreads) A.qn[e] = qh[e] * scl;
-  __syncthreads();
-  float qb;  // q_nope . b_k
-  // absorbed query qa[j] = sum_e qn[e] s[e] (W_knope[h][e][j]): thread (byte jb, group eg) takes the four
-  // latent entries of packed byte jb over the rows e = eg, eg + G, ...; the G group sums are added in order
-  {
-    const int nb = (Lt + 3) >> 2, G = kThreads / nb;
-    const unsigned char* wkn = cst + c_wkn;
-    const uint16_t* skn = reinterpret_cast<const uint16_t*>(cst + c_skn);
-    const int jb = tid % nb, eg = tid / nb;
-    if (eg < G) {
-      float a4[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int e = eg; e < nope; e += G) {
-        const int byte = wkn[e * rb + jb];
-        const float q = A.qn[e] * h2f(skn[e * ss + (jb >> 5)]);
-#pragma unroll
-        for (int f = 0; f < 4; ++f) a4[f] = fmaf(q, code_m1(static_cast<unsigned>(byte) >> (2 * f)), a4[f]);
-      }
-#pragma unroll
-      for (int f = 0; f < 4; ++f) A.scr[eg * 4 * nb + 4 * jb + f] = a4[f];
-    }
-    float pp = 0.0f;
-    const float* bkn = reinterpret_cast<const float*>(cst + c_bkn);
-    for (int e = tid; e < nope; e += kThreads) pp = fmaf(A.qn[e], bkn[e], pp);
-    qb = block_sum(pp, red);  // its barrier also orders the partial sums above
-    const int l32 = (Lt + 31) / 32 * 32;
-    for (int j = tid; j < l32; j += kThreads) {
-      float s = 0.0f;
-      if (j < Lt)
-        for (int g = 0; g < G; ++g) s += A.scr[g * 4 * nb + j];
-      A.qa[j] = s;  // zero beyond the latent width (the score loop reads whole chunks)
-    }
-  }
-  __syncthreads();
-  c.tick(1);
-  float m_run, l_run;
-  float u_acc[16 * kMaxLatentPerLane / 16 * 4];
-  const int lc = D.lpad >> 4;
-  bool tiles_ok;
-  if (lc <= 8) {
-    float acc[16];
-    tiles_ok = attn_tiles<1, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) u_acc[i] = acc[i];
-  } else if (lc <= 16) {
-    float acc[32];
-    // the Nano latent (256: 16 chunks) with its row shape fixed at compile time
-    tiles_ok = lc == 16 ? attn_tiles<2, 16>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc)
-                        : attn_tiles<2, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
-#pragma unroll
-    for (int i = 0; i < 32; ++i) u_acc[i] = acc[i];
-  } else {
-    float acc[64];
-    tiles_ok = attn_tiles<4, 0>(c, p, D, L, A, h, P, a_cur, qb, m_run, l_run, acc);
-#pragma unroll
-    for (int i = 0; i < 64; ++i) u_acc[i] = acc[i];
-  }
-  ok &= tiles_ok;
-  c.tick(2);
+  bool ok = !__syncthreads_or(cst == nullptr);
   if (ok) {
-    // the four lane groups of a warp hold the same chunks: add them, then the warps' sums in warp order
-    const int sub = lane & 7, cpl = (lc + 7) >> 3;
-    float* part = reinterpret_cast<float*>(A.tiles);  // [kWarps][lpad] (both tile buffers are free now)
-#pragma unroll
-    for (int j = 0; j < kMaxLatentPerLane / 4; ++j) {
-      if (j < cpl) {
-#pragma unroll
-        for (int e = 0; e < 16; ++e) {
-          float v = u_acc[16 * j + e];
-          v += __shfl_xor_sync(kFull, v, 8);
-          v += __shfl_xor_sync(kFull, v, 16);
-          if (lane < 8 && sub + 8 * j < lc) part[warp * D.lpad + 16 * (sub + 8 * j) + e] = v;
-        }
+    const AttnSmem A = attn_smem(c.U, D);
+    const float* qh = c.xl;           // gathered q of the head
+    const float* lat = c.xl + hd;     // the latent
+    const float* kh = lat + Lt;       // k_rope of the head
+    // the latent's codes (GEMV layout, with the half-chunk sums) and scale; the cache keeps them in order
+    const float a_cur = gather_quantize_reg<4>(nullptr, Lt, flag, const_cast<float*>(lat), nullptr, 0.0f, 0.0f, D.act_eps, c.act,
+                                               c.xsum, red, p.timeout_ns, nullptr);
+    for (int j = tid; j < D.lpad; j += kThreads)
+      lat_q[static_cast<size_t>(P) * D.lpad + j] = j < Lt ? c.act[act_slot(j)] : static_cast<int8_t>(0);
+    if (tid == 0) lat_s[P] = a_cur;
+    cp_async_wait_all();  // the rope row of this position
+    __syncthreads();
+    c.tick(0);
+    // k_nope and v of this position: the head's kv up-projection rows against the codes
+    rows_decode(cst, kv_rows, kv_rb, kv_ss, 1, a_cur, c.act, c.xsum, Lt, kv_lg, A.kv, EPI_STORE, nullptr, nullptr, flag);
+    // the scaled query (rope pairs rotated) and the rope part of this position's key (rotated, rounded
+    // to fp16 as the k_rope cache holds it)
+    const float scl = L.attn_scale;
+    for (int e = tid; e < nope; e += kThreads) A.q[e] = qh[e] * scl;
+    for (int jr = tid; jr < D.rope / 2; jr += kThreads) {
+      const float cs = c.rope_s[2 * jr], sn = c.rope_s[2 * jr + 1];
+      const float q0 = qh[nope + 2 * jr], q1 = qh[nope + 2 * jr + 1];
+      A.q[nope + 2 * jr] = (q0 * cs - q1 * sn) * scl;
+      A.q[nope + 2 * jr + 1] = (q0 * sn + q1 * cs) * scl;
+      const float k0 = kh[2 * jr], k1 = kh[2 * jr + 1];
+      const uint16_t r0 = f2h(k0 * cs - k1 * sn), r1 = f2h(k0 * sn + k1 * cs);
+      uint16_t* kc = kr_cache + (static_cast<size_t>(h) * D.max_len + P) * D.rpad;
+      kc[2 * jr] = r0;
+      kc[2 * jr + 1] = r1;
+      A.kcur[nope + 2 * jr] = h2f(r0);
+      A.kcur[nope + 2 * jr + 1] = h2f(r1);
+    }
+    for (int e = hd + tid; e < kvpad; e += kThreads) {
+      A.q[e] = 0.0f;
+      A.kcur[e] = 0.0f;
+    }
+    __syncthreads();  // the kv rows are in A.kv
+    for (int e = tid; e < nope; e += kThreads) A.kcur[e] = A.kv[e];
+    __syncthreads();
+    {
+      const size_t row = (static_cast<size_t>(h) * D.max_len + P) * kvpad;
+      for (int e = tid; e < kvpad; e += kThreads) {
+        k_cache[row + e] = A.kcur[e];
+        v_cache[row + e] = e < hd ? A.kv[nope + e] : 0.0f;
       }
     }
-    __syncthreads();
-    for (int j = tid; j < D.lpad; j += kThreads) {
-      float s = 0.0f;
-      for (int w = 0; w < kWarps; ++w) s += part[w * D.lpad + j];
-      A.u[j] = j < Lt ? s : 0.0f;
-    }
-    __syncthreads();
-    // out[e] = s[e] (W_v[h][e] . u) / l + b_v[e]: LP lanes per output, lane q taking the packed words
-    // q, q + LP, ... of the row (16 latent entries, one scale group each)
-    const unsigned char* wv = cst + c_wv;
-    const uint16_t* sv = reinterpret_cast<const uint16_t*>(cst + c_sv);
-    const float* bv = reinterpret_cast<const float*>(cst + c_bv);
-    const float inv_l = 1.0f / l_run;
-    int LP = 32;
-    while (LP > 1 && LP * hd > kThreads) LP >>= 1;
-    const int q = tid & (LP - 1), nw = (Lt + 15) >> 4;
-    for (int e0 = 0; e0 < hd; e0 += kThreads / LP) {
-      const int e = e0 + tid / LP;
-      float acc0 = 0.0f, acc1 = 0.0f;
-      if (e < hd) {
-        const unsigned* row = reinterpret_cast<const unsigned*>(wv + e * rb);
-        for (int w = q; w < nw; w += LP) {
-          const unsigned bits = row[w];
-          const float4* uu = reinterpret_cast<const float4*>(A.u + 16 * w);
-          float t0 = 0.0f, t1 = 0.0f;
-#pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float4 u4 = uu[t];
-            const unsigned b = bits >> (8 * t);
-            t0 = fmaf(code_m1(b), u4.x, t0);
-            t1 = fmaf(code_m1(b >> 2), u4.y, t1);
-            t0 = fmaf(code_m1(b >> 4), u4.z, t0);
-            t1 = fmaf(code_m1(b >> 6), u4.w, t1);
-          }
-          const float sc = h2f(sv[e * ss + (w >> 3)]);
-          if (w & 1) acc1 = fmaf(sc, t0 + t1, acc1);
-          else acc0 = fmaf(sc, t0 + t1, acc0);
-        }
+    c.tick(1);
+    float l_run;
+    float4 acc;
+    const int kq = kvpad >> 2;
+    ok = kq <= 8    ? attn_tiles<1>(c, p, D, L, A, h, P, l_run, acc)
+         : kq <= 16 ? attn_tiles<2>(c, p, D, L, A, h, P, l_run, acc)
+                    : attn_tiles<4>(c, p, D, L, A, h, P, l_run, acc);
+    c.tick(2);
+    if (ok) {
+      // the position groups' value sums, added in group order, over the softmax total
+      const int G = kThreads / kq, pg = tid / kq;
+      if (pg < G) reinterpret_cast<float4*>(A.part)[pg * kq + tid % kq] = acc;
+      __syncthreads();
+      const float inv_l = 1.0f / l_run;
+      for (int e = tid; e < hd; e += kThreads) {
+        float s = 0.0f;
+        for (int g = 0; g < G; ++g) s += A.part[g * kvpad + e];
+        stg[e] = s * inv_l;
       }
-      float acc = acc0 + acc1;
-      for (int o = 1; o < LP; o <<= 1) acc += __shfl_xor_sync(kFull, acc, o);
-      if (e < hd && q == 0) stg[e] = acc * inv_l + bv[e];
+      __syncthreads();
+      ll_put(p.ll + ll_out, h * hd, stg, hd, flag);
+      c.tick(3);
     }
-    __syncthreads();
-    ll_put(p.ll + ll_out, h * hd, stg, hd, flag);
-    c.tick(3);
   }
   asm volatile("fence.proxy.async.global;" ::: "memory");
   if (!ok) c.fail(IVB_ETIMEOUT);
@@ -977,6 +879,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     c.U = smem + M.u;
     c.abar = abar;
     c.apar[0] = c.apar[1] = 0u;
+    c.apend = 0u;
     c.marks = nullptr;
     c.pos = ldcg_i64(p.position);
     c.inv_t = 1.0f / __ldcg(p.sampling);
@@ -1021,7 +924,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         // the first tile of cached positions (independent of this token) before the input arrives
         if (tid == 0 && pos > 0)
           tile_issue(lay, D, tile_buf(attn_smem(c.U, D).tiles, D, 0), h, 0, min(static_cast<int>(pos), D.tile), &abar[0],
-                     p.error);
+                     c.apend, 0);
         // the rope row of this position (waited for inside), and the head's q, the latent and the
         // head's k_rope from the entry op's output [q | latent | k_rope]
         const float* rrow = lay.rope + static_cast<size_t>(pos) * D.rope;
@@ -1038,6 +941,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
           for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
           mark(c.marks, 7);
         }
+        if (!ok && tid == 0) attn_drain(c, p.timeout_ns);  // tile copies a failed op left in flight
         cp_async_wait_all();
         ++opk;
         const bool failed = __syncthreads_or(!ok);
@@ -1230,6 +1134,7 @@ static int32_t validate(const IvbModelDesc& d) {
   if (d.latent_dim > 32 * kMaxLatentPerLane) return fail(IVB_EINVAL, "latent_dim %d > %d", d.latent_dim, 32 * kMaxLatentPerLane);
   if (d.rope_dim + d.nope_dim != d.head_dim || (d.rope_dim & 1)) return fail(IVB_EINVAL, "rope_dim + nope_dim must equal head_dim");
   if ((d.head_dim & 1) || (d.latent_dim & 1)) return fail(IVB_EINVAL, "head_dim and latent_dim must be even");
+  if (d.head_dim > 128) return fail(IVB_EINVAL, "head_dim %d > 128", d.head_dim);
   if (d.max_top_k <= 0) return fail(IVB_EINVAL, "max_top_k must be positive");
   if (!d.layers || !d.logits || !d.token || !d.position || !d.seen || !d.sampling || !d.top_k || !d.rng || !d.final_norm)
     return fail(IVB_EINVAL, "null state pointer in the model description");
@@ -1275,6 +1180,8 @@ static int32_t validate(const IvbModelDesc& d) {
       if ((reinterpret_cast<uintptr_t>(L.latent_q) & 15) || (reinterpret_cast<uintptr_t>(L.latent_scale) & 15) ||
           (reinterpret_cast<uintptr_t>(L.k_rope_cache) & 15))
         return fail(IVB_EINVAL, "layer %d: the latent cache must be 16-byte aligned", i);
+      if (!L.k_cache || !L.v_cache || (reinterpret_cast<uintptr_t>(L.k_cache) & 15) || (reinterpret_cast<uintptr_t>(L.v_cache) & 15))
+        return fail(IVB_EINVAL, "layer %d: missing or unaligned key/value cache", i);
     } else {
       return fail(IVB_EINVAL, "layer %d: unknown kind %d", i, L.kind);
     }
@@ -1311,6 +1218,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   D.act_eps = md.act_eps;
   D.clip = md.norm_clip;
   D.lpad = static_cast<int>(r16(md.latent_dim));
+  D.kvpad = r4(md.head_dim);
   D.rpad = (md.rope_dim + 7) / 8 * 8;
   D.rb_lat = static_cast<int>(r16((md.latent_dim + 3) / 4));
   D.ss_lat = ((md.latent_dim + 127) / 128 + 7) / 8 * 8;
@@ -1414,8 +1322,19 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
       a.op.layer = li;
       a.op.in_dst = IN_LATENT;
       a.op.in_n = Lt;
-      a.op.rows_per = 0;
+      // the head's kv up-projection rows (k_nope, then v) as one GEMV row chunk of its stream
+      a.op.rows_per = D.nope + hd;
       a.op.rows_total = 0;
+      a.op.row_bytes = D.rb_lat;
+      a.op.scale_stride = D.ss_lat;
+      a.op.has_bias = 1;
+      {
+        const int chunks = (Lt + 63) / 64;
+        int lg = 0;
+        while (lg < 5 && ((chunks + (1 << lg) - 1) >> lg) > kRowsKPL) ++lg;
+        while (lg < 4 && (1 << (lg + 1)) <= chunks && (a.op.rows_per << (lg + 1)) <= kThreads) ++lg;
+        a.op.lpr_log = lg;
+      }
       a.const_kind = 3;
       a.layer = &L;
       a.out_words = d;  // the heads' outputs, written by the attention CTAs
@@ -1474,19 +1393,9 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
       op.c_convb = static_cast<int>(off);
       off += r16(cpc * 4);
     }
-    if (pl.const_kind == 3) {
-      op.c_wkn = static_cast<int>(off);
-      off += r16(static_cast<size_t>(D.nope) * D.rb_lat);
-      op.c_skn = static_cast<int>(off);
-      off += r16(static_cast<size_t>(D.nope) * D.ss_lat * 2);
-      op.c_bkn = static_cast<int>(off);
-      off += r16(D.nope * 4);
-      op.c_wv = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hd) * D.rb_lat);
-      op.c_sv = static_cast<int>(off);
-      off += r16(static_cast<size_t>(hd) * D.ss_lat * 2);
-      op.c_bv = static_cast<int>(off);
-      off += r16(hd * 4);
+    if (pl.const_kind == 3) {  // [k x row_bytes][k x scale_stride fp16, 16B pad][k x fp32 bias], k = nope + hd
+      const size_t k = static_cast<size_t>(D.nope + hd);
+      off = k * D.rb_lat + r16(k * D.ss_lat * 2) + r16(k * 4);
     }
     op.has_const = pl.const_kind != 0;
     max_const = std::max(max_const, off);
@@ -1526,7 +1435,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   M.ring = 0;
   M.stage_bytes = static_cast<int>(stage);
   o += kStages * stage;
-  const int max_in = std::max(d, F);
+  const int max_in = std::max(std::max(d, F), Lt);  // GEMV inputs, the latent's codes included
   const int pad_in = (max_in + 63) / 64 * 64;
   M.xv = static_cast<int>(o);
   o += r16(static_cast<size_t>(pad_in) * 4);
@@ -1601,10 +1510,7 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   int tile = 0;
   if (any_mla) {
     // two tile buffers of tile + 1 rows (the last tile also holds the current position)
-    auto attn_bytes = [&](int t) {
-      const size_t rows = static_cast<size_t>(t) + 1;
-      return attn_fixed_bytes(Lt, D.rope, D.nope, t) + 2 * (r16(rows * D.lpad) + r16(rows * 4) + r16(rows * D.rpad * 2));
-    };
+    auto attn_bytes = [&](int t) { return attn_fixed_bytes(D.nope, hd, t) + 4 * tile_bytes(t, D.kvpad); };
     tile = std::min(256, (md.max_len + 15) / 16 * 16);
     while (tile >= 16 && attn_bytes(tile) > room) tile -= 16;
     if (tile < 16) {
@@ -1742,21 +1648,22 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   for (int h = 0; h < dec->A; ++h)
     for (int mi = 0; mi < n_mla; ++mi) {
       const OpPlan& pl = plans[dec->attn_ops[mi]];
-      const Op& op = pl.op;
       const IvbLayerDesc& L = *pl.layer;
       const IvbTernary& kn = L.k_nope_up;
       const IvbTernary& vu = L.v_up;
       const size_t sgroups = static_cast<size_t>((Lt + 127) / 128) * 2;
-      const size_t base = cursor;
-      add(base + op.c_wkn, kn.packed + static_cast<size_t>(h) * D.nope * kn.row_bytes, D.rb_lat, D.nope, kn.row_bytes, D.rb_lat);
-      add(base + op.c_skn, kn.scales + static_cast<size_t>(h) * D.nope * kn.scale_stride, sgroups, D.nope,
+      const size_t base = cursor, k = static_cast<size_t>(D.nope + hd), nn = static_cast<size_t>(D.nope);
+      const size_t sc_off = k * D.rb_lat, b_off = sc_off + r16(k * D.ss_lat * 2);
+      // rows [0, nope): k_nope rows of head h; rows [nope, nope + hd): its v rows (absent biases are zero)
+      add(base, kn.packed + static_cast<size_t>(h) * D.nope * kn.row_bytes, D.rb_lat, nn, kn.row_bytes, D.rb_lat);
+      add(base + nn * D.rb_lat, vu.packed + static_cast<size_t>(h) * hd * vu.row_bytes, D.rb_lat, hd, vu.row_bytes, D.rb_lat);
+      add(base + sc_off, kn.scales + static_cast<size_t>(h) * D.nope * kn.scale_stride, sgroups, nn,
           static_cast<size_t>(kn.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
-      add(base + op.c_bkn, kn.bias ? static_cast<const void*>(kn.bias + h * D.nope) : nullptr, D.nope * 4, 1, 0, 0);
-      add(base + op.c_wv, vu.packed + static_cast<size_t>(h) * hd * vu.row_bytes, D.rb_lat, hd, vu.row_bytes, D.rb_lat);
-      add(base + op.c_sv, vu.scales + static_cast<size_t>(h) * hd * vu.scale_stride, sgroups, hd,
+      add(base + sc_off + nn * D.ss_lat * 2, vu.scales + static_cast<size_t>(h) * hd * vu.scale_stride, sgroups, hd,
           static_cast<size_t>(vu.scale_stride) * 2, static_cast<size_t>(D.ss_lat) * 2);
-      add(base + op.c_bv, vu.bias ? static_cast<const void*>(vu.bias + h * hd) : nullptr, hd * 4, 1, 0, 0);
-      const size_t bytes = r16(static_cast<size_t>(op.c_bv) + r16(hd * 4));
+      add(base + b_off, kn.bias ? static_cast<const void*>(kn.bias + h * D.nope) : nullptr, nn * 4, 1, 0, 0);
+      add(base + b_off + nn * 4, vu.bias ? static_cast<const void*>(vu.bias + h * hd) : nullptr, static_cast<size_t>(hd) * 4, 1, 0, 0);
+      const size_t bytes = r16(b_off + r16(k * 4));
       dec->attn_off[static_cast<size_t>(h) * n_mla + mi] = base;
       dec->attn_bytes[static_cast<size_t>(h) * n_mla + mi] = static_cast<unsigned>(bytes);
       cursor = r16(base + bytes);

@@ -501,6 +501,26 @@ __global__ void kv_split_kernel(IvbLayerDesc L, const float* knope, const float*
   (void)vlw;
 }
 
+// The decode kernel's key / value cache rows of positions pos0 .. pos0 + T - 1 (layout of
+// IvbLayerDesc.k_cache / v_cache): keys [K_nope | rotated k_rope as k_rope_cache holds it], values, zero
+// padding to kvpad floats. One thread per (position, head, dim).
+__global__ void kv_cache_kernel(IvbLayerDesc L, const float* knope, const float* vbuf, int pos0, int T, int H, int hd, int nope,
+                                int max_len, int rpad, int kvpad) {
+  pdl_enter();
+  const long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= static_cast<long long>(T) * H * kvpad) return;
+  const int e = static_cast<int>(i % kvpad);
+  const long long r = i / kvpad;
+  const int h = static_cast<int>(r % H), pos = pos0 + static_cast<int>(r / H);
+  float k = 0.0f, v = 0.0f;
+  if (e < nope) k = knope[static_cast<size_t>(pos) * H * nope + h * nope + e];
+  else if (e < hd) k = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + pos) * rpad + (e - nope)]);
+  if (e < hd) v = vbuf[static_cast<size_t>(pos) * H * hd + h * hd + e];
+  const size_t o = (static_cast<size_t>(h) * max_len + pos) * kvpad + e;
+  L.k_cache[o] = k;
+  L.v_cache[o] = v;
+}
+
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
 }
@@ -908,6 +928,13 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
       if (int32_t rc = ternary_gemm_into(&L.v_up, kvq8, ldl, L.latent_scale, P, IVB_EPI_STORE, vbuf, d, err, partial,
                                          kGemmPartialFloats, stream))
         return rc;
+      if (L.k_cache != nullptr && L.v_cache != nullptr) {  // the decode kernel's cache rows of the new positions
+        const int kvpad = (hd + 3) & ~3;
+        const long long n = static_cast<long long>(count) * H * kvpad;
+        IVB_CUDA(launch_pdl(kv_cache_kernel, dim3(static_cast<unsigned>((n + 255) / 256)), dim3(256), 0, s, L, knope, vbuf,
+                            start_position, count, H, hd, nope, md.max_len, rpad, kvpad));
+        IVB_CUDA(cudaGetLastError());
+      }
       if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, kvh, start_position, count, d, H, hd, rope,
                                               nope, md.max_len, rpad, y, s))
         return rc;

@@ -163,6 +163,7 @@ class B200Decoder(StaticDecoder):
         self.final_norm = model.final_norm.weight.float().to(dev).contiguous()
         self.layer_matrices: list[dict[str, DeviceMatrix]] = []
         self.latent_caches: dict[int, tuple[Tensor, Tensor, Tensor]] = {}
+        self.kv_caches: dict[int, tuple[Tensor, Tensor]] = {}
         self._keep: list[Tensor] = []
         layers = (native.IvbLayerDesc * len(model.blocks))()
         dims = {"state": int(config.state_dim), "latent": int(config.latent_dim), "rope": 2, "nope": head_dim - 2}
@@ -224,14 +225,22 @@ class B200Decoder(StaticDecoder):
                 # bulk copies read scales in 16-byte units: pad so a tile ending at max_len stays inside
                 latent_scale = torch.zeros((self.max_len + 7) // 4 * 4, dtype=torch.float32, device=dev)
                 k_rope = torch.zeros(mixer.num_heads, self.max_len, rpad, dtype=torch.float16, device=dev)
+                # the decode kernel's decompressed cache: per head and position, fp32 keys [k_nope |
+                # rotated k_rope] and values, rows padded to 16 bytes
+                kvpad = (int(mixer.head_dim) + 3) // 4 * 4
+                k_cache = torch.zeros(mixer.num_heads, self.max_len, kvpad, dtype=torch.float32, device=dev)
+                v_cache = torch.zeros_like(k_cache)
                 self._keep.append(rope)
                 self.latent_caches[index] = (latent_q, latent_scale, k_rope)
+                self.kv_caches[index] = (k_cache, v_cache)
                 desc.k_nope_up = mats["k_nope_up"].desc()
                 desc.v_up = mats["v_up"].desc()
                 desc.rope = rope.data_ptr()
                 desc.latent_q = latent_q.data_ptr()
                 desc.latent_scale = latent_scale.data_ptr()
                 desc.k_rope_cache = k_rope.data_ptr()
+                desc.k_cache = k_cache.data_ptr()
+                desc.v_cache = v_cache.data_ptr()
                 desc.attn_scale = 1.0 / math.sqrt(mixer.head_dim)
                 dims.update(latent=int(mixer.latent_dim), rope=int(mixer.rope_dim), nope=int(mixer.nope_dim))
             else:
