@@ -23,7 +23,8 @@
 
 namespace ivb {
 
-constexpr int kStages = 6;
+constexpr int kStages = 6;      // ring stages of a GEMV CTA's weight stream
+constexpr int kAttnStages = 2;  // ring stages of an attention CTA (the last two of the ring; the rest holds tiles)
 
 enum OpKind : int32_t {
   OP_ENTRY_MAMBA = 0, OP_ENTRY_MLA = 1, OP_ATTN = 2, OP_OUT = 3, OP_GATE_UP = 4, OP_DOWN = 5, OP_HEAD = 6, OP_MERGE = 7
@@ -39,7 +40,6 @@ struct Op {
   int32_t in_dst;                  // InDst of the gathered input
   int32_t ll_in, ll_in_words;      // input: word offset of the previous op's output buffer and its length (-1: none)
   int32_t ll_out;                  // word offset of this op's output buffer
-  int32_t push_per;                // entry of an mla block: latent rows per CTA (output slice stride)
   int32_t in_n;                    // GEMV input length
   int32_t rows_per, rows_total;    // uniform row partition across the CTAs (attention: the head's kv rows)
   int32_t chunk_rows;              // rows per stream chunk
@@ -229,7 +229,7 @@ __device__ __forceinline__ bool ll_gather(const unsigned long long* buf, int n, 
 // consumers address chunk number `idx` of the run (every thread knows it: the chunks consumed by
 // earlier tokens plus the op's first chunk), so no per-thread counter travels between routines.
 struct Stream {
-  unsigned long long* full;  // [kStages] mbarriers
+  unsigned long long* full;  // [NS] mbarriers
   unsigned char* ring;
   int stage_bytes;
   const unsigned long long* caddr;  // this CTA's chunk table (shared copy): device addresses
@@ -247,7 +247,8 @@ __device__ __forceinline__ int chunks_of_step(const DecodeParams& p, const Strea
   return head_needed(p, step) ? s->cpt : s->head_first;
 }
 
-// thread 0 only: queue the next chunk of this CTA's stream into the next ring stage
+// thread 0 only: queue the next chunk of this CTA's stream into the next of its NS ring stages
+template <int NS = kStages>
 __device__ __forceinline__ void stream_issue(const DecodeParams& p, Stream* s) {
   if (s->p_step >= p.steps) return;
   if (s->p_chunk == s->head_first && !head_needed(p, s->p_step)) {
@@ -255,7 +256,7 @@ __device__ __forceinline__ void stream_issue(const DecodeParams& p, Stream* s) {
     if (++s->p_step >= p.steps) return;
   }
   const unsigned bytes = s->cbytes[s->p_chunk];
-  const int stage = s->issued % kStages;
+  const int stage = s->issued % NS;
   unsigned long long* bar = s->full + stage;
   mbar_expect_tx(bar, bytes);  // the stage is only ever written by the copy engine: no proxy fence
   bulk_copy(s->ring + static_cast<size_t>(stage) * s->stage_bytes, reinterpret_cast<const void*>(s->caddr[s->p_chunk]), bytes,
@@ -284,17 +285,19 @@ __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsig
 // every thread: wait until chunk `idx` of the run has landed in its ring stage (each thread's own
 // mbarrier wait makes the copied bytes visible to it; no CTA barrier). Returns the stage base, or
 // nullptr when this thread's bounded wait ran out (the op reports it after its closing barrier).
+template <int NS = kStages>
 __device__ __forceinline__ const unsigned char* stream_acquire(const DecodeParams& p, const Stream* s, unsigned idx) {
-  const int stage = idx % kStages;
-  const unsigned parity = (idx / kStages) & 1u;
+  const int stage = idx % NS;
+  const unsigned parity = (idx / NS) & 1u;
   if (!mbar_wait_bounded(s->full + stage, parity, p.timeout_ns)) return nullptr;
   return s->ring + static_cast<size_t>(stage) * s->stage_bytes;
 }
 
 // thread 0, after a CTA barrier that follows the last read of the stages: refill every stage freed
 // since the last call (chunks below `consumed` are no longer read), keeping the ring full.
+template <int NS = kStages>
 __device__ __forceinline__ void stream_refill(const DecodeParams& p, Stream* s, unsigned consumed) {
-  while (s->issued < consumed + kStages && s->p_step < p.steps) stream_issue(p, s);
+  while (s->issued < consumed + NS && s->p_step < p.steps) stream_issue<NS>(p, s);
 }
 
 // ---- GEMV rows from a ring stage ----------------------------------------------------------------

@@ -186,19 +186,35 @@ __device__ __forceinline__ float gather_quantize_reg(const unsigned long long* b
   const float scale = fmaxf(__uint_as_float(mbits) / 127.0f, act_eps);
   const float rscale = 1.0f / scale;
   const int padded = (n + 63) & ~63;
+  // every code first (the rare value within rounding distance of a half takes the IEEE division), so
+  // the E warp reductions below run back to back after one reconvergence
+  int qk[E];
+  bool near = false;
+#pragma unroll
+  for (int k = 0; k < E; ++k) {
+    bool nr = false;
+    qk[k] = tid + k * kThreads < n ? quant_code_fast(v[k], rscale, nr) : 0;
+    near |= nr;
+  }
+  if (near) {
+#pragma unroll
+    for (int k = 0; k < E; ++k) {
+      bool nr = false;
+      if (tid + k * kThreads < n) {
+        quant_code_fast(v[k], rscale, nr);
+        if (nr) qk[k] = static_cast<int>(rintf(v[k] / scale));
+      }
+    }
+  }
+  // the code sum of the half chunk each warp holds (64-input chunk u = 4k + warp / 2), for the row dots
+  int hs[E];
+#pragma unroll
+  for (int k = 0; k < E; ++k) hs[k] = __reduce_add_sync(kFull, qk[k]);
 #pragma unroll
   for (int k = 0; k < E; ++k) {
     const int i = tid + k * kThreads;
-    int q = 0;
-    if (i < n) {
-      bool nr = false;
-      q = quant_code_fast(v[k], rscale, nr);
-      if (nr) q = static_cast<int>(rintf(v[k] / scale));  // within rounding distance of a half: the IEEE division
-    }
-    if (i < padded) codes[act_slot(i)] = static_cast<int8_t>(q);
-    // the code sum of the half chunk this warp holds (64-input chunk u = 4k + warp / 2), for the row dots
-    const int hs = __reduce_add_sync(kFull, q);
-    if (lane == 0 && k * kThreads + warp * 32 < padded) xhalf[2 * (4 * k + (warp >> 1)) + (warp & 1)] = hs;
+    if (i < padded) codes[act_slot(i)] = static_cast<int8_t>(qk[k]);
+    if (lane == 0 && k * kThreads + warp * 32 < padded) xhalf[2 * (4 * k + (warp >> 1)) + (warp & 1)] = hs[k];
   }
   __syncthreads();
   return scale;
@@ -242,24 +258,23 @@ struct Ctx {
 
 // Shared-memory layout of the attention op inside the union region (the plan sizes it the same way):
 // kv rows of this position [nope + head_dim] | scaled query, rope pairs rotated [kvpad] | this
-// position's key row [kvpad] | scores [tile + 4] | partial value sums [4 * kThreads] | 16-byte aligned
-// double tile buffer (tile_buf).
+// position's key row [kvpad] | the warps' value sums [4 * kThreads] | 16-byte aligned double tile
+// buffer (tile_buf).
 struct AttnSmem {
-  float *kv, *q, *kcur, *sc, *part;
+  float *kv, *q, *kcur, *part;
   unsigned char* tiles;
 };
 __host__ __device__ __forceinline__ int r4(int n) { return (n + 3) & ~3; }
-__host__ __device__ __forceinline__ size_t attn_fixed_bytes(int nope, int hd, int tile) {
+__host__ __device__ __forceinline__ size_t attn_fixed_bytes(int nope, int hd) {
   const int kvpad = r4(hd);
-  return static_cast<size_t>(r4(nope + hd) + 2 * kvpad + r4(tile + 4) + 4 * kThreads) * 4 + 16;
+  return static_cast<size_t>(r4(nope + hd) + 2 * kvpad + 4 * kThreads) * 4 + 16;
 }
 __device__ __forceinline__ AttnSmem attn_smem(unsigned char* U, const DecodeDims& D) {
   AttnSmem a;
   a.kv = reinterpret_cast<float*>(U);
   a.q = a.kv + r4(D.nope + D.head_dim);
   a.kcur = a.q + D.kvpad;
-  a.sc = a.kcur + D.kvpad;
-  a.part = a.sc + r4(D.tile + 4);
+  a.part = a.kcur + D.kvpad;
   unsigned char* t = reinterpret_cast<unsigned char*>(a.part + 4 * kThreads);
   a.tiles = t + ((16 - (reinterpret_cast<uintptr_t>(t) & 15)) & 15);
   return a;
@@ -275,73 +290,37 @@ __device__ __forceinline__ void attn_drain(Ctx& c, unsigned long long timeout_ns
     }
 }
 
-// Scores of the npos positions of a tile (keys K [npos][kq float4]): 8 lanes per position, lane q
-// taking the quads q, q + 8, ... of the key row against the query quads it holds in qv; the lane sums
-// are added by a butterfly and the score goes to sc[k]. One phase of a 16-byte load is one position's
-// 128 contiguous bytes, free of bank conflicts. Returns the thread's maximum score.
-template <int NQ>
-__device__ __forceinline__ float attn_scores(const float4 (&qv)[NQ], const float* K, int kq, int npos, float* sc) {
-  const int tid = threadIdx.x, q = tid & 7;
-  float wmax = -INFINITY;
-  for (int k0 = 0; k0 < npos; k0 += kThreads / 8) {
-    const int k = k0 + (tid >> 3);
-    float d0 = 0.0f, d1 = 0.0f;
-    if (k < npos) {
-      const float4* row = reinterpret_cast<const float4*>(K) + static_cast<size_t>(k) * kq;
-#pragma unroll
-      for (int j = 0; j < NQ; ++j) {
-        if (q + 8 * j < kq) {
-          const float4 kk = row[q + 8 * j];
-          d0 = fmaf(qv[j].x, kk.x, d0);
-          d1 = fmaf(qv[j].y, kk.y, d1);
-          d0 = fmaf(qv[j].z, kk.z, d0);
-          d1 = fmaf(qv[j].w, kk.w, d1);
-        }
-      }
-    }
-    float dot = d0 + d1;
-#pragma unroll
-    for (int o = 1; o < 8; o <<= 1) dot += __shfl_xor_sync(kFull, dot, o);  // a position's lanes are in or out together
-    if (k < npos) {
-      if (q == 0) sc[k] = dot;
-      wmax = fmaxf(wmax, dot);
-    }
-  }
-  return wmax;
-}
-
-// The tile loop of the attention op: online softmax over positions 0..P, tile by tile, the current
-// position as the extra last row of the last tile. Value sum: thread (quad dq = tid % kq, group
-// pg = tid / kq) adds the weighted quad dq of the positions pg, pg + G, ... (G = kThreads / kq groups).
-// Returns false when a tile's wait ran out; l_run (the softmax total, scaled by exp(-max)) and the
-// thread's partial value quad `acc` are the results.
-template <int NQ>
+// The tile loop of the attention op: positions 0..P in tiles (the current position as the extra last
+// row of the last tile; the caller issued the copies of tiles 0 and 1), each warp running its own
+// online softmax over its positions 32 i + 4 w + g of every tile (lane group g = lane / 8), so a tile
+// needs no CTA-wide reduction. Scores: 8 lanes per position, lane q taking the key quads q, q + 8, ...
+// against the query quads it holds (one 16-byte load phase is one position's 128 contiguous bytes),
+// added by a butterfly over the group. Value sum: lane l owns the value pairs l, l + 32, ... of every
+// position the warp holds (a warp reads whole rows). Results per warp: the running maximum m_run, the
+// total l_run (scaled by exp(-m_run)) and the value pairs acc. Returns false when a tile's wait ran out.
+template <int NQ, int NV>
 __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const DecodeDims& D, const IvbLayerDesc& L,
-                                           const AttnSmem& A, int h, int P, float& l_run, float4& acc) {
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int kq = D.kvpad >> 2, tile = D.tile, kvpad = D.kvpad, hd = D.head_dim, nope = D.nope;
-  const int G = kThreads / kq, dq = tid % kq, pg = tid / kq;
-  float* const red = c.red;
+                                           const AttnSmem& A, int h, int P, float& m_run, float& l_run, float2 (&acc)[NV]) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, g = lane >> 3, q = lane & 7;
+  const int kq = D.kvpad >> 2, kv2 = D.kvpad >> 1, tile = D.tile, kvpad = D.kvpad, hd = D.head_dim, nope = D.nope;
   unsigned long long* const abar = c.abar;
   float4 qv[NQ];
 #pragma unroll
   for (int j = 0; j < NQ; ++j) {
-    const int qi = (tid & 7) + 8 * j;
+    const int qi = q + 8 * j;
     qv[j] = qi < kq ? reinterpret_cast<const float4*>(A.q)[qi] : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
   }
   const int n_tiles = P == 0 ? 1 : (P + tile - 1) / tile;
   bool ok = true;
-  float m_run = -INFINITY;
+  m_run = -INFINITY;
   l_run = 0.0f;
-  acc = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+  for (int j = 0; j < NV; ++j) acc[j] = make_float2(0.0f, 0.0f);
   for (int ti = 0; ti < n_tiles; ++ti) {
     const int start = ti * tile;
     const int count = max(0, min(tile, P - start));
     const bool last = ti == n_tiles - 1;
     const TileBuf tb = tile_buf(A.tiles, D, ti & 1);
-    if (tid == 0 && !last)
-      tile_issue(L, D, tile_buf(A.tiles, D, (ti + 1) & 1), h, start + tile, min(tile, P - start - tile), &abar[(ti + 1) & 1],
-                 c.apend, (ti + 1) & 1);
     if (last) {
       // the current position as row `count` (the bulk copy writes the rows below it)
       for (int e = tid; e < kvpad; e += kThreads) {
@@ -361,39 +340,78 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
     }
     if (last) __syncthreads();
     const int npos = count + (last ? 1 : 0);
-    const float wmax = attn_scores<NQ>(qv, tb.k, kq, npos, A.sc);
-    const float wm = warp_max(wmax);  // every lane takes part in the shuffles
-    if (lane == 0) red[32 + warp] = wm;  // block_sum below uses red[0 .. kWarps)
-    __syncthreads();
-    float mx = red[32];
-    for (int w = 1; w < kWarps; ++w) mx = fmaxf(mx, red[32 + w]);
-    const float m_new = fmaxf(m_run, mx);
-    const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
-    float ls = 0.0f;
-    for (int k = tid; k < npos; k += kThreads) {
-      const float e = expf(A.sc[k] - m_new);
-      A.sc[k] = e;
-      ls += e;
-    }
-    ls = block_sum(ls, red);  // its barrier also orders the weights above before the sums below
-    l_run = l_run * corr + ls;
-    acc.x *= corr;
-    acc.y *= corr;
-    acc.z *= corr;
-    acc.w *= corr;
-    if (pg < G) {
-      const float4* V = reinterpret_cast<const float4*>(tb.v);
-      for (int k = pg; k < npos; k += G) {
-        const float wk = A.sc[k];
-        const float4 v = V[k * kq + dq];
-        acc.x = fmaf(wk, v.x, acc.x);
-        acc.y = fmaf(wk, v.y, acc.y);
-        acc.z = fmaf(wk, v.z, acc.z);
-        acc.w = fmaf(wk, v.w, acc.w);
+    // scores: pass i covers positions 32 i + 4 w + g; after the group's butterfly, lane q keeps the
+    // score of pass q (npos <= 256, so a tile has at most 8 passes)
+    const int npass = (npos - 4 * warp + 31) >> 5;  // passes that hold a position of this warp (<= 0: none)
+    float my_s = -INFINITY;
+    for (int i = 0; i < npass; i += 2) {
+      const int ka = 32 * i + 4 * warp + g, kb = ka + 32;
+      float a0 = 0.0f, a1 = 0.0f, b0 = 0.0f, b1 = 0.0f;
+      const float4* ra = reinterpret_cast<const float4*>(tb.k) + static_cast<size_t>(ka) * kq;
+      const float4* rb = ra + 32 * kq;
+#pragma unroll
+      for (int j = 0; j < NQ; ++j) {
+        if (q + 8 * j < kq) {
+          if (ka < npos) {
+            const float4 kk = ra[q + 8 * j];
+            a0 = fmaf(qv[j].x, kk.x, a0);
+            a1 = fmaf(qv[j].y, kk.y, a1);
+            a0 = fmaf(qv[j].z, kk.z, a0);
+            a1 = fmaf(qv[j].w, kk.w, a1);
+          }
+          if (kb < npos) {
+            const float4 kk = rb[q + 8 * j];
+            b0 = fmaf(qv[j].x, kk.x, b0);
+            b1 = fmaf(qv[j].y, kk.y, b1);
+            b0 = fmaf(qv[j].z, kk.z, b0);
+            b1 = fmaf(qv[j].w, kk.w, b1);
+          }
+        }
       }
+      float da = a0 + a1, db = b0 + b1;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) {
+        da += __shfl_xor_sync(kFull, da, o);
+        db += __shfl_xor_sync(kFull, db, o);
+      }
+      if (q == i && ka < npos) my_s = da;
+      if (q == i + 1 && kb < npos) my_s = db;
     }
-    m_run = m_new;
-    __syncthreads();  // the tile buffer and the weights are reused
+    const float m_new = fmaxf(m_run, warp_max(my_s));
+    if (m_new != -INFINITY) {  // warp-uniform: the warp holds a position of this tile or an earlier one
+      const float corr = m_run == -INFINITY ? 0.0f : expf(m_run - m_new);
+      const float my_e = expf(my_s - m_new);  // 0 where the lane holds no position
+      l_run = l_run * corr + warp_sum(my_e);
+#pragma unroll
+      for (int j = 0; j < NV; ++j) {
+        acc[j].x *= corr;
+        acc[j].y *= corr;
+      }
+      // value sum: the weight of position 32 i + 4 w + gg sits in lane 8 gg + i
+      const float2* V = reinterpret_cast<const float2*>(tb.v);
+      for (int i = 0; i < npass; ++i) {
+#pragma unroll
+        for (int gg = 0; gg < 4; ++gg) {
+          const float wk = __shfl_sync(kFull, my_e, 8 * gg + i);
+          const int k = 32 * i + 4 * warp + gg;
+          if (k < npos) {
+#pragma unroll
+            for (int j = 0; j < NV; ++j) {
+              if (lane + 32 * j < kv2) {
+                const float2 v = V[k * kv2 + lane + 32 * j];
+                acc[j].x = fmaf(wk, v.x, acc[j].x);
+                acc[j].y = fmaf(wk, v.y, acc[j].y);
+              }
+            }
+          }
+        }
+      }
+      m_run = m_new;
+    }
+    __syncthreads();  // the tile buffer is reused
+    // each later tile refills the buffer just freed
+    if (tid == 0 && ti + 2 < n_tiles)
+      tile_issue(L, D, tb, h, start + 2 * tile, min(tile, P - start - 2 * tile), &abar[ti & 1], c.apend, ti & 1);
   }
   return ok;
 }
@@ -404,7 +422,7 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
 // rows give this position's k_nope = W_k(latent) + b_k and v = W_v(latent) + b_v, the key row
 // [k_nope | rotated k_rope] and the value row are appended to the head's fp32 cache, and the scaled
 // query (rope pairs rotated) attends over positions 0..P with an online softmax. Cached positions
-// arrive in tiles by bulk copy (double buffered); the caller issues the first tile before this call.
+// arrive in tiles by bulk copy (double buffered); the caller issues the first two tiles before this call.
 // Publishes the head's outputs. `chunk`: the op's stream chunk (the head's kv rows, a GEMV row chunk).
 __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
@@ -423,7 +441,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
   const int tid = threadIdx.x;
   const int Lt = D.latent, nope = D.nope, hd = D.head_dim, kvpad = D.kvpad;
   const int P = static_cast<int>(c.pos);
-  const unsigned char* cst = stream_acquire(p, c.st, chunk);
+  const unsigned char* cst = stream_acquire<kAttnStages>(p, c.st, chunk);
   bool ok = !__syncthreads_or(cst == nullptr);
   if (ok) {
     const AttnSmem A = attn_smem(c.U, D);
@@ -473,23 +491,43 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
       }
     }
     c.tick(1);
-    float l_run;
-    float4 acc;
-    const int kq = kvpad >> 2;
-    ok = kq <= 8    ? attn_tiles<1>(c, p, D, L, A, h, P, l_run, acc)
-         : kq <= 16 ? attn_tiles<2>(c, p, D, L, A, h, P, l_run, acc)
-                    : attn_tiles<4>(c, p, D, L, A, h, P, l_run, acc);
+    float m_run, l_run;
+    float2 acc[2];
+    const int kq = kvpad >> 2, lane = tid & 31, warp = tid >> 5;
+    if (kq <= 8) {
+      float2 a1[1];
+      ok = attn_tiles<1, 1>(c, p, D, L, A, h, P, m_run, l_run, a1);
+      acc[0] = a1[0];
+    } else if (kq <= 16) {
+      float2 a1[1];
+      ok = attn_tiles<2, 1>(c, p, D, L, A, h, P, m_run, l_run, a1);
+      acc[0] = a1[0];
+    } else {
+      ok = attn_tiles<4, 2>(c, p, D, L, A, h, P, m_run, l_run, acc);
+    }
     c.tick(2);
     if (ok) {
-      // the position groups' value sums, added in group order, over the softmax total
-      const int G = kThreads / kq, pg = tid / kq;
-      if (pg < G) reinterpret_cast<float4*>(A.part)[pg * kq + tid % kq] = acc;
+      // the warps' softmax states merged: out = sum_w f_w acc_w / sum_w f_w l_w, f_w = exp(m_w - max m)
+      float* const wm = red + 32;
+      float* const wl = red + 40;
+      if (lane == 0) {
+        wm[warp] = m_run;
+        wl[warp] = l_run;
+      }
+      for (int j = 0; j < 2; ++j)
+        if (lane + 32 * j < (kvpad >> 1) && (j == 0 || kq > 16))
+          reinterpret_cast<float2*>(A.part + warp * kvpad)[lane + 32 * j] = acc[j];
       __syncthreads();
-      const float inv_l = 1.0f / l_run;
+      float M = wm[0];
+      for (int w = 1; w < kWarps; ++w) M = fmaxf(M, wm[w]);
       for (int e = tid; e < hd; e += kThreads) {
-        float s = 0.0f;
-        for (int g = 0; g < G; ++g) s += A.part[g * kvpad + e];
-        stg[e] = s * inv_l;
+        float num = 0.0f, den = 0.0f;
+        for (int w = 0; w < kWarps; ++w) {
+          const float f = wm[w] == -INFINITY ? 0.0f : expf(wm[w] - M);
+          num = fmaf(f, A.part[w * kvpad + e], num);
+          den = fmaf(f, wl[w], den);
+        }
+        stg[e] = num / den;
       }
       __syncthreads();
       ll_put(p.ll + ll_out, h * hd, stg, hd, flag);
@@ -853,7 +891,9 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     mbar_init(&abar[1], 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     st.full = full;
-    st.ring = smem + M.ring;
+    // an attention CTA streams through the ring's last kAttnStages stages; the rest of the ring extends
+    // its attention tiles
+    st.ring = smem + M.ring + (attn_cta ? (kStages - kAttnStages) * M.stage_bytes : 0);
     st.stage_bytes = M.stage_bytes;
     st.caddr = caddr;
     st.cbytes = cbytes;
@@ -895,7 +935,11 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     c.n_groups = (R + D.group - 1) / D.group;
     c.two_level = c.n_groups > 1 && R * c.kp > D.cand_cap;
     c.kq = (min(c.K, D.group * c.kp) + 1) & ~1;
-    for (int k = 0; k < kStages; ++k) stream_issue(p, &st);
+    if (attn_cta) {
+      for (int k = 0; k < kAttnStages; ++k) stream_issue<kAttnStages>(p, &st);
+    } else {
+      for (int k = 0; k < kStages; ++k) stream_issue(p, &st);
+    }
   }
   cp_async_wait_all();
   __syncthreads();
@@ -921,10 +965,13 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
           c.prof_t = c.marks != nullptr ? clock64() : 0;
           mark(c.marks, 0);
         }
-        // the first tile of cached positions (independent of this token) before the input arrives
-        if (tid == 0 && pos > 0)
-          tile_issue(lay, D, tile_buf(attn_smem(c.U, D).tiles, D, 0), h, 0, min(static_cast<int>(pos), D.tile), &abar[0],
-                     c.apend, 0);
+        // the first two tiles of cached positions (independent of this token) before the input arrives
+        if (tid == 0 && pos > 0) {
+          const int np = static_cast<int>(pos);
+          unsigned char* tiles = attn_smem(c.U, D).tiles;
+          tile_issue(lay, D, tile_buf(tiles, D, 0), h, 0, min(np, D.tile), &abar[0], c.apend, 0);
+          if (np > D.tile) tile_issue(lay, D, tile_buf(tiles, D, 1), h, D.tile, min(np - D.tile, D.tile), &abar[1], c.apend, 1);
+        }
         // the rope row of this position (waited for inside), and the head's q, the latent and the
         // head's k_rope from the entry op's output [q | latent | k_rope]
         const float* rrow = lay.rope + static_cast<size_t>(pos) * D.rope;
@@ -945,7 +992,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         cp_async_wait_all();
         ++opk;
         const bool failed = __syncthreads_or(!ok);
-        if (tid == 0) stream_refill(p, &st, chunk + 1);
+        if (tid == 0) stream_refill<kAttnStages>(p, &st, chunk + 1);
         if (failed) alive = false;
       }
       if (tid == 0) {
@@ -1037,12 +1084,13 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     if (rank == 0 && tid == 0) *p.epoch = epoch0 + static_cast<unsigned>(p.steps);
   }
   // let every in-flight copy land before the CTA's shared memory goes away: the descriptor prefetch,
-  // and the ring (at most the last kStages chunks issued can still be in flight)
+  // and the ring (at most the last ns chunks issued can still be in flight)
   cp_async_wait_all();
   if (tid == 0) {
     const unsigned issued = st.issued;
-    for (unsigned k = issued > kStages ? issued - kStages : 0u; k < issued; ++k)
-      if (!mbar_wait_bounded(full + k % kStages, (k / kStages) & 1u, p.timeout_ns)) break;
+    const unsigned ns = attn_cta ? kAttnStages : kStages;
+    for (unsigned k = issued > ns ? issued - ns : 0u; k < issued; ++k)
+      if (!mbar_wait_bounded(full + k % ns, (k / ns) & 1u, p.timeout_ns)) break;
   }
   __syncthreads();
 }
@@ -1430,11 +1478,13 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     op.n_chunks = op.has_norm_chunk + op.has_const + (op.rows_per + cr - 1) / cr;
   }
   // ---- shared memory map ----------------------------------------------------------------------------
+  // [fixed regions][union region][ring of kStages stages]: a GEMV CTA's union region ends where the ring
+  // starts; an attention CTA streams through the ring's last kAttnStages stages only, so its union region
+  // (the attention tiles) runs on through the others
   DecodeSmem& M = dec->sm;
   size_t o = 0;
-  M.ring = 0;
   M.stage_bytes = static_cast<int>(stage);
-  o += kStages * stage;
+  const size_t ring_bytes = kStages * stage, attn_ring_bytes = kAttnStages * stage;
   const int max_in = std::max(std::max(d, F), Lt);  // GEMV inputs, the latent's codes included
   const int pad_in = (max_in + 63) / 64 * 64;
   M.xv = static_cast<int>(o);
@@ -1466,12 +1516,12 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   M.seen = static_cast<int>(o);
   o += r16(static_cast<size_t>(Vper));
   M.u = static_cast<int>(o);
-  if (o >= smem_cap) {
+  if (o + ring_bytes >= smem_cap) {
     why = "the decoder's fixed shared-memory regions exceed a CTA's shared memory";
     return false;
   }
   const int kc = dec->kc;
-  const size_t room = smem_cap - o;  // for the union region
+  const size_t room = smem_cap - o - ring_bytes;  // a GEMV CTA's union region
   // recurrent op: constants, scratch and prefetched state of the CTA's channels
   size_t u_need = r16(static_cast<size_t>(ssm_smem_floats(cpc, S, D.taps)) * 4);
   // head: keys [256] and its candidates [kc]; merges: scratch, then the gathered candidate arrays
@@ -1510,17 +1560,24 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   int tile = 0;
   if (any_mla) {
     // two tile buffers of tile + 1 rows (the last tile also holds the current position)
-    auto attn_bytes = [&](int t) { return attn_fixed_bytes(D.nope, hd, t) + 4 * tile_bytes(t, D.kvpad); };
-    tile = std::min(256, (md.max_len + 15) / 16 * 16);
-    while (tile >= 16 && attn_bytes(tile) > room) tile -= 16;
+    auto attn_bytes = [&](int t) { return attn_fixed_bytes(D.nope, hd) + 4 * tile_bytes(t, D.kvpad); };
+    const size_t attn_room = smem_cap - o - attn_ring_bytes;
+    // at most 240 positions: a tile and the current row then take at most 8 passes of 32 (attn_tiles)
+    tile = std::min(240, (md.max_len + 15) / 16 * 16);
+    while (tile >= 16 && attn_bytes(tile) > attn_room) tile -= 16;
     if (tile < 16) {
       why = "no room for an attention tile in shared memory";
       return false;
     }
-    u_need = std::max(u_need, attn_bytes(tile));
+    // the ring starts late enough for the attention region to end at its last kAttnStages stages
+    const size_t attn_end = o + r16(attn_bytes(tile));
+    const size_t ring_lo = attn_end > (ring_bytes - attn_ring_bytes) ? attn_end - (ring_bytes - attn_ring_bytes) : 0;
+    u_need = std::max(u_need, r16(ring_lo > o ? ring_lo - o : 0));
   }
   D.tile = std::max(tile, 16);
   o += r16(u_need);
+  M.ring = static_cast<int>(o);
+  o += ring_bytes;
   M.total = static_cast<int>(o);
   if (o > smem_cap) {
     why = "the decoder needs more shared memory than a CTA has";

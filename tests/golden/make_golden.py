@@ -18,7 +18,9 @@ It imports LuisOezdem/ivonar-inference unmodified and records, on seeded synthet
                   (decoder.py:324-333)
   model_*.npz     whole-model runs: torch StaticDecoder (fp32) prefill logits and 256-token greedy and
                   penalised-greedy streams (config 0 and tiny: the penalised stream's per-step logits),
-                  numba CpuDecoder greedy streams (from the torch prefill, and stepped through the prompt)
+                  numba CpuDecoder greedy streams (from the torch prefill, and stepped through the prompt);
+                  config 1 also the reference's own spread: per-step mean and max |torch - numba| of the
+                  logits, both decoders teacher-forced along the torch greedy stream (ref_spread_*)
 Everything is generated from this repository's synthetic models (ivonar_inference_b200.synthetic),
 whose state dicts the reference loader reads as-is.
 """
@@ -224,7 +226,39 @@ def model_run(ref, payload: dict, seed: int, style: str, prompt_len: int, steps:
     return out, model
 
 
+def spread_run(ref, payload: dict, seed: int, style: str, data: dict, max_len: int) -> dict:
+    """The reference's own fp32 spread on a model: its torch StaticDecoder and numba CpuDecoder
+    prefill the same prompt and are teacher-forced along the torch greedy stream; per step the mean and
+    max |logit difference|."""
+    cpu, ModelConfig, StaticDecoder, build_model, materialize_weights, _ = ref
+    state = synthetic.synthetic_state(payload, seed, style)
+    model = build_model(ModelConfig.from_payload(payload), state).eval()
+    materialize_weights(model, torch.float32)
+    prompt = torch.from_numpy(data["prompt"]).view(1, -1)
+    dec = StaticDecoder(model, max_len=max_len, device="cpu", sampling=True)
+    cdec = cpu.CpuDecoder(model, max_len=max_len, sampling=True)
+    dec.prefill(prompt)
+    cdec.prefill(prompt)
+    means, maxes = [], []
+    for tok in data["torch_greedy"][:-1]:
+        a = dec.step(torch.tensor([int(tok)]))[0].numpy()
+        b = cdec.step(torch.tensor([int(tok)]))[0].numpy()
+        d = np.abs(a - b)
+        means.append(d.mean())
+        maxes.append(d.max())
+    return {"ref_spread_mean": np.array(means, np.float32), "ref_spread_max": np.array(maxes, np.float32)}
+
+
 def main() -> None:
+    if "--spread-only" in sys.argv:
+        # add the spread arrays to an existing config-1 fixture (its other arrays stay as they are)
+        ref = _reference()
+        path = OUT / "model_config1.npz"
+        data = dict(np.load(path))
+        data.update(spread_run(ref, synthetic.config1(seq_len=2048), 0, "baseline", data, 320))
+        np.savez_compressed(path, **data)
+        print(f"{path.name}: {path.stat().st_size} bytes")
+        return
     ref = _reference()
     cpu, ModelConfig, StaticDecoder, build_model, materialize_weights, TernaryLinear = ref
     np.savez_compressed(OUT / "quantizer.npz", **quantizer_vectors(cpu))
@@ -239,6 +273,7 @@ def main() -> None:
     np.savez_compressed(OUT / "model_tiny.npz", seq_len=np.int64(STREAM_CONTEXT), **data)
     if "--no-nano" not in sys.argv:
         data, _ = model_run(ref, synthetic.config1(seq_len=2048), 0, "baseline", 36, STREAM, False, True)
+        data.update(spread_run(ref, synthetic.config1(seq_len=2048), 0, "baseline", data, 320))
         np.savez_compressed(OUT / "model_config1.npz", seq_len=np.int64(2048), **data)
     for path in sorted(OUT.glob("*.npz")):
         print(f"{path.name}: {path.stat().st_size} bytes")

@@ -118,9 +118,14 @@ def test_nano_decoder_matches_the_oracle(oracle_lib) -> None:
         maxes.append(float(d.max()))
         means.append(float(d.mean()))
     print(f"nano teacher-forced: worst max {max(maxes):.3f}, worst mean {max(means):.4f}, average mean {np.mean(means):.4f}")
-    assert max(maxes) < 0.4 and max(means) < 0.05, (max(maxes), max(means))
-    # over the whole stream the typical step sits inside the reference's own mean spread (0.033-0.048)
-    assert float(np.mean(means)) < 0.045, float(np.mean(means))
+    # the bar is the reference's own spread along this stream: its torch and numba decoders, teacher-forced
+    # the same way, differ per step by 0.0366 mean |dlogit| on average, 0.0463 at the worst step and 0.29
+    # at the worst logit (ref_spread_*). The typical step must sit within it; the worst of 255 noisy steps
+    # within a quarter (mean) and a half (single logit) of the reference's worst
+    spread_mean, spread_max = g["ref_spread_mean"], g["ref_spread_max"]
+    assert float(np.mean(means)) < 1.1 * float(spread_mean.mean()), (float(np.mean(means)), float(spread_mean.mean()))
+    assert max(means) < 1.25 * float(spread_mean.max()), (max(means), float(spread_mean.max()))
+    assert max(maxes) < 1.5 * float(spread_max.max()), (max(maxes), float(spread_max.max()))
     # free-running greedy on the GPU; the oracle follows the GPU's tokens to price the first split
     dec.prefill(prompt)
     dec.configure_sampling(1.0, 1, 1.0)
