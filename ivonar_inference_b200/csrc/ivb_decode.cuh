@@ -63,6 +63,7 @@ struct DecodeDims {
   int32_t cpc;                     // recurrent channels per GEMV CTA (hidden / R, within one head)
   int32_t A;                       // attention CTAs (heads, or 0 without attention blocks)
   int32_t taps;                    // conv taps
+  int32_t ssm_v16, ssm_lg_cs;      // recurrent state prefetch: one 16-byte copy per thread; log2(cpc / 2)
   int32_t lpad, rpad;              // latent cache row stride (bytes), k_rope cache row stride (halves)
   int32_t kvpad;                   // key / value cache row stride (floats): head_dim rounded up to 4
   int32_t rb_lat, ss_lat;          // row bytes / scale stride of latent-input matrices
@@ -76,7 +77,7 @@ struct DecodeDims {
 // Shared-memory map (byte offsets from the dynamic shared memory base).
 struct DecodeSmem {
   int32_t ring, stage_bytes;
-  int32_t xv, act, xsum, resid, pub, pub_n, loc, red, xl;  // xl: the attention op's gathered [q_h | latent | k_rope_h]
+  int32_t act, xsum, resid, pub, pub_n, loc, red, xl;  // xl: the attention op's gathered [q_h | latent | k_rope_h]
   int32_t ctab;                    // chunk table of the CTA: [cpt] u64 addresses, then [cpt] u32 sizes
   int32_t cand;                    // offset inside the union region of the gathered candidate arrays (keys, ids)
   int32_t rope_row;                // rope (cos, sin) row of the current position, prefetched by the mla entry op

@@ -228,13 +228,14 @@ struct Ctx {
   Stream* st;
   unsigned chunk_base;  // stream chunks consumed by the tokens before this one
   unsigned rank;
-  float *xv, *resid, *loc, *red, *xl, *stg, *rope_s, *seen_s;
+  float *resid, *loc, *red, *xl, *stg, *rope_s, *seen_s;
   int8_t* act;
   int* xsum;
   unsigned char* U;
   unsigned long long* abar;
   unsigned apar[2];     // phase parities of the two attention tile barriers (flipped by thread 0)
   unsigned apend;       // bit b: a copy into tile buffer b was issued and not yet waited for (thread 0)
+  int ssm_row0;         // GEMV CTA: (head * state_dim) * head_dim + first channel in the head (recurrent state rows)
   long long pos;
   unsigned flag;
   int K, kp, kq, n_groups;
@@ -547,6 +548,8 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
 // ssmc: [decay S | theta S | skip cpc | conv w cpc*taps | conv b cpc] from the constants chunk, then
 // scratch [coef 5S | vals cpc | cpart cpc*S], then the prefetched state [cpc per state: S x cpc x 2 |
 // S x cpc prev force | cpc x (taps - 1) conv window].
+// float offset of the prefetched state in that region
+__host__ __device__ __forceinline__ int ssm_state_off(int cpc, int S, int taps) { return 7 * S + cpc * (3 + taps) + cpc * S; }
 __host__ __device__ __forceinline__ int ssm_smem_floats(int cpc, int S, int taps) {
   return 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S + 3 * S * cpc + cpc * (taps - 1);
 }
@@ -616,7 +619,19 @@ __device__ __forceinline__ void ssm_step(Ctx& c, const Op& op, const IvbLayerDes
   __syncthreads();
   for (int cl = tid; cl < cpc; cl += kThreads) {
     float contrib = 0.0f;
-    for (int s2 = 0; s2 < S; ++s2) contrib += cpart[cl * S + s2];
+    const float* cp = cpart + cl * S;
+    if ((S & 3) == 0 && (reinterpret_cast<uintptr_t>(cp) & 15) == 0) {
+#pragma unroll 4
+      for (int s4 = 0; s4 < S; s4 += 4) {  // independent 16-byte loads; the sum stays in state order
+        const float4 v = *reinterpret_cast<const float4*>(cp + s4);
+        contrib += v.x;
+        contrib += v.y;
+        contrib += v.z;
+        contrib += v.w;
+      }
+    } else {
+      for (int s2 = 0; s2 < S; ++s2) contrib += cp[s2];
+    }
     stg[cl] = (contrib + skip[cl] * vals[cl]) * sigmoid_f(rows_out[cpc + cl]);
   }
   __syncthreads();
@@ -671,23 +686,51 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
   } else if (op.kind == OP_ENTRY_MAMBA) {
     // the recurrent state of my channels streams into shared memory while the rows are computed:
     // per state s the cpc complex values and previous forces of my channels, then the conv windows
-    const int hd = D.head_dim, ch0 = c.rank * cpc, h = ch0 / hd, dd0 = ch0 - h * hd;
-    float* dst = ssmc + 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S;
-    const int l0 = 2 * S * cpc, l1 = S * cpc, l2 = cpc * (taps - 1);
-    for (int i = tid; i < l0 + l1 + l2; i += kThreads) {
-      const float* src;
-      if (i < l0) {
-        const int s2 = i / (2 * cpc), r = i - s2 * 2 * cpc;
-        src = lay.ssm_state + (static_cast<size_t>(h * S + s2) * hd + dd0) * 2 + r;
-      } else if (i < l0 + l1) {
-        const int s2 = (i - l0) / cpc, r = (i - l0) - s2 * cpc;
-        src = lay.prev_force + static_cast<size_t>(h * S + s2) * hd + dd0 + r;
-      } else {
-        src = lay.conv_state + static_cast<size_t>(ch0) * (taps - 1) + (i - l0 - l1);
+    const int hd = D.head_dim, ch0 = c.rank * cpc;
+    float* dst = ssmc + ssm_state_off(cpc, S, taps);
+    if (D.ssm_v16) {
+      // one 16-byte copy per thread, indices by shifts: per state cpc / 2 chunks of complex values and
+      // cpc / 4 of previous forces, then the conv windows (every piece 16-byte aligned, checked on the host)
+      const int lg = D.ssm_lg_cs, cs = 1 << lg, n0 = S << lg, n1 = S << (lg - 1), n2 = (cpc * (taps - 1)) >> 2;
+      const int row0 = c.ssm_row0;
+      const int j = tid;
+      if (j < n0 + n1 + n2) {
+        const float* src;
+        float* d2;
+        if (j < n0) {
+          const int s2 = j >> lg, r = j & (cs - 1);
+          src = lay.ssm_state + static_cast<size_t>(row0 + s2 * hd) * 2 + 4 * r;
+          d2 = dst + 2 * cpc * s2 + 4 * r;
+        } else if (j < n0 + n1) {
+          const int jj = j - n0, s2 = jj >> (lg - 1), r = jj & ((cs >> 1) - 1);
+          src = lay.prev_force + static_cast<size_t>(row0 + s2 * hd) + 4 * r;
+          d2 = dst + 2 * S * cpc + cpc * s2 + 4 * r;
+        } else {
+          const int jj = j - n0 - n1;
+          src = lay.conv_state + static_cast<size_t>(ch0) * (taps - 1) + 4 * jj;
+          d2 = dst + 3 * S * cpc + 4 * jj;
+        }
+        cp_async_16(d2, src);
       }
-      cp_async_f32(dst + i, src);
+      cp_async_commit();
+    } else {
+      const int h = ch0 / hd, dd0 = ch0 - h * hd;
+      const int l0 = 2 * S * cpc, l1 = S * cpc, l2 = cpc * (taps - 1);
+      for (int i = tid; i < l0 + l1 + l2; i += kThreads) {
+        const float* src;
+        if (i < l0) {
+          const int s2 = i / (2 * cpc), r = i - s2 * 2 * cpc;
+          src = lay.ssm_state + (static_cast<size_t>(h * S + s2) * hd + dd0) * 2 + r;
+        } else if (i < l0 + l1) {
+          const int s2 = (i - l0) / cpc, r = (i - l0) - s2 * cpc;
+          src = lay.prev_force + static_cast<size_t>(h * S + s2) * hd + dd0 + r;
+        } else {
+          src = lay.conv_state + static_cast<size_t>(ch0) * (taps - 1) + (i - l0 - l1);
+        }
+        cp_async_f32(dst + i, src);
+      }
+      cp_async_commit();
     }
-    cp_async_commit();
   }
   c.tick(0);
   // the input: the previous op's output gathered from its flag words (or the embedding / combined
@@ -698,7 +741,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
     if (nrm == nullptr) ok = false;
   }
   const bool from_smem = op.ll_in < 0;
-  float* keep = op.in_dst == IN_RESID ? c.resid : c.xv;
+  float* keep = op.in_dst == IN_RESID ? c.resid : nullptr;  // the residual replica; other inputs live in registers only
   long long* t_arr = c.marks != nullptr ? &c.prof_t2 : nullptr;
   const unsigned long long* src = from_smem ? nullptr : p.ll + op.ll_in;
   const float* nw = op.has_norm ? reinterpret_cast<const float*>(nrm) : nullptr;
@@ -906,7 +949,6 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     c.st = &st;
     c.chunk_base = 0u;
     c.rank = rank;
-    c.xv = reinterpret_cast<float*>(smem + M.xv);
     c.resid = reinterpret_cast<float*>(smem + M.resid);
     c.loc = reinterpret_cast<float*>(smem + M.loc);
     c.red = reinterpret_cast<float*>(smem + M.red);
@@ -920,6 +962,10 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     c.abar = abar;
     c.apar[0] = c.apar[1] = 0u;
     c.apend = 0u;
+    {
+      const int ch0 = static_cast<int>(rank) * D.cpc, h = ch0 / D.head_dim;
+      c.ssm_row0 = h * D.state_dim * D.head_dim + (ch0 - h * D.head_dim);
+    }
     c.marks = nullptr;
     c.pos = ldcg_i64(p.position);
     c.inv_t = 1.0f / __ldcg(p.sampling);
@@ -1288,6 +1334,17 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
     return false;
   }
   D.cpc = d / R;
+  // the recurrent state of a CTA's channels arrives by one 16-byte copy per thread when cpc is a power
+  // of two of at least 4 and every piece is 16-byte aligned
+  {
+    int lg = 0;
+    while ((2 << lg) < D.cpc) ++lg;  // cpc / 2 = 2^lg
+    const int S = md.state_dim, taps = D.taps;
+    const bool pow2 = D.cpc >= 4 && (2 << lg) == D.cpc;
+    D.ssm_lg_cs = lg;
+    D.ssm_v16 = pow2 && md.head_dim % 4 == 0 && (D.cpc * (taps - 1)) % 4 == 0 && ssm_state_off(D.cpc, S, taps) % 4 == 0 &&
+                (S << lg) + (S << (lg - 1)) + (D.cpc * (taps - 1)) / 4 <= kThreads;
+  }
   D.A = 0;
   for (const IvbLayerDesc& L : dec->layers)
     if (L.kind == IVB_MLA) D.A = H;
@@ -1487,8 +1544,6 @@ static bool plan(IvbDecoder* dec, int R, size_t smem_cap, std::string& why) {
   const size_t ring_bytes = kStages * stage, attn_ring_bytes = kAttnStages * stage;
   const int max_in = std::max(std::max(d, F), Lt);  // GEMV inputs, the latent's codes included
   const int pad_in = (max_in + 63) / 64 * 64;
-  M.xv = static_cast<int>(o);
-  o += r16(static_cast<size_t>(pad_in) * 4);
   M.act = static_cast<int>(o);
   o += r16(pad_in);
   M.xsum = static_cast<int>(o);
