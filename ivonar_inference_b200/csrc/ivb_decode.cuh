@@ -248,25 +248,41 @@ __device__ __forceinline__ int chunks_of_step(const DecodeParams& p, const Strea
   return head_needed(p, step) ? s->cpt : s->head_first;
 }
 
-// thread 0 only: queue the next chunk of this CTA's stream into the next of its NS ring stages
+// thread 0 only, after a CTA barrier that follows the last read of the freed stages (chunks below
+// `consumed` are no longer read): queue the chunks of this CTA's stream that follow, into its NS ring stages in turn,
+// until `consumed + NS` chunks are issued or the run's steps are exhausted. The cursor and the stream's
+// constants are read from shared memory once and kept in registers while the copies are issued (a
+// chain of dependent shared-memory accesses per chunk would put hundreds of cycles between an op's end
+// and the next op's gather on the CTA that finishes last).
 template <int NS = kStages>
-__device__ __forceinline__ void stream_issue(const DecodeParams& p, Stream* s) {
-  if (s->p_step >= p.steps) return;
-  if (s->p_chunk == s->head_first && !head_needed(p, s->p_step)) {
-    s->p_chunk = 0;
-    if (++s->p_step >= p.steps) return;
+__device__ __forceinline__ void stream_refill(const DecodeParams& p, Stream* s, unsigned consumed) {
+  unsigned issued = s->issued;
+  int p_step = s->p_step, p_chunk = s->p_chunk;
+  const int steps = p.steps;
+  if (issued >= consumed + NS || p_step >= steps) return;
+  const int cpt = s->cpt, head_first = s->head_first, stage_bytes = s->stage_bytes;
+  unsigned long long* const full = s->full;
+  unsigned char* const ring = s->ring;
+  const unsigned long long* const caddr = s->caddr;
+  const unsigned* const cbytes = s->cbytes;
+  while (issued < consumed + NS && p_step < steps) {
+    if (p_chunk == head_first && !head_needed(p, p_step)) {  // a token without a head skips its chunks
+      p_chunk = 0;
+      if (++p_step >= steps) break;
+    }
+    const unsigned bytes = cbytes[p_chunk];
+    const int stage = static_cast<int>(issued % NS);
+    mbar_expect_tx(full + stage, bytes);  // the stage is only ever written by the copy engine: no proxy fence
+    bulk_copy(ring + static_cast<size_t>(stage) * stage_bytes, reinterpret_cast<const void*>(caddr[p_chunk]), bytes, full + stage);
+    ++issued;
+    if (++p_chunk == cpt) {
+      p_chunk = 0;
+      ++p_step;
+    }
   }
-  const unsigned bytes = s->cbytes[s->p_chunk];
-  const int stage = s->issued % NS;
-  unsigned long long* bar = s->full + stage;
-  mbar_expect_tx(bar, bytes);  // the stage is only ever written by the copy engine: no proxy fence
-  bulk_copy(s->ring + static_cast<size_t>(stage) * s->stage_bytes, reinterpret_cast<const void*>(s->caddr[s->p_chunk]), bytes,
-            bar);
-  ++s->issued;
-  if (++s->p_chunk == s->cpt) {
-    s->p_chunk = 0;
-    ++s->p_step;
-  }
+  s->issued = issued;
+  s->p_step = p_step;
+  s->p_chunk = p_chunk;
 }
 
 // Bounded wait on an mbarrier phase by one thread; true when the phase completed.
@@ -294,12 +310,6 @@ __device__ __forceinline__ const unsigned char* stream_acquire(const DecodeParam
   return s->ring + static_cast<size_t>(stage) * s->stage_bytes;
 }
 
-// thread 0, after a CTA barrier that follows the last read of the stages: refill every stage freed
-// since the last call (chunks below `consumed` are no longer read), keeping the ring full.
-template <int NS = kStages>
-__device__ __forceinline__ void stream_refill(const DecodeParams& p, Stream* s, unsigned consumed) {
-  while (s->issued < consumed + NS && s->p_step < p.steps) stream_issue<NS>(p, s);
-}
 
 // ---- GEMV rows from a ring stage ----------------------------------------------------------------
 // dp4a with unsigned weight bytes and signed activation bytes.

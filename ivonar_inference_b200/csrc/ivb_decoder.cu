@@ -257,6 +257,13 @@ struct Ctx {
   }
 };
 
+// The kernel is compiled twice: with kTrace the op routines record their per-part cycle counts (the
+// per-op device timeline of ivb_decoder_trace); without it they contain no tracing code at all.
+template <bool kTrace>
+__device__ __forceinline__ void tick(Ctx& c, int part) {
+  if constexpr (kTrace) c.tick(part);
+}
+
 // Shared-memory layout of the attention op inside the union region (the plan sizes it the same way):
 // kv rows of this position [nope + head_dim] | scaled query, rope pairs rotated [kvpad] | this
 // position's key row [kvpad] | the warps' value sums [4 * kThreads] | 16-byte aligned double tile
@@ -425,6 +432,7 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
 // query (rope pairs rotated) attends over positions 0..P with an online softmax. Cached positions
 // arrive in tiles by bulk copy (double buffered); the caller issues the first two tiles before this call.
 // Publishes the head's outputs. `chunk`: the op's stream chunk (the head's kv rows, a GEMV row chunk).
+template <bool kTrace>
 __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
   // the context, the op record and the parameters also live, so reads through them would repeat
@@ -457,7 +465,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
     if (tid == 0) lat_s[P] = a_cur;
     cp_async_wait_all();  // the rope row of this position
     __syncthreads();
-    c.tick(0);
+    tick<kTrace>(c, 0);
     // k_nope and v of this position: the head's kv up-projection rows against the codes
     rows_decode(cst, kv_rows, kv_rb, kv_ss, 1, a_cur, c.act, c.xsum, Lt, kv_lg, A.kv, EPI_STORE, nullptr, nullptr, flag);
     // the scaled query (rope pairs rotated) and the rope part of this position's key (rotated, rounded
@@ -491,7 +499,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
         v_cache[row + e] = e < hd ? A.kv[nope + e] : 0.0f;
       }
     }
-    c.tick(1);
+    tick<kTrace>(c, 1);
     float m_run, l_run;
     float2 acc[2];
     const int kq = kvpad >> 2, lane = tid & 31, warp = tid >> 5;
@@ -506,7 +514,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
     } else {
       ok = attn_tiles<4, 2>(c, p, D, L, A, h, P, m_run, l_run, acc);
     }
-    c.tick(2);
+    tick<kTrace>(c, 2);
     if (ok) {
       // the warps' softmax states merged: out = sum_w f_w acc_w / sum_w f_w l_w, f_w = exp(m_w - max m)
       float* const wm = red + 32;
@@ -532,7 +540,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
       }
       __syncthreads();
       ll_put(p.ll + ll_out, h * hd, stg, hd, flag);
-      c.tick(3);
+      tick<kTrace>(c, 3);
     }
   }
   asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -661,6 +669,7 @@ static __device__ __noinline__ void topk_by_rank(const unsigned* keys, int n, in
 // epilogue, the gathered and (normed) quantised input, its rows chunk by chunk from the weight ring,
 // and the epilogue (publish the output slice, residual add, SwiGLU, the recurrent step, or the head's
 // logits and local top-k candidates).
+template <bool kTrace>
 __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDesc& lay, int rows_c) {
   // the op record, the dimensions and the context fields used below are read once into registers (the
   // op stores to shared memory, where all three live)
@@ -732,7 +741,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
       cp_async_commit();
     }
   }
-  c.tick(0);
+  tick<kTrace>(c, 0);
   // the input: the previous op's output gathered from its flag words (or the embedding / combined
   // attention already in shared memory), normed with the weights of its own stream chunk, quantised
   const unsigned char* nrm = nullptr;
@@ -742,7 +751,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
   }
   const bool from_smem = op.ll_in < 0;
   float* keep = op.in_dst == IN_RESID ? c.resid : nullptr;  // the residual replica; other inputs live in registers only
-  long long* t_arr = c.marks != nullptr ? &c.prof_t2 : nullptr;
+  long long* t_arr = kTrace && c.marks != nullptr ? &c.prof_t2 : nullptr;
   const unsigned long long* src = from_smem ? nullptr : p.ll + op.ll_in;
   const float* nw = op.has_norm ? reinterpret_cast<const float*>(nrm) : nullptr;
   const float act_scale =
@@ -751,7 +760,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
           : gather_quantize_reg<kMaxEPT>(src, op.in_n, flag, keep, nw, op.norm_eps, D.clip, D.act_eps, c.act, c.xsum, c.red, p.timeout_ns,
                                          t_arr);
   if (act_scale < 0.0f) ok = false;
-  if (tid == 0 && c.marks != nullptr && !from_smem) {  // split the wait for the input from the quantiser
+  if (kTrace && tid == 0 && c.marks != nullptr && !from_smem) {  // split the wait for the input from the quantiser
     c.prof[1] += c.prof_t2 - c.prof_t;
     c.prof_t = c.prof_t2;
   }
@@ -759,7 +768,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
     cst = stream_acquire(p, st, idx++);
     if (cst == nullptr) ok = false;
   }
-  c.tick(2);
+  tick<kTrace>(c, 2);
   // SSM constants leave the stage before it is recycled
   if (op.kind == OP_ENTRY_MAMBA && cst != nullptr) {
     const int e0 = S, e1 = 2 * S, e2 = e1 + cpc, e3 = e2 + cpc * taps, e4 = e3 + cpc;
@@ -794,7 +803,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
     }
   }
   if (epi == EPI_STORE) __syncthreads();  // every row of this CTA is in rows_out
-  c.tick(3);
+  tick<kTrace>(c, 3);
   float* stg = c.stg;
   // epilogues that need every row of the CTA
   if (op.kind == OP_GATE_UP && epi == EPI_STORE) {
@@ -826,7 +835,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
     __syncthreads();
     ssm_step(c, opr, lay, rows_out, ssmc);
   }
-  c.tick(4);
+  tick<kTrace>(c, 4);
   if (!ok) atomicCAS(p.error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
   return ok;
 }
@@ -886,6 +895,7 @@ static __device__ __noinline__ int draw_next(Ctx& c, uint64_t rkey, uint64_t rct
   return draw_token(sk, si, kk, cdf, c.red, rkey, rctr);
 }
 
+template <bool kTrace>
 __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_constant__ DecodeParams p) {
   extern __shared__ __align__(128) unsigned char smem[];
   __shared__ __align__(8) unsigned long long full[kStages];
@@ -981,11 +991,8 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
     c.n_groups = (R + D.group - 1) / D.group;
     c.two_level = c.n_groups > 1 && R * c.kp > D.cand_cap;
     c.kq = (min(c.K, D.group * c.kp) + 1) & ~1;
-    if (attn_cta) {
-      for (int k = 0; k < kAttnStages; ++k) stream_issue<kAttnStages>(p, &st);
-    } else {
-      for (int k = 0; k < kStages; ++k) stream_issue(p, &st);
-    }
+    if (attn_cta) stream_refill<kAttnStages>(p, &st, 0u);
+    else stream_refill(p, &st, 0u);
   }
   cp_async_wait_all();
   __syncthreads();
@@ -1005,7 +1012,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         const Op& op = opbuf[opk & 1].op;
         const IvbLayerDesc& lay = opbuf[opk & 1].layer;
         fetch_op(p.attn_ops[mi + 1 < p.n_mla ? mi + 1 : 0], (opk + 1) & 1);
-        if (tid == 0) {
+        if (kTrace && tid == 0) {
           c.marks = tracing ? p.trace + (static_cast<size_t>(oi) * (R + D.A) + rank) * 8 : nullptr;
           for (int k = 0; k < 6; ++k) c.prof[k] = 0;
           c.prof_t = c.marks != nullptr ? clock64() : 0;
@@ -1026,11 +1033,11 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         const unsigned long long* src = p.ll + op.ll_in;
         bool ok = ll_gather3(src + h * D.head_dim, D.head_dim, src + D.hidden, D.latent, src + D.hidden + D.latent + h * D.rope,
                              D.rope, flag, reinterpret_cast<unsigned*>(c.xl), p.timeout_ns);
-        c.tick(5);
+        tick<kTrace>(c, 5);
         const unsigned chunk = c.chunk_base + static_cast<unsigned>(mi);
-        if (ok) ok = op_attention(c, op, lay, h, chunk);
+        if (ok) ok = op_attention<kTrace>(c, op, lay, h, chunk);
         else c.fail(IVB_ETIMEOUT);
-        if (tid == 0 && c.marks != nullptr) {
+        if (kTrace && tid == 0 && c.marks != nullptr) {
           for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
           mark(c.marks, 7);
         }
@@ -1075,7 +1082,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         const IvbLayerDesc& lay = opbuf[opk & 1].layer;
         const int rows_c = rowsbuf[opk & 1][0];
         fetch_op(oi + 1 < n_run ? oi + 1 : 0, (opk + 1) & 1);  // the op after this one (op 0 of the next token)
-        if (tid == 0) {
+        if (kTrace && tid == 0) {
           c.marks = tracing && op.kind != OP_ATTN ? p.trace + (static_cast<size_t>(oi) * (R + D.A) + rank) * 8 : nullptr;
           for (int k = 0; k < 6; ++k) c.prof[k] = 0;
           c.prof_t = c.marks != nullptr ? clock64() : 0;
@@ -1085,10 +1092,10 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         if (op.kind == OP_MERGE) {
           ok = op_merge(c, op);
         } else if (op.kind != OP_ATTN) {  // the attention CTAs run the attention ops
-          ok = op_gemv(c, op, lay, rows_c);
+          ok = op_gemv<kTrace>(c, op, lay, rows_c);
         }
-        c.tick(5);
-        if (tid == 0 && c.marks != nullptr) {
+        tick<kTrace>(c, 5);
+        if (kTrace && tid == 0 && c.marks != nullptr) {
           for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
           mark(c.marks, 7);
         }
@@ -1888,9 +1895,12 @@ int32_t ivb_decoder_create(const IvbModelDesc* desc, int32_t ctas, IvbDecoder** 
       if (why == "no CTA count fits") why = w;
       continue;
     }
-    IVB_CUDA(cudaFuncSetAttribute(grid_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
-    int per_sm = 0;
-    IVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_decode_kernel, kThreads, dec->smem));
+    IVB_CUDA(cudaFuncSetAttribute(grid_decode_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
+    IVB_CUDA(cudaFuncSetAttribute(grid_decode_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(dec->smem)));
+    int per_sm = 0, per_sm_trace = 0;
+    IVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, grid_decode_kernel<false>, kThreads, dec->smem));
+    IVB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_trace, grid_decode_kernel<true>, kThreads, dec->smem));
+    per_sm = std::min(per_sm, per_sm_trace);
     if (per_sm < 1 || per_sm * sms < R + dec->A) {
       why = "the device cannot hold every CTA of the decode kernel at once";
       continue;
@@ -2048,7 +2058,7 @@ int32_t ivb_decoder_run(IvbDecoder* dec, int32_t steps, const int64_t* feed, int
   at[0].val.cooperative = 1;
   cfg.attrs = at;
   cfg.numAttrs = 1;
-  IVB_CUDA(cudaLaunchKernelEx(&cfg, grid_decode_kernel, p));
+  IVB_CUDA(cudaLaunchKernelEx(&cfg, p.trace != nullptr ? grid_decode_kernel<true> : grid_decode_kernel<false>, p));
   return IVB_OK;
 }
 
