@@ -229,6 +229,15 @@ __device__ __forceinline__ bool ll_gather(const unsigned long long* buf, int n, 
 // Lives in shared memory. The producer cursor (issued, p_step, p_chunk) belongs to thread 0; the
 // consumers address chunk number `idx` of the run (every thread knows it: the chunks consumed by
 // earlier tokens plus the op's first chunk), so no per-thread counter travels between routines.
+// What a consumer of the stream needs, held by value (registers or rematerialised constants) so that
+// acquiring a chunk does not first chase pointers through shared memory.
+struct RingView {
+  unsigned long long* full;  // the ring's mbarriers
+  unsigned char* ring;       // its first stage
+  int stage_bytes;
+  unsigned long long timeout_ns;
+};
+
 struct Stream {
   unsigned long long* full;  // [NS] mbarriers
   unsigned char* ring;
@@ -303,11 +312,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(unsigned long long* bar, unsig
 // mbarrier wait makes the copied bytes visible to it; no CTA barrier). Returns the stage base, or
 // nullptr when this thread's bounded wait ran out (the op reports it after its closing barrier).
 template <int NS = kStages>
-__device__ __forceinline__ const unsigned char* stream_acquire(const DecodeParams& p, const Stream* s, unsigned idx) {
+__device__ __forceinline__ const unsigned char* stream_acquire(const RingView& v, unsigned idx) {
   const int stage = idx % NS;
   const unsigned parity = (idx / NS) & 1u;
-  if (!mbar_wait_bounded(s->full + stage, parity, p.timeout_ns)) return nullptr;
-  return s->ring + static_cast<size_t>(stage) * s->stage_bytes;
+  if (!mbar_wait_bounded(v.full + stage, parity, v.timeout_ns)) return nullptr;
+  return v.ring + static_cast<size_t>(stage) * v.stage_bytes;
 }
 
 

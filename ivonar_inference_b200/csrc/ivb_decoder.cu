@@ -433,10 +433,10 @@ __device__ __forceinline__ bool attn_tiles(Ctx& c, const DecodeParams& p, const 
 // arrive in tiles by bulk copy (double buffered); the caller issues the first two tiles before this call.
 // Publishes the head's outputs. `chunk`: the op's stream chunk (the head's kv rows, a GEMV row chunk).
 template <bool kTrace>
-__device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLayerDesc& L, int h, unsigned chunk) {
+__device__ __forceinline__ bool op_attention(Ctx& c, const DecodeParams& p, const RingView& rv, const Op& opr, const IvbLayerDesc& L, int h,
+                                             unsigned chunk) {
   // every field used in a loop is read once into a register: the loops store to shared memory, where
-  // the context, the op record and the parameters also live, so reads through them would repeat
-  const DecodeParams& p = *c.p;
+  // the context and the op record live, so reads through them would repeat
   const DecodeDims D = p.d;
   const int ll_out = opr.ll_out, kv_rows = opr.rows_per, kv_rb = opr.row_bytes, kv_ss = opr.scale_stride, kv_lg = opr.lpr_log;
   int8_t* const lat_q = L.latent_q;
@@ -450,7 +450,7 @@ __device__ __forceinline__ bool op_attention(Ctx& c, const Op& opr, const IvbLay
   const int tid = threadIdx.x;
   const int Lt = D.latent, nope = D.nope, hd = D.head_dim, kvpad = D.kvpad;
   const int P = static_cast<int>(c.pos);
-  const unsigned char* cst = stream_acquire<kAttnStages>(p, c.st, chunk);
+  const unsigned char* cst = stream_acquire<kAttnStages>(rv, chunk);
   bool ok = !__syncthreads_or(cst == nullptr);
   if (ok) {
     const AttnSmem A = attn_smem(c.U, D);
@@ -561,8 +561,8 @@ __host__ __device__ __forceinline__ int ssm_state_off(int cpc, int S, int taps) 
 __host__ __device__ __forceinline__ int ssm_smem_floats(int cpc, int S, int taps) {
   return 2 * S + cpc * (2 + taps) + 5 * S + cpc + cpc * S + 3 * S * cpc + cpc * (taps - 1);
 }
-__device__ __forceinline__ void ssm_step(Ctx& c, const Op& op, const IvbLayerDesc& L, const float* rows_out, float* ssmc) {
-  const DecodeParams& p = *c.p;
+__device__ __forceinline__ void ssm_step(Ctx& c, const DecodeParams& p, const Op& op, const IvbLayerDesc& L, const float* rows_out,
+                                         float* ssmc) {
   const DecodeDims D = p.d;  // registers: the loops below store to shared memory, where p lives
   const int tid = threadIdx.x;
   const int S = D.state_dim, hd = D.head_dim, taps = D.taps, cpc = D.cpc;
@@ -670,12 +670,11 @@ static __device__ __noinline__ void topk_by_rank(const unsigned* keys, int n, in
 // and the epilogue (publish the output slice, residual add, SwiGLU, the recurrent step, or the head's
 // logits and local top-k candidates).
 template <bool kTrace>
-__device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDesc& lay, int rows_c) {
+__device__ __forceinline__ bool op_gemv(Ctx& c, const DecodeParams& p, const RingView& rv, const Op& opr, const IvbLayerDesc& lay,
+                                        int rows_c) {
   // the op record, the dimensions and the context fields used below are read once into registers (the
   // op stores to shared memory, where all three live)
-  const DecodeParams& p = *c.p;
   const Op op = opr;
-  Stream* st = c.st;
   unsigned idx = c.chunk_base + op.first_chunk;  // the op's chunks: [norm] [constants] rows...
   const DecodeDims D = p.d;
   unsigned char* U = c.U;
@@ -746,7 +745,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
   // attention already in shared memory), normed with the weights of its own stream chunk, quantised
   const unsigned char* nrm = nullptr;
   if (op.has_norm_chunk) {
-    nrm = stream_acquire(p, st, idx++);
+    nrm = stream_acquire(rv, idx++);
     if (nrm == nullptr) ok = false;
   }
   const bool from_smem = op.ll_in < 0;
@@ -765,7 +764,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
     c.prof_t = c.prof_t2;
   }
   if (op.has_const) {
-    cst = stream_acquire(p, st, idx++);
+    cst = stream_acquire(rv, idx++);
     if (cst == nullptr) ok = false;
   }
   tick<kTrace>(c, 2);
@@ -791,7 +790,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
   const float* const resid = c.resid + lo;
   const int n_row_chunks = op.n_chunks - op.has_const - op.has_norm_chunk;
   for (int ch = 0; ch < n_row_chunks; ++ch) {
-    const unsigned char* stage = stream_acquire(p, st, idx++);
+    const unsigned char* stage = stream_acquire(rv, idx++);
     if (!__all_sync(kFull, stage != nullptr)) {
       ok = false;
     } else {
@@ -833,7 +832,7 @@ __device__ __forceinline__ bool op_gemv(Ctx& c, const Op& opr, const IvbLayerDes
   } else if (op.kind == OP_ENTRY_MAMBA) {
     cp_async_wait_all();
     __syncthreads();
-    ssm_step(c, opr, lay, rows_out, ssmc);
+    ssm_step(c, p, opr, lay, rows_out, ssmc);
   }
   tick<kTrace>(c, 4);
   if (!ok) atomicCAS(p.error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
@@ -996,6 +995,8 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
   }
   cp_async_wait_all();
   __syncthreads();
+  // the ring as its consumers see it (an attention CTA streams through the last kAttnStages stages)
+  const RingView rv{full, smem + M.ring + (attn_cta ? (kStages - kAttnStages) * M.stage_bytes : 0), M.stage_bytes, p.timeout_ns};
   unsigned opk = 0;  // ops run so far (selects the descriptor slot)
   bool alive = true;
   if (attn_cta) {
@@ -1035,7 +1036,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
                              D.rope, flag, reinterpret_cast<unsigned*>(c.xl), p.timeout_ns);
         tick<kTrace>(c, 5);
         const unsigned chunk = c.chunk_base + static_cast<unsigned>(mi);
-        if (ok) ok = op_attention<kTrace>(c, op, lay, h, chunk);
+        if (ok) ok = op_attention<kTrace>(c, p, rv, op, lay, h, chunk);
         else c.fail(IVB_ETIMEOUT);
         if (kTrace && tid == 0 && c.marks != nullptr) {
           for (int k = 0; k < 6; ++k) c.marks[1 + k] = static_cast<unsigned long long>(c.prof[k]);
@@ -1092,7 +1093,7 @@ __global__ void __launch_bounds__(kThreads, 1) grid_decode_kernel(const __grid_c
         if (op.kind == OP_MERGE) {
           ok = op_merge(c, op);
         } else if (op.kind != OP_ATTN) {  // the attention CTAs run the attention ops
-          ok = op_gemv<kTrace>(c, op, lay, rows_c);
+          ok = op_gemv<kTrace>(c, p, rv, op, lay, rows_c);
         }
         tick<kTrace>(c, 5);
         if (kTrace && tid == 0 && c.marks != nullptr) {
