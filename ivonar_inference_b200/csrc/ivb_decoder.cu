@@ -579,31 +579,42 @@ __device__ __forceinline__ void ssm_step(Ctx& c, const DecodeParams& p, const Op
   const float* s_prev = s_state + 2 * S * cpc;   // [S][cpc]
   const float* s_conv = s_prev + S * cpc;        // [cpc][taps - 1]
   const float* bcdt = rows_out + 2 * cpc;
-  for (int s2 = tid; s2 < S; s2 += kThreads) {
-    const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
-    const float mag = expf(2.0f * half_dt * decay[s2]);
-    float sn, cs;
-    sincosf(2.0f * half_dt * theta[s2], &sn, &cs);
-    coef[s2] = tanhf(bcdt[s2]);
-    coef[S + s2] = tanhf(bcdt[S + s2]);
-    coef[2 * S + s2] = half_dt;
-    coef[3 * S + s2] = mag * cs;
-    coef[4 * S + s2] = mag * sn;
-  }
   float* const conv_state = L.conv_state;
   float2* const ssm_state = reinterpret_cast<float2*>(L.ssm_state);
   float* const prev_force = L.prev_force;
   float* const stg = c.stg;
-  for (int cl = tid; cl < cpc; cl += kThreads) {
-    const float* win = s_conv + cl * (taps - 1);
-    float* gwin = conv_state + static_cast<size_t>(ch0 + cl) * (taps - 1);
-    const float incoming = rows_out[cl];
-    float conv = convb[cl];
-    for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
-    conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
-    for (int k2 = 0; k2 + 1 < taps - 1; ++k2) gwin[k2] = win[k2 + 1];
-    if (taps > 1) gwin[taps - 2] = incoming;
-    vals[cl] = silu_f(conv);
+  // the independent transcendental chains side by side, one warp each: the step coefficients of the
+  // states (sigmoid -> exp, sincos), tanh of B, tanh of C, the causal conv + SiLU of the channels and
+  // the output gate's sigmoid (kept in stg for the readout's thread of the same channel)
+  const int warp = tid >> 5, lane = tid & 31;
+  if (warp == 0) {
+    for (int s2 = lane; s2 < S; s2 += 32) {
+      const float half_dt = D.half_dt_min + sigmoid_f(bcdt[2 * S + s2]) * D.half_dt_range;
+      const float mag = expf(2.0f * half_dt * decay[s2]);
+      float sn, cs;
+      sincosf(2.0f * half_dt * theta[s2], &sn, &cs);
+      coef[2 * S + s2] = half_dt;
+      coef[3 * S + s2] = mag * cs;
+      coef[4 * S + s2] = mag * sn;
+    }
+  } else if (warp == 1) {
+    for (int s2 = lane; s2 < S; s2 += 32) coef[s2] = tanhf(bcdt[s2]);
+  } else if (warp == 2) {
+    for (int s2 = lane; s2 < S; s2 += 32) coef[S + s2] = tanhf(bcdt[S + s2]);
+  } else if (warp == 3) {
+    for (int cl = lane; cl < cpc; cl += 32) {
+      const float* win = s_conv + cl * (taps - 1);
+      float* gwin = conv_state + static_cast<size_t>(ch0 + cl) * (taps - 1);
+      const float incoming = rows_out[cl];
+      float conv = convb[cl];
+      for (int k2 = 0; k2 < taps - 1; ++k2) conv = fmaf(convw[cl * taps + k2], win[k2], conv);
+      conv = fmaf(convw[cl * taps + taps - 1], incoming, conv);
+      for (int k2 = 0; k2 + 1 < taps - 1; ++k2) gwin[k2] = win[k2 + 1];
+      if (taps > 1) gwin[taps - 2] = incoming;
+      vals[cl] = silu_f(conv);
+    }
+  } else if (warp == 4) {
+    for (int cl = lane; cl < cpc; cl += 32) stg[cl] = sigmoid_f(rows_out[cpc + cl]);
   }
   __syncthreads();
   // one (channel, state) pair per thread: lanes run along the channels of a state (contiguous state memory)
@@ -640,10 +651,9 @@ __device__ __forceinline__ void ssm_step(Ctx& c, const DecodeParams& p, const Op
     } else {
       for (int s2 = 0; s2 < S; ++s2) contrib += cp[s2];
     }
-    stg[cl] = (contrib + skip[cl] * vals[cl]) * sigmoid_f(rows_out[cpc + cl]);
+    // published by the thread that computed it (its gate sigmoid is in stg[cl])
+    ll_store(p.ll + op.ll_out + ch0 + cl, __float_as_uint((contrib + skip[cl] * vals[cl]) * stg[cl]), c.flag);
   }
-  __syncthreads();
-  ll_put(p.ll + op.ll_out, ch0, stg, cpc, c.flag);
 }
 
 // Local top-k of the head op: keys[0, n) (n <= 256, one per thread) ranked by (key desc, index asc);
