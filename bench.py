@@ -94,9 +94,9 @@ def measured_peaks() -> tuple[float, str]:
 
 
 # dram__bytes_read.sum + dram__bytes_write.sum of one ncu capture (--set full) of a 16-token
-# grid_decode_kernel launch of this workload (1,815,794,944 + 64,375,040 bytes), per token; scaled to a
+# grid_decode_kernel launch of this workload (1,870,212,352 + 65,810,688 bytes), per token; scaled to a
 # launch by the tokens it runs.
-NCU_DRAM_BYTES_PER_TOKEN = (1_815_794_944 + 64_375_040) / 16
+NCU_DRAM_BYTES_PER_TOKEN = (1_870_212_352 + 65_810_688) / 16
 TRAFFIC_SOURCE = ("ncu --set full capture of a 16-token grid_decode_kernel launch at positions 37-52 "
                   "(python bench.py --steps 1 --warmup 1 --tokens 16 ...), scaled by tokens per launch")
 
