@@ -16,6 +16,7 @@
 
 #include "ivb_common.h"
 #include "ivb_decode.cuh"
+#include "ivb_tc.cuh"
 #include "ivb_tiles.cuh"
 
 namespace ivb {
@@ -409,13 +410,11 @@ __global__ void __launch_bounds__(kThreads) mla_cache_kernel(IvbLayerDesc L, con
   }
 }
 
-// ---- causal attention of the prefill on tensor cores ---------------------------------------------
-// Non-absorbed form: the cached latent of every position p (int8 codes ql_p, scale a_p) is expanded
-// by the tcgen05 GEMM into per-head keys K_nope[p] = a_p W_k ql_p + b_k and values V[p] = a_p W_v ql_p
-// + b_v, which is the same arithmetic as the decode kernel's absorbed form regrouped:
-// a_p <W_k^T q, ql_p> + q.b_k = q.K_nope[p] and W_v (sum_p w_p a_p ql_p) + b_v = sum_p w_p V[p] (the
-// weights w sum to one). Then a flash-attention kernel per (64-token query block, head) runs
-// mma.sync m16n8k16 with fp16 operands in a three-product split (x = hi + lo, x.y ~ hi.hi' + hi.lo' +
+// ---- causal attention of the prefill ------------------------------------------------------------
+// The reference decoder's form: the cached latent of every position p (int8 codes ql_p, scale a_p) is
+// expanded by the tcgen05 GEMM into per-head keys K_nope[p] = a_p W_k ql_p + b_k and values V[p] =
+// a_p W_v ql_p + b_v (the rows the decode kernel appends to its key/value cache). The attention itself
+// runs on tcgen05 with fp16 operands in a three-product split (x = hi + lo, x.y ~ hi.hi' + hi.lo' +
 // lo.hi'), which keeps about 22 significant bits, close to the fp32 arithmetic of the decode path.
 
 // Latent codes of positions 0..P-1 into the tiled GEMM activation layout (ldq = latent rounded to 128).
@@ -440,65 +439,12 @@ __global__ void latent_tile_kernel(const int8_t* latent_q, int lpad, int Lt, int
   *reinterpret_cast<uint4*>(q8 + q8_chunk_offset(p, k, ldq)) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, {%0, %1, %2, %3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
 // x = hi + lo with hi, lo fp16 (packed pairs)
 __device__ __forceinline__ void split2(float x0, float x1, uint32_t& hi, uint32_t& lo) {
   const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1);
   const __half l0 = __float2half_rn(x0 - __half2float(h0)), l1 = __float2half_rn(x1 - __half2float(h1));
   hi = static_cast<uint32_t>(__half_as_ushort(h0)) | (static_cast<uint32_t>(__half_as_ushort(h1)) << 16);
   lo = static_cast<uint32_t>(__half_as_ushort(l0)) | (static_cast<uint32_t>(__half_as_ushort(l1)) << 16);
-}
-
-constexpr int kFaTok = 64;      // query tokens per CTA (4 warps x 16)
-constexpr int kFaPos = 64;      // key positions per tile
-constexpr int kFaThreads = 128;
-
-// Keys and values of positions 0..P-1 of one layer as fp16 hi/lo pairs, laid out for whole-tile copies:
-// kh/kl [H][Ppad][DK] (K_nope then k_rope, zero padded), vh/vl [H][DV][Ppad] (transposed, zero padded),
-// Ppad = P rounded up to kFaPos. One thread per (head, position, 8 dims).
-template <int DK>
-__global__ void kv_split_kernel(IvbLayerDesc L, const float* knope, const float* vbuf, int P, int Ppad, int d, int H,
-                                int hd, int rope, int nope, int max_len, int rpad, __half* kh, __half* kl, __half* vh,
-                                __half* vl) {
-  pdl_enter();
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  const int per_head = Ppad * (DK / 8);
-  if (i >= H * per_head) return;
-  const int h = i / per_head, rest = i - h * per_head, p = rest / (DK / 8), e0 = (rest - p * (DK / 8)) * 8;
-  uint32_t khw[4], klw[4], vhw[8], vlw[8];
-  float kv[8], vv[8];
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    const int e = e0 + j;
-    float k = 0.0f, v = 0.0f;
-    if (p < P) {
-      if (e < nope) k = knope[static_cast<size_t>(p) * H * nope + h * nope + e];
-      else if (e < nope + rope) k = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + p) * rpad + (e - nope)]);
-      if (e < hd) v = vbuf[static_cast<size_t>(p) * d + h * hd + e];
-    }
-    kv[j] = k;
-    vv[j] = v;
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) split2(kv[2 * j], kv[2 * j + 1], khw[j], klw[j]);
-  const size_t ko = (static_cast<size_t>(h) * Ppad + p) * DK + e0;
-  *reinterpret_cast<uint4*>(kh + ko) = make_uint4(khw[0], khw[1], khw[2], khw[3]);
-  *reinterpret_cast<uint4*>(kl + ko) = make_uint4(klw[0], klw[1], klw[2], klw[3]);
-#pragma unroll
-  for (int j = 0; j < 8; ++j) {
-    if (e0 + j >= DK) break;
-    const __half hv = __float2half_rn(vv[j]);
-    const size_t vo = (static_cast<size_t>(h) * DK + e0 + j) * Ppad + p;
-    vh[vo] = hv;
-    vl[vo] = __float2half_rn(vv[j] - __half2float(hv));
-  }
-  (void)vhw;
-  (void)vlw;
 }
 
 // The decode kernel's key / value cache rows of positions pos0 .. pos0 + T - 1 (layout of
@@ -521,238 +467,305 @@ __global__ void kv_cache_kernel(IvbLayerDesc L, const float* knope, const float*
   L.v_cache[o] = v;
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+// ---- causal prefill attention on the 5th-generation tensor cores ---------------------------------
+// One CTA per (128 queries, head), 128 threads: thread r owns query row r, which is TMEM lane r of the
+// two accumulators. Per tile of 64 keys: S = Q K^T and O_t = P V on tcgen05 (kind::f16, fp32 in TMEM),
+// each as the three products of a hi/lo fp16 split (x = hi + lo; Qh Kh + Qh Kl + Ql Kh), issued by one
+// thread and completed on an mbarrier by tcgen05.commit; between them each thread loads its score row
+// from TMEM, masks it causally, runs the online softmax in registers and writes its probability row as
+// the hi/lo A operand of P V. O accumulates in registers (o = o exp(m_old - m_new) + O_t). Every operand
+// (Q, K, P, V) sits in shared memory as a K-major tile of 8-row x 16-byte core matrices (LBO 128 bytes);
+// the key and value tiles come in that layout from fa_kv_tiles_kernel, one bulk copy each.
+constexpr int kFaQ = 128;        // queries per CTA (MMA M, TMEM lanes)
+constexpr int kFaKeys = 64;      // keys per tile (N of S, K of P V)
+constexpr int kFaTcThreads = 128;
+
+// Byte offset of 16-byte chunk c of row r in a K-major core-matrix tile with cpr chunks per row.
+__host__ __device__ __forceinline__ int cm_off(int r, int c, int cpr) { return ((r >> 3) * cpr + c) * 128 + ((r & 7) << 4); }
+
+// Keys and values of positions 0..P-1 of one layer as fp16 hi/lo tiles for the tensor-core attention:
+// per (head, tile of 64 keys) a key tile [64 keys][DK dims] and a value tile [DK dims][64 keys], each a
+// K-major core-matrix tile of DK * 64 halves; arrays kh, kl, vh, vl of H * Ppad * DK halves (Ppad = P
+// rounded up to 64, padding zero). One thread per (head, position, 8 dims).
+template <int DK>
+__global__ void fa_kv_tiles_kernel(IvbLayerDesc L, const float* knope, const float* vbuf, int P, int Ppad, int d, int H, int hd,
+                                   int rope, int nope, int max_len, int rpad, __half* kh, __half* kl, __half* vh, __half* vl) {
+  pdl_enter();
+  constexpr int cpr = DK / 8;
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  const int per_head = Ppad * cpr;
+  if (i >= H * per_head) return;
+  const int h = i / per_head, rest = i - h * per_head, p = rest / cpr, c = rest - p * cpr;
+  float kv[8], vv[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const int e = 8 * c + j;
+    float k = 0.0f, v = 0.0f;
+    if (p < P) {
+      if (e < nope) k = knope[static_cast<size_t>(p) * H * nope + h * nope + e];
+      else if (e < nope + rope) k = h2f(L.k_rope_cache[(static_cast<size_t>(h) * max_len + p) * rpad + (e - nope)]);
+      if (e < hd) v = vbuf[static_cast<size_t>(p) * d + h * hd + e];
+    }
+    kv[j] = k;
+    vv[j] = v;
+  }
+  uint32_t khw[4], klw[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) split2(kv[2 * j], kv[2 * j + 1], khw[j], klw[j]);
+  const size_t block = (static_cast<size_t>(h) * (Ppad / kFaKeys) + p / kFaKeys) * kFaKeys * DK * 2;  // bytes
+  const int r = p & (kFaKeys - 1);
+  unsigned char* khb = reinterpret_cast<unsigned char*>(kh) + block;
+  unsigned char* klb = reinterpret_cast<unsigned char*>(kl) + block;
+  *reinterpret_cast<uint4*>(khb + cm_off(r, c, cpr)) = make_uint4(khw[0], khw[1], khw[2], khw[3]);
+  *reinterpret_cast<uint4*>(klb + cm_off(r, c, cpr)) = make_uint4(klw[0], klw[1], klw[2], klw[3]);
+  // the value tile's rows are the dims: dim 8c + j of key r is half (r & 7) of chunk r / 8 of row 8c + j
+  unsigned char* vhb = reinterpret_cast<unsigned char*>(vh) + block;
+  unsigned char* vlb = reinterpret_cast<unsigned char*>(vl) + block;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const __half hv = __float2half_rn(vv[j]);
+    const int off = cm_off(8 * c + j, r >> 3, kFaKeys / 8) + (r & 7) * 2;
+    *reinterpret_cast<__half*>(vhb + off) = hv;
+    *reinterpret_cast<__half*>(vlb + off) = __float2half_rn(vv[j] - __half2float(hv));
+  }
 }
 
-// Grid (ceil(count / 64), heads). DK: query/key dims (nope + rope) padded to 16 (= value dims padded).
-// q from the entry rows (scaled by attn_scale, rope part rotated); keys and values from kv_split_kernel.
-// Tiles of 64 positions are double-buffered with cp.async.
+// Grid (heads, query blocks of 128, last block first). q from the entry rows (scaled by attn_scale, rope
+// pairs rotated), keys and values from fa_kv_tiles_kernel; y [count][d] gets the head's outputs. Every
+// wait is bounded: a wait that runs out records IVB_ETIMEOUT in *error and the CTA stops after the
+// tensor-core work it issued has completed (bounded again), releasing its tensor memory.
 template <int DK>
-__global__ void __launch_bounds__(kFaThreads, DK <= 64 ? 3 : 1) flash_attention_kernel(IvbLayerDesc L, const float* ent, int ld_ent,
-                                                                     const __half* kh, const __half* kl,
-                                                                     const __half* vh, const __half* vl, int Ppad,
-                                                                     int start, int count, int d, int hd, int rope,
-                                                                     int nope, float* y) {
+__global__ void __launch_bounds__(kFaTcThreads, 1)
+    flash_attention_tc_kernel(IvbLayerDesc L, const float* ent, int ld_ent, const __half* kh, const __half* kl, const __half* vh,
+                              const __half* vl, int Ppad, int start, int count, int d, int hd, int rope, int nope, float* y,
+                              unsigned long long timeout_ns, unsigned* error) {
   pdl_enter();
-  constexpr int DV = DK;
-  constexpr int kKs = DK + 8;       // key tile row stride (halves)
-  constexpr int kVs = kFaPos + 8;   // transposed value tile row stride (halves)
-  constexpr int kTileHalves = 2 * kFaPos * kKs + 2 * DV * kVs;  // k_hi, k_lo, v_hi, v_lo
-  extern __shared__ __align__(16) unsigned char fa_smem[];
-  __half* tiles = reinterpret_cast<__half*>(fa_smem);
-  float* qs = reinterpret_cast<float*>(fa_smem);  // the query block, before the first key tile
-  // grid (heads, query tiles) with the last query tile first: the causal tiles with the most keys start
-  // in the first wave and the short ones fill the tail
-  const int h = blockIdx.x, tq0 = (gridDim.y - 1 - blockIdx.y) * kFaTok;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, grp = lane >> 2, tig = lane & 3;
-  const float scl = L.attn_scale;
-  for (int i = tid; i < kFaTok * DK; i += kFaThreads) {
-    const int tl = i / DK, e = i - tl * DK, t = tq0 + tl;
-    float v = 0.0f;
-    if (t < count && e < nope + rope) {
-      const float* q = ent + static_cast<size_t>(t) * ld_ent + h * hd;
-      if (e < nope) {
-        v = q[e] * scl;
-      } else {
-        const int jr = (e - nope) >> 1;
-        const float* rt = L.rope + static_cast<size_t>(start + t) * rope;
-        const float cs = __ldg(rt + 2 * jr), sn = __ldg(rt + 2 * jr + 1);
-        const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
-        v = (((e - nope) & 1) == 0 ? q0 * cs - q1 * sn : q0 * sn + q1 * cs) * scl;
+  constexpr int cq = DK / 8;                        // 16-byte chunks per query / key row
+  constexpr int kQBytes = kFaQ * DK * 2;            // one of Qh, Ql
+  constexpr int kKBytes = kFaKeys * DK * 2;         // one of Kh, Kl, Vh, Vl
+  constexpr int kPBytes = kFaQ * kFaKeys * 2;       // one of Ph, Pl
+  constexpr int kTmemCols = (kFaKeys + DK) <= 128 ? 128 : 256;
+  constexpr uint32_t kIdescS = idesc_f16(kFaQ, kFaKeys), kIdescO = idesc_f16(kFaQ, DK);
+  extern __shared__ __align__(128) unsigned char fa_tc_smem[];
+  unsigned char* const qhs = fa_tc_smem;
+  unsigned char* const qls = qhs + kQBytes;
+  unsigned char* const khs = qls + kQBytes;
+  unsigned char* const kls = khs + kKBytes;
+  unsigned char* const vhs = kls + kKBytes;
+  unsigned char* const vls = vhs + kKBytes;
+  unsigned char* const phs = vls + kKBytes;
+  unsigned char* const pls = phs + kPBytes;
+  __shared__ __align__(8) unsigned long long kvbar, sbar, obar;
+  __shared__ unsigned tmem_base;
+  const int h = blockIdx.x, tq0 = (gridDim.y - 1 - blockIdx.y) * kFaQ;
+  const int tid = threadIdx.x, warp = tid >> 5;
+  if (tid == 0) {
+    mbar_init(&kvbar, 1);
+    mbar_init(&sbar, 1);
+    mbar_init(&obar, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
+                 "r"(kTmemCols));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  // my query row (scaled, rope pairs rotated) as hi/lo fp16 chunks of the A operand of S
+  const int t = tq0 + tid;
+  {
+    const float scl = L.attn_scale;
+    const float* q = ent + static_cast<size_t>(t < count ? t : 0) * ld_ent + h * hd;
+    const float* rt = L.rope + static_cast<size_t>(start + (t < count ? t : 0)) * rope;
+#pragma unroll
+    for (int c = 0; c < cq; ++c) {
+      float v[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int e = 8 * c + j;
+        float x = 0.0f;
+        if (t < count && e < nope + rope) {
+          if (e < nope) {
+            x = q[e] * scl;
+          } else {
+            const int jr = (e - nope) >> 1;
+            const float cs = __ldg(rt + 2 * jr), sn = __ldg(rt + 2 * jr + 1);
+            const float q0 = q[nope + 2 * jr], q1 = q[nope + 2 * jr + 1];
+            x = (((e - nope) & 1) == 0 ? q0 * cs - q1 * sn : q0 * sn + q1 * cs) * scl;
+          }
+        }
+        v[j] = x;
       }
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) split2(v[2 * j], v[2 * j + 1], hw[j], lw[j]);
+      *reinterpret_cast<uint4*>(qhs + cm_off(tid, c, cq)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(qls + cm_off(tid, c, cq)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
     }
-    qs[i] = v;
   }
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the MMA reads what the threads wrote
+  tc_fence_before();
   __syncthreads();
-  uint32_t qh[DK / 16][4], ql[DK / 16][4];
-  const int r0 = 16 * warp + grp;
+  tc_fence_after();
+  const unsigned tmem = tmem_base;
+  const unsigned tS = tmem, tO = tmem + kFaKeys;  // S in columns [0, 64), O_t in [64, 64 + DK)
+  const unsigned lane_off = static_cast<unsigned>(32 * warp) << 16;
+  const int t_last = min(count, tq0 + kFaQ) - 1;
+  const int p_end = start + t_last + 1;  // keys 0..p_end-1 serve the block
+  const int tiles_n = (p_end + kFaKeys - 1) / kFaKeys;
+  const int pos = start + t;            // my query's position
+  const size_t head_tiles = static_cast<size_t>(Ppad / kFaKeys);
+  float o[DK];
 #pragma unroll
-  for (int kk = 0; kk < DK / 16; ++kk) {
-    const int c = 16 * kk + 2 * tig;
-    split2(qs[r0 * DK + c], qs[r0 * DK + c + 1], qh[kk][0], ql[kk][0]);
-    split2(qs[(r0 + 8) * DK + c], qs[(r0 + 8) * DK + c + 1], qh[kk][1], ql[kk][1]);
-    split2(qs[r0 * DK + c + 8], qs[r0 * DK + c + 9], qh[kk][2], ql[kk][2]);
-    split2(qs[(r0 + 8) * DK + c + 8], qs[(r0 + 8) * DK + c + 9], qh[kk][3], ql[kk][3]);
-  }
-  __syncthreads();  // qs is overwritten by the tiles
-  const __half* khh = kh + static_cast<size_t>(h) * Ppad * DK;
-  const __half* klh = kl + static_cast<size_t>(h) * Ppad * DK;
-  const __half* vhh = vh + static_cast<size_t>(h) * DV * Ppad;
-  const __half* vlh = vl + static_cast<size_t>(h) * DV * Ppad;
-  auto load_tile = [&](int buf, int p0) {
-    __half* base = tiles + buf * kTileHalves;
-    __half* khs = base;
-    __half* kls = khs + kFaPos * kKs;
-    __half* vhs = kls + kFaPos * kKs;
-    __half* vls = vhs + DV * kVs;
-    for (int i = tid; i < kFaPos * (DK / 8); i += kFaThreads) {
-      const int pl = i / (DK / 8), c = i - pl * (DK / 8);
-      const size_t src = static_cast<size_t>(p0 + pl) * DK + 8 * c;
-      cp_async16(khs + pl * kKs + 8 * c, khh + src);
-      cp_async16(kls + pl * kKs + 8 * c, klh + src);
+  for (int e = 0; e < DK; ++e) o[e] = 0.0f;
+  float m_run = -INFINITY, l_run = 0.0f;
+  bool ok = true;
+  // thread 0: copies and MMA commits issued and not yet waited for, with the parity of their phase
+  int kv_pending = -1, s_pending = -1, o_pending = -1;
+  for (int it = 0; it < tiles_n && ok; ++it) {
+    const unsigned par = static_cast<unsigned>(it) & 1u;
+    // this tile's keys and values (the previous tile's MMAs completed before its O_t was read)
+    if (tid == 0) {
+      const size_t block = (static_cast<size_t>(h) * head_tiles + it) * kKBytes;
+      mbar_expect_tx(&kvbar, 4u * kKBytes);
+      bulk_copy(khs, reinterpret_cast<const unsigned char*>(kh) + block, kKBytes, &kvbar);
+      bulk_copy(kls, reinterpret_cast<const unsigned char*>(kl) + block, kKBytes, &kvbar);
+      bulk_copy(vhs, reinterpret_cast<const unsigned char*>(vh) + block, kKBytes, &kvbar);
+      bulk_copy(vls, reinterpret_cast<const unsigned char*>(vl) + block, kKBytes, &kvbar);
+      kv_pending = static_cast<int>(par);
     }
-    for (int i = tid; i < DV * (kFaPos / 8); i += kFaThreads) {
-      const int e = i / (kFaPos / 8), c = i - e * (kFaPos / 8);
-      const size_t src = static_cast<size_t>(e) * Ppad + p0 + 8 * c;
-      cp_async16(vhs + e * kVs + 8 * c, vhh + src);
-      cp_async16(vls + e * kVs + 8 * c, vlh + src);
+    if (__syncthreads_or(!mbar_wait_bounded(&kvbar, par, timeout_ns))) {
+      ok = false;
+      break;
     }
-    asm volatile("cp.async.commit_group;" ::: "memory");
-  };
-  float o[DV / 8][4];
-#pragma unroll
-  for (int n = 0; n < DV / 8; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.0f, 0.0f};
-  const int pos_a = start + tq0 + r0, pos_b = pos_a + 8;  // positions of this thread's two query rows
-  const int t_last = min(count, tq0 + kFaTok) - 1;
-  const int p_end = start + t_last + 1;                   // keys 0..p_end-1 serve the block
-  const int warp_last = start + min(count - 1, tq0 + 16 * warp + 15);
-  const int tiles_n = (p_end + kFaPos - 1) / kFaPos;
-  load_tile(0, 0);
-  for (int it = 0; it < tiles_n; ++it) {
-    const int p0 = it * kFaPos, buf = it & 1;
-    if (it + 1 < tiles_n) {
-      load_tile(buf ^ 1, p0 + kFaPos);
-      asm volatile("cp.async.wait_group 1;" ::: "memory");
-    } else {
-      asm volatile("cp.async.wait_group 0;" ::: "memory");
-    }
-    __syncthreads();
-    const __half* k_hi = tiles + buf * kTileHalves;
-    const __half* k_lo = k_hi + kFaPos * kKs;
-    const __half* v_hi = k_lo + kFaPos * kKs;
-    const __half* v_lo = v_hi + DV * kVs;
-    if (p0 <= warp_last) {
-      float s[kFaPos / 8][4];
-#pragma unroll
-      for (int n = 0; n < kFaPos / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.0f;
-      // the three products of a split go to one accumulator; consecutive MMAs target different
-      // accumulators so none waits on the previous one
+    if (tid == 0) kv_pending = -1;
+    // S = Q K^T
+    if (tid == 0) {
+      tc_fence_after();
+      const unsigned qa = smem_addr(qhs), ql = smem_addr(qls), ka = smem_addr(khs), kb = smem_addr(kls);
 #pragma unroll
       for (int kk = 0; kk < DK / 16; ++kk) {
-        uint32_t bh[kFaPos / 8][2], bl[kFaPos / 8][2];
-#pragma unroll
-        for (int n = 0; n < kFaPos / 8; ++n) {
-          const int row = (8 * n + grp) * kKs + 16 * kk + 2 * tig;
-          bh[n][0] = *reinterpret_cast<const uint32_t*>(k_hi + row);
-          bh[n][1] = *reinterpret_cast<const uint32_t*>(k_hi + row + 8);
-          bl[n][0] = *reinterpret_cast<const uint32_t*>(k_lo + row);
-          bl[n][1] = *reinterpret_cast<const uint32_t*>(k_lo + row + 8);
-        }
-#pragma unroll
-        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], qh[kk], bh[n][0], bh[n][1]);
-#pragma unroll
-        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], qh[kk], bl[n][0], bl[n][1]);
-#pragma unroll
-        for (int n = 0; n < kFaPos / 8; ++n) mma16816(s[n], ql[kk], bh[n][0], bh[n][1]);
+        const unsigned off = kk * 256;
+        umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, kk > 0);
+        umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(kb + off, cq * 128), kIdescS, true);
+        umma_f16_ss(tS, smem_desc(ql + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, true);
       }
-      // causal mask and online softmax (rows pos_a: s[n][0..1], pos_b: s[n][2..3])
-      float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-      for (int n = 0; n < kFaPos / 8; ++n) {
-        const int p = p0 + 8 * n + 2 * tig;
-        if (p > pos_a) s[n][0] = -INFINITY;
-        if (p + 1 > pos_a) s[n][1] = -INFINITY;
-        if (p > pos_b) s[n][2] = -INFINITY;
-        if (p + 1 > pos_b) s[n][3] = -INFINITY;
-        mx[0] = fmaxf(mx[0], fmaxf(s[n][0], s[n][1]));
-        mx[1] = fmaxf(mx[1], fmaxf(s[n][2], s[n][3]));
-      }
-      float corr[2], sum[2] = {0.0f, 0.0f};
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 1));
-        mx[r] = fmaxf(mx[r], __shfl_xor_sync(kFull, mx[r], 2));
-        const float m_new = fmaxf(m_run[r], mx[r]);
-        corr[r] = m_new == -INFINITY ? 1.0f : expf(m_run[r] - m_new);
-        m_run[r] = m_new;
-      }
-      uint32_t ph[kFaPos / 16][4], pl2[kFaPos / 16][4];
-#pragma unroll
-      for (int n = 0; n < kFaPos / 8; ++n) {
-        float e[4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const float m = m_run[c >> 1];
-          e[c] = (s[n][c] == -INFINITY) ? 0.0f : expf(s[n][c] - m);
-        }
-        sum[0] += e[0] + e[1];
-        sum[1] += e[2] + e[3];
-        // C fragment of position tile n -> A fragment of k-step n / 2 (regs 0, 1 or 2, 3)
-        split2(e[0], e[1], ph[n >> 1][(n & 1) * 2], pl2[n >> 1][(n & 1) * 2]);
-        split2(e[2], e[3], ph[n >> 1][(n & 1) * 2 + 1], pl2[n >> 1][(n & 1) * 2 + 1]);
-      }
-#pragma unroll
-      for (int r = 0; r < 2; ++r) {
-        sum[r] += __shfl_xor_sync(kFull, sum[r], 1);
-        sum[r] += __shfl_xor_sync(kFull, sum[r], 2);
-        l_run[r] = l_run[r] * corr[r] + sum[r];
-      }
-#pragma unroll
-      for (int n = 0; n < DV / 8; ++n) {
-        o[n][0] *= corr[0];
-        o[n][1] *= corr[0];
-        o[n][2] *= corr[1];
-        o[n][3] *= corr[1];
-      }
-#pragma unroll
-      for (int kk = 0; kk < kFaPos / 16; ++kk) {
-#pragma unroll
-        for (int n0 = 0; n0 < DV / 8; n0 += 8) {  // eight value columns at a time bound the registers
-          constexpr int kG = DV / 8 < 8 ? DV / 8 : 8;
-          uint32_t bh[kG][2], bl[kG][2];
-#pragma unroll
-          for (int j = 0; j < kG; ++j) {
-            const int row = (8 * (n0 + j) + grp) * kVs + 16 * kk + 2 * tig;
-            bh[j][0] = *reinterpret_cast<const uint32_t*>(v_hi + row);
-            bh[j][1] = *reinterpret_cast<const uint32_t*>(v_hi + row + 8);
-            bl[j][0] = *reinterpret_cast<const uint32_t*>(v_lo + row);
-            bl[j][1] = *reinterpret_cast<const uint32_t*>(v_lo + row + 8);
-          }
-#pragma unroll
-          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], ph[kk], bh[j][0], bh[j][1]);
-#pragma unroll
-          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], ph[kk], bl[j][0], bl[j][1]);
-#pragma unroll
-          for (int j = 0; j < kG; ++j) mma16816(o[n0 + j], pl2[kk], bh[j][0], bh[j][1]);
-        }
-      }
+      umma_commit(&sbar);
+      s_pending = static_cast<int>(par);
     }
-    __syncthreads();  // buffer buf is refilled by the next iteration's prefetch
+    if (__syncthreads_or(!mbar_wait_bounded(&sbar, par, timeout_ns))) {
+      ok = false;
+      break;
+    }
+    if (tid == 0) s_pending = -1;
+    tc_fence_after();
+    // my score row, causally masked; online softmax; probabilities as the hi/lo A operand of P V
+    const int p0 = it * kFaKeys;
+    float sc[kFaKeys];
+    {
+      uint32_t v[32];
+      tmem_ld32(tS + lane_off, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sc[j] = __uint_as_float(v[j]);
+      tmem_ld32(tS + lane_off + 32, v);
+#pragma unroll
+      for (int j = 0; j < 32; ++j) sc[32 + j] = __uint_as_float(v[j]);
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < kFaKeys; ++j) {
+      if (p0 + j > pos) sc[j] = -INFINITY;
+      mx = fmaxf(mx, sc[j]);
+    }
+    const float m_new = fmaxf(m_run, mx);
+    const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
+    float sum = 0.0f;
+#pragma unroll
+    for (int c = 0; c < kFaKeys / 8; ++c) {
+      uint32_t hw[4], lw[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float e0 = m_new == -INFINITY ? 0.0f : expf(sc[8 * c + 2 * j] - m_new);
+        const float e1 = m_new == -INFINITY ? 0.0f : expf(sc[8 * c + 2 * j + 1] - m_new);
+        sum += e0 + e1;
+        split2(e0, e1, hw[j], lw[j]);
+      }
+      *reinterpret_cast<uint4*>(phs + cm_off(tid, c, kFaKeys / 8)) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+      *reinterpret_cast<uint4*>(pls + cm_off(tid, c, kFaKeys / 8)) = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    }
+    l_run = l_run * corr + sum;
+    m_run = m_new;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    tc_fence_before();
+    __syncthreads();
+    // O_t = P V
+    if (tid == 0) {
+      tc_fence_after();
+      const unsigned pa = smem_addr(phs), pb = smem_addr(pls), va = smem_addr(vhs), vb = smem_addr(vls);
+#pragma unroll
+      for (int kk = 0; kk < kFaKeys / 16; ++kk) {
+        const unsigned off = kk * 256;
+        umma_f16_ss(tO, smem_desc(pa + off), smem_desc(va + off), kIdescO, kk > 0);
+        umma_f16_ss(tO, smem_desc(pa + off), smem_desc(vb + off), kIdescO, true);
+        umma_f16_ss(tO, smem_desc(pb + off), smem_desc(va + off), kIdescO, true);
+      }
+      umma_commit(&obar);
+      o_pending = static_cast<int>(par);
+    }
+    if (__syncthreads_or(!mbar_wait_bounded(&obar, par, timeout_ns))) {
+      ok = false;
+      break;
+    }
+    if (tid == 0) o_pending = -1;
+    tc_fence_after();
+#pragma unroll
+    for (int c0 = 0; c0 < DK; c0 += 16) {
+      uint32_t v[16];
+      tmem_ld16(tO + lane_off + c0, v);
+#pragma unroll
+      for (int j = 0; j < 16; ++j) o[c0 + j] = fmaf(o[c0 + j], corr, __uint_as_float(v[j]));
+    }
+    tc_fence_before();
+    __syncthreads();  // S, O_t and the operand tiles are rewritten by the next tile
   }
-  const int ta = tq0 + r0, tb = ta + 8;
-  const float inv_a = 1.0f / l_run[0], inv_b = 1.0f / l_run[1];
+  if (!ok) {
+    if (tid == 0) {
+      atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
+      // let the copies and the tensor-core work this CTA issued finish before its shared and tensor
+      // memory are released
+      if (kv_pending >= 0) mbar_wait_bounded(&kvbar, static_cast<unsigned>(kv_pending), timeout_ns);
+      if (s_pending >= 0) mbar_wait_bounded(&sbar, static_cast<unsigned>(s_pending), timeout_ns);
+      if (o_pending >= 0) mbar_wait_bounded(&obar, static_cast<unsigned>(o_pending), timeout_ns);
+    }
+  } else if (t < count) {
+    const float inv = 1.0f / l_run;
+    float* yr = y + static_cast<size_t>(t) * d + h * hd;
 #pragma unroll
-  for (int n = 0; n < DV / 8; ++n) {
-    const int e = 8 * n + 2 * tig;
-    if (ta < count) {
-      if (e < hd) y[static_cast<size_t>(ta) * d + h * hd + e] = o[n][0] * inv_a;
-      if (e + 1 < hd) y[static_cast<size_t>(ta) * d + h * hd + e + 1] = o[n][1] * inv_a;
-    }
-    if (tb < count) {
-      if (e < hd) y[static_cast<size_t>(tb) * d + h * hd + e] = o[n][2] * inv_b;
-      if (e + 1 < hd) y[static_cast<size_t>(tb) * d + h * hd + e + 1] = o[n][3] * inv_b;
-    }
+    for (int e = 0; e < DK; ++e)
+      if (e < hd) yr[e] = o[e] * inv;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols));
   }
 }
 
 template <int DK>
 int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf,
                   __half* kvh, int start, int count, int d, int H, int hd, int rope, int nope, int max_len, int rpad,
-                  float* y, cudaStream_t s) {
-  const int P = start + count, Ppad = (P + kFaPos - 1) / kFaPos * kFaPos;
+                  float* y, unsigned* error, cudaStream_t s) {
+  const int P = start + count, Ppad = (P + kFaKeys - 1) / kFaKeys * kFaKeys;
   const size_t per = static_cast<size_t>(H) * Ppad * DK;  // halves per split array
   __half *kh = kvh, *kl = kh + per, *vh = kl + per, *vl = vh + per;
   const int threads = H * Ppad * (DK / 8);
-  IVB_CUDA(launch_pdl(kv_split_kernel<DK>, dim3((threads + 255) / 256), dim3(256), 0, s, L, knope, vbuf, P, Ppad, d, H, hd, rope, nope, max_len, rpad,
-                                                            kh, kl, vh, vl));
+  IVB_CUDA(launch_pdl(fa_kv_tiles_kernel<DK>, dim3((threads + 255) / 256), dim3(256), 0, s, L, knope, vbuf, P, Ppad, d, H, hd, rope,
+                      nope, max_len, rpad, kh, kl, vh, vl));
   IVB_CUDA(cudaGetLastError());
-  const size_t tile = (2 * static_cast<size_t>(kFaPos) * (DK + 8) + 2 * static_cast<size_t>(DK) * (kFaPos + 8)) * 2;
-  const size_t smem = std::max(2 * tile, static_cast<size_t>(kFaTok) * DK * 4);
-  IVB_CUDA(cudaFuncSetAttribute(flash_attention_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
-  IVB_CUDA(launch_pdl(flash_attention_kernel<DK>, dim3(H, (count + kFaTok - 1) / kFaTok), dim3(kFaThreads), smem, s, 
-      L, ent, ld_ent, kh, kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y));
+  const size_t smem = 2 * static_cast<size_t>(kFaQ) * DK * 2 + 4 * static_cast<size_t>(kFaKeys) * DK * 2 + 2 * static_cast<size_t>(kFaQ) * kFaKeys * 2;
+  IVB_CUDA(cudaFuncSetAttribute(flash_attention_tc_kernel<DK>, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  IVB_CUDA(launch_pdl(flash_attention_tc_kernel<DK>, dim3(H, (count + kFaQ - 1) / kFaQ), dim3(kFaTcThreads), smem, s, L, ent, ld_ent, kh,
+                      kl, vh, vl, Ppad, start, count, d, hd, rope, nope, y, 2000000000ull, error));
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
@@ -760,12 +773,12 @@ int32_t launch_fa(const IvbLayerDesc& L, const float* ent, int ld_ent, const flo
 // Query/key dims (nope + rope) and value dims (head_dim) are equal for these models; both padded to 16.
 int32_t launch_flash_attention(const IvbLayerDesc& L, const float* ent, int ld_ent, const float* knope, const float* vbuf,
                                __half* kvh, int start, int count, int d, int H, int hd, int rope, int nope, int max_len,
-                               int rpad, float* y, cudaStream_t s) {
+                               int rpad, float* y, unsigned* error, cudaStream_t s) {
   const int dk = std::max(nope + rope, hd);
-  if (dk <= 16) return launch_fa<16>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 32) return launch_fa<32>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 64) return launch_fa<64>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
-  if (dk <= 128) return launch_fa<128>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, s);
+  if (dk <= 16) return launch_fa<16>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, error, s);
+  if (dk <= 32) return launch_fa<32>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, error, s);
+  if (dk <= 64) return launch_fa<64>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, error, s);
+  if (dk <= 128) return launch_fa<128>(L, ent, ld_ent, knope, vbuf, kvh, start, count, d, H, hd, rope, nope, max_len, rpad, y, error, s);
   return fail(IVB_EINVAL, "ivb_decoder_prefill: head dims %d beyond the attention kernel", dk);
 }
 
@@ -936,7 +949,7 @@ int32_t ivb_decoder_prefill(IvbDecoder* dec, const int64_t* tokens, int32_t coun
         IVB_CUDA(cudaGetLastError());
       }
       if (int32_t rc = launch_flash_attention(L, ent, L.entry.rows, knope, vbuf, kvh, start_position, count, d, H, hd, rope,
-                                              nope, md.max_len, rpad, y, s))
+                                              nope, md.max_len, rpad, y, err, s))
         return rc;
     }
     if (int32_t rc = quant(y, d, nullptr, 0.0f)) return rc;
