@@ -555,12 +555,13 @@ __global__ void __launch_bounds__(kFaTcThreads, 1)
   unsigned char* const vls = vhs + kKBytes;
   unsigned char* const phs = vls + kKBytes;
   unsigned char* const pls = phs + kPBytes;
-  __shared__ __align__(8) unsigned long long kvbar, sbar, obar;
+  __shared__ __align__(8) unsigned long long kbar, vbar, sbar, obar;
   __shared__ unsigned tmem_base;
   const int h = blockIdx.x, tq0 = (gridDim.y - 1 - blockIdx.y) * kFaQ;
   const int tid = threadIdx.x, warp = tid >> 5;
   if (tid == 0) {
-    mbar_init(&kvbar, 1);
+    mbar_init(&kbar, 1);
+    mbar_init(&vbar, 1);
     mbar_init(&sbar, 1);
     mbar_init(&obar, 1);
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -618,47 +619,79 @@ __global__ void __launch_bounds__(kFaTcThreads, 1)
 #pragma unroll
   for (int e = 0; e < DK; ++e) o[e] = 0.0f;
   float m_run = -INFINITY, l_run = 0.0f;
-  bool ok = true;
-  // thread 0: copies and MMA commits issued and not yet waited for, with the parity of their phase
-  int kv_pending = -1, s_pending = -1, o_pending = -1;
-  for (int it = 0; it < tiles_n && ok; ++it) {
-    const unsigned par = static_cast<unsigned>(it) & 1u;
-    // this tile's keys and values (the previous tile's MMAs completed before its O_t was read)
-    if (tid == 0) {
-      const size_t block = (static_cast<size_t>(h) * head_tiles + it) * kKBytes;
-      mbar_expect_tx(&kvbar, 4u * kKBytes);
-      bulk_copy(khs, reinterpret_cast<const unsigned char*>(kh) + block, kKBytes, &kvbar);
-      bulk_copy(kls, reinterpret_cast<const unsigned char*>(kl) + block, kKBytes, &kvbar);
-      bulk_copy(vhs, reinterpret_cast<const unsigned char*>(vh) + block, kKBytes, &kvbar);
-      bulk_copy(vls, reinterpret_cast<const unsigned char*>(vl) + block, kKBytes, &kvbar);
-      kv_pending = static_cast<int>(par);
-    }
-    if (__syncthreads_or(!mbar_wait_bounded(&kvbar, par, timeout_ns))) {
-      ok = false;
-      break;
-    }
-    if (tid == 0) kv_pending = -1;
-    // S = Q K^T
-    if (tid == 0) {
-      tc_fence_after();
-      const unsigned qa = smem_addr(qhs), ql = smem_addr(qls), ka = smem_addr(khs), kb = smem_addr(kls);
-#pragma unroll
-      for (int kk = 0; kk < DK / 16; ++kk) {
-        const unsigned off = kk * 256;
-        umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, kk > 0);
-        umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(kb + off, cq * 128), kIdescS, true);
-        umma_f16_ss(tS, smem_desc(ql + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, true);
-      }
-      umma_commit(&sbar);
-      s_pending = static_cast<int>(par);
-    }
-    if (__syncthreads_or(!mbar_wait_bounded(&sbar, par, timeout_ns))) {
-      ok = false;
-      break;
-    }
-    if (tid == 0) s_pending = -1;
+  // Pipeline (thread 0 issues; every thread runs the softmax): the key tile of it + 1 is copied as soon
+  // as S(it) is done with the key buffer, the value tile of it + 1 as soon as O(it) is done with the
+  // value buffer, and S(it + 1) is issued right behind O(it), so the tensor pipe runs O(it) and S(it + 1)
+  // while the threads take O(it) out of TMEM. Thread 0 keeps the parity of every copy and commit it
+  // issued and has not waited for (-1: none), to drain them if a wait runs out.
+  int k_pend = -1, v_pend = -1, s_pend = -1, o_pend = -1;
+  const unsigned char* const khg = reinterpret_cast<const unsigned char*>(kh) + static_cast<size_t>(h) * head_tiles * kKBytes;
+  const unsigned char* const klg = reinterpret_cast<const unsigned char*>(kl) + static_cast<size_t>(h) * head_tiles * kKBytes;
+  const unsigned char* const vhg = reinterpret_cast<const unsigned char*>(vh) + static_cast<size_t>(h) * head_tiles * kKBytes;
+  const unsigned char* const vlg = reinterpret_cast<const unsigned char*>(vl) + static_cast<size_t>(h) * head_tiles * kKBytes;
+  auto issue_k = [&](int it) {
+    mbar_expect_tx(&kbar, 2u * kKBytes);
+    bulk_copy(khs, khg + static_cast<size_t>(it) * kKBytes, kKBytes, &kbar);
+    bulk_copy(kls, klg + static_cast<size_t>(it) * kKBytes, kKBytes, &kbar);
+    k_pend = it & 1;
+  };
+  auto issue_v = [&](int it) {
+    mbar_expect_tx(&vbar, 2u * kKBytes);
+    bulk_copy(vhs, vhg + static_cast<size_t>(it) * kKBytes, kKBytes, &vbar);
+    bulk_copy(vls, vlg + static_cast<size_t>(it) * kKBytes, kKBytes, &vbar);
+    v_pend = it & 1;
+  };
+  const unsigned qa = smem_addr(qhs), qb = smem_addr(qls), ka = smem_addr(khs), kb = smem_addr(kls);
+  const unsigned pa = smem_addr(phs), pb = smem_addr(pls), va = smem_addr(vhs), vb = smem_addr(vls);
+  auto issue_s = [&](int it) {  // S = Q K^T
     tc_fence_after();
-    // my score row, causally masked; online softmax; probabilities as the hi/lo A operand of P V
+#pragma unroll
+    for (int kk = 0; kk < DK / 16; ++kk) {
+      const unsigned off = kk * 256;
+      umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, kk > 0);
+      umma_f16_ss(tS, smem_desc(qa + off, cq * 128), smem_desc(kb + off, cq * 128), kIdescS, true);
+      umma_f16_ss(tS, smem_desc(qb + off, cq * 128), smem_desc(ka + off, cq * 128), kIdescS, true);
+    }
+    umma_commit(&sbar);
+    s_pend = it & 1;
+  };
+  auto issue_o = [&](int it) {  // O_t = P V
+    tc_fence_after();
+#pragma unroll
+    for (int kk = 0; kk < kFaKeys / 16; ++kk) {
+      const unsigned off = kk * 256;
+      umma_f16_ss(tO, smem_desc(pa + off), smem_desc(va + off), kIdescO, kk > 0);
+      umma_f16_ss(tO, smem_desc(pa + off), smem_desc(vb + off), kIdescO, true);
+      umma_f16_ss(tO, smem_desc(pb + off), smem_desc(va + off), kIdescO, true);
+    }
+    umma_commit(&obar);
+    o_pend = it & 1;
+  };
+  bool t0_ok = true;  // thread 0's own waits (the key and value copies)
+  if (tid == 0) {
+    issue_k(0);
+    issue_v(0);
+    t0_ok = mbar_wait_bounded(&kbar, 0u, timeout_ns);
+    if (t0_ok) {
+      k_pend = -1;
+      issue_s(0);
+    }
+  }
+  bool ok = true;
+  constexpr float kLog2e = 1.4426950408889634f;
+  for (int it = 0; it < tiles_n; ++it) {
+    const unsigned par = static_cast<unsigned>(it) & 1u;
+    if (__syncthreads_or((tid == 0 && !t0_ok) || !mbar_wait_bounded(&sbar, par, timeout_ns))) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    if (tid == 0) {
+      s_pend = -1;
+      if (it + 1 < tiles_n) issue_k(it + 1);  // S(it) is done with the key buffer
+    }
+    // my score row, causally masked; online softmax (exp2 of log2e-scaled differences); probabilities
+    // as the hi/lo A operand of P V (the previous P V finished with it)
     const int p0 = it * kFaKeys;
     float sc[kFaKeys];
     {
@@ -677,15 +710,16 @@ __global__ void __launch_bounds__(kFaTcThreads, 1)
       mx = fmaxf(mx, sc[j]);
     }
     const float m_new = fmaxf(m_run, mx);
-    const float corr = m_new == -INFINITY ? 1.0f : expf(m_run - m_new);
+    const float corr = m_new == -INFINITY ? 1.0f : exp2f((m_run - m_new) * kLog2e);
+    const float mb = m_new == -INFINITY ? 0.0f : m_new * kLog2e;
     float sum = 0.0f;
 #pragma unroll
     for (int c = 0; c < kFaKeys / 8; ++c) {
       uint32_t hw[4], lw[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const float e0 = m_new == -INFINITY ? 0.0f : expf(sc[8 * c + 2 * j] - m_new);
-        const float e1 = m_new == -INFINITY ? 0.0f : expf(sc[8 * c + 2 * j + 1] - m_new);
+        const float e0 = exp2f(fmaf(sc[8 * c + 2 * j], kLog2e, -mb));
+        const float e1 = exp2f(fmaf(sc[8 * c + 2 * j + 1], kLog2e, -mb));
         sum += e0 + e1;
         split2(e0, e1, hw[j], lw[j]);
       }
@@ -696,27 +730,30 @@ __global__ void __launch_bounds__(kFaTcThreads, 1)
     m_run = m_new;
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     tc_fence_before();
-    __syncthreads();
-    // O_t = P V
-    if (tid == 0) {
-      tc_fence_after();
-      const unsigned pa = smem_addr(phs), pb = smem_addr(pls), va = smem_addr(vhs), vb = smem_addr(vls);
-#pragma unroll
-      for (int kk = 0; kk < kFaKeys / 16; ++kk) {
-        const unsigned off = kk * 256;
-        umma_f16_ss(tO, smem_desc(pa + off), smem_desc(va + off), kIdescO, kk > 0);
-        umma_f16_ss(tO, smem_desc(pa + off), smem_desc(vb + off), kIdescO, true);
-        umma_f16_ss(tO, smem_desc(pb + off), smem_desc(va + off), kIdescO, true);
+    __syncthreads();  // P(it) written; every thread has read S(it)
+    if (tid == 0 && t0_ok) {
+      t0_ok = mbar_wait_bounded(&vbar, par, timeout_ns);  // V(it)
+      if (t0_ok) {
+        v_pend = -1;
+        issue_o(it);
+        if (it + 1 < tiles_n) {
+          t0_ok = mbar_wait_bounded(&kbar, (par ^ 1u), timeout_ns);  // K(it + 1)
+          if (t0_ok) {
+            k_pend = -1;
+            issue_s(it + 1);
+          }
+        }
       }
-      umma_commit(&obar);
-      o_pending = static_cast<int>(par);
     }
-    if (__syncthreads_or(!mbar_wait_bounded(&obar, par, timeout_ns))) {
+    if (__syncthreads_or((tid == 0 && !t0_ok) || !mbar_wait_bounded(&obar, par, timeout_ns))) {
       ok = false;
       break;
     }
-    if (tid == 0) o_pending = -1;
     tc_fence_after();
+    if (tid == 0) {
+      o_pend = -1;
+      if (it + 1 < tiles_n) issue_v(it + 1);  // O(it) is done with the value buffer
+    }
 #pragma unroll
     for (int c0 = 0; c0 < DK; c0 += 16) {
       uint32_t v[16];
@@ -725,16 +762,17 @@ __global__ void __launch_bounds__(kFaTcThreads, 1)
       for (int j = 0; j < 16; ++j) o[c0 + j] = fmaf(o[c0 + j], corr, __uint_as_float(v[j]));
     }
     tc_fence_before();
-    __syncthreads();  // S, O_t and the operand tiles are rewritten by the next tile
+    __syncthreads();  // every thread has read O(it) before O(it + 1) is issued
   }
   if (!ok) {
     if (tid == 0) {
       atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
       // let the copies and the tensor-core work this CTA issued finish before its shared and tensor
       // memory are released
-      if (kv_pending >= 0) mbar_wait_bounded(&kvbar, static_cast<unsigned>(kv_pending), timeout_ns);
-      if (s_pending >= 0) mbar_wait_bounded(&sbar, static_cast<unsigned>(s_pending), timeout_ns);
-      if (o_pending >= 0) mbar_wait_bounded(&obar, static_cast<unsigned>(o_pending), timeout_ns);
+      if (k_pend >= 0) mbar_wait_bounded(&kbar, static_cast<unsigned>(k_pend), timeout_ns);
+      if (v_pend >= 0) mbar_wait_bounded(&vbar, static_cast<unsigned>(v_pend), timeout_ns);
+      if (s_pend >= 0) mbar_wait_bounded(&sbar, static_cast<unsigned>(s_pend), timeout_ns);
+      if (o_pend >= 0) mbar_wait_bounded(&obar, static_cast<unsigned>(o_pend), timeout_ns);
     }
   } else if (t < count) {
     const float inv = 1.0f / l_run;
