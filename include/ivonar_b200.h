@@ -259,6 +259,24 @@ int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int3
                          const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
                          int64_t* history, int32_t history_len, const int32_t* step_counter, void* stream);
 
+/* Vocabulary-sharded sampling (tensor parallel, head rows split over the ranks). ivb_batch_topk_slice:
+ * per sequence, the top min(K, vloc) candidates of this rank's slice [v0, v0 + vloc) of the vocabulary
+ * (logits and repetition flags [batch][vloc]) by (score key desc, id asc), as the sampler's order-
+ * preserving score keys and global ids in slots [0, kc) of keys / ids [batch][kc], padded with key 0
+ * (kc >= min(max_top_k, vocab, 256)). ivb_batch_sample_merge: the gathered candidates of all ranks
+ * ([world][batch][kc], rank-major, ranks' slices in vocabulary order) merged by the unsharded sampler's
+ * selection, CDF and Philox draw, so every rank draws the token ivb_batch_sample would draw over the whole
+ * vocabulary; then history (at step_counter - 1), position += 1, and the repetition flag when the token
+ * lies in [v0, v0 + vloc). Replaces the replicated head + sampler of ternary.cu:374 (gemv_prequant_store)
+ * and :1099-1337 (sample_token). */
+int32_t ivb_batch_topk_slice(const float* logits, const uint8_t* seen, int32_t vloc, int32_t v0, int32_t vocab, int32_t batch,
+                             const float* sampling, const int64_t* top_k, int32_t max_top_k, int32_t kc, uint32_t* keys,
+                             int32_t* ids, void* stream);
+int32_t ivb_batch_sample_merge(const uint32_t* keys, const int32_t* ids, int32_t world, int32_t batch, int32_t kc, int32_t vocab,
+                               const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
+                               int64_t* history, int32_t history_len, const int32_t* step_counter, uint8_t* seen, int32_t v0,
+                               int32_t vloc, void* stream);
+
 /* Per-row max |x| (rows x n fp32) into amax [rows]; with ivb_quantize_rows_amax the quantisation of a
  * row-parallel shard uses the amax of the whole row (after an all-reduce MAX), so every shard's codes
  * equal the unsharded quantiser's: scale = max(amax / 127, act_eps), code = rint(x / scale). */

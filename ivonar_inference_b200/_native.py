@@ -167,6 +167,10 @@ SIGNATURES = {
                                 c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
     "ivb_batch_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
+    "ivb_batch_topk_slice": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32,
+                                       c_int32, c_void_p, c_void_p, c_void_p]),
+    "ivb_batch_sample_merge": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p,
+                                         c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p]),
     "ivb_rows_amax": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_void_p]),
     "ivb_quantize_rows_amax": (c_int32, [c_void_p, c_int32, c_int32, c_void_p, c_float, c_void_p, c_int32, c_void_p, c_void_p]),
     "ivb_decoder_check": (c_int32, [c_void_p, c_void_p]),

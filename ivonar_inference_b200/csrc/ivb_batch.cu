@@ -721,6 +721,74 @@ __global__ void __launch_bounds__(kThreads, 1) batch_sample_kernel(const float* 
   if (threadIdx.x == 0) positions[b] += 1;
 }
 
+// ---- vocabulary-sharded sampling (tensor parallel) ----------------------------------------------
+// The requested top-k as every sampler clamps it.
+__device__ __forceinline__ int sampler_k(const int64_t* top_k, int max_top_k, int vocab) {
+  const long long kreq = ldcg_i64(top_k);
+  const int cap = min(min(max_top_k, vocab), kMaxTopK);
+  return static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
+}
+
+// Sequence blockIdx.x, one rank's vocabulary slice [v0, v0 + vloc): the scores of its logits and
+// repetition flags (the sampler's keys), their top min(K, vloc) by (key desc, index asc) into slots
+// [0, kc) of keys / ids (global ids), the rest padded with key 0, below every score.
+__global__ void __launch_bounds__(kThreads, 1) batch_topk_slice_kernel(const float* logits, const uint8_t* seen, int vloc, int v0,
+                                                                       int vocab, const float* sampling, const int64_t* top_k,
+                                                                       int max_top_k, int kc, unsigned* keys, int* ids) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  SampleSmem sm;
+  carve_sample(smem, vloc, sm);
+  const int b = blockIdx.x, tid = threadIdx.x;
+  const float* lg = logits + static_cast<size_t>(b) * vloc;
+  const uint8_t* fl = seen + static_cast<size_t>(b) * vloc;
+  const float inv_t = 1.0f / __ldcg(sampling);
+  const float pen = __ldcg(sampling + 1), ipen = __ldcg(sampling + 2);
+  for (int i = tid; i < vloc; i += kThreads) sm.keys[i] = score_key(__ldcg(lg + i), __ldcg(fl + i), inv_t, pen, ipen);
+  __syncthreads();
+  const int kl = min(sampler_k(top_k, max_top_k, vocab), vloc);
+  select_topk(sm, vloc, kl);
+  for (int r = tid; r < kc; r += kThreads) {
+    keys[static_cast<size_t>(b) * kc + r] = r < kl ? sm.hist[r] : 0u;
+    ids[static_cast<size_t>(b) * kc + r] = r < kl ? v0 + static_cast<int>(sm.hist[kMaxTopK + r]) : vocab + r;
+  }
+}
+
+// Sequence blockIdx.x: the candidates of all ranks ([world][batch][kc], rank-major, each rank's list in
+// (key desc, id asc) order, so the position order of equal keys is their id order) merged by the same
+// selection and draw as the unsharded sampler, which therefore picks the same token; then history,
+// position, and the repetition flag when the token lies in this rank's slice [v0, v0 + vloc).
+__global__ void __launch_bounds__(kThreads, 1) batch_merge_sample_kernel(const unsigned* keys, const int* ids, int world, int batch,
+                                                                         int kc, int vocab, const int64_t* top_k, int max_top_k,
+                                                                         uint64_t* rng, int64_t* tokens, int64_t* positions,
+                                                                         int64_t* history, int history_len,
+                                                                         const int32_t* step_counter, uint8_t* seen, int v0,
+                                                                         int vloc) {
+  extern __shared__ __align__(16) unsigned char smem[];
+  const int n = world * kc;
+  SampleSmem sm;
+  carve_sample(smem, n, sm);
+  int* cid = reinterpret_cast<int*>(smem + sample_smem_bytes(n));
+  const int b = blockIdx.x, tid = threadIdx.x;
+  for (int i = tid; i < n; i += kThreads) {
+    const int r = i / kc, j = i - r * kc;
+    const size_t src = (static_cast<size_t>(r) * batch + b) * kc + j;
+    sm.keys[i] = keys[src];
+    cid[i] = ids[src];
+  }
+  __syncthreads();
+  const int K = sampler_k(top_k, max_top_k, vocab);
+  select_topk(sm, n, K);
+  const int chosen = draw_sorted(sm, K, rng + 2 * b);
+  if (tid == 0) {
+    const int token = cid[sm.hist[kMaxTopK + chosen]];
+    tokens[b] = token;
+    const int step = step_counter != nullptr ? *step_counter - 1 : -1;  // advanced by this step's embedding kernel
+    if (history != nullptr && step >= 0 && step < history_len) history[static_cast<size_t>(b) * history_len + step] = token;
+    if (token >= v0 && token < v0 + vloc) seen[static_cast<size_t>(b) * vloc + (token - v0)] = 1;
+    positions[b] += 1;
+  }
+}
+
 // One CTA per sequence (a warp per head, the latent tiles shared) when there are enough sequences to fill
 // the SMs and the heads fit in one CTA; else one CTA per (sequence, head), more parallel for few sequences.
 int32_t launch_batch_attention(const IvbLayerDesc& L, const IvbBatchLayer& BL, const float* ent, int ld, const int64_t* positions,
@@ -919,6 +987,38 @@ int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int3
   IVB_CUDA(cudaFuncSetAttribute(batch_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   batch_sample_kernel<<<batch, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
       logits, seen, vocab, sampling, top_k, max_top_k, rng, tokens, positions, history, history_len, step_counter);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_batch_topk_slice(const float* logits, const uint8_t* seen, int32_t vloc, int32_t v0, int32_t vocab, int32_t batch,
+                             const float* sampling, const int64_t* top_k, int32_t max_top_k, int32_t kc, uint32_t* keys,
+                             int32_t* ids, void* stream) {
+  using namespace ivb;
+  if (logits == nullptr || seen == nullptr || sampling == nullptr || top_k == nullptr || keys == nullptr || ids == nullptr ||
+      batch <= 0 || vloc <= 0 || v0 < 0 || v0 + vloc > vocab || kc < std::min(std::min(max_top_k, vocab), kMaxTopK) || kc <= 0)
+    return fail(IVB_EINVAL, "ivb_batch_topk_slice: bad argument");
+  const size_t smem = sample_smem_bytes(vloc);
+  IVB_CUDA(cudaFuncSetAttribute(batch_topk_slice_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  batch_topk_slice_kernel<<<batch, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(logits, seen, vloc, v0, vocab, sampling,
+                                                                                         top_k, max_top_k, kc, keys, ids);
+  IVB_CUDA(cudaGetLastError());
+  return IVB_OK;
+}
+
+int32_t ivb_batch_sample_merge(const uint32_t* keys, const int32_t* ids, int32_t world, int32_t batch, int32_t kc, int32_t vocab,
+                               const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
+                               int64_t* history, int32_t history_len, const int32_t* step_counter, uint8_t* seen, int32_t v0,
+                               int32_t vloc, void* stream) {
+  using namespace ivb;
+  if (keys == nullptr || ids == nullptr || top_k == nullptr || rng == nullptr || tokens == nullptr || positions == nullptr ||
+      seen == nullptr || world <= 0 || batch <= 0 || kc <= 0 || vocab <= 0 || vloc <= 0 || v0 < 0 || v0 + vloc > vocab)
+    return fail(IVB_EINVAL, "ivb_batch_sample_merge: bad argument");
+  const size_t smem = sample_smem_bytes(world * kc) + static_cast<size_t>(world) * kc * 4;
+  IVB_CUDA(cudaFuncSetAttribute(batch_merge_sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
+  batch_merge_sample_kernel<<<batch, kThreads, smem, static_cast<cudaStream_t>(stream)>>>(
+      keys, ids, world, batch, kc, vocab, top_k, max_top_k, rng, tokens, positions, history, history_len, step_counter, seen, v0,
+      vloc);
   IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }

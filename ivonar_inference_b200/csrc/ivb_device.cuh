@@ -935,44 +935,11 @@ static __device__ int radix_digit(const SampleSmem& sm, const unsigned* keys, in
   return bin;
 }
 
-static __device__ void sample_block(const float* logits, uint8_t* seen, int vocab, const float* sampling, const int64_t* top_k_ptr,
-                                    int max_top_k, uint64_t* rng, int64_t* token, int64_t* history, const SampleSmem& sm,
-                                    unsigned long long* marks = nullptr) {
+// The K best of keys[0, n) (sm.keys) by (key desc, index asc): sm.hist[r] gets the key of rank r and
+// sm.hist[kMaxTopK + r] its index. Radix select of the K-th largest key (first digit over all keys, the
+// rest over a compact list when the selected bin fits), then a gather and a rank-by-counting order.
+static __device__ void select_topk(const SampleSmem& sm, int vocab, int K, unsigned long long* marks = nullptr) {
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const float inv_t = 1.0f / __ldcg(sampling);
-  const float pen = __ldcg(sampling + 1), ipen = __ldcg(sampling + 2);
-  const long long kreq = ldcg_i64(top_k_ptr);
-  const int cap = min(min(max_top_k, vocab), kMaxTopK);
-  const int K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
-  // scores -> order-preserving keys, four logits and flags per load, four loads in flight
-  const int n4 = vocab >> 2;
-  const float4* l4 = reinterpret_cast<const float4*>(logits);
-  const uchar4* f4 = reinterpret_cast<const uchar4*>(seen);
-  for (int base = 0; base < n4; base += 4 * kThreads) {
-    float4 lv[4];
-    uchar4 fv[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int q = base + tid + u * kThreads;
-      if (q < n4) {
-        lv[u] = __ldcg(l4 + q);
-        fv[u] = __ldcg(f4 + q);
-      }
-    }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int q = base + tid + u * kThreads;
-      if (q < n4) {
-        sm.keys[4 * q] = score_key(lv[u].x, fv[u].x, inv_t, pen, ipen);
-        sm.keys[4 * q + 1] = score_key(lv[u].y, fv[u].y, inv_t, pen, ipen);
-        sm.keys[4 * q + 2] = score_key(lv[u].z, fv[u].z, inv_t, pen, ipen);
-        sm.keys[4 * q + 3] = score_key(lv[u].w, fv[u].w, inv_t, pen, ipen);
-      }
-    }
-  }
-  for (int i = 4 * n4 + tid; i < vocab; i += kThreads) sm.keys[i] = score_key(__ldcg(logits + i), __ldcg(seen + i), inv_t, pen, ipen);
-  __syncthreads();
-  mark(marks, 1);
   // radix select of the K-th largest key: first digit over all keys, the rest over a compact list
   unsigned prefix = 0u, mask = 0u;
   int remaining = K;
@@ -1056,6 +1023,14 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
   }
   __syncthreads();
   mark(marks, 5);
+}
+
+// The Philox draw over the K candidates that select_topk ordered: probabilities exp(v - top) of their
+// scores, the canonical CDF (per 32-chunk inclusive scan, chunk carries added in order) and the count of
+// CDF entries at or below u * total. Returns the chosen rank (the same in every thread); thread 0
+// advances the draw counter rng[1].
+static __device__ int draw_sorted(const SampleSmem& sm, int K, uint64_t* rng, unsigned long long* marks = nullptr) {
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const float top = key_value(sm.hist[0]);
   for (int c = tid; c < K; c += kThreads) sm.cprob[c] = sample_exp(key_value(sm.hist[c]) - top);
   __syncthreads();
@@ -1082,8 +1057,52 @@ static __device__ void sample_block(const float* logits, uint8_t* seen, int voca
   float below = 0.0f;  // number of candidates whose cdf <= target (cdf is non-decreasing)
   for (int c = tid; c < K; c += kThreads) below += sm.cprob[c] <= target ? 1.0f : 0.0f;
   const int chosen = min(static_cast<int>(block_sum(below, sm.red)), K - 1);
+  __syncthreads();  // every thread has read the draw counter
+  if (tid == 0) rng[1] = ctr + 1;
+  return chosen;
+}
+
+static __device__ void sample_block(const float* logits, uint8_t* seen, int vocab, const float* sampling, const int64_t* top_k_ptr,
+                                    int max_top_k, uint64_t* rng, int64_t* token, int64_t* history, const SampleSmem& sm,
+                                    unsigned long long* marks = nullptr) {
+  const int tid = threadIdx.x;
+  const float inv_t = 1.0f / __ldcg(sampling);
+  const float pen = __ldcg(sampling + 1), ipen = __ldcg(sampling + 2);
+  const long long kreq = ldcg_i64(top_k_ptr);
+  const int cap = min(min(max_top_k, vocab), kMaxTopK);
+  const int K = static_cast<int>(kreq < 1 ? 1 : (kreq > cap ? cap : kreq));
+  // scores -> order-preserving keys, four logits and flags per load, four loads in flight
+  const int n4 = vocab >> 2;
+  const float4* l4 = reinterpret_cast<const float4*>(logits);
+  const uchar4* f4 = reinterpret_cast<const uchar4*>(seen);
+  for (int base = 0; base < n4; base += 4 * kThreads) {
+    float4 lv[4];
+    uchar4 fv[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = base + tid + u * kThreads;
+      if (q < n4) {
+        lv[u] = __ldcg(l4 + q);
+        fv[u] = __ldcg(f4 + q);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int q = base + tid + u * kThreads;
+      if (q < n4) {
+        sm.keys[4 * q] = score_key(lv[u].x, fv[u].x, inv_t, pen, ipen);
+        sm.keys[4 * q + 1] = score_key(lv[u].y, fv[u].y, inv_t, pen, ipen);
+        sm.keys[4 * q + 2] = score_key(lv[u].z, fv[u].z, inv_t, pen, ipen);
+        sm.keys[4 * q + 3] = score_key(lv[u].w, fv[u].w, inv_t, pen, ipen);
+      }
+    }
+  }
+  for (int i = 4 * n4 + tid; i < vocab; i += kThreads) sm.keys[i] = score_key(__ldcg(logits + i), __ldcg(seen + i), inv_t, pen, ipen);
+  __syncthreads();
+  mark(marks, 1);
+  select_topk(sm, vocab, K, marks);
+  const int chosen = draw_sorted(sm, K, rng, marks);
   if (tid == 0) {
-    rng[1] = ctr + 1;
     const int index = static_cast<int>(sm.hist[kMaxTopK + chosen]);
     *token = index;
     if (history != nullptr) *history = index;

@@ -14,9 +14,12 @@ row-parallel. Per block and step:
 The all-reduces are NCCL collectives over NVLink (torch.distributed, backend "nccl") on the stream
 the kernels run on; the global amax keeps every shard's activation codes equal to the unsharded
 quantiser's, so a sharded step differs from one GPU's only in the order of the fp32 partial sums.
-The embedding and the head are replicated and every rank samples the same tokens (same seeds).
-The kernels are the batched decode's unit steps (`ivb_batch_*`, `ivb_ternary_gemm`,
-`ivb_quantize_rows[_amax]`). Prompts run through the same step teacher-forced, one token per step.
+The embedding is replicated; the head is sharded by vocabulary rows: each rank computes the logits of
+its slice and their top-k candidates (`ivb_batch_topk_slice`), an NCCL all-gather brings every rank's
+candidates to every rank, and each rank runs the same merge and Philox draw (`ivb_batch_sample_merge`),
+so all ranks sample the token the unsharded sampler would (same seeds). The kernels are the batched
+decode's unit steps (`ivb_batch_*`, `ivb_ternary_gemm`, `ivb_quantize_rows[_amax]`). Prompts run through
+the same step teacher-forced, one token per step.
 """
 
 from __future__ import annotations
@@ -107,7 +110,14 @@ class B200TensorParallel:
         self.ffn_local = f1 - f0
         if self.ffn_local <= 0:
             raise ValueError(f"{first.in_features} FFN inputs do not fill {world} shards of 128-input groups")
-        self.head = DeviceMatrix([model.token_io.projection], dev)
+        self.head = DeviceMatrix([model.token_io.projection], dev)  # the embedding rows (replicated)
+        # this rank's vocabulary slice of the head (rows in 128-row units, so the slices tile the GEMM)
+        self.v_range = split_even(self.vocab, world, 128)[rank]
+        v0, v1 = self.v_range
+        self.vloc = v1 - v0
+        if self.vloc <= 0:
+            raise ValueError(f"{self.vocab} vocabulary rows do not fill {world} shards of 128 rows")
+        self.head_shard = DeviceMatrix([row_slice(model.token_io.projection, v0, v1)], dev)
         self.final_norm = model.final_norm.weight.float().to(dev).contiguous()
         self.final_eps = float(model.final_norm.eps)
         self.act_eps = float(getattr(model.token_io.projection, "eps", 1e-5))
@@ -200,8 +210,14 @@ class B200TensorParallel:
         self.h = torch.zeros(B, self.ffn_local, **f32)
         self.q8 = torch.zeros(rows128, ldq, dtype=torch.int8, device=dev)
         self.act_scale, self.amax = torch.zeros(B, **f32), torch.zeros(B, **f32)
-        self.logits = torch.zeros(B, self.vocab, **f32)
-        self.seen = torch.zeros(B, self.vocab, dtype=torch.uint8, device=dev)
+        self.logits = torch.zeros(B, self.vloc, **f32)  # this rank's slice
+        self.seen = torch.zeros(B, self.vloc, dtype=torch.uint8, device=dev)
+        # sampler candidates: this rank's top-k per sequence, and every rank's after the all-gather
+        self.kc = max(2, min(self.max_top_k, self.vocab, 256))
+        self.cand_keys = torch.zeros(B, self.kc, dtype=torch.int32, device=dev)
+        self.cand_ids = torch.zeros(B, self.kc, dtype=torch.int32, device=dev)
+        self.all_keys = torch.zeros(world, B, self.kc, dtype=torch.int32, device=dev)
+        self.all_ids = torch.zeros(world, B, self.kc, dtype=torch.int32, device=dev)
         self.tokens = torch.zeros(B, dtype=torch.int64, device=dev)
         self.positions = torch.zeros(B, dtype=torch.int64, device=dev)
         self.rng = torch.zeros(B, 2, dtype=torch.int64, device=dev)
@@ -237,6 +253,28 @@ class B200TensorParallel:
         native.check(self.lib.ivb_quantize_rows_amax(x.data_ptr(), self.batch, n, self.amax.data_ptr(), self.act_eps,
                                                      self.q8.data_ptr(), ldq, self.act_scale.data_ptr(), self._stream()),
                      "ivb_quantize_rows_amax")
+
+    def _sample(self, history: bool) -> None:
+        """Every rank draws the same token per sequence from the candidates of all vocabulary slices."""
+
+        st = self._stream()
+        v0 = self.v_range[0]
+        native.check(self.lib.ivb_batch_topk_slice(self.logits.data_ptr(), self.seen.data_ptr(), self.vloc, v0, self.vocab,
+                                                   self.batch, self.sampling.data_ptr(), self.top_k.data_ptr(),
+                                                   self.max_top_k, self.kc, self.cand_keys.data_ptr(),
+                                                   self.cand_ids.data_ptr(), st), "ivb_batch_topk_slice")
+        if self.world > 1:
+            torch.distributed.all_gather_into_tensor(self.all_keys, self.cand_keys, group=self.group)
+            torch.distributed.all_gather_into_tensor(self.all_ids, self.cand_ids, group=self.group)
+        else:
+            self.all_keys[0].copy_(self.cand_keys)
+            self.all_ids[0].copy_(self.cand_ids)
+        native.check(self.lib.ivb_batch_sample_merge(
+            self.all_keys.data_ptr(), self.all_ids.data_ptr(), self.world, self.batch, self.kc, self.vocab,
+            self.top_k.data_ptr(), self.max_top_k, self.rng.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
+            self.history.data_ptr() if history else None, self.history.shape[1] if history else 0,
+            self.step_counter.data_ptr() if history else None, self.seen.data_ptr(), v0, self.vloc, st),
+            "ivb_batch_sample_merge")
 
     def _gemm(self, m: DeviceMatrix, epilogue: int, out: Tensor, ldo: int) -> None:
         desc = m.desc()
@@ -288,13 +326,9 @@ class B200TensorParallel:
             self._quant_shard(self.h, self.ffn_local)
             self._row_parallel(layer["down"])
         self._quant(self.resid, self.hidden, self.final_norm.data_ptr(), self.final_eps)
-        self._gemm(self.head, native.IVB_EPI_STORE, self.logits, self.vocab)
+        self._gemm(self.head_shard, native.IVB_EPI_STORE, self.logits, self.vloc)
         if sample:
-            rc = self.lib.ivb_batch_sample(self.logits.data_ptr(), self.seen.data_ptr(), self.vocab, self.batch,
-                                           self.sampling.data_ptr(), self.top_k.data_ptr(), self.max_top_k,
-                                           self.rng.data_ptr(), self.tokens.data_ptr(), self.positions.data_ptr(),
-                                           self.history.data_ptr(), self.history.shape[1], self.step_counter.data_ptr(), st)
-            native.check(rc, "ivb_batch_sample")
+            self._sample(history=True)
         else:
             self.positions.add_(1)
         self.host_position += 1
@@ -320,10 +354,7 @@ class B200TensorParallel:
         self.rng[:, 0] = torch.as_tensor([int(s) for s in seeds], dtype=torch.int64, device=self.device)
         self.rng[:, 1] = 0
         # the first sampled token comes from the prompt's last logits
-        rc = self.lib.ivb_batch_sample(self.logits.data_ptr(), self.seen.data_ptr(), self.vocab, self.batch,
-                                       self.sampling.data_ptr(), self.top_k.data_ptr(), self.max_top_k, self.rng.data_ptr(),
-                                       self.tokens.data_ptr(), self.positions.data_ptr(), None, 0, None, self._stream())
-        native.check(rc, "ivb_batch_sample")
+        self._sample(history=False)
         self.positions.sub_(1)  # the sampler advanced the position; the sampled token is fed at the same slot
 
     @torch.no_grad()

@@ -86,3 +86,66 @@ def test_shards_reassemble_the_unsharded_products_over_gloo() -> None:
     result = manager.dict()
     mp.start_processes(_worker, args=(2, port, result), nprocs=2, join=True, start_method="spawn")
     assert result["down"] < 1e-9 and result["gate"] < 1e-9 and result["out"] < 1e-9, dict(result)
+
+
+def _topk_order(keys: torch.Tensor, ids: torch.Tensor, k: int) -> tuple[torch.Tensor, torch.Tensor]:
+    """The k best (key desc, id asc), as the samplers order their candidates."""
+    order = sorted(range(keys.numel()), key=lambda i: (-float(keys[i]), int(ids[i])))[:k]
+    return keys[order], ids[order]
+
+
+def _vocab_worker(rank: int, world: int, port: int, result) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from ivonar_inference_b200.tp import split_even
+
+        vocab, k, batch = 700, 40, 3
+        gen = torch.Generator().manual_seed(7)
+        # scores with many exact ties (rounded), the same on every rank
+        scores = torch.round(torch.randn(batch, vocab, generator=gen, dtype=torch.float64) * 4.0) / 4.0
+        ranges = split_even(vocab, world, 128)
+        v0, v1 = ranges[rank]
+        kc = k
+        keys = torch.full((batch, kc), -1e30, dtype=torch.float64)
+        ids = torch.zeros(batch, kc, dtype=torch.int64)
+        for b in range(batch):
+            local = scores[b, v0:v1]
+            kk, ii = _topk_order(local, torch.arange(v0, v1), min(k, v1 - v0))
+            keys[b, : kk.numel()], ids[b, : ii.numel()] = kk, ii
+            ids[b, ii.numel():] = vocab + torch.arange(kc - ii.numel())
+        all_keys = [torch.zeros_like(keys) for _ in range(world)]
+        all_ids = [torch.zeros_like(ids) for _ in range(world)]
+        dist.all_gather(all_keys, keys)
+        dist.all_gather(all_ids, ids)
+        # rank-major candidates: equal keys appear in id order, so ranking them by position (as the merge
+        # kernel does) ranks them by id
+        ok = True
+        for b in range(batch):
+            ck = torch.cat([a[b] for a in all_keys])
+            ci = torch.cat([a[b] for a in all_ids])
+            pos = torch.arange(ck.numel())
+            mk, mp = _topk_order(ck, pos, k)
+            gk, gi = _topk_order(scores[b], torch.arange(vocab), k)
+            ok = ok and torch.equal(mk, gk) and torch.equal(ci[mp], gi)
+        if rank == 0:
+            result["ok"] = bool(ok)
+            result["ranges"] = ranges
+    finally:
+        dist.destroy_process_group()
+
+
+def test_vocabulary_shards_merge_to_the_unsharded_top_k_over_gloo() -> None:
+    """The sharded head's sampler plan (tp.py, ivb_batch_topk_slice + ivb_batch_sample_merge): per-slice
+    top-k candidates, gathered rank-major and merged by position, give the unsharded top-k with its id
+    order among equal scores."""
+    import socket
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    manager = mp.get_context("spawn").Manager()
+    result = manager.dict()
+    mp.start_processes(_vocab_worker, args=(2, port, result), nprocs=2, join=True, start_method="spawn")
+    assert result["ok"], dict(result)
+    assert result["ranges"] == [(0, 384), (384, 700)]
