@@ -75,10 +75,10 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-batch", action="store_true")
     ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks) at N=1")
     ap.add_argument("--no-tp", action="store_true", help="skip config 4, which runs by default on more than one GPU")
-    ap.add_argument("--only", choices=("prefill", "gemm", "tp", "batch"), default=None,
+    ap.add_argument("--only", choices=("prefill", "gemm", "tp", "batch", "ingest"), default=None,
                     help="run one secondary measurement alone (for profiler captures): a prefill of "
                          "--prefill-tokens tokens, the prefill GEMM on the gate/up shape, config 4, or "
-                         "config 3 (--batch-tokens decode tokens per sequence)")
+                         "config 3 (--batch-tokens decode tokens per sequence), or the checkpoint load")
     ap.add_argument("--prefill-tokens", type=int, default=2048)
     ap.add_argument("--batch-tokens", type=int, default=512, help="decode tokens per sequence of --only batch")
     ap.add_argument("--kernel-table", action="store_true", help="--only batch: per-kernel device time of a step")
@@ -513,6 +513,53 @@ def tp_measure(device, world: int, rank: int) -> dict:
     return out
 
 
+def ingest_measure(device, reps: int) -> dict:
+    """Checkpoint load of config 1 (packed, on local disk, in the page cache after one untimed load):
+    the reference's load_model to the GPU and ingest.load_model, wall clock with the device synchronised
+    (median of `reps`), and the one-launch device validation alone (CUDA events)."""
+    import torch
+
+    from ivonar_inference_b200 import _reference, ingest, synthetic
+
+    loader = _reference.module("loader")
+    payload = synthetic.config1(seq_len=PROMPT + TOKENS + 16)
+    state = {k: v.cpu() for k, v in synthetic.synthetic_state(payload, 0, "fast").items()}
+    checked = {k: v for k, v in state.items() if k.endswith((".packed_weight", ".weight_scales"))}
+    checked_bytes = sum(v.numel() * v.element_size() for v in checked.values())
+    out: dict = {"metric": "checkpoint load ms, config 1", "unit": "ms", "reps": reps}
+    with tempfile.TemporaryDirectory() as tmp:
+        path = Path(tmp) / "packed_inference_checkpoint.pt"
+        torch.save({"format": loader.PACKED_FORMAT, "schema_version": loader.PACKED_SCHEMA_VERSION,
+                    "config": payload, "model_state": state}, path)
+        out["file_bytes"] = path.stat().st_size
+        for name, load in (("reference", loader.load_model), ("b200", ingest.load_model)):
+            times = []
+            for i in range(reps + 1):
+                torch.cuda.synchronize(device)
+                t0 = time.perf_counter()
+                loaded = load(path, device, materialize=False)
+                torch.cuda.synchronize(device)
+                if i:
+                    times.append((time.perf_counter() - t0) * 1000.0)
+                del loaded
+            out[name] = {"ms": statistics.median(times), "min_ms": min(times)}
+    on_device = {k: v.to(device) for k, v in checked.items()}
+    ingest.validate_state_device(on_device, device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(reps):
+        ingest.validate_state_device(on_device, device)
+    end.record()
+    torch.cuda.synchronize(device)
+    ms = start.elapsed_time(end) / reps
+    peak, peak_kind = measured_peaks()
+    out["validate"] = {"buffers": len(checked), "bytes": checked_bytes, "ms": ms,
+                       "gbs": checked_bytes / (ms / 1000.0) / 1e9, "peak_gbs": peak, "peak_kind": peak_kind,
+                       "note": "per call: descriptor copy, one launch, one synchronising read of 12 bytes"}
+    out["speedup"] = out["reference"]["ms"] / out["b200"]["ms"]
+    return out
+
+
 def run_b200(args) -> None:
     import torch
     import torch.distributed as dist
@@ -679,6 +726,8 @@ def main() -> None:
         device = torch.device("cuda", 0)
         if args.only == "prefill":
             print(json.dumps(prefill_measure(device, lengths=((args.prefill_tokens, args.steps),), gemm_reps=0)), flush=True)
+        elif args.only == "ingest":
+            print(json.dumps(ingest_measure(device, args.steps)), flush=True)
         elif args.only == "batch":
             r = batch_measure(device, 1, 0, tokens=args.batch_tokens, kernel_table=args.kernel_table)
             r["tok_s"] = r["sequences_per_gpu"] * r["steps"] / (r["ms"] / 1000.0)

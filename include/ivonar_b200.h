@@ -259,6 +259,23 @@ int32_t ivb_batch_sample(const float* logits, uint8_t* seen, int32_t vocab, int3
                          const int64_t* top_k, int32_t max_top_k, uint64_t* rng, int64_t* tokens, int64_t* positions,
                          int64_t* history, int32_t history_len, const int32_t* step_counter, void* stream);
 
+/* Checkpoint ingest: validation of a checkpoint's packed buffers once they are on the device, in one
+ * launch (replaces the reference loader's chunked CPU checks, loader.py:94-112). Each buffer is a packed
+ * ternary weight array (uint8, kind IVB_CHECK_PACKED: the reserved 2-bit code 3 is an error) or a g128
+ * scale array (fp16, kind IVB_CHECK_SCALES: every scale finite and positive). `buffers` is a device
+ * array of `count` descriptors; bad[0..2] (device int32) receive the lowest index of a buffer holding
+ * code 3, a non-finite scale, a non-positive scale, or `count` when none does. Asynchronous on
+ * `stream` (the caller reads bad after synchronising). */
+#define IVB_CHECK_PACKED 0
+#define IVB_CHECK_SCALES 1
+typedef struct IvbCheckBuffer {
+  const void* data;
+  int64_t count;              /* bytes (packed) or fp16 values (scales) */
+  int32_t kind;               /* IVB_CHECK_PACKED or IVB_CHECK_SCALES */
+  int32_t pad;
+} IvbCheckBuffer;
+int32_t ivb_validate_buffers(const IvbCheckBuffer* buffers, int32_t count, int32_t* bad, void* stream);
+
 /* Vocabulary-sharded sampling (tensor parallel, head rows split over the ranks). ivb_batch_topk_slice:
  * per sequence, the top min(K, vloc) candidates of this rank's slice [v0, v0 + vloc) of the vocabulary
  * (logits and repetition flags [batch][vloc]) by (score key desc, id asc), as the sampler's order-

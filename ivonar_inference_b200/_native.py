@@ -10,7 +10,7 @@ from __future__ import annotations
 import ctypes
 import glob
 import os
-from ctypes import POINTER, Structure, c_char_p, c_float, c_int32, c_uint64, c_void_p
+from ctypes import POINTER, Structure, c_char_p, c_float, c_int32, c_int64, c_uint64, c_void_p
 from pathlib import Path
 
 PACKAGE = Path(__file__).resolve().parent
@@ -37,6 +37,14 @@ class IvbTernary(Structure):
         ("row_bytes", c_int32),
         ("scale_stride", c_int32),
     ]
+
+
+IVB_CHECK_PACKED = 0
+IVB_CHECK_SCALES = 1
+
+
+class IvbCheckBuffer(Structure):
+    _fields_ = [("data", c_void_p), ("count", c_int64), ("kind", c_int32), ("pad", c_int32)]
 
 
 class IvbLayerDesc(Structure):
@@ -167,6 +175,7 @@ SIGNATURES = {
                                 c_int32, c_int32, c_int32, c_int32, c_int32, c_int32, c_float, c_void_p, c_void_p, c_void_p]),
     "ivb_batch_sample": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_void_p,
                                    c_void_p, c_void_p, c_int32, c_void_p, c_void_p]),
+    "ivb_validate_buffers": (c_int32, [c_void_p, c_int32, c_void_p, c_void_p]),
     "ivb_batch_topk_slice": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_void_p, c_int32,
                                        c_int32, c_void_p, c_void_p, c_void_p]),
     "ivb_batch_sample_merge": (c_int32, [c_void_p, c_void_p, c_int32, c_int32, c_int32, c_int32, c_void_p, c_int32, c_void_p,

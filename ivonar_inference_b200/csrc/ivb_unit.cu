@@ -142,6 +142,48 @@ __global__ void probe_wait_kernel(unsigned* counter, unsigned* error_word, unsig
   grid_barrier(s, 2u, &flag);
 }
 
+
+// ---- checkpoint ingest: validation of the packed buffers on the device ---------------------------
+// Grid (blocks, buffers). Packed ternary bytes: a 2-bit field holding the reserved code 3 has both of its
+// bits set, so (b & (b >> 1) & 0x55) != 0 finds it (loader.py:94-112); fp16 scales must be finite
+// (exponent field not all ones) and positive (sign clear, not zero). The lowest offending buffer index
+// per test goes to bad[0] (code 3), bad[1] (not finite), bad[2] (not positive) by atomicMin.
+// bad[0..2] = count: "no buffer failed" for each of the three checks.
+__global__ void validate_init_kernel(int32_t* bad, int32_t count) {
+  if (threadIdx.x < 3) bad[threadIdx.x] = count;
+}
+
+__global__ void validate_buffers_kernel(const IvbCheckBuffer* bufs, int32_t* bad) {
+  const IvbCheckBuffer b = bufs[blockIdx.y];
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  const long long i0 = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  bool code3 = false, nonfinite = false, nonpositive = false;
+  if (b.kind == IVB_CHECK_PACKED) {
+    const unsigned char* q = static_cast<const unsigned char*>(b.data);
+    const long long n16 = (reinterpret_cast<uintptr_t>(q) & 15) == 0 ? b.count / 16 : 0;
+    const uint4* q4 = reinterpret_cast<const uint4*>(q);
+    for (long long i = i0; i < n16; i += stride) {
+      const uint4 v = __ldg(q4 + i);
+      const unsigned m = (v.x & (v.x >> 1)) | (v.y & (v.y >> 1)) | (v.z & (v.z >> 1)) | (v.w & (v.w >> 1));
+      code3 |= (m & 0x55555555u) != 0u;
+    }
+    for (long long i = 16 * n16 + i0; i < b.count; i += stride) {
+      const unsigned v = __ldg(q + i);
+      code3 |= (v & (v >> 1) & 0x55u) != 0u;
+    }
+  } else {
+    const unsigned short* h = static_cast<const unsigned short*>(b.data);
+    for (long long i = i0; i < b.count; i += stride) {
+      const unsigned v = __ldg(h + i);
+      nonfinite |= (v & 0x7C00u) == 0x7C00u;
+      nonpositive |= (v & 0x8000u) != 0u || (v & 0x7FFFu) == 0u;
+    }
+  }
+  if (__syncthreads_or(code3) && threadIdx.x == 0) atomicMin(bad, static_cast<int32_t>(blockIdx.y));
+  if (__syncthreads_or(nonfinite) && threadIdx.x == 0) atomicMin(bad + 1, static_cast<int32_t>(blockIdx.y));
+  if (__syncthreads_or(nonpositive) && threadIdx.x == 0) atomicMin(bad + 2, static_cast<int32_t>(blockIdx.y));
+}
+
 }  // namespace ivb
 
 size_t ivb_sample_smem_bytes(int vocab) { return ivb::sample_smem_bytes(vocab); }
@@ -246,6 +288,17 @@ int32_t ivb_probe_wait_timeout(uint32_t* counter, uint32_t* error_word, uint64_t
   uint32_t word = 0;
   IVB_CUDA(cudaMemcpy(&word, error_word, sizeof(word), cudaMemcpyDeviceToHost));
   if (word != 0) return fail(static_cast<int32_t>(word), "bounded wait gave up (device error word %u)", word);
+  return IVB_OK;
+}
+
+int32_t ivb_validate_buffers(const IvbCheckBuffer* buffers, int32_t count, int32_t* bad, void* stream) {
+  using namespace ivb;
+  if (buffers == nullptr || bad == nullptr || count <= 0 || count > 65535) return fail(IVB_EINVAL, "ivb_validate_buffers: bad argument");
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  validate_init_kernel<<<1, 32, 0, s>>>(bad, count);
+  IVB_CUDA(cudaGetLastError());
+  validate_buffers_kernel<<<dim3(64, count), 256, 0, s>>>(buffers, bad);
+  IVB_CUDA(cudaGetLastError());
   return IVB_OK;
 }
 

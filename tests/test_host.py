@@ -36,7 +36,7 @@ def test_library_exports_every_declared_entry_point() -> None:
 def test_ctypes_structs_match_the_c_layout(tmp_path: Path) -> None:
     from ivonar_inference_b200 import _native
 
-    structs = [_native.IvbTernary, _native.IvbLayerDesc, _native.IvbModelDesc]
+    structs = [_native.IvbTernary, _native.IvbLayerDesc, _native.IvbModelDesc, _native.IvbCheckBuffer]
     lines = ['#include <cstddef>', '#include <cstdio>', '#include "ivonar_b200.h"', "int main() {"]
     for st in structs:
         lines.append(f'  printf("{st.__name__} sizeof %zu\\n", sizeof({st.__name__}));')
@@ -136,3 +136,73 @@ def test_build_decoder_leaves_other_devices_to_the_reference_dispatch() -> None:
     model = synthetic.synthetic_model(synthetic.tiny(), 0, "reference_tests")
     dec, backend, note = decoder.build_decoder(model, "cpu", kernels=False)
     assert isinstance(dec, _reference.module("decoder").StaticDecoder) and backend == "torch" and note is None
+
+
+def test_ingest_leaves_other_devices_to_the_reference_loader(tmp_path: Path) -> None:
+    from ivonar_inference_b200 import _reference, ingest, synthetic
+
+    payload = synthetic.tiny()
+    state = synthetic.synthetic_state(payload, 0, "reference_tests")
+    loader = _reference.module("loader")
+    path = tmp_path / "packed.pt"
+    torch.save({"format": loader.PACKED_FORMAT, "schema_version": loader.PACKED_SCHEMA_VERSION, "config": payload,
+                "model_state": state, "step": 3}, path)
+    ours = ingest.load_model(path, "cpu", materialize=False)
+    ref = loader.load_model(path, "cpu", materialize=False)
+    assert isinstance(ours, loader.LoadedModel) and ours.step == 3 and ours.config == ref.config
+    for key, value in ref.model.state_dict().items():
+        assert torch.equal(value, ours.model.state_dict()[key]), key
+    # a corrupted checkpoint raises the reference's own error
+    state["blocks.1.ffn.up_proj.weight_scales"] = -state["blocks.1.ffn.up_proj.weight_scales"]
+    torch.save({"format": loader.PACKED_FORMAT, "schema_version": loader.PACKED_SCHEMA_VERSION, "config": payload,
+                "model_state": state}, path)
+    with pytest.raises(RuntimeError, match="positive values: blocks.1.ffn.up_proj.weight_scales"):
+        ingest.load_model(path, "cpu")
+
+
+def test_ingest_block_copy_rebuilds_every_tensor_at_its_offset(tmp_path: Path) -> None:
+    """The one-block copy of a memory-mapped checkpoint, aimed at the host: every tensor (views that share
+    a storage, a strided view, an empty tensor, non-tensor entries) comes back equal at its offset."""
+    from ivonar_inference_b200 import ingest, synthetic
+
+    state = dict(synthetic.synthetic_state(synthetic.tiny(), 0, "reference_tests"))
+    base = torch.arange(60, dtype=torch.float32).view(6, 10)
+    state.update({"shared.a": base, "shared.b": base[2:5, 1:7:2], "shared.t": base.t(), "empty": torch.empty(0, 3),
+                  "half": torch.randn(7, dtype=torch.float16), "note": "text"})
+    path = tmp_path / "state.pt"
+    torch.save(state, path)
+    mapped = torch.load(path, map_location="cpu", weights_only=True, mmap=True)
+    out = ingest._state_to_device(mapped, torch.device("cpu"), path.stat().st_size)
+    assert out.keys() == state.keys() and out["note"] == "text"
+    for key, value in state.items():
+        if isinstance(value, torch.Tensor):
+            assert out[key].dtype == value.dtype and out[key].shape == value.shape, key
+            assert torch.equal(out[key], value), key
+    # views of one saved storage stay views of one block
+    assert out["shared.b"].untyped_storage().data_ptr() == out["shared.a"].untyped_storage().data_ptr()
+
+
+def test_ingest_archive_reader_matches_torch_load(tmp_path: Path) -> None:
+    """The direct reader of a torch.save archive, aimed at the host: the same payload as torch.load
+    (nested config, shared and strided storages, empty tensors), and None (torch.load takes over) for an
+    archive holding anything else."""
+    from ivonar_inference_b200 import ingest, synthetic
+
+    payload = synthetic.tiny()
+    state = dict(synthetic.synthetic_state(payload, 0, "reference_tests"))
+    base = torch.arange(60, dtype=torch.float32).view(6, 10)
+    state.update({"shared.a": base, "shared.b": base[2:5, 1:7:2], "shared.t": base.t(), "empty": torch.empty(0, 3),
+                  "bf16": torch.randn(5, dtype=torch.bfloat16), "ids": torch.arange(9)})
+    path = tmp_path / "model.pt"
+    torch.save({"format": "f", "config": payload, "model_state": state, "step": 4, "none": None}, path)
+    got = ingest._read_archive(path, torch.device("cpu"))
+    want = torch.load(path, map_location="cpu", weights_only=True)
+    assert got is not None and got.keys() == want.keys() and got["config"] == want["config"] and got["none"] is None
+    for key, value in want["model_state"].items():
+        ours = got["model_state"][key]
+        assert ours.dtype == value.dtype and ours.shape == value.shape and ours.stride() == value.stride(), key
+        assert torch.equal(ours, value), key
+    torch.save({"p": torch.nn.Parameter(torch.ones(3))}, path)
+    assert ingest._read_archive(path, torch.device("cpu")) is None
+    path.write_bytes(b"not an archive")
+    assert ingest._read_archive(path, torch.device("cpu")) is None
