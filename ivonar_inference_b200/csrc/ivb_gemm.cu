@@ -36,18 +36,21 @@ namespace ivb {
 
 constexpr int kGemmRows = 128;       // weight rows per tile (MMA M, TMEM lanes)
 constexpr int kGemmTok = 128;        // tokens per tile (MMA N, accumulator columns)
-constexpr int kGemmStages = 4;       // activation stages = TMEM A slots (groups in flight)
+constexpr int kGemmStages = 8;       // activation stages in shared memory (groups copied ahead)
+constexpr int kGemmASlots = 4;       // TMEM A slots of 32 columns (expanded groups in flight)
 constexpr int kGemmBufs = 3;         // TMEM accumulators of 128 columns
-constexpr int kGemmACol = kGemmBufs * kGemmTok;  // first TMEM column of the A slots (32 columns each)
+constexpr int kGemmACol = kGemmBufs * kGemmTok;  // first TMEM column of the A slots
 constexpr int kGemmEpiWarps = 16;    // warps 0-15: epilogue
 constexpr int kGemmEpiCols = 32;     // accumulator columns (tokens) per epilogue thread
 constexpr int kGemmMmaWarp = 16;     // warp 16: TMEM allocation and the MMA thread
-constexpr int kGemmTeams = 2;        // producer teams: team t stages the groups g = t (mod 2)
+constexpr int kGemmTeams = 2;        // producer teams: team t expands the groups G = t (mod 2)
 constexpr int kGemmProdWarps = 4 * kGemmTeams;  // warps 17-24: producers (lane quarter = warp % 4)
 constexpr int kGemmProducers = 128;  // threads of one team (one per weight row / TMEM lane)
-constexpr int kGemmThreads = 32 * (kGemmEpiWarps + 1 + kGemmProdWarps);
-constexpr int kPackSlots = 4;                    // packed weight blocks in flight
+constexpr int kGemmLoadWarp = kGemmMmaWarp + 1 + kGemmProdWarps;  // warp 25: lane 0 issues every copy
+constexpr int kGemmThreads = 32 * (kGemmLoadWarp + 1);
+constexpr int kPackSlots = 8;                    // packed weight blocks in flight
 constexpr int kPackSlot = kGemmRows * 32;        // packed bytes of one group for the tile's 128 rows
+constexpr uint32_t kAccBias = 0x4B400000u;       // accumulator start value: the float 12582912 as an integer
 
 // kind::i8 instruction descriptor: D s32, A s8 (weight codes - 1, TMEM), B s8 (activations, shared
 // memory), both K-major, M 128, N 128.
@@ -62,41 +65,66 @@ __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, i
       "l"(map), "r"(x), "r"(y), "r"(smem_addr(bar))
       : "memory");
 }
-// Grid (row tiles, token tiles). q8: the tiled activation layout (q8_chunk_offset), act_scale [T];
-// wmap: 2-D tensor map over the packed weights (row_bytes x rows bytes, box 32 x 128).
+// Persistent: grid = min(units, SMs); CTA b takes the units b, b + gridDim.x, ... A unit is one
+// (row tile x, token tile y, split z) with x fastest. Every role walks the same sequence of (unit, group)
+// pairs, and its running group count G picks the ring entries and their phases, so the copies and
+// expansions of the next unit overlap the current unit's last MMAs and its epilogue.
+// q8: the tiled activation layout (q8_chunk_offset), act_scale [T]; wmap: 2-D tensor map over the packed
+// weights (row_bytes x rows bytes, box 32 x 128).
+struct GemmUnit {
+  int r0, t0, z, g_lo, groups;
+};
+
+__device__ __forceinline__ GemmUnit gemm_unit(int u, int row_tiles, int tok_tiles, int g_per, int groups_all) {
+  GemmUnit w;
+  const int per_z = row_tiles * tok_tiles;
+  w.z = u / per_z;
+  const int rest = u - w.z * per_z;
+  const int y = rest / row_tiles;
+  w.r0 = (rest - y * row_tiles) * kGemmRows;
+  w.t0 = y * kGemmTok;
+  w.g_lo = w.z * g_per;
+  w.groups = max(0, min(groups_all, w.g_lo + g_per) - w.g_lo);
+  return w;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
     ternary_gemm_kernel(const __grid_constant__ CUtensorMap wmap, const IvbTernary m, const int8_t* __restrict__ q8,
                         int ldq, const float* __restrict__ act_scale, int T, int epilogue, float* out, int ldo,
-                        int g_per, float* partial, unsigned long long timeout_ns, unsigned* error) {
+                        int g_per, int row_tiles, int tok_tiles, int units, float* partial,
+                        unsigned long long timeout_ns, unsigned* error) {
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char* smem =
       smem_raw + ((1024u - (static_cast<unsigned>(__cvta_generic_to_shared(smem_raw)) & 1023u)) & 1023u);
-  __shared__ __align__(8) unsigned long long full_bar[kGemmStages], empty_bar[kGemmStages];
+  // act_full/act_empty: activation stages (loader -> MMA); a_full/a_empty: TMEM A slots (producers ->
+  // MMA); tfull/tempty: accumulators (MMA -> epilogue); pk_bar/pk_empty: packed weights (loader ->
+  // producers)
+  __shared__ __align__(8) unsigned long long act_full[kGemmStages], act_empty[kGemmStages];
+  __shared__ __align__(8) unsigned long long a_full[kGemmASlots], a_empty[kGemmASlots];
   __shared__ __align__(8) unsigned long long tfull_bar[kGemmBufs], tempty_bar[kGemmBufs];
   __shared__ __align__(8) unsigned long long pk_bar[kPackSlots], pk_empty[kPackSlots];
   __shared__ unsigned tmem_base;
   __shared__ int failed;
   __shared__ int stage_group[kGemmStages], slot_group[kPackSlots];  // last group copied into each (error drain)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int r0 = blockIdx.x * kGemmRows, t0 = blockIdx.y * kGemmTok;
   const int groups_all = (m.in_features + 127) >> 7;
-  // split-K: this CTA's groups [g_lo, g_lo + groups); loop indices below are local to the split
-  const int g_lo = blockIdx.z * g_per;
-  const int groups = max(0, min(groups_all, g_lo + g_per) - g_lo);
-  unsigned char* pack = smem + kGemmStages * kGemmTile;           // packed ring
-  float* scale_tab = reinterpret_cast<float*>(pack + kPackSlots * kPackSlot);  // [groups][128 rows]
+  unsigned char* pack = smem + kGemmStages * kGemmTile;  // packed ring
+  const bool loader = tid == 32 * kGemmLoadWarp;
   if (warp == kGemmMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  const int pj = tid - 32 * (kGemmMmaWarp + 1);  // producer index 0..255
-  const int team = pj >> 7, tj = pj & 127;        // tj == 0: the team's copy issuer
-  if (pj == 0) {
+  if (loader) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(&wmap) : "memory");
     for (int i = 0; i < kGemmStages; ++i) {
-      mbar_init(full_bar + i, kGemmProducers);
-      mbar_init(empty_bar + i, 1);
+      mbar_init(act_full + i, 1);
+      mbar_init(act_empty + i, 1);
+      stage_group[i] = -1;
+    }
+    for (int i = 0; i < kGemmASlots; ++i) {
+      mbar_init(a_full + i, kGemmProducers);
+      mbar_init(a_empty + i, 1);
     }
     for (int i = 0; i < kGemmBufs; ++i) {
       mbar_init(tfull_bar + i, 1);
@@ -105,23 +133,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     for (int i = 0; i < kPackSlots; ++i) {
       mbar_init(pk_bar + i, 1);
       mbar_init(pk_empty + i, kGemmProducers);
+      slot_group[i] = -1;
     }
     failed = 0;
-    for (int i = 0; i < kGemmStages; ++i) stage_group[i] = -1;
-    for (int i = 0; i < kPackSlots; ++i) slot_group[i] = -1;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    for (int g = 0; g < kPackSlots && g < groups; ++g) {
-      slot_group[g] = g;
-      mbar_expect_tx(pk_bar + g, kPackSlot);
-      tma_load_2d(pack + g * kPackSlot, &wmap, (g_lo + g) << 5, r0, pk_bar + g);
-    }
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  // launched as a programmatic dependent: everything above (TMEM, barriers, the first packed-weight
-  // copies) may overlap the previous kernel; its outputs (activations, scales, a residual to add to)
-  // are read only after this wait
+  // launched as a programmatic dependent: the set-up above may overlap the previous kernel; its outputs
+  // (activations, scales, a residual to add to) are read only after this wait
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const unsigned tmem = tmem_base;
@@ -129,177 +150,217 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int row = 32 * quarter + lane;        // epilogue and producer warps: the weight row (TMEM lane)
   const unsigned lane_base = tmem + (static_cast<unsigned>(32 * quarter) << 16);
   const int col0 = (warp >> 2) * kGemmEpiCols;  // epilogue warps: first token column
-
-  float2 acc[kGemmEpiCols / 2];
+  volatile int* fail_flag = &failed;
   bool late = false;
-  if (warp > kGemmMmaWarp) {
-    // ---- producers: team `team` stages groups team, team + 2, ... ----
-    const int8_t* a_src = q8 + static_cast<size_t>(blockIdx.y) * (ldq >> 7) * kGemmTile;
-    for (int g = team; g < groups; g += kGemmTeams) {
-      const int st = g % kGemmStages, slot = g % kPackSlots;
-      if (!mbar_wait_bounded(pk_bar + slot, (g / kPackSlots) & 1, timeout_ns) ||
-          (g >= kGemmStages && !mbar_wait_bounded(empty_bar + st, ((g / kGemmStages) - 1) & 1, timeout_ns))) {
-        late = true;
-        break;
-      }
-      if (tj == 0) {
-        stage_group[st] = g;
-        mbar_expect(full_bar + st, kGemmTile);
-        bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(g_lo + g) * kGemmTile, kGemmTile, full_bar + st);
-      }
-      // row's 16 packed words -> 32 TMEM columns: column 4c + f holds the codes (w_c >> 2f) & 0x03030303
-      // (inputs 16c + 4b + f, b = 0..3), each byte turned into the signed code - 1
-      const uint4* pk = reinterpret_cast<const uint4*>(pack + slot * kPackSlot + row * 32);
-      const uint4 p0 = pk[0], p1 = pk[1];
-      const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
-      uint32_t v[32];
-#pragma unroll
-      for (int c = 0; c < 8; ++c)
-#pragma unroll
-        for (int f = 0; f < 4; ++f) v[4 * c + f] = (((words[c] >> (2 * f)) & 0x03030303u) + 0x7F7F7F7Fu) ^ 0x80808080u;
-      mbar_arrive(pk_empty + slot);
-      tmem_st32(lane_base + kGemmACol + st * 32, v);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(full_bar + st);
-      // refill the slot of the team's previous group (read by the whole team by now) with that group
-      // + kPackSlots (the same team's)
-      const int prev = g - kGemmTeams, nxt = prev + kPackSlots;
-      if (tj == 0 && prev >= 0 && nxt < groups) {
-        if (!mbar_wait_bounded(pk_empty + prev % kPackSlots, (prev / kPackSlots) & 1, timeout_ns)) {
-          late = true;
-          break;
-        }
-        slot_group[prev % kPackSlots] = nxt;
-        mbar_expect_tx(pk_bar + prev % kPackSlots, kPackSlot);
-        tma_load_2d(pack + (prev % kPackSlots) * kPackSlot, &wmap, (g_lo + nxt) << 5, r0, pk_bar + prev % kPackSlots);
-      }
-    }
-    if (late) atomicExch(&failed, 1);
-  } else if (warp == kGemmMmaWarp) {
-    // ---- MMA issuer ----
+  unsigned G = 0;  // groups of this CTA's sequence handled so far (by this role)
+
+  if (warp == kGemmLoadWarp) {
+    // ---- loader: every copy, up to kGemmStages groups of activations and kPackSlots of packed weights
+    // ahead of the MMA ----
     if (lane == 0) {
-      for (int g = 0; g < groups; ++g) {
-        const int st = g % kGemmStages, b = g % kGemmBufs;
-        // tempty completion k of accumulator b: armed for group b + 3k (k = 0: the initial arming)
-        if (!mbar_wait_bounded(full_bar + st, (g / kGemmStages) & 1, timeout_ns) ||
-            !mbar_wait_bounded(tempty_bar + b, (g / kGemmBufs) & 1, timeout_ns)) {
-          late = true;
-          break;
+      for (int u = blockIdx.x; u < units && !late; u += gridDim.x) {
+        const GemmUnit w = gemm_unit(u, row_tiles, tok_tiles, g_per, groups_all);
+        const int8_t* a_src = q8 + static_cast<size_t>(w.t0 >> 7) * (ldq >> 7) * kGemmTile;
+        for (int g = 0; g < w.groups; ++g, ++G) {
+          const int st = G % kGemmStages, slot = G % kPackSlots;
+          if (*fail_flag || (G >= kGemmStages && !mbar_wait_bounded(act_empty + st, ((G / kGemmStages) - 1) & 1, timeout_ns))) {
+            late = true;
+            break;
+          }
+          stage_group[st] = static_cast<int>(G);
+          mbar_expect_tx(act_full + st, kGemmTile);
+          bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(w.g_lo + g) * kGemmTile, kGemmTile, act_full + st);
+          if (G >= kPackSlots && !mbar_wait_bounded(pk_empty + slot, ((G / kPackSlots) - 1) & 1, timeout_ns)) {
+            late = true;
+            break;
+          }
+          slot_group[slot] = static_cast<int>(G);
+          mbar_expect_tx(pk_bar + slot, kPackSlot);
+          tma_load_2d(pack + slot * kPackSlot, &wmap, (w.g_lo + g) << 5, w.r0, pk_bar + slot);
         }
-        tc_fence_after();
-        const unsigned bsm = smem_addr(smem + st * kGemmTile);
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          umma_i8_ta(tmem + b * kGemmTok, tmem + kGemmACol + st * 32 + kk * 8, smem_desc(bsm + kk * 256), kGemmIdesc, kk > 0);
-        umma_commit(empty_bar + st);
-        umma_commit(tfull_bar + b);
       }
       if (late) atomicExch(&failed, 1);
     }
     __syncwarp();
-  } else {
-    // ---- epilogue: drain, scale, accumulate ----
-    for (int i = tid; i < groups * kGemmRows; i += 32 * kGemmEpiWarps) {
-      const int g = g_lo + (i >> 7), r = r0 + (i & 127);
-      scale_tab[i] = r < m.rows ? h2f(__ldg(m.scales + static_cast<size_t>(r) * m.scale_stride + g)) : 0.0f;
+  } else if (warp > kGemmMmaWarp) {
+    // ---- producers: team `team` expands the groups G = team (mod 2) into TMEM A slot G % 4 ----
+    const int team = (warp - kGemmMmaWarp - 1) >> 2;
+    for (int u = blockIdx.x; u < units && !late; u += gridDim.x) {
+      const GemmUnit w = gemm_unit(u, row_tiles, tok_tiles, g_per, groups_all);
+      for (int g = 0; g < w.groups; ++g, ++G) {
+        if ((G & 1u) != static_cast<unsigned>(team)) continue;
+        const int slot = G % kPackSlots, as = G % kGemmASlots;
+        if (*fail_flag || !mbar_wait_bounded(pk_bar + slot, (G / kPackSlots) & 1, timeout_ns) ||
+            (G >= kGemmASlots && !mbar_wait_bounded(a_empty + as, ((G / kGemmASlots) - 1) & 1, timeout_ns))) {
+          late = true;
+          break;
+        }
+        // row's 16 packed words -> 32 TMEM columns: column 4c + f holds the codes (w_c >> 2f) & 0x03030303
+        // (inputs 16c + 4b + f, b = 0..3), each byte turned into the signed code - 1
+        const uint4* pk = reinterpret_cast<const uint4*>(pack + slot * kPackSlot + row * 32);
+        const uint4 p0 = pk[0], p1 = pk[1];
+        const uint32_t words[8] = {p0.x, p0.y, p0.z, p0.w, p1.x, p1.y, p1.z, p1.w};
+        uint32_t v[32];
+#pragma unroll
+        for (int c = 0; c < 8; ++c)
+#pragma unroll
+          for (int f = 0; f < 4; ++f) v[4 * c + f] = (((words[c] >> (2 * f)) & 0x03030303u) + 0x7F7F7F7Fu) ^ 0x80808080u;
+        mbar_arrive(pk_empty + slot);
+        tmem_st32(lane_base + kGemmACol + as * 32, v);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(a_full + as);
+      }
     }
-    asm volatile("bar.sync 1, %0;" ::"n"(32 * kGemmEpiWarps) : "memory");
+    if (late) atomicExch(&failed, 1);
+  } else if (warp == kGemmMmaWarp) {
+    // ---- MMA issuer: group G = four 128x128x32 int8 MMAs into accumulator G % 3 ----
+    int last = -1;  // accumulator of the last group issued (the exit waits for its MMAs)
+    unsigned last_g = 0;
+    if (lane == 0) {
+      for (int u = blockIdx.x; u < units && !late; u += gridDim.x) {
+        const GemmUnit w = gemm_unit(u, row_tiles, tok_tiles, g_per, groups_all);
+        for (int g = 0; g < w.groups; ++g, ++G) {
+          const int st = G % kGemmStages, as = G % kGemmASlots, b = G % kGemmBufs;
+          // tempty completion k of accumulator b: armed for group b + 3k (k = 0: the initial arming)
+          if (*fail_flag || !mbar_wait_bounded(act_full + st, (G / kGemmStages) & 1, timeout_ns) ||
+              !mbar_wait_bounded(a_full + as, (G / kGemmASlots) & 1, timeout_ns) ||
+              !mbar_wait_bounded(tempty_bar + b, (G / kGemmBufs) & 1, timeout_ns)) {
+            late = true;
+            break;
+          }
+          tc_fence_after();
+          const unsigned bsm = smem_addr(smem + st * kGemmTile);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            umma_i8_ta(tmem + b * kGemmTok, tmem + kGemmACol + as * 32 + kk * 8, smem_desc(bsm + kk * 256), kGemmIdesc, true);
+          umma_commit(act_empty + st);
+          umma_commit(a_empty + as);
+          umma_commit(tfull_bar + b);
+          last = b;
+          last_g = G;
+        }
+      }
+      if (late) atomicExch(&failed, 1);
+      // no MMA may still be writing tensor memory when it is released
+      if (last >= 0) mbar_wait_bounded(tfull_bar + last, (last_g / kGemmBufs) & 1, timeout_ns);
+    }
+    __syncwarp();
+  } else {
+    // ---- epilogue: drain, scale, accumulate; then write the unit's outputs straight from registers ----
+    // Exact int32 -> float without a conversion: every accumulator starts a group holding the integer
+    // 0x4B400000 and the MMAs add the group's dot to it, so its bits are the float 12582912 + dot
+    // (|dot| <= 128 * 127 < 2^22 keeps it in [2^23, 2^24), where float steps are 1); one paired
+    // subtract leaves dot. The drain puts the start value back for the accumulator's next group.
+    for (int b = 0; b < kGemmBufs; ++b) tmem_fill32(lane_base + b * kGemmTok + col0, kAccBias);
+    tmem_wait_st();
+    tc_fence_before();
     __syncwarp();
     if (lane == 0)
       for (int b = 0; b < kGemmBufs; ++b) mbar_arrive(tempty_bar + b);
+    const float2 m2 = make_float2(-12582912.0f, -12582912.0f);
+    for (int u = blockIdx.x; u < units && !late; u += gridDim.x) {
+      const GemmUnit w = gemm_unit(u, row_tiles, tok_tiles, g_per, groups_all);
+      const int r = w.r0 + row;
+      const uint16_t* srow = r < m.rows ? m.scales + static_cast<size_t>(r) * m.scale_stride + w.g_lo : nullptr;
+      float2 acc[kGemmEpiCols / 2];
 #pragma unroll
-    for (int n = 0; n < kGemmEpiCols / 2; ++n) acc[n] = make_float2(0.0f, 0.0f);
-    for (int g = 0; g < groups; ++g) {
-      const int b = g % kGemmBufs;
-      late = !mbar_wait_bounded(tfull_bar + b, (g / kGemmBufs) & 1, timeout_ns);
-      if (__any_sync(kFull, late)) {
-        late = true;
-        break;
-      }
-      tc_fence_after();
-      uint32_t d[32];
-      tmem_ld32(lane_base + b * kGemmTok + col0, d);
-      const float sv = scale_tab[g * kGemmRows + row];
-      const float2 s2 = make_float2(sv, sv);
-      // exact int32 -> float without the conversion unit: the bits of 0x4B400000 + dot are the float
-      // 12582912 + dot (|dot| < 2^22), and one paired subtract leaves dot
-      const float2 m2 = make_float2(-12582912.0f, -12582912.0f);
+      for (int n = 0; n < kGemmEpiCols / 2; ++n) acc[n] = make_float2(0.0f, 0.0f);
+      // the row's group scales, loaded two groups ahead of their use
+      float s_cur = srow != nullptr && w.groups > 0 ? h2f(__ldg(srow)) : 0.0f;
+      float s_nxt = srow != nullptr && w.groups > 1 ? h2f(__ldg(srow + 1)) : 0.0f;
+      // the unit's per-token and per-row epilogue inputs, loaded before the drain so their latency hides
+      // behind it: lane l holds act_scale of token t0 + col0 + l
+      const int tb = w.t0 + col0;
+      const int nt = min(kGemmEpiCols, T - tb);  // tokens of this warp's columns that exist
+      const float asc = partial == nullptr && lane < nt ? __ldg(act_scale + tb + lane) : 0.0f;
+      const float bias_r = partial == nullptr && m.bias != nullptr && r < m.rows ? __ldg(m.bias + r) : 0.0f;
+      for (int g = 0; g < w.groups; ++g, ++G) {
+        const int b = G % kGemmBufs;
+        const float s_far = srow != nullptr && g + 2 < w.groups ? h2f(__ldg(srow + g + 2)) : 0.0f;
+        late = !mbar_wait_bounded(tfull_bar + b, (G / kGemmBufs) & 1, timeout_ns);
+        if (__any_sync(kFull, late)) {
+          late = true;
+          break;
+        }
+        tc_fence_after();
+        const float2 s2 = make_float2(s_cur, s_cur);
 #pragma unroll
-      for (int q = 0; q < 16; ++q) {
-        const float2 x = __fadd2_rn(make_float2(__int_as_float(static_cast<int>(d[2 * q]) + 0x4B400000),
-                                                __int_as_float(static_cast<int>(d[2 * q + 1]) + 0x4B400000)), m2);
-        acc[q] = __ffma2_rn(x, s2, acc[q]);
+        for (int h = 0; h < 4; ++h) {
+          uint32_t d[8];
+          tmem_ld8(lane_base + b * kGemmTok + col0 + 8 * h, d);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 x = __fadd2_rn(make_float2(__uint_as_float(d[2 * q]), __uint_as_float(d[2 * q + 1])), m2);
+            acc[4 * h + q] = __ffma2_rn(x, s2, acc[4 * h + q]);
+          }
+          tmem_fill8(lane_base + b * kGemmTok + col0 + 8 * h, kAccBias);
+        }
+        tmem_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(tempty_bar + b);
+        s_cur = s_nxt;
+        s_nxt = s_far;
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar + b);
+      if (late) break;
+      // token t = t0 + col0 + j of this warp: its 32 lanes hold 32 consecutive weight rows, so every
+      // store below is one contiguous 128-byte (64-byte for silu pairs) run per warp
+      if (partial == nullptr && epilogue == IVB_EPI_SILU_PAIR) {
+        // tokens j (even) and j + 1 at once: rows 2i (gate) and 2i + 1 (up) of token j go to lane i,
+        // those of token j + 1 to lane 16 + i, so each lane evaluates one silu per two tokens
+        const int src = 2 * (lane & 15), rg = w.r0 + 32 * quarter + src;
+        const bool second = lane >= 16;
+#pragma unroll
+        for (int j = 0; j < kGemmEpiCols; j += 2) {
+          if (j >= nt) break;
+          const float v0 = acc[j >> 1].x * __shfl_sync(kFull, asc, j) + bias_r;
+          const float v1 = acc[j >> 1].y * __shfl_sync(kFull, asc, j + 1) + bias_r;
+          const float g0 = __shfl_sync(kFull, v0, src), u0 = __shfl_sync(kFull, v0, src + 1);
+          const float g1 = __shfl_sync(kFull, v1, src), u1 = __shfl_sync(kFull, v1, src + 1);
+          const int jj = j + (second ? 1 : 0);
+          if (jj < nt && rg + 1 < m.rows)
+            out[static_cast<size_t>(tb + jj) * ldo + (rg >> 1)] = silu_f(second ? g1 : g0) * (second ? u1 : u0);
+        }
+      } else {
+        // four tokens at a time so that a residual's loads are issued together
+#pragma unroll
+        for (int jb = 0; jb < kGemmEpiCols; jb += 4) {
+          if (jb >= nt) break;
+          float old[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            old[e] = epilogue == IVB_EPI_RESIDUAL && partial == nullptr && jb + e < nt && r < m.rows
+                         ? out[static_cast<size_t>(tb + jb + e) * ldo + r]
+                         : 0.0f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int j = jb + e;
+            const float a = (j & 1) ? acc[j >> 1].y : acc[j >> 1].x;
+            const float sc = __shfl_sync(kFull, asc, j);
+            const size_t t = static_cast<size_t>(tb + j);
+            if (j >= nt || r >= m.rows) continue;
+            if (partial != nullptr) {  // split-K: this split's raw sums; scale, bias and epilogue in the reduction
+              partial[(static_cast<size_t>(w.z) * T + t) * m.rows + r] = a;
+            } else {
+              const float v = a * sc + bias_r;
+              out[t * ldo + r] = epilogue == IVB_EPI_RESIDUAL ? old[e] + v : v;
+            }
+          }
+        }
+      }
     }
     if (late && lane == 0) atomicExch(&failed, 1);
   }
   __syncthreads();
-  const bool bad = failed != 0;
-  if (bad) {
+  if (failed != 0) {
     if (tid == 0) atomicCAS(error, 0u, static_cast<unsigned>(IVB_ETIMEOUT));
     // no bulk or tensor copy may still be writing this CTA's shared memory when it exits
-    if (pj == 0) {
+    if (loader) {
       for (int i = 0; i < kGemmStages; ++i)
-        if (stage_group[i] >= 0) mbar_wait_bounded(full_bar + i, (stage_group[i] / kGemmStages) & 1, timeout_ns);
+        if (stage_group[i] >= 0) mbar_wait_bounded(act_full + i, (stage_group[i] / kGemmStages) & 1, timeout_ns);
       for (int i = 0; i < kPackSlots; ++i)
         if (slot_group[i] >= 0) mbar_wait_bounded(pk_bar + i, (slot_group[i] / kPackSlots) & 1, timeout_ns);
-    }
-  } else {
-    // stage the tile as [token][row] fp32 in the (now idle) stages, then write it out row by row, coalesced
-    constexpr int kLd = kGemmRows + 4;
-    float* tile = reinterpret_cast<float*>(smem);
-    if (warp < kGemmEpiWarps) {
-#pragma unroll
-      for (int q = 0; q < kGemmEpiCols / 2; ++q) {
-        tile[(col0 + 2 * q) * kLd + row] = acc[q].x;
-        tile[(col0 + 2 * q + 1) * kLd + row] = acc[q].y;
-      }
-    }
-    __syncthreads();
-    const bool vec = (ldo & 3) == 0 && (reinterpret_cast<uintptr_t>(out) & 15) == 0;
-    for (int tr = warp; tr < kGemmTok && t0 + tr < T; tr += kGemmThreads / 32) {
-      const int tt = t0 + tr;
-      if (partial != nullptr) {  // split-K: this split's raw sums; scale, bias and epilogue in the reduction
-        const float4 v4 = *reinterpret_cast<const float4*>(tile + tr * kLd + 4 * lane);
-        const float pv[4] = {v4.x, v4.y, v4.z, v4.w};
-        float* prow = partial + (static_cast<size_t>(blockIdx.z) * T + tt) * m.rows;
-        const int r = r0 + 4 * lane;
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (r + e < m.rows) prow[r + e] = pv[e];
-        continue;
-      }
-      const float sc = __ldg(act_scale + tt);
-      const float4 v4 = *reinterpret_cast<const float4*>(tile + tr * kLd + 4 * lane);
-      float v[4] = {v4.x * sc, v4.y * sc, v4.z * sc, v4.w * sc};
-      const int r = r0 + 4 * lane;
-#pragma unroll
-      for (int e = 0; e < 4; ++e)
-        if (m.bias != nullptr && r + e < m.rows) v[e] += __ldg(m.bias + r + e);
-      float* orow = out + static_cast<size_t>(tt) * ldo;
-      if (epilogue == IVB_EPI_SILU_PAIR) {
-        // rows r, r+1 (gate, up) -> output r/2; rows r+2, r+3 -> r/2 + 1 (m.rows is even)
-        if (r + 1 < m.rows) orow[r >> 1] = silu_f(v[0]) * v[1];
-        if (r + 3 < m.rows) orow[(r >> 1) + 1] = silu_f(v[2]) * v[3];
-      } else if (vec && r + 3 < m.rows) {
-        float4* o4 = reinterpret_cast<float4*>(orow + r);
-        if (epilogue == IVB_EPI_RESIDUAL) {
-          const float4 old = *o4;
-          v[0] += old.x;
-          v[1] += old.y;
-          v[2] += old.z;
-          v[3] += old.w;
-        }
-        *o4 = make_float4(v[0], v[1], v[2], v[3]);
-      } else {
-#pragma unroll
-        for (int e = 0; e < 4; ++e)
-          if (r + e < m.rows) orow[r + e] = epilogue == IVB_EPI_RESIDUAL ? orow[r + e] + v[e] : v[e];
-      }
     }
   }
   tc_fence_before();
@@ -479,6 +540,20 @@ extern "C" {
 
 namespace ivb {
 namespace {
+// Multiprocessor count of device `dev`, looked up once per device.
+cudaError_t sm_count(int dev, int* out) {
+  static std::mutex lock;
+  static int table[64] = {};
+  if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> guard(lock);
+  if (table[dev] == 0) {
+    const cudaError_t rc = cudaDeviceGetAttribute(&table[dev], cudaDevAttrMultiProcessorCount, dev);
+    if (rc != cudaSuccess) return rc;
+  }
+  *out = table[dev];
+  return cudaSuccess;
+}
+
 int32_t gemm_scratch(int dev, float** out) {
   static std::mutex lock;
   static float* table[64] = {};
@@ -525,9 +600,9 @@ int32_t ivb::ternary_gemm_into(const IvbTernary* m, const int8_t* q8, int32_t ld
   if (!device_is_sm100()) return fail(IVB_EUNSUPPORTED, "ivb_ternary_gemm: needs an sm_100 device");
   const int groups = (m->in_features + 127) / 128;
   constexpr size_t kSmemCap = 227 * 1024 - 2048;  // dynamic shared memory beside the static barriers
-  const size_t smem = static_cast<size_t>(kGemmStages) * kGemmTile + kPackSlots * kPackSlot +
-                      static_cast<size_t>(groups) * kGemmRows * 4 + 1024;
-  if (smem > kSmemCap) return fail(IVB_EINVAL, "ivb_ternary_gemm: %d inputs leave too little shared memory", m->in_features);
+  const size_t smem = static_cast<size_t>(kGemmStages) * kGemmTile + kPackSlots * kPackSlot + 1024;
+  static_assert(static_cast<size_t>(kGemmStages) * kGemmTile + kPackSlots * kPackSlot + 1024 <= kSmemCap,
+                "the GEMM's rings exceed shared memory");
   IVB_CUDA(cudaFuncSetAttribute(ternary_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)));
   PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
   if (encode == nullptr) return fail(IVB_EUNSUPPORTED, "ivb_ternary_gemm: cuTensorMapEncodeTiled is unavailable");
@@ -550,7 +625,11 @@ int32_t ivb::ternary_gemm_into(const IvbTernary* m, const int8_t* q8, int32_t ld
   const int g_per = (groups + splits - 1) / splits;
   splits = (groups + g_per - 1) / g_per;
   if (splits == 1) partial = nullptr;
-  const dim3 grid(row_tiles, tok_tiles, splits);
+  const int units = row_tiles * tok_tiles * splits;
+  int dev = 0, sms = 0;
+  IVB_CUDA(cudaGetDevice(&dev));
+  IVB_CUDA(sm_count(dev, &sms));
+  const dim3 grid(std::min(units, sms));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   // programmatic dependent launch: the kernel's set-up overlaps the tail of the previous kernel on the
   // stream (the kernel waits for that grid with griddepcontrol.wait before reading its outputs)
@@ -566,7 +645,7 @@ int32_t ivb::ternary_gemm_into(const IvbTernary* m, const int8_t* q8, int32_t ld
   cfg.numAttrs = 1;
   const IvbTernary mv = *m;
   IVB_CUDA(cudaLaunchKernelEx(&cfg, ternary_gemm_kernel, wmap, mv, q8, ldq, act_scale, static_cast<int>(rows_t), static_cast<int>(epilogue),
-                              out, static_cast<int>(ldo), g_per, partial, 2000000000ull, error));
+                              out, static_cast<int>(ldo), g_per, row_tiles, tok_tiles, units, partial, 2000000000ull, error));
   if (splits > 1) {
     const int per_row = epilogue == IVB_EPI_SILU_PAIR ? m->rows / 2 : m->rows;
     const int n = rows_t * per_row;

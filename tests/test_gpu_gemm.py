@@ -82,8 +82,10 @@ def test_gemm_matches_the_oracle_gemv_per_token(oracle_lib, epilogue: int) -> No
     gen = torch.Generator().manual_seed(20 + epilogue)
     stream = torch.cuda.current_stream().cuda_stream
     err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    # the first four and the last split K (few row x token tiles); the others run every epilogue in the
+    # GEMM itself, over several tiles per CTA, ragged row and token tiles included
     for rows, cols, tokens in ((128, 1024, 1), (256, 1024, 37), (1792, 1024, 130), (1024, 2816, 64), (64, 100, 3),
-                               (5632, 1024, 16)):
+                               (256, 384, 200), (1216, 1024, 1300), (5632, 1024, 16)):
         desc, keep, (p, s, b) = _matrix(gen, rows, cols)
         x = torch.randn(tokens, cols, generator=gen)
         w = 1.0 + 0.1 * torch.randn(cols, generator=gen)
