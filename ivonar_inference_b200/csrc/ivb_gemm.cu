@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   const int groups_all = (m.in_features + 127) >> 7;
   unsigned char* pack = smem + kGemmStages * kGemmTile;  // packed ring
   const bool loader = tid == 32 * kGemmLoadWarp;
+  unsigned pre = 0;  // loader: packed-weight groups copied before the wait for the previous kernel
   if (warp == kGemmMmaWarp) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(&tmem_base)),
                  "r"(512));
@@ -137,6 +138,16 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
     failed = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    {
+      // the packed weights do not depend on the previous kernel: the first unit's first four groups
+      // are copied before the wait for it below
+      const GemmUnit w = gemm_unit(blockIdx.x, row_tiles, tok_tiles, g_per, groups_all);
+      for (int g = 0; g < w.groups && pre < 4; ++g, ++pre) {
+        slot_group[pre] = static_cast<int>(pre);
+        mbar_expect_tx(pk_bar + pre, kPackSlot);
+        tma_load_2d(pack + pre * kPackSlot, &wmap, (w.g_lo + g) << 5, w.r0, pk_bar + pre);
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -170,6 +181,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           stage_group[st] = static_cast<int>(G);
           mbar_expect_tx(act_full + st, kGemmTile);
           bulk_copy(smem + st * kGemmTile, a_src + static_cast<size_t>(w.g_lo + g) * kGemmTile, kGemmTile, act_full + st);
+          if (G < pre) continue;  // its packed weights were copied before the wait
           if (G >= kPackSlots && !mbar_wait_bounded(pk_empty + slot, ((G / kPackSlots) - 1) & 1, timeout_ns)) {
             late = true;
             break;
