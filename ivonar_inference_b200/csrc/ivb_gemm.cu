@@ -317,7 +317,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       }
       if (late) break;
       // token t = t0 + col0 + j of this warp: its 32 lanes hold 32 consecutive weight rows, so every
-      // store below is one contiguous 128-byte (64-byte for silu pairs) run per warp
+      // store below is one contiguous 128-byte (64-byte for silu pairs) run per warp. All 32 columns are
+      // evaluated without a branch, so that the unrolled iterations overlap; tokens past T are not stored.
       if (partial == nullptr && epilogue == IVB_EPI_SILU_PAIR) {
         // tokens j (even) and j + 1 at once: rows 2i (gate) and 2i + 1 (up) of token j go to lane i,
         // those of token j + 1 to lane 16 + i, so each lane evaluates one silu per two tokens
@@ -325,7 +326,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         const bool second = lane >= 16;
 #pragma unroll
         for (int j = 0; j < kGemmEpiCols; j += 2) {
-          if (j >= nt) break;
           const float v0 = acc[j >> 1].x * __shfl_sync(kFull, asc, j) + bias_r;
           const float v1 = acc[j >> 1].y * __shfl_sync(kFull, asc, j + 1) + bias_r;
           const float g0 = __shfl_sync(kFull, v0, src), u0 = __shfl_sync(kFull, v0, src + 1);
@@ -338,7 +338,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // four tokens at a time so that a residual's loads are issued together
 #pragma unroll
         for (int jb = 0; jb < kGemmEpiCols; jb += 4) {
-          if (jb >= nt) break;
           float old[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e)
