@@ -35,16 +35,13 @@ from . import _reference
 _PATCH_LOCK = threading.Lock()
 
 
-def validate_state_device(state: dict[str, Any], device: torch.device) -> None:
-    """The reference's state checks (``loader.py:94-112``) with the content checks on the device: one
-    launch over every packed and scale buffer of the right dtype, one synchronisation. Then the entries
-    are walked in the reference's order and the first failing check raises the reference's message."""
+def _plan_checks(state: dict[str, Any]) -> tuple[dict[int, str], list[tuple[int, str, int]]]:
+    """The host part of the reference's state checks (``loader.py:94-112``): the type and dtype errors by
+    entry position, and the (position, key, kind) of every buffer whose content the device checks."""
 
-    errors: dict[int, str] = {}  # entry position -> message of its type or dtype error
-    checked: list[tuple[int, str, int]] = []  # (entry position, key, kind) of the device checks
-    keys = list(state)
-    for pos, key in enumerate(keys):
-        value = state[key]
+    errors: dict[int, str] = {}
+    checked: list[tuple[int, str, int]] = []
+    for pos, (key, value) in enumerate(state.items()):
         if not isinstance(value, torch.Tensor):
             errors[pos] = f"model_state entry is not a tensor: {key}"
         elif key.endswith(".packed_weight"):
@@ -57,6 +54,32 @@ def validate_state_device(state: dict[str, Any], device: torch.device) -> None:
                 errors[pos] = f"g128 scale buffer must be float16: {key}"
             else:
                 checked.append((pos, key, native.IVB_CHECK_SCALES))
+    return errors, checked
+
+
+def _first_error(errors: dict[int, str], checked: list[tuple[int, str, int]], bad: tuple[int, int, int]) -> str | None:
+    """The message the reference raises first: `bad` holds the device's lowest failing index into
+    `checked` per content check (reserved code 3, non-finite scale, non-positive scale; len(checked)
+    when none failed). Entries are taken in state order, and one scale buffer fails "finite" before
+    "positive", as the reference tests them."""
+
+    errors = dict(errors)
+    for idx, message in zip(bad, ("packed ternary buffer contains the reserved code 3: {}",
+                                  "g128 scale buffer must contain only finite values: {}",
+                                  "g128 scale buffer must contain only positive values: {}")):
+        if 0 <= idx < len(checked):
+            pos, key, _ = checked[idx]
+            errors.setdefault(pos, message.format(key))
+    return errors[min(errors)] if errors else None
+
+
+def validate_state_device(state: dict[str, Any], device: torch.device) -> None:
+    """The reference's state checks (``loader.py:94-112``) with the content checks on the device: one
+    launch over every packed and scale buffer of the right dtype, one synchronisation. Then the entries
+    are walked in the reference's order and the first failing check raises the reference's message."""
+
+    errors, checked = _plan_checks(state)
+    bad = (len(checked),) * 3
     if checked:
         lib = native.library()
         descs = (native.IvbCheckBuffer * len(checked))()
@@ -69,22 +92,14 @@ def validate_state_device(state: dict[str, Any], device: torch.device) -> None:
             descs[i].kind = kind
         raw = torch.frombuffer(bytearray(ctypes.string_at(ctypes.addressof(descs), ctypes.sizeof(descs))), dtype=torch.uint8)
         dev_descs = raw.to(device)
-        bad = torch.empty(3, dtype=torch.int32, device=device)
+        out = torch.empty(3, dtype=torch.int32, device=device)
         stream = torch.cuda.current_stream(device).cuda_stream
-        native.check(lib.ivb_validate_buffers(dev_descs.data_ptr(), len(checked), bad.data_ptr(), stream),
+        native.check(lib.ivb_validate_buffers(dev_descs.data_ptr(), len(checked), out.data_ptr(), stream),
                      "ivb_validate_buffers")
-        code3, nonfinite, nonpositive = (int(v) for v in bad.cpu())
-        # the device reports the first failing buffer per check; a scale buffer fails "finite" before
-        # "positive" as in the reference
-        for idx, message in ((code3, "packed ternary buffer contains the reserved code 3: {}"),
-                             (nonfinite, "g128 scale buffer must contain only finite values: {}"),
-                             (nonpositive, "g128 scale buffer must contain only positive values: {}")):
-            if idx < len(checked):
-                pos, key, _ = checked[idx]
-                if pos not in errors:
-                    errors[pos] = message.format(key)
-    if errors:
-        raise RuntimeError(errors[min(errors)])
+        bad = tuple(int(v) for v in out.cpu())
+    message = _first_error(errors, checked, bad)
+    if message is not None:
+        raise RuntimeError(message)
 
 
 _STORAGE_DTYPES = {

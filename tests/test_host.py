@@ -206,3 +206,62 @@ def test_ingest_archive_reader_matches_torch_load(tmp_path: Path) -> None:
     assert ingest._read_archive(path, torch.device("cpu")) is None
     path.write_bytes(b"not an archive")
     assert ingest._read_archive(path, torch.device("cpu")) is None
+
+
+def _device_checks_on_the_host(state: dict, checked: list) -> tuple[int, int, int]:
+    """What ivb_validate_buffers reports, computed with numpy: the lowest index into `checked` of a
+    packed buffer holding code 3, of a scale buffer with a non-finite value, and of one with a
+    non-positive value (len(checked) when none)."""
+    import numpy as np
+
+    bad = [len(checked)] * 3
+    for i, (_, key, kind) in enumerate(checked):
+        if kind == 0:
+            b = state[key].numpy().reshape(-1).astype(np.uint32)
+            flags = (bool(np.any(b & (b >> 1) & 0x55)), False, False)
+        else:
+            h = state[key].view(torch.int16).numpy().reshape(-1).astype(np.uint32) & 0xFFFF
+            flags = (False, bool(np.any((h & 0x7C00) == 0x7C00)), bool(np.any(((h & 0x8000) != 0) | ((h & 0x7FFF) == 0))))
+        for j in range(3):
+            if flags[j]:
+                bad[j] = min(bad[j], i)
+    return tuple(bad)
+
+
+def test_ingest_reports_the_reference_loaders_first_error() -> None:
+    """The order in which the device-checked state raises: for random corruptions (reserved codes,
+    NaN/inf/zero/negative scales, wrong dtypes, non-tensors, several at once) the message chosen from
+    the device's per-check lowest indices is the one the reference's own _validate_state raises."""
+    from ivonar_inference_b200 import _reference, ingest, synthetic
+
+    loader = _reference.module("loader")
+    clean = synthetic.synthetic_state(synthetic.tiny(), 0, "reference_tests")
+    keys = list(clean)
+    gen = torch.Generator().manual_seed(11)
+    for trial in range(200):
+        state = {k: v.clone() for k, v in clean.items()}
+        for _ in range(int(torch.randint(0, 4, (1,), generator=gen))):
+            key = keys[int(torch.randint(0, len(keys), (1,), generator=gen))]
+            value = state[key]
+            kind = int(torch.randint(0, 6, (1,), generator=gen))
+            if not isinstance(value, torch.Tensor):
+                continue
+            flat = value.view(-1)
+            at = int(torch.randint(0, flat.numel(), (1,), generator=gen))
+            if key.endswith(".packed_weight") and kind < 3:
+                flat[at] = int(flat[at]) | (3 << (2 * (kind % 4)))
+            elif key.endswith(".weight_scales") and kind < 4:
+                flat[at] = (float("nan"), float("inf"), 0.0, -0.25)[kind]
+            elif kind == 4 and value.dtype in (torch.uint8, torch.float16):
+                state[key] = value.float()
+            elif kind == 5:
+                state[key] = [1, 2, 3]
+        errors, checked = ingest._plan_checks(state)
+        bad = _device_checks_on_the_host(state, checked)
+        ours = ingest._first_error(errors, checked, bad)
+        try:
+            loader._validate_state(state)
+            expected = None
+        except RuntimeError as exc:
+            expected = str(exc)
+        assert ours == expected, (trial, ours, expected)
