@@ -146,7 +146,7 @@ class _ArchiveUnpickler(pickle.Unpickler):
         view = self.views.get(key)
         if view is None:
             offset, nbytes = self.records.get(f"data/{key}", (0, -1))
-            if nbytes != int(numel) * kind.dtype.itemsize:
+            if nbytes != int(numel) * kind.dtype.itemsize or offset % kind.dtype.itemsize:
                 raise _Unsupported(f"storage {key}")
             view = self.block[offset:offset + nbytes].view(kind.dtype)
             self.views[key] = view
