@@ -31,6 +31,10 @@ installed unmodified in baseline/_ref) and B200Decoder timed by the same procedu
 API on the same GPU: prefill, configure_sampling, sample, then CUDA events around advance_many bursts that
 produce the 256 decode tokens (the reference eager and with its CUDA graphs captured).
 
+Secondary, rank 0 at N=1 (`ingest`): loading the config-1 checkpoint (88.8 MB, in the page cache) to
+the GPU through the reference's load_model and through ingest.load_model, median wall-clock ms of 3
+loads each with the device synchronised, and the device validation call alone.
+
 --impl reference times the reference's own CPU decoder (the numba CpuDecoder chosen by the reference's
 build_decoder for device "cpu", installed unmodified in baseline/_ref) on this host's cores, rank 0 only:
 each timed step decodes the workload's 256 sampled tokens after an untimed prefill.
@@ -73,6 +77,7 @@ def parse() -> argparse.Namespace:
     ap.add_argument("--no-gpu-reference", action="store_true", help="skip the reference KernelDecoder on this GPU")
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-batch", action="store_true")
+    ap.add_argument("--no-ingest", action="store_true", help="skip the checkpoint-load measurement (N=1 only)")
     ap.add_argument("--tp", action="store_true", help="also measure config 4 (7B-shaped, tensor parallel over the ranks) at N=1")
     ap.add_argument("--no-tp", action="store_true", help="skip config 4, which runs by default on more than one GPU")
     ap.add_argument("--only", choices=("prefill", "gemm", "tp", "batch", "ingest"), default=None,
@@ -689,6 +694,11 @@ def run_b200(args) -> None:
             line["prefill"] = prefill_measure(device)
         if not args.no_gpu_reference:
             line["gpu_reference"] = gpu_reference(device, tokens)
+        if world == 1 and not args.no_ingest:
+            try:
+                line["ingest"] = ingest_measure(device, 3)
+            except Exception as exc:  # a secondary measurement must not cost the main line
+                line["ingest"] = {"error": f"{type(exc).__name__}: {exc}"}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(model, 32)
         print(json.dumps(line), flush=True)
