@@ -5,20 +5,24 @@
 // the fp16 group scale in fp32. Reference: kernels/ternary.cu:688-765 gemm_tile_body (per-token int8
 // tiles, dp4a), which subtracts the activation group sum instead of offsetting the codes.
 //
-// One CTA computes a 128-row x 128-token tile. The weights are the MMA's A operand and live in tensor
-// memory: they never pass through shared memory as bytes. Warp-specialised roles per 128-input group g:
-//   * two producer teams of 4 warps (one TMEM lane quarter each), team t taking the groups g = t (mod 2)
-//     so two groups are staged at once: the team's leader fetches the tile's packed weights of the group
-//     (128 rows x 32 bytes) with one TMA tensor load into a small packed ring and bulk-copies the group's
-//     16 KB activation tile (core matrices, laid out by ivb_quantize_rows) into an operand stage; then
-//     every thread of the team expands its row's 128 two-bit codes to signed bytes (code - 1) in
-//     registers and stores them into the group's A slot in TMEM (tcgen05.st, 32 columns);
+// Persistent: one CTA per SM walks units of 128 weight rows x 128 tokens (x one split of K), and every
+// role keeps a running group count over the CTA's whole sequence, so the next unit's copies, expansion
+// and MMAs overlap the current unit's epilogue. The weights are the MMA's A operand and live in tensor
+// memory: they never pass through shared memory as expanded bytes. Warp-specialised roles per
+// 128-input group G:
+//   * a copy warp (one thread) issues every copy up to eight groups ahead: the unit's packed weights of
+//     the group (128 rows x 32 bytes) with one TMA tensor load into a packed ring, and the group's 16 KB
+//     activation tile (core matrices, laid out by ivb_quantize_rows) with one bulk copy into an
+//     8-stage ring;
+//   * two producer teams of 4 warps (one TMEM lane quarter each), team t expanding the groups
+//     G = t (mod 2): every thread turns its row's 128 two-bit codes into signed bytes (code - 1) in
+//     registers and stores them into A slot G % 4 in TMEM (tcgen05.st, 32 columns);
 //   * one MMA thread: four 128x128x32 int8 MMAs (A from TMEM, B = activations from shared memory) into
-//     TMEM accumulator g % 3 (the first one overwrites it), committed to the stage's "empty" barrier and
-//     to the accumulator's "full" barrier;
+//     TMEM accumulator G % 3, committed to the stage's, the A slot's and the accumulator's barriers;
 //   * epilogue warps (16; warp w reads TMEM lane quarter w % 4 = weight rows, columns 32 (w / 4).. =
-//     tokens): drain the accumulator (tcgen05.ld), convert the exact int32 group dots, scale them by the
-//     row's group scale and accumulate in fp32 registers (paired multiply-adds).
+//     tokens): drain the accumulator (tcgen05.ld), recover the exact int32 group dots from the biased
+//     accumulator, scale them by the row's group scale and accumulate in fp32 registers (paired
+//     multiply-adds); at the end of a unit, store the outputs straight from registers.
 // TMEM: 3 accumulators x 128 columns + 4 A slots x 32 columns = all 512 columns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
