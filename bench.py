@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the Ivonar token loop on B200 (one JSON line on stdout from rank 0).
 
-Workload: Nano-shaped ternary hybrid (vocab 32768, d 1024, 24 blocks), batch 1,
+Workload (benchmark configuration 1): Nano-shaped ternary hybrid (vocab 32768, d 1024, 24 blocks), batch 1,
 a 36-token random prompt, then 256 sampled decode tokens (T 0.5, top-k 40, repetition penalty 1.15).
 A step is one such generation. `value` is decode tokens/s of the persistent decode kernel with the
 prompt already prefilled in HBM (CUDA events around the one launch that decodes 256 tokens; L2 is
@@ -11,18 +11,18 @@ advance_many(16), host copies included. With --gpus N (torchrun) every rank deco
 independent sequences on its own GPU (data parallel, no collective on the data path); value is the
 total over ranks divided by the slowest rank's time.
 
-Secondary, rank 0: prompt prefill tok/s at 512, 2048 and 8192 tokens through
+Secondary, rank 0 (benchmark configuration 2): prompt prefill tok/s at 512, 2048 and 8192 tokens through
 B200Decoder.prefill (tcgen05 GEMMs, recurrent scan, latent-cache fill and causal attention) at batch 1
 and at batch 8 (eight independent prompts, one decoder and one CUDA stream each, timed together), and
 the int8 tensor-core throughput of the prefill GEMM alone on the gate/up shape at 2048 tokens.
 
-Secondary, every rank: batched serving, 256 independent sequences split evenly over
+Secondary, every rank (benchmark configuration 3): batched serving, 256 independent sequences split evenly over
 the N GPUs (data parallel, no collective on the data path), each a 128-token random prompt and then
 sampled tokens (T 0.5, top-k 40, rp 1.15, per-sequence seeds) through B200BatchDecoder; `batched.value`
 is the aggregate decode tok/s (all sequences' tokens over the slowest rank's CUDA-event time of the
 timed decode steps).
 
-Secondary, every rank: the 7B-shaped model (weights drawn on the GPU) tensor
+Secondary, every rank (benchmark configuration 4): the 7B-shaped model (weights drawn on the GPU) tensor
 parallel over the N ranks (`tp`): a 512-token random prompt teacher-forced, then sampled decode at batch
 1 and batch 32, tok/s over the slowest rank's CUDA-event time.
 

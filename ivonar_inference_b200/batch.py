@@ -1,4 +1,4 @@
-"""Batched decode of independent sequences on one B200.
+"""Batched decode of independent sequences on one B200 (benchmark configuration 3).
 
 `B200BatchDecoder` advances `batch` sequences one token per step together through
 `ivb_batch_decode`: every projection of every layer runs once per step as a tcgen05 GEMM over the

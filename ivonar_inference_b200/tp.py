@@ -1,4 +1,4 @@
-"""Tensor-parallel batched decode (the 7B-shaped model over 2/4/8 B200).
+"""Tensor-parallel batched decode (benchmark configuration 4: the 7B-shaped model over 2/4/8 B200).
 
 Each rank holds a shard of every block: the mixer by heads (mamba: the value/gate channels and the
 B, C, dt rows of its heads, their SSM constants and state; mla: the q and k_rope rows, k_nope/v
